@@ -1,0 +1,388 @@
+// Paged-KV grouped-query decode attention (flash-decoding with split KV), bf16 KV,
+// head_dim 64 / 128 / 256, any page size, 1..N query tokens per request (N > 1 is the
+// speculative-verify mode: query j of a request sees the first
+// kv_len - q_len + 1 + j cached tokens).
+//
+// The op is bound by reading the KV cache once: every CTA owns one (request, kv head,
+// 16-row query tile, KV split); each of its 4 warps streams its own 32- (or 16-)token
+// KV tiles through a private 2-stage cp.async ring, computes S = Q K^T and O += P V
+// with bf16 mma.sync (tensor throughput is not the limit here; bytes are) and keeps
+// a private online-softmax state. Warps merge through shared memory, splits merge in
+// a second small kernel through an fp32 workspace.
+//
+// Reference behaviour: the trtllm-gen paged decode call in
+// python/minisgl/attention/trtllm.py:136-178 (bf16 KV, NHD pages, q_len_per_req for
+// verify).
+#include "common.cuh"
+
+namespace afd {
+
+__device__ __forceinline__ void cp_async16(void* smem_dst, const void* gsrc) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)), "l"(gsrc) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+__device__ __forceinline__ void mma_bf16_16816(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+struct DecodeAttnArgs {
+  const __nv_bfloat16* q;        // [B*q_len][Hq][D]
+  const __nv_bfloat16* k_cache;  // [slots][Hkv][D]
+  const __nv_bfloat16* v_cache;
+  const int* page_table;         // [B][max_pages]
+  const int* seq_lens;           // [B] KV length including the query tokens
+  __nv_bfloat16* out;            // [B*q_len][Hq][D]
+  float* part_o;                 // [B][Hkv][m_tiles][splits][16][D]
+  float* part_lse;               // [B][Hkv][m_tiles][splits][16]
+  int B, Hq, Hkv, q_len, page_size, max_pages, splits, m_tiles;
+  long cache_slots;
+  float scale_log2;              // softmax scale * log2(e)
+  int* status;
+};
+
+// Row-major [rows][D] bf16 tile in shared memory with 16-byte chunks XOR-swizzled by
+// the row, so that ldmatrix reads are free of bank conflicts.
+template <int D>
+__device__ __forceinline__ uint32_t tile_off(int row, int chunk) {
+  return static_cast<uint32_t>(row * D * 2 + ((chunk ^ (row & 7)) << 4));
+}
+
+template <int D, int TOK>
+__global__ void __launch_bounds__(128, 1) decode_attn_kernel(const DecodeAttnArgs a) {
+  constexpr int CH = D / 8;            // 16-byte chunks per row
+  constexpr int KT = D / 16;           // k-steps of S
+  constexpr int NT = TOK / 8;          // n-tiles of S
+  constexpr int TILE_BYTES = TOK * D * 2;
+  constexpr int WARP_BYTES = 4 * TILE_BYTES;   // 2 stages x (K + V)
+  extern __shared__ __align__(128) uint8_t smem[];
+  uint8_t* sq = smem;                          // Q tile 16 x D
+  uint8_t* swarp = smem + 16 * D * 2;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int split = blockIdx.x;
+  const int kvh = blockIdx.y / a.m_tiles, mt = blockIdx.y % a.m_tiles;
+  const int b = blockIdx.z;
+  const int G = a.Hq / a.Hkv;
+  const int M = G * a.q_len;                   // valid query rows of this (b, kvh)
+  int kv_len = a.seq_lens[b];
+  if (kv_len < 0) kv_len = 0;
+  if (kv_len > a.max_pages * a.page_size) {
+    set_status(a.status, kStatusBadExtent);
+    kv_len = a.max_pages * a.page_size;
+  }
+
+  // ---- stage Q (rows = j*G + g), zero for padding rows ----
+  for (int idx = threadIdx.x; idx < 16 * CH; idx += 128) {
+    const int r = idx / CH, c = idx % CH;
+    const int row = mt * 16 + r;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (row < M) {
+      const int j = row / G, g = row % G;
+      v = *reinterpret_cast<const uint4*>(a.q + ((static_cast<size_t>(b) * a.q_len + j) * a.Hq + kvh * G + g) * D + c * 8);
+    }
+    *reinterpret_cast<uint4*>(sq + tile_off<D>(r, c)) = v;
+  }
+  __syncthreads();
+
+  // ---- this CTA's KV range ----
+  const int per_split = ((kv_len + a.splits - 1) / a.splits + TOK * 4 - 1) / (TOK * 4) * (TOK * 4);
+  const int kv_begin = split * per_split;
+  const int kv_end = min(kv_len, kv_begin + per_split);
+  const int n_tiles = kv_end > kv_begin ? (kv_end - kv_begin + TOK - 1) / TOK : 0;
+
+  uint8_t* my = swarp + warp * WARP_BYTES;
+  const int* pt = a.page_table + static_cast<size_t>(b) * a.max_pages;
+
+  auto load_tile = [&](int tile, int stage) {
+    uint8_t* sk = my + stage * 2 * TILE_BYTES;
+    uint8_t* sv = sk + TILE_BYTES;
+    const int t0 = kv_begin + tile * TOK;
+    for (int idx = lane; idx < TOK * CH; idx += 32) {
+      const int r = idx / CH, c = idx % CH;
+      const int t = t0 + r;
+      if (t < kv_end) {
+        const int page = pt[t / a.page_size];
+        const long slot = static_cast<long>(page) * a.page_size + (t % a.page_size);
+        if (slot >= 0 && slot < a.cache_slots) {
+          const size_t off = (static_cast<size_t>(slot) * a.Hkv + kvh) * D + c * 8;
+          cp_async16(sk + tile_off<D>(r, c), a.k_cache + off);
+          cp_async16(sv + tile_off<D>(r, c), a.v_cache + off);
+          continue;
+        }
+        set_status(a.status, kStatusBadExtent);
+      }
+      *reinterpret_cast<uint4*>(sk + tile_off<D>(r, c)) = make_uint4(0, 0, 0, 0);
+      *reinterpret_cast<uint4*>(sv + tile_off<D>(r, c)) = make_uint4(0, 0, 0, 0);
+    }
+  };
+
+  float o[D / 8][4];
+#pragma unroll
+  for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  float m_run[2] = {-INFINITY, -INFINITY};
+  float l_run[2] = {0.f, 0.f};
+  // causal limit per row (rows lane/4 and lane/4 + 8)
+  int lim[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int row = mt * 16 + (lane >> 2) + h * 8;
+    const int j = row < M ? row / G : 0;
+    lim[h] = row < M ? kv_len - a.q_len + 1 + j : 0;
+  }
+
+  int it = 0;
+  if (warp < n_tiles) load_tile(warp, 0);
+  cp_async_commit();
+  for (int tile = warp; tile < n_tiles; tile += 4, ++it) {
+    const int stage = it & 1;
+    if (tile + 4 < n_tiles) load_tile(tile + 4, stage ^ 1);
+    cp_async_commit();
+    cp_async_wait<1>();
+    __syncwarp();
+    const uint32_t sk = smem_u32(my + stage * 2 * TILE_BYTES);
+    const uint32_t sv = sk + TILE_BYTES;
+    const uint32_t sqa = smem_u32(sq);
+
+    float s[NT][4];
+#pragma unroll
+    for (int n = 0; n < NT; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
+#pragma unroll
+    for (int ks = 0; ks < KT; ++ks) {
+      uint32_t qa[4];
+      {
+        const int mat = lane >> 3;
+        const int row = (mat & 1) * 8 + (lane & 7);
+        ldsm_x4(sqa + tile_off<D>(row, ks * 2 + (mat >> 1)), qa[0], qa[1], qa[2], qa[3]);
+      }
+#pragma unroll
+      for (int np = 0; np < NT / 2; ++np) {
+        const int mat = lane >> 3;
+        const int row = np * 16 + (mat >> 1) * 8 + (lane & 7);
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(sk + tile_off<D>(row, ks * 2 + (mat & 1)), b0, b1, b2, b3);
+        mma_bf16_16816(s[np * 2], qa, b0, b1);
+        mma_bf16_16816(s[np * 2 + 1], qa, b2, b3);
+      }
+    }
+    // ---- mask + online softmax ----
+    const int t0 = kv_begin + tile * TOK;
+    float mx[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int t = t0 + n * 8 + (lane & 3) * 2 + (e & 1);
+        const int h = e >> 1;
+        float v = s[n][e] * a.scale_log2;
+        if (t >= lim[h] || t >= kv_end) v = -INFINITY;
+        s[n][e] = v;
+        mx[h] = fmaxf(mx[h], v);
+      }
+    }
+    float corr[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
+      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
+      const float m_new = fmaxf(m_run[h], mx[h]);
+      corr[h] = (m_new == -INFINITY) ? 1.f : exp2f(m_run[h] - m_new);
+      m_run[h] = m_new;
+      l_run[h] *= corr[h];
+    }
+#pragma unroll
+    for (int i = 0; i < D / 8; ++i) {
+      o[i][0] *= corr[0];
+      o[i][1] *= corr[0];
+      o[i][2] *= corr[1];
+      o[i][3] *= corr[1];
+    }
+    uint32_t pa[NT / 2][4];
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+      float p[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int h = e >> 1;
+        p[e] = (m_run[h] == -INFINITY) ? 0.f : exp2f(s[n][e] - m_run[h]);
+        l_run[h] += p[e];
+      }
+      pa[n / 2][(n & 1) * 2 + 0] = pack_bf16(p[0], p[1]);
+      pa[n / 2][(n & 1) * 2 + 1] = pack_bf16(p[2], p[3]);
+    }
+    // ---- O += P V ----
+#pragma unroll
+    for (int ks = 0; ks < TOK / 16; ++ks) {
+#pragma unroll
+      for (int dp = 0; dp < D / 16; ++dp) {
+        const int mat = lane >> 3;
+        const int row = ks * 16 + (mat & 1) * 8 + (lane & 7);
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(sv + tile_off<D>(row, dp * 2 + (mat >> 1)), b0, b1, b2, b3);
+        mma_bf16_16816(o[dp * 2], pa[ks], b0, b1);
+        mma_bf16_16816(o[dp * 2 + 1], pa[ks], b2, b3);
+      }
+    }
+    __syncwarp();
+  }
+  cp_async_wait<0>();
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 1);
+    l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 2);
+  }
+
+  // ---- merge the 4 warps through shared memory (each warp reuses its own ring) ----
+  __syncwarp();
+  float* wo = reinterpret_cast<float*>(my);          // [16][D]
+  float* wm = wo + 16 * D;                           // [16]
+  float* wl = wm + 16;                               // [16]
+#pragma unroll
+  for (int i = 0; i < D / 8; ++i) {
+    const int r = lane >> 2, c = i * 8 + (lane & 3) * 2;
+    wo[r * D + c] = o[i][0];
+    wo[r * D + c + 1] = o[i][1];
+    wo[(r + 8) * D + c] = o[i][2];
+    wo[(r + 8) * D + c + 1] = o[i][3];
+  }
+  if ((lane & 3) == 0) {
+    wm[lane >> 2] = m_run[0];
+    wm[(lane >> 2) + 8] = m_run[1];
+    wl[lane >> 2] = l_run[0];
+    wl[(lane >> 2) + 8] = l_run[1];
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < 16 * D; idx += 128) {
+    const int r = idx / D, d = idx % D;
+    float mm = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) mm = fmaxf(mm, reinterpret_cast<float*>(swarp + w * WARP_BYTES)[16 * D + r]);
+    float acc = 0.f, l = 0.f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const float* base = reinterpret_cast<float*>(swarp + w * WARP_BYTES);
+      const float mw = base[16 * D + r];
+      const float f = (mw == -INFINITY) ? 0.f : exp2f(mw - mm);
+      acc += base[r * D + d] * f;
+      l += base[16 * D + 16 + r] * f;
+    }
+    const float val = l > 0.f ? acc / l : 0.f;
+    const int row = mt * 16 + r;
+    if (a.splits == 1) {
+      if (row < M) {
+        const int j = row / G, g = row % G;
+        a.out[((static_cast<size_t>(b) * a.q_len + j) * a.Hq + kvh * G + g) * D + d] = __float2bfloat16(val);
+      }
+    } else {
+      const size_t pidx = ((static_cast<size_t>(b) * a.Hkv + kvh) * a.m_tiles + mt) * a.splits + split;
+      a.part_o[(pidx * 16 + r) * D + d] = val;
+      if (d == 0) a.part_lse[pidx * 16 + r] = l > 0.f ? mm + log2f(l) : -INFINITY;
+    }
+  }
+}
+
+template <int D>
+__global__ void decode_attn_merge_kernel(const DecodeAttnArgs a) {
+  const int kvh = blockIdx.y / a.m_tiles, mt = blockIdx.y % a.m_tiles;
+  const int b = blockIdx.z;
+  const int r = blockIdx.x;   // row within the 16-row tile
+  const int G = a.Hq / a.Hkv;
+  const int M = G * a.q_len;
+  const int row = mt * 16 + r;
+  if (row >= M) return;
+  const size_t p0 = ((static_cast<size_t>(b) * a.Hkv + kvh) * a.m_tiles + mt) * a.splits;
+  float mm = -INFINITY;
+  for (int s = 0; s < a.splits; ++s) mm = fmaxf(mm, a.part_lse[(p0 + s) * 16 + r]);
+  const int j = row / G, g = row % G;
+  __nv_bfloat16* dst = a.out + ((static_cast<size_t>(b) * a.q_len + j) * a.Hq + kvh * G + g) * D;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float acc = 0.f, wsum = 0.f;
+    for (int s = 0; s < a.splits; ++s) {
+      const float lse = a.part_lse[(p0 + s) * 16 + r];
+      const float w = (lse == -INFINITY) ? 0.f : exp2f(lse - mm);
+      acc += a.part_o[((p0 + s) * 16 + r) * D + d] * w;
+      wsum += w;
+    }
+    dst[d] = __float2bfloat16(wsum > 0.f ? acc / wsum : 0.f);
+  }
+}
+
+template <int D, int TOK>
+static int launch_decode(const DecodeAttnArgs& a, cudaStream_t st) {
+  constexpr int smem = 16 * D * 2 + 4 * 4 * TOK * D * 2;
+  auto kern = decode_attn_kernel<D, TOK>;
+  static bool set = false;
+  if (!set) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return static_cast<int>(e);
+    set = true;
+  }
+  dim3 grid(a.splits, a.Hkv * a.m_tiles, a.B);
+  kern<<<grid, 128, smem, st>>>(a);
+  AFD_CHECK_LAUNCH();
+  if (a.splits > 1) {
+    dim3 g2(16, a.Hkv * a.m_tiles, a.B);
+    decode_attn_merge_kernel<D><<<g2, D / 2 > 32 ? D / 2 : 32, 0, st>>>(a);
+    AFD_CHECK_LAUNCH();
+  }
+  return 0;
+}
+
+}  // namespace afd
+
+// Workspace needed for `splits` > 1, in bytes: part_o then part_lse.
+extern "C" long afd_decode_attn_workspace_bytes(int B, int Hq, int Hkv, int q_len, int D, int splits) {
+  const int G = Hq / Hkv;
+  const long m_tiles = (G * q_len + 15) / 16;
+  const long tiles = static_cast<long>(B) * Hkv * m_tiles * splits;
+  return tiles * 16 * D * 4 + tiles * 16 * 4;
+}
+
+extern "C" int afd_decode_attention(const void* q, const void* k_cache, const void* v_cache,
+                                    const void* page_table, const void* seq_lens, void* out,
+                                    void* workspace, int B, int Hq, int Hkv, int D, int q_len,
+                                    int page_size, int max_pages, long cache_slots, int splits,
+                                    float sm_scale, void* status, void* stream) {
+  using namespace afd;
+  if (B == 0) return 0;
+  if (Hq % Hkv != 0 || splits < 1 || page_size < 1) return -1;
+  if (splits > 1 && workspace == nullptr) return -2;
+  DecodeAttnArgs a{};
+  a.q = static_cast<const __nv_bfloat16*>(q);
+  a.k_cache = static_cast<const __nv_bfloat16*>(k_cache);
+  a.v_cache = static_cast<const __nv_bfloat16*>(v_cache);
+  a.page_table = static_cast<const int*>(page_table);
+  a.seq_lens = static_cast<const int*>(seq_lens);
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.B = B; a.Hq = Hq; a.Hkv = Hkv; a.q_len = q_len; a.page_size = page_size; a.max_pages = max_pages;
+  a.splits = splits;
+  a.m_tiles = ((Hq / Hkv) * q_len + 15) / 16;
+  a.cache_slots = cache_slots;
+  a.scale_log2 = sm_scale * 1.4426950408889634f;
+  a.status = static_cast<int*>(status);
+  const long tiles = static_cast<long>(B) * Hkv * a.m_tiles * splits;
+  a.part_o = static_cast<float*>(workspace);
+  a.part_lse = a.part_o ? a.part_o + tiles * 16 * D : nullptr;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (D == 128) return launch_decode<128, 32>(a, st);
+  if (D == 256) return launch_decode<256, 16>(a, st);
+  if (D == 64) return launch_decode<64, 32>(a, st);
+  return -3;
+}

@@ -1,0 +1,502 @@
+// N2M dispatch / M2N combine over NVLink peer memory, and the expert-side grouping.
+//
+// Protocol (one "lane" = one micro-batch's private set of buffers and flags; a lane
+// strictly alternates dispatch -> combine per layer, so buffers are never
+// overwritten while a peer still reads them and no credit counters are needed):
+//
+//   attention GPU a                                  expert GPU e
+//   ----------------------------------------------   ------------------------------------------
+//   dispatch_push: (optional 1x128 FP8 quant of the
+//     row), store the row into e's recv_x[a][t]
+//     for every e that owns one of the token's
+//     experts; store the token's top-k ids into
+//     every e's recv_idx[a][t]; last CTA releases
+//     n2m_flag[a] = epoch on every e            =>   eg_group: wait n2m_flag[*] >= epoch (bounded),
+//                                                      count per local expert, pad to the token
+//                                                      tile, assign pool rows, emit tile_info /
+//                                                      row_meta
+//                                                    eg_gather: recv_x rows -> expert-grouped pool
+//                                                    grouped GEMM (SwiGLU) ; grouped GEMM (COMBINE):
+//   ag_combine: wait m2n_flag[*] >= epoch       <=     rows stored into a's combine[k][t], last CTA
+//     (bounded), y[t] = sum_k w[t,k] combine[k][t]     releases m2n_flag[e] = epoch on every a
+//     in fp32, optional residual add + RMSNorm
+//
+// Epochs live in device memory and are advanced by the kernels themselves, so the
+// whole exchange can sit inside a replayed CUDA graph. Every wait is bounded by a
+// caller-given timeout in nanoseconds; on expiry the kernel records
+// kStatusFlagTimeout in the status word and carries on without faulting.
+//
+// Reference behaviour: dispatch / combine roles of
+// python/minisgl/kernel/csrc/deepgemm/deep_gemm/include/deep_gemm/impls/sm100_mega_moe_m2n.cuh
+// (AG kernel :212-1265; EG pull + pool :2023-2254) and python/minisgl/moe/megamoe_m2n_afd.py:336-470.
+// This design pushes instead of pulling and needs no global barrier.
+#include "common.cuh"
+
+namespace afd {
+
+constexpr int kMaxRanks = 16;
+
+struct DispatchArgs {
+  const __nv_bfloat16* x;      // [T][H]
+  const int* topk_idx;         // [T][K] global expert ids
+  int T, H, K;
+  int src_rank;                // this attention rank's index among attention ranks
+  int num_eg, experts_per_eg;
+  int fp8;                     // 1: quantise rows to e4m3 with 1x128 scales while pushing
+  int recv_tokens;             // T capacity of the receive buffers
+  void* peer_recv_x[kMaxRanks];        // [A][recv_tokens][H] bf16 or e4m3
+  float* peer_recv_scale[kMaxRanks];   // [A][recv_tokens][H/128] (fp8)
+  int* peer_recv_idx[kMaxRanks];       // [A][recv_tokens][K]
+  uint32_t* peer_flag[kMaxRanks];      // &n2m_flag[src_rank] on each expert GPU
+  uint32_t* epoch;
+  unsigned int* done_counter;
+  int* status;
+};
+
+__global__ void dispatch_push_kernel(const DispatchArgs a) {
+  const int t = blockIdx.x;
+  __shared__ uint32_t s_mask;
+  if (threadIdx.x == 0) {
+    uint32_t mask = 0;
+    for (int k = 0; k < a.K; ++k) {
+      const int e = a.topk_idx[static_cast<size_t>(t) * a.K + k];
+      if (e >= 0) {
+        const int eg = e / a.experts_per_eg;
+        if (eg < a.num_eg) mask |= 1u << eg;
+        else set_status(a.status, kStatusBadExtent);
+      }
+    }
+    s_mask = mask;
+  }
+  if (threadIdx.x < a.K) {
+    const int e = a.topk_idx[static_cast<size_t>(t) * a.K + threadIdx.x];
+    for (int eg = 0; eg < a.num_eg; ++eg) {
+      a.peer_recv_idx[eg][(static_cast<size_t>(a.src_rank) * a.recv_tokens + t) * a.K + threadIdx.x] = e;
+    }
+  }
+  __syncthreads();
+  const uint32_t mask = s_mask;
+  const size_t dst_row = static_cast<size_t>(a.src_rank) * a.recv_tokens + t;
+  const __nv_bfloat16* xr = a.x + static_cast<size_t>(t) * a.H;
+  if (!a.fp8) {
+    for (int i = threadIdx.x * 8; i < a.H; i += blockDim.x * 8) {
+      const uint4 v = *reinterpret_cast<const uint4*>(xr + i);
+      for (int eg = 0; eg < a.num_eg; ++eg) {
+        if (mask & (1u << eg)) {
+          *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.peer_recv_x[eg]) + dst_row * a.H + i) = v;
+        }
+      }
+    }
+  } else {
+    // one warp per 128-wide group: 4 elements per lane
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+    const int groups = a.H / 128;
+    for (int g = warp; g < groups; g += nw) {
+      const uint2 raw = *reinterpret_cast<const uint2*>(xr + g * 128 + lane * 4);
+      const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+      const float2 f0 = __bfloat1622float2(b2[0]), f1 = __bfloat1622float2(b2[1]);
+      float amax = fmaxf(fmaxf(fabsf(f0.x), fabsf(f0.y)), fmaxf(fabsf(f1.x), fabsf(f1.y)));
+      amax = warp_max(amax);
+      const float scale = fmaxf(amax, 1e-10f) / 448.f;
+      const float inv = 1.f / scale;
+      uint32_t packed = 0;
+      packed |= static_cast<uint32_t>(__nv_cvt_float_to_fp8(f0.x * inv, __NV_SATFINITE, __NV_E4M3));
+      packed |= static_cast<uint32_t>(__nv_cvt_float_to_fp8(f0.y * inv, __NV_SATFINITE, __NV_E4M3)) << 8;
+      packed |= static_cast<uint32_t>(__nv_cvt_float_to_fp8(f1.x * inv, __NV_SATFINITE, __NV_E4M3)) << 16;
+      packed |= static_cast<uint32_t>(__nv_cvt_float_to_fp8(f1.y * inv, __NV_SATFINITE, __NV_E4M3)) << 24;
+      for (int eg = 0; eg < a.num_eg; ++eg) {
+        if (mask & (1u << eg)) {
+          *reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(a.peer_recv_x[eg]) + dst_row * a.H + g * 128 + lane * 4) = packed;
+          if (lane == 0) a.peer_recv_scale[eg][dst_row * groups + g] = scale;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    const unsigned int prev = atomicAdd(a.done_counter, 1u);
+    if (prev == gridDim.x - 1) {
+      __threadfence_system();
+      const uint32_t e = *a.epoch;
+      for (int eg = 0; eg < a.num_eg; ++eg) st_release_sys(a.peer_flag[eg], e);
+      *a.epoch = e + 1;
+      *a.done_counter = 0;
+      __threadfence();
+    }
+  }
+}
+
+struct GroupArgs {
+  const int* recv_idx;       // [A][recv_tokens][K]
+  const uint32_t* n2m_flag;  // [A]
+  uint32_t* epoch;           // expected epoch, advanced by the kernel
+  int A, T, K, recv_tokens;
+  int expert_base, experts_local;
+  int block_tok;
+  int pool_rows, max_tok_tiles;
+  uint32_t* row_meta;        // [pool_rows]
+  int4* tile_info;           // [max_tok_tiles]
+  int* counters;             // [0] = num_tok_tiles, [1] = total rows (padded), [2] = routed rows
+  int* expert_counts;        // [experts_local] (for load statistics), may be null
+  uint64_t timeout_ns;
+  int* status;
+};
+
+// One CTA. Shared memory: 3 * experts_local ints.
+__global__ void eg_group_kernel(const GroupArgs a) {
+  extern __shared__ int sm[];
+  int* cnt = sm;
+  int* off = sm + a.experts_local;
+  int* cur = sm + 2 * a.experts_local;
+  __shared__ uint32_t s_epoch;
+  if (threadIdx.x == 0) s_epoch = *a.epoch;
+  for (int e = threadIdx.x; e < a.experts_local; e += blockDim.x) {
+    cnt[e] = 0;
+    cur[e] = 0;
+  }
+  __syncthreads();
+  if (threadIdx.x < a.A) wait_flag_ge(a.n2m_flag + threadIdx.x, s_epoch, a.timeout_ns, a.status);
+  __syncthreads();
+  const int per_src = a.T * a.K;
+  const int total = a.A * per_src;
+  for (int i = threadIdx.x; i < total; i += blockDim.x) {
+    const int src = i / per_src, r = i - src * per_src;
+    const int e = a.recv_idx[static_cast<size_t>(src) * a.recv_tokens * a.K + r] - a.expert_base;
+    if (e >= 0 && e < a.experts_local) atomicAdd(&cnt[e], 1);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int rows = 0, tiles = 0, routed = 0;
+    for (int e = 0; e < a.experts_local; ++e) {
+      const int c = cnt[e];
+      const int nt = (c + a.block_tok - 1) / a.block_tok;
+      off[e] = rows;
+      for (int j = 0; j < nt; ++j) {
+        if (tiles < a.max_tok_tiles) {
+          a.tile_info[tiles] = make_int4(e, rows + j * a.block_tok, min(a.block_tok, c - j * a.block_tok), 0);
+        }
+        ++tiles;
+      }
+      rows += nt * a.block_tok;
+      routed += c;
+      if (a.expert_counts) a.expert_counts[e] = c;
+    }
+    if (tiles > a.max_tok_tiles || rows > a.pool_rows) {
+      set_status(a.status, kStatusCapacity);
+      tiles = min(tiles, a.max_tok_tiles);
+    }
+    a.counters[0] = tiles;
+    a.counters[1] = rows;
+    a.counters[2] = routed;
+    *a.epoch = s_epoch + 1;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < total; i += blockDim.x) {
+    const int src = i / per_src, r = i - src * per_src;
+    const int t = r / a.K, k = r - t * a.K;
+    const int e = a.recv_idx[static_cast<size_t>(src) * a.recv_tokens * a.K + r] - a.expert_base;
+    if (e >= 0 && e < a.experts_local) {
+      const int row = off[e] + atomicAdd(&cur[e], 1);
+      if (row < a.pool_rows) {
+        a.row_meta[row] = (static_cast<uint32_t>(src) << 24) | (static_cast<uint32_t>(k) << 16) |
+                          static_cast<uint32_t>(t);
+      }
+    }
+  }
+  // mark padding rows (never read by the combine epilogue: valid_rows excludes them)
+}
+
+struct GatherArgs {
+  const void* recv_x;          // [A][recv_tokens][H]
+  const float* recv_scale;     // fp8: [A][recv_tokens][H/128]
+  const uint32_t* row_meta;
+  const int4* tile_info;
+  const int* counters;
+  void* pool_x;                // [pool_rows][H]
+  float* pool_scale;           // fp8: [pool_rows][H/128]
+  int recv_tokens, row_bytes, scale_per_row, block_tok, max_tok_tiles;
+};
+
+// One CTA per (token tile); copies the tile's valid rows into the pool.
+__global__ void eg_gather_kernel(const GatherArgs a) {
+  const int ntiles = min(a.counters[0], a.max_tok_tiles);
+  for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+    const int4 ti = a.tile_info[tile];
+    const int vec_per_row = a.row_bytes / 16;
+    for (int idx = threadIdx.x; idx < ti.z * vec_per_row; idx += blockDim.x) {
+      const int r = idx / vec_per_row, v = idx - r * vec_per_row;
+      const int row = ti.y + r;
+      const uint32_t meta = a.row_meta[row];
+      const int src = meta >> 24, tok = meta & 0xffff;
+      const uint4* s = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(a.recv_x) +
+                                                      (static_cast<size_t>(src) * a.recv_tokens + tok) * a.row_bytes);
+      reinterpret_cast<uint4*>(static_cast<uint8_t*>(a.pool_x) + static_cast<size_t>(row) * a.row_bytes)[v] = s[v];
+    }
+    if (a.recv_scale != nullptr) {
+      for (int idx = threadIdx.x; idx < ti.z * a.scale_per_row; idx += blockDim.x) {
+        const int r = idx / a.scale_per_row, v = idx - r * a.scale_per_row;
+        const int row = ti.y + r;
+        const uint32_t meta = a.row_meta[row];
+        const int src = meta >> 24, tok = meta & 0xffff;
+        a.pool_scale[static_cast<size_t>(row) * a.scale_per_row + v] =
+            a.recv_scale[(static_cast<size_t>(src) * a.recv_tokens + tok) * a.scale_per_row + v];
+      }
+    }
+  }
+}
+
+struct CombineArgs {
+  const __nv_bfloat16* combine;   // [K][combine_tokens][H]
+  const float* topk_w;            // [T][K]
+  const int* topk_idx;            // [T][K] (entries < 0 are skipped)
+  const uint32_t* m2n_flag;       // [num_eg]
+  uint32_t* epoch;
+  unsigned int* done_counter;
+  int T, H, K, combine_tokens, num_eg;
+  float scale;                    // routed_scaling_factor
+  const __nv_bfloat16* extra;     // optional [T][H] added to y (shared-expert output)
+  __nv_bfloat16* y;               // [T][H] (may be null when norm outputs are given)
+  // optional fused residual add + RMSNorm of the next block
+  __nv_bfloat16* residual;        // [T][H] in/out
+  const __nv_bfloat16* norm_w;    // [H]
+  __nv_bfloat16* normed;          // [T][H]
+  float eps;
+  int offset1;
+  uint64_t timeout_ns;
+  int* status;
+};
+
+__global__ void ag_combine_kernel(const CombineArgs a) {
+  extern __shared__ float sbuf[];   // H floats + 32
+  float* red = sbuf + a.H;
+  __shared__ uint32_t s_epoch;
+  if (threadIdx.x == 0) s_epoch = *a.epoch;
+  __syncthreads();
+  if (threadIdx.x < a.num_eg) wait_flag_ge(a.m2n_flag + threadIdx.x, s_epoch, a.timeout_ns, a.status);
+  __syncthreads();
+  const int t = blockIdx.x;
+  float ss = 0.f;
+  for (int i = threadIdx.x * 8; i < a.H; i += blockDim.x * 8) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    for (int k = 0; k < a.K; ++k) {
+      if (a.topk_idx != nullptr && a.topk_idx[static_cast<size_t>(t) * a.K + k] < 0) continue;
+      const float w = a.topk_w[static_cast<size_t>(t) * a.K + k];
+      const uint4 raw = *reinterpret_cast<const uint4*>(
+          a.combine + (static_cast<size_t>(k) * a.combine_tokens + t) * a.H + i);
+      const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(b2[j]);
+        acc[2 * j] = fmaf(w, f.x, acc[2 * j]);
+        acc[2 * j + 1] = fmaf(w, f.y, acc[2 * j + 1]);
+      }
+    }
+    uint4 oraw;
+    __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&oraw);
+    uint4 eraw = make_uint4(0, 0, 0, 0);
+    if (a.extra) eraw = *reinterpret_cast<const uint4*>(a.extra + static_cast<size_t>(t) * a.H + i);
+    const __nv_bfloat162* e2 = reinterpret_cast<const __nv_bfloat162*>(&eraw);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float vx = acc[2 * j] * a.scale, vy = acc[2 * j + 1] * a.scale;
+      if (a.extra) {
+        const float2 f = __bfloat1622float2(e2[j]);
+        vx += f.x;
+        vy += f.y;
+      }
+      o2[j] = __floats2bfloat162_rn(vx, vy);
+    }
+    if (a.y) *reinterpret_cast<uint4*>(a.y + static_cast<size_t>(t) * a.H + i) = oraw;
+    if (a.residual) {
+      uint4 rraw = *reinterpret_cast<const uint4*>(a.residual + static_cast<size_t>(t) * a.H + i);
+      __nv_bfloat162* r2 = reinterpret_cast<__nv_bfloat162*>(&rraw);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 yv = __bfloat1622float2(o2[j]);
+        float2 rv = __bfloat1622float2(r2[j]);
+        rv.x += yv.x;
+        rv.y += yv.y;
+        r2[j] = __floats2bfloat162_rn(rv.x, rv.y);
+        rv = __bfloat1622float2(r2[j]);
+        sbuf[i + 2 * j] = rv.x;
+        sbuf[i + 2 * j + 1] = rv.y;
+        ss += rv.x * rv.x + rv.y * rv.y;
+      }
+      *reinterpret_cast<uint4*>(a.residual + static_cast<size_t>(t) * a.H + i) = rraw;
+    }
+  }
+  if (a.residual && a.normed) {
+    ss = warp_sum(ss);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) red[warp] = ss;
+    __syncthreads();
+    float tot = lane < (blockDim.x >> 5) ? red[lane] : 0.f;
+    tot = warp_sum(tot);
+    const float inv = rsqrtf(tot / a.H + a.eps);
+    for (int i = threadIdx.x * 8; i < a.H; i += blockDim.x * 8) {
+      const uint4 wraw = *reinterpret_cast<const uint4*>(a.norm_w + i);
+      const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&wraw);
+      uint4 oraw;
+      __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&oraw);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        float2 g = __bfloat1622float2(w2[j]);
+        if (a.offset1) {
+          g.x += 1.f;
+          g.y += 1.f;
+        }
+        o2[j] = __floats2bfloat162_rn(sbuf[i + 2 * j] * inv * g.x, sbuf[i + 2 * j + 1] * inv * g.y);
+      }
+      *reinterpret_cast<uint4*>(a.normed + static_cast<size_t>(t) * a.H + i) = oraw;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned int prev = atomicAdd(a.done_counter, 1u);
+    if (prev == gridDim.x - 1) {
+      *a.epoch = s_epoch + 1;
+      *a.done_counter = 0;
+      __threadfence();
+    }
+  }
+}
+
+// A bounded wait on one flag as a kernel of its own: used by tests (a flag that
+// nothing sets must come back as a timeout status, with the context intact) and
+// by the host runtime to order a stream after a peer's signal.
+__global__ void wait_flag_kernel(const uint32_t* flag, uint32_t target, uint64_t timeout_ns, int* status) {
+  if (threadIdx.x == 0) wait_flag_ge(flag, target, timeout_ns, status);
+}
+__global__ void set_flag_kernel(uint32_t* flag, uint32_t value) {
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    st_release_sys(flag, value);
+  }
+}
+
+}  // namespace afd
+
+using namespace afd;
+
+struct AfdDispatchDesc {
+  const void* x; const void* topk_idx;
+  int T, H, K, src_rank, num_eg, experts_per_eg, fp8, recv_tokens;
+  void* peer_recv_x[kMaxRanks]; void* peer_recv_scale[kMaxRanks]; void* peer_recv_idx[kMaxRanks];
+  void* peer_flag[kMaxRanks];
+  void* epoch; void* done_counter; void* status;
+};
+
+extern "C" int afd_dispatch_push(const AfdDispatchDesc* d, void* stream) {
+  if (d->T == 0) return -1;   // a lane always pushes at least its padding tokens
+  if (d->num_eg > kMaxRanks || d->H % 128 != 0 || d->K > 32 || d->T > d->recv_tokens) return -2;
+  DispatchArgs a{};
+  a.x = static_cast<const __nv_bfloat16*>(d->x);
+  a.topk_idx = static_cast<const int*>(d->topk_idx);
+  a.T = d->T; a.H = d->H; a.K = d->K; a.src_rank = d->src_rank; a.num_eg = d->num_eg;
+  a.experts_per_eg = d->experts_per_eg; a.fp8 = d->fp8; a.recv_tokens = d->recv_tokens;
+  for (int i = 0; i < d->num_eg; ++i) {
+    a.peer_recv_x[i] = d->peer_recv_x[i];
+    a.peer_recv_scale[i] = static_cast<float*>(d->peer_recv_scale[i]);
+    a.peer_recv_idx[i] = static_cast<int*>(d->peer_recv_idx[i]);
+    a.peer_flag[i] = static_cast<uint32_t*>(d->peer_flag[i]);
+  }
+  a.epoch = static_cast<uint32_t*>(d->epoch);
+  a.done_counter = static_cast<unsigned int*>(d->done_counter);
+  a.status = static_cast<int*>(d->status);
+  dispatch_push_kernel<<<d->T, 256, 0, static_cast<cudaStream_t>(stream)>>>(a);
+  AFD_CHECK_LAUNCH();
+  return 0;
+}
+
+struct AfdGroupDesc {
+  const void* recv_idx; const void* n2m_flag; void* epoch;
+  int A, T, K, recv_tokens, expert_base, experts_local, block_tok, pool_rows, max_tok_tiles;
+  void* row_meta; void* tile_info; void* counters; void* expert_counts;
+  unsigned long long timeout_ns;
+  void* status;
+  // gather
+  const void* recv_x; const void* recv_scale; void* pool_x; void* pool_scale;
+  int row_bytes, scale_per_row;
+};
+
+extern "C" int afd_eg_group_gather(const AfdGroupDesc* d, void* stream) {
+  if (d->A > kMaxRanks || d->A > 1024 || d->T > 65535 || d->K > 255) return -1;
+  if (d->row_bytes % 16 != 0) return -2;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  GroupArgs g{};
+  g.recv_idx = static_cast<const int*>(d->recv_idx);
+  g.n2m_flag = static_cast<const uint32_t*>(d->n2m_flag);
+  g.epoch = static_cast<uint32_t*>(d->epoch);
+  g.A = d->A; g.T = d->T; g.K = d->K; g.recv_tokens = d->recv_tokens;
+  g.expert_base = d->expert_base; g.experts_local = d->experts_local; g.block_tok = d->block_tok;
+  g.pool_rows = d->pool_rows; g.max_tok_tiles = d->max_tok_tiles;
+  g.row_meta = static_cast<uint32_t*>(d->row_meta);
+  g.tile_info = static_cast<int4*>(d->tile_info);
+  g.counters = static_cast<int*>(d->counters);
+  g.expert_counts = static_cast<int*>(d->expert_counts);
+  g.timeout_ns = d->timeout_ns;
+  g.status = static_cast<int*>(d->status);
+  eg_group_kernel<<<1, 1024, 3 * d->experts_local * sizeof(int), st>>>(g);
+  AFD_CHECK_LAUNCH();
+  GatherArgs ga{};
+  ga.recv_x = d->recv_x; ga.recv_scale = static_cast<const float*>(d->recv_scale);
+  ga.row_meta = g.row_meta; ga.tile_info = g.tile_info; ga.counters = g.counters;
+  ga.pool_x = d->pool_x; ga.pool_scale = static_cast<float*>(d->pool_scale);
+  ga.recv_tokens = d->recv_tokens; ga.row_bytes = d->row_bytes; ga.scale_per_row = d->scale_per_row;
+  ga.block_tok = d->block_tok; ga.max_tok_tiles = d->max_tok_tiles;
+  const int grid = d->max_tok_tiles < 592 ? d->max_tok_tiles : 592;
+  eg_gather_kernel<<<grid, 256, 0, st>>>(ga);
+  AFD_CHECK_LAUNCH();
+  return 0;
+}
+
+struct AfdCombineDesc {
+  const void* combine; const void* topk_w; const void* topk_idx; const void* m2n_flag;
+  void* epoch; void* done_counter;
+  int T, H, K, combine_tokens, num_eg;
+  float scale;
+  const void* extra; void* y; void* residual; const void* norm_w; void* normed;
+  float eps; int offset1;
+  unsigned long long timeout_ns;
+  void* status;
+};
+
+extern "C" int afd_ag_combine(const AfdCombineDesc* d, void* stream) {
+  if (d->T == 0) return -1;
+  if (d->H % 8 != 0 || d->num_eg > kMaxRanks) return -2;
+  CombineArgs a{};
+  a.combine = static_cast<const __nv_bfloat16*>(d->combine);
+  a.topk_w = static_cast<const float*>(d->topk_w);
+  a.topk_idx = static_cast<const int*>(d->topk_idx);
+  a.m2n_flag = static_cast<const uint32_t*>(d->m2n_flag);
+  a.epoch = static_cast<uint32_t*>(d->epoch);
+  a.done_counter = static_cast<unsigned int*>(d->done_counter);
+  a.T = d->T; a.H = d->H; a.K = d->K; a.combine_tokens = d->combine_tokens; a.num_eg = d->num_eg;
+  a.scale = d->scale;
+  a.extra = static_cast<const __nv_bfloat16*>(d->extra);
+  a.y = static_cast<__nv_bfloat16*>(d->y);
+  a.residual = static_cast<__nv_bfloat16*>(d->residual);
+  a.norm_w = static_cast<const __nv_bfloat16*>(d->norm_w);
+  a.normed = static_cast<__nv_bfloat16*>(d->normed);
+  a.eps = d->eps; a.offset1 = d->offset1; a.timeout_ns = d->timeout_ns;
+  a.status = static_cast<int*>(d->status);
+  const int threads = d->H / 8 >= 512 ? 512 : 256;
+  ag_combine_kernel<<<d->T, threads, (d->H + 32) * sizeof(float), static_cast<cudaStream_t>(stream)>>>(a);
+  AFD_CHECK_LAUNCH();
+  return 0;
+}
+
+extern "C" int afd_wait_flag(const void* flag, unsigned int target, unsigned long long timeout_ns,
+                             void* status, void* stream) {
+  wait_flag_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint32_t*>(flag), target, timeout_ns, static_cast<int*>(status));
+  AFD_CHECK_LAUNCH();
+  return 0;
+}
+
+extern "C" int afd_set_flag(void* flag, unsigned int value, void* stream) {
+  set_flag_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(static_cast<uint32_t*>(flag), value);
+  AFD_CHECK_LAUNCH();
+  return 0;
+}

@@ -1,0 +1,233 @@
+"""Attention-side and expert-side endpoints of the fused N2M / M2N exchange (CUDA).
+
+One *lane* per micro-batch. The attention endpoint pushes routed rows into the expert
+GPUs' receive slots (optionally quantising to FP8 on the way) and later reduces the
+top-k rows that the expert GPUs' down-projection epilogues stored into its combine
+buffer. The expert endpoint waits for all attention ranks, groups rows by expert and
+runs the two tcgen05 grouped GEMMs; the second one writes over NVLink.
+
+Role parity with the reference: ``MegaMoEM2NAfdAdapter.ag_moe`` / ``eg_moe``
+(python/minisgl/moe/megamoe_m2n_afd.py:336-470,755-911). Unlike the reference there is
+no hidden % 512 / intermediate % 512 restriction: hidden % 128 == 0 and
+intermediate % 128 == 0 (bf16: % 64) suffice.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+from dataclasses import dataclass
+from typing import List, Optional
+
+import torch
+
+from ..ops import EPI_COMBINE, EPI_SWIGLU, NUM_SMS, grouped_gemm
+from ..ops._lib import CombineDesc, DispatchDesc, GroupDesc, check, cur_stream, lib, ptr
+from ..parallel.fabric import Fabric, Layout
+
+DEFAULT_TIMEOUT_NS = int(float(os.environ.get("FASTAFD_FLAG_TIMEOUT_S", "20")) * 1e9)
+
+
+@dataclass(frozen=True)
+class MoeCommConfig:
+    num_ag: int              # attention ranks (dispatch sources)
+    num_eg: int              # expert ranks
+    num_lanes: int           # micro-batches in flight
+    max_tokens: int          # tokens per attention rank per lane (receive capacity)
+    hidden: int
+    topk: int
+    num_experts: int         # global routed experts (padded to a multiple of num_eg)
+    intermediate: int
+    fp8: bool = False
+    block_tok: int = 32
+
+    @property
+    def experts_per_eg(self) -> int:
+        return (self.num_experts + self.num_eg - 1) // self.num_eg
+
+    @property
+    def row_bytes(self) -> int:
+        return self.hidden * (1 if self.fp8 else 2)
+
+    @property
+    def pool_rows(self) -> int:
+        k_eff = min(self.topk, self.experts_per_eg)
+        return self.num_ag * self.max_tokens * k_eff + self.experts_per_eg * self.block_tok
+
+    @property
+    def max_tok_tiles(self) -> int:
+        k_eff = min(self.topk, self.experts_per_eg)
+        return (self.num_ag * self.max_tokens * k_eff + self.block_tok - 1) // self.block_tok + self.experts_per_eg
+
+
+def ag_layout(cfg: MoeCommConfig) -> Layout:
+    lay = Layout()
+    for lane in range(cfg.num_lanes):
+        lay.add(f"combine{lane}", cfg.topk * cfg.max_tokens * cfg.hidden * 2)
+        lay.add(f"m2n_flag{lane}", 4 * cfg.num_eg)
+    return lay
+
+
+def eg_layout(cfg: MoeCommConfig) -> Layout:
+    lay = Layout()
+    for lane in range(cfg.num_lanes):
+        lay.add(f"recv_x{lane}", cfg.num_ag * cfg.max_tokens * cfg.row_bytes)
+        lay.add(f"recv_scale{lane}", cfg.num_ag * cfg.max_tokens * (cfg.hidden // 128) * 4)
+        lay.add(f"recv_idx{lane}", cfg.num_ag * cfg.max_tokens * cfg.topk * 4)
+        lay.add(f"n2m_flag{lane}", 4 * cfg.num_ag)
+    return lay
+
+
+class _LaneWords:
+    """Small device words a lane's kernels keep between launches."""
+
+    def __init__(self, device):
+        self.words = torch.zeros(8, dtype=torch.int32, device=device)
+        self.words[0] = 1  # epoch to publish / expect next (flags start at 0)
+        self.words[2] = 1  # second epoch (expert side: publish epoch)
+        self.epoch = self.words[0:1]
+        self.done = self.words[1:2]
+        self.epoch2 = self.words[2:3]
+        self.done2 = self.words[3:4]
+
+
+class AgMoeEndpoint:
+    """Attention rank `ag_index`: dispatch_push + combine over the fabric.
+
+    `fabric.bases` is indexed by global rank; `eg_ranks[i]` is the global rank of expert
+    GPU i."""
+
+    def __init__(self, cfg: MoeCommConfig, fabric: Fabric, ag_index: int, eg_ranks: List[int],
+                 device: torch.device, timeout_ns: int = DEFAULT_TIMEOUT_NS):
+        self.cfg, self.fabric, self.ag_index, self.eg_ranks, self.device = cfg, fabric, ag_index, eg_ranks, device
+        self.timeout_ns = timeout_ns
+        self.lay, self.eg_lay = ag_layout(cfg), eg_layout(cfg)
+        self.status = torch.zeros(1, dtype=torch.int32, device=device)
+        self.lanes = [_LaneWords(device) for _ in range(cfg.num_lanes)]
+        heap = fabric.heap
+        self.combine = [heap.view(self.lay.offset(f"combine{l}"), (cfg.topk, cfg.max_tokens, cfg.hidden),
+                                  torch.bfloat16) for l in range(cfg.num_lanes)]
+        self.m2n_flag = [heap.view(self.lay.offset(f"m2n_flag{l}"), (cfg.num_eg,), torch.int32)
+                         for l in range(cfg.num_lanes)]
+        self._dispatch_desc = [self._make_dispatch_desc(l) for l in range(cfg.num_lanes)]
+
+    def _make_dispatch_desc(self, lane: int) -> DispatchDesc:
+        cfg, d = self.cfg, DispatchDesc()
+        d.H, d.K, d.src_rank, d.num_eg = cfg.hidden, cfg.topk, self.ag_index, cfg.num_eg
+        d.experts_per_eg, d.fp8, d.recv_tokens = cfg.experts_per_eg, int(cfg.fp8), cfg.max_tokens
+        for i, r in enumerate(self.eg_ranks):
+            d.peer_recv_x[i] = self.fabric.peer_ptr(r, self.eg_lay.offset(f"recv_x{lane}"))
+            d.peer_recv_scale[i] = self.fabric.peer_ptr(r, self.eg_lay.offset(f"recv_scale{lane}"))
+            d.peer_recv_idx[i] = self.fabric.peer_ptr(r, self.eg_lay.offset(f"recv_idx{lane}"))
+            d.peer_flag[i] = self.fabric.peer_ptr(r, self.eg_lay.offset(f"n2m_flag{lane}")) + 4 * self.ag_index
+        w = self.lanes[lane]
+        d.epoch, d.done_counter, d.status = ptr(w.epoch), ptr(w.done), ptr(self.status)
+        return d
+
+    def dispatch(self, lane: int, x: torch.Tensor, topk_idx: torch.Tensor) -> None:
+        """Push x [T,H] bf16 (rows of tokens routed to each expert GPU) and the top-k ids."""
+        d = self._dispatch_desc[lane]
+        assert x.is_contiguous() and topk_idx.is_contiguous() and topk_idx.dtype == torch.int32
+        d.x, d.topk_idx, d.T = ptr(x), ptr(topk_idx), x.shape[0]
+        check(lib().afd_dispatch_push(C.byref(d), cur_stream()), "dispatch_push")
+
+    def combine_reduce(self, lane: int, topk_w: torch.Tensor, topk_idx: Optional[torch.Tensor], T: int,
+                       scale: float = 1.0, extra: Optional[torch.Tensor] = None,
+                       y: Optional[torch.Tensor] = None, residual: Optional[torch.Tensor] = None,
+                       norm_w: Optional[torch.Tensor] = None, normed: Optional[torch.Tensor] = None,
+                       eps: float = 1e-6, offset1: bool = False):
+        """Wait for every expert GPU's M2N flag, then y[t] = scale * sum_k w[t,k] * combine[k][t]
+        (+ extra). With residual/norm_w/normed also residual += y; normed = rmsnorm(residual)."""
+        cfg, d = self.cfg, CombineDesc()
+        w = self.lanes[lane]
+        d.combine, d.topk_w, d.topk_idx = ptr(self.combine[lane]), ptr(topk_w), ptr(topk_idx)
+        d.m2n_flag, d.epoch, d.done_counter = ptr(self.m2n_flag[lane]), ptr(w.epoch2), ptr(w.done2)
+        d.T, d.H, d.K, d.combine_tokens, d.num_eg = T, cfg.hidden, cfg.topk, cfg.max_tokens, cfg.num_eg
+        d.scale = scale
+        if y is None and normed is None:
+            y = torch.empty(T, cfg.hidden, dtype=torch.bfloat16, device=self.device)
+        d.extra, d.y, d.residual, d.norm_w, d.normed = ptr(extra), ptr(y), ptr(residual), ptr(norm_w), ptr(normed)
+        d.eps, d.offset1, d.timeout_ns, d.status = eps, int(offset1), self.timeout_ns, ptr(self.status)
+        check(lib().afd_ag_combine(C.byref(d), cur_stream()), "ag_combine")
+        return y if normed is None else normed
+
+
+class EgMoeEndpoint:
+    """Expert rank `eg_index`: wait + group + gather, SwiGLU grouped GEMM, down grouped GEMM
+    with the M2N store epilogue."""
+
+    def __init__(self, cfg: MoeCommConfig, fabric: Fabric, eg_index: int, ag_ranks: List[int],
+                 device: torch.device, timeout_ns: int = DEFAULT_TIMEOUT_NS, grid: int = NUM_SMS):
+        self.cfg, self.fabric, self.eg_index, self.ag_ranks, self.device = cfg, fabric, eg_index, ag_ranks, device
+        self.timeout_ns, self.grid = timeout_ns, grid
+        self.lay, self.ag_lay = eg_layout(cfg), ag_layout(cfg)
+        self.status = torch.zeros(1, dtype=torch.int32, device=device)
+        self.lanes = [_LaneWords(device) for _ in range(cfg.num_lanes)]
+        heap, L = fabric.heap, cfg.num_lanes
+        xdt = torch.float8_e4m3fn if cfg.fp8 else torch.bfloat16
+        self.recv_x = [heap.view(self.lay.offset(f"recv_x{l}"), (cfg.num_ag, cfg.max_tokens, cfg.hidden), xdt)
+                       for l in range(L)]
+        self.recv_scale = [heap.view(self.lay.offset(f"recv_scale{l}"),
+                                     (cfg.num_ag, cfg.max_tokens, cfg.hidden // 128), torch.float32) for l in range(L)]
+        self.recv_idx = [heap.view(self.lay.offset(f"recv_idx{l}"), (cfg.num_ag, cfg.max_tokens, cfg.topk),
+                                   torch.int32) for l in range(L)]
+        self.n2m_flag = [heap.view(self.lay.offset(f"n2m_flag{l}"), (cfg.num_ag,), torch.int32) for l in range(L)]
+        R, I = cfg.pool_rows, cfg.intermediate
+        # Pools are shared by the lanes: a lane's layer runs to completion on one stream.
+        self.pool_x = torch.zeros(R, cfg.hidden, dtype=xdt, device=device)
+        self.pool_xs = torch.ones(R, cfg.hidden // 128, dtype=torch.float32, device=device) if cfg.fp8 else None
+        self.pool_h = torch.zeros(R, I, dtype=xdt, device=device)
+        self.pool_hs = torch.ones(R, max(I // 128, 1), dtype=torch.float32, device=device) if cfg.fp8 else None
+        self.row_meta = torch.zeros(R, dtype=torch.int32, device=device)
+        self.tile_info = torch.zeros(cfg.max_tok_tiles, 4, dtype=torch.int32, device=device)
+        self.counters = torch.zeros(4, dtype=torch.int32, device=device)
+        self.expert_counts = torch.zeros(cfg.experts_per_eg, dtype=torch.int32, device=device)
+        self.expert_base = eg_index * cfg.experts_per_eg
+        self.experts_local = cfg.experts_per_eg
+        self.peer_combine = [[fabric.peer_ptr(r, self.ag_lay.offset(f"combine{l}")) for r in ag_ranks] for l in range(L)]
+        self.peer_flag = [[fabric.peer_ptr(r, self.ag_lay.offset(f"m2n_flag{l}")) + 4 * eg_index for r in ag_ranks]
+                          for l in range(L)]
+
+    def group_gather(self, lane: int, T: int) -> None:
+        cfg, d = self.cfg, GroupDesc()
+        w = self.lanes[lane]
+        d.recv_idx, d.n2m_flag, d.epoch = ptr(self.recv_idx[lane]), ptr(self.n2m_flag[lane]), ptr(w.epoch)
+        d.A, d.T, d.K, d.recv_tokens = cfg.num_ag, T, cfg.topk, cfg.max_tokens
+        d.expert_base, d.experts_local, d.block_tok = self.expert_base, self.experts_local, cfg.block_tok
+        d.pool_rows, d.max_tok_tiles = cfg.pool_rows, cfg.max_tok_tiles
+        d.row_meta, d.tile_info, d.counters = ptr(self.row_meta), ptr(self.tile_info), ptr(self.counters)
+        d.expert_counts, d.timeout_ns, d.status = ptr(self.expert_counts), self.timeout_ns, ptr(self.status)
+        d.recv_x, d.recv_scale = ptr(self.recv_x[lane]), ptr(self.recv_scale[lane]) if cfg.fp8 else None
+        d.pool_x, d.pool_scale = ptr(self.pool_x), ptr(self.pool_xs)
+        d.row_bytes, d.scale_per_row = cfg.row_bytes, cfg.hidden // 128
+        check(lib().afd_eg_group_gather(C.byref(d), cur_stream()), "eg_group_gather")
+
+    def run_layer(self, lane: int, T: int, w13: torch.Tensor, w2: torch.Tensor,
+                  w13_scale: Optional[torch.Tensor] = None, w2_scale: Optional[torch.Tensor] = None) -> None:
+        """One MoE layer for one lane. w13: [E_local, 2I, H] gate/up interleaved (see
+        ops.interleave_gate_up); w2: [E_local, H, I]. FP8 mode takes per-tile scales."""
+        cfg = self.cfg
+        self.group_gather(lane, T)
+        ntiles = self.counters[0:1]
+        grouped_gemm(w=w13, x=self.pool_x, num_experts=self.experts_local, n_per_expert=2 * cfg.intermediate,
+                     k=cfg.hidden, tile_info=self.tile_info, num_tok_tiles=ntiles, block_tok=cfg.block_tok,
+                     epilogue=EPI_SWIGLU, out=None if cfg.fp8 else self.pool_h, out_ld=cfg.intermediate,
+                     fp8=cfg.fp8, x_scale=self.pool_xs, w_scale=w13_scale,
+                     out_q=self.pool_h if cfg.fp8 else None, out_scale=self.pool_hs,
+                     status=self.status, grid=self.grid)
+        w = self.lanes[lane]
+        grouped_gemm(w=w2, x=self.pool_h, num_experts=self.experts_local, n_per_expert=cfg.hidden,
+                     k=cfg.intermediate, tile_info=self.tile_info, num_tok_tiles=ntiles,
+                     block_tok=cfg.block_tok, epilogue=EPI_COMBINE, fp8=cfg.fp8, x_scale=self.pool_hs,
+                     w_scale=w2_scale, row_meta=self.row_meta, peer_combine=self.peer_combine[lane],
+                     peer_flag=self.peer_flag[lane], combine_tokens=cfg.max_tokens, hidden=cfg.hidden,
+                     epoch=w.epoch2, done_counter=w.done2, status=self.status, grid=self.grid)
+
+
+def check_status(status: torch.Tensor, what: str) -> None:
+    """Raise if a kernel recorded a timeout / bounds / capacity code (host sync)."""
+    code = int(status.item())
+    if code != 0:
+        names = {1: "mbarrier wait timed out", 2: "peer flag wait timed out",
+                 3: "index out of bounds (access skipped)", 4: "capacity exceeded"}
+        status.zero_()
+        raise RuntimeError(f"{what}: device status {code} ({names.get(code, 'unknown')})")

@@ -1,0 +1,230 @@
+"""Operator surface. CUDA tensors go to the sm_100a kernel library; CPU tensors go to the
+PyTorch oracle in :mod:`fastafd_b200.reference.ops_ref` (CPU/gloo runs and tests).
+
+There is one CUDA implementation per op and no backend selection: a CUDA tensor on a
+machine without the built library raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from typing import Optional
+
+import torch
+
+from ..reference import ops_ref as ref
+from . import _lib
+from ._lib import GroupedGemmDesc, check, cur_stream, lib, ptr
+
+EPI_STORE, EPI_SWIGLU, EPI_COMBINE = 0, 1, 2
+NUM_SMS = 148
+
+
+# ----------------------------------------------------------------------------- norms
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, offset1: bool = False,
+            out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    if not x.is_cuda:
+        return ref.rmsnorm(x, w, eps, offset1)
+    x2 = x.reshape(-1, x.shape[-1])
+    out = torch.empty_like(x2) if out is None else out
+    check(lib().afd_rmsnorm(ptr(x2), None, ptr(w), ptr(out), x2.shape[0], x2.shape[1], eps,
+                            int(offset1), cur_stream()), "rmsnorm")
+    return out.view(x.shape)
+
+
+def add_rmsnorm(x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, eps: float,
+                offset1: bool = False, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """residual <- x + residual in place; returns rmsnorm(residual) * w."""
+    if not x.is_cuda:
+        return ref.add_rmsnorm(x, residual, w, eps, offset1)
+    out = torch.empty_like(x) if out is None else out
+    check(lib().afd_rmsnorm(ptr(x), ptr(residual), ptr(w), ptr(out), x.shape[0], x.shape[1], eps,
+                            int(offset1), cur_stream()), "add_rmsnorm")
+    return out
+
+
+def qk_norm_rope_store(qkv, qw, kw, cos_sin, positions, out_loc, k_cache, v_cache, Hq, Hkv, D,
+                       rot_dim, eps, status=None):
+    """In place on qkv [T, (Hq+2Hkv)*D]: per-head RMSNorm of q/k (when weights given), NeoX
+    RoPE, and a store of k/v into the paged cache ([slots,Hkv,D]) at out_loc (-1 skips)."""
+    if not qkv.is_cuda:
+        return ref.qk_norm_rope_store(qkv, qw, kw, cos_sin, positions, out_loc, k_cache, v_cache,
+                                      Hq, Hkv, D, rot_dim, eps)
+    T = qkv.shape[0]
+    slots = k_cache.shape[0] if k_cache is not None else 0
+    check(lib().afd_qk_norm_rope_store(ptr(qkv), ptr(qw), ptr(kw), ptr(cos_sin), ptr(positions),
+                                       ptr(out_loc), ptr(k_cache), ptr(v_cache), T, Hq, Hkv, D,
+                                       rot_dim, eps, cos_sin.shape[0], slots, ptr(status),
+                                       cur_stream()), "qk_norm_rope_store")
+    return qkv
+
+
+def embedding(ids: torch.Tensor, table: torch.Tensor, vocab_start: int = 0,
+              out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Rows of `table` for ids in [vocab_start, vocab_start + rows); zeros elsewhere."""
+    if not table.is_cuda:
+        local = ids.long() - vocab_start
+        ok = (local >= 0) & (local < table.shape[0])
+        res = table[local.clamp(0, table.shape[0] - 1)]
+        return torch.where(ok[:, None], res, torch.zeros_like(res))
+    T, H = ids.shape[0], table.shape[1]
+    out = torch.empty(T, H, dtype=table.dtype, device=table.device) if out is None else out
+    check(lib().afd_embedding(ptr(ids), ptr(table), ptr(out), T, H, vocab_start,
+                              vocab_start + table.shape[0], cur_stream()), "embedding")
+    return out
+
+
+def silu_mul(gate_up: torch.Tensor) -> torch.Tensor:
+    if not gate_up.is_cuda:
+        return ref.silu_mul(gate_up)
+    rows, I2 = gate_up.shape
+    out = torch.empty(rows, I2 // 2, dtype=gate_up.dtype, device=gate_up.device)
+    check(lib().afd_silu_mul(ptr(gate_up), ptr(out), rows, I2 // 2, cur_stream()), "silu_mul")
+    return out
+
+
+def topk_route(logits: torch.Tensor, bias: Optional[torch.Tensor], K: int, scoring: str = "softmax",
+               renorm: bool = True, scale: float = 1.0, out_idx=None, out_w=None):
+    """Router scoring + top-k. logits fp32 [T,E]. Returns (idx int32 [T,K], w fp32 [T,K])."""
+    if not logits.is_cuda:
+        return ref.topk_route(logits, bias, K, scoring, renorm, scale)
+    T, E = logits.shape
+    logits = logits.float().contiguous() if logits.dtype != torch.float32 else logits
+    idx = torch.empty(T, K, dtype=torch.int32, device=logits.device) if out_idx is None else out_idx
+    w = torch.empty(T, K, dtype=torch.float32, device=logits.device) if out_w is None else out_w
+    check(lib().afd_topk_route(ptr(logits), ptr(bias), ptr(idx), ptr(w), T, E, K,
+                               0 if scoring == "softmax" else 1, int(renorm), scale, cur_stream()),
+          "topk_route")
+    return idx, w
+
+
+def argmax(logits: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    if not logits.is_cuda:
+        return ref.argmax_lowest(logits)
+    T, V = logits.shape
+    out = torch.empty(T, dtype=torch.int32, device=logits.device) if out is None else out
+    if logits.dtype not in (torch.bfloat16, torch.float32):
+        logits = logits.float()
+    check(lib().afd_argmax(ptr(logits), ptr(out), T, V, logits.stride(0),
+                           int(logits.dtype == torch.bfloat16), cur_stream()), "argmax")
+    return out
+
+
+def group_quant_fp8(x: torch.Tensor, group: int = 128, pow2: bool = False):
+    if not x.is_cuda:
+        return ref.group_quant_fp8(x, group, pow2)
+    rows, H = x.shape
+    q = torch.empty(rows, H, dtype=torch.float8_e4m3fn, device=x.device)
+    s = torch.empty(rows, H // group, dtype=torch.float32, device=x.device)
+    check(lib().afd_group_quant_fp8(ptr(x), ptr(q), ptr(s), rows, H, group, int(pow2), cur_stream()),
+          "group_quant_fp8")
+    return q, s
+
+
+# ------------------------------------------------------------------------- attention
+def decode_attn_workspace(B, Hq, Hkv, q_len, D, splits, device) -> Optional[torch.Tensor]:
+    if splits <= 1:
+        return None
+    n = lib().afd_decode_attn_workspace_bytes(B, Hq, Hkv, q_len, D, splits)
+    return torch.empty(n, dtype=torch.uint8, device=device)
+
+
+def pick_attn_splits(B: int, Hkv: int, m_tiles: int, max_kv: int, tok_tile: int = 32) -> int:
+    """Enough KV splits to fill the SMs about twice, never finer than 4 tiles per split."""
+    ctas = max(1, B * Hkv * m_tiles)
+    want = max(1, (2 * NUM_SMS + ctas - 1) // ctas)
+    cap = max(1, max_kv // (tok_tile * 4 * 4))
+    return max(1, min(want, cap, 32))
+
+
+def decode_attention(q, k_cache, v_cache, page_table, seq_lens, Hq, Hkv, D, q_len, page_size,
+                     sm_scale, splits: int = 1, workspace=None, out=None, status=None):
+    """Paged GQA decode attention. q [B*q_len, Hq, D] bf16; caches [slots, Hkv, D]."""
+    if not q.is_cuda:
+        return ref.decode_attention(q, k_cache, v_cache, page_table, seq_lens, Hq, Hkv, D, q_len,
+                                    page_size, sm_scale)
+    B = seq_lens.shape[0]
+    out = torch.empty_like(q) if out is None else out
+    if splits > 1 and workspace is None:
+        workspace = decode_attn_workspace(B, Hq, Hkv, q_len, D, splits, q.device)
+    check(lib().afd_decode_attention(ptr(q), ptr(k_cache), ptr(v_cache), ptr(page_table),
+                                     ptr(seq_lens), ptr(out), ptr(workspace), B, Hq, Hkv, D, q_len,
+                                     page_size, page_table.shape[1], k_cache.shape[0], splits,
+                                     sm_scale, ptr(status), cur_stream()), "decode_attention")
+    return out
+
+
+# ---------------------------------------------------------------------- grouped GEMM
+def interleave_gate_up(w_gate_up: torch.Tensor) -> torch.Tensor:
+    """[E, 2I, H] with gate rows then up rows -> rows interleaved in groups of 16
+    (rows 32b..32b+15 = gate features 16b.., rows 32b+16..32b+31 = up features 16b..),
+    the layout the SWIGLU epilogue of the grouped GEMM expects."""
+    E, I2, H = w_gate_up.shape
+    I = I2 // 2
+    g = w_gate_up[:, :I].reshape(E, I // 16, 16, H)
+    u = w_gate_up[:, I:].reshape(E, I // 16, 16, H)
+    return torch.stack([g, u], dim=2).reshape(E, I2, H).contiguous()
+
+
+def interleave_gate_up_scales(scale: torch.Tensor, I: int, block: int = 128) -> torch.Tensor:
+    """Block scales [E, 2I/128, K/128] of a gate-then-up weight -> per-tile-half scales
+    [E, n_tiles, 2, K/128] for the interleaved layout (half 0 = gate lanes, 1 = up lanes)."""
+    E, _, KB = scale.shape
+    n_tiles = 2 * I // 128
+    gate_blocks = I // block
+    tiles = torch.arange(n_tiles, device=scale.device)
+    feat0 = tiles * 64
+    gb = feat0 // block
+    ub = gate_blocks + gb
+    return torch.stack([scale[:, gb], scale[:, ub]], dim=2).contiguous()
+
+
+def plain_tile_scales(scale: torch.Tensor) -> torch.Tensor:
+    """[E, N/128, K/128] -> [E, n_tiles, 2, K/128] for non-interleaved weights."""
+    return torch.stack([scale, scale], dim=2).contiguous()
+
+
+def dense_tile_schedule(M: int, block_tok: int, device) -> tuple[torch.Tensor, torch.Tensor]:
+    """tile_info / num_tok_tiles for a single-expert (dense) GEMM over M rows."""
+    n = (M + block_tok - 1) // block_tok
+    info = torch.zeros(max(n, 1), 4, dtype=torch.int32)
+    for t in range(n):
+        info[t, 0] = 0
+        info[t, 1] = t * block_tok
+        info[t, 2] = min(block_tok, M - t * block_tok)
+    return info.to(device), torch.tensor([n], dtype=torch.int32, device=device)
+
+
+def grouped_gemm(*, w, x, num_experts, n_per_expert, k, tile_info, num_tok_tiles, block_tok,
+                 epilogue, out=None, out_ld=0, fp8=False, x_scale=None, w_scale=None, out_q=None,
+                 out_scale=None, row_meta=None, peer_combine=(), peer_flag=(), combine_tokens=0,
+                 hidden=0, epoch=None, done_counter=None, status=None, grid=NUM_SMS):
+    """Low-level launcher of the tcgen05 grouped GEMM (see csrc/grouped_gemm.cu)."""
+    d = GroupedGemmDesc()
+    d.w, d.x = ptr(w), ptr(x)
+    d.num_experts, d.n_per_expert, d.k, d.pool_rows = num_experts, n_per_expert, k, x.shape[0]
+    d.block_tok, d.fp8, d.epilogue, d.grid = block_tok, int(fp8), epilogue, grid
+    d.tile_info, d.num_tok_tiles = ptr(tile_info), ptr(num_tok_tiles)
+    d.max_tok_tiles = tile_info.shape[0]
+    d.out, d.out_ld = ptr(out), out_ld
+    d.x_scale, d.w_scale, d.out_q, d.out_scale = ptr(x_scale), ptr(w_scale), ptr(out_q), ptr(out_scale)
+    d.row_meta = ptr(row_meta)
+    for i, p in enumerate(peer_combine):
+        d.peer_combine[i] = p
+    for i, p in enumerate(peer_flag):
+        d.peer_flag[i] = p
+    d.num_peers, d.combine_tokens, d.hidden = len(peer_combine), combine_tokens, hidden
+    d.epoch, d.done_counter, d.status = ptr(epoch), ptr(done_counter), ptr(status)
+    check(lib().afd_grouped_gemm(C.byref(d), cur_stream()), "grouped_gemm")
+
+
+def dense_gemm(x: torch.Tensor, w: torch.Tensor, block_tok: Optional[int] = None, status=None):
+    """out = x @ w.T on the tcgen05 path (bf16, N % 128 == 0, K % 64 == 0)."""
+    M, K = x.shape
+    N = w.shape[0]
+    if block_tok is None:
+        block_tok = 16 if M <= 16 else 32 if M <= 32 else 64 if M <= 64 else 128
+    info, n = dense_tile_schedule(M, block_tok, x.device)
+    out = torch.empty(M, N, dtype=torch.bfloat16, device=x.device)
+    grouped_gemm(w=w, x=x, num_experts=1, n_per_expert=N, k=K, tile_info=info, num_tok_tiles=n,
+                 block_tok=block_tok, epilogue=EPI_STORE, out=out, out_ld=N, status=status)
+    return out

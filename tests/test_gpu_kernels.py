@@ -1,0 +1,162 @@
+"""Numerics of each sm_100a kernel against the PyTorch fp32 oracle of the same op."""
+import math
+
+import pytest
+import torch
+
+from fastafd_b200 import ops
+from fastafd_b200.reference import ops_ref as ref
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _bf(*shape, scale=1.0, seed=0):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    return (torch.randn(*shape, generator=g) * scale).to(torch.bfloat16).to(DEV)
+
+
+@pytest.mark.parametrize("H", [256, 2048, 4096])
+def test_rmsnorm_and_add(H):
+    x, r, w = _bf(37, H, seed=1), _bf(37, H, seed=2), _bf(H, seed=3)
+    out = ops.rmsnorm(x, w, 1e-6)
+    torch.testing.assert_close(out.float(), ref.rmsnorm(x.cpu(), w.cpu(), 1e-6).float().to(DEV), atol=2e-2, rtol=2e-2)
+    r_ref = r.cpu().clone()
+    exp = ref.add_rmsnorm(x.cpu(), r_ref, w.cpu(), 1e-6, offset1=True)
+    r_k = r.clone()
+    got = ops.add_rmsnorm(x, r_k, w, 1e-6, offset1=True)
+    torch.testing.assert_close(r_k.cpu(), r_ref)
+    torch.testing.assert_close(got.float().cpu(), exp.float(), atol=3e-2, rtol=2e-2)
+
+
+@pytest.mark.parametrize("D,rot", [(128, 128), (128, 64), (256, 64), (64, 64)])
+def test_qk_norm_rope_store(D, rot):
+    T, Hq, Hkv, slots = 19, 8, 2, 64
+    qkv = _bf(T, (Hq + 2 * Hkv) * D, seed=4)
+    qw, kw = _bf(D, seed=5) + 1, _bf(D, seed=6) + 1
+    cs = ref.build_cos_sin_cache(512, rot, 1e6).to(DEV)
+    pos = torch.randint(0, 512, (T,), dtype=torch.int32, device=DEV)
+    loc = torch.randperm(slots, device=DEV)[:T].to(torch.int32)
+    loc[3] = -1
+    kc, vc = torch.zeros(slots, Hkv, D, dtype=torch.bfloat16, device=DEV), torch.zeros(slots, Hkv, D, dtype=torch.bfloat16, device=DEV)
+    q_ref, kc_ref, vc_ref = qkv.cpu().clone(), kc.cpu().clone(), vc.cpu().clone()
+    ref.qk_norm_rope_store(q_ref, qw.cpu(), kw.cpu(), cs.cpu(), pos.cpu(), loc.cpu(), kc_ref, vc_ref, Hq, Hkv, D, rot, 1e-6)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    ops.qk_norm_rope_store(qkv, qw, kw, cs, pos, loc, kc, vc, Hq, Hkv, D, rot, 1e-6, status=status)
+    assert int(status) == 0
+    qk_cols = (Hq + Hkv) * D
+    torch.testing.assert_close(qkv.cpu().float()[:, :qk_cols], q_ref.float()[:, :qk_cols], atol=6e-2, rtol=3e-2)
+    torch.testing.assert_close(kc.cpu().float(), kc_ref.float(), atol=6e-2, rtol=3e-2)
+    torch.testing.assert_close(vc.cpu(), vc_ref)
+
+
+@pytest.mark.parametrize("E,K,scoring", [(128, 8, "softmax"), (256, 8, "sigmoid"), (512, 10, "softmax"), (8, 2, "softmax")])
+def test_topk_route(E, K, scoring):
+    T = 45
+    g = torch.Generator().manual_seed(7)
+    logits = torch.randn(T, E, generator=g).to(DEV)
+    bias = (torch.randn(E, generator=g) * 0.1).to(DEV) if scoring == "sigmoid" else None
+    idx, w = ops.topk_route(logits, bias, K, scoring, True, 1.0)
+    ridx, rw = ref.topk_route(logits.cpu(), None if bias is None else bias.cpu(), K, scoring, True, 1.0)
+    assert torch.equal(idx.cpu(), ridx)
+    torch.testing.assert_close(w.cpu(), rw, atol=1e-5, rtol=1e-4)
+
+
+def test_argmax_and_embedding():
+    logits = _bf(9, 151936, seed=8)
+    assert torch.equal(ops.argmax(logits).cpu(), ref.argmax_lowest(logits.cpu()))
+    table = _bf(1000, 256, seed=9)
+    ids = torch.tensor([0, 5, 999, 1000, 77], dtype=torch.int32, device=DEV)
+    out = ops.embedding(ids, table)
+    assert torch.equal(out[:3], table[ids[:3].long()]) and float(out[3].abs().sum()) == 0
+
+
+@pytest.mark.parametrize("group,pow2", [(128, False), (32, True)])
+def test_group_quant_fp8(group, pow2):
+    x = _bf(33, 2048, seed=10)
+    q, s = ops.group_quant_fp8(x, group, pow2)
+    rq, rs = ref.group_quant_fp8(x.cpu(), group, pow2)
+    torch.testing.assert_close(s.cpu(), rs, rtol=1e-6, atol=0)
+    # round-to-nearest of x/scale may differ by one ulp where the division differs; compare dequantised
+    torch.testing.assert_close(ref.group_dequant_fp8(q.cpu(), s.cpu(), group), ref.group_dequant_fp8(rq, rs, group), atol=0.13, rtol=0.07)
+    assert (q.cpu().view(torch.uint8) == rq.view(torch.uint8)).float().mean() > 0.995
+
+
+@pytest.mark.parametrize("Hq,Hkv,D,q_len,page,splits", [
+    (32, 4, 128, 1, 16, 1), (32, 4, 128, 1, 16, 3), (64, 4, 128, 1, 16, 2), (32, 2, 256, 1, 16, 2),
+    (16, 4, 128, 4, 16, 2), (8, 2, 64, 1, 1, 1), (48, 8, 128, 1, 64, 4),
+])
+def test_decode_attention(Hq, Hkv, D, q_len, page, splits):
+    B = 5
+    lens = torch.tensor([1 + q_len, 37, 300, 1025, 513], dtype=torch.int32)[:B]
+    max_pages = (int(lens.max()) + page - 1) // page + 1
+    n_pages = B * max_pages + 3
+    perm = torch.randperm(n_pages)
+    pt = perm[:B * max_pages].view(B, max_pages).to(torch.int32)
+    kc, vc = _bf(n_pages * page, Hkv, D, seed=11), _bf(n_pages * page, Hkv, D, seed=12)
+    q = _bf(B * q_len, Hq, D, seed=13)
+    scale = 1 / math.sqrt(D)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    out = ops.decode_attention(q, kc, vc, pt.to(DEV), lens.to(DEV), Hq, Hkv, D, q_len, page, scale, splits=splits, status=status)
+    exp = ref.decode_attention(q.cpu(), kc.cpu(), vc.cpu(), pt, lens, Hq, Hkv, D, q_len, page, scale)
+    assert int(status) == 0
+    torch.testing.assert_close(out.cpu().float(), exp.float(), atol=2e-2, rtol=2e-2)
+
+
+@pytest.mark.parametrize("M,N,K,bt", [(16, 256, 128, 16), (32, 512, 2048, 32), (77, 1536, 2048, 32), (64, 2048, 768, 64), (200, 1024, 512, 128), (5, 128, 64, 16)])
+def test_dense_gemm_tcgen05(M, N, K, bt):
+    x, w = _bf(M, K, seed=14), _bf(N, K, scale=0.05, seed=15)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    out = ops.dense_gemm(x, w, bt, status=status)
+    torch.cuda.synchronize()
+    assert int(status) == 0
+    exp = (x.float() @ w.float().t())
+    torch.testing.assert_close(out.float(), exp, atol=3e-2, rtol=2e-2)
+
+
+def _tile_schedule(counts, bt):
+    info, row = [], 0
+    for e, c in enumerate(counts):
+        for j in range((c + bt - 1) // bt):
+            info.append([e, row + j * bt, min(bt, c - j * bt), 0])
+        row += (c + bt - 1) // bt * bt
+    return torch.tensor(info, dtype=torch.int32), row
+
+
+@pytest.mark.parametrize("bt", [16, 32, 64])
+def test_grouped_swiglu_bf16(bt):
+    E, I, H = 6, 256, 512
+    counts = [3, 0, bt, bt + 5, 1, 40]
+    info, rows = _tile_schedule(counts, bt)
+    x = _bf(rows, H, seed=16)
+    wgu = _bf(E, 2 * I, H, scale=0.05, seed=17)
+    out = torch.zeros(rows, I, dtype=torch.bfloat16, device=DEV)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    ops.grouped_gemm(w=ops.interleave_gate_up(wgu), x=x, num_experts=E, n_per_expert=2 * I, k=H,
+                     tile_info=info.to(DEV), num_tok_tiles=torch.tensor([info.shape[0]], dtype=torch.int32, device=DEV),
+                     block_tok=bt, epilogue=ops.EPI_SWIGLU, out=out, out_ld=I, status=status)
+    torch.cuda.synchronize()
+    assert int(status) == 0
+    for t in range(info.shape[0]):
+        e, r0, v, _ = info[t].tolist()
+        gu = (x[r0:r0 + v].float() @ wgu[e].float().t())
+        exp = torch.nn.functional.silu(gu[:, :I]) * gu[:, I:]
+        torch.testing.assert_close(out[r0:r0 + v].float(), exp, atol=3e-2, rtol=3e-2)
+
+
+@pytest.mark.parametrize("bt", [16, 32])
+def test_fp8_block_scaled_gemm(bt):
+    M, N, K = 50, 512, 1024
+    x, w = _bf(M, K, seed=18), _bf(N, K, scale=0.05, seed=19)
+    xq, xs = ref.group_quant_fp8(x.cpu(), 128)
+    wq, ws = ref.block_quant_fp8(w.cpu(), 128)
+    exp = ref.fp8_gemm_nt(xq, xs, wq, ws)
+    info, n = ops.dense_tile_schedule(M, bt, DEV)
+    out = torch.zeros(M, N, dtype=torch.bfloat16, device=DEV)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    ops.grouped_gemm(w=wq.to(DEV), x=xq.to(DEV), num_experts=1, n_per_expert=N, k=K, tile_info=info, num_tok_tiles=n,
+                     block_tok=bt, epilogue=ops.EPI_STORE, out=out, out_ld=N, fp8=True, x_scale=xs.to(DEV),
+                     w_scale=ops.plain_tile_scales(ws[None].to(DEV)), status=status)
+    torch.cuda.synchronize()
+    assert int(status) == 0
+    torch.testing.assert_close(out.cpu().float(), exp.float(), atol=3e-2, rtol=2e-2)
