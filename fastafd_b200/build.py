@@ -78,7 +78,9 @@ def build_extension(force: bool = False, verbose: bool = False) -> Path:
 
     with ThreadPoolExecutor(max_workers=min(8, len(sources))) as ex:
         objs = list(ex.map(compile_one, sources))
-    link = [nvcc, "-shared", "-o", str(lib_path()), *map(str, objs), "-gencode",
+    # The CUDA runtime is linked dynamically: the process already holds torch's libcudart.so.12,
+    # so kernels, streams and allocations share one runtime instance with PyTorch.
+    link = [nvcc, "-shared", "--cudart", "shared", "-o", str(lib_path()), *map(str, objs), "-gencode",
             "arch=compute_100a,code=sm_100a"]
     r = subprocess.run(link, capture_output=True, text=True)
     if r.returncode != 0:

@@ -1,0 +1,544 @@
+"""Stage-structured transformer models for Attention-FFN disaggregation.
+
+A model is split into two stages that live on different GPUs:
+
+* :class:`AttentionStage` (attention GPU): embedding, per-layer attention block
+  (input norm -> qkv projection -> q/k norm + RoPE + paged KV store -> paged attention ->
+  o_proj), post-attention norm, router, optional local dense MLP / shared expert, final
+  norm, LM head.
+* :class:`ExpertStage` (expert GPU): the routed experts of every MoE layer for one
+  expert-parallel rank.
+
+The same classes run on CPU in fp32 (oracle, CPU/gloo slice) and on CUDA in bf16 where
+every op below lands in the sm_100a kernel library (`fastafd_b200.ops`); dense
+projections use cuBLAS through ``torch.nn.functional.linear``.
+
+Families covered by configuration: Qwen3-MoE, MiniMax-M2 (sigmoid + bias routing,
+cross-head q/k norm, partial rotary), GLM-4-MoE (first-k dense layers, shared experts,
+routed scaling), Qwen3.5 hybrid (gated DeltaNet layers, gated full attention, shared
+expert with sigmoid gate), and the dense Llama / Qwen2 / Qwen3 / Mistral models.
+
+Stage API parity with the reference: python/minisgl/models/qwen3_moe_afd.py:201-228
+(embed_input_ids / forward_attention / route / finalize_hidden / forward_lm_head) and
+:280-290 (run_experts); families in python/minisgl/models/{minimax_m2,glm4_moe,qwen35_moe}_afd.py.
+"""
+from __future__ import annotations
+
+import hashlib
+from dataclasses import dataclass
+from typing import Dict, List, Optional, Tuple
+
+import torch
+import torch.nn.functional as F
+
+from .. import ops
+from ..config import ModelConfig
+from ..reference import ops_ref as ref
+
+Tensor = torch.Tensor
+
+
+# ------------------------------------------------------------------ deterministic init
+def seeded_normal(name: str, shape, std: float, seed: int, device, dtype, fast: bool = False) -> Tensor:
+    """N(0, std) values that depend only on (seed, name): every process that creates the
+    tensor `name` gets the same numbers. ``fast`` draws on the target CUDA device (large
+    benchmark models); otherwise on CPU (tests compare across processes and devices)."""
+    h = int.from_bytes(hashlib.sha256(f"{seed}:{name}".encode()).digest()[:7], "little")
+    if fast and torch.device(device).type == "cuda":
+        g = torch.Generator(device=device).manual_seed(h)
+        return torch.empty(shape, dtype=torch.float32 if dtype == torch.float8_e4m3fn else dtype,
+                           device=device).normal_(0.0, std, generator=g)
+    g = torch.Generator(device="cpu").manual_seed(h)
+    return (torch.randn(shape, generator=g, dtype=torch.float32) * std).to(dtype).to(device)
+
+
+@dataclass
+class AttnMeta:
+    """Per-micro-batch attention inputs (device tensors with graph-stable addresses)."""
+    positions: Tensor          # [T] int32
+    out_loc: Tensor            # [T] int32 KV slot of each token (-1 = padding, no store)
+    page_table: Tensor         # [B, max_pages] int32
+    seq_lens: Tensor           # [B] int32, KV length including this step's tokens
+    q_len: int = 1             # tokens per request in this step (decode 1, verify block)
+    is_prefill: bool = False
+    prefill_lens: Optional[List[int]] = None   # tokens of each request in this prefill step
+    state_slots: Optional[Tensor] = None       # [B] int32 GDN state slot per request
+    splits: int = 1
+    workspace: Optional[Tensor] = None
+    status: Optional[Tensor] = None
+
+
+class KVPool:
+    """bf16 (or fp32 on CPU) paged KV cache: [full_layers][slots, kv_heads, head_dim] x {K, V}.
+    Reference: python/minisgl/kvcache/mha_pool.py:10-66."""
+
+    def __init__(self, cfg: ModelConfig, num_pages: int, page_size: int, kv_heads: int, device, dtype):
+        self.num_pages, self.page_size = num_pages, page_size
+        n = cfg.num_full_attn_layers
+        self.k = torch.zeros(n, num_pages * page_size, kv_heads, cfg.head_dim, dtype=dtype, device=device)
+        self.v = torch.zeros_like(self.k)
+
+    @staticmethod
+    def bytes_per_page(cfg: ModelConfig, page_size: int, kv_heads: int, elem: int = 2) -> int:
+        return 2 * cfg.num_full_attn_layers * page_size * kv_heads * cfg.head_dim * elem
+
+
+class GDNStatePool:
+    """Per-request recurrent state of the gated-DeltaNet layers: conv taps and the fp32
+    [Hv, Dv, Dk] matrix. Reference: python/minisgl/kvcache/hybrid_pool.py:20-62."""
+
+    def __init__(self, cfg: ModelConfig, slots: int, device, dtype, tp: int = 1):
+        n = cfg.num_linear_layers
+        hk, hv = cfg.gdn_num_k_heads // tp, cfg.gdn_num_v_heads // tp
+        conv_dim = 2 * hk * cfg.gdn_head_k_dim + hv * cfg.gdn_head_v_dim
+        self.conv = torch.zeros(n, slots, cfg.gdn_conv_kernel - 1, conv_dim, dtype=dtype, device=device)
+        self.rec = torch.zeros(n, slots, hv, cfg.gdn_head_v_dim, cfg.gdn_head_k_dim, dtype=torch.float32, device=device)
+
+    def reset(self, slot_ids: Tensor) -> None:
+        self.conv[:, slot_ids.long()] = 0
+        self.rec[:, slot_ids.long()] = 0
+
+
+def _linear(x: Tensor, w: Tensor, b: Optional[Tensor] = None) -> Tensor:
+    return F.linear(x, w, b)
+
+
+class AttentionStage:
+    """Everything of the model that runs on an attention GPU. Tensor-parallel over `tp`
+    ranks (heads split; o_proj row-parallel; vocab-parallel embedding and LM head); the
+    all-reduce / all-gather is delegated to `comm` (None = single rank)."""
+
+    def __init__(self, cfg: ModelConfig, device, dtype, tp_rank: int = 0, tp_size: int = 1, comm=None):
+        self.cfg, self.device, self.dtype = cfg, torch.device(device), dtype
+        self.tp_rank, self.tp_size, self.comm = tp_rank, tp_size, comm
+        assert cfg.num_q_heads % tp_size == 0
+        self.hq = cfg.num_q_heads // tp_size
+        # GQA: kv heads are replicated when there are fewer of them than TP ranks
+        self.hkv = max(1, cfg.num_kv_heads // tp_size)
+        self.kv_rep = max(1, tp_size // cfg.num_kv_heads)
+        self.w: Dict[str, Tensor] = {}
+        self.full_index = {}   # layer -> index among full-attention layers
+        self.lin_index = {}
+        for i in range(cfg.num_layers):
+            if cfg.layer_type(i) == "full":
+                self.full_index[i] = len(self.full_index)
+            else:
+                self.lin_index[i] = len(self.lin_index)
+        self.cos_sin: Optional[Tensor] = None
+        self.vocab_local = (cfg.vocab_size + tp_size - 1) // tp_size
+        self.vocab_start = tp_rank * self.vocab_local
+
+    # ------------------------------------------------------------------ weights
+    def param_shapes(self) -> Dict[str, Tuple[Tuple[int, ...], str]]:
+        """name -> (local shape, kind) where kind in {weight, norm, fp32}."""
+        c, H, D = self.cfg, self.cfg.hidden_size, self.cfg.head_dim
+        out: Dict[str, Tuple[Tuple[int, ...], str]] = {}
+        vl = min(self.vocab_local, c.vocab_size - self.vocab_start)
+        out["model.embed_tokens.weight"] = ((vl, H), "weight")
+        out["model.norm.weight"] = ((H,), "norm")
+        if not c.tie_embeddings:
+            out["lm_head.weight"] = ((vl, H), "weight")
+        for i in range(c.num_layers):
+            p = f"model.layers.{i}."
+            out[p + "input_layernorm.weight"] = ((H,), "norm")
+            out[p + "post_attention_layernorm.weight"] = ((H,), "norm")
+            if c.layer_type(i) == "full":
+                qmul = 2 if c.attn_output_gate else 1
+                out[p + "self_attn.qkv_proj.weight"] = (((self.hq * qmul + 2 * self.hkv) * D, H), "weight")
+                if c.attention_bias:
+                    out[p + "self_attn.qkv_proj.bias"] = (((self.hq * qmul + 2 * self.hkv) * D,), "weight")
+                out[p + "self_attn.o_proj.weight"] = ((H, self.hq * D), "weight")
+                if c.qk_norm == "head":
+                    out[p + "self_attn.q_norm.weight"] = ((D,), "norm")
+                    out[p + "self_attn.k_norm.weight"] = ((D,), "norm")
+                elif c.qk_norm == "cross_head":
+                    out[p + "self_attn.q_norm.weight"] = ((self.hq * D,), "norm")
+                    out[p + "self_attn.k_norm.weight"] = ((self.hkv * D,), "norm")
+            else:
+                hk, hv = c.gdn_num_k_heads // self.tp_size, c.gdn_num_v_heads // self.tp_size
+                dk, dv = c.gdn_head_k_dim, c.gdn_head_v_dim
+                conv_dim = 2 * hk * dk + hv * dv
+                out[p + "linear_attn.in_proj_qkv.weight"] = ((conv_dim, H), "weight")
+                out[p + "linear_attn.in_proj_z.weight"] = ((hv * dv, H), "weight")
+                out[p + "linear_attn.in_proj_b.weight"] = ((hv, H), "weight")
+                out[p + "linear_attn.in_proj_a.weight"] = ((hv, H), "weight")
+                out[p + "linear_attn.conv1d.weight"] = ((conv_dim, c.gdn_conv_kernel), "weight")
+                out[p + "linear_attn.A_log"] = ((hv,), "fp32")
+                out[p + "linear_attn.dt_bias"] = ((hv,), "fp32")
+                out[p + "linear_attn.norm.weight"] = ((dv,), "norm")
+                out[p + "linear_attn.out_proj.weight"] = ((H, hv * dv), "weight")
+            if c.is_moe_layer(i):
+                out[p + "mlp.gate.weight"] = ((c.num_experts, H), "fp32" if c.router_fp32 else "weight")
+                if c.router_bias:
+                    out[p + "mlp.gate.e_score_correction_bias"] = ((c.num_experts,), "fp32")
+                if c.num_shared_experts > 0:
+                    si = c.shared_expert_intermediate_size // self.tp_size
+                    out[p + "mlp.shared_expert.gate_up_proj.weight"] = ((2 * si, H), "weight")
+                    out[p + "mlp.shared_expert.down_proj.weight"] = ((H, si), "weight")
+                    if c.shared_expert_gate:
+                        out[p + "mlp.shared_expert_gate.weight"] = ((1, H), "weight")
+            else:
+                inter = c.intermediate_size // self.tp_size
+                out[p + "mlp.gate_up_proj.weight"] = ((2 * inter, H), "weight")
+                out[p + "mlp.down_proj.weight"] = ((H, inter), "weight")
+        return out
+
+    def init_random(self, seed: int = 0, std: float = 0.02, fast: bool = False) -> "AttentionStage":
+        """Random-init weights. TP shards take their slice of the full tensor so that a TP run
+        equals the single-rank run."""
+        for name, (shape, kind) in self.param_shapes().items():
+            dt = torch.float32 if kind == "fp32" else self.dtype
+            if kind == "norm":
+                base = torch.zeros(shape) if self.cfg.norm_offset1 else torch.ones(shape)
+                self.w[name] = (base + seeded_normal(name, shape, 0.02, seed, "cpu", torch.float32)).to(dt).to(self.device)
+            elif name.endswith("A_log"):
+                self.w[name] = seeded_normal(name, shape, 0.5, seed, self.device, dt, fast)
+            elif self.tp_size == 1:
+                self.w[name] = seeded_normal(name, shape, std, seed, self.device, dt, fast)
+            else:
+                self.w[name] = self._tp_slice(name, seed, std, dt)
+        self._post_load()
+        return self
+
+    def _tp_slice(self, name: str, seed: int, std: float, dt) -> Tensor:
+        """Slice of the full-size random tensor that this TP rank owns (CPU init only)."""
+        single = AttentionStage(self.cfg, "cpu", torch.float32)
+        full_shape = single.param_shapes()[name][0]
+        full = seeded_normal(name, full_shape, std, seed, "cpu", torch.float32)
+        return shard_attention_param(self.cfg, name, full, self.tp_rank, self.tp_size).to(dt).to(self.device)
+
+    def load_state(self, state: Dict[str, Tensor]) -> None:
+        for name, (shape, kind) in self.param_shapes().items():
+            t = state[name]
+            assert tuple(t.shape) == tuple(shape), f"{name}: {tuple(t.shape)} != {shape}"
+            self.w[name] = t.to(self.device, torch.float32 if kind == "fp32" else self.dtype)
+        self._post_load()
+
+    def _post_load(self) -> None:
+        c = self.cfg
+        self.cos_sin = ref.build_cos_sin_cache(min(c.max_position, 1 << 17), c.rotary_dim, c.rope.theta, self.device)
+
+    # ------------------------------------------------------------------ forward pieces
+    def embed(self, ids: Tensor) -> Tensor:
+        h = ops.embedding(ids, self.w["model.embed_tokens.weight"], self.vocab_start)
+        if self.tp_size > 1:
+            h = self.comm.all_reduce(h)
+        return h
+
+    def input_norm(self, layer: int, x: Tensor, residual: Optional[Tensor]) -> Tuple[Tensor, Tensor]:
+        """Pre-attention norm. With `residual`, adds x into it first. Returns (normed, residual)."""
+        w = self.w[f"model.layers.{layer}.input_layernorm.weight"]
+        if residual is None:
+            return ops.rmsnorm(x, w, self.cfg.rms_eps, self.cfg.norm_offset1), x
+        return ops.add_rmsnorm(x, residual, w, self.cfg.rms_eps, self.cfg.norm_offset1), residual
+
+    def attention(self, layer: int, x: Tensor, meta: AttnMeta, kv: KVPool, gdn: Optional[GDNStatePool] = None) -> Tensor:
+        """x: normed hidden [T,H] -> attention block output [T,H] (after o_proj and TP reduce)."""
+        if self.cfg.layer_type(layer) == "linear":
+            out = self._linear_attention(layer, x, meta, gdn)
+        else:
+            out = self._full_attention(layer, x, meta, kv)
+        if self.tp_size > 1:
+            out = self.comm.all_reduce(out)
+        return out
+
+    def _full_attention(self, layer: int, x: Tensor, meta: AttnMeta, kv: KVPool) -> Tensor:
+        c, D = self.cfg, self.cfg.head_dim
+        p = f"model.layers.{layer}.self_attn."
+        qkv = _linear(x, self.w[p + "qkv_proj.weight"], self.w.get(p + "qkv_proj.bias"))
+        T = x.shape[0]
+        gate = None
+        if c.attn_output_gate:
+            # rows are [q(hq*D) | gate(hq*D) | k | v]
+            q_part, gate, kv_part = qkv[:, :self.hq * D], qkv[:, self.hq * D:2 * self.hq * D], qkv[:, 2 * self.hq * D:]
+            qkv = torch.cat([q_part, kv_part], dim=-1).contiguous()
+        li = self.full_index[layer]
+        kc, vc = kv.k[li], kv.v[li]
+        qw = kw = None
+        if c.qk_norm == "head":
+            qw, kw = self.w[p + "q_norm.weight"], self.w[p + "k_norm.weight"]
+            if c.norm_offset1:
+                qw, kw = qw + 1, kw + 1
+        elif c.qk_norm == "cross_head":
+            qkv = self._cross_head_norm(qkv, self.w[p + "q_norm.weight"], self.w[p + "k_norm.weight"])
+        ops.qk_norm_rope_store(qkv, qw, kw, self.cos_sin, meta.positions, meta.out_loc, kc, vc, self.hq, self.hkv,
+                               D, c.rotary_dim, c.rms_eps, status=meta.status)
+        q = qkv.view(T, self.hq + 2 * self.hkv, D)[:, :self.hq]
+        scale = ref.softmax_scale(D)
+        if meta.is_prefill:
+            o = self._prefill_attention(q, kc, vc, meta, scale)
+        else:
+            o = ops.decode_attention(q.contiguous(), kc, vc, meta.page_table, meta.seq_lens, self.hq, self.hkv, D,
+                                     meta.q_len, kv.page_size, scale, splits=meta.splits,
+                                     workspace=meta.workspace, status=meta.status)
+        o = o.reshape(T, self.hq * D)
+        if gate is not None:
+            o = (o.float() * torch.sigmoid(gate.float())).to(o.dtype)
+        return _linear(o, self.w[p + "o_proj.weight"])
+
+    def _prefill_attention(self, q: Tensor, kc: Tensor, vc: Tensor, meta: AttnMeta, scale: float) -> Tensor:
+        """Causal attention of each request's new chunk against its paged KV (which already holds
+        the chunk: K/V were stored before this call). Runs the multi-token mode of the paged
+        kernel per request on CUDA; the oracle on CPU."""
+        D = self.cfg.head_dim
+        out = torch.empty_like(q)
+        off = 0
+        for b, n in enumerate(meta.prefill_lens):
+            if n == 0:
+                continue
+            qb = q[off:off + n].contiguous()
+            ob = ops.decode_attention(qb, kc, vc, meta.page_table[b:b + 1], meta.seq_lens[b:b + 1], self.hq, self.hkv,
+                                      D, n, self._page_size(meta, kc), scale, splits=1, status=meta.status)
+            out[off:off + n] = ob
+            off += n
+        return out
+
+    @staticmethod
+    def _page_size(meta: AttnMeta, kc: Tensor) -> int:
+        return meta.page_size if hasattr(meta, "page_size") else 16
+
+    def _cross_head_norm(self, qkv: Tensor, qw: Tensor, kw: Tensor) -> Tensor:
+        """MiniMax-M2: RMSNorm over all q heads jointly (and all k heads jointly). Under TP the
+        sum of squares is all-reduced. Reference: python/minisgl/layers/norm.py:110-149."""
+        c, D = self.cfg, self.cfg.head_dim
+        qn, kn = self.hq * D, self.hkv * D
+        q, k = qkv[:, :qn].float(), qkv[:, qn:qn + kn].float()
+        sq = torch.stack([q.pow(2).sum(-1), k.pow(2).sum(-1)], dim=-1)
+        if self.tp_size > 1:
+            sq = self.comm.all_reduce(sq)
+        qd, kd = c.num_q_heads * D, max(c.num_kv_heads, self.tp_size) * D
+        q = q * torch.rsqrt(sq[:, 0:1] / qd + c.rms_eps) * qw.float()
+        k = k * torch.rsqrt(sq[:, 1:2] / kd + c.rms_eps) * kw.float()
+        out = qkv.clone()
+        out[:, :qn] = q.to(qkv.dtype)
+        out[:, qn:qn + kn] = k.to(qkv.dtype)
+        return out
+
+    def _linear_attention(self, layer: int, x: Tensor, meta: AttnMeta, gdn: GDNStatePool) -> Tensor:
+        """Gated DeltaNet block: in-proj -> causal conv (k taps) + SiLU -> gated delta rule ->
+        per-head gated RMSNorm -> out-proj. Reference: python/minisgl/models/qwen35_moe.py:58-247."""
+        from ..ops import gdn as gdn_ops
+
+        c = self.cfg
+        p = f"model.layers.{layer}.linear_attn."
+        li = self.lin_index[layer]
+        hk, hv = c.gdn_num_k_heads // self.tp_size, c.gdn_num_v_heads // self.tp_size
+        dk, dv = c.gdn_head_k_dim, c.gdn_head_v_dim
+        mixed = _linear(x, self.w[p + "in_proj_qkv.weight"])
+        z = _linear(x, self.w[p + "in_proj_z.weight"])
+        b = _linear(x, self.w[p + "in_proj_b.weight"])
+        a = _linear(x, self.w[p + "in_proj_a.weight"])
+        out = gdn_ops.gdn_block(mixed, z, a, b, self.w[p + "conv1d.weight"], self.w[p + "A_log"], self.w[p + "dt_bias"],
+                                self.w[p + "norm.weight"], gdn.conv[li], gdn.rec[li], meta, hk, hv, dk, dv, c.rms_eps)
+        return _linear(out, self.w[p + "out_proj.weight"])
+
+    def post_attn_norm(self, layer: int, attn_out: Tensor, residual: Tensor) -> Tensor:
+        w = self.w[f"model.layers.{layer}.post_attention_layernorm.weight"]
+        return ops.add_rmsnorm(attn_out, residual, w, self.cfg.rms_eps, self.cfg.norm_offset1)
+
+    def route(self, layer: int, x: Tensor) -> Tuple[Tensor, Tensor]:
+        """Router of MoE layer `layer` on normed hidden x: (topk_idx int32 [T,K], topk_w fp32 [T,K])."""
+        c = self.cfg
+        p = f"model.layers.{layer}.mlp.gate."
+        gw = self.w[p + "weight"]
+        logits = _linear(x.float() if gw.dtype == torch.float32 else x, gw).float()
+        bias = self.w.get(p + "e_score_correction_bias")
+        if c.n_group > 1:
+            return ref.grouped_topk_route(logits, bias, c.num_experts_per_tok, c.n_group, c.topk_group,
+                                          c.norm_topk_prob, 1.0)
+        return ops.topk_route(logits, bias, c.num_experts_per_tok, c.scoring, c.norm_topk_prob, 1.0)
+
+    def local_mlp(self, layer: int, x: Tensor) -> Optional[Tensor]:
+        """Work that stays on the attention GPU: the dense MLP of non-MoE layers, or the shared
+        expert of an MoE layer (None when the layer has neither)."""
+        c = self.cfg
+        p = f"model.layers.{layer}.mlp."
+        if not c.is_moe_layer(layer):
+            h = ops.silu_mul(_linear(x, self.w[p + "gate_up_proj.weight"]))
+            out = _linear(h, self.w[p + "down_proj.weight"])
+        elif c.num_shared_experts > 0:
+            h = ops.silu_mul(_linear(x, self.w[p + "shared_expert.gate_up_proj.weight"]))
+            out = _linear(h, self.w[p + "shared_expert.down_proj.weight"])
+            if c.shared_expert_gate:
+                g = torch.sigmoid(_linear(x, self.w[p + "shared_expert_gate.weight"]).float())
+                out = (out.float() * g).to(out.dtype)
+        else:
+            return None
+        if self.tp_size > 1:
+            out = self.comm.all_reduce(out)
+        return out
+
+    def final_norm(self, x: Tensor, residual: Tensor) -> Tensor:
+        return ops.add_rmsnorm(x, residual, self.w["model.norm.weight"], self.cfg.rms_eps, self.cfg.norm_offset1)
+
+    def lm_head(self, x: Tensor) -> Tensor:
+        w = self.w["model.embed_tokens.weight"] if self.cfg.tie_embeddings else self.w["lm_head.weight"]
+        logits = _linear(x, w)
+        if self.tp_size > 1:
+            logits = self.comm.all_gather_last_dim(logits)[:, :self.cfg.vocab_size]
+        return logits
+
+
+def shard_attention_param(cfg: ModelConfig, name: str, full: Tensor, rank: int, tp: int) -> Tensor:
+    """TP shard of an attention-stage tensor given at full size (merged-qkv aware, GQA
+    replication when kv_heads < tp). Reference: python/minisgl/models/weight.py:142-185."""
+    if tp == 1:
+        return full
+    D = cfg.head_dim
+    hq = cfg.num_q_heads // tp
+    hkv = max(1, cfg.num_kv_heads // tp)
+    kv_rank = rank * cfg.num_kv_heads // tp if cfg.num_kv_heads < tp else rank
+
+    def rows(t, n):  # even split of dim 0
+        return t[rank * n:(rank + 1) * n]
+
+    if name.endswith("qkv_proj.weight") or name.endswith("qkv_proj.bias"):
+        qmul = 2 if cfg.attn_output_gate else 1
+        qn = cfg.num_q_heads * D * qmul
+        q, k, v = full[:qn], full[qn:qn + cfg.num_kv_heads * D], full[qn + cfg.num_kv_heads * D:]
+        if qmul == 2:
+            qq, gg = q[:qn // 2], q[qn // 2:]
+            qs = torch.cat([rows(qq, hq * D), rows(gg, hq * D)], 0)
+        else:
+            qs = rows(q, hq * D)
+        ks = k[kv_rank * hkv * D:(kv_rank + 1) * hkv * D]
+        vs = v[kv_rank * hkv * D:(kv_rank + 1) * hkv * D]
+        return torch.cat([qs, ks, vs], 0).contiguous()
+    if name.endswith("o_proj.weight") or name.endswith("out_proj.weight") or name.endswith("down_proj.weight"):
+        n = full.shape[1] // tp
+        return full[:, rank * n:(rank + 1) * n].contiguous()
+    if name.endswith("gate_up_proj.weight"):
+        I = full.shape[0] // 2
+        n = I // tp
+        return torch.cat([full[rank * n:(rank + 1) * n], full[I + rank * n:I + (rank + 1) * n]], 0).contiguous()
+    if name.endswith("embed_tokens.weight") or name.endswith("lm_head.weight"):
+        vl = (cfg.vocab_size + tp - 1) // tp
+        return full[rank * vl:(rank + 1) * vl].contiguous()
+    if name.endswith("self_attn.q_norm.weight") and cfg.qk_norm == "cross_head":
+        return rows(full, hq * D).contiguous()
+    if name.endswith("self_attn.k_norm.weight") and cfg.qk_norm == "cross_head":
+        return full[kv_rank * hkv * D:(kv_rank + 1) * hkv * D].contiguous()
+    if ".linear_attn." in name:
+        hk, hv = cfg.gdn_num_k_heads // tp, cfg.gdn_num_v_heads // tp
+        dk, dv = cfg.gdn_head_k_dim, cfg.gdn_head_v_dim
+        if name.endswith("in_proj_qkv.weight") or name.endswith("conv1d.weight"):
+            kq = cfg.gdn_num_k_heads * dk
+            q, k, v = full[:kq], full[kq:2 * kq], full[2 * kq:]
+            return torch.cat([rows(q, hk * dk), rows(k, hk * dk), rows(v, hv * dv)], 0).contiguous()
+        if name.endswith("in_proj_z.weight"):
+            return rows(full, hv * dv).contiguous()
+        if name.endswith(("in_proj_a.weight", "in_proj_b.weight", "A_log", "dt_bias")):
+            return rows(full, hv).contiguous()
+    return full
+
+
+class ExpertStage:
+    """The routed experts owned by expert-parallel rank `ep_rank` of `ep_size`, every MoE layer.
+
+    Weights per layer: gate_up [E_local, 2I, H] (gate rows then up rows) and down
+    [E_local, H, I]; experts beyond the global count on the last rank are zero padding.
+    On CUDA the gate/up rows are re-laid out for the SWIGLU epilogue of the grouped GEMM, and
+    with block-FP8 weights the scales are turned into per-tile scale tables."""
+
+    def __init__(self, cfg: ModelConfig, device, dtype, ep_rank: int = 0, ep_size: int = 1):
+        self.cfg, self.device, self.dtype = cfg, torch.device(device), dtype
+        self.ep_rank, self.ep_size = ep_rank, ep_size
+        self.experts_local = (cfg.num_experts + ep_size - 1) // ep_size
+        self.expert_base = ep_rank * self.experts_local
+        self.moe_layers = [i for i in range(cfg.num_layers) if cfg.is_moe_layer(i)]
+        self.gate_up: Dict[int, Tensor] = {}
+        self.down: Dict[int, Tensor] = {}
+        self.gate_up_scale: Dict[int, Tensor] = {}
+        self.down_scale: Dict[int, Tensor] = {}
+        # kernel-ready forms (CUDA)
+        self.w13: Dict[int, Tensor] = {}
+        self.w2: Dict[int, Tensor] = {}
+        self.w13_scale: Dict[int, Optional[Tensor]] = {}
+        self.w2_scale: Dict[int, Optional[Tensor]] = {}
+
+    @property
+    def fp8(self) -> bool:
+        return self.cfg.quant.is_fp8 and self.device.type == "cuda"
+
+    def init_random(self, seed: int = 0, std: float = 0.02, fast: bool = False) -> "ExpertStage":
+        c, E = self.cfg, self.experts_local
+        valid = max(0, min(E, c.num_experts - self.expert_base))
+        for i in self.moe_layers:
+            gu = torch.zeros(E, 2 * c.moe_intermediate_size, c.hidden_size, dtype=self.dtype, device=self.device)
+            dn = torch.zeros(E, c.hidden_size, c.moe_intermediate_size, dtype=self.dtype, device=self.device)
+            if fast and self.device.type == "cuda":
+                name = f"model.layers.{i}.mlp.experts.rank{self.ep_rank}of{self.ep_size}"
+                gu[:valid] = seeded_normal(name + ".gate_up", gu[:valid].shape, std, seed, self.device, self.dtype, True)
+                dn[:valid] = seeded_normal(name + ".down", dn[:valid].shape, std, seed, self.device, self.dtype, True)
+            else:
+                for e in range(valid):
+                    ge = self.expert_base + e
+                    name = f"model.layers.{i}.mlp.experts.{ge}."
+                    gu[e] = seeded_normal(name + "gate_up_proj.weight", gu[e].shape, std, seed, self.device, self.dtype)
+                    dn[e] = seeded_normal(name + "down_proj.weight", dn[e].shape, std, seed, self.device, self.dtype)
+            self.set_layer(i, gu, dn)
+        return self
+
+    def set_layer(self, layer: int, gate_up: Tensor, down: Tensor, gate_up_scale: Optional[Tensor] = None,
+                  down_scale: Optional[Tensor] = None) -> None:
+        """Install one layer's expert weights. bf16/fp32 tensors, or e4m3 tensors with their
+        128x128 block scales ([E, 2I/128, H/128] and [E, H/128, I/128])."""
+        c = self.cfg
+        if self.device.type != "cuda":
+            if gate_up.dtype == torch.float8_e4m3fn:
+                gate_up = torch.stack([ref.block_dequant_fp8(gate_up[e], gate_up_scale[e]) for e in range(gate_up.shape[0])])
+                down = torch.stack([ref.block_dequant_fp8(down[e], down_scale[e]) for e in range(down.shape[0])])
+            self.gate_up[layer], self.down[layer] = gate_up.to(self.dtype), down.to(self.dtype)
+            return
+        if c.quant.is_fp8:
+            if gate_up.dtype != torch.float8_e4m3fn:
+                gate_up, gate_up_scale = _block_quant_experts(gate_up)
+                down, down_scale = _block_quant_experts(down)
+            I = c.moe_intermediate_size
+            self.w13[layer] = ops.interleave_gate_up(gate_up.view(torch.uint8)).view(torch.float8_e4m3fn)
+            self.w13_scale[layer] = ops.interleave_gate_up_scales(gate_up_scale.float(), I)
+            self.w2[layer] = down.contiguous()
+            self.w2_scale[layer] = ops.plain_tile_scales(down_scale.float())
+        else:
+            self.w13[layer] = ops.interleave_gate_up(gate_up.to(self.dtype))
+            self.w2[layer] = down.to(self.dtype).contiguous()
+            self.w13_scale[layer] = self.w2_scale[layer] = None
+
+    def run_experts_dense(self, layer: int, x: Tensor, topk_idx: Tensor) -> Tensor:
+        """CPU path: per-(k, token) expert output rows [K, T, H] for experts on this rank, zeros
+        elsewhere (the combine buffer contents that the CUDA epilogue would write)."""
+        K = topk_idx.shape[1]
+        T, H = x.shape
+        rows = torch.zeros(K, T, H, dtype=x.dtype, device=x.device)
+        gu_all, dn_all = self.gate_up[layer], self.down[layer]
+        for e in range(self.experts_local):
+            sel = (topk_idx == e + self.expert_base)
+            if not sel.any():
+                continue
+            tok, k = sel.nonzero(as_tuple=True)
+            gu = _linear(x[tok], gu_all[e])
+            h = ref.silu_mul(gu)
+            rows[k, tok] = _linear(h, dn_all[e])
+        return rows
+
+
+def _block_quant_experts(w: Tensor):
+    qs, ss = [], []
+    for e in range(w.shape[0]):
+        q, s = ref.block_quant_fp8(w[e])
+        qs.append(q)
+        ss.append(s)
+    return torch.stack(qs), torch.stack(ss)
+
+
+def combine_rows(rows: Tensor, topk_w: Tensor, topk_idx: Optional[Tensor] = None, scale: float = 1.0) -> Tensor:
+    """y[t] = scale * sum_k w[t,k] * rows[k,t] in fp32, k ascending: the attention-side M2N
+    reduction (same order as the CUDA combine kernel)."""
+    K, T, H = rows.shape
+    acc = torch.zeros(T, H, dtype=torch.float32, device=rows.device)
+    for k in range(K):
+        w = topk_w[:, k].float()
+        if topk_idx is not None:
+            w = torch.where(topk_idx[:, k] >= 0, w, torch.zeros_like(w))
+        acc = torch.addcmul(acc, rows[k].float(), w[:, None])
+    return (acc * scale).to(rows.dtype)

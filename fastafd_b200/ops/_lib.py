@@ -107,6 +107,8 @@ class KernelLibraryError(RuntimeError):
 @lru_cache(maxsize=1)
 def lib() -> C.CDLL:
     """Load the kernel library, building it first when the binary is absent."""
+    import torch  # noqa: F401  (loads libcudart.so.12, which the kernel library links against)
+
     path = lib_path()
     if not path.exists():
         path = build_extension()
