@@ -1,0 +1,251 @@
+"""One process of an AFD deployment, and an SPMD driver for it.
+
+:class:`AfdEngine` builds what this rank needs from the topology:
+
+* world 1 (colocated): attention stage and expert stage in one process on one device; the
+  expert layer is launched right behind each dispatch.
+* world > 1: rank < attn_world is an attention worker, the others are expert workers. On
+  CUDA they share peer-mapped heaps (:class:`fastafd_b200.parallel.fabric.Fabric`) and talk
+  through the fused kernels; on CPU they exchange tensors over gloo.
+
+:class:`SpmdDriver` runs requests through the engines without a separate coordinator
+process: every rank holds the lane schedulers and the ranks agree on each step's phase and
+sizes with one small all-gather (used by the offline ``LLM`` API, the tests and the
+benchmark; the server uses :mod:`fastafd_b200.coordinator` instead).
+
+Reference: python/minisgl/afd_worker_base.py:560-715 (_init_afd_runtime),
+python/minisgl/engine/engine.py:212-433 (colocated Engine).
+"""
+from __future__ import annotations
+
+import time
+from typing import Dict, List, Optional, Sequence, Tuple
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from .config import ModelConfig, RuntimeConfig
+from .core import SamplingParams
+from .models.transformer import ExpertStage
+from .protocol import AfdTopology, AgStepPlan, AgStepReply, EgStepPlan, EgStepReply
+from .scheduler.buckets import normalize_buckets, per_mb_real, select_bucket
+from .scheduler.lane import LaneScheduler
+from .worker.attention_worker import AttentionWorker
+from .worker.expert_worker import ExpertWorker
+from .worker.moe_client import (FabricMoeClient, FabricMoeServer, GlooMoeClient, GlooMoeServer, LocalMoeClient)
+
+
+def _torch_dtype(name: str, device: torch.device) -> torch.dtype:
+    if device.type != "cuda":
+        return torch.float32
+    return {"bfloat16": torch.bfloat16, "float16": torch.float16, "float32": torch.float32}[name]
+
+
+class AfdEngine:
+    def __init__(self, cfg: ModelConfig, rt: RuntimeConfig, topo: AfdTopology, rank: int, device,
+                 group=None, seed: int = 0, fast_init: bool = False, max_comm_tokens: Optional[int] = None):
+        self.cfg, self.rt, self.topo, self.rank, self.group = cfg, rt, topo, rank, group
+        self.device = torch.device(device)
+        self.dtype = _torch_dtype(rt.dtype, self.device)
+        self.colocated = topo.world == 1
+        self.is_attention = self.colocated or topo.is_attention(rank)
+        self.is_expert = self.colocated or topo.is_expert(rank)
+        cuda = self.device.type == "cuda"
+        self.buckets = normalize_buckets(rt.decode_graph_bs, rt.cuda_graph_max_bs)
+        cap = self.buckets[-1]
+        self.max_comm_tokens = max_comm_tokens or max(cap, min(2048, rt.max_batched_tokens // max(rt.num_mb, 1)))
+        self.fabric = None
+        self.attn: Optional[AttentionWorker] = None
+        self.expert: Optional[ExpertWorker] = None
+        num_eg = 1 if self.colocated else topo.mlp_world
+        num_ag = 1 if self.colocated else topo.attn_world
+
+        stage = None
+        if self.is_expert and cfg.is_moe:
+            ep_rank = 0 if self.colocated else topo.expert_index(rank)
+            stage = ExpertStage(cfg, self.device, self.dtype, ep_rank, num_eg).init_random(seed, fast=fast_init)
+        self.expert_stage = stage
+
+        client = server = None
+        eg_status = None
+        if cfg.is_moe:
+            if cuda:
+                from .moe.afd_moe import AgMoeEndpoint, EgMoeEndpoint, MoeCommConfig, ag_layout, eg_layout
+                from .parallel.fabric import Fabric
+
+                mcfg = MoeCommConfig(num_ag=num_ag, num_eg=num_eg, num_lanes=rt.num_mb, max_tokens=self.max_comm_tokens,
+                                     hidden=cfg.hidden_size, topk=cfg.num_experts_per_tok, num_experts=cfg.num_experts,
+                                     intermediate=cfg.moe_intermediate_size, fp8=cfg.quant.is_fp8, block_tok=rt.moe_block_tok)
+                timeout_ns = int(rt.flag_timeout_s * 1e9)
+                if self.colocated:
+                    fabs = Fabric.local([ag_layout(mcfg).size, eg_layout(mcfg).size], self.device)
+                    self.fabric = fabs
+                    eg_ep = EgMoeEndpoint(mcfg, fabs[1], 0, [0], self.device, timeout_ns)
+                    server = FabricMoeServer(eg_ep, stage)
+                    client = FabricMoeClient(AgMoeEndpoint(mcfg, fabs[0], 0, [1], self.device, timeout_ns), colocated=server)
+                    eg_status = eg_ep.status
+                else:
+                    size = ag_layout(mcfg).size if self.is_attention else eg_layout(mcfg).size
+                    self.fabric = Fabric.ipc(size, self.device, group)
+                    if self.is_attention:
+                        client = FabricMoeClient(AgMoeEndpoint(mcfg, self.fabric, rank, topo.expert_ranks(), self.device, timeout_ns))
+                    else:
+                        eg_ep = EgMoeEndpoint(mcfg, self.fabric, topo.expert_index(rank), topo.attention_ranks(),
+                                              self.device, timeout_ns)
+                        server = FabricMoeServer(eg_ep, stage)
+                        eg_status = eg_ep.status
+            else:
+                if self.colocated:
+                    client = LocalMoeClient([stage])
+                elif self.is_attention:
+                    client = GlooMoeClient(topo.expert_ranks(), cfg.hidden_size, cfg.num_experts_per_tok, group)
+                else:
+                    server = GlooMoeServer(stage, topo.attention_ranks(), cfg.hidden_size, cfg.num_experts_per_tok,
+                                           self.dtype, group)
+        if self.is_attention:
+            tp_rank = 0 if self.colocated else topo.attn_tp_rank(rank)
+            self.attn = AttentionWorker(cfg, rt, self.device, client, tp_rank=tp_rank, tp_size=topo.attn_tp,
+                                        tp_comm=None, dtype=self.dtype, rank=rank, max_bucket=cap,
+                                        weight_init=lambda m: m.init_random(seed, fast=fast_init))
+        if self.is_expert and not self.colocated:
+            self.expert = ExpertWorker(cfg, rt, self.device, stage, server, rank, eg_status)
+        self._server = server
+
+    # ------------------------------------------------------------------ stepping
+    def step(self, plan, mb_tokens: Optional[List[int]] = None):
+        """Run one planned step on this rank and wait for it (attention: returns the sampled
+        tokens; expert: returns after the kernels were queued)."""
+        if isinstance(plan, EgStepPlan):
+            return self.expert.run_step(plan)
+        return self.attn.run_step(plan, mb_tokens)
+
+    def launch(self, plan: AgStepPlan) -> None:
+        self.attn.launch_decode(plan)
+
+    def finish(self, plan: AgStepPlan) -> AgStepReply:
+        return self.attn.finish_decode(plan)
+
+    def synchronize(self) -> int:
+        """Wait for queued work; returns the device status word (0 = ok)."""
+        if self.device.type == "cuda":
+            torch.cuda.synchronize(self.device)
+        code = 0
+        if self.attn is not None:
+            code = self.attn.read_status()
+        if self.expert is not None:
+            code = code or self.expert.finish()
+        return code
+
+    def close(self) -> None:
+        if self.fabric is None:
+            return
+        for f in (self.fabric if isinstance(self.fabric, list) else [self.fabric]):
+            f.close()
+        self.fabric = None
+
+
+class SpmdDriver:
+    """Coordinator logic replicated on every rank (no separate coordinator process).
+
+    Every rank builds the same lane schedulers from the same request list; attention rank r
+    executes lane r's plans, expert ranks execute the matching expert plans. Step decisions
+    depend on the sampled tokens only through request completion, which the attention ranks
+    share with one gloo all-gather per step."""
+
+    def __init__(self, engine: AfdEngine, num_pages: Optional[int] = None):
+        self.e = engine
+        topo, rt, cfg = engine.topo, engine.rt, engine.cfg
+        self.num_lanes = 1 if engine.colocated else topo.attn_dp
+        pages = num_pages or (engine.attn.num_pages if engine.attn is not None else rt.num_pages)
+        if not engine.colocated and dist.is_initialized():
+            t = torch.tensor([pages if engine.attn is not None else 1 << 30], dtype=torch.int64)
+            dist.all_reduce(t, op=dist.ReduceOp.MIN, group=engine.group)
+            pages = int(t[0])
+        self.lanes = [LaneScheduler(l, num_pages=pages, page_size=rt.page_size, max_running=rt.max_running_requests,
+                                    max_seq_len=rt.max_seq_len or cfg.max_position, num_mb=rt.num_mb,
+                                    max_batched_tokens=rt.max_batched_tokens, max_comm_tokens=engine.max_comm_tokens,
+                                    cache_type=rt.cache_type, eos_token_ids=cfg.eos_token_ids)
+                      for l in range(self.num_lanes)]
+        self.step_id = 0
+        self.my_lane = None
+        if engine.attn is not None:
+            self.my_lane = 0 if engine.colocated else topo.attn_lane(engine.rank)
+
+    def add_requests(self, prompts: Sequence[Sequence[int]], sampling: SamplingParams) -> List[int]:
+        uids = []
+        for i, p in enumerate(prompts):
+            lane = min(range(self.num_lanes), key=lambda l: (self.lanes[l].load, l))
+            uid = getattr(self, "_next_uid", 0)
+            self._next_uid = uid + 1
+            self.lanes[lane].add_req(uid, p, sampling)
+            uids.append(uid)
+        return uids
+
+    def _exchange_tokens(self, reply: Optional[AgStepReply], sizes: List[int]) -> List[np.ndarray]:
+        """Every rank learns every lane's sampled tokens of this step."""
+        if self.e.colocated or not dist.is_initialized():
+            return [reply.next_tokens]
+        n = max(sizes) if sizes else 0
+        mine = torch.full((n + 1,), -1, dtype=torch.int64)
+        if reply is not None:
+            mine[0] = reply.status
+            mine[1:1 + len(reply.next_tokens)] = torch.from_numpy(reply.next_tokens.astype(np.int64))
+        else:
+            mine[0] = 0
+        bufs = [torch.empty_like(mine) for _ in range(self.e.topo.world)]
+        dist.all_gather(bufs, mine, group=self.e.group)
+        out = []
+        for lane in range(self.num_lanes):
+            src = lane * self.e.topo.attn_tp
+            if int(bufs[src][0]) != 0:
+                raise RuntimeError(f"attention rank {src} reported device status {int(bufs[src][0])}")
+            out.append(bufs[src][1:1 + sizes[lane]].numpy().astype(np.int32))
+        return out
+
+    def run_step(self) -> Optional[List[Tuple[int, List[int], bool]]]:
+        """Plan and execute one global step; returns [(uid, new_tokens, finished)] or None when idle."""
+        lanes = self.lanes
+        if all(l.idle() for l in lanes):
+            return None
+        sid = self.step_id
+        self.step_id += 1
+        if any(l.has_prefill() for l in lanes):
+            plans = [l.schedule_prefill(sid) if l.has_prefill() else l.dummy_step(sid, "prefill", 0) for l in lanes]
+            mb_tokens = [max(max(p.mbs[m].num_tokens for p in plans), 1) for m in range(self.e.rt.num_mb)]
+            phase, bucket = "prefill", 0
+        else:
+            real = max(l.decode_real() for l in lanes)
+            if real == 0:
+                for l in lanes:
+                    l.check_admission_stall()
+                return []
+            bucket = select_bucket(per_mb_real(real, self.e.rt.num_mb), self.e.buckets)
+            plans = [l.schedule_decode(sid, bucket) if l.decode_real() else l.dummy_step(sid, "decode", bucket) for l in lanes]
+            mb_tokens = [bucket] * self.e.rt.num_mb
+            phase = "decode"
+        reply = None
+        if self.e.attn is not None:
+            reply = self.e.step(plans[self.my_lane], mb_tokens)
+        if self.e.expert is not None:
+            self.e.step(EgStepPlan(step_id=sid, phase=phase, tokens_per_mb=mb_tokens))
+        sizes = [sum(len(mb.rows) for mb in p.mbs) for p in plans]
+        toks = self._exchange_tokens(reply, sizes)
+        out = []
+        for lane, l in enumerate(lanes):
+            out += l.complete(sid, toks[lane])
+        return out
+
+    def generate(self, prompts: Sequence[Sequence[int]], sampling: SamplingParams) -> List[List[int]]:
+        uids = self.add_requests(prompts, sampling)
+        results: Dict[int, List[int]] = {u: [] for u in uids}
+        while True:
+            out = self.run_step()
+            if out is None:
+                break
+            for uid, toks, _ in out:
+                results[uid] += toks
+        code = self.e.synchronize()
+        if code:
+            raise RuntimeError(f"device status {code}")
+        return [results[u] for u in uids]

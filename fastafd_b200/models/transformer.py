@@ -266,7 +266,7 @@ class AttentionStage:
         q = qkv.view(T, self.hq + 2 * self.hkv, D)[:, :self.hq]
         scale = ref.softmax_scale(D)
         if meta.is_prefill:
-            o = self._prefill_attention(q, kc, vc, meta, scale)
+            o = self._prefill_attention(q, kc, vc, meta, scale, kv.page_size)
         else:
             o = ops.decode_attention(q.contiguous(), kc, vc, meta.page_table, meta.seq_lens, self.hq, self.hkv, D,
                                      meta.q_len, kv.page_size, scale, splits=meta.splits,
@@ -276,26 +276,22 @@ class AttentionStage:
             o = (o.float() * torch.sigmoid(gate.float())).to(o.dtype)
         return _linear(o, self.w[p + "o_proj.weight"])
 
-    def _prefill_attention(self, q: Tensor, kc: Tensor, vc: Tensor, meta: AttnMeta, scale: float) -> Tensor:
+    def _prefill_attention(self, q: Tensor, kc: Tensor, vc: Tensor, meta: AttnMeta, scale: float, page_size: int) -> Tensor:
         """Causal attention of each request's new chunk against its paged KV (which already holds
         the chunk: K/V were stored before this call). Runs the multi-token mode of the paged
         kernel per request on CUDA; the oracle on CPU."""
         D = self.cfg.head_dim
-        out = torch.empty_like(q)
+        out = torch.zeros_like(q)
         off = 0
         for b, n in enumerate(meta.prefill_lens):
             if n == 0:
                 continue
             qb = q[off:off + n].contiguous()
             ob = ops.decode_attention(qb, kc, vc, meta.page_table[b:b + 1], meta.seq_lens[b:b + 1], self.hq, self.hkv,
-                                      D, n, self._page_size(meta, kc), scale, splits=1, status=meta.status)
+                                      D, n, page_size, scale, splits=1, status=meta.status)
             out[off:off + n] = ob
             off += n
         return out
-
-    @staticmethod
-    def _page_size(meta: AttnMeta, kc: Tensor) -> int:
-        return meta.page_size if hasattr(meta, "page_size") else 16
 
     def _cross_head_norm(self, qkv: Tensor, qw: Tensor, kw: Tensor) -> Tensor:
         """MiniMax-M2: RMSNorm over all q heads jointly (and all k heads jointly). Under TP the

@@ -1,0 +1,442 @@
+"""Attention-GPU worker: request-local state, the micro-batch ping-pong pipeline, CUDA
+graph capture per decode bucket, sampling and device-side token write-back.
+
+Per step the host sends only request rows, sequence lengths and page grants (from pinned
+staging buffers); input tokens of decode steps are read on the device from the token pool,
+where the previous step's sampler wrote them, so consecutive decode steps need no host
+round trip on the critical path.
+
+Pipeline (2 micro-batches A, B; `main` = compute stream, one lane stream per micro-batch):
+
+    main : compute(0,A) compute(0,B) | compute(1,A) compute(1,B) | ...
+    laneA:            dispatch(0,A) ....... combine(0,A)  dispatch(1,A) ...
+    laneB:                         dispatch(0,B) ....... combine(0,B) ...
+
+compute(l) = attention block + post-attention norm + router (+ shared expert);
+combine(l) waits for the expert GPUs, reduces the top-k rows and already applies the next
+block's input norm. While lane A is away at the experts, `main` runs B's attention.
+
+Reference: python/minisgl/afd_attention_worker.py:709-955 (_run_ag_pipeline_body),
+:304-648 (AfdAgDecodeGraphRunner), python/minisgl/afd_attention_runtime.py:99-483
+(token pool, materialize_ag_plan, page grants), python/minisgl/cuda_graph_utils.py.
+"""
+from __future__ import annotations
+
+import time
+from contextlib import contextmanager, nullcontext
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional
+
+import numpy as np
+import torch
+
+from .. import ops
+from ..config import ModelConfig, RuntimeConfig
+from ..models.transformer import AttentionStage, AttnMeta, GDNStatePool, KVPool
+from ..protocol import AgStepPlan, AgStepReply, MicroBatchPlan
+from ..reference import ops_ref as ref
+from ..utils.trace import nvtx_range
+from .moe_client import MoeClient
+
+
+@dataclass
+class _MbBuffers:
+    """Static device buffers of one micro-batch (capacity = largest decode bucket)."""
+    rows: torch.Tensor
+    seq_lens: torch.Tensor
+    positions: torch.Tensor
+    out_loc: torch.Tensor
+    ids: torch.Tensor
+    page_table: torch.Tensor
+    x_moe: torch.Tensor
+    topk_idx: torch.Tensor
+    topk_w: torch.Tensor
+    normed: torch.Tensor
+    residual: torch.Tensor
+    next_tokens: torch.Tensor
+    logits: Optional[torch.Tensor] = None
+    host_in: Optional[torch.Tensor] = None      # pinned [2, cap] int32: rows, seq_lens
+    host_out: Optional[torch.Tensor] = None     # pinned [cap] int32
+    workspace: Optional[torch.Tensor] = None
+
+
+@dataclass
+class _MbCtx:
+    """View of the buffers for the token count of the current step."""
+    lane: int
+    T: int
+    ids: torch.Tensor
+    meta: AttnMeta
+    x_moe: torch.Tensor
+    topk_idx: torch.Tensor
+    topk_w: torch.Tensor
+    normed: torch.Tensor
+    residual: torch.Tensor
+    extra: Optional[torch.Tensor] = None
+    pad_from: int = 0
+    keep: list = field(default_factory=list)
+
+
+def determine_num_pages(cfg: ModelConfig, rt: RuntimeConfig, device: torch.device, kv_heads: int,
+                        elem: int = 2) -> int:
+    """Pages that fit in `memory_ratio` of the free device memory once the weights are resident,
+    capped by what max_running_requests x max_seq_len can use. Explicit rt.num_pages wins.
+    Reference: python/minisgl/afd_attention_worker.py:144-203."""
+    if rt.num_pages > 0:
+        return rt.num_pages
+    want = rt.max_running_requests * (((rt.max_seq_len or cfg.max_position) + rt.page_size - 1) // rt.page_size) + 1
+    if device.type != "cuda":
+        return min(want, 4096)
+    per_page = KVPool.bytes_per_page(cfg, rt.page_size, kv_heads, elem)
+    free, _total = torch.cuda.mem_get_info(device)
+    budget = int(free * rt.memory_ratio) - (2 << 30)
+    return max(2, min(budget // max(per_page, 1), want))
+
+
+class AttentionWorker:
+    def __init__(self, cfg: ModelConfig, rt: RuntimeConfig, device, client: MoeClient, *, num_pages: int = 0,
+                 tp_rank: int = 0, tp_size: int = 1, tp_comm=None, dtype=None, rank: int = 0,
+                 max_bucket: Optional[int] = None, weight_init=None):
+        self.cfg, self.rt, self.device, self.client, self.rank = cfg, rt, torch.device(device), client, rank
+        self.cuda = self.device.type == "cuda"
+        self.dtype = dtype or (torch.bfloat16 if self.cuda else torch.float32)
+        self.model = AttentionStage(cfg, self.device, self.dtype, tp_rank, tp_size, tp_comm)
+        if weight_init is not None:
+            weight_init(self.model)          # weights first: the KV pool is sized from what is left
+        self.num_mb, self.page_size = rt.num_mb, rt.page_size
+        self.max_seq_len = rt.max_seq_len or cfg.max_position
+        self.max_pages = (self.max_seq_len + self.page_size - 1) // self.page_size
+        self.max_running = rt.max_running_requests
+        self.dummy_row = self.max_running
+        self.num_pages = num_pages = num_pages or determine_num_pages(
+            cfg, rt, self.device, self.model.hkv, 2 if self.cuda else 4)
+        self.kv = KVPool(cfg, num_pages, self.page_size, self.model.hkv, self.device, self.dtype)
+        self.gdn = GDNStatePool(cfg, self.max_running + 1, self.device, self.dtype, tp_size) if cfg.num_linear_layers else None
+        self.token_pool = torch.zeros(self.max_running + 1, self.max_seq_len + 8, dtype=torch.int32, device=self.device)
+        self.page_table_all = torch.zeros(self.max_running + 1, self.max_pages, dtype=torch.int32, device=self.device)
+        self.page_table_host = np.zeros((self.max_running + 1, self.max_pages), np.int32)
+        self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.cap = max_bucket or max(rt.cuda_graph_max_bs, 1)
+        self.bufs = [self._make_bufs(self.cap) for _ in range(self.num_mb)]
+        self.graphs: Dict[int, "torch.cuda.CUDAGraph"] = {}
+        self.kernel_launches = 0
+        if self.cuda:
+            self.main_stream = torch.cuda.Stream(self.device)
+            self.lane_streams = [torch.cuda.Stream(self.device) for _ in range(self.num_mb)]
+            self.d2h_event = torch.cuda.Event()
+
+    # ------------------------------------------------------------------ buffers
+    def _make_bufs(self, cap: int) -> _MbBuffers:
+        c, dev, dt = self.cfg, self.device, self.dtype
+        K = max(c.num_experts_per_tok, 1)
+        z = lambda *s, d=dt: torch.zeros(*s, dtype=d, device=dev)  # noqa: E731
+        b = _MbBuffers(
+            rows=z(cap, d=torch.int64), seq_lens=z(cap, d=torch.int32), positions=z(cap, d=torch.int32),
+            out_loc=z(cap, d=torch.int32), ids=z(cap, d=torch.int32), page_table=z(cap, self.max_pages, d=torch.int32),
+            x_moe=z(cap, c.hidden_size), topk_idx=z(cap, K, d=torch.int32), topk_w=z(cap, K, d=torch.float32),
+            normed=z(cap, c.hidden_size), residual=z(cap, c.hidden_size), next_tokens=z(cap, d=torch.int32))
+        b.rows.fill_(self.dummy_row)
+        b.seq_lens.fill_(1)
+        if self.cuda:
+            b.host_in = torch.zeros(2, cap, dtype=torch.int32).pin_memory()
+            b.host_out = torch.zeros(cap, dtype=torch.int32).pin_memory()
+        return b
+
+    # ------------------------------------------------------------------ plan application
+    def apply_grants(self, plan: AgStepPlan) -> None:
+        n = len(plan.grant_rows)
+        if n == 0:
+            return
+        self.page_table_host[plan.grant_rows, plan.grant_slots] = plan.grant_pages
+        if self.cuda:
+            g = torch.from_numpy(np.stack([plan.grant_rows, plan.grant_slots, plan.grant_pages]).astype(np.int64)).pin_memory()
+            gd = g.to(self.device, non_blocking=True)
+            self.page_table_all.index_put_((gd[0], gd[1]), gd[2].to(torch.int32))
+        else:
+            self.page_table_all[torch.from_numpy(plan.grant_rows).long(), torch.from_numpy(plan.grant_slots).long()] = \
+                torch.from_numpy(plan.grant_pages)
+
+    def h2d_bytes(self, plan: AgStepPlan) -> int:
+        n = sum(2 * len(mb.rows) * 4 for mb in plan.mbs) + 3 * 8 * len(plan.grant_rows)
+        n += sum(mb.input_ids.nbytes for mb in plan.mbs if mb.input_ids is not None)
+        return n
+
+    # ------------------------------------------------------------------ pipeline
+    @contextmanager
+    def _on_lane(self, lane: int, after_main: bool = True):
+        """Run the enclosed launches on the lane's stream, ordered after what `main` has queued
+        so far; the caller orders `main` after the lane later with `_join_lane`."""
+        if not self.cuda:
+            yield
+            return
+        s = self.lane_streams[lane]
+        if after_main:
+            s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            yield
+
+    def _join_lane(self, lane: int) -> None:
+        if self.cuda:
+            torch.cuda.current_stream().wait_stream(self.lane_streams[lane])
+
+    def _next_norm_weight(self, layer: int) -> torch.Tensor:
+        if layer + 1 < self.cfg.num_layers:
+            return self.model.w[f"model.layers.{layer + 1}.input_layernorm.weight"]
+        return self.model.w["model.norm.weight"]
+
+    def _compute(self, layer: int, mb: _MbCtx) -> None:
+        """Attention block + post-attention norm + router for one layer of one micro-batch; for
+        MoE layers ends with the dispatch on the lane stream, for dense layers with the local MLP."""
+        m, c = self.model, self.cfg
+        with nvtx_range(f"AFD_AG_Attn_L{layer}_mb{mb.lane}"):
+            attn_out = m.attention(layer, mb.normed, mb.meta, self.kv, self.gdn)
+            x = m.post_attn_norm(layer, attn_out, mb.residual)
+        if c.is_moe_layer(layer):
+            idx, w = m.route(layer, x)
+            mb.x_moe.copy_(x)
+            mb.topk_idx.copy_(idx)
+            mb.topk_w.copy_(w)
+            if mb.meta.is_prefill and mb.pad_from < mb.T:
+                mb.topk_idx[mb.pad_from:] = -1          # padding tokens are routed nowhere
+            mb.extra = m.local_mlp(layer, x)
+            mb.keep += [attn_out, x, idx, w, mb.extra]
+            with self._on_lane(mb.lane):
+                with nvtx_range(f"AFD_AG_Dispatch_L{layer}_mb{mb.lane}"):
+                    self.client.dispatch(mb.lane, layer, mb.x_moe, mb.topk_idx, mb.topk_w)
+        else:
+            y = m.local_mlp(layer, x)
+            normed = ops.add_rmsnorm(y, mb.residual, self._next_norm_weight(layer), c.rms_eps, c.norm_offset1)
+            mb.normed.copy_(normed)
+            mb.keep += [attn_out, x, y, normed]
+
+    def _combine(self, layer: int, mb: _MbCtx) -> None:
+        c = self.cfg
+        if not c.is_moe_layer(layer):
+            return
+        with self._on_lane(mb.lane, after_main=False):
+            with nvtx_range(f"AFD_AG_Combine_L{layer}_mb{mb.lane}"):
+                self.client.combine(mb.lane, layer, mb.T, mb.topk_w, mb.topk_idx, mb.residual,
+                                    self._next_norm_weight(layer), c.rms_eps, extra=mb.extra,
+                                    scale=c.routed_scaling_factor, offset1=c.norm_offset1, normed_out=mb.normed)
+        self._join_lane(mb.lane)
+
+    def _pipeline(self, mbs: List[_MbCtx]) -> None:
+        """All layers for all micro-batches; on return mb.normed holds the final-norm output."""
+        m, L = self.model, self.cfg.num_layers
+        for mb in mbs:
+            h = m.embed(mb.ids)
+            mb.residual.copy_(h)
+            n0 = ops.rmsnorm(h, m.w["model.layers.0.input_layernorm.weight"], self.cfg.rms_eps, self.cfg.norm_offset1)
+            mb.normed.copy_(n0)
+            mb.keep += [h, n0]
+            self._compute(0, mb)
+        for l in range(L):
+            for mb in mbs:
+                self._combine(l, mb)
+                if l + 1 < L:
+                    self._compute(l + 1, mb)
+
+    # ------------------------------------------------------------------ decode
+    def _decode_ctx(self, lane: int, bucket: int, q_len: int = 1) -> _MbCtx:
+        b = self.bufs[lane]
+        T = bucket * q_len
+        meta = AttnMeta(positions=b.positions[:T], out_loc=b.out_loc[:T], page_table=b.page_table[:bucket],
+                        seq_lens=b.seq_lens[:bucket], q_len=q_len, state_slots=b.rows[:bucket].to(torch.int32) if self.gdn else None,
+                        status=self.status)
+        if self.cuda:
+            max_kv = self.max_seq_len
+            m_tiles = (self.model.hq // self.model.hkv * q_len + 15) // 16
+            meta.splits = self.decode_splits if hasattr(self, "decode_splits") else ops.pick_attn_splits(
+                bucket, self.model.hkv, m_tiles, min(max_kv, 4096))
+            if meta.splits > 1:
+                if b.workspace is None:
+                    b.workspace = ops.decode_attn_workspace(self.cap, self.model.hq, self.model.hkv, q_len,
+                                                            self.cfg.head_dim, 32, self.device)
+                meta.workspace = b.workspace
+        mb = _MbCtx(lane=lane, T=T, ids=b.ids[:T], meta=meta, x_moe=b.x_moe[:T], topk_idx=b.topk_idx[:T],
+                    topk_w=b.topk_w[:T], normed=b.normed[:T], residual=b.residual[:T])
+        mb.pad_from = T
+        return mb
+
+    def _prepare_decode_inputs(self, lane: int, bucket: int) -> None:
+        """From (rows, seq_lens): gather the page-table rows, positions, KV slots and the input
+        token of every request out of device state."""
+        b, ps = self.bufs[lane], self.page_size
+        rows, seq = b.rows[:bucket], b.seq_lens[:bucket]
+        pos = seq - 1
+        b.positions[:bucket].copy_(pos)
+        torch.index_select(self.page_table_all, 0, rows, out=b.page_table[:bucket])
+        page = torch.gather(b.page_table[:bucket], 1, (pos // ps).long()[:, None])[:, 0]
+        b.out_loc[:bucket].copy_(page * ps + pos % ps)
+        b.ids[:bucket].copy_(self.token_pool[rows, pos.long()])
+
+    def _sample_and_writeback(self, lane: int, mb: _MbCtx, bucket: int) -> None:
+        b = self.bufs[lane]
+        logits = self.model.lm_head(mb.normed)
+        b.logits = logits
+        ops.argmax(logits, out=b.next_tokens[:bucket]) if self.cuda else b.next_tokens[:bucket].copy_(ops.argmax(logits))
+        self.token_pool[b.rows[:bucket], b.seq_lens[:bucket].long()] = b.next_tokens[:bucket]
+
+    def _decode_body(self, bucket: int) -> None:
+        mbs = []
+        for lane in range(self.num_mb):
+            self._prepare_decode_inputs(lane, bucket)
+            mbs.append(self._decode_ctx(lane, bucket))
+        self._pipeline(mbs)
+        for lane, mb in enumerate(mbs):
+            self._sample_and_writeback(lane, mb, bucket)
+        self._last_mbs = mbs
+
+    def capture_decode_graph(self, bucket: int) -> None:
+        """Warm up eagerly (sets kernel attributes, primes allocators), then capture the whole
+        multi-stream decode step for this bucket."""
+        assert self.cuda
+        for b in self.bufs:          # warm up on padding rows only: no request state is touched
+            b.rows.fill_(self.dummy_row)
+            b.seq_lens.fill_(1)
+        with torch.cuda.stream(self.main_stream):
+            self._decode_body(bucket)
+        torch.cuda.synchronize(self.device)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=self.main_stream, capture_error_mode="thread_local"):
+            self._decode_body(bucket)
+        self.graphs[bucket] = g
+
+    def _stage_decode(self, plan: AgStepPlan) -> None:
+        for lane, mbp in enumerate(plan.mbs):
+            b, n = self.bufs[lane], len(mbp.rows)
+            if self.cuda:
+                b.host_in[0, :n] = torch.from_numpy(mbp.rows)
+                b.host_in[1, :n] = torch.from_numpy(mbp.seq_lens)
+                b.rows[:n].copy_(b.host_in[0, :n], non_blocking=True)
+                b.seq_lens[:n].copy_(b.host_in[1, :n], non_blocking=True)
+            else:
+                b.rows[:n] = torch.from_numpy(mbp.rows).long()
+                b.seq_lens[:n] = torch.from_numpy(mbp.seq_lens)
+
+    def launch_decode(self, plan: AgStepPlan) -> None:
+        """Queue one decode step (H2D of the plan, graph replay or eager body, D2H of tokens)."""
+        bucket = plan.bucket
+        ctx = torch.cuda.stream(self.main_stream) if self.cuda else nullcontext()
+        with ctx:
+            self.apply_grants(plan)
+            self._stage_decode(plan)
+            if self.cuda and self.rt.use_cuda_graph:
+                if bucket not in self.graphs:
+                    self.capture_decode_graph(bucket)
+                    self._stage_decode(plan)
+                self.graphs[bucket].replay()
+            else:
+                self._decode_body(bucket)
+            if plan.temperatures is not None:
+                self._resample(plan)
+            if self.cuda:
+                for lane in range(self.num_mb):
+                    b = self.bufs[lane]
+                    b.host_out[:bucket].copy_(b.next_tokens[:bucket], non_blocking=True)
+                self.d2h_event.record()
+
+    def finish_decode(self, plan: AgStepPlan) -> AgStepReply:
+        bucket = plan.bucket
+        if self.cuda:
+            self.d2h_event.synchronize()
+            toks = np.concatenate([self.bufs[l].host_out[:bucket].numpy().copy() for l in range(self.num_mb)])
+        else:
+            toks = np.concatenate([self.bufs[l].next_tokens[:bucket].numpy().copy() for l in range(self.num_mb)])
+        return AgStepReply(step_id=plan.step_id, rank=self.rank, next_tokens=toks.astype(np.int32),
+                           status=self.read_status())
+
+    def _resample(self, plan: AgStepPlan) -> None:
+        off = 0
+        for lane in range(self.num_mb):
+            b, n = self.bufs[lane], plan.bucket
+            t = torch.from_numpy(plan.temperatures[off:off + n]).to(self.device)
+            if bool((t > 0).any()):
+                toks = ref.sample(b.logits.float(), t, torch.from_numpy(plan.top_ks[off:off + n]).to(self.device),
+                                  torch.from_numpy(plan.top_ps[off:off + n]).to(self.device))
+                b.next_tokens[:n].copy_(toks)
+                self.token_pool[b.rows[:n], b.seq_lens[:n].long()] = b.next_tokens[:n]
+            off += n
+
+    # ------------------------------------------------------------------ prefill
+    def run_prefill(self, plan: AgStepPlan, mb_tokens: List[int]) -> AgStepReply:
+        """Eager chunked prefill. Each micro-batch is padded to mb_tokens[m] tokens (the count the
+        expert GPUs expect from every source this step); padding tokens are routed nowhere."""
+        ctx = torch.cuda.stream(self.main_stream) if self.cuda else nullcontext()
+        dev, ps = self.device, self.page_size
+        with ctx:
+            self.apply_grants(plan)
+            mbs: List[_MbCtx] = []
+            for lane, mbp in enumerate(plan.mbs):
+                T_real, T = int(mbp.extend_lens.sum()) if len(mbp.extend_lens) else 0, mb_tokens[lane]
+                pos = np.zeros(T, np.int32)
+                loc = np.full(T, -1, np.int32)
+                ids = np.zeros(T, np.int32)
+                off = 0
+                for r, (row, n, sl) in enumerate(zip(mbp.rows, mbp.extend_lens, mbp.seq_lens)):
+                    p = np.arange(sl - n, sl, dtype=np.int32)
+                    pos[off:off + n] = p
+                    loc[off:off + n] = self.page_table_host[row, p // ps] * ps + p % ps
+                    off += n
+                ids[:T_real] = mbp.input_ids
+                B = len(mbp.rows)
+                rows_t = torch.from_numpy(mbp.rows.astype(np.int64)).to(dev)
+                meta = AttnMeta(positions=torch.from_numpy(pos).to(dev), out_loc=torch.from_numpy(loc).to(dev),
+                                page_table=torch.from_numpy(self.page_table_host[mbp.rows]).to(dev) if B else
+                                torch.zeros(0, self.max_pages, dtype=torch.int32, device=dev),
+                                seq_lens=torch.from_numpy(mbp.seq_lens).to(dev), is_prefill=True,
+                                prefill_lens=[int(n) for n in mbp.extend_lens],
+                                state_slots=rows_t.to(torch.int32), status=self.status)
+                c = self.cfg
+                K = max(c.num_experts_per_tok, 1)
+                mb = _MbCtx(lane=lane, T=T, ids=torch.from_numpy(ids).to(dev), meta=meta,
+                            x_moe=torch.zeros(T, c.hidden_size, dtype=self.dtype, device=dev),
+                            topk_idx=torch.zeros(T, K, dtype=torch.int32, device=dev),
+                            topk_w=torch.zeros(T, K, dtype=torch.float32, device=dev),
+                            normed=torch.zeros(T, c.hidden_size, dtype=self.dtype, device=dev),
+                            residual=torch.zeros(T, c.hidden_size, dtype=self.dtype, device=dev))
+                mb.pad_from = T_real
+                mbs.append(mb)
+            self._pipeline(mbs)
+            out = []
+            for lane, (mb, mbp) in enumerate(zip(mbs, plan.mbs)):
+                B = len(mbp.rows)
+                toks = np.full(B, -1, np.int32)
+                if B and mbp.sample_rows.any():
+                    last = np.cumsum(mbp.extend_lens) - 1
+                    sel = torch.from_numpy(last[mbp.sample_rows]).long().to(dev)
+                    logits = self.model.lm_head(mb.normed[sel])
+                    t = ops.argmax(logits)
+                    if plan.temperatures is not None:
+                        base = sum(len(p.rows) for p in plan.mbs[:lane])
+                        mask = mbp.sample_rows
+                        temps = torch.from_numpy(plan.temperatures[base:base + B][mask]).to(dev)
+                        if bool((temps > 0).any()):
+                            t = ref.sample(logits.float(), temps, torch.from_numpy(plan.top_ks[base:base + B][mask]).to(dev),
+                                           torch.from_numpy(plan.top_ps[base:base + B][mask]).to(dev))
+                    rows_s = torch.from_numpy(mbp.rows[mbp.sample_rows].astype(np.int64)).to(dev)
+                    lens_s = torch.from_numpy(mbp.seq_lens[mbp.sample_rows].astype(np.int64)).to(dev)
+                    self.token_pool[rows_s, lens_s] = t.to(torch.int32)
+                    toks[mbp.sample_rows] = t.cpu().numpy()
+                out.append(toks)
+            if self.cuda:
+                torch.cuda.current_stream().synchronize()
+        return AgStepReply(step_id=plan.step_id, rank=self.rank,
+                           next_tokens=np.concatenate(out) if out else np.zeros(0, np.int32), status=self.read_status())
+
+    # ------------------------------------------------------------------ misc
+    def run_step(self, plan: AgStepPlan, mb_tokens: Optional[List[int]] = None) -> AgStepReply:
+        t0 = time.perf_counter()
+        if plan.phase == "prefill":
+            reply = self.run_prefill(plan, mb_tokens or [mb.num_tokens for mb in plan.mbs])
+        else:
+            self.launch_decode(plan)
+            reply = self.finish_decode(plan)
+        reply.step_ms = (time.perf_counter() - t0) * 1e3
+        return reply
+
+    def read_status(self) -> int:
+        code = int(self.status.item()) if self.status is not None else 0
+        for s in self.client.status_tensors():
+            code = code or int(s.item())
+        return code

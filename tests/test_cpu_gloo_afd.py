@@ -1,0 +1,60 @@
+"""Tiny Qwen3-MoE-shaped AFD decode on CPU/gloo: world 2 (rank 0 attention server, rank 1
+MLP server), fp32, 4 requests x 32 prompt tokens, 16 greedy tokens, 2 micro-batches. The
+output must match the single-process engine token for token. Also a 2+2 layout."""
+import os
+import socket
+import tempfile
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from fastafd_b200.config import PRESETS, RuntimeConfig
+from fastafd_b200.core import SamplingParams
+from fastafd_b200.engine import AfdEngine, SpmdDriver
+from fastafd_b200.protocol import AfdTopology
+
+
+def _rt():
+    return RuntimeConfig(model_path="tiny-qwen3-moe", num_mb=2, page_size=16, num_pages=64, max_running_requests=8,
+                         max_seq_len=128, cuda_graph_max_bs=8, device="cpu", dtype="float32", use_cuda_graph=False)
+
+
+def _prompts(cfg, n=4, length=32):
+    g = torch.Generator().manual_seed(0)
+    return [torch.randint(0, cfg.vocab_size, (length,), generator=g).tolist() for _ in range(n)]
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world, port, topo_kw, out_path, n_new):
+    os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    torch.set_num_threads(1)
+    cfg = PRESETS["tiny-qwen3-moe"]
+    topo = AfdTopology(**topo_kw)
+    eng = AfdEngine(cfg, _rt(), topo, rank, "cpu", seed=0)
+    out = SpmdDriver(eng).generate(_prompts(cfg), SamplingParams(max_tokens=n_new, ignore_eos=True))
+    if rank == 0:
+        torch.save(out, out_path)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("topo_kw", [dict(attn_dp=1, mlp_ep=1), dict(attn_dp=2, mlp_ep=2)])
+def test_gloo_afd_matches_single_process(topo_kw):
+    cfg = PRESETS["tiny-qwen3-moe"]
+    n_new = 16
+    single = AfdEngine(cfg, _rt(), AfdTopology(colocated=True), 0, "cpu", seed=0)
+    exp = SpmdDriver(single).generate(_prompts(cfg), SamplingParams(max_tokens=n_new, ignore_eos=True))
+    world = AfdTopology(**topo_kw).world
+    with tempfile.TemporaryDirectory() as d:
+        path = os.path.join(d, "out.pt")
+        mp.spawn(_worker, args=(world, _free_port(), topo_kw, path, n_new), nprocs=world, join=True)
+        got = torch.load(path)
+    assert got == exp
