@@ -236,6 +236,75 @@ class SpmdDriver:
             out += l.complete(sid, toks[lane])
         return out
 
+    # ------------------------------------------------------------------ steady-state decode
+    def install_prefilled(self, per_lane: int, prompt_len: int, max_tokens: int, seed: int = 0) -> None:
+        """Synthetic serving state: `per_lane` requests per attention lane whose prompts of
+        `prompt_len` tokens are taken as already prefilled. The KV cache of the attention ranks is
+        filled with N(0,1) values and each request's last token is a random id, so decode steps
+        do the same work as after a real prefill of random prompts."""
+        sp = SamplingParams(max_tokens=max_tokens, ignore_eos=True)
+        for lane in self.lanes:
+            for _ in range(per_lane):
+                uid = getattr(self, "_next_uid", 0)
+                self._next_uid = uid + 1
+                lane.add_prefilled(uid, prompt_len, sp)
+        a = self.e.attn
+        if a is not None:
+            g = torch.Generator(device=a.device).manual_seed(seed + 17 * self.e.rank)
+            for t in (a.kv.k, a.kv.v):
+                for li in range(t.shape[0]):
+                    t[li].normal_(0.0, 1.0, generator=g)
+            a.token_pool.copy_(torch.randint(0, self.e.cfg.vocab_size, a.token_pool.shape, generator=g,
+                                             device=a.device, dtype=torch.int32))
+
+    def run_decode_steps(self, n: int, pipelined: bool = True) -> int:
+        """n decode steps of the running batch through plan -> H2D -> replay -> D2H -> complete.
+        Requests must be greedy / ignore_eos with enough max_tokens left, so that every rank can
+        plan without exchanging tokens (the one-step-ahead assumption of the coordinator: step
+        N+1 is planned as if step N produced one token per request). With `pipelined`, step N+1
+        is planned and queued before step N's tokens are read back. Returns tokens generated by
+        this rank's lane."""
+        e, rt = self.e, self.e.rt
+        produced = 0
+        pending = None
+        for _ in range(n):
+            sid = self.step_id
+            self.step_id += 1
+            real = max(l.decode_real() for l in self.lanes)
+            bucket = select_bucket(per_mb_real(real, rt.num_mb), e.buckets)
+            plans = [l.schedule_decode(sid, bucket) for l in self.lanes]
+            if e.attn is not None:
+                mine = plans[self.my_lane]
+                e.attn.launch_decode(mine)
+                if pending is not None:
+                    produced += self._finish_fast(*pending)
+                    pending = None
+                if pipelined:
+                    pending = (sid, plans, mine)
+                else:
+                    produced += self._finish_fast(sid, plans, mine)
+            if e.expert is not None:
+                e.step(EgStepPlan(step_id=sid, phase="decode", tokens_per_mb=[bucket] * rt.num_mb))
+            if e.attn is None:
+                for lane, l in enumerate(self.lanes):
+                    l.complete(sid, np.zeros(sum(len(mb.rows) for mb in plans[lane].mbs), np.int32))
+        if pending is not None:
+            produced += self._finish_fast(*pending)
+        return produced
+
+    def _finish_fast(self, sid: int, plans, mine) -> int:
+        reply = self.e.attn.finish_decode(mine)
+        if reply.status:
+            raise RuntimeError(f"device status {reply.status} in step {sid}")
+        n = 0
+        for lane, l in enumerate(self.lanes):
+            size = sum(len(mb.rows) for mb in plans[lane].mbs)
+            toks = reply.next_tokens if lane == self.my_lane else np.zeros(size, np.int32)
+            out = l.complete(sid, toks)
+            if lane == self.my_lane:
+                n += sum(len(t) for _, t, _ in out)
+        return n
+
     def generate(self, prompts: Sequence[Sequence[int]], sampling: SamplingParams) -> List[List[int]]:
         uids = self.add_requests(prompts, sampling)
         results: Dict[int, List[int]] = {u: [] for u in uids}

@@ -150,6 +150,8 @@ def decode_attention(q, k_cache, v_cache, page_table, seq_lens, Hq, Hkv, D, q_le
                                      ptr(seq_lens), ptr(out), ptr(workspace), B, Hq, Hkv, D, q_len,
                                      page_size, page_table.shape[1], k_cache.shape[0], splits,
                                      sm_scale, ptr(status), cur_stream()), "decode_attention")
+    if splits > 1:
+        _lib.LAUNCHES["count"] += 1      # the split-merge kernel
     return out
 
 

@@ -122,8 +122,15 @@ def lib() -> C.CDLL:
     return handle
 
 
+# Kernel launches issued through this library since import (graph capture counts the
+# launches recorded into the graph once; replays are accounted for by the caller).
+LAUNCHES = {"count": 0}
+_KERNELS_PER_CALL = {"eg_group_gather": 2}
+
+
 def check(code: int, what: str) -> None:
     if code == 0:
+        LAUNCHES["count"] += _KERNELS_PER_CALL.get(what, 1)
         return
     if code > 0:
         msg = lib().afd_cuda_error_string(code).decode()

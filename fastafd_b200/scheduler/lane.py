@@ -64,6 +64,7 @@ class LaneScheduler:
         self.reserved_pages = 0
         self.records: Dict[int, StepRecord] = {}
         self._pending_free_rows: List[int] = []
+        self._carry_grants: List[Tuple[int, int, int]] = []     # grants made outside a plan
 
     # ------------------------------------------------------------------ admission
     def add_req(self, uid: int, input_ids: Sequence[int], sampling: SamplingParams) -> None:
@@ -75,6 +76,26 @@ class LaneScheduler:
         if self.cache.pages_for(total) > self.cache.num_pages - 1:
             raise AdmissionError(f"request {uid} needs more KV pages than the lane has")
         self.waiting.append(Req(uid=uid, input_ids=list(input_ids), sampling=sampling, lane=self.lane))
+
+    def add_prefilled(self, uid: int, prompt_len: int, sampling: SamplingParams, first_token: int = 0) -> Req:
+        """Admit a request whose prompt KV is already in the cache (synthetic benchmark state,
+        or a request migrated from a prefill instance): rows and pages are assigned now and the
+        page grants travel with the next plan."""
+        if not self.free_rows:
+            raise AdmissionError("no free request row")
+        req = Req(uid=uid, input_ids=[0] * prompt_len, sampling=sampling, lane=self.lane)
+        req.table_idx = self.free_rows.pop()
+        need = self.cache.pages_for(req.max_total_len + self.spec_block)
+        if self.reserved_pages + need > self.cache.num_pages - 1:
+            self.free_rows.append(req.table_idx)
+            raise AdmissionError(f"request {uid} needs {need} pages; lane has {self.cache.num_pages - 1 - self.reserved_pages}")
+        st = _ReqState(req, planned_len=prompt_len, planned_out=1, reserved_pages=need)
+        req.cached_len = prompt_len
+        req.output_ids = [first_token]
+        self.reserved_pages += need
+        self.states[uid] = st
+        self._grow_pages(st, prompt_len + 1, self._carry_grants)
+        return req
 
     def abort(self, uid: int) -> None:
         for r in list(self.waiting):
@@ -161,7 +182,8 @@ class LaneScheduler:
     def _finish_plan(self, step_id: int, phase: str, bucket: int, mbs: List[MicroBatchPlan],
                      grants: List[Tuple[int, int, int]], record: StepRecord,
                      sampling_rows: List[Optional[_ReqState]]) -> AgStepPlan:
-        g = np.asarray(grants, dtype=np.int32).reshape(-1, 3)
+        g = np.asarray(self._carry_grants + grants, dtype=np.int32).reshape(-1, 3)
+        self._carry_grants = []
         plan = AgStepPlan(step_id=step_id, phase=phase, bucket=bucket, mbs=mbs,
                           grant_rows=g[:, 0].copy(), grant_slots=g[:, 1].copy(), grant_pages=g[:, 2].copy(),
                           free_rows=np.asarray(self._pending_free_rows, dtype=np.int32), spec_block=self.spec_block)

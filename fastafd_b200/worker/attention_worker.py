@@ -39,6 +39,9 @@ from ..utils.trace import nvtx_range
 from .moe_client import MoeClient
 
 
+RING = 3   # pinned staging slots: up to two steps in flight plus the one being written
+
+
 @dataclass
 class _MbBuffers:
     """Static device buffers of one micro-batch (capacity = largest decode bucket)."""
@@ -55,8 +58,8 @@ class _MbBuffers:
     residual: torch.Tensor
     next_tokens: torch.Tensor
     logits: Optional[torch.Tensor] = None
-    host_in: Optional[torch.Tensor] = None      # pinned [2, cap] int32: rows, seq_lens
-    host_out: Optional[torch.Tensor] = None     # pinned [cap] int32
+    host_in: Optional[torch.Tensor] = None      # pinned [RING, 2, cap] int32: rows, seq_lens
+    host_out: Optional[torch.Tensor] = None     # pinned [RING, cap] int32
     workspace: Optional[torch.Tensor] = None
 
 
@@ -119,11 +122,12 @@ class AttentionWorker:
         self.cap = max_bucket or max(rt.cuda_graph_max_bs, 1)
         self.bufs = [self._make_bufs(self.cap) for _ in range(self.num_mb)]
         self.graphs: Dict[int, "torch.cuda.CUDAGraph"] = {}
-        self.kernel_launches = 0
+        self.kernels_per_step: Dict[int, int] = {}
         if self.cuda:
             self.main_stream = torch.cuda.Stream(self.device)
             self.lane_streams = [torch.cuda.Stream(self.device) for _ in range(self.num_mb)]
-            self.d2h_event = torch.cuda.Event()
+            self.d2h_events = [torch.cuda.Event() for _ in range(RING)]
+            self.status_host = torch.zeros(RING, 4, dtype=torch.int32).pin_memory()
 
     # ------------------------------------------------------------------ buffers
     def _make_bufs(self, cap: int) -> _MbBuffers:
@@ -138,8 +142,8 @@ class AttentionWorker:
         b.rows.fill_(self.dummy_row)
         b.seq_lens.fill_(1)
         if self.cuda:
-            b.host_in = torch.zeros(2, cap, dtype=torch.int32).pin_memory()
-            b.host_out = torch.zeros(cap, dtype=torch.int32).pin_memory()
+            b.host_in = torch.zeros(RING, 2, cap, dtype=torch.int32).pin_memory()
+            b.host_out = torch.zeros(RING, cap, dtype=torch.int32).pin_memory()
         return b
 
     # ------------------------------------------------------------------ plan application
@@ -155,6 +159,9 @@ class AttentionWorker:
         else:
             self.page_table_all[torch.from_numpy(plan.grant_rows).long(), torch.from_numpy(plan.grant_slots).long()] = \
                 torch.from_numpy(plan.grant_pages)
+
+    def d2h_bytes(self, plan: AgStepPlan) -> int:
+        return sum(len(mb.rows) * 4 for mb in plan.mbs) + 4 * (1 + len(self.client.status_tensors()))
 
     def h2d_bytes(self, plan: AgStepPlan) -> int:
         n = sum(2 * len(mb.rows) * 4 for mb in plan.mbs) + 3 * 8 * len(plan.grant_rows)
@@ -297,19 +304,24 @@ class AttentionWorker:
         with torch.cuda.stream(self.main_stream):
             self._decode_body(bucket)
         torch.cuda.synchronize(self.device)
+        from ..ops._lib import LAUNCHES
+
         g = torch.cuda.CUDAGraph()
+        c0 = LAUNCHES["count"]
         with torch.cuda.graph(g, stream=self.main_stream, capture_error_mode="thread_local"):
             self._decode_body(bucket)
+        self.kernels_per_step[bucket] = LAUNCHES["count"] - c0     # library kernels in one replay
         self.graphs[bucket] = g
 
     def _stage_decode(self, plan: AgStepPlan) -> None:
+        slot = plan.step_id % RING
         for lane, mbp in enumerate(plan.mbs):
             b, n = self.bufs[lane], len(mbp.rows)
             if self.cuda:
-                b.host_in[0, :n] = torch.from_numpy(mbp.rows)
-                b.host_in[1, :n] = torch.from_numpy(mbp.seq_lens)
-                b.rows[:n].copy_(b.host_in[0, :n], non_blocking=True)
-                b.seq_lens[:n].copy_(b.host_in[1, :n], non_blocking=True)
+                b.host_in[slot, 0, :n] = torch.from_numpy(mbp.rows)
+                b.host_in[slot, 1, :n] = torch.from_numpy(mbp.seq_lens)
+                b.rows[:n].copy_(b.host_in[slot, 0, :n], non_blocking=True)
+                b.seq_lens[:n].copy_(b.host_in[slot, 1, :n], non_blocking=True)
             else:
                 b.rows[:n] = torch.from_numpy(mbp.rows).long()
                 b.seq_lens[:n] = torch.from_numpy(mbp.seq_lens)
@@ -327,24 +339,33 @@ class AttentionWorker:
                     self._stage_decode(plan)
                 self.graphs[bucket].replay()
             else:
+                from ..ops._lib import LAUNCHES
+
+                c0 = LAUNCHES["count"]
                 self._decode_body(bucket)
+                self.kernels_per_step[bucket] = LAUNCHES["count"] - c0
             if plan.temperatures is not None:
                 self._resample(plan)
             if self.cuda:
+                slot = plan.step_id % RING
                 for lane in range(self.num_mb):
                     b = self.bufs[lane]
-                    b.host_out[:bucket].copy_(b.next_tokens[:bucket], non_blocking=True)
-                self.d2h_event.record()
+                    b.host_out[slot, :bucket].copy_(b.next_tokens[:bucket], non_blocking=True)
+                for i, st in enumerate([self.status] + self.client.status_tensors()):
+                    self.status_host[slot, i:i + 1].copy_(st, non_blocking=True)
+                self.d2h_events[slot].record()
 
     def finish_decode(self, plan: AgStepPlan) -> AgStepReply:
         bucket = plan.bucket
         if self.cuda:
-            self.d2h_event.synchronize()
-            toks = np.concatenate([self.bufs[l].host_out[:bucket].numpy().copy() for l in range(self.num_mb)])
+            slot = plan.step_id % RING
+            self.d2h_events[slot].synchronize()
+            toks = np.concatenate([self.bufs[l].host_out[slot, :bucket].numpy().copy() for l in range(self.num_mb)])
+            status = int(self.status_host[slot].max())
         else:
             toks = np.concatenate([self.bufs[l].next_tokens[:bucket].numpy().copy() for l in range(self.num_mb)])
-        return AgStepReply(step_id=plan.step_id, rank=self.rank, next_tokens=toks.astype(np.int32),
-                           status=self.read_status())
+            status = self.read_status()
+        return AgStepReply(step_id=plan.step_id, rank=self.rank, next_tokens=toks.astype(np.int32), status=status)
 
     def _resample(self, plan: AgStepPlan) -> None:
         off = 0

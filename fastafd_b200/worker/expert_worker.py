@@ -29,6 +29,7 @@ class ExpertWorker:
         self.cuda = self.device.type == "cuda"
         self.status = status
         self.graphs: Dict[tuple, "torch.cuda.CUDAGraph"] = {}
+        self.kernels_per_step = 0
         if self.cuda:
             self.stream = torch.cuda.Stream(self.device)
 
@@ -47,9 +48,13 @@ class ExpertWorker:
                     if key not in self.graphs:
                         self._body(list(key))                    # eager pass: pairs with the peers' warm-up
                         torch.cuda.synchronize(self.device)
+                        from ..ops._lib import LAUNCHES
+
                         g = torch.cuda.CUDAGraph()
+                        c0 = LAUNCHES["count"]
                         with torch.cuda.graph(g, stream=self.stream, capture_error_mode="thread_local"):
                             self._body(list(key))
+                        self.kernels_per_step = LAUNCHES["count"] - c0
                         self.graphs[key] = g
                     self.graphs[key].replay()
                 else:
