@@ -4,11 +4,12 @@
 // kv_len - q_len + 1 + j cached tokens).
 //
 // The op is bound by reading the KV cache once: every CTA owns one (request, kv head,
-// 16-row query tile, KV split); each of its 4 warps streams its own 32- (or 16-)token
-// KV tiles through a private 2-stage cp.async ring, computes S = Q K^T and O += P V
+// 16-row query tile, KV split); each of its 4 warps streams its own 16-token
+// KV tiles through a private 3-stage cp.async ring, computes S = Q K^T and O += P V
 // with bf16 mma.sync (tensor throughput is not the limit here; bytes are) and keeps
-// a private online-softmax state. Warps merge through shared memory, splits merge in
-// a second small kernel through an fp32 workspace.
+// a private online-softmax state. Warps merge through shared memory; splits merge in
+// the same launch: each split CTA writes its partial to an fp32 workspace and the last one
+// to arrive (a counter per output tile, which it resets) combines them.
 //
 // Reference behaviour: the trtllm-gen paged decode call in
 // python/minisgl/attention/trtllm.py:136-178 (bf16 KV, NHD pages, q_len_per_req for
@@ -53,7 +54,8 @@ struct DecodeAttnArgs {
   __nv_bfloat16* out;            // [B*q_len][Hq][D]
   float* part_o;                 // [B][Hkv][m_tiles][splits][16][D]
   float* part_lse;               // [B][Hkv][m_tiles][splits][16]
-  int B, Hq, Hkv, q_len, page_size, max_pages, splits, m_tiles;
+  unsigned int* part_count;      // [B][Hkv][m_tiles] arrival counters (zero between launches)
+  int B, Hq, Hkv, q_len, page_size, page_shift, max_pages, splits, m_tiles;
   long cache_slots;
   float scale_log2;              // softmax scale * log2(e)
   int* status;
@@ -66,13 +68,27 @@ __device__ __forceinline__ uint32_t tile_off(int row, int chunk) {
   return static_cast<uint32_t>(row * D * 2 + ((chunk ^ (row & 7)) << 4));
 }
 
-template <int D, int TOK>
-__global__ void __launch_bounds__(128, 1) decode_attn_kernel(const DecodeAttnArgs a) {
+template <int D>
+struct AttnCfg {
+  static constexpr int TOK = 16;                       // KV tokens per warp tile
+  static constexpr int STAGES = D <= 128 ? 3 : 2;      // cp.async ring depth per warp
+  static constexpr int TILE_BYTES = TOK * D * 2;       // one of K / V
+  static constexpr int WARP_BYTES = STAGES * 2 * TILE_BYTES;
+  static constexpr int MERGE_BYTES = (16 * D + 32) * 4;
+  static constexpr int WARP_REGION = WARP_BYTES > MERGE_BYTES ? WARP_BYTES : MERGE_BYTES;
+  static constexpr int SMEM = 16 * D * 2 + 4 * WARP_REGION;
+  static constexpr int CTAS_PER_SM = (220 * 1024) / SMEM >= 2 ? 2 : 1;
+};
+
+template <int D>
+__global__ void __launch_bounds__(128, AttnCfg<D>::CTAS_PER_SM) decode_attn_kernel(const DecodeAttnArgs a) {
+  using Cfg = AttnCfg<D>;
+  constexpr int TOK = Cfg::TOK;
   constexpr int CH = D / 8;            // 16-byte chunks per row
   constexpr int KT = D / 16;           // k-steps of S
-  constexpr int NT = TOK / 8;          // n-tiles of S
-  constexpr int TILE_BYTES = TOK * D * 2;
-  constexpr int WARP_BYTES = 4 * TILE_BYTES;   // 2 stages x (K + V)
+  constexpr int NT = TOK / 8;          // n-tiles of S (2)
+  constexpr int TILE_BYTES = Cfg::TILE_BYTES;
+  constexpr bool Q_REGS = D <= 128;
   extern __shared__ __align__(128) uint8_t smem[];
   uint8_t* sq = smem;                          // Q tile 16 x D
   uint8_t* swarp = smem + 16 * D * 2;
@@ -102,44 +118,98 @@ __global__ void __launch_bounds__(128, 1) decode_attn_kernel(const DecodeAttnArg
   }
   __syncthreads();
 
-  // ---- this CTA's KV range ----
-  const int per_split = ((kv_len + a.splits - 1) / a.splits + TOK * 4 - 1) / (TOK * 4) * (TOK * 4);
+  // ---- this CTA's KV range: only what the rows of this tile may see (causal) ----
+  const int j_max = min((mt * 16 + 15) / G, a.q_len - 1);
+  const int visible = max(0, kv_len - a.q_len + 1 + j_max);
+  const int per_split = ((visible + a.splits - 1) / a.splits + TOK * 4 - 1) / (TOK * 4) * (TOK * 4);
   const int kv_begin = split * per_split;
-  const int kv_end = min(kv_len, kv_begin + per_split);
+  const int kv_end = min(visible, kv_begin + per_split);
   const int n_tiles = kv_end > kv_begin ? (kv_end - kv_begin + TOK - 1) / TOK : 0;
 
-  uint8_t* my = swarp + warp * WARP_BYTES;
+  uint8_t* my = swarp + warp * Cfg::WARP_REGION;
   const int* pt = a.page_table + static_cast<size_t>(b) * a.max_pages;
+  const uint32_t ps_mask = static_cast<uint32_t>(a.page_size - 1);
 
+  // One tile = 16 rows of K and of V. Lane r (< 16) resolves row r's cache slot once; the
+  // warp then issues whole rows, one 16-byte chunk per lane.
   auto load_tile = [&](int tile, int stage) {
     uint8_t* sk = my + stage * 2 * TILE_BYTES;
     uint8_t* sv = sk + TILE_BYTES;
     const int t0 = kv_begin + tile * TOK;
-    for (int idx = lane; idx < TOK * CH; idx += 32) {
-      const int r = idx / CH, c = idx % CH;
-      const int t = t0 + r;
+    long my_slot = -1;
+    if (lane < TOK) {
+      const int t = t0 + lane;
       if (t < kv_end) {
-        const int page = pt[t / a.page_size];
-        const long slot = static_cast<long>(page) * a.page_size + (t % a.page_size);
-        if (slot >= 0 && slot < a.cache_slots) {
-          const size_t off = (static_cast<size_t>(slot) * a.Hkv + kvh) * D + c * 8;
-          cp_async16(sk + tile_off<D>(r, c), a.k_cache + off);
-          cp_async16(sv + tile_off<D>(r, c), a.v_cache + off);
-          continue;
+        const int page = pt[t >> a.page_shift];
+        my_slot = static_cast<long>(page) * a.page_size + (t & ps_mask);
+        if (my_slot < 0 || my_slot >= a.cache_slots) {
+          set_status(a.status, kStatusBadExtent);
+          my_slot = -1;
         }
-        set_status(a.status, kStatusBadExtent);
       }
-      *reinterpret_cast<uint4*>(sk + tile_off<D>(r, c)) = make_uint4(0, 0, 0, 0);
-      *reinterpret_cast<uint4*>(sv + tile_off<D>(r, c)) = make_uint4(0, 0, 0, 0);
+    }
+    constexpr int PER_ROW = 2 * CH;                       // chunks of K and V in one row
+    if constexpr (PER_ROW <= 32) {
+      constexpr int ROWS_PER_IT = 32 / PER_ROW;
+      const int rsub = lane / PER_ROW, c2 = lane % PER_ROW;
+      const bool is_v = c2 >= CH;
+      const int c = is_v ? c2 - CH : c2;
+#pragma unroll
+      for (int r0 = 0; r0 < TOK; r0 += ROWS_PER_IT) {
+        const int r = r0 + rsub;
+        const long slot = __shfl_sync(0xffffffffu, my_slot, r);
+        uint8_t* dst = (is_v ? sv : sk) + tile_off<D>(r, c);
+        if (slot >= 0) {
+          const size_t off = (static_cast<size_t>(slot) * a.Hkv + kvh) * D + c * 8;
+          cp_async16(dst, (is_v ? a.v_cache : a.k_cache) + off);
+        } else {
+          *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
+        }
+      }
+    } else {
+#pragma unroll 4
+      for (int r = 0; r < TOK; ++r) {
+        const long slot = __shfl_sync(0xffffffffu, my_slot, r);
+#pragma unroll
+        for (int c = lane; c < CH; c += 32) {
+          if (slot >= 0) {
+            const size_t off = (static_cast<size_t>(slot) * a.Hkv + kvh) * D + c * 8;
+            cp_async16(sk + tile_off<D>(r, c), a.k_cache + off);
+            cp_async16(sv + tile_off<D>(r, c), a.v_cache + off);
+          } else {
+            *reinterpret_cast<uint4*>(sk + tile_off<D>(r, c)) = make_uint4(0, 0, 0, 0);
+            *reinterpret_cast<uint4*>(sv + tile_off<D>(r, c)) = make_uint4(0, 0, 0, 0);
+          }
+        }
+      }
     }
   };
+
+  // prologue: fill STAGES-1 stages
+  int next_tile = warp;
+#pragma unroll
+  for (int s = 0; s < Cfg::STAGES - 1; ++s) {
+    if (next_tile < n_tiles) load_tile(next_tile, s);
+    cp_async_commit();
+    next_tile += 4;
+  }
+
+  const uint32_t sqa = smem_u32(sq);
+  uint32_t qreg[Q_REGS ? KT : 1][4];
+  if constexpr (Q_REGS) {
+#pragma unroll
+    for (int ks = 0; ks < KT; ++ks) {
+      const int mat = lane >> 3;
+      const int row = (mat & 1) * 8 + (lane & 7);
+      ldsm_x4(sqa + tile_off<D>(row, ks * 2 + (mat >> 1)), qreg[ks][0], qreg[ks][1], qreg[ks][2], qreg[ks][3]);
+    }
+  }
 
   float o[D / 8][4];
 #pragma unroll
   for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
   float m_run[2] = {-INFINITY, -INFINITY};
   float l_run[2] = {0.f, 0.f};
-  // causal limit per row (rows lane/4 and lane/4 + 8)
   int lim[2];
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
@@ -148,18 +218,20 @@ __global__ void __launch_bounds__(128, 1) decode_attn_kernel(const DecodeAttnArg
     lim[h] = row < M ? kv_len - a.q_len + 1 + j : 0;
   }
 
-  int it = 0;
-  if (warp < n_tiles) load_tile(warp, 0);
-  cp_async_commit();
-  for (int tile = warp; tile < n_tiles; tile += 4, ++it) {
-    const int stage = it & 1;
-    if (tile + 4 < n_tiles) load_tile(tile + 4, stage ^ 1);
-    cp_async_commit();
-    cp_async_wait<1>();
+  int stage = 0;
+  for (int tile = warp; tile < n_tiles; tile += 4) {
+    // keep the ring full: the stage consumed in the previous iteration is free now
+    {
+      int ls = stage + Cfg::STAGES - 1;
+      if (ls >= Cfg::STAGES) ls -= Cfg::STAGES;
+      if (next_tile < n_tiles) load_tile(next_tile, ls);
+      cp_async_commit();
+      next_tile += 4;
+    }
+    cp_async_wait<Cfg::STAGES - 1>();
     __syncwarp();
     const uint32_t sk = smem_u32(my + stage * 2 * TILE_BYTES);
     const uint32_t sv = sk + TILE_BYTES;
-    const uint32_t sqa = smem_u32(sq);
 
     float s[NT][4];
 #pragma unroll
@@ -167,20 +239,19 @@ __global__ void __launch_bounds__(128, 1) decode_attn_kernel(const DecodeAttnArg
 #pragma unroll
     for (int ks = 0; ks < KT; ++ks) {
       uint32_t qa[4];
-      {
+      if constexpr (Q_REGS) {
+        qa[0] = qreg[ks][0]; qa[1] = qreg[ks][1]; qa[2] = qreg[ks][2]; qa[3] = qreg[ks][3];
+      } else {
         const int mat = lane >> 3;
         const int row = (mat & 1) * 8 + (lane & 7);
         ldsm_x4(sqa + tile_off<D>(row, ks * 2 + (mat >> 1)), qa[0], qa[1], qa[2], qa[3]);
       }
-#pragma unroll
-      for (int np = 0; np < NT / 2; ++np) {
-        const int mat = lane >> 3;
-        const int row = np * 16 + (mat >> 1) * 8 + (lane & 7);
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4(sk + tile_off<D>(row, ks * 2 + (mat & 1)), b0, b1, b2, b3);
-        mma_bf16_16816(s[np * 2], qa, b0, b1);
-        mma_bf16_16816(s[np * 2 + 1], qa, b2, b3);
-      }
+      const int mat = lane >> 3;
+      const int row = (mat >> 1) * 8 + (lane & 7);
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4(sk + tile_off<D>(row, ks * 2 + (mat & 1)), b0, b1, b2, b3);
+      mma_bf16_16816(s[0], qa, b0, b1);
+      mma_bf16_16816(s[1], qa, b2, b3);
     }
     // ---- mask + online softmax ----
     const int t0 = kv_begin + tile * TOK;
@@ -214,7 +285,7 @@ __global__ void __launch_bounds__(128, 1) decode_attn_kernel(const DecodeAttnArg
       o[i][2] *= corr[1];
       o[i][3] *= corr[1];
     }
-    uint32_t pa[NT / 2][4];
+    uint32_t pa[4];
 #pragma unroll
     for (int n = 0; n < NT; ++n) {
       float p[4];
@@ -224,23 +295,21 @@ __global__ void __launch_bounds__(128, 1) decode_attn_kernel(const DecodeAttnArg
         p[e] = (m_run[h] == -INFINITY) ? 0.f : exp2f(s[n][e] - m_run[h]);
         l_run[h] += p[e];
       }
-      pa[n / 2][(n & 1) * 2 + 0] = pack_bf16(p[0], p[1]);
-      pa[n / 2][(n & 1) * 2 + 1] = pack_bf16(p[2], p[3]);
+      pa[n * 2 + 0] = pack_bf16(p[0], p[1]);
+      pa[n * 2 + 1] = pack_bf16(p[2], p[3]);
     }
-    // ---- O += P V ----
+    // ---- O += P V (one k-step of 16 tokens) ----
 #pragma unroll
-    for (int ks = 0; ks < TOK / 16; ++ks) {
-#pragma unroll
-      for (int dp = 0; dp < D / 16; ++dp) {
-        const int mat = lane >> 3;
-        const int row = ks * 16 + (mat & 1) * 8 + (lane & 7);
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4_t(sv + tile_off<D>(row, dp * 2 + (mat >> 1)), b0, b1, b2, b3);
-        mma_bf16_16816(o[dp * 2], pa[ks], b0, b1);
-        mma_bf16_16816(o[dp * 2 + 1], pa[ks], b2, b3);
-      }
+    for (int dp = 0; dp < D / 16; ++dp) {
+      const int mat = lane >> 3;
+      const int row = (mat & 1) * 8 + (lane & 7);
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4_t(sv + tile_off<D>(row, dp * 2 + (mat >> 1)), b0, b1, b2, b3);
+      mma_bf16_16816(o[dp * 2], pa, b0, b1);
+      mma_bf16_16816(o[dp * 2 + 1], pa, b2, b3);
     }
     __syncwarp();
+    if (++stage == Cfg::STAGES) stage = 0;
   }
   cp_async_wait<0>();
 #pragma unroll
@@ -269,15 +338,16 @@ __global__ void __launch_bounds__(128, 1) decode_attn_kernel(const DecodeAttnArg
     wl[(lane >> 2) + 8] = l_run[1];
   }
   __syncthreads();
+  const size_t tile_id = (static_cast<size_t>(b) * a.Hkv + kvh) * a.m_tiles + mt;
   for (int idx = threadIdx.x; idx < 16 * D; idx += 128) {
     const int r = idx / D, d = idx % D;
     float mm = -INFINITY;
 #pragma unroll
-    for (int w = 0; w < 4; ++w) mm = fmaxf(mm, reinterpret_cast<float*>(swarp + w * WARP_BYTES)[16 * D + r]);
+    for (int w = 0; w < 4; ++w) mm = fmaxf(mm, reinterpret_cast<float*>(swarp + w * Cfg::WARP_REGION)[16 * D + r]);
     float acc = 0.f, l = 0.f;
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
-      const float* base = reinterpret_cast<float*>(swarp + w * WARP_BYTES);
+      const float* base = reinterpret_cast<float*>(swarp + w * Cfg::WARP_REGION);
       const float mw = base[16 * D + r];
       const float f = (mw == -INFINITY) ? 0.f : exp2f(mw - mm);
       acc += base[r * D + d] * f;
@@ -291,57 +361,58 @@ __global__ void __launch_bounds__(128, 1) decode_attn_kernel(const DecodeAttnArg
         a.out[((static_cast<size_t>(b) * a.q_len + j) * a.Hq + kvh * G + g) * D + d] = __float2bfloat16(val);
       }
     } else {
-      const size_t pidx = ((static_cast<size_t>(b) * a.Hkv + kvh) * a.m_tiles + mt) * a.splits + split;
+      const size_t pidx = tile_id * a.splits + split;
       a.part_o[(pidx * 16 + r) * D + d] = val;
       if (d == 0) a.part_lse[pidx * 16 + r] = l > 0.f ? mm + log2f(l) : -INFINITY;
     }
   }
-}
+  if (a.splits == 1) return;
 
-template <int D>
-__global__ void decode_attn_merge_kernel(const DecodeAttnArgs a) {
-  const int kvh = blockIdx.y / a.m_tiles, mt = blockIdx.y % a.m_tiles;
-  const int b = blockIdx.z;
-  const int r = blockIdx.x;   // row within the 16-row tile
-  const int G = a.Hq / a.Hkv;
-  const int M = G * a.q_len;
-  const int row = mt * 16 + r;
-  if (row >= M) return;
-  const size_t p0 = ((static_cast<size_t>(b) * a.Hkv + kvh) * a.m_tiles + mt) * a.splits;
-  float mm = -INFINITY;
-  for (int s = 0; s < a.splits; ++s) mm = fmaxf(mm, a.part_lse[(p0 + s) * 16 + r]);
-  const int j = row / G, g = row % G;
-  __nv_bfloat16* dst = a.out + ((static_cast<size_t>(b) * a.q_len + j) * a.Hq + kvh * G + g) * D;
-  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+  // ---- the last split CTA of this (request, kv head, row tile) merges the splits ----
+  __shared__ int s_last;
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned int prev = atomicAdd(a.part_count + tile_id, 1u);
+    s_last = (prev == static_cast<unsigned int>(a.splits) - 1u);
+    if (s_last) a.part_count[tile_id] = 0;     // ready for the next launch
+  }
+  __syncthreads();
+  if (!s_last) return;
+  __threadfence();
+  const size_t p0 = tile_id * a.splits;
+  for (int idx = threadIdx.x; idx < 16 * D; idx += 128) {
+    const int r = idx / D, d = idx % D;
+    const int row = mt * 16 + r;
+    if (row >= M) continue;
+    float mm = -INFINITY;
+    for (int s2 = 0; s2 < a.splits; ++s2) mm = fmaxf(mm, __ldcg(a.part_lse + (p0 + s2) * 16 + r));
     float acc = 0.f, wsum = 0.f;
-    for (int s = 0; s < a.splits; ++s) {
-      const float lse = a.part_lse[(p0 + s) * 16 + r];
+    for (int s2 = 0; s2 < a.splits; ++s2) {
+      const float lse = __ldcg(a.part_lse + (p0 + s2) * 16 + r);
       const float w = (lse == -INFINITY) ? 0.f : exp2f(lse - mm);
-      acc += a.part_o[((p0 + s) * 16 + r) * D + d] * w;
+      acc += __ldcg(a.part_o + ((p0 + s2) * 16 + r) * D + d) * w;
       wsum += w;
     }
-    dst[d] = __float2bfloat16(wsum > 0.f ? acc / wsum : 0.f);
+    const int j = row / G, g = row % G;
+    a.out[((static_cast<size_t>(b) * a.q_len + j) * a.Hq + kvh * G + g) * D + d] =
+        __float2bfloat16(wsum > 0.f ? acc / wsum : 0.f);
   }
 }
 
-template <int D, int TOK>
+template <int D>
 static int launch_decode(const DecodeAttnArgs& a, cudaStream_t st) {
-  constexpr int smem = 16 * D * 2 + 4 * 4 * TOK * D * 2;
-  auto kern = decode_attn_kernel<D, TOK>;
+  using Cfg = AttnCfg<D>;
+  auto kern = decode_attn_kernel<D>;
   static bool set = false;
   if (!set) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
     if (e != cudaSuccess) return static_cast<int>(e);
     set = true;
   }
   dim3 grid(a.splits, a.Hkv * a.m_tiles, a.B);
-  kern<<<grid, 128, smem, st>>>(a);
+  kern<<<grid, 128, Cfg::SMEM, st>>>(a);
   AFD_CHECK_LAUNCH();
-  if (a.splits > 1) {
-    dim3 g2(16, a.Hkv * a.m_tiles, a.B);
-    decode_attn_merge_kernel<D><<<g2, D / 2 > 32 ? D / 2 : 32, 0, st>>>(a);
-    AFD_CHECK_LAUNCH();
-  }
   return 0;
 }
 
@@ -352,7 +423,8 @@ extern "C" long afd_decode_attn_workspace_bytes(int B, int Hq, int Hkv, int q_le
   const int G = Hq / Hkv;
   const long m_tiles = (G * q_len + 15) / 16;
   const long tiles = static_cast<long>(B) * Hkv * m_tiles * splits;
-  return tiles * 16 * D * 4 + tiles * 16 * 4;
+  // partial outputs, partial log-sum-exps, and one arrival counter per (request, head, row tile)
+  return tiles * 16 * D * 4 + tiles * 16 * 4 + static_cast<long>(B) * Hkv * m_tiles * 4;
 }
 
 extern "C" int afd_decode_attention(const void* q, const void* k_cache, const void* v_cache,
@@ -380,9 +452,13 @@ extern "C" int afd_decode_attention(const void* q, const void* k_cache, const vo
   const long tiles = static_cast<long>(B) * Hkv * a.m_tiles * splits;
   a.part_o = static_cast<float*>(workspace);
   a.part_lse = a.part_o ? a.part_o + tiles * 16 * D : nullptr;
+  a.part_count = a.part_o ? reinterpret_cast<unsigned int*>(a.part_lse + tiles * 16) : nullptr;
+  if ((page_size & (page_size - 1)) != 0) return -4;     // page sizes are powers of two
+  a.page_shift = 0;
+  while ((1 << a.page_shift) < page_size) ++a.page_shift;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (D == 128) return launch_decode<128, 32>(a, st);
-  if (D == 256) return launch_decode<256, 16>(a, st);
-  if (D == 64) return launch_decode<64, 32>(a, st);
+  if (D == 128) return launch_decode<128>(a, st);
+  if (D == 256) return launch_decode<256>(a, st);
+  if (D == 64) return launch_decode<64>(a, st);
   return -3;
 }

@@ -305,29 +305,20 @@ __global__ void topk_route_kernel(const float* __restrict__ logits, const float*
   }
 }
 
-// Arg-max over the vocabulary, one CTA per token; ties to the lowest index.
-template <typename T>
-__global__ void argmax_kernel(const T* __restrict__ logits, int* __restrict__ out, int V, long ld) {
-  __shared__ float sv[32];
-  __shared__ int si[32];
-  const T* lr = logits + static_cast<size_t>(blockIdx.x) * ld;
-  float best = -INFINITY;
-  int bi = 0x7fffffff;
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    const float v = static_cast<float>(lr[i]);
-    if (v > best) {
-      best = v;
-      bi = i;
-    }
+// Arg-max over the vocabulary; ties to the lowest index. Two phases so that a handful of
+// tokens still fills the GPU: grid (chunks, T) writes one (value, index) candidate per
+// chunk, then one CTA per token reduces the candidates.
+__device__ __forceinline__ void argmax_combine(float& best, int& bi, float ob, int oi) {
+  if (ob > best || (ob == best && oi < bi)) {
+    best = ob;
+    bi = oi;
   }
+}
+
+__device__ __forceinline__ void argmax_block_reduce(float& best, int& bi, float* sv, int* si) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) {
-    const float ob = __shfl_xor_sync(0xffffffffu, best, o);
-    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-    if (ob > best || (ob == best && oi < bi)) {
-      best = ob;
-      bi = oi;
-    }
+    argmax_combine(best, bi, __shfl_xor_sync(0xffffffffu, best, o), __shfl_xor_sync(0xffffffffu, bi, o));
   }
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (lane == 0) {
@@ -341,15 +332,45 @@ __global__ void argmax_kernel(const T* __restrict__ logits, int* __restrict__ ou
     bi = lane < nw ? si[lane] : 0x7fffffff;
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
-      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (ob > best || (ob == best && oi < bi)) {
-        best = ob;
-        bi = oi;
-      }
+      argmax_combine(best, bi, __shfl_xor_sync(0xffffffffu, best, o), __shfl_xor_sync(0xffffffffu, bi, o));
     }
-    if (lane == 0) out[blockIdx.x] = bi;
   }
+}
+
+template <typename T>
+__global__ void argmax_partial_kernel(const T* __restrict__ logits, float* __restrict__ pv, int* __restrict__ pi,
+                                      int V, long ld, int chunk) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  const T* lr = logits + static_cast<size_t>(blockIdx.y) * ld;
+  const int begin = blockIdx.x * chunk, end = min(V, begin + chunk);
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = begin + threadIdx.x; i < end; i += blockDim.x) {
+    const float v = static_cast<float>(lr[i]);
+    if (v > best) {          // indices grow along the loop: strict > keeps the lowest
+      best = v;
+      bi = i;
+    }
+  }
+  argmax_block_reduce(best, bi, sv, si);
+  if (threadIdx.x == 0) {
+    pv[blockIdx.y * gridDim.x + blockIdx.x] = best;
+    pi[blockIdx.y * gridDim.x + blockIdx.x] = bi;
+  }
+}
+
+__global__ void argmax_final_kernel(const float* __restrict__ pv, const int* __restrict__ pi, int* __restrict__ out,
+                                    int chunks) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  float best = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = threadIdx.x; i < chunks; i += blockDim.x) {
+    argmax_combine(best, bi, pv[blockIdx.x * chunks + i], pi[blockIdx.x * chunks + i]);
+  }
+  argmax_block_reduce(best, bi, sv, si);
+  if (threadIdx.x == 0) out[blockIdx.x] = bi;
 }
 
 // Per-token, per-`group`-wide FP8 e4m3 quantisation. scale = amax/448 floored at
@@ -474,11 +495,26 @@ extern "C" int afd_topk_route(const void* logits, const void* bias, void* topk_i
   return 0;
 }
 
-extern "C" int afd_argmax(const void* logits, void* out, int T, int V, long ld, int is_bf16, void* stream) {
+// scratch: at least T * afd_argmax_chunks(V) * 8 bytes (candidate values, then indices).
+extern "C" int afd_argmax_chunks(int V) {
+  const int c = (V + 4095) / 4096;
+  return c < 1 ? 1 : c;
+}
+
+extern "C" int afd_argmax(const void* logits, void* out, int T, int V, long ld, int is_bf16, void* scratch,
+                          void* stream) {
   if (T == 0) return 0;
+  if (scratch == nullptr) return -1;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (is_bf16) argmax_kernel<__nv_bfloat16><<<T, 1024, 0, st>>>(static_cast<const __nv_bfloat16*>(logits), static_cast<int*>(out), V, ld);
-  else argmax_kernel<float><<<T, 1024, 0, st>>>(static_cast<const float*>(logits), static_cast<int*>(out), V, ld);
+  const int chunks = afd_argmax_chunks(V);
+  const int chunk = (V + chunks - 1) / chunks;
+  float* pv = static_cast<float*>(scratch);
+  int* pi = reinterpret_cast<int*>(pv + static_cast<size_t>(T) * chunks);
+  dim3 grid(chunks, T);
+  if (is_bf16) argmax_partial_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(logits), pv, pi, V, ld, chunk);
+  else argmax_partial_kernel<float><<<grid, 256, 0, st>>>(static_cast<const float*>(logits), pv, pi, V, ld, chunk);
+  AFD_CHECK_LAUNCH();
+  argmax_final_kernel<<<T, 64, 0, st>>>(pv, pi, static_cast<int*>(out), chunks);
   AFD_CHECK_LAUNCH();
   return 0;
 }

@@ -166,30 +166,83 @@ __global__ void eg_group_kernel(const GroupArgs a) {
     if (e >= 0 && e < a.experts_local) atomicAdd(&cnt[e], 1);
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int rows = 0, tiles = 0, routed = 0;
-    for (int e = 0; e < a.experts_local; ++e) {
-      const int c = cnt[e];
+  // Exclusive scan over the local experts of (token tiles, padded rows): one thread per
+  // expert, chunks of 1024 experts at a time, shuffle scan inside warps + a scan of warp sums.
+  {
+    __shared__ int s_wtiles[32], s_wrouted[32];
+    __shared__ int s_base_tiles, s_base_routed;
+    if (threadIdx.x == 0) {
+      s_base_tiles = 0;
+      s_base_routed = 0;
+    }
+    __syncthreads();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int e0 = 0; e0 < a.experts_local; e0 += blockDim.x) {
+      const int e = e0 + threadIdx.x;
+      const int c = e < a.experts_local ? cnt[e] : 0;
       const int nt = (c + a.block_tok - 1) / a.block_tok;
-      off[e] = rows;
-      for (int j = 0; j < nt; ++j) {
-        if (tiles < a.max_tok_tiles) {
-          a.tile_info[tiles] = make_int4(e, rows + j * a.block_tok, min(a.block_tok, c - j * a.block_tok), 0);
+      int incl_t = nt, incl_c = c;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int vt = __shfl_up_sync(0xffffffffu, incl_t, o);
+        const int vc = __shfl_up_sync(0xffffffffu, incl_c, o);
+        if (lane >= o) {
+          incl_t += vt;
+          incl_c += vc;
         }
-        ++tiles;
       }
-      rows += nt * a.block_tok;
-      routed += c;
-      if (a.expert_counts) a.expert_counts[e] = c;
+      if (lane == 31) {
+        s_wtiles[warp] = incl_t;
+        s_wrouted[warp] = incl_c;
+      }
+      __syncthreads();
+      if (warp == 0) {
+        int wt = lane < (blockDim.x >> 5) ? s_wtiles[lane] : 0;
+        int wc = lane < (blockDim.x >> 5) ? s_wrouted[lane] : 0;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+          const int vt = __shfl_up_sync(0xffffffffu, wt, o);
+          const int vc = __shfl_up_sync(0xffffffffu, wc, o);
+          if (lane >= o) {
+            wt += vt;
+            wc += vc;
+          }
+        }
+        s_wtiles[lane] = wt;       // inclusive sums of the warps
+        s_wrouted[lane] = wc;
+      }
+      __syncthreads();
+      const int warp_off_t = warp > 0 ? s_wtiles[warp - 1] : 0;
+      const int tile0 = s_base_tiles + warp_off_t + incl_t - nt;     // first tile of expert e
+      if (e < a.experts_local) {
+        off[e] = tile0 * a.block_tok;
+        for (int j = 0; j < nt; ++j) {
+          if (tile0 + j < a.max_tok_tiles) {
+            a.tile_info[tile0 + j] =
+                make_int4(e, (tile0 + j) * a.block_tok, min(a.block_tok, c - j * a.block_tok), 0);
+          }
+        }
+        if (a.expert_counts) a.expert_counts[e] = c;
+      }
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        s_base_tiles += s_wtiles[(blockDim.x >> 5) - 1];
+        s_base_routed += s_wrouted[(blockDim.x >> 5) - 1];
+      }
+      __syncthreads();
     }
-    if (tiles > a.max_tok_tiles || rows > a.pool_rows) {
-      set_status(a.status, kStatusCapacity);
-      tiles = min(tiles, a.max_tok_tiles);
+    if (threadIdx.x == 0) {
+      int tiles = s_base_tiles;
+      const int rows = tiles * a.block_tok;
+      if (tiles > a.max_tok_tiles || rows > a.pool_rows) {
+        set_status(a.status, kStatusCapacity);
+        tiles = min(tiles, a.max_tok_tiles);
+      }
+      a.counters[0] = tiles;
+      a.counters[1] = rows;
+      a.counters[2] = s_base_routed;
+      *a.epoch = s_epoch + 1;
     }
-    a.counters[0] = tiles;
-    a.counters[1] = rows;
-    a.counters[2] = routed;
-    *a.epoch = s_epoch + 1;
   }
   __syncthreads();
   for (int i = threadIdx.x; i < total; i += blockDim.x) {

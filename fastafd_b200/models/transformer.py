@@ -328,11 +328,12 @@ class AttentionStage:
                                 self.w[p + "norm.weight"], gdn.conv[li], gdn.rec[li], meta, hk, hv, dk, dv, c.rms_eps)
         return _linear(out, self.w[p + "out_proj.weight"])
 
-    def post_attn_norm(self, layer: int, attn_out: Tensor, residual: Tensor) -> Tensor:
+    def post_attn_norm(self, layer: int, attn_out: Tensor, residual: Tensor, out: Optional[Tensor] = None) -> Tensor:
         w = self.w[f"model.layers.{layer}.post_attention_layernorm.weight"]
-        return ops.add_rmsnorm(attn_out, residual, w, self.cfg.rms_eps, self.cfg.norm_offset1)
+        return ops.add_rmsnorm(attn_out, residual, w, self.cfg.rms_eps, self.cfg.norm_offset1, out=out)
 
-    def route(self, layer: int, x: Tensor) -> Tuple[Tensor, Tensor]:
+    def route(self, layer: int, x: Tensor, out_idx: Optional[Tensor] = None,
+              out_w: Optional[Tensor] = None) -> Tuple[Tensor, Tensor]:
         """Router of MoE layer `layer` on normed hidden x: (topk_idx int32 [T,K], topk_w fp32 [T,K])."""
         c = self.cfg
         p = f"model.layers.{layer}.mlp.gate."
@@ -340,9 +341,13 @@ class AttentionStage:
         logits = _linear(x.float() if gw.dtype == torch.float32 else x, gw).float()
         bias = self.w.get(p + "e_score_correction_bias")
         if c.n_group > 1:
-            return ref.grouped_topk_route(logits, bias, c.num_experts_per_tok, c.n_group, c.topk_group,
-                                          c.norm_topk_prob, 1.0)
-        return ops.topk_route(logits, bias, c.num_experts_per_tok, c.scoring, c.norm_topk_prob, 1.0)
+            idx, w = ref.grouped_topk_route(logits, bias, c.num_experts_per_tok, c.n_group, c.topk_group,
+                                            c.norm_topk_prob, 1.0)
+            if out_idx is not None:
+                return out_idx.copy_(idx), out_w.copy_(w)
+            return idx, w
+        return ops.topk_route(logits, bias, c.num_experts_per_tok, c.scoring, c.norm_topk_prob, 1.0,
+                              out_idx=out_idx, out_w=out_w)
 
     def local_mlp(self, layer: int, x: Tensor) -> Optional[Tensor]:
         """Work that stays on the attention GPU: the dense MLP of non-MoE layers, or the shared

@@ -35,7 +35,8 @@ def add_rmsnorm(x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, eps: f
                 offset1: bool = False, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """residual <- x + residual in place; returns rmsnorm(residual) * w."""
     if not x.is_cuda:
-        return ref.add_rmsnorm(x, residual, w, eps, offset1)
+        r = ref.add_rmsnorm(x, residual, w, eps, offset1)
+        return r if out is None else out.copy_(r)
     out = torch.empty_like(x) if out is None else out
     check(lib().afd_rmsnorm(ptr(x), ptr(residual), ptr(w), ptr(out), x.shape[0], x.shape[1], eps,
                             int(offset1), cur_stream()), "add_rmsnorm")
@@ -86,7 +87,10 @@ def topk_route(logits: torch.Tensor, bias: Optional[torch.Tensor], K: int, scori
                renorm: bool = True, scale: float = 1.0, out_idx=None, out_w=None):
     """Router scoring + top-k. logits fp32 [T,E]. Returns (idx int32 [T,K], w fp32 [T,K])."""
     if not logits.is_cuda:
-        return ref.topk_route(logits, bias, K, scoring, renorm, scale)
+        idx, w = ref.topk_route(logits, bias, K, scoring, renorm, scale)
+        if out_idx is not None:
+            return out_idx.copy_(idx), out_w.copy_(w)
+        return idx, w
     T, E = logits.shape
     logits = logits.float().contiguous() if logits.dtype != torch.float32 else logits
     idx = torch.empty(T, K, dtype=torch.int32, device=logits.device) if out_idx is None else out_idx
@@ -104,8 +108,9 @@ def argmax(logits: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Te
     out = torch.empty(T, dtype=torch.int32, device=logits.device) if out is None else out
     if logits.dtype not in (torch.bfloat16, torch.float32):
         logits = logits.float()
+    scratch = torch.empty(T * lib().afd_argmax_chunks(V) * 2, dtype=torch.float32, device=logits.device)
     check(lib().afd_argmax(ptr(logits), ptr(out), T, V, logits.stride(0),
-                           int(logits.dtype == torch.bfloat16), cur_stream()), "argmax")
+                           int(logits.dtype == torch.bfloat16), ptr(scratch), cur_stream()), "argmax")
     return out
 
 
@@ -125,15 +130,17 @@ def decode_attn_workspace(B, Hq, Hkv, q_len, D, splits, device) -> Optional[torc
     if splits <= 1:
         return None
     n = lib().afd_decode_attn_workspace_bytes(B, Hq, Hkv, q_len, D, splits)
-    return torch.empty(n, dtype=torch.uint8, device=device)
+    return torch.zeros(n, dtype=torch.uint8, device=device)    # arrival counters start at zero
 
 
-def pick_attn_splits(B: int, Hkv: int, m_tiles: int, max_kv: int, tok_tile: int = 32) -> int:
-    """Enough KV splits to fill the SMs about twice, never finer than 4 tiles per split."""
+def pick_attn_splits(B: int, Hkv: int, m_tiles: int, max_kv: int, D: int = 128) -> int:
+    """KV splits so that the grid stays within one wave of resident CTAs (2 per SM for head
+    dims up to 128, else 1) and every split still has at least 256 tokens to stream."""
+    slots = NUM_SMS * (2 if D <= 128 else 1)
     ctas = max(1, B * Hkv * m_tiles)
-    want = max(1, (2 * NUM_SMS + ctas - 1) // ctas)
-    cap = max(1, max_kv // (tok_tile * 4 * 4))
-    return max(1, min(want, cap, 32))
+    by_fill = max(1, slots // ctas)
+    by_len = max(1, max_kv // 256)
+    return max(1, min(by_fill, by_len, 32))
 
 
 def decode_attention(q, k_cache, v_cache, page_table, seq_lens, Hq, Hkv, D, q_len, page_size,
@@ -150,8 +157,6 @@ def decode_attention(q, k_cache, v_cache, page_table, seq_lens, Hq, Hkv, D, q_le
                                      ptr(seq_lens), ptr(out), ptr(workspace), B, Hq, Hkv, D, q_len,
                                      page_size, page_table.shape[1], k_cache.shape[0], splits,
                                      sm_scale, ptr(status), cur_stream()), "decode_attention")
-    if splits > 1:
-        _lib.LAUNCHES["count"] += 1      # the split-merge kernel
     return out
 
 

@@ -197,16 +197,14 @@ class AttentionWorker:
         m, c = self.model, self.cfg
         with nvtx_range(f"AFD_AG_Attn_L{layer}_mb{mb.lane}"):
             attn_out = m.attention(layer, mb.normed, mb.meta, self.kv, self.gdn)
-            x = m.post_attn_norm(layer, attn_out, mb.residual)
-        if c.is_moe_layer(layer):
-            idx, w = m.route(layer, x)
-            mb.x_moe.copy_(x)
-            mb.topk_idx.copy_(idx)
-            mb.topk_w.copy_(w)
+            moe = c.is_moe_layer(layer)
+            x = m.post_attn_norm(layer, attn_out, mb.residual, out=mb.x_moe if moe else None)
+        if moe:
+            m.route(layer, x, out_idx=mb.topk_idx, out_w=mb.topk_w)
             if mb.meta.is_prefill and mb.pad_from < mb.T:
                 mb.topk_idx[mb.pad_from:] = -1          # padding tokens are routed nowhere
             mb.extra = m.local_mlp(layer, x)
-            mb.keep += [attn_out, x, idx, w, mb.extra]
+            mb.keep += [attn_out, mb.extra]
             with self._on_lane(mb.lane):
                 with nvtx_range(f"AFD_AG_Dispatch_L{layer}_mb{mb.lane}"):
                     self.client.dispatch(mb.lane, layer, mb.x_moe, mb.topk_idx, mb.topk_w)
@@ -254,7 +252,7 @@ class AttentionWorker:
             max_kv = self.max_seq_len
             m_tiles = (self.model.hq // self.model.hkv * q_len + 15) // 16
             meta.splits = self.decode_splits if hasattr(self, "decode_splits") else ops.pick_attn_splits(
-                bucket, self.model.hkv, m_tiles, min(max_kv, 4096))
+                bucket, self.model.hkv, m_tiles, max_kv, self.cfg.head_dim)
             if meta.splits > 1:
                 if b.workspace is None:
                     b.workspace = ops.decode_attn_workspace(self.cap, self.model.hq, self.model.hkv, q_len,
