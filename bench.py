@@ -47,7 +47,7 @@ def parse_args():
     ap.add_argument("--model", default="qwen3-30b-a3b")
     ap.add_argument("--batch-per-attn-gpu", type=int, default=64)
     ap.add_argument("--context", type=int, default=1024)
-    ap.add_argument("--num-mb", type=int, default=2)
+    ap.add_argument("--num-mb", type=int, default=0, help="micro-batches in flight; 0 = 1 when colocated (nothing to overlap), 2 with separate expert GPUs")
     ap.add_argument("--block-tok", type=int, default=16)
     ap.add_argument("--layers", type=int, default=0, help="debug only: truncate the model (marks the result invalid)")
     ap.add_argument("--no-graph", action="store_true")
@@ -144,6 +144,8 @@ def main():
         cfg = cfg.with_layers(args.layers)
         truncated = True
     topo = AfdTopology.for_world(world)
+    if args.num_mb <= 0:
+        args.num_mb = 1 if topo.colocated else 2
     b = args.batch_per_attn_gpu
     per_mb = (b + args.num_mb - 1) // args.num_mb
     total_steps = 2 * (args.steps + args.warmup) + 8

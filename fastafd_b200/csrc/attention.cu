@@ -46,7 +46,8 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
 }
 
 struct DecodeAttnArgs {
-  const __nv_bfloat16* q;        // [B*q_len][Hq][D]
+  const __nv_bfloat16* q;        // [B*q_len] rows of q_stride elements; heads [Hq][D] first
+  long q_stride;
   const __nv_bfloat16* k_cache;  // [slots][Hkv][D]
   const __nv_bfloat16* v_cache;
   const int* page_table;         // [B][max_pages]
@@ -112,7 +113,7 @@ __global__ void __launch_bounds__(128, AttnCfg<D>::CTAS_PER_SM) decode_attn_kern
     uint4 v = make_uint4(0, 0, 0, 0);
     if (row < M) {
       const int j = row / G, g = row % G;
-      v = *reinterpret_cast<const uint4*>(a.q + ((static_cast<size_t>(b) * a.q_len + j) * a.Hq + kvh * G + g) * D + c * 8);
+      v = *reinterpret_cast<const uint4*>(a.q + (static_cast<size_t>(b) * a.q_len + j) * a.q_stride + (kvh * G + g) * D + c * 8);
     }
     *reinterpret_cast<uint4*>(sq + tile_off<D>(r, c)) = v;
   }
@@ -427,17 +428,38 @@ extern "C" long afd_decode_attn_workspace_bytes(int B, int Hq, int Hkv, int q_le
   return tiles * 16 * D * 4 + tiles * 16 * 4 + static_cast<long>(B) * Hkv * m_tiles * 4;
 }
 
+extern "C" int afd_decode_attention_strided(const void* q, long q_stride, const void* k_cache,
+                                            const void* v_cache, const void* page_table,
+                                            const void* seq_lens, void* out, void* workspace, int B,
+                                            int Hq, int Hkv, int D, int q_len, int page_size,
+                                            int max_pages, long cache_slots, int splits, float sm_scale,
+                                            void* status, void* stream);
+
 extern "C" int afd_decode_attention(const void* q, const void* k_cache, const void* v_cache,
                                     const void* page_table, const void* seq_lens, void* out,
                                     void* workspace, int B, int Hq, int Hkv, int D, int q_len,
                                     int page_size, int max_pages, long cache_slots, int splits,
                                     float sm_scale, void* status, void* stream) {
+  return afd_decode_attention_strided(q, static_cast<long>(Hq) * D, k_cache, v_cache, page_table, seq_lens, out,
+                                      workspace, B, Hq, Hkv, D, q_len, page_size, max_pages, cache_slots, splits,
+                                      sm_scale, status, stream);
+}
+
+// Same, with q rows `q_stride` elements apart (q read in place from a merged qkv buffer).
+extern "C" int afd_decode_attention_strided(const void* q, long q_stride, const void* k_cache,
+                                            const void* v_cache, const void* page_table,
+                                            const void* seq_lens, void* out, void* workspace, int B,
+                                            int Hq, int Hkv, int D, int q_len, int page_size,
+                                            int max_pages, long cache_slots, int splits, float sm_scale,
+                                            void* status, void* stream) {
   using namespace afd;
   if (B == 0) return 0;
   if (Hq % Hkv != 0 || splits < 1 || page_size < 1) return -1;
   if (splits > 1 && workspace == nullptr) return -2;
   DecodeAttnArgs a{};
   a.q = static_cast<const __nv_bfloat16*>(q);
+  a.q_stride = q_stride;
+  if (q_stride % 8 != 0) return -5;
   a.k_cache = static_cast<const __nv_bfloat16*>(k_cache);
   a.v_cache = static_cast<const __nv_bfloat16*>(v_cache);
   a.page_table = static_cast<const int*>(page_table);

@@ -211,20 +211,20 @@ __global__ void silu_mul_kernel(const __nv_bfloat16* __restrict__ gate_up, __nv_
 // renorm: divide the selected weights by their sum; scale multiplies the result.
 // Ties go to the lower expert index (the order torch.topk gives on equal values is
 // not specified; the oracle in the tests uses the same rule).
-template <int MAX_PER_LANE>
-__global__ void topk_route_kernel(const float* __restrict__ logits, const float* __restrict__ bias,
+template <int MAX_PER_LANE, typename LT>
+__global__ void topk_route_kernel(const LT* __restrict__ logits, const float* __restrict__ bias,
                                   int* __restrict__ topk_idx, float* __restrict__ topk_w, int T, int E,
                                   int K, int scoring, int renorm, float scale) {
   const int tok = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (tok >= T) return;
   float sc[MAX_PER_LANE], sel[MAX_PER_LANE];
-  const float* lr = logits + static_cast<size_t>(tok) * E;
+  const LT* lr = logits + static_cast<size_t>(tok) * E;
   float mx = -INFINITY;
 #pragma unroll
   for (int j = 0; j < MAX_PER_LANE; ++j) {
     const int e = j * 32 + lane;
-    sc[j] = e < E ? lr[e] : -INFINITY;
+    sc[j] = e < E ? static_cast<float>(lr[e]) : -INFINITY;
     mx = fmaxf(mx, sc[j]);
   }
   if (scoring == 0) {
@@ -477,20 +477,28 @@ extern "C" int afd_silu_mul(const void* gate_up, void* out, long rows, int I, vo
   return 0;
 }
 
+template <typename LT>
+static void launch_topk(const void* logits, const float* b, int* ti, float* tw, int T, int E, int K, int scoring,
+                        int renorm, float scale, cudaStream_t st) {
+  const int threads = 128;
+  const int blocks = (T * 32 + threads - 1) / threads;
+  auto l = static_cast<const LT*>(logits);
+  if (E <= 128) topk_route_kernel<4, LT><<<blocks, threads, 0, st>>>(l, b, ti, tw, T, E, K, scoring, renorm, scale);
+  else if (E <= 256) topk_route_kernel<8, LT><<<blocks, threads, 0, st>>>(l, b, ti, tw, T, E, K, scoring, renorm, scale);
+  else topk_route_kernel<16, LT><<<blocks, threads, 0, st>>>(l, b, ti, tw, T, E, K, scoring, renorm, scale);
+}
+
 extern "C" int afd_topk_route(const void* logits, const void* bias, void* topk_idx, void* topk_w, int T,
-                              int E, int K, int scoring, int renorm, float scale, void* stream) {
+                              int E, int K, int scoring, int renorm, float scale, int logits_bf16,
+                              void* stream) {
   if (T == 0) return 0;
   if (E > 512 || K > 32 || K > E) return -1;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  const int threads = 128;
-  const int blocks = (T * 32 + threads - 1) / threads;
-  auto l = static_cast<const float*>(logits);
   auto b = static_cast<const float*>(bias);
   auto ti = static_cast<int*>(topk_idx);
   auto tw = static_cast<float*>(topk_w);
-  if (E <= 128) topk_route_kernel<4><<<blocks, threads, 0, st>>>(l, b, ti, tw, T, E, K, scoring, renorm, scale);
-  else if (E <= 256) topk_route_kernel<8><<<blocks, threads, 0, st>>>(l, b, ti, tw, T, E, K, scoring, renorm, scale);
-  else topk_route_kernel<16><<<blocks, threads, 0, st>>>(l, b, ti, tw, T, E, K, scoring, renorm, scale);
+  if (logits_bf16) launch_topk<__nv_bfloat16>(logits, b, ti, tw, T, E, K, scoring, renorm, scale, st);
+  else launch_topk<float>(logits, b, ti, tw, T, E, K, scoring, renorm, scale, st);
   AFD_CHECK_LAUNCH();
   return 0;
 }

@@ -268,7 +268,7 @@ class AttentionStage:
         if meta.is_prefill:
             o = self._prefill_attention(q, kc, vc, meta, scale, kv.page_size)
         else:
-            o = ops.decode_attention(q.contiguous(), kc, vc, meta.page_table, meta.seq_lens, self.hq, self.hkv, D,
+            o = ops.decode_attention(q, kc, vc, meta.page_table, meta.seq_lens, self.hq, self.hkv, D,
                                      meta.q_len, kv.page_size, scale, splits=meta.splits,
                                      workspace=meta.workspace, status=meta.status)
         o = o.reshape(T, self.hq * D)
@@ -338,7 +338,9 @@ class AttentionStage:
         c = self.cfg
         p = f"model.layers.{layer}.mlp.gate."
         gw = self.w[p + "weight"]
-        logits = _linear(x.float() if gw.dtype == torch.float32 else x, gw).float()
+        logits = _linear(x.float() if gw.dtype == torch.float32 else x, gw)
+        if not logits.is_cuda:
+            logits = logits.float()
         bias = self.w.get(p + "e_score_correction_bias")
         if c.n_group > 1:
             idx, w = ref.grouped_topk_route(logits, bias, c.num_experts_per_tok, c.n_group, c.topk_group,

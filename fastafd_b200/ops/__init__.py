@@ -92,11 +92,13 @@ def topk_route(logits: torch.Tensor, bias: Optional[torch.Tensor], K: int, scori
             return out_idx.copy_(idx), out_w.copy_(w)
         return idx, w
     T, E = logits.shape
-    logits = logits.float().contiguous() if logits.dtype != torch.float32 else logits
+    if logits.dtype not in (torch.float32, torch.bfloat16) or not logits.is_contiguous():
+        logits = logits.float().contiguous()
     idx = torch.empty(T, K, dtype=torch.int32, device=logits.device) if out_idx is None else out_idx
     w = torch.empty(T, K, dtype=torch.float32, device=logits.device) if out_w is None else out_w
     check(lib().afd_topk_route(ptr(logits), ptr(bias), ptr(idx), ptr(w), T, E, K,
-                               0 if scoring == "softmax" else 1, int(renorm), scale, cur_stream()),
+                               0 if scoring == "softmax" else 1, int(renorm), scale,
+                               int(logits.dtype == torch.bfloat16), cur_stream()),
           "topk_route")
     return idx, w
 
@@ -145,15 +147,18 @@ def pick_attn_splits(B: int, Hkv: int, m_tiles: int, max_kv: int, D: int = 128) 
 
 def decode_attention(q, k_cache, v_cache, page_table, seq_lens, Hq, Hkv, D, q_len, page_size,
                      sm_scale, splits: int = 1, workspace=None, out=None, status=None):
-    """Paged GQA decode attention. q [B*q_len, Hq, D] bf16; caches [slots, Hkv, D]."""
+    """Paged GQA decode attention. q [B*q_len, Hq, D] bf16 (rows may be strided, e.g. a view
+    into a merged qkv buffer); caches [slots, Hkv, D]. Returns a contiguous [B*q_len, Hq, D]."""
     if not q.is_cuda:
         return ref.decode_attention(q, k_cache, v_cache, page_table, seq_lens, Hq, Hkv, D, q_len,
                                     page_size, sm_scale)
     B = seq_lens.shape[0]
-    out = torch.empty_like(q) if out is None else out
+    if q.stride(2) != 1 or q.stride(1) != D:
+        q = q.contiguous()
+    out = torch.empty(q.shape, dtype=q.dtype, device=q.device) if out is None else out
     if splits > 1 and workspace is None:
         workspace = decode_attn_workspace(B, Hq, Hkv, q_len, D, splits, q.device)
-    check(lib().afd_decode_attention(ptr(q), ptr(k_cache), ptr(v_cache), ptr(page_table),
+    check(lib().afd_decode_attention_strided(ptr(q), q.stride(0), ptr(k_cache), ptr(v_cache), ptr(page_table),
                                      ptr(seq_lens), ptr(out), ptr(workspace), B, Hq, Hkv, D, q_len,
                                      page_size, page_table.shape[1], k_cache.shape[0], splits,
                                      sm_scale, ptr(status), cur_stream()), "decode_attention")

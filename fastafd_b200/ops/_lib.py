@@ -78,7 +78,10 @@ _SIGNATURES = {
     "afd_embedding": (C.c_int, [VP, VP, VP, C.c_int, C.c_int, C.c_int, C.c_int, VP]),
     "afd_silu_mul": (C.c_int, [VP, VP, C.c_long, C.c_int, VP]),
     "afd_topk_route": (C.c_int, [VP, VP, VP, VP, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
-                                 C.c_float, VP]),
+                                 C.c_float, C.c_int, VP]),
+    "afd_decode_attention_strided": (C.c_int, [VP, C.c_long, VP, VP, VP, VP, VP, VP, C.c_int, C.c_int, C.c_int,
+                                               C.c_int, C.c_int, C.c_int, C.c_int, C.c_long, C.c_int, C.c_float,
+                                               VP, VP]),
     "afd_argmax": (C.c_int, [VP, VP, C.c_int, C.c_int, C.c_long, C.c_int, VP, VP]),
     "afd_argmax_chunks": (C.c_int, [C.c_int]),
     "afd_group_quant_fp8": (C.c_int, [VP, VP, VP, C.c_long, C.c_int, C.c_int, C.c_int, VP]),
