@@ -204,6 +204,21 @@ def main():
     e2e_ms = max_over_ranks(e2e_ms)
     status = eng.synchronize()
 
+    trace_info = None
+    if os.environ.get("FASTAFD_COMM_TRACE") == "1":
+        from fastafd_b200.moe.afd_moe import summarize_trace
+
+        mine = []
+        if eng.attn is not None and getattr(eng.attn.client, "ep", None) is not None and eng.attn.client.ep.trace:
+            mine.append(("attention", [summarize_trace(t, "attention") for t in eng.attn.client.ep.trace]))
+        if eng._server is not None and eng._server.ep.trace:
+            mine.append(("expert", [summarize_trace(t, "expert") for t in eng._server.ep.trace]))
+        if world > 1:
+            allinfo = [None] * world
+            dist.all_gather_object(allinfo, mine)
+            trace_info = {f"rank{r}": v for r, v in enumerate(allinfo)}
+        else:
+            trace_info = {"rank0": mine}
     n_attn = 1 if topo.colocated else topo.attn_world
     tokens = b * n_attn * args.steps
     value = tokens / (dev_ms / 1e3)
@@ -240,6 +255,8 @@ def main():
             "kernels_per_step_rank0": kernels_per_step,
             "device_status": status, "build_s": round(build_s, 1),
         }
+        if trace_info is not None:
+            out["comm_trace"] = trace_info
         if truncated:
             out["invalid"] = "model truncated with --layers (debug run)"
         print(json.dumps(out))

@@ -81,13 +81,21 @@ struct AttnCfg {
   static constexpr int CTAS_PER_SM = (220 * 1024) / SMEM >= 2 ? 2 : 1;
 };
 
-template <int D>
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+
+// NQ = query-row n-tiles per CTA (8 rows each): 1 when a (request, kv head) has at most 8
+// query rows (decode with a GQA group of 8), else 2.
+template <int D, int NQ>
 __global__ void __launch_bounds__(128, AttnCfg<D>::CTAS_PER_SM) decode_attn_kernel(const DecodeAttnArgs a) {
   using Cfg = AttnCfg<D>;
+  constexpr int ROWS = 8 * NQ;
   constexpr int TOK = Cfg::TOK;
   constexpr int CH = D / 8;            // 16-byte chunks per row
   constexpr int KT = D / 16;           // k-steps of S
-  constexpr int NT = TOK / 8;          // n-tiles of S (2)
   constexpr int TILE_BYTES = Cfg::TILE_BYTES;
   constexpr bool Q_REGS = D <= 128;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -109,9 +117,9 @@ __global__ void __launch_bounds__(128, AttnCfg<D>::CTAS_PER_SM) decode_attn_kern
   // ---- stage Q (rows = j*G + g), zero for padding rows ----
   for (int idx = threadIdx.x; idx < 16 * CH; idx += 128) {
     const int r = idx / CH, c = idx % CH;
-    const int row = mt * 16 + r;
+    const int row = mt * ROWS + r;
     uint4 v = make_uint4(0, 0, 0, 0);
-    if (row < M) {
+    if (row < M && r < ROWS) {
       const int j = row / G, g = row % G;
       v = *reinterpret_cast<const uint4*>(a.q + (static_cast<size_t>(b) * a.q_len + j) * a.q_stride + (kvh * G + g) * D + c * 8);
     }
@@ -120,7 +128,7 @@ __global__ void __launch_bounds__(128, AttnCfg<D>::CTAS_PER_SM) decode_attn_kern
   __syncthreads();
 
   // ---- this CTA's KV range: only what the rows of this tile may see (causal) ----
-  const int j_max = min((mt * 16 + 15) / G, a.q_len - 1);
+  const int j_max = min((mt * ROWS + ROWS - 1) / G, a.q_len - 1);
   const int visible = max(0, kv_len - a.q_len + 1 + j_max);
   const int per_split = ((visible + a.splits - 1) / a.splits + TOK * 4 - 1) / (TOK * 4) * (TOK * 4);
   const int kv_begin = split * per_split;
@@ -195,33 +203,42 @@ __global__ void __launch_bounds__(128, AttnCfg<D>::CTAS_PER_SM) decode_attn_kern
     next_tile += 4;
   }
 
+  // The products are computed transposed so that the query rows (8 per n-tile: exactly one
+  // GQA group of 8 heads) sit on the MMA N side and no tensor work is spent on padding:
+  //   S^T[tok, qrow] = K[tok, :] . Q[qrow, :]        (A = K tile, B = Q^T)
+  //   O^T[d,  qrow] += V^T[d, tok] . P^T[tok, qrow]   (A = V^T via ldmatrix.trans, B = P^T)
   const uint32_t sqa = smem_u32(sq);
-  uint32_t qreg[Q_REGS ? KT : 1][4];
+  uint32_t qb[Q_REGS ? KT : 1][4];
   if constexpr (Q_REGS) {
 #pragma unroll
     for (int ks = 0; ks < KT; ++ks) {
       const int mat = lane >> 3;
-      const int row = (mat & 1) * 8 + (lane & 7);
-      ldsm_x4(sqa + tile_off<D>(row, ks * 2 + (mat >> 1)), qreg[ks][0], qreg[ks][1], qreg[ks][2], qreg[ks][3]);
+      const int row = (mat >> 1) * 8 + (lane & 7);
+      ldsm_x4(sqa + tile_off<D>(row, ks * 2 + (mat & 1)), qb[ks][0], qb[ks][1], qb[ks][2], qb[ks][3]);
     }
   }
 
-  float o[D / 8][4];
+  float ot[D / 16][NQ][4];
 #pragma unroll
-  for (int i = 0; i < D / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-  float m_run[2] = {-INFINITY, -INFINITY};
-  float l_run[2] = {0.f, 0.f};
-  int lim[2];
+  for (int i = 0; i < D / 16; ++i)
 #pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    const int row = mt * 16 + (lane >> 2) + h * 8;
-    const int j = row < M ? row / G : 0;
-    lim[h] = row < M ? kv_len - a.q_len + 1 + j : 0;
-  }
+    for (int n = 0; n < NQ; ++n) ot[i][n][0] = ot[i][n][1] = ot[i][n][2] = ot[i][n][3] = 0.f;
+  // per-thread columns: qrow = n*8 + 2*(lane%4) + c, c in {0,1}
+  float m_run[NQ][2], l_run[NQ][2];
+  int lim[NQ][2];
+#pragma unroll
+  for (int n = 0; n < NQ; ++n)
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      m_run[n][c] = -INFINITY;
+      l_run[n][c] = 0.f;
+      const int row = mt * ROWS + n * 8 + (lane & 3) * 2 + c;
+      const int j = row < M ? row / G : 0;
+      lim[n][c] = row < M ? kv_len - a.q_len + 1 + j : 0;
+    }
 
   int stage = 0;
   for (int tile = warp; tile < n_tiles; tile += 4) {
-    // keep the ring full: the stage consumed in the previous iteration is free now
     {
       int ls = stage + Cfg::STAGES - 1;
       if (ls >= Cfg::STAGES) ls -= Cfg::STAGES;
@@ -234,90 +251,94 @@ __global__ void __launch_bounds__(128, AttnCfg<D>::CTAS_PER_SM) decode_attn_kern
     const uint32_t sk = smem_u32(my + stage * 2 * TILE_BYTES);
     const uint32_t sv = sk + TILE_BYTES;
 
-    float s[NT][4];
+    float st[NQ][4];
 #pragma unroll
-    for (int n = 0; n < NT; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
+    for (int n = 0; n < NQ; ++n) st[n][0] = st[n][1] = st[n][2] = st[n][3] = 0.f;
 #pragma unroll
     for (int ks = 0; ks < KT; ++ks) {
-      uint32_t qa[4];
-      if constexpr (Q_REGS) {
-        qa[0] = qreg[ks][0]; qa[1] = qreg[ks][1]; qa[2] = qreg[ks][2]; qa[3] = qreg[ks][3];
-      } else {
+      uint32_t ka[4];
+      {
         const int mat = lane >> 3;
         const int row = (mat & 1) * 8 + (lane & 7);
-        ldsm_x4(sqa + tile_off<D>(row, ks * 2 + (mat >> 1)), qa[0], qa[1], qa[2], qa[3]);
+        ldsm_x4(sk + tile_off<D>(row, ks * 2 + (mat >> 1)), ka[0], ka[1], ka[2], ka[3]);
       }
+      uint32_t q0, q1, q2, q3;
+      if constexpr (Q_REGS) {
+        q0 = qb[ks][0]; q1 = qb[ks][1]; q2 = qb[ks][2]; q3 = qb[ks][3];
+      } else {
+        const int mat = lane >> 3;
+        const int row = (mat >> 1) * 8 + (lane & 7);
+        ldsm_x4(sqa + tile_off<D>(row, ks * 2 + (mat & 1)), q0, q1, q2, q3);
+      }
+      mma_bf16_16816(st[0], ka, q0, q1);
+      if constexpr (NQ == 2) mma_bf16_16816(st[1], ka, q2, q3);
+    }
+    // ---- mask + online softmax over the token (row) dimension ----
+    const int t0 = kv_begin + tile * TOK;
+    uint32_t pb[NQ][2];
+#pragma unroll
+    for (int n = 0; n < NQ; ++n) {
+      float corr[2];
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        // elements of column c: st[n][c] (token lane/4) and st[n][c + 2] (token lane/4 + 8)
+        float mx = -INFINITY;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int t = t0 + (lane >> 2) + h * 8;
+          float v = st[n][c + 2 * h] * a.scale_log2;
+          if (t >= lim[n][c] || t >= kv_end) v = -INFINITY;
+          st[n][c + 2 * h] = v;
+          mx = fmaxf(mx, v);
+        }
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+        const float m_new = fmaxf(m_run[n][c], mx);
+        corr[c] = (m_new == -INFINITY) ? 1.f : exp2f(m_run[n][c] - m_new);
+        m_run[n][c] = m_new;
+        float lsum = 0.f;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const float p = (m_new == -INFINITY) ? 0.f : exp2f(st[n][c + 2 * h] - m_new);
+          st[n][c + 2 * h] = p;
+          lsum += p;
+        }
+        l_run[n][c] = l_run[n][c] * corr[c] + lsum;
+      }
+#pragma unroll
+      for (int i = 0; i < D / 16; ++i) {
+        ot[i][n][0] *= corr[0];
+        ot[i][n][1] *= corr[1];
+        ot[i][n][2] *= corr[0];
+        ot[i][n][3] *= corr[1];
+      }
+      // P^T as the B operand: transpose the two 8x8 blocks (tokens 0-7, 8-15) in registers
+      pb[n][0] = movmatrix_trans(pack_bf16(st[n][0], st[n][1]));
+      pb[n][1] = movmatrix_trans(pack_bf16(st[n][2], st[n][3]));
+    }
+    // ---- O^T += V^T P^T ----
+#pragma unroll
+    for (int dt = 0; dt < D / 16; ++dt) {
+      uint32_t va[4];
       const int mat = lane >> 3;
       const int row = (mat >> 1) * 8 + (lane & 7);
-      uint32_t b0, b1, b2, b3;
-      ldsm_x4(sk + tile_off<D>(row, ks * 2 + (mat & 1)), b0, b1, b2, b3);
-      mma_bf16_16816(s[0], qa, b0, b1);
-      mma_bf16_16816(s[1], qa, b2, b3);
-    }
-    // ---- mask + online softmax ----
-    const int t0 = kv_begin + tile * TOK;
-    float mx[2] = {-INFINITY, -INFINITY};
-#pragma unroll
-    for (int n = 0; n < NT; ++n) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int t = t0 + n * 8 + (lane & 3) * 2 + (e & 1);
-        const int h = e >> 1;
-        float v = s[n][e] * a.scale_log2;
-        if (t >= lim[h] || t >= kv_end) v = -INFINITY;
-        s[n][e] = v;
-        mx[h] = fmaxf(mx[h], v);
-      }
-    }
-    float corr[2];
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 1));
-      mx[h] = fmaxf(mx[h], __shfl_xor_sync(0xffffffffu, mx[h], 2));
-      const float m_new = fmaxf(m_run[h], mx[h]);
-      corr[h] = (m_new == -INFINITY) ? 1.f : exp2f(m_run[h] - m_new);
-      m_run[h] = m_new;
-      l_run[h] *= corr[h];
-    }
-#pragma unroll
-    for (int i = 0; i < D / 8; ++i) {
-      o[i][0] *= corr[0];
-      o[i][1] *= corr[0];
-      o[i][2] *= corr[1];
-      o[i][3] *= corr[1];
-    }
-    uint32_t pa[4];
-#pragma unroll
-    for (int n = 0; n < NT; ++n) {
-      float p[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int h = e >> 1;
-        p[e] = (m_run[h] == -INFINITY) ? 0.f : exp2f(s[n][e] - m_run[h]);
-        l_run[h] += p[e];
-      }
-      pa[n * 2 + 0] = pack_bf16(p[0], p[1]);
-      pa[n * 2 + 1] = pack_bf16(p[2], p[3]);
-    }
-    // ---- O += P V (one k-step of 16 tokens) ----
-#pragma unroll
-    for (int dp = 0; dp < D / 16; ++dp) {
-      const int mat = lane >> 3;
-      const int row = (mat & 1) * 8 + (lane & 7);
-      uint32_t b0, b1, b2, b3;
-      ldsm_x4_t(sv + tile_off<D>(row, dp * 2 + (mat >> 1)), b0, b1, b2, b3);
-      mma_bf16_16816(o[dp * 2], pa, b0, b1);
-      mma_bf16_16816(o[dp * 2 + 1], pa, b2, b3);
+      ldsm_x4_t(sv + tile_off<D>(row, dt * 2 + (mat & 1)), va[0], va[1], va[2], va[3]);
+      mma_bf16_16816(ot[dt][0], va, pb[0][0], pb[0][1]);
+      if constexpr (NQ == 2) mma_bf16_16816(ot[dt][1], va, pb[1][0], pb[1][1]);
     }
     __syncwarp();
     if (++stage == Cfg::STAGES) stage = 0;
   }
   cp_async_wait<0>();
 #pragma unroll
-  for (int h = 0; h < 2; ++h) {
-    l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 1);
-    l_run[h] += __shfl_xor_sync(0xffffffffu, l_run[h], 2);
-  }
+  for (int n = 0; n < NQ; ++n)
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      l_run[n][c] += __shfl_xor_sync(0xffffffffu, l_run[n][c], 4);
+      l_run[n][c] += __shfl_xor_sync(0xffffffffu, l_run[n][c], 8);
+      l_run[n][c] += __shfl_xor_sync(0xffffffffu, l_run[n][c], 16);
+    }
 
   // ---- merge the 4 warps through shared memory (each warp reuses its own ring) ----
   __syncwarp();
@@ -325,22 +346,28 @@ __global__ void __launch_bounds__(128, AttnCfg<D>::CTAS_PER_SM) decode_attn_kern
   float* wm = wo + 16 * D;                           // [16]
   float* wl = wm + 16;                               // [16]
 #pragma unroll
-  for (int i = 0; i < D / 8; ++i) {
-    const int r = lane >> 2, c = i * 8 + (lane & 3) * 2;
-    wo[r * D + c] = o[i][0];
-    wo[r * D + c + 1] = o[i][1];
-    wo[(r + 8) * D + c] = o[i][2];
-    wo[(r + 8) * D + c + 1] = o[i][3];
-  }
-  if ((lane & 3) == 0) {
-    wm[lane >> 2] = m_run[0];
-    wm[(lane >> 2) + 8] = m_run[1];
-    wl[lane >> 2] = l_run[0];
-    wl[(lane >> 2) + 8] = l_run[1];
+  for (int dt = 0; dt < D / 16; ++dt)
+#pragma unroll
+    for (int n = 0; n < NQ; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int qrow = n * 8 + (lane & 3) * 2 + (e & 1);
+        const int d = dt * 16 + (lane >> 2) + (e >> 1) * 8;
+        wo[qrow * D + d] = ot[dt][n][e];
+      }
+  if ((lane >> 2) == 0) {
+#pragma unroll
+    for (int n = 0; n < NQ; ++n)
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int qrow = n * 8 + (lane & 3) * 2 + c;
+        wm[qrow] = m_run[n][c];
+        wl[qrow] = l_run[n][c];
+      }
   }
   __syncthreads();
   const size_t tile_id = (static_cast<size_t>(b) * a.Hkv + kvh) * a.m_tiles + mt;
-  for (int idx = threadIdx.x; idx < 16 * D; idx += 128) {
+  for (int idx = threadIdx.x; idx < ROWS * D; idx += 128) {
     const int r = idx / D, d = idx % D;
     float mm = -INFINITY;
 #pragma unroll
@@ -355,7 +382,7 @@ __global__ void __launch_bounds__(128, AttnCfg<D>::CTAS_PER_SM) decode_attn_kern
       l += base[16 * D + 16 + r] * f;
     }
     const float val = l > 0.f ? acc / l : 0.f;
-    const int row = mt * 16 + r;
+    const int row = mt * ROWS + r;
     if (a.splits == 1) {
       if (row < M) {
         const int j = row / G, g = row % G;
@@ -382,9 +409,9 @@ __global__ void __launch_bounds__(128, AttnCfg<D>::CTAS_PER_SM) decode_attn_kern
   if (!s_last) return;
   __threadfence();
   const size_t p0 = tile_id * a.splits;
-  for (int idx = threadIdx.x; idx < 16 * D; idx += 128) {
+  for (int idx = threadIdx.x; idx < ROWS * D; idx += 128) {
     const int r = idx / D, d = idx % D;
-    const int row = mt * 16 + r;
+    const int row = mt * ROWS + r;
     if (row >= M) continue;
     float mm = -INFINITY;
     for (int s2 = 0; s2 < a.splits; ++s2) mm = fmaxf(mm, __ldcg(a.part_lse + (p0 + s2) * 16 + r));
@@ -401,10 +428,10 @@ __global__ void __launch_bounds__(128, AttnCfg<D>::CTAS_PER_SM) decode_attn_kern
   }
 }
 
-template <int D>
-static int launch_decode(const DecodeAttnArgs& a, cudaStream_t st) {
+template <int D, int NQ>
+static int launch_decode_nq(const DecodeAttnArgs& a, cudaStream_t st) {
   using Cfg = AttnCfg<D>;
-  auto kern = decode_attn_kernel<D>;
+  auto kern = decode_attn_kernel<D, NQ>;
   static bool set = false;
   if (!set) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM);
@@ -415,6 +442,12 @@ static int launch_decode(const DecodeAttnArgs& a, cudaStream_t st) {
   kern<<<grid, 128, Cfg::SMEM, st>>>(a);
   AFD_CHECK_LAUNCH();
   return 0;
+}
+
+template <int D>
+static int launch_decode(const DecodeAttnArgs& a, cudaStream_t st) {
+  const int M = (a.Hq / a.Hkv) * a.q_len;
+  return M <= 8 ? launch_decode_nq<D, 1>(a, st) : launch_decode_nq<D, 2>(a, st);
 }
 
 }  // namespace afd

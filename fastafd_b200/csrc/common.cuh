@@ -252,6 +252,16 @@ __device__ __forceinline__ bool wait_flag_ge(const uint32_t* flag, uint32_t targ
   return false;
 }
 
+// ---- device-side timeline (optional) -----------------------------------------------------
+// Kernels of the N2M / M2N exchange can stamp the GPU's global timer into a ring of
+// kTraceLen rows x 4 events per lane, indexed by the lane's epoch. A null pointer switches
+// it off. Rows of an attention lane: {dispatch released, combine start, combine flags seen,
+// combine end}; of an expert lane: {group start, flags seen, gather end, down-proj released}.
+constexpr int kTraceLen = 1024;
+__device__ __forceinline__ void trace_stamp(unsigned long long* trace, uint32_t epoch, int event) {
+  if (trace != nullptr) trace[(epoch % kTraceLen) * 4 + event] = globaltimer_ns();
+}
+
 // ---- math ----------------------------------------------------------------------------
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

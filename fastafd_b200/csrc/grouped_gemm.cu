@@ -67,6 +67,7 @@ struct GroupedGemmArgs {
   uint32_t* epoch;           // device word: value to publish, then incremented (COMBINE)
   unsigned int* done_counter;  // device word for the last-CTA election (COMBINE), starts 0
   int* status;
+  unsigned long long* trace;   // optional timeline ring (COMBINE: event 3 = flags released)
 };
 
 template <int BLOCK_TOK, bool FP8>
@@ -431,6 +432,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
         __threadfence_system();
         const uint32_t e = *args.epoch;
         for (int p = 0; p < args.num_peers; ++p) st_release_sys(args.peer_flag[p], e);
+        trace_stamp(args.trace, e, 3);
         *args.epoch = e + 1;
         *args.done_counter = 0;
         __threadfence();
@@ -524,7 +526,7 @@ struct AfdGroupedGemmDesc {
   void* peer_combine[afd::kMaxPeers];
   void* peer_flag[afd::kMaxPeers];
   int num_peers, combine_tokens, hidden;
-  void* epoch; void* done_counter; void* status;
+  void* epoch; void* done_counter; void* status; void* trace;
 };
 
 extern "C" int afd_grouped_gemm(const AfdGroupedGemmDesc* d, void* stream_v) {
@@ -565,6 +567,7 @@ extern "C" int afd_grouped_gemm(const AfdGroupedGemmDesc* d, void* stream_v) {
   a.epoch = static_cast<uint32_t*>(d->epoch);
   a.done_counter = static_cast<unsigned int*>(d->done_counter);
   a.status = static_cast<int*>(d->status);
+  a.trace = static_cast<unsigned long long*>(d->trace);
   const int grid = d->grid > 0 ? d->grid : 148;
   if (d->fp8) {
     switch (d->epilogue) {

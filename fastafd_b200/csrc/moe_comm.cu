@@ -51,6 +51,7 @@ struct DispatchArgs {
   uint32_t* epoch;
   unsigned int* done_counter;
   int* status;
+  unsigned long long* trace;
 };
 
 __global__ void dispatch_push_kernel(const DispatchArgs a) {
@@ -120,8 +121,277 @@ __global__ void dispatch_push_kernel(const DispatchArgs a) {
       __threadfence_system();
       const uint32_t e = *a.epoch;
       for (int eg = 0; eg < a.num_eg; ++eg) st_release_sys(a.peer_flag[eg], e);
+      trace_stamp(a.trace, e, 0);
       *a.epoch = e + 1;
       *a.done_counter = 0;
+      __threadfence();
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// Fused post-attention step of an attention rank, one CTA per token:
+//   residual += attn_out ; x = RMSNorm(residual) * w        (x also kept locally for the
+//   shared expert) ; logits = x . gate^T ; scoring + top-k (+ renorm) ; push the row and the
+//   top-k ids into the expert GPUs ; last CTA releases the N2M flags.
+// It replaces four launches (add+norm, gate GEMM, top-k, dispatch) on the decode path; the
+// gate matrix (E x H) stays L2-resident, so re-reading it per token is cheap for decode-sized
+// T. Reference: the fused tensor-core router python/minisgl/kernel/csrc/jit/gate_topk_fused.cu
+// (which can also emit the dispatch quantisation) and the AG kernel's in-kernel gate
+// (sm100_mega_moe_m2n.cuh:571-712).
+// ---------------------------------------------------------------------------------------
+struct RouteDispatchArgs {
+  const __nv_bfloat16* attn_out;   // [T][H]
+  __nv_bfloat16* residual;         // [T][H] in/out
+  const __nv_bfloat16* norm_w;     // [H]
+  const void* gate_w;              // [E][H] bf16 or fp32
+  const float* gate_bias;          // [E] or null (selection bias, sigmoid scoring)
+  __nv_bfloat16* x_out;            // [T][H] normed hidden (local copy)
+  int* topk_idx_out;               // [T][K]
+  float* topk_w_out;               // [T][K]
+  int E, gate_fp32, scoring, renorm, offset1;
+  float eps, route_scale;
+  DispatchArgs d;                  // d.x / d.topk_idx are ignored (produced here)
+};
+
+template <int MAX_PER_LANE>
+__device__ __forceinline__ void warp_topk(const float* s_logit, const float* bias, int E, int K, int scoring,
+                                          int renorm, float scale, int* out_idx, float* out_w, int lane) {
+  float sc[MAX_PER_LANE], sel[MAX_PER_LANE];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < MAX_PER_LANE; ++j) {
+    const int e = j * 32 + lane;
+    sc[j] = e < E ? s_logit[e] : -INFINITY;
+    mx = fmaxf(mx, sc[j]);
+  }
+  if (scoring == 0) {
+    mx = warp_max(mx);
+    float sum = 0.f;
+#pragma unroll
+    for (int j = 0; j < MAX_PER_LANE; ++j) {
+      const int e = j * 32 + lane;
+      sc[j] = e < E ? expf(sc[j] - mx) : 0.f;
+      sum += sc[j];
+    }
+    sum = warp_sum(sum);
+    const float inv = 1.f / sum;
+#pragma unroll
+    for (int j = 0; j < MAX_PER_LANE; ++j) {
+      const int e = j * 32 + lane;
+      sc[j] *= inv;
+      sel[j] = e < E ? sc[j] : -INFINITY;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < MAX_PER_LANE; ++j) {
+      const int e = j * 32 + lane;
+      sc[j] = e < E ? 1.f / (1.f + expf(-sc[j])) : 0.f;
+      sel[j] = e < E ? sc[j] + (bias ? bias[e] : 0.f) : -INFINITY;
+    }
+  }
+  float wsum = 0.f, my_w = 0.f;
+  int my_i = 0;
+  for (int k = 0; k < K; ++k) {
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+#pragma unroll
+    for (int j = 0; j < MAX_PER_LANE; ++j) {
+      if (sel[j] > best) {
+        best = sel[j];
+        bi = j * 32 + lane;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+      if (ob > best || (ob == best && oi < bi)) {
+        best = ob;
+        bi = oi;
+      }
+    }
+    float wv = 0.f;
+#pragma unroll
+    for (int j = 0; j < MAX_PER_LANE; ++j) {
+      if (j * 32 + lane == bi) {
+        wv = sc[j];
+        sel[j] = -INFINITY;
+      }
+    }
+    wv = warp_sum(wv);
+    wsum += wv;
+    if (lane == k) {
+      my_w = wv;
+      my_i = bi;
+    }
+  }
+  const float mul = (renorm ? 1.f / fmaxf(wsum, 1e-20f) : 1.f) * scale;
+  if (lane < K) {
+    out_idx[lane] = my_i;
+    out_w[lane] = my_w * mul;
+  }
+}
+
+__global__ void __launch_bounds__(512) ag_route_dispatch_kernel(const RouteDispatchArgs a) {
+  extern __shared__ float rsm[];        // x (H floats) | logits (E floats) | red (32)
+  const DispatchArgs& d = a.d;
+  const int H = d.H, t = blockIdx.x;
+  float* xs = rsm;
+  float* s_logit = rsm + H;
+  float* red = s_logit + a.E;
+  __shared__ int s_idx[32];
+  __shared__ float s_w[32];
+  __shared__ uint32_t s_mask;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+
+  // 1. residual add + RMSNorm
+  float ss = 0.f;
+  for (int i = threadIdx.x * 8; i < H; i += blockDim.x * 8) {
+    const uint4 xa = *reinterpret_cast<const uint4*>(a.attn_out + static_cast<size_t>(t) * H + i);
+    uint4 ra = *reinterpret_cast<const uint4*>(a.residual + static_cast<size_t>(t) * H + i);
+    const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&xa);
+    __nv_bfloat162* r2 = reinterpret_cast<__nv_bfloat162*>(&ra);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float2 xv = __bfloat1622float2(x2[j]);
+      float2 rv = __bfloat1622float2(r2[j]);
+      rv.x += xv.x;
+      rv.y += xv.y;
+      r2[j] = __floats2bfloat162_rn(rv.x, rv.y);
+      rv = __bfloat1622float2(r2[j]);
+      xs[i + 2 * j] = rv.x;
+      xs[i + 2 * j + 1] = rv.y;
+      ss += rv.x * rv.x + rv.y * rv.y;
+    }
+    *reinterpret_cast<uint4*>(a.residual + static_cast<size_t>(t) * H + i) = ra;
+  }
+  ss = warp_sum(ss);
+  if (lane == 0) red[warp] = ss;
+  __syncthreads();
+  float tot = lane < nw ? red[lane] : 0.f;
+  tot = warp_sum(tot);
+  const float inv = rsqrtf(tot / H + a.eps);
+  __syncthreads();
+  for (int i = threadIdx.x * 8; i < H; i += blockDim.x * 8) {
+    const uint4 wa = *reinterpret_cast<const uint4*>(a.norm_w + i);
+    const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&wa);
+    uint4 oa;
+    __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&oa);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float2 g = __bfloat1622float2(w2[j]);
+      if (a.offset1) {
+        g.x += 1.f;
+        g.y += 1.f;
+      }
+      o2[j] = __floats2bfloat162_rn(xs[i + 2 * j] * inv * g.x, xs[i + 2 * j + 1] * inv * g.y);
+      const float2 back = __bfloat1622float2(o2[j]);    // the router sees the bf16-rounded x
+      xs[i + 2 * j] = back.x;
+      xs[i + 2 * j + 1] = back.y;
+    }
+    *reinterpret_cast<uint4*>(a.x_out + static_cast<size_t>(t) * H + i) = oa;
+  }
+  __syncthreads();
+
+  // 2. router logits: one warp per expert, lanes split H
+  for (int e = warp; e < a.E; e += nw) {
+    float acc = 0.f;
+    if (a.gate_fp32) {
+      const float* g = static_cast<const float*>(a.gate_w) + static_cast<size_t>(e) * H;
+      for (int i = lane * 4; i < H; i += 128) {
+        const float4 gv = *reinterpret_cast<const float4*>(g + i);
+        acc += gv.x * xs[i] + gv.y * xs[i + 1] + gv.z * xs[i + 2] + gv.w * xs[i + 3];
+      }
+    } else {
+      const __nv_bfloat16* g = static_cast<const __nv_bfloat16*>(a.gate_w) + static_cast<size_t>(e) * H;
+      for (int i = lane * 8; i < H; i += 256) {
+        const uint4 ga = *reinterpret_cast<const uint4*>(g + i);
+        const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&ga);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const float2 gv = __bfloat1622float2(g2[j]);
+          acc = fmaf(gv.x, xs[i + 2 * j], acc);
+          acc = fmaf(gv.y, xs[i + 2 * j + 1], acc);
+        }
+      }
+    }
+    acc = warp_sum(acc);
+    if (lane == 0) s_logit[e] = acc;
+  }
+  __syncthreads();
+
+  // 3. scoring + top-k by warp 0
+  if (warp == 0) {
+    if (a.E <= 128) warp_topk<4>(s_logit, a.gate_bias, a.E, d.K, a.scoring, a.renorm, a.route_scale, s_idx, s_w, lane);
+    else if (a.E <= 256) warp_topk<8>(s_logit, a.gate_bias, a.E, d.K, a.scoring, a.renorm, a.route_scale, s_idx, s_w, lane);
+    else warp_topk<16>(s_logit, a.gate_bias, a.E, d.K, a.scoring, a.renorm, a.route_scale, s_idx, s_w, lane);
+    __syncwarp();
+    uint32_t mask = 0;
+    if (lane < d.K) {
+      const int e = s_idx[lane];
+      a.topk_idx_out[static_cast<size_t>(t) * d.K + lane] = e;
+      a.topk_w_out[static_cast<size_t>(t) * d.K + lane] = s_w[lane];
+      const int eg = e / d.experts_per_eg;
+      if (eg < d.num_eg) mask = 1u << eg;
+      else set_status(d.status, kStatusBadExtent);
+      for (int g = 0; g < d.num_eg; ++g) {
+        d.peer_recv_idx[g][(static_cast<size_t>(d.src_rank) * d.recv_tokens + t) * d.K + lane] = e;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mask |= __shfl_xor_sync(0xffffffffu, mask, o);
+    if (lane == 0) s_mask = mask;
+  }
+  __syncthreads();
+
+  // 4. push the row to every expert GPU that owns one of its experts
+  const uint32_t mask = s_mask;
+  const size_t dst_row = static_cast<size_t>(d.src_rank) * d.recv_tokens + t;
+  if (!d.fp8) {
+    for (int i = threadIdx.x * 8; i < H; i += blockDim.x * 8) {
+      uint4 v;
+      __nv_bfloat162* v2 = reinterpret_cast<__nv_bfloat162*>(&v);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) v2[j] = __floats2bfloat162_rn(xs[i + 2 * j], xs[i + 2 * j + 1]);
+      for (int g = 0; g < d.num_eg; ++g) {
+        if (mask & (1u << g)) {
+          *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(d.peer_recv_x[g]) + dst_row * H + i) = v;
+        }
+      }
+    }
+  } else {
+    const int groups = H / 128;
+    for (int g128 = warp; g128 < groups; g128 += nw) {
+      const float4 f = *reinterpret_cast<const float4*>(xs + g128 * 128 + lane * 4);
+      float amax = fmaxf(fmaxf(fabsf(f.x), fabsf(f.y)), fmaxf(fabsf(f.z), fabsf(f.w)));
+      amax = warp_max(amax);
+      const float scale = fmaxf(amax, 1e-10f) / 448.f;
+      const float is = 1.f / scale;
+      uint32_t packed = 0;
+      packed |= static_cast<uint32_t>(__nv_cvt_float_to_fp8(f.x * is, __NV_SATFINITE, __NV_E4M3));
+      packed |= static_cast<uint32_t>(__nv_cvt_float_to_fp8(f.y * is, __NV_SATFINITE, __NV_E4M3)) << 8;
+      packed |= static_cast<uint32_t>(__nv_cvt_float_to_fp8(f.z * is, __NV_SATFINITE, __NV_E4M3)) << 16;
+      packed |= static_cast<uint32_t>(__nv_cvt_float_to_fp8(f.w * is, __NV_SATFINITE, __NV_E4M3)) << 24;
+      for (int g = 0; g < d.num_eg; ++g) {
+        if (mask & (1u << g)) {
+          *reinterpret_cast<uint32_t*>(static_cast<uint8_t*>(d.peer_recv_x[g]) + dst_row * H + g128 * 128 + lane * 4) = packed;
+          if (lane == 0) d.peer_recv_scale[g][dst_row * groups + g128] = scale;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    const unsigned int prev = atomicAdd(d.done_counter, 1u);
+    if (prev == gridDim.x - 1) {
+      __threadfence_system();
+      const uint32_t e = *d.epoch;
+      for (int g = 0; g < d.num_eg; ++g) st_release_sys(d.peer_flag[g], e);
+      trace_stamp(d.trace, e, 0);
+      *d.epoch = e + 1;
+      *d.done_counter = 0;
       __threadfence();
     }
   }
@@ -141,6 +411,7 @@ struct GroupArgs {
   int* expert_counts;        // [experts_local] (for load statistics), may be null
   uint64_t timeout_ns;
   int* status;
+  unsigned long long* trace;
 };
 
 // One CTA. Shared memory: 3 * experts_local ints.
@@ -150,7 +421,10 @@ __global__ void eg_group_kernel(const GroupArgs a) {
   int* off = sm + a.experts_local;
   int* cur = sm + 2 * a.experts_local;
   __shared__ uint32_t s_epoch;
-  if (threadIdx.x == 0) s_epoch = *a.epoch;
+  if (threadIdx.x == 0) {
+    s_epoch = *a.epoch;
+    trace_stamp(a.trace, s_epoch, 0);
+  }
   for (int e = threadIdx.x; e < a.experts_local; e += blockDim.x) {
     cnt[e] = 0;
     cur[e] = 0;
@@ -158,6 +432,7 @@ __global__ void eg_group_kernel(const GroupArgs a) {
   __syncthreads();
   if (threadIdx.x < a.A) wait_flag_ge(a.n2m_flag + threadIdx.x, s_epoch, a.timeout_ns, a.status);
   __syncthreads();
+  if (threadIdx.x == 0) trace_stamp(a.trace, s_epoch, 1);
   const int per_src = a.T * a.K;
   const int total = a.A * per_src;
   for (int i = threadIdx.x; i < total; i += blockDim.x) {
@@ -318,16 +593,21 @@ struct CombineArgs {
   int offset1;
   uint64_t timeout_ns;
   int* status;
+  unsigned long long* trace;
 };
 
 __global__ void ag_combine_kernel(const CombineArgs a) {
   extern __shared__ float sbuf[];   // H floats + 32
   float* red = sbuf + a.H;
   __shared__ uint32_t s_epoch;
-  if (threadIdx.x == 0) s_epoch = *a.epoch;
+  if (threadIdx.x == 0) {
+    s_epoch = *a.epoch;
+    if (blockIdx.x == 0) trace_stamp(a.trace, s_epoch, 1);
+  }
   __syncthreads();
   if (threadIdx.x < a.num_eg) wait_flag_ge(a.m2n_flag + threadIdx.x, s_epoch, a.timeout_ns, a.status);
   __syncthreads();
+  if (threadIdx.x == 0 && blockIdx.x == 0) trace_stamp(a.trace, s_epoch, 2);
   const int t = blockIdx.x;
   float ss = 0.f;
   for (int i = threadIdx.x * 8; i < a.H; i += blockDim.x * 8) {
@@ -408,6 +688,7 @@ __global__ void ag_combine_kernel(const CombineArgs a) {
   if (threadIdx.x == 0) {
     const unsigned int prev = atomicAdd(a.done_counter, 1u);
     if (prev == gridDim.x - 1) {
+      trace_stamp(a.trace, s_epoch, 3);
       *a.epoch = s_epoch + 1;
       *a.done_counter = 0;
       __threadfence();
@@ -437,7 +718,7 @@ struct AfdDispatchDesc {
   int T, H, K, src_rank, num_eg, experts_per_eg, fp8, recv_tokens;
   void* peer_recv_x[kMaxRanks]; void* peer_recv_scale[kMaxRanks]; void* peer_recv_idx[kMaxRanks];
   void* peer_flag[kMaxRanks];
-  void* epoch; void* done_counter; void* status;
+  void* epoch; void* done_counter; void* status; void* trace;
 };
 
 extern "C" int afd_dispatch_push(const AfdDispatchDesc* d, void* stream) {
@@ -457,7 +738,50 @@ extern "C" int afd_dispatch_push(const AfdDispatchDesc* d, void* stream) {
   a.epoch = static_cast<uint32_t*>(d->epoch);
   a.done_counter = static_cast<unsigned int*>(d->done_counter);
   a.status = static_cast<int*>(d->status);
+  a.trace = static_cast<unsigned long long*>(d->trace);
   dispatch_push_kernel<<<d->T, 256, 0, static_cast<cudaStream_t>(stream)>>>(a);
+  AFD_CHECK_LAUNCH();
+  return 0;
+}
+
+struct AfdRouteDispatchDesc {
+  const void* attn_out; void* residual; const void* norm_w; const void* gate_w; const void* gate_bias;
+  void* x_out; void* topk_idx_out; void* topk_w_out;
+  int E, gate_fp32, scoring, renorm, offset1;
+  float eps, route_scale;
+  AfdDispatchDesc d;
+};
+
+extern "C" int afd_ag_route_dispatch(const AfdRouteDispatchDesc* r, void* stream) {
+  const AfdDispatchDesc* d = &r->d;
+  if (d->T == 0) return -1;
+  if (d->num_eg > kMaxRanks || d->H % 256 != 0 || d->K > 32 || d->T > d->recv_tokens || r->E > 512) return -2;
+  RouteDispatchArgs a{};
+  a.attn_out = static_cast<const __nv_bfloat16*>(r->attn_out);
+  a.residual = static_cast<__nv_bfloat16*>(r->residual);
+  a.norm_w = static_cast<const __nv_bfloat16*>(r->norm_w);
+  a.gate_w = r->gate_w;
+  a.gate_bias = static_cast<const float*>(r->gate_bias);
+  a.x_out = static_cast<__nv_bfloat16*>(r->x_out);
+  a.topk_idx_out = static_cast<int*>(r->topk_idx_out);
+  a.topk_w_out = static_cast<float*>(r->topk_w_out);
+  a.E = r->E; a.gate_fp32 = r->gate_fp32; a.scoring = r->scoring; a.renorm = r->renorm; a.offset1 = r->offset1;
+  a.eps = r->eps; a.route_scale = r->route_scale;
+  DispatchArgs& da = a.d;
+  da.T = d->T; da.H = d->H; da.K = d->K; da.src_rank = d->src_rank; da.num_eg = d->num_eg;
+  da.experts_per_eg = d->experts_per_eg; da.fp8 = d->fp8; da.recv_tokens = d->recv_tokens;
+  for (int i = 0; i < d->num_eg; ++i) {
+    da.peer_recv_x[i] = d->peer_recv_x[i];
+    da.peer_recv_scale[i] = static_cast<float*>(d->peer_recv_scale[i]);
+    da.peer_recv_idx[i] = static_cast<int*>(d->peer_recv_idx[i]);
+    da.peer_flag[i] = static_cast<uint32_t*>(d->peer_flag[i]);
+  }
+  da.epoch = static_cast<uint32_t*>(d->epoch);
+  da.done_counter = static_cast<unsigned int*>(d->done_counter);
+  da.status = static_cast<int*>(d->status);
+  da.trace = static_cast<unsigned long long*>(d->trace);
+  const size_t smem = (static_cast<size_t>(d->H) + r->E + 32) * sizeof(float);
+  ag_route_dispatch_kernel<<<d->T, 512, smem, static_cast<cudaStream_t>(stream)>>>(a);
   AFD_CHECK_LAUNCH();
   return 0;
 }
@@ -471,6 +795,7 @@ struct AfdGroupDesc {
   // gather
   const void* recv_x; const void* recv_scale; void* pool_x; void* pool_scale;
   int row_bytes, scale_per_row;
+  void* trace;
 };
 
 extern "C" int afd_eg_group_gather(const AfdGroupDesc* d, void* stream) {
@@ -490,6 +815,7 @@ extern "C" int afd_eg_group_gather(const AfdGroupDesc* d, void* stream) {
   g.expert_counts = static_cast<int*>(d->expert_counts);
   g.timeout_ns = d->timeout_ns;
   g.status = static_cast<int*>(d->status);
+  g.trace = static_cast<unsigned long long*>(d->trace);
   eg_group_kernel<<<1, 1024, 3 * d->experts_local * sizeof(int), st>>>(g);
   AFD_CHECK_LAUNCH();
   GatherArgs ga{};
@@ -513,6 +839,7 @@ struct AfdCombineDesc {
   float eps; int offset1;
   unsigned long long timeout_ns;
   void* status;
+  void* trace;
 };
 
 extern "C" int afd_ag_combine(const AfdCombineDesc* d, void* stream) {
@@ -534,6 +861,7 @@ extern "C" int afd_ag_combine(const AfdCombineDesc* d, void* stream) {
   a.normed = static_cast<__nv_bfloat16*>(d->normed);
   a.eps = d->eps; a.offset1 = d->offset1; a.timeout_ns = d->timeout_ns;
   a.status = static_cast<int*>(d->status);
+  a.trace = static_cast<unsigned long long*>(d->trace);
   const int threads = d->H / 8 >= 512 ? 512 : 256;
   ag_combine_kernel<<<d->T, threads, (d->H + 32) * sizeof(float), static_cast<cudaStream_t>(stream)>>>(a);
   AFD_CHECK_LAUNCH();

@@ -21,10 +21,15 @@ from typing import List, Optional
 import torch
 
 from ..ops import EPI_COMBINE, EPI_SWIGLU, NUM_SMS, grouped_gemm
-from ..ops._lib import CombineDesc, DispatchDesc, GroupDesc, check, cur_stream, lib, ptr
+from ..ops._lib import CombineDesc, DispatchDesc, GroupDesc, RouteDispatchDesc, check, cur_stream, lib, ptr
 from ..parallel.fabric import Fabric, Layout
 
 DEFAULT_TIMEOUT_NS = int(float(os.environ.get("FASTAFD_FLAG_TIMEOUT_S", "20")) * 1e9)
+TRACE_LEN = 1024      # rows of the device-side timeline ring (kTraceLen in csrc/common.cuh)
+
+
+def _trace_enabled() -> bool:
+    return os.environ.get("FASTAFD_COMM_TRACE", "0") == "1"
 
 
 @dataclass(frozen=True)
@@ -103,6 +108,8 @@ class AgMoeEndpoint:
         self.lay, self.eg_lay = ag_layout(cfg), eg_layout(cfg)
         self.status = torch.zeros(1, dtype=torch.int32, device=device)
         self.lanes = [_LaneWords(device) for _ in range(cfg.num_lanes)]
+        self.trace = ([torch.zeros(TRACE_LEN, 4, dtype=torch.int64, device=device) for _ in range(cfg.num_lanes)]
+                      if _trace_enabled() else None)
         heap = fabric.heap
         self.combine = [heap.view(self.lay.offset(f"combine{l}"), (cfg.topk, cfg.max_tokens, cfg.hidden),
                                   torch.bfloat16) for l in range(cfg.num_lanes)]
@@ -121,6 +128,7 @@ class AgMoeEndpoint:
             d.peer_flag[i] = self.fabric.peer_ptr(r, self.eg_lay.offset(f"n2m_flag{lane}")) + 4 * self.ag_index
         w = self.lanes[lane]
         d.epoch, d.done_counter, d.status = ptr(w.epoch), ptr(w.done), ptr(self.status)
+        d.trace = ptr(self.trace[lane]) if self.trace else None
         return d
 
     def dispatch(self, lane: int, x: torch.Tensor, topk_idx: torch.Tensor) -> None:
@@ -129,6 +137,22 @@ class AgMoeEndpoint:
         assert x.is_contiguous() and topk_idx.is_contiguous() and topk_idx.dtype == torch.int32
         d.x, d.topk_idx, d.T = ptr(x), ptr(topk_idx), x.shape[0]
         check(lib().afd_dispatch_push(C.byref(d), cur_stream()), "dispatch_push")
+
+    def route_dispatch(self, lane: int, attn_out: torch.Tensor, residual: torch.Tensor, norm_w: torch.Tensor,
+                       gate_w: torch.Tensor, gate_bias: Optional[torch.Tensor], x_out: torch.Tensor,
+                       topk_idx: torch.Tensor, topk_w: torch.Tensor, *, scoring: str, renorm: bool, eps: float,
+                       offset1: bool = False, route_scale: float = 1.0) -> None:
+        """One launch for: residual += attn_out; x = rmsnorm(residual); router; push to experts."""
+        r = RouteDispatchDesc()
+        C.memmove(C.byref(r.d), C.byref(self._dispatch_desc[lane]), C.sizeof(DispatchDesc))
+        r.d.T = attn_out.shape[0]
+        r.attn_out, r.residual, r.norm_w = ptr(attn_out), ptr(residual), ptr(norm_w)
+        r.gate_w, r.gate_bias = ptr(gate_w), ptr(gate_bias)
+        r.x_out, r.topk_idx_out, r.topk_w_out = ptr(x_out), ptr(topk_idx), ptr(topk_w)
+        r.E, r.gate_fp32 = gate_w.shape[0], int(gate_w.dtype == torch.float32)
+        r.scoring, r.renorm, r.offset1 = (0 if scoring == "softmax" else 1), int(renorm), int(offset1)
+        r.eps, r.route_scale = eps, route_scale
+        check(lib().afd_ag_route_dispatch(C.byref(r), cur_stream()), "ag_route_dispatch")
 
     def combine_reduce(self, lane: int, topk_w: torch.Tensor, topk_idx: Optional[torch.Tensor], T: int,
                        scale: float = 1.0, extra: Optional[torch.Tensor] = None,
@@ -147,6 +171,7 @@ class AgMoeEndpoint:
             y = torch.empty(T, cfg.hidden, dtype=torch.bfloat16, device=self.device)
         d.extra, d.y, d.residual, d.norm_w, d.normed = ptr(extra), ptr(y), ptr(residual), ptr(norm_w), ptr(normed)
         d.eps, d.offset1, d.timeout_ns, d.status = eps, int(offset1), self.timeout_ns, ptr(self.status)
+        d.trace = ptr(self.trace[lane]) if self.trace else None
         check(lib().afd_ag_combine(C.byref(d), cur_stream()), "ag_combine")
         return y if normed is None else normed
 
@@ -162,6 +187,8 @@ class EgMoeEndpoint:
         self.lay, self.ag_lay = eg_layout(cfg), ag_layout(cfg)
         self.status = torch.zeros(1, dtype=torch.int32, device=device)
         self.lanes = [_LaneWords(device) for _ in range(cfg.num_lanes)]
+        self.trace = ([torch.zeros(TRACE_LEN, 4, dtype=torch.int64, device=device) for _ in range(cfg.num_lanes)]
+                      if _trace_enabled() else None)
         heap, L = fabric.heap, cfg.num_lanes
         xdt = torch.float8_e4m3fn if cfg.fp8 else torch.bfloat16
         self.recv_x = [heap.view(self.lay.offset(f"recv_x{l}"), (cfg.num_ag, cfg.max_tokens, cfg.hidden), xdt)
@@ -199,6 +226,7 @@ class EgMoeEndpoint:
         d.recv_x, d.recv_scale = ptr(self.recv_x[lane]), ptr(self.recv_scale[lane]) if cfg.fp8 else None
         d.pool_x, d.pool_scale = ptr(self.pool_x), ptr(self.pool_xs)
         d.row_bytes, d.scale_per_row = cfg.row_bytes, cfg.hidden // 128
+        d.trace = ptr(self.trace[lane]) if self.trace else None
         check(lib().afd_eg_group_gather(C.byref(d), cur_stream()), "eg_group_gather")
 
     def run_layer(self, lane: int, T: int, w13: torch.Tensor, w2: torch.Tensor,
@@ -220,7 +248,26 @@ class EgMoeEndpoint:
                      block_tok=cfg.block_tok, epilogue=EPI_COMBINE, fp8=cfg.fp8, x_scale=self.pool_hs,
                      w_scale=w2_scale, row_meta=self.row_meta, peer_combine=self.peer_combine[lane],
                      peer_flag=self.peer_flag[lane], combine_tokens=cfg.max_tokens, hidden=cfg.hidden,
-                     epoch=w.epoch2, done_counter=w.done2, status=self.status, grid=self.grid)
+                     epoch=w.epoch2, done_counter=w.done2, status=self.status, grid=self.grid,
+                     trace=self.trace[lane] if self.trace else None)
+
+
+def summarize_trace(trace: torch.Tensor, role: str, last: int = 256) -> dict:
+    """Mean durations (microseconds) over the most recent `last` rounds of one lane's timeline.
+    attention: wait = combine start -> flags seen (idle time waiting for the experts),
+               reduce = flags seen -> combine end, round = dispatch released -> combine end.
+    expert   : wait = group start -> flags seen (idle time waiting for attention ranks),
+               busy = flags seen -> down-projection flags released."""
+    t = trace.cpu().numpy().astype("int64")
+    rows = t[(t > 0).all(axis=1)] if role == "attention" else t[(t[:, [0, 1, 3]] > 0).all(axis=1)]
+    rows = rows[rows[:, 0].argsort()][-last:]
+    if len(rows) == 0:
+        return {}
+    us = lambda a: float(a.mean()) / 1e3  # noqa: E731
+    if role == "attention":
+        return {"wait_us": us(rows[:, 2] - rows[:, 1]), "reduce_us": us(rows[:, 3] - rows[:, 2]),
+                "round_trip_us": us(rows[:, 3] - rows[:, 0]), "rounds": len(rows)}
+    return {"wait_us": us(rows[:, 1] - rows[:, 0]), "busy_us": us(rows[:, 3] - rows[:, 1]), "rounds": len(rows)}
 
 
 def check_status(status: torch.Tensor, what: str) -> None:

@@ -209,7 +209,7 @@ def dense_tile_schedule(M: int, block_tok: int, device) -> tuple[torch.Tensor, t
 def grouped_gemm(*, w, x, num_experts, n_per_expert, k, tile_info, num_tok_tiles, block_tok,
                  epilogue, out=None, out_ld=0, fp8=False, x_scale=None, w_scale=None, out_q=None,
                  out_scale=None, row_meta=None, peer_combine=(), peer_flag=(), combine_tokens=0,
-                 hidden=0, epoch=None, done_counter=None, status=None, grid=NUM_SMS):
+                 hidden=0, epoch=None, done_counter=None, status=None, grid=NUM_SMS, trace=None):
     """Low-level launcher of the tcgen05 grouped GEMM (see csrc/grouped_gemm.cu)."""
     d = GroupedGemmDesc()
     d.w, d.x = ptr(w), ptr(x)
@@ -225,7 +225,7 @@ def grouped_gemm(*, w, x, num_experts, n_per_expert, k, tile_info, num_tok_tiles
     for i, p in enumerate(peer_flag):
         d.peer_flag[i] = p
     d.num_peers, d.combine_tokens, d.hidden = len(peer_combine), combine_tokens, hidden
-    d.epoch, d.done_counter, d.status = ptr(epoch), ptr(done_counter), ptr(status)
+    d.epoch, d.done_counter, d.status, d.trace = ptr(epoch), ptr(done_counter), ptr(status), ptr(trace)
     check(lib().afd_grouped_gemm(C.byref(d), cur_stream()), "grouped_gemm")
 
 

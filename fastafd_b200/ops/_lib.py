@@ -28,7 +28,7 @@ class GroupedGemmDesc(C.Structure):
         ("row_meta", VP),
         ("peer_combine", VP * MAX_PEERS), ("peer_flag", VP * MAX_PEERS),
         ("num_peers", C.c_int), ("combine_tokens", C.c_int), ("hidden", C.c_int),
-        ("epoch", VP), ("done_counter", VP), ("status", VP),
+        ("epoch", VP), ("done_counter", VP), ("status", VP), ("trace", VP),
     ]
 
 
@@ -39,7 +39,17 @@ class DispatchDesc(C.Structure):
         ("num_eg", C.c_int), ("experts_per_eg", C.c_int), ("fp8", C.c_int), ("recv_tokens", C.c_int),
         ("peer_recv_x", VP * MAX_PEERS), ("peer_recv_scale", VP * MAX_PEERS),
         ("peer_recv_idx", VP * MAX_PEERS), ("peer_flag", VP * MAX_PEERS),
-        ("epoch", VP), ("done_counter", VP), ("status", VP),
+        ("epoch", VP), ("done_counter", VP), ("status", VP), ("trace", VP),
+    ]
+
+
+class RouteDispatchDesc(C.Structure):
+    _fields_ = [
+        ("attn_out", VP), ("residual", VP), ("norm_w", VP), ("gate_w", VP), ("gate_bias", VP),
+        ("x_out", VP), ("topk_idx_out", VP), ("topk_w_out", VP),
+        ("E", C.c_int), ("gate_fp32", C.c_int), ("scoring", C.c_int), ("renorm", C.c_int), ("offset1", C.c_int),
+        ("eps", C.c_float), ("route_scale", C.c_float),
+        ("d", DispatchDesc),
     ]
 
 
@@ -54,6 +64,7 @@ class GroupDesc(C.Structure):
         ("status", VP),
         ("recv_x", VP), ("recv_scale", VP), ("pool_x", VP), ("pool_scale", VP),
         ("row_bytes", C.c_int), ("scale_per_row", C.c_int),
+        ("trace", VP),
     ]
 
 
@@ -67,6 +78,7 @@ class CombineDesc(C.Structure):
         ("eps", C.c_float), ("offset1", C.c_int),
         ("timeout_ns", C.c_ulonglong),
         ("status", VP),
+        ("trace", VP),
     ]
 
 
@@ -89,6 +101,7 @@ _SIGNATURES = {
     "afd_decode_attention": (C.c_int, [VP, VP, VP, VP, VP, VP, VP, C.c_int, C.c_int, C.c_int, C.c_int,
                                        C.c_int, C.c_int, C.c_int, C.c_long, C.c_int, C.c_float, VP, VP]),
     "afd_dispatch_push": (C.c_int, [C.POINTER(DispatchDesc), VP]),
+    "afd_ag_route_dispatch": (C.c_int, [C.POINTER(RouteDispatchDesc), VP]),
     "afd_eg_group_gather": (C.c_int, [C.POINTER(GroupDesc), VP]),
     "afd_ag_combine": (C.c_int, [C.POINTER(CombineDesc), VP]),
     "afd_wait_flag": (C.c_int, [VP, C.c_uint, C.c_ulonglong, VP, VP]),

@@ -195,11 +195,27 @@ class AttentionWorker:
         """Attention block + post-attention norm + router for one layer of one micro-batch; for
         MoE layers ends with the dispatch on the lane stream, for dense layers with the local MLP."""
         m, c = self.model, self.cfg
+        moe = c.is_moe_layer(layer)
+        fused = (moe and self.cuda and not mb.meta.is_prefill and c.n_group == 1
+                 and self.client.can_fuse_route(mb.T, c.num_experts, c.hidden_size))
         with nvtx_range(f"AFD_AG_Attn_L{layer}_mb{mb.lane}"):
             attn_out = m.attention(layer, mb.normed, mb.meta, self.kv, self.gdn)
-            moe = c.is_moe_layer(layer)
-            x = m.post_attn_norm(layer, attn_out, mb.residual, out=mb.x_moe if moe else None)
-        if moe:
+            if fused:
+                p = f"model.layers.{layer}."
+                self.client.route_dispatch(
+                    mb.lane, layer, attn_out, mb.residual, m.w[p + "post_attention_layernorm.weight"],
+                    m.w[p + "mlp.gate.weight"], m.w.get(p + "mlp.gate.e_score_correction_bias"), mb.x_moe,
+                    mb.topk_idx, mb.topk_w, scoring=c.scoring, renorm=c.norm_topk_prob, eps=c.rms_eps,
+                    offset1=c.norm_offset1)
+                x = mb.x_moe
+            else:
+                x = m.post_attn_norm(layer, attn_out, mb.residual, out=mb.x_moe if moe else None)
+        if moe and fused:
+            mb.extra = m.local_mlp(layer, x)
+            mb.keep += [attn_out, mb.extra]
+            with self._on_lane(mb.lane):
+                self.client.after_dispatch(mb.lane, layer, mb.T)
+        elif moe:
             m.route(layer, x, out_idx=mb.topk_idx, out_w=mb.topk_w)
             if mb.meta.is_prefill and mb.pad_from < mb.T:
                 mb.topk_idx[mb.pad_from:] = -1          # padding tokens are routed nowhere

@@ -38,6 +38,11 @@ class MoeClient:
     def status_tensors(self) -> List[torch.Tensor]:
         return []
 
+    # Optional fast path: one launch for post-attention norm + router + dispatch. Clients that
+    # have it return True from `can_fuse_route`.
+    def can_fuse_route(self, T: int, num_experts: int, hidden: int) -> bool:
+        return False
+
 
 def _finish_combine(y, residual, norm_w, eps, offset1, normed_out):
     normed = ops.add_rmsnorm(y, residual, norm_w, eps, offset1)
@@ -113,6 +118,19 @@ class FabricMoeClient(MoeClient):
         self.ep.dispatch(lane, x, topk_idx)
         if self.colocated is not None:
             self.colocated.serve(lane, layer, x.shape[0])
+
+    def can_fuse_route(self, T, num_experts, hidden):
+        return T <= 256 and num_experts <= 512 and hidden % 256 == 0
+
+    def route_dispatch(self, lane, layer, attn_out, residual, norm_w, gate_w, gate_bias, x_out, topk_idx, topk_w, *,
+                       scoring, renorm, eps, offset1=False):
+        self.ep.route_dispatch(lane, attn_out, residual, norm_w, gate_w, gate_bias, x_out, topk_idx, topk_w,
+                               scoring=scoring, renorm=renorm, eps=eps, offset1=offset1)
+
+    def after_dispatch(self, lane, layer, T):
+        """Work that follows a push in the same process (colocated expert stage)."""
+        if self.colocated is not None:
+            self.colocated.serve(lane, layer, T)
 
     def combine(self, lane, layer, T, topk_w, topk_idx, residual, norm_w, eps, *, extra=None, scale=1.0,
                 offset1=False, normed_out=None):

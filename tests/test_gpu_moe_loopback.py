@@ -117,3 +117,39 @@ def test_combine_times_out_when_expert_rank_is_silent():
         check_status(ags[0].status, "ag")
     for f in fabs:
         f.close()
+
+
+@pytest.mark.parametrize("scoring,gate_fp32", [("softmax", False), ("sigmoid", True)])
+def test_fused_route_dispatch_matches_separate_ops(scoring, gate_fp32):
+    """residual add + RMSNorm + router + push in one launch == the four separate ops."""
+    H, I, E, K, T = 512, 256, 16, 4, 19
+    cfg = MoeCommConfig(num_ag=1, num_eg=2, num_lanes=1, max_tokens=32, hidden=H, topk=K, num_experts=E,
+                        intermediate=I, block_tok=16)
+    fabs, ags, egs = _setup(cfg)
+    g = torch.Generator().manual_seed(3)
+    attn_out = torch.randn(T, H, generator=g).to(torch.bfloat16).to(DEV)
+    residual = torch.randn(T, H, generator=g).to(torch.bfloat16).to(DEV)
+    norm_w = (1 + 0.1 * torch.randn(H, generator=g)).to(torch.bfloat16).to(DEV)
+    gate = (torch.randn(E, H, generator=g) * 0.1).to(torch.float32 if gate_fp32 else torch.bfloat16).to(DEV)
+    bias = (torch.randn(E, generator=g) * 0.1).to(DEV) if scoring == "sigmoid" else None
+    res_ref = residual.clone()
+    x_ref = ops.add_rmsnorm(attn_out, res_ref, norm_w, 1e-6)
+    logits = torch.nn.functional.linear(x_ref.float(), gate.float())
+    idx_ref, w_ref = ref.topk_route(logits.cpu(), None if bias is None else bias.cpu(), K, scoring, True)
+    x_out = torch.empty_like(attn_out)
+    idx = torch.empty(T, K, dtype=torch.int32, device=DEV)
+    w = torch.empty(T, K, dtype=torch.float32, device=DEV)
+    ags[0].route_dispatch(0, attn_out, residual, norm_w, gate, bias, x_out, idx, w, scoring=scoring, renorm=True, eps=1e-6)
+    torch.cuda.synchronize()
+    check_status(ags[0].status, "ag")
+    assert torch.equal(residual, res_ref) and torch.equal(x_out, x_ref)
+    assert torch.equal(idx.cpu(), idx_ref)
+    torch.testing.assert_close(w.cpu(), w_ref, atol=1e-5, rtol=1e-4)
+    # what landed in the expert GPUs' receive slots
+    for e, eg in enumerate(egs):
+        assert torch.equal(eg.recv_idx[0][0, :T].cpu(), idx_ref)
+        owns = ((idx_ref // cfg.experts_per_eg) == e).any(dim=1)
+        assert torch.equal(eg.recv_x[0][0, :T][owns.to(DEV)], x_ref[owns.to(DEV)])
+        assert int(eg.n2m_flag[0][0]) == 1
+    for f in fabs:
+        f.close()
