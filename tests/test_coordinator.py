@@ -1,0 +1,140 @@
+"""Coordinator behaviour on CPU: overlap window, dummy lanes, admission, failure detection
+(injected on the host: a fake worker that stops replying, a worker that reports an error
+status), admission stall, shutdown idempotence."""
+import numpy as np
+import pytest
+import torch
+
+from fastafd_b200.config import PRESETS, RuntimeConfig
+from fastafd_b200.coordinator import AfdCoordinator, CoordinatorError, InProcTransport, WorkerTransport
+from fastafd_b200.core import SamplingParams
+from fastafd_b200.engine import AfdEngine, SpmdDriver
+from fastafd_b200.protocol import AfdTopology, AgStepReply, EgStepReply, WorkerFailure
+from fastafd_b200.scheduler.lane import AdmissionError
+
+
+def _rt(**kw):
+    base = dict(model_path="tiny-qwen3-moe", num_mb=2, page_size=16, num_pages=64, max_running_requests=8,
+                max_seq_len=128, cuda_graph_max_bs=8, device="cpu", dtype="float32", use_cuda_graph=False)
+    base.update(kw)
+    return RuntimeConfig(**base)
+
+
+class FakeWorkers(WorkerTransport):
+    """Workers that answer every plan with token 7 (or misbehave on request)."""
+
+    def __init__(self, drop_rank=None, bad_status_rank=None, fail_rank=None):
+        self.out, self.drop_rank, self.bad_status_rank, self.fail_rank = [], drop_rank, bad_status_rank, fail_rank
+        self.sent = []
+
+    def send_step(self, step_id, ag_plans, eg_plans):
+        self.sent.append((step_id, sorted(ag_plans), sorted(eg_plans)))
+        for r, (plan, _) in ag_plans.items():
+            if r == self.drop_rank:
+                continue
+            if r == self.fail_rank:
+                self.out.append(WorkerFailure(rank=r, error="boom"))
+                continue
+            n = sum(len(mb.rows) for mb in plan.mbs)
+            self.out.append(AgStepReply(step_id=step_id, rank=r, next_tokens=np.full(n, 7, np.int32),
+                                        status=2 if r == self.bad_status_rank else 0))
+        for r in eg_plans:
+            self.out.append(EgStepReply(step_id=step_id, rank=r))
+
+    def poll(self, timeout_s):
+        out, self.out = self.out, []
+        return out
+
+
+def test_coordinator_matches_spmd_driver_on_cpu_engine():
+    cfg = PRESETS["tiny-qwen3-moe"]
+    g = torch.Generator().manual_seed(0)
+    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (20, 33, 5)]
+    sp = SamplingParams(max_tokens=5, ignore_eos=True)
+    exp = SpmdDriver(AfdEngine(cfg, _rt(), AfdTopology(colocated=True), 0, "cpu", seed=0)).generate(prompts, sp)
+    eng = AfdEngine(cfg, _rt(), AfdTopology(colocated=True), 0, "cpu", seed=0)
+    got = {i: [] for i in range(len(prompts))}
+    coord = AfdCoordinator(cfg, _rt(async_pending_steps=1), AfdTopology(colocated=True), InProcTransport({0: eng}),
+                           num_pages=64, max_comm_tokens=eng.max_comm_tokens,
+                           on_tokens=lambda items: [got[u].extend(t) for u, t, _ in items])
+    for i, p in enumerate(prompts):
+        coord.add_request(i, p, sp)
+    coord.run_until_idle()
+    assert [got[i] for i in range(len(prompts))] == exp
+
+
+def test_overlap_window_dummy_lanes_and_completion():
+    cfg = PRESETS["tiny-qwen3-moe"]
+    topo = AfdTopology(attn_dp=2, mlp_ep=2)
+    fake = FakeWorkers()
+    done = []
+    coord = AfdCoordinator(cfg, _rt(async_pending_steps=3), topo, fake, num_pages=64,
+                           on_tokens=lambda items: done.extend(items))
+    coord.add_request(0, [1, 2, 3], SamplingParams(max_tokens=4, ignore_eos=True))   # only lane 0 gets work
+    coord.run_until_idle()
+    toks = [t for u, ts, _ in done for t in ts]
+    assert toks == [7, 7, 7, 7] and done[-1][2] is True
+    # every step went to all four ranks even though lane 1 had nothing to do
+    assert all(ag == [0, 1] and eg == [2, 3] for _, ag, eg in fake.sent)
+    # 1 prefill + 3 decode steps, no extra step planned past max_tokens
+    assert len(fake.sent) == 4
+    for l in coord.lanes:
+        l.check_integrity()
+        assert l.cache.free_pages == 63 and len(l.free_rows) == 8
+
+
+def test_eos_found_late_drops_tokens_planned_ahead():
+    cfg = PRESETS["tiny-qwen3-moe"]
+    from dataclasses import replace
+    cfg = replace(cfg, eos_token_ids=(7,))
+    fake = FakeWorkers()
+    done = []
+    coord = AfdCoordinator(cfg, _rt(async_pending_steps=3), AfdTopology(attn_dp=1, mlp_ep=1), fake, num_pages=64,
+                           on_tokens=lambda items: done.extend(items))
+    coord.add_request(0, [1, 2, 3], SamplingParams(max_tokens=16))
+    coord.run_until_idle()
+    assert [t for _, ts, _ in done for t in ts] == [7]      # EOS right away; later planned steps ignored
+    assert coord.lanes[0].cache.free_pages == 63
+
+
+def test_silent_worker_is_reported_not_waited_for_forever():
+    cfg = PRESETS["tiny-qwen3-moe"]
+    coord = AfdCoordinator(cfg, _rt(), AfdTopology(attn_dp=2, mlp_ep=2), FakeWorkers(drop_rank=1), num_pages=64,
+                           worker_timeout_s=0.3)
+    coord.add_request(0, [1, 2, 3], SamplingParams(max_tokens=2, ignore_eos=True))
+    with pytest.raises(CoordinatorError, match=r"no reply from ranks \[1\]"):
+        coord.run_until_idle()
+    assert "no reply" in coord.get_failure()
+
+
+@pytest.mark.parametrize("kw,msg", [(dict(bad_status_rank=0), "device status 2"), (dict(fail_rank=1), "worker 1 failed: boom")])
+def test_worker_error_surfaces(kw, msg):
+    cfg = PRESETS["tiny-qwen3-moe"]
+    coord = AfdCoordinator(cfg, _rt(), AfdTopology(attn_dp=2, mlp_ep=2), FakeWorkers(**kw), num_pages=64)
+    coord.add_request(0, [1, 2, 3], SamplingParams(max_tokens=2, ignore_eos=True))
+    with pytest.raises(CoordinatorError, match=msg):
+        coord.run_until_idle()
+    with pytest.raises(CoordinatorError):
+        coord.add_request(1, [1], SamplingParams())
+
+
+def test_admission_errors_and_stall():
+    cfg = PRESETS["tiny-qwen3-moe"]
+    coord = AfdCoordinator(cfg, _rt(num_pages=4), AfdTopology(attn_dp=1, mlp_ep=1), FakeWorkers(), num_pages=4)
+    with pytest.raises(AdmissionError):
+        coord.add_request(0, list(range(100)), SamplingParams(max_tokens=100))   # > max_seq_len
+    with pytest.raises(AdmissionError):
+        coord.add_request(1, list(range(40)), SamplingParams(max_tokens=40))     # more pages than the lane has
+
+
+def test_shutdown_is_idempotent():
+    class T(FakeWorkers):
+        stops = 0
+
+        def stop(self):
+            self.stops += 1
+    t = T()
+    coord = AfdCoordinator(PRESETS["tiny-qwen3-moe"], _rt(), AfdTopology(attn_dp=1, mlp_ep=1), t, num_pages=8)
+    coord.shutdown()
+    coord.shutdown()
+    assert t.stops == 1
