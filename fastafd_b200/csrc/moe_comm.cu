@@ -234,22 +234,27 @@ __device__ __forceinline__ void warp_topk(const float* s_logit, const float* bia
 }
 
 __global__ void __launch_bounds__(512) ag_route_dispatch_kernel(const RouteDispatchArgs a) {
-  extern __shared__ float rsm[];        // x (H floats) | logits (E floats) | red (32)
+  // shared: x as bf16 (H * 2 bytes, 16-byte aligned rows read as uint4: conflict-free) |
+  //         logits (E floats) | red (32 floats)
+  extern __shared__ __align__(16) uint8_t rsm_raw[];
   const DispatchArgs& d = a.d;
   const int H = d.H, t = blockIdx.x;
-  float* xs = rsm;
-  float* s_logit = rsm + H;
+  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(rsm_raw);
+  float* s_logit = reinterpret_cast<float*>(rsm_raw + static_cast<size_t>(H) * 2);
   float* red = s_logit + a.E;
   __shared__ int s_idx[32];
   __shared__ float s_w[32];
   __shared__ uint32_t s_mask;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
 
-  // 1. residual add + RMSNorm
+  // 1. residual add + RMSNorm (each thread keeps its 8 elements in registers; H <= 8 * 512)
+  float rv8[8];
   float ss = 0.f;
-  for (int i = threadIdx.x * 8; i < H; i += blockDim.x * 8) {
-    const uint4 xa = *reinterpret_cast<const uint4*>(a.attn_out + static_cast<size_t>(t) * H + i);
-    uint4 ra = *reinterpret_cast<const uint4*>(a.residual + static_cast<size_t>(t) * H + i);
+  const int i0 = threadIdx.x * 8;
+  const bool active = i0 < H;
+  if (active) {
+    const uint4 xa = *reinterpret_cast<const uint4*>(a.attn_out + static_cast<size_t>(t) * H + i0);
+    uint4 ra = *reinterpret_cast<const uint4*>(a.residual + static_cast<size_t>(t) * H + i0);
     const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&xa);
     __nv_bfloat162* r2 = reinterpret_cast<__nv_bfloat162*>(&ra);
 #pragma unroll
@@ -260,11 +265,11 @@ __global__ void __launch_bounds__(512) ag_route_dispatch_kernel(const RouteDispa
       rv.y += xv.y;
       r2[j] = __floats2bfloat162_rn(rv.x, rv.y);
       rv = __bfloat1622float2(r2[j]);
-      xs[i + 2 * j] = rv.x;
-      xs[i + 2 * j + 1] = rv.y;
+      rv8[2 * j] = rv.x;
+      rv8[2 * j + 1] = rv.y;
       ss += rv.x * rv.x + rv.y * rv.y;
     }
-    *reinterpret_cast<uint4*>(a.residual + static_cast<size_t>(t) * H + i) = ra;
+    *reinterpret_cast<uint4*>(a.residual + static_cast<size_t>(t) * H + i0) = ra;
   }
   ss = warp_sum(ss);
   if (lane == 0) red[warp] = ss;
@@ -272,9 +277,8 @@ __global__ void __launch_bounds__(512) ag_route_dispatch_kernel(const RouteDispa
   float tot = lane < nw ? red[lane] : 0.f;
   tot = warp_sum(tot);
   const float inv = rsqrtf(tot / H + a.eps);
-  __syncthreads();
-  for (int i = threadIdx.x * 8; i < H; i += blockDim.x * 8) {
-    const uint4 wa = *reinterpret_cast<const uint4*>(a.norm_w + i);
+  if (active) {
+    const uint4 wa = *reinterpret_cast<const uint4*>(a.norm_w + i0);
     const __nv_bfloat162* w2 = reinterpret_cast<const __nv_bfloat162*>(&wa);
     uint4 oa;
     __nv_bfloat162* o2 = reinterpret_cast<__nv_bfloat162*>(&oa);
@@ -285,34 +289,45 @@ __global__ void __launch_bounds__(512) ag_route_dispatch_kernel(const RouteDispa
         g.x += 1.f;
         g.y += 1.f;
       }
-      o2[j] = __floats2bfloat162_rn(xs[i + 2 * j] * inv * g.x, xs[i + 2 * j + 1] * inv * g.y);
-      const float2 back = __bfloat1622float2(o2[j]);    // the router sees the bf16-rounded x
-      xs[i + 2 * j] = back.x;
-      xs[i + 2 * j + 1] = back.y;
+      o2[j] = __floats2bfloat162_rn(rv8[2 * j] * inv * g.x, rv8[2 * j + 1] * inv * g.y);
     }
-    *reinterpret_cast<uint4*>(a.x_out + static_cast<size_t>(t) * H + i) = oa;
+    *reinterpret_cast<uint4*>(a.x_out + static_cast<size_t>(t) * H + i0) = oa;
+    *reinterpret_cast<uint4*>(xs + i0) = oa;          // the router sees the bf16-rounded x
   }
   __syncthreads();
 
-  // 2. router logits: one warp per expert, lanes split H
-  for (int e = warp; e < a.E; e += nw) {
+  // 2. router logits: one warp per expert, lanes split H. CTAs start at different experts so
+  //    that they do not all pull the same gate rows out of L2 at the same moment.
+  const int rot = (blockIdx.x * 5) % a.E;
+  for (int e0 = warp; e0 < a.E; e0 += nw) {
+    int e = e0 + rot;
+    if (e >= a.E) e -= a.E;
     float acc = 0.f;
     if (a.gate_fp32) {
       const float* g = static_cast<const float*>(a.gate_w) + static_cast<size_t>(e) * H;
-      for (int i = lane * 4; i < H; i += 128) {
-        const float4 gv = *reinterpret_cast<const float4*>(g + i);
-        acc += gv.x * xs[i] + gv.y * xs[i + 1] + gv.z * xs[i + 2] + gv.w * xs[i + 3];
+      for (int i = lane * 8; i < H; i += 256) {
+        const float4 g0 = *reinterpret_cast<const float4*>(g + i);
+        const float4 g1 = *reinterpret_cast<const float4*>(g + i + 4);
+        const uint4 xa = *reinterpret_cast<const uint4*>(xs + i);
+        const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&xa);
+        const float2 a0 = __bfloat1622float2(x2[0]), a1 = __bfloat1622float2(x2[1]);
+        const float2 a2 = __bfloat1622float2(x2[2]), a3 = __bfloat1622float2(x2[3]);
+        acc += g0.x * a0.x + g0.y * a0.y + g0.z * a1.x + g0.w * a1.y + g1.x * a2.x + g1.y * a2.y + g1.z * a3.x + g1.w * a3.y;
       }
     } else {
       const __nv_bfloat16* g = static_cast<const __nv_bfloat16*>(a.gate_w) + static_cast<size_t>(e) * H;
+#pragma unroll 4
       for (int i = lane * 8; i < H; i += 256) {
         const uint4 ga = *reinterpret_cast<const uint4*>(g + i);
+        const uint4 xa = *reinterpret_cast<const uint4*>(xs + i);
         const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&ga);
+        const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&xa);
 #pragma unroll
         for (int j = 0; j < 4; ++j) {
           const float2 gv = __bfloat1622float2(g2[j]);
-          acc = fmaf(gv.x, xs[i + 2 * j], acc);
-          acc = fmaf(gv.y, xs[i + 2 * j + 1], acc);
+          const float2 xv = __bfloat1622float2(x2[j]);
+          acc = fmaf(gv.x, xv.x, acc);
+          acc = fmaf(gv.y, xv.y, acc);
         }
       }
     }
@@ -350,10 +365,7 @@ __global__ void __launch_bounds__(512) ag_route_dispatch_kernel(const RouteDispa
   const size_t dst_row = static_cast<size_t>(d.src_rank) * d.recv_tokens + t;
   if (!d.fp8) {
     for (int i = threadIdx.x * 8; i < H; i += blockDim.x * 8) {
-      uint4 v;
-      __nv_bfloat162* v2 = reinterpret_cast<__nv_bfloat162*>(&v);
-#pragma unroll
-      for (int j = 0; j < 4; ++j) v2[j] = __floats2bfloat162_rn(xs[i + 2 * j], xs[i + 2 * j + 1]);
+      const uint4 v = *reinterpret_cast<const uint4*>(xs + i);
       for (int g = 0; g < d.num_eg; ++g) {
         if (mask & (1u << g)) {
           *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(d.peer_recv_x[g]) + dst_row * H + i) = v;
@@ -363,7 +375,10 @@ __global__ void __launch_bounds__(512) ag_route_dispatch_kernel(const RouteDispa
   } else {
     const int groups = H / 128;
     for (int g128 = warp; g128 < groups; g128 += nw) {
-      const float4 f = *reinterpret_cast<const float4*>(xs + g128 * 128 + lane * 4);
+      const uint2 fr = *reinterpret_cast<const uint2*>(xs + g128 * 128 + lane * 4);
+      const __nv_bfloat162* f2 = reinterpret_cast<const __nv_bfloat162*>(&fr);
+      const float2 fa = __bfloat1622float2(f2[0]), fb = __bfloat1622float2(f2[1]);
+      const float4 f = make_float4(fa.x, fa.y, fb.x, fb.y);
       float amax = fmaxf(fmaxf(fabsf(f.x), fabsf(f.y)), fmaxf(fabsf(f.z), fabsf(f.w)));
       amax = warp_max(amax);
       const float scale = fmaxf(amax, 1e-10f) / 448.f;
@@ -755,7 +770,7 @@ struct AfdRouteDispatchDesc {
 extern "C" int afd_ag_route_dispatch(const AfdRouteDispatchDesc* r, void* stream) {
   const AfdDispatchDesc* d = &r->d;
   if (d->T == 0) return -1;
-  if (d->num_eg > kMaxRanks || d->H % 256 != 0 || d->K > 32 || d->T > d->recv_tokens || r->E > 512) return -2;
+  if (d->num_eg > kMaxRanks || d->H % 256 != 0 || d->H > 4096 || d->K > 32 || d->T > d->recv_tokens || r->E > 512) return -2;
   RouteDispatchArgs a{};
   a.attn_out = static_cast<const __nv_bfloat16*>(r->attn_out);
   a.residual = static_cast<__nv_bfloat16*>(r->residual);
@@ -780,7 +795,7 @@ extern "C" int afd_ag_route_dispatch(const AfdRouteDispatchDesc* r, void* stream
   da.done_counter = static_cast<unsigned int*>(d->done_counter);
   da.status = static_cast<int*>(d->status);
   da.trace = static_cast<unsigned long long*>(d->trace);
-  const size_t smem = (static_cast<size_t>(d->H) + r->E + 32) * sizeof(float);
+  const size_t smem = static_cast<size_t>(d->H) * 2 + (r->E + 32) * sizeof(float);
   ag_route_dispatch_kernel<<<d->T, 512, smem, static_cast<cudaStream_t>(stream)>>>(a);
   AFD_CHECK_LAUNCH();
   return 0;

@@ -62,14 +62,20 @@ class AfdEngine:
         num_ag = 1 if self.colocated else topo.attn_world
 
         stage = None
-        if self.is_expert and cfg.is_moe:
+        import os as _os0
+        if self.is_expert and cfg.is_moe and _os0.environ.get("FASTAFD_DEBUG_NULL_MOE") != "1":
             ep_rank = 0 if self.colocated else topo.expert_index(rank)
             stage = ExpertStage(cfg, self.device, self.dtype, ep_rank, num_eg).init_random(seed, fast=fast_init)
         self.expert_stage = stage
 
         client = server = None
         eg_status = None
-        if cfg.is_moe:
+        import os as _os
+        if _os.environ.get("FASTAFD_DEBUG_NULL_MOE") == "1" and cfg.is_moe:
+            from .worker.moe_client import NullMoeClient
+
+            client, stage = NullMoeClient(), None
+        elif cfg.is_moe:
             if cuda:
                 from .moe.afd_moe import AgMoeEndpoint, EgMoeEndpoint, MoeCommConfig, ag_layout, eg_layout
                 from .parallel.fabric import Fabric

@@ -74,6 +74,18 @@ class LocalMoeClient(MoeClient):
         return _finish_combine(y, residual, norm_w, eps, offset1, normed_out)
 
 
+class NullMoeClient(MoeClient):
+    """No experts at all: the MoE output is taken to be zero. Only for measuring the
+    attention side in isolation."""
+
+    def dispatch(self, lane, layer, x, topk_idx, topk_w):
+        pass
+
+    def combine(self, lane, layer, T, topk_w, topk_idx, residual, norm_w, eps, *, extra=None, scale=1.0,
+                offset1=False, normed_out=None):
+        return ops.rmsnorm(residual, norm_w, eps, offset1, out=normed_out)
+
+
 class GlooMoeClient(MoeClient):
     """CPU multi-process: send (x, idx) to every expert rank, receive per-(k, token) rows."""
 
@@ -120,7 +132,7 @@ class FabricMoeClient(MoeClient):
             self.colocated.serve(lane, layer, x.shape[0])
 
     def can_fuse_route(self, T, num_experts, hidden):
-        return T <= 256 and num_experts <= 512 and hidden % 256 == 0
+        return T <= 256 and num_experts <= 512 and hidden % 256 == 0 and hidden <= 4096
 
     def route_dispatch(self, lane, layer, attn_out, residual, norm_w, gate_w, gate_bias, x_out, topk_idx, topk_w, *,
                        scoring, renorm, eps, offset1=False):
