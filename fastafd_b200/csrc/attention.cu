@@ -72,14 +72,20 @@ __device__ __forceinline__ uint32_t tile_off(int row, int chunk) {
 template <int D>
 struct AttnCfg {
   static constexpr int TOK = 16;                       // KV tokens per warp tile
-  static constexpr int STAGES = D <= 128 ? 3 : 2;      // cp.async ring depth per warp
+  static constexpr int STAGES = 2;                     // cp.async ring depth per warp
   static constexpr int TILE_BYTES = TOK * D * 2;       // one of K / V
   static constexpr int WARP_BYTES = STAGES * 2 * TILE_BYTES;
   static constexpr int MERGE_BYTES = (16 * D + 32) * 4;
   static constexpr int WARP_REGION = WARP_BYTES > MERGE_BYTES ? WARP_BYTES : MERGE_BYTES;
   static constexpr int SMEM = 16 * D * 2 + 4 * WARP_REGION;
-  static constexpr int CTAS_PER_SM = (220 * 1024) / SMEM >= 2 ? 2 : 1;
+  static constexpr int CTAS_PER_SM = (222 * 1024) / (SMEM + 1024) >= 3 ? 3 : ((222 * 1024) / (SMEM + 1024) >= 2 ? 2 : 1);
 };
+
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 __device__ __forceinline__ uint32_t movmatrix_trans(uint32_t x) {
   uint32_t y;
@@ -139,56 +145,61 @@ __global__ void __launch_bounds__(128, AttnCfg<D>::CTAS_PER_SM) decode_attn_kern
   const int* pt = a.page_table + static_cast<size_t>(b) * a.max_pages;
   const uint32_t ps_mask = static_cast<uint32_t>(a.page_size - 1);
 
+  // Per-lane constants of the load path. A row of K plus the same row of V is PER_ROW
+  // 16-byte chunks; with PER_ROW <= 32 a warp issues ROWS_PER_IT whole rows per instruction.
+  constexpr int PER_ROW = 2 * CH;
+  constexpr int ROWS_PER_IT = PER_ROW <= 32 ? 32 / PER_ROW : 1;
+  const int ld_rsub = PER_ROW <= 32 ? lane / PER_ROW : 0;
+  const int ld_c2 = PER_ROW <= 32 ? lane % PER_ROW : lane;
+  const bool ld_is_v = PER_ROW <= 32 ? (ld_c2 >= CH) : false;
+  const int ld_c = ld_is_v ? ld_c2 - CH : ld_c2;
+  const size_t row_stride_bytes = static_cast<size_t>(a.Hkv) * D * 2;
+  const char* ld_gbase = reinterpret_cast<const char*>(ld_is_v ? a.v_cache : a.k_cache) +
+                         (static_cast<size_t>(kvh) * D + ld_c * 8) * 2;
+  const uint32_t ld_sbase = smem_u32(my) + (ld_is_v ? TILE_BYTES : 0);
+
   // One tile = 16 rows of K and of V. Lane r (< 16) resolves row r's cache slot once; the
   // warp then issues whole rows, one 16-byte chunk per lane.
   auto load_tile = [&](int tile, int stage) {
-    uint8_t* sk = my + stage * 2 * TILE_BYTES;
-    uint8_t* sv = sk + TILE_BYTES;
     const int t0 = kv_begin + tile * TOK;
-    long my_slot = -1;
+    int my_slot = -1;
     if (lane < TOK) {
       const int t = t0 + lane;
       if (t < kv_end) {
         const int page = pt[t >> a.page_shift];
-        my_slot = static_cast<long>(page) * a.page_size + (t & ps_mask);
-        if (my_slot < 0 || my_slot >= a.cache_slots) {
-          set_status(a.status, kStatusBadExtent);
-          my_slot = -1;
-        }
+        const long sl = static_cast<long>(page) * a.page_size + (t & ps_mask);
+        if (sl < 0 || sl >= a.cache_slots) set_status(a.status, kStatusBadExtent);
+        else my_slot = static_cast<int>(sl);
       }
     }
-    constexpr int PER_ROW = 2 * CH;                       // chunks of K and V in one row
+    const uint32_t sstage = ld_sbase + stage * 2 * TILE_BYTES;
     if constexpr (PER_ROW <= 32) {
-      constexpr int ROWS_PER_IT = 32 / PER_ROW;
-      const int rsub = lane / PER_ROW, c2 = lane % PER_ROW;
-      const bool is_v = c2 >= CH;
-      const int c = is_v ? c2 - CH : c2;
 #pragma unroll
       for (int r0 = 0; r0 < TOK; r0 += ROWS_PER_IT) {
-        const int r = r0 + rsub;
-        const long slot = __shfl_sync(0xffffffffu, my_slot, r);
-        uint8_t* dst = (is_v ? sv : sk) + tile_off<D>(r, c);
+        const int r = r0 + ld_rsub;
+        const int slot = __shfl_sync(0xffffffffu, my_slot, r);
+        const uint32_t dst = sstage + tile_off<D>(r, ld_c);
         if (slot >= 0) {
-          const size_t off = (static_cast<size_t>(slot) * a.Hkv + kvh) * D + c * 8;
-          cp_async16(dst, (is_v ? a.v_cache : a.k_cache) + off);
+          asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst),
+                       "l"(ld_gbase + static_cast<size_t>(slot) * row_stride_bytes) : "memory");
         } else {
-          *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
+          asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(dst), "r"(0) : "memory");
         }
       }
     } else {
 #pragma unroll 4
       for (int r = 0; r < TOK; ++r) {
-        const long slot = __shfl_sync(0xffffffffu, my_slot, r);
-#pragma unroll
-        for (int c = lane; c < CH; c += 32) {
-          if (slot >= 0) {
-            const size_t off = (static_cast<size_t>(slot) * a.Hkv + kvh) * D + c * 8;
-            cp_async16(sk + tile_off<D>(r, c), a.k_cache + off);
-            cp_async16(sv + tile_off<D>(r, c), a.v_cache + off);
-          } else {
-            *reinterpret_cast<uint4*>(sk + tile_off<D>(r, c)) = make_uint4(0, 0, 0, 0);
-            *reinterpret_cast<uint4*>(sv + tile_off<D>(r, c)) = make_uint4(0, 0, 0, 0);
-          }
+        const int slot = __shfl_sync(0xffffffffu, my_slot, r);
+        const uint32_t dk = sstage + tile_off<D>(r, ld_c);
+        if (slot >= 0) {
+          const char* g = ld_gbase + static_cast<size_t>(slot) * row_stride_bytes;
+          asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dk), "l"(g) : "memory");
+          asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dk + TILE_BYTES),
+                       "l"(g + (reinterpret_cast<const char*>(a.v_cache) - reinterpret_cast<const char*>(a.k_cache)))
+                       : "memory");
+        } else {
+          asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(dk), "r"(0) : "memory");
+          asm volatile("st.shared.v4.u32 [%0], {%1, %1, %1, %1};" ::"r"(dk + TILE_BYTES), "r"(0) : "memory");
         }
       }
     }
@@ -295,23 +306,25 @@ __global__ void __launch_bounds__(128, AttnCfg<D>::CTAS_PER_SM) decode_attn_kern
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
         const float m_new = fmaxf(m_run[n][c], mx);
-        corr[c] = (m_new == -INFINITY) ? 1.f : exp2f(m_run[n][c] - m_new);
+        corr[c] = (m_new == -INFINITY) ? 1.f : fast_exp2(m_run[n][c] - m_new);
         m_run[n][c] = m_new;
         float lsum = 0.f;
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          const float p = (m_new == -INFINITY) ? 0.f : exp2f(st[n][c + 2 * h] - m_new);
+          const float p = (m_new == -INFINITY) ? 0.f : fast_exp2(st[n][c + 2 * h] - m_new);
           st[n][c + 2 * h] = p;
           lsum += p;
         }
         l_run[n][c] = l_run[n][c] * corr[c] + lsum;
       }
+      if (__any_sync(0xffffffffu, corr[0] != 1.f || corr[1] != 1.f)) {
 #pragma unroll
-      for (int i = 0; i < D / 16; ++i) {
-        ot[i][n][0] *= corr[0];
-        ot[i][n][1] *= corr[1];
-        ot[i][n][2] *= corr[0];
-        ot[i][n][3] *= corr[1];
+        for (int i = 0; i < D / 16; ++i) {
+          ot[i][n][0] *= corr[0];
+          ot[i][n][1] *= corr[1];
+          ot[i][n][2] *= corr[0];
+          ot[i][n][3] *= corr[1];
+        }
       }
       // P^T as the B operand: transpose the two 8x8 blocks (tokens 0-7, 8-15) in registers
       pb[n][0] = movmatrix_trans(pack_bf16(st[n][0], st[n][1]));
@@ -508,7 +521,8 @@ extern "C" int afd_decode_attention_strided(const void* q, long q_stride, const 
   a.part_o = static_cast<float*>(workspace);
   a.part_lse = a.part_o ? a.part_o + tiles * 16 * D : nullptr;
   a.part_count = a.part_o ? reinterpret_cast<unsigned int*>(a.part_lse + tiles * 16) : nullptr;
-  if ((page_size & (page_size - 1)) != 0) return -4;     // page sizes are powers of two
+  if ((page_size & (page_size - 1)) != 0) return -4;
+  if (cache_slots > 0x7fffffffL) return -6;     // page sizes are powers of two
   a.page_shift = 0;
   while ((1 << a.page_shift) < page_size) ++a.page_shift;
   cudaStream_t st = static_cast<cudaStream_t>(stream);

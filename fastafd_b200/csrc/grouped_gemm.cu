@@ -431,7 +431,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
       if (prev == gridDim.x - 1) {
         __threadfence_system();
         const uint32_t e = *args.epoch;
-        for (int p = 0; p < args.num_peers; ++p) st_release_sys(args.peer_flag[p], e);
+        for (int p = 0; p < args.num_peers; ++p) st_relaxed_sys(args.peer_flag[p], e);   // ordered by the fence above
         trace_stamp(args.trace, e, 3);
         *args.epoch = e + 1;
         *args.done_counter = 0;

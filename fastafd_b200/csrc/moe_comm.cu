@@ -120,7 +120,7 @@ __global__ void dispatch_push_kernel(const DispatchArgs a) {
     if (prev == gridDim.x - 1) {
       __threadfence_system();
       const uint32_t e = *a.epoch;
-      for (int eg = 0; eg < a.num_eg; ++eg) st_release_sys(a.peer_flag[eg], e);
+      for (int eg = 0; eg < a.num_eg; ++eg) st_relaxed_sys(a.peer_flag[eg], e);   // ordered by the fence above
       trace_stamp(a.trace, e, 0);
       *a.epoch = e + 1;
       *a.done_counter = 0;
@@ -233,7 +233,7 @@ __device__ __forceinline__ void warp_topk(const float* s_logit, const float* bia
   }
 }
 
-__global__ void __launch_bounds__(512) ag_route_dispatch_kernel(const RouteDispatchArgs a) {
+__global__ void __launch_bounds__(1024) ag_route_dispatch_kernel(const RouteDispatchArgs a) {
   // shared: x as bf16 (H * 2 bytes, 16-byte aligned rows read as uint4: conflict-free) |
   //         logits (E floats) | red (32 floats)
   extern __shared__ __align__(16) uint8_t rsm_raw[];
@@ -247,7 +247,19 @@ __global__ void __launch_bounds__(512) ag_route_dispatch_kernel(const RouteDispa
   __shared__ uint32_t s_mask;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
 
-  // 1. residual add + RMSNorm (each thread keeps its 8 elements in registers; H <= 8 * 512)
+  // 0. pull the gate matrix towards L2 while the norm runs: it was last touched a whole
+  //    decode step ago, and the logits loop below is a chain of dependent loads.
+  {
+    const size_t gate_bytes = static_cast<size_t>(a.E) * H * (a.gate_fp32 ? 4 : 2);
+    const char* gp = static_cast<const char*>(a.gate_w);
+    const size_t per_cta = (gate_bytes / gridDim.x + 127) / 128 * 128;
+    const size_t lo = per_cta * blockIdx.x, hi = min(gate_bytes, lo + per_cta);
+    for (size_t off = lo + static_cast<size_t>(threadIdx.x) * 128; off < hi; off += static_cast<size_t>(blockDim.x) * 128) {
+      asm volatile("prefetch.global.L2 [%0];" ::"l"(gp + off));
+    }
+  }
+
+  // 1. residual add + RMSNorm (each thread keeps its 8 elements in registers; H <= 8 * 1024)
   float rv8[8];
   float ss = 0.f;
   const int i0 = threadIdx.x * 8;
@@ -299,12 +311,13 @@ __global__ void __launch_bounds__(512) ag_route_dispatch_kernel(const RouteDispa
   // 2. router logits: one warp per expert, lanes split H. CTAs start at different experts so
   //    that they do not all pull the same gate rows out of L2 at the same moment.
   const int rot = (blockIdx.x * 5) % a.E;
-  for (int e0 = warp; e0 < a.E; e0 += nw) {
-    int e = e0 + rot;
-    if (e >= a.E) e -= a.E;
-    float acc = 0.f;
-    if (a.gate_fp32) {
+  if (a.gate_fp32) {
+    for (int e0 = warp; e0 < a.E; e0 += nw) {
+      int e = e0 + rot;
+      if (e >= a.E) e -= a.E;
+      float acc = 0.f;
       const float* g = static_cast<const float*>(a.gate_w) + static_cast<size_t>(e) * H;
+#pragma unroll 4
       for (int i = lane * 8; i < H; i += 256) {
         const float4 g0 = *reinterpret_cast<const float4*>(g + i);
         const float4 g1 = *reinterpret_cast<const float4*>(g + i + 4);
@@ -314,25 +327,58 @@ __global__ void __launch_bounds__(512) ag_route_dispatch_kernel(const RouteDispa
         const float2 a2 = __bfloat1622float2(x2[2]), a3 = __bfloat1622float2(x2[3]);
         acc += g0.x * a0.x + g0.y * a0.y + g0.z * a1.x + g0.w * a1.y + g1.x * a2.x + g1.y * a2.y + g1.z * a3.x + g1.w * a3.y;
       }
-    } else {
-      const __nv_bfloat16* g = static_cast<const __nv_bfloat16*>(a.gate_w) + static_cast<size_t>(e) * H;
-#pragma unroll 4
-      for (int i = lane * 8; i < H; i += 256) {
-        const uint4 ga = *reinterpret_cast<const uint4*>(g + i);
-        const uint4 xa = *reinterpret_cast<const uint4*>(xs + i);
-        const __nv_bfloat162* g2 = reinterpret_cast<const __nv_bfloat162*>(&ga);
-        const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&xa);
+      acc = warp_sum(acc);
+      if (lane == 0) s_logit[e] = acc;
+    }
+  } else {
+    // two experts per pass, every load of both rows issued before the first use
+    const int iters = H / 256;            // <= 16
+    for (int e0 = warp; e0 < a.E; e0 += 2 * nw) {
+      int ea = e0 + rot, eb = e0 + nw + rot;
+      if (ea >= a.E) ea -= a.E;
+      const bool has_b = e0 + nw < a.E;
+      if (eb >= a.E) eb -= a.E;
+      if (!has_b) eb = ea;
+      const __nv_bfloat16* ga = static_cast<const __nv_bfloat16*>(a.gate_w) + static_cast<size_t>(ea) * H;
+      const __nv_bfloat16* gb = static_cast<const __nv_bfloat16*>(a.gate_w) + static_cast<size_t>(eb) * H;
+      float acc_a = 0.f, acc_b = 0.f;
+#pragma unroll 1
+      for (int base = 0; base < iters; base += 4) {
+        uint4 ba[4], bb[4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const float2 gv = __bfloat1622float2(g2[j]);
-          const float2 xv = __bfloat1622float2(x2[j]);
-          acc = fmaf(gv.x, xv.x, acc);
-          acc = fmaf(gv.y, xv.y, acc);
+        for (int it = 0; it < 4; ++it) {
+          if (base + it < iters) {
+            ba[it] = *reinterpret_cast<const uint4*>(ga + (base + it) * 256 + lane * 8);
+            bb[it] = *reinterpret_cast<const uint4*>(gb + (base + it) * 256 + lane * 8);
+          }
+        }
+#pragma unroll
+        for (int it = 0; it < 4; ++it) {
+          if (base + it < iters) {
+            const uint4 xa = *reinterpret_cast<const uint4*>(xs + (base + it) * 256 + lane * 8);
+            const __nv_bfloat162* x2 = reinterpret_cast<const __nv_bfloat162*>(&xa);
+            const __nv_bfloat162* a2 = reinterpret_cast<const __nv_bfloat162*>(&ba[it]);
+            const __nv_bfloat162* b2 = reinterpret_cast<const __nv_bfloat162*>(&bb[it]);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              const float2 xv = __bfloat1622float2(x2[j]);
+              const float2 av = __bfloat1622float2(a2[j]);
+              const float2 bv = __bfloat1622float2(b2[j]);
+              acc_a = fmaf(av.x, xv.x, acc_a);
+              acc_a = fmaf(av.y, xv.y, acc_a);
+              acc_b = fmaf(bv.x, xv.x, acc_b);
+              acc_b = fmaf(bv.y, xv.y, acc_b);
+            }
+          }
         }
       }
+      acc_a = warp_sum(acc_a);
+      acc_b = warp_sum(acc_b);
+      if (lane == 0) {
+        s_logit[ea] = acc_a;
+        if (has_b) s_logit[eb] = acc_b;
+      }
     }
-    acc = warp_sum(acc);
-    if (lane == 0) s_logit[e] = acc;
   }
   __syncthreads();
 
@@ -403,7 +449,7 @@ __global__ void __launch_bounds__(512) ag_route_dispatch_kernel(const RouteDispa
     if (prev == gridDim.x - 1) {
       __threadfence_system();
       const uint32_t e = *d.epoch;
-      for (int g = 0; g < d.num_eg; ++g) st_release_sys(d.peer_flag[g], e);
+      for (int g = 0; g < d.num_eg; ++g) st_relaxed_sys(d.peer_flag[g], e);   // ordered by the fence above
       trace_stamp(d.trace, e, 0);
       *d.epoch = e + 1;
       *d.done_counter = 0;
@@ -585,6 +631,184 @@ __global__ void eg_gather_kernel(const GatherArgs a) {
         a.pool_scale[static_cast<size_t>(row) * a.scale_per_row + v] =
             a.recv_scale[(static_cast<size_t>(src) * a.recv_tokens + tok) * a.scale_per_row + v];
       }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------
+// Decode-sized grouping + gather in ONE launch (no single-CTA stage, no second launch):
+// CTA j owns token tile j. Every CTA waits for the attention ranks' flags itself, rebuilds
+// the per-expert histogram from the received top-k ids (a few KB), finds the expert and
+// row range of its tile, selects its rows in entry order (deterministic: all CTAs agree
+// without talking to each other), writes tile_info[j] / row_meta and copies the rows into
+// the expert-grouped pool. Used when A*T*K <= kFusedGroupMaxEntries.
+// ---------------------------------------------------------------------------------------
+constexpr int kFusedGroupMaxEntries = 8192;
+constexpr int kFusedGroupThreads = 256;
+
+struct FusedGroupArgs {
+  GroupArgs g;
+  const void* recv_x;
+  const float* recv_scale;
+  void* pool_x;
+  float* pool_scale;
+  int row_bytes, scale_per_row;
+  unsigned int* done_counter;
+};
+
+__global__ void __launch_bounds__(kFusedGroupThreads) eg_group_gather_fused_kernel(const FusedGroupArgs fa) {
+  const GroupArgs& a = fa.g;
+  extern __shared__ int sm[];
+  int* cnt = sm;                              // [experts_local]
+  int* tstart = sm + a.experts_local;         // [experts_local + 1] first tile of each expert
+  __shared__ uint32_t s_epoch;
+  __shared__ int s_e, s_first, s_total_tiles, s_routed;
+  __shared__ int s_wsum[kFusedGroupThreads / 32];
+  __shared__ uint32_t s_meta[128];            // rows of this tile (block_tok <= 128)
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if (tid == 0) {
+    s_epoch = *a.epoch;
+    s_e = -1;
+    if (blockIdx.x == 0) trace_stamp(a.trace, s_epoch, 0);
+  }
+  for (int e = tid; e < a.experts_local; e += blockDim.x) cnt[e] = 0;
+  __syncthreads();
+  if (tid < a.A) wait_flag_ge(a.n2m_flag + tid, s_epoch, a.timeout_ns, a.status);
+  __syncthreads();
+  if (tid == 0 && blockIdx.x == 0) trace_stamp(a.trace, s_epoch, 1);
+
+  const int per_src = a.T * a.K;
+  const int total = a.A * per_src;
+  // histogram over all entries
+  for (int i = tid; i < total; i += blockDim.x) {
+    const int src = i / per_src, r = i - src * per_src;
+    const int e = a.recv_idx[static_cast<size_t>(src) * a.recv_tokens * a.K + r] - a.expert_base;
+    if (e >= 0 && e < a.experts_local) atomicAdd(&cnt[e], 1);
+  }
+  __syncthreads();
+  // tile prefix over experts: warp 0, each lane a contiguous slice of experts
+  if (warp == 0) {
+    const int per = (a.experts_local + 31) / 32;
+    const int lo = min(lane * per, a.experts_local), hi = min(lo + per, a.experts_local);
+    int t = 0, c = 0;
+    for (int e = lo; e < hi; ++e) {
+      t += (cnt[e] + a.block_tok - 1) / a.block_tok;
+      c += cnt[e];
+    }
+    int incl = t, cincl = c;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      const int vc = __shfl_up_sync(0xffffffffu, cincl, o);
+      if (lane >= o) {
+        incl += v;
+        cincl += vc;
+      }
+    }
+    int run = incl - t;
+    for (int e = lo; e < hi; ++e) {
+      tstart[e] = run;
+      run += (cnt[e] + a.block_tok - 1) / a.block_tok;
+    }
+    if (lane == 31) {
+      tstart[a.experts_local] = incl;
+      s_total_tiles = incl;
+      s_routed = cincl;
+    }
+  }
+  __syncthreads();
+  const int my_tile = blockIdx.x;
+  for (int e = tid; e < a.experts_local; e += blockDim.x) {
+    if (tstart[e] <= my_tile && my_tile < tstart[e + 1]) {
+      s_e = e;
+      s_first = my_tile - tstart[e];
+    }
+  }
+  __syncthreads();
+  const int e_mine = s_e;
+  if (e_mine >= 0) {
+    const int want_lo = s_first * a.block_tok;
+    const int valid = min(a.block_tok, cnt[e_mine] - want_lo);
+    const int row0 = my_tile * a.block_tok;
+    // ordered rank of every matching entry: contiguous chunk per thread + block scan
+    const int per = (total + blockDim.x - 1) / blockDim.x;
+    const int lo = min(tid * per, total), hi = min(lo + per, total);
+    int mine = 0;
+    for (int i = lo; i < hi; ++i) {
+      const int src = i / per_src, r = i - src * per_src;
+      mine += (a.recv_idx[static_cast<size_t>(src) * a.recv_tokens * a.K + r] - a.expert_base) == e_mine;
+    }
+    int incl = mine;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    if (lane == 31) s_wsum[warp] = incl;
+    __syncthreads();
+    int base = incl - mine;
+    for (int w = 0; w < warp; ++w) base += s_wsum[w];
+    for (int i = lo; i < hi; ++i) {
+      const int src = i / per_src, r = i - src * per_src;
+      if ((a.recv_idx[static_cast<size_t>(src) * a.recv_tokens * a.K + r] - a.expert_base) == e_mine) {
+        const int slot = base - want_lo;
+        if (slot >= 0 && slot < valid) {
+          const int t = r / a.K, k = r - t * a.K;
+          s_meta[slot] = (static_cast<uint32_t>(src) << 24) | (static_cast<uint32_t>(k) << 16) | static_cast<uint32_t>(t);
+        }
+        ++base;
+      }
+    }
+    __syncthreads();
+    if (row0 + a.block_tok <= a.pool_rows && my_tile < a.max_tok_tiles) {
+      if (tid == 0) a.tile_info[my_tile] = make_int4(e_mine, row0, valid, 0);
+      for (int i = tid; i < valid; i += blockDim.x) a.row_meta[row0 + i] = s_meta[i];
+      const int vec_per_row = fa.row_bytes / 16;
+      for (int idx = tid; idx < valid * vec_per_row; idx += blockDim.x) {
+        const int r = idx / vec_per_row, v = idx - r * vec_per_row;
+        const uint32_t meta = s_meta[r];
+        const int src = meta >> 24, tok = meta & 0xffff;
+        const uint4* sp = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(fa.recv_x) +
+                                                         (static_cast<size_t>(src) * a.recv_tokens + tok) * fa.row_bytes);
+        reinterpret_cast<uint4*>(static_cast<uint8_t*>(fa.pool_x) + static_cast<size_t>(row0 + r) * fa.row_bytes)[v] = sp[v];
+      }
+      if (fa.recv_scale != nullptr) {
+        for (int idx = tid; idx < valid * fa.scale_per_row; idx += blockDim.x) {
+          const int r = idx / fa.scale_per_row, v = idx - r * fa.scale_per_row;
+          const uint32_t meta = s_meta[r];
+          const int src = meta >> 24, tok = meta & 0xffff;
+          fa.pool_scale[static_cast<size_t>(row0 + r) * fa.scale_per_row + v] =
+              fa.recv_scale[(static_cast<size_t>(src) * a.recv_tokens + tok) * fa.scale_per_row + v];
+        }
+      }
+    } else {
+      set_status(a.status, kStatusCapacity);
+    }
+  }
+  if (blockIdx.x == 0) {
+    for (int e = tid; e < a.experts_local; e += blockDim.x) {
+      if (a.expert_counts) a.expert_counts[e] = cnt[e];
+    }
+    if (tid == 0) {
+      int tiles = s_total_tiles;
+      if (tiles > a.max_tok_tiles || tiles > static_cast<int>(gridDim.x) || tiles * a.block_tok > a.pool_rows) {
+        set_status(a.status, kStatusCapacity);
+        tiles = min(min(tiles, a.max_tok_tiles), static_cast<int>(gridDim.x));
+      }
+      a.counters[0] = tiles;
+      a.counters[1] = tiles * a.block_tok;
+      a.counters[2] = s_routed;
+    }
+  }
+  __syncthreads();
+  if (tid == 0) {
+    __threadfence();
+    const unsigned int prev = atomicAdd(fa.done_counter, 1u);
+    if (prev == gridDim.x - 1) {
+      trace_stamp(a.trace, s_epoch, 2);
+      *a.epoch = s_epoch + 1;
+      *fa.done_counter = 0;
+      __threadfence();
     }
   }
 }
@@ -796,7 +1020,7 @@ extern "C" int afd_ag_route_dispatch(const AfdRouteDispatchDesc* r, void* stream
   da.status = static_cast<int*>(d->status);
   da.trace = static_cast<unsigned long long*>(d->trace);
   const size_t smem = static_cast<size_t>(d->H) * 2 + (r->E + 32) * sizeof(float);
-  ag_route_dispatch_kernel<<<d->T, 512, smem, static_cast<cudaStream_t>(stream)>>>(a);
+  ag_route_dispatch_kernel<<<d->T, 1024, smem, static_cast<cudaStream_t>(stream)>>>(a);
   AFD_CHECK_LAUNCH();
   return 0;
 }
@@ -811,6 +1035,7 @@ struct AfdGroupDesc {
   const void* recv_x; const void* recv_scale; void* pool_x; void* pool_scale;
   int row_bytes, scale_per_row;
   void* trace;
+  void* done_counter;   // device word (0) for the fused one-launch path; null = two-launch path
 };
 
 extern "C" int afd_eg_group_gather(const AfdGroupDesc* d, void* stream) {
@@ -831,6 +1056,21 @@ extern "C" int afd_eg_group_gather(const AfdGroupDesc* d, void* stream) {
   g.timeout_ns = d->timeout_ns;
   g.status = static_cast<int*>(d->status);
   g.trace = static_cast<unsigned long long*>(d->trace);
+  if (static_cast<long>(d->A) * d->T * d->K <= kFusedGroupMaxEntries && d->block_tok <= 128 && d->done_counter != nullptr) {
+    FusedGroupArgs fa{};
+    fa.g = g;
+    fa.recv_x = d->recv_x; fa.recv_scale = static_cast<const float*>(d->recv_scale);
+    fa.pool_x = d->pool_x; fa.pool_scale = static_cast<float*>(d->pool_scale);
+    fa.row_bytes = d->row_bytes; fa.scale_per_row = d->scale_per_row;
+    fa.done_counter = static_cast<unsigned int*>(d->done_counter);
+    // every possible tile gets a CTA: at most ceil(entries / block_tok) + experts_local tiles
+    const long entries = static_cast<long>(d->A) * d->T * d->K;
+    int grid = static_cast<int>((entries + d->block_tok - 1) / d->block_tok) + d->experts_local;
+    if (grid > d->max_tok_tiles) grid = d->max_tok_tiles;
+    eg_group_gather_fused_kernel<<<grid, kFusedGroupThreads, (2 * d->experts_local + 1) * sizeof(int), st>>>(fa);
+    AFD_CHECK_LAUNCH();
+    return 0;
+  }
   eg_group_kernel<<<1, 1024, 3 * d->experts_local * sizeof(int), st>>>(g);
   AFD_CHECK_LAUNCH();
   GatherArgs ga{};

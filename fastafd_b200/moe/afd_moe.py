@@ -227,7 +227,9 @@ class EgMoeEndpoint:
         d.pool_x, d.pool_scale = ptr(self.pool_x), ptr(self.pool_xs)
         d.row_bytes, d.scale_per_row = cfg.row_bytes, cfg.hidden // 128
         d.trace = ptr(self.trace[lane]) if self.trace else None
-        check(lib().afd_eg_group_gather(C.byref(d), cur_stream()), "eg_group_gather")
+        d.done_counter = ptr(w.done)
+        fused = cfg.num_ag * T * cfg.topk <= 8192 and cfg.block_tok <= 128      # one launch, else two
+        check(lib().afd_eg_group_gather(C.byref(d), cur_stream()), "eg_group_gather_fused" if fused else "eg_group_gather")
 
     def run_layer(self, lane: int, T: int, w13: torch.Tensor, w2: torch.Tensor,
                   w13_scale: Optional[torch.Tensor] = None, w2_scale: Optional[torch.Tensor] = None) -> None:

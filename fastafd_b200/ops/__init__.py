@@ -138,7 +138,7 @@ def decode_attn_workspace(B, Hq, Hkv, q_len, D, splits, device) -> Optional[torc
 def pick_attn_splits(B: int, Hkv: int, m_tiles: int, max_kv: int, D: int = 128) -> int:
     """KV splits so that the grid stays within one wave of resident CTAs (2 per SM for head
     dims up to 128, else 1) and every split still has at least 256 tokens to stream."""
-    slots = NUM_SMS * (2 if D <= 128 else 1)
+    slots = NUM_SMS * (3 if D <= 128 else 1)
     ctas = max(1, B * Hkv * m_tiles)
     by_fill = max(1, slots // ctas)
     by_len = max(1, max_kv // 256)

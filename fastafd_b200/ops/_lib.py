@@ -64,7 +64,7 @@ class GroupDesc(C.Structure):
         ("status", VP),
         ("recv_x", VP), ("recv_scale", VP), ("pool_x", VP), ("pool_scale", VP),
         ("row_bytes", C.c_int), ("scale_per_row", C.c_int),
-        ("trace", VP),
+        ("trace", VP), ("done_counter", VP),
     ]
 
 

@@ -26,10 +26,12 @@ def _setup(cfg, timeout_ns=int(2e9)):
 
 
 @pytest.mark.parametrize("fp8", [False, True])
-@pytest.mark.parametrize("num_ag,num_eg,T,bt", [(2, 2, 24, 16), (1, 1, 7, 32), (3, 2, 33, 32)])
+@pytest.mark.parametrize("num_ag,num_eg,T,bt", [(2, 2, 24, 16), (1, 1, 7, 32), (3, 2, 33, 32), (3, 2, 700, 64)])
 def test_moe_roundtrip(num_ag, num_eg, T, bt, fp8):
     H, I, E, K = 512, 256, 16, 4
-    cfg = MoeCommConfig(num_ag=num_ag, num_eg=num_eg, num_lanes=2, max_tokens=40, hidden=H, topk=K,
+    if T > 100 and fp8:
+        pytest.skip("the per-token fp8 oracle loop is too slow for the large case")
+    cfg = MoeCommConfig(num_ag=num_ag, num_eg=num_eg, num_lanes=2, max_tokens=max(40, T), hidden=H, topk=K,
                         num_experts=E, intermediate=I, fp8=fp8, block_tok=bt)
     fabs, ags, egs = _setup(cfg)
     g = torch.Generator().manual_seed(0)
