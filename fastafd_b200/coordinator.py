@@ -273,3 +273,51 @@ class InProcTransport(WorkerTransport):
     def poll(self, timeout_s):
         out, self._out = self._out, []
         return out
+
+
+class ZmqWorkerTransport(WorkerTransport):
+    """Coordinator side of the ZeroMQ link: one PUSH socket per worker, one shared PULL."""
+
+    def __init__(self, cmd_addrs: Dict[int, str], reply_addr: str):
+        from .protocol import RunStepCmd, StopCmd, decode, encode
+        from .utils.mp import ZmqPullQueue, ZmqPushQueue
+
+        self._Run, self._Stop = RunStepCmd, StopCmd
+        self.replies = ZmqPullQueue(reply_addr, bind=True, encode=encode, decode=decode)
+        self.cmd = {r: ZmqPushQueue(a, bind=False, encode=encode, decode=decode) for r, a in cmd_addrs.items()}
+
+    def send_step(self, step_id, ag_plans, eg_plans):
+        for r, (plan, mb_tokens) in ag_plans.items():
+            self.cmd[r].put(self._Run(plan=plan, mb_tokens=list(mb_tokens)))
+        for r, plan in eg_plans.items():
+            self.cmd[r].put(self._Run(plan=plan))
+
+    def poll(self, timeout_s):
+        out = []
+        m = self.replies.get(timeout_ms=int(timeout_s * 1000)) if timeout_s > 0 else self.replies.get_nowait()
+        while m is not None:
+            out.append(m)
+            m = self.replies.get_nowait()
+        return out
+
+    def wait_ready(self, n: int, timeout_s: float) -> List[object]:
+        """Block until n workers said ready; raises on a reported failure or on timeout."""
+        from .protocol import WorkerFailure, WorkerReady
+
+        ready, deadline = [], time.monotonic() + timeout_s
+        while len(ready) < n:
+            m = self.replies.get(timeout_ms=500)
+            if isinstance(m, WorkerFailure):
+                raise CoordinatorError(f"worker {m.rank} failed during start-up: {m.error}")
+            if isinstance(m, WorkerReady):
+                ready.append(m)
+            if time.monotonic() > deadline:
+                raise CoordinatorError(f"only {len(ready)} of {n} workers became ready within {timeout_s}s")
+        return ready
+
+    def stop(self):
+        for q in self.cmd.values():
+            try:
+                q.put(self._Stop())
+            except Exception:
+                pass

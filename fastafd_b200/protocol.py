@@ -166,6 +166,7 @@ class EgStepPlan:
 @dataclass
 class RunStepCmd:
     plan: Any
+    mb_tokens: Optional[List[int]] = None    # tokens every source sends per micro-batch (prefill padding)
 
 
 @dataclass

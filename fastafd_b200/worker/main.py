@@ -1,0 +1,78 @@
+"""Worker process of a served deployment: one per GPU (or per CPU rank in tests).
+
+It joins the host-side process group, builds its :class:`AfdEngine`, then serves step
+commands from the coordinator over ZeroMQ until told to stop. Decode steps are software
+pipelined: when the next command is already waiting, it is queued on the GPU before the
+previous step's tokens are read back, so host work hides behind device work.
+
+Reference: python/minisgl/afd_worker_base.py:1183-1276 (start_hot_rpc_loop, shutdown),
+python/minisgl/afd_attention_worker.py:1013 (centralized_overlap_loop),
+python/minisgl/afd_expert_worker.py:648.
+"""
+from __future__ import annotations
+
+import os
+import traceback
+from collections import deque
+from typing import Dict
+
+from ..protocol import (AgStepPlan, EgStepPlan, RunStepCmd, StopCmd, WorkerFailure, WorkerReady, decode, encode)
+
+
+def worker_main(rank: int, world: int, server_args, addrs: Dict[str, object], master_port: int) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from ..config import get_model_config
+    from ..engine import AfdEngine
+    from ..utils.mp import ZmqPullQueue, ZmqPushQueue
+
+    reply_q = ZmqPushQueue(addrs["reply"], bind=False, encode=encode, decode=decode)
+    try:
+        topo = server_args.topology
+        rt = server_args.runtime_config()
+        cfg = get_model_config(server_args.model_path)
+        cuda = server_args.device == "cuda"
+        if cuda:
+            torch.cuda.set_device(rank % torch.cuda.device_count())
+            device = torch.device("cuda", rank % torch.cuda.device_count())
+        else:
+            device = torch.device("cpu")
+            torch.set_num_threads(1)
+        if world > 1:
+            os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(master_port)
+            dist.init_process_group("cpu:gloo,cuda:nccl" if cuda else "gloo", rank=rank, world_size=world,
+                                    **({"device_id": device} if cuda else {}))
+        engine = AfdEngine(cfg, rt, topo, rank, device, seed=server_args.seed, fast_init=cuda,
+                           max_comm_tokens=addrs.get("max_comm_tokens"))
+        cmd_q = ZmqPullQueue(addrs["cmd"][rank], bind=True, encode=encode, decode=decode)
+        reply_q.put(WorkerReady(rank=rank, role="attention" if engine.attn is not None else "expert",
+                                num_pages=engine.attn.num_pages if engine.attn is not None else 0,
+                                info={"max_comm_tokens": engine.max_comm_tokens}))
+        pending = deque()
+        while True:
+            cmd = cmd_q.get_nowait() if pending else cmd_q.get()
+            if cmd is None:                      # nothing new: finish the oldest queued decode step
+                reply_q.put(engine.finish(pending.popleft()))
+                continue
+            if isinstance(cmd, StopCmd):
+                break
+            plan = cmd.plan
+            if isinstance(plan, EgStepPlan):
+                reply_q.put(engine.step(plan))
+            elif plan.phase == "prefill":
+                while pending:
+                    reply_q.put(engine.finish(pending.popleft()))
+                reply_q.put(engine.step(plan, cmd.mb_tokens))
+            else:
+                engine.launch(plan)
+                pending.append(plan)
+                while len(pending) > 1:
+                    reply_q.put(engine.finish(pending.popleft()))
+        engine.synchronize()
+        engine.close()
+        if world > 1:
+            dist.destroy_process_group()
+    except Exception as e:  # report instead of dying silently: the coordinator turns it into a failure
+        reply_q.put(WorkerFailure(rank=rank, error=f"{type(e).__name__}: {e}\n{traceback.format_exc()[-1500:]}"))
+        raise

@@ -1,0 +1,126 @@
+"""The serving shell on CPU: flag parsing, message codec, tokenizer worker logic, the offline
+LLM API, and a full HTTP round trip against a 1+1 CPU/gloo deployment (processes, ZeroMQ)."""
+import json
+import socket
+import threading
+import time
+
+import pytest
+
+from fastafd_b200.core import SamplingParams
+from fastafd_b200.message import DetokenizeMsg, TokenizeMsg, UserMsg, deserialize, serialize
+from fastafd_b200.server.args import parse_args
+from fastafd_b200.server.prompt_ids import validate_prompt_ids
+from fastafd_b200.tokenizer import ByteTokenizer, DetokenizeManager
+
+
+def test_parse_args_and_validation():
+    a = parse_args(["--mode", "afd-serve", "--model-path", "tiny-qwen3-moe", "--afd-attn-dp-size", "2",
+                    "--afd-mlp-ep-size", "2", "--afd-num-mb", "2", "--afd-decode-graph-bs", "4,8", "--device", "cpu"])
+    assert a.topology.world == 4 and a.afd_decode_graph_bs == (4, 8)
+    rt = a.runtime_config()
+    assert rt.num_mb == 2 and rt.dtype == "float32" and not rt.use_cuda_graph
+    with pytest.raises(ValueError):
+        parse_args(["--afd-num-mb", "9"])
+    with pytest.raises(ValueError):
+        parse_args(["--afd-attn-tp-size", "3"])          # 4 query heads
+    with pytest.raises(ValueError):
+        parse_args(["--launch-backend", "ray"])          # ray is not installed here
+    with pytest.raises(ValueError):
+        parse_args(["--spec-block", "4", "--cache-type", "radix"])
+
+
+def test_message_codec_roundtrip():
+    m = TokenizeMsg(uid=3, input_ids=[1, 2], sampling=SamplingParams(temperature=0.5, max_tokens=7, stop_token_ids=(9,)))
+    r = deserialize(serialize(m))
+    assert r == m and isinstance(r.sampling, SamplingParams) and r.sampling.stop_token_ids == (9,)
+    assert deserialize(serialize(UserMsg(uid=1, input_ids=[5], sampling=SamplingParams()))).input_ids == [5]
+
+
+def test_prompt_ids_validation():
+    assert validate_prompt_ids([1, 2, 3], 10, 8) == [1, 2, 3]
+    for bad in ([], [1, 10], [-1], [1.5], [True], list(range(8))):
+        with pytest.raises(ValueError):
+            validate_prompt_ids(bad, 10, 8)
+
+
+def test_incremental_detokenize_holds_back_partial_characters():
+    tok = ByteTokenizer()
+    d = DetokenizeManager(tok)
+    ids = tok.encode("hé!")                      # é is two bytes
+    pieces = [d.step(DetokenizeMsg(uid=0, token_ids=[i], finished=(k == len(ids) - 1))).text for k, i in enumerate(ids)]
+    assert "".join(pieces) == "hé!" and pieces[1] == ""      # first byte of é alone prints nothing
+    assert 0 not in d.state
+
+
+def test_offline_llm_api_cpu():
+    from fastafd_b200.llm import LLM
+
+    llm = LLM("tiny-qwen3-moe", device="cpu", num_pages=64, max_seq_len=128, max_running_requests=8, cuda_graph_max_bs=8)
+    out = llm.generate([[1, 2, 3, 4], "hi"], SamplingParams(max_tokens=3, ignore_eos=True))
+    assert len(out) == 2 and all(len(o["token_ids"]) == 3 for o in out)
+    again = llm.generate([[1, 2, 3, 4]], SamplingParams(max_tokens=3, ignore_eos=True))
+    assert again[0]["token_ids"] == out[0]["token_ids"]      # deterministic, state cleaned up between calls
+    llm.shutdown()
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.timeout(300)
+def test_http_round_trip_cpu_afd():
+    import requests
+    import uvicorn
+
+    from fastafd_b200.server.api_server import FrontendManager, create_app
+    from fastafd_b200.server.supervisor import LocalSupervisor
+
+    args = parse_args(["--mode", "afd-serve", "--model-path", "tiny-qwen3-moe", "--device", "cpu", "--afd-num-mb", "2",
+                       "--num-pages", "64", "--max-seq-len-override", "128", "--afd-max-running-requests", "8",
+                       "--cuda-graph-max-bs", "8"])
+    sup = LocalSupervisor(args)
+    addrs = sup.start()
+    port = _free_port()
+    server = None
+    try:
+        manager = FrontendManager(addrs.to_tokenizer, addrs.from_tokenizer)
+        app = create_app(manager, args.model_path)
+        server = uvicorn.Server(uvicorn.Config(app, host="127.0.0.1", port=port, log_level="warning"))
+        th = threading.Thread(target=server.run, daemon=True)
+        th.start()
+        for _ in range(100):
+            try:
+                if requests.get(f"http://127.0.0.1:{port}/v1/models", timeout=1).ok:
+                    break
+            except Exception:
+                time.sleep(0.1)
+        base = f"http://127.0.0.1:{port}"
+        assert requests.get(base + "/v1/models").json()["data"][0]["id"] == "tiny-qwen3-moe"
+        r = requests.post(base + "/v1/chat/completions", json={"input_ids": [1, 2, 3, 4, 5], "max_tokens": 4,
+                                                               "temperature": 0, "ignore_eos": True,
+                                                               "return_token_ids": True}, stream=True, timeout=120)
+        toks, done = [], False
+        for line in r.iter_lines():
+            if not line:
+                continue
+            payload = line.decode()[len("data: "):]
+            if payload == "[DONE]":
+                done = True
+                break
+            toks += json.loads(payload)["choices"][0].get("token_ids") or []
+        assert done and len(toks) == 4
+        rb = requests.post(base + "/v1/chat/completions/batch", json={"prompts": ["ab", "cde"], "max_tokens": 3,
+                                                                      "temperature": 0, "ignore_eos": True,
+                                                                      "return_token_ids": True}, timeout=120).json()
+        assert [len(c["token_ids"]) for c in rb["choices"]] == [3, 3]
+        bad = requests.post(base + "/v1/chat/completions", json={"input_ids": [99999], "max_tokens": 2}, stream=True, timeout=60)
+        assert "outside the vocabulary" in bad.text
+        assert sup.get_failures() == []
+    finally:
+        if server is not None:
+            server.should_exit = True
+        sup.shutdown()
+        sup.shutdown()          # idempotent
