@@ -1,0 +1,203 @@
+"""Hugging Face safetensors checkpoint loading, split by serving role.
+
+* streaming: tensors are read file by file with ``safe_open`` and placed straight into the
+  stage that needs them; nothing else is kept.
+* role split: an attention rank skips every routed-expert tensor, an expert rank skips
+  everything else.
+* merging: ``q_proj | k_proj | v_proj`` -> ``qkv_proj`` and ``gate_proj | up_proj`` ->
+  ``gate_up_proj`` (each shard merged after tensor-parallel slicing, with GQA kv-head
+  replication when there are fewer kv heads than TP ranks).
+* expert parallelism: rank r owns experts [r*ceil(E/ep), (r+1)*ceil(E/ep)); missing experts
+  on the last rank are zero padding. Per-expert tensors are stacked to [E_local, ...].
+* block FP8: ``weight`` in e4m3 with ``weight_scale_inv`` per 128x128 block (scales always
+  handled in fp32, even if stored in bf16). Expert weights stay FP8 with their exact block
+  scales; dense attention-side projections are dequantised to the compute dtype at load
+  (they run as plain library GEMMs). Static KV-cache scales in the checkpoint are ignored
+  (the KV cache is bf16).
+
+Reference: python/minisgl/models/weight.py (key normalisation :76-99, TP shard rules
+:142-185, scale sharding :274-312, merges :24-41,585-594, expert stacking :394-402,596-620,
+role split :506-513, dtype casting :123-139).
+"""
+from __future__ import annotations
+
+import glob
+import json
+import os
+import re
+from typing import Dict, Iterator, List, Optional, Tuple
+
+import torch
+
+from ..config import ModelConfig
+from ..reference import ops_ref as ref
+from .transformer import AttentionStage, ExpertStage, shard_attention_param
+
+_EXPERT_RE = re.compile(r"\.(?:mlp|block_sparse_moe)\.experts\.(\d+)\.(gate_proj|up_proj|down_proj|w1|w2|w3)\.(weight|weight_scale_inv)$")
+_EXPERT_ALIAS = {"w1": "gate_proj", "w3": "up_proj", "w2": "down_proj"}
+
+
+def normalize_key(name: str) -> Optional[str]:
+    """Checkpoint key -> internal key, or None for tensors this build does not use."""
+    if name.startswith("model.language_model."):
+        name = "model." + name[len("model.language_model."):]
+    if name.startswith("language_model."):
+        name = name[len("language_model."):]
+    if ".visual." in name or name.startswith("visual.") or "mtp." in name:
+        return None
+    if name.endswith((".k_scale", ".v_scale", ".kv_scale", "rotary_emb.inv_freq")):
+        return None
+    name = name.replace(".block_sparse_moe.gate.", ".mlp.gate.")
+    name = name.replace(".block_sparse_moe.e_score_correction_bias", ".mlp.gate.e_score_correction_bias")
+    name = name.replace(".mlp.shared_experts.", ".mlp.shared_expert.")
+    return name
+
+
+def iter_checkpoint(path: str) -> Iterator[Tuple[str, torch.Tensor]]:
+    from safetensors import safe_open
+
+    files = sorted(glob.glob(os.path.join(path, "*.safetensors")))
+    if not files:
+        raise FileNotFoundError(f"no .safetensors files in {path}")
+    for f in files:
+        with safe_open(f, framework="pt", device="cpu") as sf:
+            for k in sf.keys():
+                yield k, sf.get_tensor(k)
+
+
+def _dequant_if_fp8(w: torch.Tensor, scale: Optional[torch.Tensor]) -> torch.Tensor:
+    if w.dtype == torch.float8_e4m3fn:
+        if scale is None:
+            raise ValueError("FP8 weight without weight_scale_inv")
+        return ref.block_dequant_fp8(w, scale.float())
+    return w
+
+
+def load_attention_stage(stage: AttentionStage, path: str) -> None:
+    """Fill an AttentionStage from a checkpoint directory (TP-sharded, merged, role-filtered)."""
+    cfg = stage.cfg
+    need = stage.param_shapes()
+    raw: Dict[str, torch.Tensor] = {}
+    scales: Dict[str, torch.Tensor] = {}
+    for key, t in iter_checkpoint(path):
+        k = normalize_key(key)
+        if k is None or _EXPERT_RE.search(k):
+            continue                                  # skip_expert_weights
+        if k.endswith(".weight_scale_inv"):
+            scales[k[:-len("_scale_inv")]] = t
+        else:
+            raw[k] = t
+    for k in list(raw):
+        if k in scales or raw[k].dtype == torch.float8_e4m3fn:
+            raw[k] = _dequant_if_fp8(raw[k], scales.get(k))
+    full: Dict[str, torch.Tensor] = {}
+    for i in range(cfg.num_layers):
+        p = f"model.layers.{i}."
+        a = p + "self_attn."
+        if a + "q_proj.weight" in raw:
+            full[a + "qkv_proj.weight"] = torch.cat([raw.pop(a + n + ".weight") for n in ("q_proj", "k_proj", "v_proj")], 0)
+            if a + "q_proj.bias" in raw:
+                full[a + "qkv_proj.bias"] = torch.cat([raw.pop(a + n + ".bias") for n in ("q_proj", "k_proj", "v_proj")], 0)
+        for m in (p + "mlp.", p + "mlp.shared_expert."):
+            if m + "gate_proj.weight" in raw:
+                full[m + "gate_up_proj.weight"] = torch.cat([raw.pop(m + "gate_proj.weight"), raw.pop(m + "up_proj.weight")], 0)
+    full.update(raw)
+    if cfg.tie_embeddings:
+        full.pop("lm_head.weight", None)
+    state = {}
+    for name, (shape, kind) in need.items():
+        if name not in full:
+            raise KeyError(f"checkpoint lacks {name}")
+        t = shard_attention_param(cfg, name, full[name], stage.tp_rank, stage.tp_size)
+        if tuple(t.shape) != tuple(shape):
+            raise ValueError(f"{name}: checkpoint shape {tuple(t.shape)} != expected {shape}")
+        state[name] = t
+    stage.load_state(state)
+
+
+def load_expert_stage(stage: ExpertStage, path: str) -> None:
+    """Fill an ExpertStage: only routed-expert tensors of this rank's expert range are read."""
+    cfg, E = stage.cfg, stage.experts_local
+    lo, hi = stage.expert_base, min(stage.expert_base + E, cfg.num_experts)
+    I, H = cfg.moe_intermediate_size, cfg.hidden_size
+    parts: Dict[int, Dict[Tuple[int, str, str], torch.Tensor]] = {}
+    for key, t in iter_checkpoint(path):
+        k = normalize_key(key)
+        if k is None:
+            continue
+        m = _EXPERT_RE.search(k)
+        if not m:
+            continue                                  # skip_non_expert_weights
+        e = int(m.group(1))
+        if not lo <= e < hi:
+            continue
+        layer = int(re.search(r"layers\.(\d+)\.", k).group(1))
+        proj = _EXPERT_ALIAS.get(m.group(2), m.group(2))
+        parts.setdefault(layer, {})[(e - lo, proj, m.group(3))] = t
+    for layer in stage.moe_layers:
+        got = parts.get(layer, {})
+        fp8 = any(t.dtype == torch.float8_e4m3fn for t in got.values())
+        wdt = torch.float8_e4m3fn if fp8 else stage.dtype
+        gu = torch.zeros(E, 2 * I, H, dtype=wdt)
+        dn = torch.zeros(E, H, I, dtype=wdt)
+        gus = torch.ones(E, (2 * I + 127) // 128, (H + 127) // 128, dtype=torch.float32) if fp8 else None
+        dns = torch.ones(E, (H + 127) // 128, (I + 127) // 128, dtype=torch.float32) if fp8 else None
+        for e in range(hi - lo):
+            try:
+                gu[e, :I], gu[e, I:], dn[e] = got[(e, "gate_proj", "weight")], got[(e, "up_proj", "weight")], got[(e, "down_proj", "weight")]
+            except KeyError as err:
+                raise KeyError(f"checkpoint lacks expert {lo + e} of layer {layer}: {err}") from None
+            if fp8:
+                gb = (I + 127) // 128
+                gus[e, :gb] = got[(e, "gate_proj", "weight_scale_inv")].float()
+                gus[e, gb:] = got[(e, "up_proj", "weight_scale_inv")].float()
+                dns[e] = got[(e, "down_proj", "weight_scale_inv")].float()
+        dev = stage.device
+        stage.set_layer(layer, gu.to(dev), dn.to(dev), None if gus is None else gus.to(dev), None if dns is None else dns.to(dev))
+
+
+def save_checkpoint(cfg: ModelConfig, attn: AttentionStage, experts: List[ExpertStage], path: str,
+                    fp8_experts: bool = False, shard_mb: int = 64) -> None:
+    """Write single-rank stages as a Hugging Face style checkpoint (separate q/k/v and gate/up
+    tensors, per-expert tensors, optional block-FP8 experts). Used to build synthetic
+    checkpoints for tests and for offline conversion."""
+    from safetensors.torch import save_file
+
+    os.makedirs(path, exist_ok=True)
+    out: Dict[str, torch.Tensor] = {}
+    D = cfg.head_dim
+    for name, t in attn.w.items():
+        t = t.detach().cpu()
+        if name.endswith("qkv_proj.weight") or name.endswith("qkv_proj.bias"):
+            qn = cfg.num_q_heads * D * (2 if cfg.attn_output_gate else 1)
+            kn = cfg.num_kv_heads * D
+            base, suf = name.rsplit("qkv_proj", 1)
+            out[base + "q_proj" + suf], out[base + "k_proj" + suf], out[base + "v_proj" + suf] = \
+                t[:qn].contiguous(), t[qn:qn + kn].contiguous(), t[qn + kn:].contiguous()
+        elif name.endswith("gate_up_proj.weight"):
+            half = t.shape[0] // 2
+            base = name[:-len("gate_up_proj.weight")]
+            out[base + "gate_proj.weight"], out[base + "up_proj.weight"] = t[:half].contiguous(), t[half:].contiguous()
+        else:
+            out[name] = t.contiguous()
+    I = cfg.moe_intermediate_size
+    for st in experts:
+        for layer in st.moe_layers:
+            gu, dn = st.gate_up[layer].cpu(), st.down[layer].cpu()
+            for e in range(min(st.experts_local, cfg.num_experts - st.expert_base)):
+                p = f"model.layers.{layer}.mlp.experts.{st.expert_base + e}."
+                for pname, w in (("gate_proj", gu[e, :I]), ("up_proj", gu[e, I:]), ("down_proj", dn[e])):
+                    if fp8_experts:
+                        q, s = ref.block_quant_fp8(w.float())
+                        out[p + pname + ".weight"], out[p + pname + ".weight_scale_inv"] = q.contiguous(), s.contiguous()
+                    else:
+                        out[p + pname + ".weight"] = w.contiguous()
+    shard, size, idx = {}, 0, 0
+    for k in sorted(out):
+        shard[k] = out[k]
+        size += out[k].numel() * out[k].element_size()
+        if size > shard_mb << 20:
+            save_file(shard, os.path.join(path, f"model-{idx:05d}.safetensors"))
+            shard, size, idx = {}, 0, idx + 1
+    if shard:
+        save_file(shard, os.path.join(path, f"model-{idx:05d}.safetensors"))
