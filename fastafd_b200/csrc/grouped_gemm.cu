@@ -426,7 +426,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
     // Publish: all of this CTA's peer stores are ordered before the counter bump;
     // the last CTA to bump releases one flag per attention GPU.
     if (threadIdx.x == 0) {
-      __threadfence_system();
+      __threadfence();            // gpu scope per CTA; the last CTA alone issues the system fence
       const unsigned int prev = atomicAdd(args.done_counter, 1u);
       if (prev == gridDim.x - 1) {
         __threadfence_system();

@@ -115,7 +115,11 @@ __global__ void dispatch_push_kernel(const DispatchArgs a) {
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence_system();
+    // gpu-scope fence + counter bump per CTA; only the last CTA pays the (chip-wide
+    // serialised) system-scope fence before it releases the flags. The chain
+    // data -> fence.gpu -> counter -> fence.sys -> flag orders every CTA's stores
+    // before the flag for an acquiring peer.
+    __threadfence();
     const unsigned int prev = atomicAdd(a.done_counter, 1u);
     if (prev == gridDim.x - 1) {
       __threadfence_system();
@@ -444,7 +448,7 @@ __global__ void __launch_bounds__(1024) ag_route_dispatch_kernel(const RouteDisp
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence_system();
+    __threadfence();              // see dispatch_push_kernel: one system fence, by the last CTA
     const unsigned int prev = atomicAdd(d.done_counter, 1u);
     if (prev == gridDim.x - 1) {
       __threadfence_system();

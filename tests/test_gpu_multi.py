@@ -1,0 +1,73 @@
+"""Two GPUs: one attention rank + one expert rank over the peer-memory fabric must produce
+exactly the tokens of the colocated single-GPU engine (same kernels, same arithmetic)."""
+import os
+import socket
+import tempfile
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _cfg():
+    from fastafd_b200.config import ModelConfig
+    return ModelConfig(num_layers=6, hidden_size=512, num_q_heads=8, num_kv_heads=2, head_dim=128, vocab_size=2048,
+                       num_experts=16, num_experts_per_tok=4, moe_intermediate_size=256)
+
+
+def _rt():
+    from fastafd_b200.config import RuntimeConfig
+    return RuntimeConfig(num_mb=2, page_size=16, num_pages=256, max_running_requests=16, max_seq_len=256,
+                         cuda_graph_max_bs=8, device="cuda", moe_block_tok=16, flag_timeout_s=5.0)
+
+
+def _prompts(cfg):
+    g = torch.Generator().manual_seed(0)
+    return [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (32, 17, 5, 40, 9, 23)]
+
+
+def _worker(rank, world, port, out_path, n_new):
+    import torch.distributed as dist
+    from fastafd_b200.core import SamplingParams
+    from fastafd_b200.engine import AfdEngine, SpmdDriver
+    from fastafd_b200.protocol import AfdTopology
+
+    os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    cfg = _cfg()
+    eng = AfdEngine(cfg, _rt(), AfdTopology(attn_dp=world // 2, mlp_ep=world - world // 2), rank, f"cuda:{rank}", seed=0)
+    out = SpmdDriver(eng).generate(_prompts(cfg), SamplingParams(max_tokens=n_new, ignore_eos=True))
+    if rank == 0:
+        torch.save(out, out_path)
+    dist.barrier()
+    eng.close()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_disaggregated_equals_colocated(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch.multiprocessing as mp
+    from fastafd_b200.core import SamplingParams
+    from fastafd_b200.engine import AfdEngine, SpmdDriver
+    from fastafd_b200.protocol import AfdTopology
+
+    cfg, n_new = _cfg(), 48
+    single = AfdEngine(cfg, _rt(), AfdTopology(colocated=True), 0, "cuda:0", seed=0)
+    exp = SpmdDriver(single).generate(_prompts(cfg), SamplingParams(max_tokens=n_new, ignore_eos=True))
+    single.close()
+    with tempfile.TemporaryDirectory() as d:
+        path = os.path.join(d, "out.pt")
+        mp.spawn(_worker, args=(world, _free_port(), path, n_new), nprocs=world, join=True)
+        got = torch.load(path)
+    assert got == exp
