@@ -68,7 +68,9 @@ class AfdEngine:
             stage = ExpertStage(cfg, self.device, self.dtype, ep_rank, num_eg).init_random(seed, fast=fast_init)
         self.expert_stage = stage
 
-        client = server = None
+        from .worker.moe_client import MoeClient
+
+        client, server = MoeClient(), None      # dense models: no experts to reach
         eg_status = None
         import os as _os
         if _os.environ.get("FASTAFD_DEBUG_NULL_MOE") == "1" and cfg.is_moe:

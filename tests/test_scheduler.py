@@ -1,0 +1,121 @@
+"""Lane scheduler, page ledgers, buckets: the host-side bookkeeping, with a CPU worker mirror
+that applies only the plan's page grants (the worker must end up with the coordinator's
+page table)."""
+import numpy as np
+import pytest
+
+from fastafd_b200.core import SamplingParams
+from fastafd_b200.scheduler.buckets import (balanced_split, default_decode_buckets, normalize_buckets, per_mb_real,
+                                            select_bucket, split_prefill)
+from fastafd_b200.scheduler.cache import NaivePageLedger, OutOfPages, RadixPageCache, mismatch_index
+from fastafd_b200.scheduler.lane import AdmissionError, LaneScheduler
+
+
+def test_bucket_ladder():
+    b = default_decode_buckets(320)
+    assert b[:4] == [1, 2, 4, 8] and 256 in b and 272 in b and 264 not in b and b[-1] == 320
+    assert default_decode_buckets(20)[-1] == 20
+    assert normalize_buckets((64, 8, 8), 256) == [8, 64]
+    assert select_bucket(5, [1, 2, 4, 8]) == 8
+    with pytest.raises(ValueError):
+        select_bucket(9, [1, 2, 4, 8])
+    assert per_mb_real(5, 2) == 3 and balanced_split(5, 2) == [3, 2] and balanced_split(1, 2) == [1, 0]
+
+
+def test_prefill_split_at_request_boundaries():
+    assert split_prefill([10, 10, 10, 10], 2) == [(0, 2), (2, 4)]
+    assert split_prefill([30, 5, 5], 2) == [(0, 1), (1, 3)]
+    assert split_prefill([7], 2) in ([(0, 1), (1, 1)], [(0, 0), (0, 1)])
+    assert split_prefill([], 2) == [(0, 0), (0, 0)]
+
+
+def test_naive_ledger():
+    l = NaivePageLedger(8, 16)
+    a = l.allocate(3)
+    assert list(a) == [1, 2, 3] and l.free_pages == 4      # page 0 is reserved
+    with pytest.raises(OutOfPages):
+        l.allocate(5)
+    l.free(a)
+    l.check_integrity()
+    with pytest.raises(RuntimeError):
+        l.free([1])                                          # double free
+
+
+def test_radix_cache_shares_and_evicts():
+    c = RadixPageCache(10, 4)
+    ids = list(range(13))
+    pages, h = c.match_prefix(ids)
+    assert pages == []
+    own = list(c.allocate(4))
+    c.release(h, ids, own, 13)                               # 3 full pages cached, 1 freed
+    assert c.cached_pages == 3 and c.free_pages == 6
+    pages, h2 = c.match_prefix(ids[:9] + [99, 98, 97, 96])
+    assert pages == own[:2]
+    assert mismatch_index(ids, ids[:9] + [99]) == 9
+    c.check_integrity()
+    # pinned pages cannot be evicted; the unpinned leaf can
+    got = c.allocate(7)
+    assert len(got) == 7 and c.cached_pages == 2
+    with pytest.raises(OutOfPages):
+        c.allocate(1)
+    c.release(h2, ids[:9] + [99, 98, 97, 96], pages + list(got[:2]), 13)
+    c.check_integrity()
+
+
+class MirrorWorker:
+    def __init__(self, rows, max_pages):
+        self.table = np.zeros((rows + 1, max_pages), np.int32)
+
+    def apply(self, plan):
+        self.table[plan.grant_rows, plan.grant_slots] = plan.grant_pages
+
+
+def test_page_grants_keep_worker_table_equal_to_ledger():
+    s = LaneScheduler(0, num_pages=64, page_size=4, max_running=4, max_seq_len=64, num_mb=2, max_batched_tokens=8,
+                      max_comm_tokens=8)
+    w = MirrorWorker(4, 16)
+    for uid, n in enumerate((11, 6, 3)):
+        s.add_req(uid, list(range(n)), SamplingParams(max_tokens=6, ignore_eos=True))
+    step = 0
+    while not s.idle():
+        if s.has_prefill():
+            plan = s.schedule_prefill(step)
+            assert sum(mb.num_tokens for mb in plan.mbs) <= 8        # chunked by the token budget
+        else:
+            plan = s.schedule_decode(step, 2)
+        w.apply(plan)
+        for st in s.states.values():
+            pages = st.req.pages
+            assert list(w.table[st.req.table_idx, :len(pages)]) == pages
+            assert len(pages) == (st.planned_len + 3) // 4
+        n = sum(len(mb.rows) for mb in plan.mbs)
+        s.complete(step, np.full(n, 5, np.int32))
+        s.check_integrity()
+        step += 1
+    assert s.cache.free_pages == 63 and sorted(s.free_rows) == [0, 1, 2, 3] and s.reserved_pages == 0
+
+
+def test_padding_is_balanced_over_micro_batches():
+    s = LaneScheduler(0, num_pages=64, page_size=16, max_running=8, max_seq_len=64, num_mb=2)
+    for uid in range(3):
+        s.add_prefilled(uid, 5, SamplingParams(max_tokens=4, ignore_eos=True))
+    plan = s.schedule_decode(0, 4)
+    assert [mb.num_real for mb in plan.mbs] == [2, 1]
+    assert all(len(mb.rows) == 4 for mb in plan.mbs)
+    assert (plan.mbs[0].rows[2:] == s.dummy_row).all() and (plan.mbs[1].seq_lens[1:] == 1).all()
+    assert len(plan.grant_rows) == 3                         # the pre-admitted requests' first pages travel here
+
+
+def test_admission_waits_for_pages_then_admits():
+    s = LaneScheduler(0, num_pages=6, page_size=4, max_running=4, max_seq_len=32, num_mb=1)
+    s.add_req(0, list(range(8)), SamplingParams(max_tokens=4, ignore_eos=True))   # 3 pages
+    s.add_req(1, list(range(8)), SamplingParams(max_tokens=4, ignore_eos=True))   # 3 pages: does not fit yet
+    assert s.has_prefill() and len(s.states) == 1 and len(s.waiting) == 1
+    step = 0
+    while not s.idle():
+        plan = s.schedule_prefill(step) if s.has_prefill() else s.schedule_decode(step, 1)
+        s.complete(step, np.full(sum(len(mb.rows) for mb in plan.mbs), 1, np.int32))
+        step += 1
+    assert not s.waiting and s.cache.free_pages == 5
+    with pytest.raises(AdmissionError):
+        s.add_req(2, list(range(30)), SamplingParams(max_tokens=30))
