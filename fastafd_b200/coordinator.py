@@ -83,7 +83,8 @@ class AfdCoordinator:
                                     max_batched_tokens=rt.max_batched_tokens, max_comm_tokens=max_comm_tokens,
                                     cache_type=rt.cache_type, eos_token_ids=cfg.eos_token_ids, spec_block=rt.spec_block)
                       for l in range(self.num_lanes)]
-        self.pending = 1 if rt.disable_overlap else max(1, rt.async_pending_steps)
+        # verify steps need the accepted lengths of the previous step: no planning ahead under speculation
+        self.pending = 1 if (rt.disable_overlap or rt.spec_block > 1) else max(1, rt.async_pending_steps)
         self.inflight: Deque[_Inflight] = deque()
         self.step_id = 0
         self.uid_lane: Dict[int, int] = {}

@@ -116,6 +116,13 @@ class AfdEngine:
             self.attn = AttentionWorker(cfg, rt, self.device, client, tp_rank=tp_rank, tp_size=topo.attn_tp,
                                         tp_comm=None, dtype=self.dtype, rank=rank, max_bucket=cap,
                                         weight_init=lambda m: m.init_random(seed, fast=fast_init))
+        if self.attn is not None and rt.spec_block > 1:
+            import os as _os1
+
+            from .spec.attn_side import SpecRunner
+
+            self.attn.spec = SpecRunner(self.attn, rt.spec_block, rt.spec_draft_path, seed,
+                                        float(_os1.environ.get("FASTAFD_SPEC_SIM_ACCEPT", "0") or 0))
         if self.is_expert and not self.colocated:
             self.expert = ExpertWorker(cfg, rt, self.device, stage, server, rank, eg_status)
         self._server = server
@@ -173,7 +180,7 @@ class SpmdDriver:
         self.lanes = [LaneScheduler(l, num_pages=pages, page_size=rt.page_size, max_running=rt.max_running_requests,
                                     max_seq_len=rt.max_seq_len or cfg.max_position, num_mb=rt.num_mb,
                                     max_batched_tokens=rt.max_batched_tokens, max_comm_tokens=engine.max_comm_tokens,
-                                    cache_type=rt.cache_type, eos_token_ids=cfg.eos_token_ids)
+                                    cache_type=rt.cache_type, eos_token_ids=cfg.eos_token_ids, spec_block=rt.spec_block)
                       for l in range(self.num_lanes)]
         self.step_id = 0
         self.my_lane = None
@@ -190,26 +197,29 @@ class SpmdDriver:
             uids.append(uid)
         return uids
 
-    def _exchange_tokens(self, reply: Optional[AgStepReply], sizes: List[int]) -> List[np.ndarray]:
-        """Every rank learns every lane's sampled tokens of this step."""
+    def _exchange_tokens(self, reply: Optional[AgStepReply], sizes: List[int], q: int = 1):
+        """Every rank learns every lane's sampled tokens (and accepted counts) of this step.
+        sizes[lane] = rows of that lane; a verify step carries q tokens per row."""
         if self.e.colocated or not dist.is_initialized():
-            return [reply.next_tokens]
+            return [reply.next_tokens], [reply.accepted]
         n = max(sizes) if sizes else 0
-        mine = torch.full((n + 1,), -1, dtype=torch.int64)
+        mine = torch.full((1 + n * q + n,), -1, dtype=torch.int64)
+        mine[0] = 0
         if reply is not None:
             mine[0] = reply.status
             mine[1:1 + len(reply.next_tokens)] = torch.from_numpy(reply.next_tokens.astype(np.int64))
-        else:
-            mine[0] = 0
+            if reply.accepted is not None:
+                mine[1 + n * q:1 + n * q + len(reply.accepted)] = torch.from_numpy(reply.accepted.astype(np.int64))
         bufs = [torch.empty_like(mine) for _ in range(self.e.topo.world)]
         dist.all_gather(bufs, mine, group=self.e.group)
-        out = []
+        toks, acc = [], []
         for lane in range(self.num_lanes):
             src = lane * self.e.topo.attn_tp
             if int(bufs[src][0]) != 0:
                 raise RuntimeError(f"attention rank {src} reported device status {int(bufs[src][0])}")
-            out.append(bufs[src][1:1 + sizes[lane]].numpy().astype(np.int32))
-        return out
+            toks.append(bufs[src][1:1 + sizes[lane] * q].numpy().astype(np.int32))
+            acc.append(bufs[src][1 + n * q:1 + n * q + sizes[lane]].numpy().astype(np.int32) if q > 1 else None)
+        return toks, acc
 
     def run_step(self) -> Optional[List[Tuple[int, List[int], bool]]]:
         """Plan and execute one global step; returns [(uid, new_tokens, finished)] or None when idle."""
@@ -221,7 +231,7 @@ class SpmdDriver:
         if any(l.has_prefill() for l in lanes):
             plans = [l.schedule_prefill(sid) if l.has_prefill() else l.dummy_step(sid, "prefill", 0) for l in lanes]
             mb_tokens = [max(max(p.mbs[m].num_tokens for p in plans), 1) for m in range(self.e.rt.num_mb)]
-            phase, bucket = "prefill", 0
+            phase, bucket, q = "prefill", 0, 1
         else:
             real = max(l.decode_real() for l in lanes)
             if real == 0:
@@ -229,19 +239,20 @@ class SpmdDriver:
                     l.check_admission_stall()
                 return []
             bucket = select_bucket(per_mb_real(real, self.e.rt.num_mb), self.e.buckets)
-            plans = [l.schedule_decode(sid, bucket) if l.decode_real() else l.dummy_step(sid, "decode", bucket) for l in lanes]
-            mb_tokens = [bucket] * self.e.rt.num_mb
-            phase = "decode"
+            q = self.e.rt.spec_block if self.e.rt.spec_block > 1 else 1
+            phase = "verify" if q > 1 else "decode"
+            plans = [l.schedule_decode(sid, bucket, q) if l.decode_real() else l.dummy_step(sid, phase, bucket) for l in lanes]
+            mb_tokens = [bucket * q] * self.e.rt.num_mb
         reply = None
         if self.e.attn is not None:
             reply = self.e.step(plans[self.my_lane], mb_tokens)
         if self.e.expert is not None:
             self.e.step(EgStepPlan(step_id=sid, phase=phase, tokens_per_mb=mb_tokens))
         sizes = [sum(len(mb.rows) for mb in p.mbs) for p in plans]
-        toks = self._exchange_tokens(reply, sizes)
+        toks, acc = self._exchange_tokens(reply, sizes, q if phase == "verify" else 1)
         out = []
         for lane, l in enumerate(lanes):
-            out += l.complete(sid, toks[lane])
+            out += l.complete(sid, toks[lane], acc[lane])
         return out
 
     # ------------------------------------------------------------------ steady-state decode

@@ -288,7 +288,8 @@ class LaneScheduler:
                 record.slots.append([])
             else:
                 mbs.append(MicroBatchPlan(rows=np.full(bucket, self.dummy_row, np.int32),
-                                          seq_lens=np.ones(bucket, np.int32), num_real=0))
+                                          seq_lens=np.full(bucket, self.spec_block if phase == "verify" else 1, np.int32),
+                                          num_real=0))
                 record.slots.append([(-1, False)] * bucket)
         return self._finish_plan(step_id, phase, bucket, mbs, [], record, [])
 

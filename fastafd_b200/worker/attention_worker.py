@@ -77,6 +77,7 @@ class _MbCtx:
     residual: torch.Tensor
     extra: Optional[torch.Tensor] = None
     pad_from: int = 0
+    capture: Optional[dict] = None
     keep: list = field(default_factory=list)
 
 
@@ -123,6 +124,7 @@ class AttentionWorker:
         self.bufs = [self._make_bufs(self.cap) for _ in range(self.num_mb)]
         self.graphs: Dict[int, "torch.cuda.CUDAGraph"] = {}
         self.kernels_per_step: Dict[int, int] = {}
+        self.spec = None          # SpecRunner when speculative decoding is on
         if self.cuda:
             self.main_stream = torch.cuda.Stream(self.device)
             self.lane_streams = [torch.cuda.Stream(self.device) for _ in range(self.num_mb)]
@@ -241,8 +243,26 @@ class AttentionWorker:
                                     scale=c.routed_scaling_factor, offset1=c.norm_offset1, normed_out=mb.normed)
         self._join_lane(mb.lane)
 
-    def _pipeline(self, mbs: List[_MbCtx]) -> None:
-        """All layers for all micro-batches; on return mb.normed holds the final-norm output."""
+    def pipeline(self, mbs: List[_MbCtx], capture_layers=()) -> None:
+        self._pipeline(mbs, capture_layers)
+
+    def make_ctx(self, lane: int, ids: torch.Tensor, meta: AttnMeta, pad_from: Optional[int] = None) -> _MbCtx:
+        """Micro-batch context with freshly allocated buffers (eager prefill / verify steps)."""
+        c, dev, T = self.cfg, self.device, ids.shape[0]
+        K = max(c.num_experts_per_tok, 1)
+        mb = _MbCtx(lane=lane, T=T, ids=ids, meta=meta,
+                    x_moe=torch.zeros(T, c.hidden_size, dtype=self.dtype, device=dev),
+                    topk_idx=torch.zeros(T, K, dtype=torch.int32, device=dev),
+                    topk_w=torch.zeros(T, K, dtype=torch.float32, device=dev),
+                    normed=torch.zeros(T, c.hidden_size, dtype=self.dtype, device=dev),
+                    residual=torch.zeros(T, c.hidden_size, dtype=self.dtype, device=dev))
+        mb.pad_from = T if pad_from is None else pad_from
+        return mb
+
+    def _pipeline(self, mbs: List[_MbCtx], capture_layers=()) -> None:
+        """All layers for all micro-batches; on return mb.normed holds the final-norm output.
+        `capture_layers`: hidden states (residual stream after that layer) kept in mb.capture
+        for the speculative draft head."""
         m, L = self.model, self.cfg.num_layers
         for mb in mbs:
             h = m.embed(mb.ids)
@@ -254,6 +274,8 @@ class AttentionWorker:
         for l in range(L):
             for mb in mbs:
                 self._combine(l, mb)
+                if l in capture_layers:
+                    mb.capture[l] = mb.residual.clone()
                 if l + 1 < L:
                     self._compute(l + 1, mb)
 
@@ -431,8 +453,10 @@ class AttentionWorker:
                             normed=torch.zeros(T, c.hidden_size, dtype=self.dtype, device=dev),
                             residual=torch.zeros(T, c.hidden_size, dtype=self.dtype, device=dev))
                 mb.pad_from = T_real
+                if self.spec is not None:
+                    mb.capture = {}
                 mbs.append(mb)
-            self._pipeline(mbs)
+            self._pipeline(mbs, self.spec.capture_layers if self.spec is not None else ())
             out = []
             for lane, (mb, mbp) in enumerate(zip(mbs, plan.mbs)):
                 B = len(mbp.rows)
@@ -453,6 +477,14 @@ class AttentionWorker:
                     lens_s = torch.from_numpy(mbp.seq_lens[mbp.sample_rows].astype(np.int64)).to(dev)
                     self.token_pool[rows_s, lens_s] = t.to(torch.int32)
                     toks[mbp.sample_rows] = t.cpu().numpy()
+                else:
+                    t = None
+                if self.spec is not None and B:
+                    T_real = int(mbp.extend_lens.sum())
+                    self.spec.write_prefill_context(
+                        torch.from_numpy(mbp.rows.astype(np.int64)).to(dev), [int(x) for x in (mbp.seq_lens - mbp.extend_lens)],
+                        [int(n) for n in mbp.extend_lens], mb.ids[:T_real],
+                        [mb.capture[l][:T_real] for l in self.spec.capture_layers], t, mbp.sample_rows)
                 out.append(toks)
             if self.cuda:
                 torch.cuda.current_stream().synchronize()
@@ -464,6 +496,10 @@ class AttentionWorker:
         t0 = time.perf_counter()
         if plan.phase == "prefill":
             reply = self.run_prefill(plan, mb_tokens or [mb.num_tokens for mb in plan.mbs])
+        elif plan.phase == "verify":
+            ctx = torch.cuda.stream(self.main_stream) if self.cuda else nullcontext()
+            with ctx:
+                reply = self.spec.run_verify(plan)
         else:
             self.launch_decode(plan)
             reply = self.finish_decode(plan)

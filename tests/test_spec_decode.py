@@ -1,0 +1,55 @@
+"""Speculative decoding: acceptance rule, simulated acceptance, and the end-to-end property
+that greedy verification is lossless (same tokens as plain greedy decoding), on CPU."""
+import numpy as np
+import pytest
+import torch
+
+from fastafd_b200.config import PRESETS, RuntimeConfig
+from fastafd_b200.core import SamplingParams
+from fastafd_b200.engine import AfdEngine, SpmdDriver
+from fastafd_b200.protocol import AfdTopology
+from fastafd_b200.reference import ops_ref as ref
+from fastafd_b200.spec.attn_side import simulated_accept
+
+
+def test_greedy_accept_rule():
+    target = torch.tensor([[5, 6, 7, 8], [5, 6, 7, 8], [1, 2, 3, 4]])
+    draft = torch.tensor([[5, 6, 7], [5, 9, 7], [0, 2, 3]])
+    n, emitted = ref.greedy_accept(draft, target)
+    assert n.tolist() == [4, 2, 1]
+    assert emitted.tolist() == [[5, 6, 7, 8], [5, 6, -1, -1], [1, -1, -1, -1]]
+
+
+def test_simulated_acceptance_mean():
+    rng = np.random.default_rng(0)
+    n = simulated_accept(20000, 4, 1.8, rng)
+    assert n.min() >= 1 and n.max() <= 2 and abs(n.mean() - 1.8) < 0.02
+    assert simulated_accept(10, 4, 9.0, rng).max() == 4
+
+
+def _rt(**kw):
+    base = dict(model_path="tiny-qwen3-moe", num_mb=2, page_size=16, num_pages=96, max_running_requests=8,
+                max_seq_len=160, cuda_graph_max_bs=8, device="cpu", dtype="float32", use_cuda_graph=False)
+    base.update(kw)
+    return RuntimeConfig(**base)
+
+
+@pytest.mark.parametrize("block", [2, 4])
+def test_speculative_greedy_output_equals_plain_greedy(block):
+    cfg = PRESETS["tiny-qwen3-moe"]
+    g = torch.Generator().manual_seed(0)
+    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (30, 7, 18)]
+    sp = SamplingParams(max_tokens=11, ignore_eos=True)
+    plain = SpmdDriver(AfdEngine(cfg, _rt(), AfdTopology(colocated=True), 0, "cpu", seed=0)).generate(prompts, sp)
+    eng = AfdEngine(cfg, _rt(spec_block=block), AfdTopology(colocated=True), 0, "cpu", seed=0)
+    spec = SpmdDriver(eng).generate(prompts, sp)
+    assert spec == plain
+    assert eng.attn.spec.accept_hist.sum() > 0 and 1.0 <= eng.attn.spec.mean_accept() <= block
+
+
+def test_self_draft_accepts_everything():
+    """With a draft that always proposes what the target will say (here: drafts planted from a
+    plain run), every block is accepted in full."""
+    target = torch.tensor([[3, 4, 5, 6]])
+    n, _ = ref.greedy_accept(target[:, :3], target)
+    assert n.tolist() == [4]
