@@ -142,7 +142,7 @@ def lib() -> C.CDLL:
 # Kernel launches issued through this library since import (graph capture counts the
 # launches recorded into the graph once; replays are accounted for by the caller).
 LAUNCHES = {"count": 0}
-_KERNELS_PER_CALL = {"eg_group_gather": 2, "argmax": 2}
+_KERNELS_PER_CALL = {"eg_group_gather": 2, "argmax": 2, "gdn_decode": 2}
 
 
 def check(code: int, what: str) -> None:

@@ -72,15 +72,17 @@ def _gdn_decode_cuda(mixed, z, a, b, conv_w, A_log, dt_bias, norm_w, conv_state,
     from ._lib import check, cur_stream, lib, ptr
 
     T = mixed.shape[0]
-    out = torch.empty(T, hv * dv, dtype=mixed.dtype, device=mixed.device)
-    fn = getattr(lib(), "afd_gdn_decode", None)
-    if fn is None:
-        raise RuntimeError("kernel library has no afd_gdn_decode; rebuild with fastafd_b200.build")
+    dev = mixed.device
+    out = torch.empty(T, hv * dv, dtype=mixed.dtype, device=dev)
+    scratch = torch.empty(T, mixed.shape[1], dtype=mixed.dtype, device=dev)
+    fn = lib().afd_gdn_decode
     fn.restype = C.c_int
-    check(fn(C.c_void_p(ptr(mixed)), C.c_void_p(ptr(z)), C.c_void_p(ptr(a)), C.c_void_p(ptr(b)),
-             C.c_void_p(ptr(conv_w)), C.c_void_p(ptr(A_log)), C.c_void_p(ptr(dt_bias)), C.c_void_p(ptr(norm_w)),
-             C.c_void_p(ptr(conv_state)), C.c_void_p(ptr(rec_state)), C.c_void_p(ptr(meta.state_slots)),
-             C.c_void_p(ptr(out)), C.c_int(T), C.c_int(hk), C.c_int(hv), C.c_int(dk), C.c_int(dv),
-             C.c_int(conv_w.shape[1]), C.c_int(conv_state.shape[0]), C.c_float(eps), C.c_void_p(cur_stream())),
-          "gdn_decode")
+    vp = C.c_void_p
+    bf = lambda t: t if t.dtype == torch.bfloat16 else t.to(torch.bfloat16)  # noqa: E731
+    args = [bf(mixed.contiguous()), bf(z.contiguous()), bf(a.contiguous()), bf(b.contiguous()), bf(conv_w.contiguous()),
+            A_log.float().contiguous(), dt_bias.float().contiguous(), bf(norm_w.contiguous())]
+    check(fn(*[vp(ptr(t)) for t in args], vp(ptr(conv_state)), vp(ptr(rec_state)), vp(ptr(meta.state_slots)),
+             vp(ptr(out)), vp(ptr(scratch)), C.c_int(T), C.c_int(hk), C.c_int(hv), C.c_int(dk), C.c_int(dv),
+             C.c_int(conv_w.shape[1]), C.c_int(conv_state.shape[0]), C.c_float(eps), vp(ptr(meta.status)),
+             vp(cur_stream())), "gdn_decode")
     return out

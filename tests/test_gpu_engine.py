@@ -2,7 +2,7 @@
 import pytest
 import torch
 
-from fastafd_b200.config import PRESETS, ModelConfig, RuntimeConfig
+from fastafd_b200.config import PRESETS, ModelConfig, RopeConfig, RuntimeConfig
 from fastafd_b200.core import SamplingParams
 from fastafd_b200.engine import AfdEngine, SpmdDriver
 from fastafd_b200.protocol import AfdTopology
@@ -11,6 +11,13 @@ pytestmark = pytest.mark.gpu
 
 MID = ModelConfig(num_layers=3, hidden_size=512, num_q_heads=8, num_kv_heads=2, head_dim=128, vocab_size=2048,
                   num_experts=16, num_experts_per_tok=4, moe_intermediate_size=256)
+
+
+HYBRID = ModelConfig(architecture="Qwen3_5MoeForCausalLM", num_layers=4, hidden_size=256, num_q_heads=4, num_kv_heads=2,
+                     head_dim=64, vocab_size=1024, num_experts=8, num_experts_per_tok=2, moe_intermediate_size=128,
+                     num_shared_experts=1, shared_expert_intermediate_size=128, shared_expert_gate=True,
+                     layer_types=("linear", "linear", "linear", "full"), gdn_num_k_heads=2, gdn_num_v_heads=4,
+                     gdn_head_k_dim=32, gdn_head_v_dim=32, gdn_conv_kernel=4, attn_output_gate=True, norm_offset1=True)
 
 
 def _rt(device, graph=True, **kw):
@@ -27,7 +34,7 @@ def _gen(cfg, device, graph, prompts, n, **kw):
     return out
 
 
-@pytest.mark.parametrize("cfg", [PRESETS["tiny-qwen3-moe"], MID], ids=["tiny", "mid"])
+@pytest.mark.parametrize("cfg", [PRESETS["tiny-qwen3-moe"], MID, HYBRID], ids=["tiny", "mid", "hybrid"])
 def test_gpu_generation_graph_equals_eager_and_tracks_oracle(cfg):
     g = torch.Generator().manual_seed(0)
     prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (32, 32, 19, 7, 50)]

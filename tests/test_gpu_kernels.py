@@ -160,3 +160,33 @@ def test_fp8_block_scaled_gemm(bt):
     torch.cuda.synchronize()
     assert int(status) == 0
     torch.testing.assert_close(out.cpu().float(), exp.float(), atol=3e-2, rtol=2e-2)
+
+
+@pytest.mark.parametrize("hk,hv,dk,dv", [(2, 4, 32, 32), (4, 16, 128, 128)])
+def test_gdn_decode_step(hk, hv, dk, dv):
+    from fastafd_b200.models.transformer import AttnMeta
+    from fastafd_b200.ops import gdn as gdn_ops
+
+    T, slots, W = 5, 9, 4
+    Cc = 2 * hk * dk + hv * dv
+    mixed, z = _bf(T, Cc, seed=20), _bf(T, hv * dv, seed=21)
+    a, b = _bf(T, hv, seed=22), _bf(T, hv, seed=23)
+    conv_w = _bf(Cc, W, scale=0.5, seed=24)
+    A_log = torch.randn(hv, generator=torch.Generator().manual_seed(25)).to(DEV) * 0.5
+    dt_bias = torch.randn(hv, generator=torch.Generator().manual_seed(26)).to(DEV) * 0.5
+    norm_w = _bf(dv, seed=27) + 1
+    conv_state = _bf(slots, W - 1, Cc, seed=28)
+    rec_state = torch.randn(slots, hv, dv, dk, generator=torch.Generator().manual_seed(29)).to(DEV) * 0.1
+    sl = torch.tensor([3, 0, 8, 5, 1], dtype=torch.int32, device=DEV)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    meta = AttnMeta(positions=None, out_loc=None, page_table=None, seq_lens=None, state_slots=sl, status=status)
+    cs_ref, rs_ref = conv_state.cpu().clone(), rec_state.cpu().clone()
+    meta_cpu = AttnMeta(positions=None, out_loc=None, page_table=None, seq_lens=None, state_slots=sl.cpu())
+    exp = gdn_ops.gdn_block(mixed.cpu(), z.cpu(), a.cpu(), b.cpu(), conv_w.cpu(), A_log.cpu(), dt_bias.cpu(), norm_w.cpu(),
+                            cs_ref, rs_ref, meta_cpu, hk, hv, dk, dv, 1e-6)
+    got = gdn_ops.gdn_block(mixed, z, a, b, conv_w, A_log, dt_bias, norm_w, conv_state, rec_state, meta, hk, hv, dk, dv, 1e-6)
+    torch.cuda.synchronize()
+    assert int(status) == 0
+    torch.testing.assert_close(conv_state.cpu(), cs_ref)
+    torch.testing.assert_close(rec_state.cpu(), rs_ref, atol=2e-3, rtol=2e-3)
+    torch.testing.assert_close(got.cpu().float(), exp.float(), atol=4e-2, rtol=4e-2)
