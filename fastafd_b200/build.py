@@ -89,5 +89,43 @@ def build_extension(force: bool = False, verbose: bool = False) -> Path:
     return lib_path()
 
 
+NCCL_LIB_NAME = "libfastafd_nccl.so"
+
+
+def nccl_lib_path() -> Path:
+    return OUT_DIR / NCCL_LIB_NAME
+
+
+def _nccl_dirs():
+    import importlib.util
+
+    spec = importlib.util.find_spec("nvidia.nccl")
+    if spec is None or not spec.submodule_search_locations:
+        return None
+    base = Path(list(spec.submodule_search_locations)[0])
+    return base / "include", base / "lib"
+
+
+def build_nccl_wrapper(force: bool = False) -> Path:
+    """Compile csrc/nccl/nccl_comm.cpp against the NCCL that ships with PyTorch. The library
+    is resolved at run time from the already loaded libnccl.so.2 of the torch process."""
+    src = CSRC / "nccl" / "nccl_comm.cpp"
+    out = nccl_lib_path()
+    OUT_DIR.mkdir(exist_ok=True)
+    if not force and out.exists() and out.stat().st_mtime >= src.stat().st_mtime:
+        return out
+    dirs = _nccl_dirs()
+    if dirs is None:
+        raise RuntimeError("the nvidia.nccl package (NCCL headers and library) is not installed")
+    inc, lib = dirs
+    cmd = [nvcc_path(), "-O2", "-std=c++17", "-shared", "-Xcompiler", "-fPIC", "--cudart", "shared", "-I", str(inc),
+           str(src), "-o", str(out), "-L", str(lib), "-l:libnccl.so.2", "-Xlinker", f"-rpath={lib}"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"nccl wrapper build failed:\n{r.stdout}\n{r.stderr}")
+    return out
+
+
 if __name__ == "__main__":
+    build_nccl_wrapper(force="--force" in sys.argv)
     print(build_extension(force="--force" in sys.argv, verbose="-v" in sys.argv))

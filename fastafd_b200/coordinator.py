@@ -76,7 +76,7 @@ class AfdCoordinator:
         self.cfg, self.rt, self.topo, self.transport = cfg, rt, topo, transport
         self.on_tokens = on_tokens or (lambda items: None)
         self.worker_timeout_s = worker_timeout_s
-        self.buckets = normalize_buckets(rt.decode_graph_bs, rt.cuda_graph_max_bs)
+        self.buckets = [b for b in normalize_buckets(rt.decode_graph_bs, rt.cuda_graph_max_bs) if b % topo.attn_tp == 0] or [topo.attn_tp]
         self.num_lanes = 1 if topo.colocated else topo.attn_dp
         self.lanes = [LaneScheduler(l, num_pages=num_pages, page_size=rt.page_size, max_running=rt.max_running_requests,
                                     max_seq_len=rt.max_seq_len or cfg.max_position, num_mb=rt.num_mb,
@@ -144,7 +144,8 @@ class AfdCoordinator:
         nmb = self.rt.num_mb
         if phase == "prefill":
             plans = [l.schedule_prefill(sid) if l.has_prefill() else l.dummy_step(sid, "prefill", 0) for l in self.lanes]
-            mb_tokens = [max(max(p.mbs[m].num_tokens for p in plans), 1) for m in range(nmb)]
+            tp = self.topo.attn_tp       # token counts are per dispatch source (= per attention rank)
+            mb_tokens = [max((max(p.mbs[m].num_tokens for p in plans) + tp - 1) // tp, 1) for m in range(nmb)]
             bucket = 0
         else:
             q = self.rt.spec_block if phase == "verify" else 1
@@ -152,7 +153,7 @@ class AfdCoordinator:
             bucket = select_bucket(per_mb_real(real, nmb), self.buckets)
             plans = [l.schedule_decode(sid, bucket, q) if l.decode_real() else l.dummy_step(sid, phase, bucket)
                      for l in self.lanes]
-            mb_tokens = [bucket * q] * nmb
+            mb_tokens = [bucket * q // self.topo.attn_tp] * nmb
         rec = _Inflight(sid, phase, bucket, time.perf_counter())
         rec.real = [sum(mb.num_real for mb in p.mbs) for p in plans]
         ag_plans, eg_plans = {}, {}

@@ -42,6 +42,34 @@ def _torch_dtype(name: str, device: torch.device) -> torch.dtype:
     return {"bfloat16": torch.bfloat16, "float16": torch.float16, "float32": torch.float32}[name]
 
 
+def decode_buckets(rt: RuntimeConfig, topo: AfdTopology) -> List[int]:
+    """Decode graph sizes; with attention TP every bucket is a multiple of the TP size (the
+    residual stream is sharded by tokens across the TP ranks)."""
+    b = [x for x in normalize_buckets(rt.decode_graph_bs, rt.cuda_graph_max_bs) if x % topo.attn_tp == 0]
+    return b or [topo.attn_tp]
+
+
+def make_tp_comms(topo: AfdTopology, rank: int, device: torch.device, group=None):
+    """One communicator per attention lane; every rank of the world takes part in creating each
+    group (torch.distributed requires it). Returns this rank's communicator or None."""
+    if topo.colocated or topo.attn_tp == 1:
+        return None
+    from .parallel.comm import NcclComm, TorchDistComm
+
+    mine = None
+    for lane in range(topo.attn_dp):
+        ranks = topo.attn_tp_group(lane)
+        if device.type == "cuda":
+            g = dist.new_group(ranks, backend="gloo")
+            if rank in ranks:
+                mine = NcclComm(ranks, device, host_group=g)
+        else:
+            g = dist.new_group(ranks)
+            if rank in ranks:
+                mine = TorchDistComm(g, ranks)
+    return mine
+
+
 class AfdEngine:
     def __init__(self, cfg: ModelConfig, rt: RuntimeConfig, topo: AfdTopology, rank: int, device,
                  group=None, seed: int = 0, fast_init: bool = False, max_comm_tokens: Optional[int] = None):
@@ -52,7 +80,7 @@ class AfdEngine:
         self.is_attention = self.colocated or topo.is_attention(rank)
         self.is_expert = self.colocated or topo.is_expert(rank)
         cuda = self.device.type == "cuda"
-        self.buckets = normalize_buckets(rt.decode_graph_bs, rt.cuda_graph_max_bs)
+        self.buckets = decode_buckets(rt, topo)
         cap = self.buckets[-1]
         self.max_comm_tokens = max_comm_tokens or max(cap, min(2048, rt.max_batched_tokens // max(rt.num_mb, 1)))
         self.fabric = None
@@ -111,10 +139,11 @@ class AfdEngine:
                 else:
                     server = GlooMoeServer(stage, topo.attention_ranks(), cfg.hidden_size, cfg.num_experts_per_tok,
                                            self.dtype, group)
+        tp_comm = make_tp_comms(topo, rank, self.device, group)
         if self.is_attention:
             tp_rank = 0 if self.colocated else topo.attn_tp_rank(rank)
             self.attn = AttentionWorker(cfg, rt, self.device, client, tp_rank=tp_rank, tp_size=topo.attn_tp,
-                                        tp_comm=None, dtype=self.dtype, rank=rank, max_bucket=cap,
+                                        tp_comm=tp_comm, dtype=self.dtype, rank=rank, max_bucket=cap,
                                         weight_init=lambda m: m.init_random(seed, fast=fast_init))
         if self.attn is not None and rt.spec_block > 1:
             import os as _os1
@@ -230,7 +259,8 @@ class SpmdDriver:
         self.step_id += 1
         if any(l.has_prefill() for l in lanes):
             plans = [l.schedule_prefill(sid) if l.has_prefill() else l.dummy_step(sid, "prefill", 0) for l in lanes]
-            mb_tokens = [max(max(p.mbs[m].num_tokens for p in plans), 1) for m in range(self.e.rt.num_mb)]
+            tp = self.e.topo.attn_tp
+            mb_tokens = [max((max(p.mbs[m].num_tokens for p in plans) + tp - 1) // tp, 1) for m in range(self.e.rt.num_mb)]
             phase, bucket, q = "prefill", 0, 1
         else:
             real = max(l.decode_real() for l in lanes)
@@ -242,7 +272,7 @@ class SpmdDriver:
             q = self.e.rt.spec_block if self.e.rt.spec_block > 1 else 1
             phase = "verify" if q > 1 else "decode"
             plans = [l.schedule_decode(sid, bucket, q) if l.decode_real() else l.dummy_step(sid, phase, bucket) for l in lanes]
-            mb_tokens = [bucket * q] * self.e.rt.num_mb
+            mb_tokens = [bucket * q // self.e.topo.attn_tp] * self.e.rt.num_mb
         reply = None
         if self.e.attn is not None:
             reply = self.e.step(plans[self.my_lane], mb_tokens)
@@ -303,7 +333,7 @@ class SpmdDriver:
                 else:
                     produced += self._finish_fast(sid, plans, mine)
             if e.expert is not None:
-                e.step(EgStepPlan(step_id=sid, phase="decode", tokens_per_mb=[bucket] * rt.num_mb))
+                e.step(EgStepPlan(step_id=sid, phase="decode", tokens_per_mb=[bucket // e.topo.attn_tp] * rt.num_mb))
             if e.attn is None:
                 for lane, l in enumerate(self.lanes):
                     l.complete(sid, np.zeros(sum(len(mb.rows) for mb in plans[lane].mbs), np.int32))

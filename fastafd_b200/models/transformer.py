@@ -219,10 +219,13 @@ class AttentionStage:
         self.cos_sin = ref.build_cos_sin_cache(min(c.max_position, 1 << 17), c.rotary_dim, c.rope.theta, self.device)
 
     # ------------------------------------------------------------------ forward pieces
-    def embed(self, ids: Tensor) -> Tensor:
+    def embed(self, ids: Tensor, scatter: bool = False) -> Tensor:
+        """Vocab-parallel gather. Under TP the partial rows are summed over the ranks: all-reduce
+        (every rank gets all T rows) or, with `scatter`, reduce-scatter (rank r keeps rows
+        [r*T/tp, (r+1)*T/tp): the token-sharded residual stream of the AFD pipeline)."""
         h = ops.embedding(ids, self.w["model.embed_tokens.weight"], self.vocab_start)
         if self.tp_size > 1:
-            h = self.comm.all_reduce(h)
+            h = self.comm.reduce_scatter(h) if scatter else self.comm.all_reduce(h)
         return h
 
     def input_norm(self, layer: int, x: Tensor, residual: Optional[Tensor]) -> Tuple[Tensor, Tensor]:
@@ -232,14 +235,17 @@ class AttentionStage:
             return ops.rmsnorm(x, w, self.cfg.rms_eps, self.cfg.norm_offset1), x
         return ops.add_rmsnorm(x, residual, w, self.cfg.rms_eps, self.cfg.norm_offset1), residual
 
-    def attention(self, layer: int, x: Tensor, meta: AttnMeta, kv: KVPool, gdn: Optional[GDNStatePool] = None) -> Tensor:
-        """x: normed hidden [T,H] -> attention block output [T,H] (after o_proj and TP reduce)."""
+    def attention(self, layer: int, x: Tensor, meta: AttnMeta, kv: KVPool, gdn: Optional[GDNStatePool] = None,
+                  reduce: str = "all_reduce") -> Tensor:
+        """x: normed hidden [T,H] -> attention block output after o_proj. Under TP the row-parallel
+        o_proj leaves partial sums: `reduce` = all_reduce ([T,H] everywhere), scatter (rank r
+        keeps its T/tp rows) or none."""
         if self.cfg.layer_type(layer) == "linear":
             out = self._linear_attention(layer, x, meta, gdn)
         else:
             out = self._full_attention(layer, x, meta, kv)
-        if self.tp_size > 1:
-            out = self.comm.all_reduce(out)
+        if self.tp_size > 1 and reduce != "none":
+            out = self.comm.reduce_scatter(out) if reduce == "scatter" else self.comm.all_reduce(out)
         return out
 
     def _full_attention(self, layer: int, x: Tensor, meta: AttnMeta, kv: KVPool) -> Tensor:
@@ -351,7 +357,7 @@ class AttentionStage:
         return ops.topk_route(logits, bias, c.num_experts_per_tok, c.scoring, c.norm_topk_prob, 1.0,
                               out_idx=out_idx, out_w=out_w)
 
-    def local_mlp(self, layer: int, x: Tensor) -> Optional[Tensor]:
+    def local_mlp(self, layer: int, x: Tensor, reduce: str = "all_reduce") -> Optional[Tensor]:
         """Work that stays on the attention GPU: the dense MLP of non-MoE layers, or the shared
         expert of an MoE layer (None when the layer has neither)."""
         c = self.cfg
@@ -367,8 +373,8 @@ class AttentionStage:
                 out = (out.float() * g).to(out.dtype)
         else:
             return None
-        if self.tp_size > 1:
-            out = self.comm.all_reduce(out)
+        if self.tp_size > 1 and reduce != "none":
+            out = self.comm.reduce_scatter(out) if reduce == "scatter" else self.comm.all_reduce(out)
         return out
 
     def final_norm(self, x: Tensor, residual: Tensor) -> Tensor:

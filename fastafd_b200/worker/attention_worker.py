@@ -67,7 +67,7 @@ class _MbBuffers:
 class _MbCtx:
     """View of the buffers for the token count of the current step."""
     lane: int
-    T: int
+    T: int                      # tokens of the micro-batch (attention works on all of them)
     ids: torch.Tensor
     meta: AttnMeta
     x_moe: torch.Tensor
@@ -77,6 +77,7 @@ class _MbCtx:
     residual: torch.Tensor
     extra: Optional[torch.Tensor] = None
     pad_from: int = 0
+    Tl: int = 0                 # tokens of the residual stream held by this TP rank (T / tp)
     capture: Optional[dict] = None
     keep: list = field(default_factory=list)
 
@@ -104,6 +105,10 @@ class AttentionWorker:
         self.cfg, self.rt, self.device, self.client, self.rank = cfg, rt, torch.device(device), client, rank
         self.cuda = self.device.type == "cuda"
         self.dtype = dtype or (torch.bfloat16 if self.cuda else torch.float32)
+        from ..parallel.comm import TpComm
+
+        self.tp = tp_comm if tp_comm is not None else TpComm()
+        assert self.tp.size == tp_size, "TP communicator size does not match attn_tp"
         self.model = AttentionStage(cfg, self.device, self.dtype, tp_rank, tp_size, tp_comm)
         if weight_init is not None:
             weight_init(self.model)          # weights first: the KV pool is sized from what is left
@@ -199,9 +204,10 @@ class AttentionWorker:
         m, c = self.model, self.cfg
         moe = c.is_moe_layer(layer)
         fused = (moe and self.cuda and not mb.meta.is_prefill and c.n_group == 1
-                 and self.client.can_fuse_route(mb.T, c.num_experts, c.hidden_size))
+                 and self.client.can_fuse_route(mb.Tl, c.num_experts, c.hidden_size))
         with nvtx_range(f"AFD_AG_Attn_L{layer}_mb{mb.lane}"):
-            attn_out = m.attention(layer, mb.normed, mb.meta, self.kv, self.gdn)
+            x_in = self.tp.all_gather(mb.normed) if self.tp.size > 1 else mb.normed
+            attn_out = m.attention(layer, x_in, mb.meta, self.kv, self.gdn, reduce="scatter")
             if fused:
                 p = f"model.layers.{layer}."
                 self.client.route_dispatch(
@@ -213,24 +219,35 @@ class AttentionWorker:
             else:
                 x = m.post_attn_norm(layer, attn_out, mb.residual, out=mb.x_moe if moe else None)
         if moe and fused:
-            mb.extra = m.local_mlp(layer, x)
+            mb.extra = self._local_mlp(layer, x)
             mb.keep += [attn_out, mb.extra]
             with self._on_lane(mb.lane):
-                self.client.after_dispatch(mb.lane, layer, mb.T)
+                self.client.after_dispatch(mb.lane, layer, mb.Tl)
         elif moe:
             m.route(layer, x, out_idx=mb.topk_idx, out_w=mb.topk_w)
-            if mb.meta.is_prefill and mb.pad_from < mb.T:
-                mb.topk_idx[mb.pad_from:] = -1          # padding tokens are routed nowhere
-            mb.extra = m.local_mlp(layer, x)
+            first_pad = mb.pad_from - self.tp.rank * mb.Tl      # padding tokens are routed nowhere
+            if mb.meta.is_prefill and first_pad < mb.Tl:
+                mb.topk_idx[max(first_pad, 0):] = -1
+            mb.extra = self._local_mlp(layer, x)
             mb.keep += [attn_out, mb.extra]
             with self._on_lane(mb.lane):
                 with nvtx_range(f"AFD_AG_Dispatch_L{layer}_mb{mb.lane}"):
                     self.client.dispatch(mb.lane, layer, mb.x_moe, mb.topk_idx, mb.topk_w)
         else:
-            y = m.local_mlp(layer, x)
+            y = self._local_mlp(layer, x)
             normed = ops.add_rmsnorm(y, mb.residual, self._next_norm_weight(layer), c.rms_eps, c.norm_offset1)
             mb.normed.copy_(normed)
             mb.keep += [attn_out, x, y, normed]
+
+    def _local_mlp(self, layer: int, x: torch.Tensor):
+        """Dense MLP / shared expert on the token shard: gather the tokens, run the TP-sharded
+        MLP, scatter the partial sums back."""
+        if self.tp.size == 1:
+            return self.model.local_mlp(layer, x)
+        c = self.cfg
+        if c.is_moe_layer(layer) and c.num_shared_experts == 0:
+            return None
+        return self.model.local_mlp(layer, self.tp.all_gather(x), reduce="scatter")
 
     def _combine(self, layer: int, mb: _MbCtx) -> None:
         c = self.cfg
@@ -238,7 +255,7 @@ class AttentionWorker:
             return
         with self._on_lane(mb.lane, after_main=False):
             with nvtx_range(f"AFD_AG_Combine_L{layer}_mb{mb.lane}"):
-                self.client.combine(mb.lane, layer, mb.T, mb.topk_w, mb.topk_idx, mb.residual,
+                self.client.combine(mb.lane, layer, mb.Tl, mb.topk_w, mb.topk_idx, mb.residual,
                                     self._next_norm_weight(layer), c.rms_eps, extra=mb.extra,
                                     scale=c.routed_scaling_factor, offset1=c.norm_offset1, normed_out=mb.normed)
         self._join_lane(mb.lane)
@@ -249,14 +266,17 @@ class AttentionWorker:
     def make_ctx(self, lane: int, ids: torch.Tensor, meta: AttnMeta, pad_from: Optional[int] = None) -> _MbCtx:
         """Micro-batch context with freshly allocated buffers (eager prefill / verify steps)."""
         c, dev, T = self.cfg, self.device, ids.shape[0]
+        assert T % self.tp.size == 0, "token count must be a multiple of the attention TP size"
+        Tl = T // self.tp.size
         K = max(c.num_experts_per_tok, 1)
         mb = _MbCtx(lane=lane, T=T, ids=ids, meta=meta,
-                    x_moe=torch.zeros(T, c.hidden_size, dtype=self.dtype, device=dev),
-                    topk_idx=torch.zeros(T, K, dtype=torch.int32, device=dev),
-                    topk_w=torch.zeros(T, K, dtype=torch.float32, device=dev),
-                    normed=torch.zeros(T, c.hidden_size, dtype=self.dtype, device=dev),
-                    residual=torch.zeros(T, c.hidden_size, dtype=self.dtype, device=dev))
+                    x_moe=torch.zeros(Tl, c.hidden_size, dtype=self.dtype, device=dev),
+                    topk_idx=torch.zeros(Tl, K, dtype=torch.int32, device=dev),
+                    topk_w=torch.zeros(Tl, K, dtype=torch.float32, device=dev),
+                    normed=torch.zeros(Tl, c.hidden_size, dtype=self.dtype, device=dev),
+                    residual=torch.zeros(Tl, c.hidden_size, dtype=self.dtype, device=dev))
         mb.pad_from = T if pad_from is None else pad_from
+        mb.Tl = Tl
         return mb
 
     def _pipeline(self, mbs: List[_MbCtx], capture_layers=()) -> None:
@@ -265,7 +285,7 @@ class AttentionWorker:
         for the speculative draft head."""
         m, L = self.model, self.cfg.num_layers
         for mb in mbs:
-            h = m.embed(mb.ids)
+            h = m.embed(mb.ids, scatter=True)
             mb.residual.copy_(h)
             n0 = ops.rmsnorm(h, m.w["model.layers.0.input_layernorm.weight"], self.cfg.rms_eps, self.cfg.norm_offset1)
             mb.normed.copy_(n0)
@@ -296,9 +316,12 @@ class AttentionWorker:
                     b.workspace = ops.decode_attn_workspace(self.cap, self.model.hq, self.model.hkv, q_len,
                                                             self.cfg.head_dim, 32, self.device)
                 meta.workspace = b.workspace
-        mb = _MbCtx(lane=lane, T=T, ids=b.ids[:T], meta=meta, x_moe=b.x_moe[:T], topk_idx=b.topk_idx[:T],
-                    topk_w=b.topk_w[:T], normed=b.normed[:T], residual=b.residual[:T])
+        assert T % self.tp.size == 0, "decode bucket must be a multiple of the attention TP size"
+        Tl = T // self.tp.size
+        mb = _MbCtx(lane=lane, T=T, ids=b.ids[:T], meta=meta, x_moe=b.x_moe[:Tl], topk_idx=b.topk_idx[:Tl],
+                    topk_w=b.topk_w[:Tl], normed=b.normed[:Tl], residual=b.residual[:Tl])
         mb.pad_from = T
+        mb.Tl = Tl
         return mb
 
     def _prepare_decode_inputs(self, lane: int, bucket: int) -> None:
@@ -315,10 +338,14 @@ class AttentionWorker:
 
     def _sample_and_writeback(self, lane: int, mb: _MbCtx, bucket: int) -> None:
         b = self.bufs[lane]
-        logits = self.model.lm_head(mb.normed)
+        logits = self.model.lm_head(self.full_tokens(mb.normed))
         b.logits = logits
         ops.argmax(logits, out=b.next_tokens[:bucket]) if self.cuda else b.next_tokens[:bucket].copy_(ops.argmax(logits))
         self.token_pool[b.rows[:bucket], b.seq_lens[:bucket].long()] = b.next_tokens[:bucket]
+
+    def full_tokens(self, x_local: torch.Tensor) -> torch.Tensor:
+        """Token-sharded rows of this TP rank -> all rows of the micro-batch."""
+        return self.tp.all_gather(x_local) if self.tp.size > 1 else x_local
 
     def _decode_body(self, bucket: int) -> None:
         mbs = []
@@ -417,15 +444,16 @@ class AttentionWorker:
 
     # ------------------------------------------------------------------ prefill
     def run_prefill(self, plan: AgStepPlan, mb_tokens: List[int]) -> AgStepReply:
-        """Eager chunked prefill. Each micro-batch is padded to mb_tokens[m] tokens (the count the
-        expert GPUs expect from every source this step); padding tokens are routed nowhere."""
+        """Eager chunked prefill. Each micro-batch is padded to mb_tokens[m] tokens per dispatch
+        source (= per TP rank; the count the expert GPUs expect from every source this step);
+        padding tokens are routed nowhere."""
         ctx = torch.cuda.stream(self.main_stream) if self.cuda else nullcontext()
         dev, ps = self.device, self.page_size
         with ctx:
             self.apply_grants(plan)
             mbs: List[_MbCtx] = []
             for lane, mbp in enumerate(plan.mbs):
-                T_real, T = int(mbp.extend_lens.sum()) if len(mbp.extend_lens) else 0, mb_tokens[lane]
+                T_real, T = int(mbp.extend_lens.sum()) if len(mbp.extend_lens) else 0, mb_tokens[lane] * self.tp.size
                 pos = np.zeros(T, np.int32)
                 loc = np.full(T, -1, np.int32)
                 ids = np.zeros(T, np.int32)
@@ -444,14 +472,7 @@ class AttentionWorker:
                                 seq_lens=torch.from_numpy(mbp.seq_lens).to(dev), is_prefill=True,
                                 prefill_lens=[int(n) for n in mbp.extend_lens],
                                 state_slots=rows_t.to(torch.int32), status=self.status)
-                c = self.cfg
-                K = max(c.num_experts_per_tok, 1)
-                mb = _MbCtx(lane=lane, T=T, ids=torch.from_numpy(ids).to(dev), meta=meta,
-                            x_moe=torch.zeros(T, c.hidden_size, dtype=self.dtype, device=dev),
-                            topk_idx=torch.zeros(T, K, dtype=torch.int32, device=dev),
-                            topk_w=torch.zeros(T, K, dtype=torch.float32, device=dev),
-                            normed=torch.zeros(T, c.hidden_size, dtype=self.dtype, device=dev),
-                            residual=torch.zeros(T, c.hidden_size, dtype=self.dtype, device=dev))
+                mb = self.make_ctx(lane, torch.from_numpy(ids).to(dev), meta)
                 mb.pad_from = T_real
                 if self.spec is not None:
                     mb.capture = {}
@@ -464,7 +485,7 @@ class AttentionWorker:
                 if B and mbp.sample_rows.any():
                     last = np.cumsum(mbp.extend_lens) - 1
                     sel = torch.from_numpy(last[mbp.sample_rows]).long().to(dev)
-                    logits = self.model.lm_head(mb.normed[sel])
+                    logits = self.model.lm_head(self.full_tokens(mb.normed)[sel])
                     t = ops.argmax(logits)
                     if plan.temperatures is not None:
                         base = sum(len(p.rows) for p in plan.mbs[:lane])
@@ -495,7 +516,8 @@ class AttentionWorker:
     def run_step(self, plan: AgStepPlan, mb_tokens: Optional[List[int]] = None) -> AgStepReply:
         t0 = time.perf_counter()
         if plan.phase == "prefill":
-            reply = self.run_prefill(plan, mb_tokens or [mb.num_tokens for mb in plan.mbs])
+            tp = self.tp.size
+            reply = self.run_prefill(plan, mb_tokens or [(mb.num_tokens + tp - 1) // tp for mb in plan.mbs])
         elif plan.phase == "verify":
             ctx = torch.cuda.stream(self.main_stream) if self.cuda else nullcontext()
             with ctx:
