@@ -49,6 +49,9 @@ def worker_main(rank: int, world: int, server_args, addrs: Dict[str, object], ma
         reply_q.put(WorkerReady(rank=rank, role="attention" if engine.attn is not None else "expert",
                                 num_pages=engine.attn.num_pages if engine.attn is not None else 0,
                                 info={"max_comm_tokens": engine.max_comm_tokens}))
+        from .profiler import StepProfiler
+
+        prof = StepProfiler()
         pending = deque()
         while True:
             cmd = cmd_q.get_nowait() if pending else cmd_q.get()
@@ -58,6 +61,7 @@ def worker_main(rank: int, world: int, server_args, addrs: Dict[str, object], ma
             if isinstance(cmd, StopCmd):
                 break
             plan = cmd.plan
+            prof.on_step(plan.step_id)
             if isinstance(plan, EgStepPlan):
                 reply_q.put(engine.step(plan))
             elif plan.phase == "prefill":
@@ -69,6 +73,7 @@ def worker_main(rank: int, world: int, server_args, addrs: Dict[str, object], ma
                 pending.append(plan)
                 while len(pending) > 1:
                     reply_q.put(engine.finish(pending.popleft()))
+        prof.close()
         engine.synchronize()
         engine.close()
         if world > 1:

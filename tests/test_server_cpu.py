@@ -124,3 +124,25 @@ def test_http_round_trip_cpu_afd():
             server.should_exit = True
         sup.shutdown()
         sup.shutdown()          # idempotent
+
+
+def test_step_profiler_window_and_client_summary():
+    from fastafd_b200.benchmark.client import RequestTrace, summarize
+    from fastafd_b200.worker.profiler import StepProfiler
+
+    class Fake:
+        calls = []
+        def start(self): self.calls.append("start")
+        def stop(self): self.calls.append("stop")
+    f = Fake()
+    p = StepProfiler(start_step=3, stop_step=5, backend=f)
+    for s in range(8):
+        p.on_step(s)
+    assert f.calls == ["start", "stop"]
+    p2 = StepProfiler(start_step=-1, backend=f)
+    p2.on_step(0)
+    assert f.calls == ["start", "stop"]
+    tr = RequestTrace(start=0.0, ticks=[0.5, 0.6, 0.7], tokens=3)
+    assert abs(tr.ttft - 0.5) < 1e-9 and abs(tr.tpot - 0.1) < 1e-9
+    s = summarize([tr, RequestTrace(start=0.0, error="x")], 1.0)
+    assert s["failed"] == 1 and s["output_tokens"] == 3 and s["tpot_ms_p50"] == 100.0
