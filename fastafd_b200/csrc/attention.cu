@@ -40,6 +40,8 @@ __device__ __forceinline__ void mma_bf16_16816(float* c, const uint32_t* a, uint
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
+constexpr int kMaxSplits = 32;   // bound of the split-merge weight table in shared memory
+
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
@@ -160,11 +162,12 @@ __global__ void __launch_bounds__(128, AttnCfg<D>::CTAS_PER_SM) decode_attn_kern
 
   // One tile = 16 rows of K and of V. Lane r (< 16) resolves row r's cache slot once; the
   // warp then issues whole rows, one 16-byte chunk per lane.
-  auto load_tile = [&](int tile, int stage) {
-    const int t0 = kv_begin + tile * TOK;
+  // Cache slot of row `lane` of a tile (lanes >= 16 and rows past kv_end: -1). Issued one tile
+  // ahead of its use, so the page-table load is off the critical path.
+  auto resolve_slot = [&](int tile) -> int {
     int my_slot = -1;
-    if (lane < TOK) {
-      const int t = t0 + lane;
+    if (lane < TOK && tile < n_tiles) {
+      const int t = kv_begin + tile * TOK + lane;
       if (t < kv_end) {
         const int page = pt[t >> a.page_shift];
         const long sl = static_cast<long>(page) * a.page_size + (t & ps_mask);
@@ -172,6 +175,9 @@ __global__ void __launch_bounds__(128, AttnCfg<D>::CTAS_PER_SM) decode_attn_kern
         else my_slot = static_cast<int>(sl);
       }
     }
+    return my_slot;
+  };
+  auto load_tile = [&](int stage, int my_slot) {
     const uint32_t sstage = ld_sbase + stage * 2 * TILE_BYTES;
     if constexpr (PER_ROW <= 32) {
 #pragma unroll
@@ -209,10 +215,11 @@ __global__ void __launch_bounds__(128, AttnCfg<D>::CTAS_PER_SM) decode_attn_kern
   int next_tile = warp;
 #pragma unroll
   for (int s = 0; s < Cfg::STAGES - 1; ++s) {
-    if (next_tile < n_tiles) load_tile(next_tile, s);
+    if (next_tile < n_tiles) load_tile(s, resolve_slot(next_tile));
     cp_async_commit();
     next_tile += 4;
   }
+  int slot_ahead = resolve_slot(next_tile);
 
   // The products are computed transposed so that the query rows (8 per n-tile: exactly one
   // GQA group of 8 heads) sit on the MMA N side and no tensor work is spent on padding:
@@ -248,14 +255,19 @@ __global__ void __launch_bounds__(128, AttnCfg<D>::CTAS_PER_SM) decode_attn_kern
       lim[n][c] = row < M ? kv_len - a.q_len + 1 + j : 0;
     }
 
+  // Smallest causal limit among the valid rows of this CTA, never past kv_end. Padding rows
+  // hold q = 0 and are never written, so a tile below this limit needs no masking at all.
+  const int first_row = mt * ROWS;
+  const int min_lim = first_row < M ? min(kv_end, kv_len - a.q_len + 1 + first_row / G) : kv_end;
   int stage = 0;
   for (int tile = warp; tile < n_tiles; tile += 4) {
     {
       int ls = stage + Cfg::STAGES - 1;
       if (ls >= Cfg::STAGES) ls -= Cfg::STAGES;
-      if (next_tile < n_tiles) load_tile(next_tile, ls);
+      if (next_tile < n_tiles) load_tile(ls, slot_ahead);
       cp_async_commit();
       next_tile += 4;
+      slot_ahead = resolve_slot(next_tile);
     }
     cp_async_wait<Cfg::STAGES - 1>();
     __syncwarp();
@@ -286,6 +298,7 @@ __global__ void __launch_bounds__(128, AttnCfg<D>::CTAS_PER_SM) decode_attn_kern
     }
     // ---- mask + online softmax over the token (row) dimension ----
     const int t0 = kv_begin + tile * TOK;
+    const bool full_tile = t0 + TOK <= min_lim;      // every row of the CTA sees the whole tile
     uint32_t pb[NQ][2];
 #pragma unroll
     for (int n = 0; n < NQ; ++n) {
@@ -298,7 +311,7 @@ __global__ void __launch_bounds__(128, AttnCfg<D>::CTAS_PER_SM) decode_attn_kern
         for (int h = 0; h < 2; ++h) {
           const int t = t0 + (lane >> 2) + h * 8;
           float v = st[n][c + 2 * h] * a.scale_log2;
-          if (t >= lim[n][c] || t >= kv_end) v = -INFINITY;
+          if (!full_tile && (t >= lim[n][c] || t >= kv_end)) v = -INFINITY;
           st[n][c + 2 * h] = v;
           mx = fmaxf(mx, v);
         }
@@ -380,37 +393,60 @@ __global__ void __launch_bounds__(128, AttnCfg<D>::CTAS_PER_SM) decode_attn_kern
   }
   __syncthreads();
   const size_t tile_id = (static_cast<size_t>(b) * a.Hkv + kvh) * a.m_tiles + mt;
-  for (int idx = threadIdx.x; idx < ROWS * D; idx += 128) {
-    const int r = idx / D, d = idx % D;
-    float mm = -INFINITY;
-#pragma unroll
-    for (int w = 0; w < 4; ++w) mm = fmaxf(mm, reinterpret_cast<float*>(swarp + w * Cfg::WARP_REGION)[16 * D + r]);
-    float acc = 0.f, l = 0.f;
+  // Per-row weights of the four warps, computed once: f[w][r] = 2^(m_w - m) / l, and the
+  // row's log-sum-exp for the split merge.
+  __shared__ float s_f[4][16];
+  __shared__ float s_lse[16];
+  if (threadIdx.x < 16) {
+    const int r = threadIdx.x;
+    float mw[4], mm = -INFINITY;
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
-      const float* base = reinterpret_cast<float*>(swarp + w * Cfg::WARP_REGION);
-      const float mw = base[16 * D + r];
-      const float f = (mw == -INFINITY) ? 0.f : exp2f(mw - mm);
-      acc += base[r * D + d] * f;
-      l += base[16 * D + 16 + r] * f;
+      mw[w] = reinterpret_cast<float*>(swarp + w * Cfg::WARP_REGION)[16 * D + r];
+      mm = fmaxf(mm, mw[w]);
     }
-    const float val = l > 0.f ? acc / l : 0.f;
+    float l = 0.f, f[4];
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      f[w] = (mw[w] == -INFINITY) ? 0.f : exp2f(mw[w] - mm);
+      l += reinterpret_cast<float*>(swarp + w * Cfg::WARP_REGION)[16 * D + 16 + r] * f[w];
+    }
+    const float inv = l > 0.f ? 1.f / l : 0.f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) s_f[w][r] = f[w] * inv;
+    s_lse[r] = l > 0.f ? mm + log2f(l) : -INFINITY;
+  }
+  __syncthreads();
+  constexpr int D4 = D / 4;
+  for (int idx = threadIdx.x; idx < ROWS * D4; idx += 128) {
+    const int r = idx / D4, d = (idx % D4) * 4;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const float4 v = *reinterpret_cast<const float4*>(reinterpret_cast<float*>(swarp + w * Cfg::WARP_REGION) + r * D + d);
+      const float f = s_f[w][r];
+      acc.x += v.x * f; acc.y += v.y * f; acc.z += v.z * f; acc.w += v.w * f;
+    }
     const int row = mt * ROWS + r;
     if (a.splits == 1) {
       if (row < M) {
         const int j = row / G, g = row % G;
-        a.out[((static_cast<size_t>(b) * a.q_len + j) * a.Hq + kvh * G + g) * D + d] = __float2bfloat16(val);
+        uint2 o;
+        o.x = pack_bf16(acc.x, acc.y);
+        o.y = pack_bf16(acc.z, acc.w);
+        *reinterpret_cast<uint2*>(a.out + ((static_cast<size_t>(b) * a.q_len + j) * a.Hq + kvh * G + g) * D + d) = o;
       }
     } else {
       const size_t pidx = tile_id * a.splits + split;
-      a.part_o[(pidx * 16 + r) * D + d] = val;
-      if (d == 0) a.part_lse[pidx * 16 + r] = l > 0.f ? mm + log2f(l) : -INFINITY;
+      *reinterpret_cast<float4*>(a.part_o + (pidx * 16 + r) * D + d) = acc;
+      if (d == 0) a.part_lse[pidx * 16 + r] = s_lse[r];
     }
   }
   if (a.splits == 1) return;
 
   // ---- the last split CTA of this (request, kv head, row tile) merges the splits ----
   __shared__ int s_last;
+  __shared__ float s_w[kMaxSplits][16];
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
@@ -422,22 +458,42 @@ __global__ void __launch_bounds__(128, AttnCfg<D>::CTAS_PER_SM) decode_attn_kern
   if (!s_last) return;
   __threadfence();
   const size_t p0 = tile_id * a.splits;
-  for (int idx = threadIdx.x; idx < ROWS * D; idx += 128) {
-    const int r = idx / D, d = idx % D;
-    const int row = mt * ROWS + r;
-    if (row >= M) continue;
+  // every (split, row) log-sum-exp is fetched by its own thread, so the loads overlap
+  for (int idx = threadIdx.x; idx < a.splits * 16; idx += 128)
+    s_w[idx >> 4][idx & 15] = __ldcg(a.part_lse + p0 * 16 + idx);
+  __syncthreads();
+  if (threadIdx.x < 16) {
+    const int r = threadIdx.x;
     float mm = -INFINITY;
-    for (int s2 = 0; s2 < a.splits; ++s2) mm = fmaxf(mm, __ldcg(a.part_lse + (p0 + s2) * 16 + r));
-    float acc = 0.f, wsum = 0.f;
+    for (int s2 = 0; s2 < a.splits; ++s2) mm = fmaxf(mm, s_w[s2][r]);
+    float wsum = 0.f;
     for (int s2 = 0; s2 < a.splits; ++s2) {
-      const float lse = __ldcg(a.part_lse + (p0 + s2) * 16 + r);
+      const float lse = s_w[s2][r];
       const float w = (lse == -INFINITY) ? 0.f : exp2f(lse - mm);
-      acc += __ldcg(a.part_o + ((p0 + s2) * 16 + r) * D + d) * w;
+      s_w[s2][r] = w;
       wsum += w;
     }
+    const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+    for (int s2 = 0; s2 < a.splits; ++s2) s_w[s2][r] *= inv;
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < ROWS * D4; idx += 128) {
+    const int r = idx / D4, d = (idx % D4) * 4;
+    const int row = mt * ROWS + r;
+    if (row >= M) continue;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    const float* src = a.part_o + (p0 * 16 + r) * D + d;
+#pragma unroll 4
+    for (int s2 = 0; s2 < a.splits; ++s2) {
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(src + static_cast<size_t>(s2) * 16 * D));
+      const float w = s_w[s2][r];
+      acc.x += v.x * w; acc.y += v.y * w; acc.z += v.z * w; acc.w += v.w * w;
+    }
     const int j = row / G, g = row % G;
-    a.out[((static_cast<size_t>(b) * a.q_len + j) * a.Hq + kvh * G + g) * D + d] =
-        __float2bfloat16(wsum > 0.f ? acc / wsum : 0.f);
+    uint2 o;
+    o.x = pack_bf16(acc.x, acc.y);
+    o.y = pack_bf16(acc.z, acc.w);
+    *reinterpret_cast<uint2*>(a.out + ((static_cast<size_t>(b) * a.q_len + j) * a.Hq + kvh * G + g) * D + d) = o;
   }
 }
 
@@ -500,7 +556,7 @@ extern "C" int afd_decode_attention_strided(const void* q, long q_stride, const 
                                             void* status, void* stream) {
   using namespace afd;
   if (B == 0) return 0;
-  if (Hq % Hkv != 0 || splits < 1 || page_size < 1) return -1;
+  if (Hq % Hkv != 0 || splits < 1 || splits > afd::kMaxSplits || page_size < 1) return -1;
   if (splits > 1 && workspace == nullptr) return -2;
   DecodeAttnArgs a{};
   a.q = static_cast<const __nv_bfloat16*>(q);

@@ -136,13 +136,24 @@ def decode_attn_workspace(B, Hq, Hkv, q_len, D, splits, device) -> Optional[torc
 
 
 def pick_attn_splits(B: int, Hkv: int, m_tiles: int, max_kv: int, D: int = 128) -> int:
-    """KV splits so that the grid stays within one wave of resident CTAs (2 per SM for head
-    dims up to 128, else 1) and every split still has at least 256 tokens to stream."""
-    slots = NUM_SMS * (3 if D <= 128 else 1)
+    """KV splits of the decode attention kernel for a grid of B*Hkv*m_tiles row tiles.
+
+    Fitted to timings on B200: one CTA streams its KV range at a rate set by latency, and an
+    SM runs two CTAs (head dims up to 128) about as fast as one, a third one at the cost of
+    more time. So the time of a launch goes as  (1/s) * max(1, ceil(ctas*s/SMs) / 2)  plus a
+    small cost per split for the merge; the grid never exceeds one wave of resident CTAs and
+    a split never gets fewer than 256 tokens."""
+    resident = 3 if D <= 128 else 1
+    conc = 2 if D <= 128 else 1
     ctas = max(1, B * Hkv * m_tiles)
-    by_fill = max(1, slots // ctas)
-    by_len = max(1, max_kv // 256)
-    return max(1, min(by_fill, by_len, 32))
+    s_max = max(1, min(max_kv // 256, (NUM_SMS * resident) // ctas, 32))
+    best, best_cost = 1, None
+    for s in range(1, s_max + 1):
+        per_sm = -(-ctas * s // NUM_SMS)
+        cost = max(1.0, per_sm / conc) / s + 0.01 * s
+        if best_cost is None or cost < best_cost - 1e-9:
+            best, best_cost = s, cost
+    return best
 
 
 def decode_attention(q, k_cache, v_cache, page_table, seq_lens, Hq, Hkv, D, q_len, page_size,
