@@ -126,6 +126,29 @@ def build_nccl_wrapper(force: bool = False) -> Path:
     return out
 
 
+HOST_LIB_NAME = "libfastafd_host.so"
+
+
+def host_lib_path() -> Path:
+    return OUT_DIR / HOST_LIB_NAME
+
+
+def build_host_lib(force: bool = False) -> Path:
+    """Compile csrc/host/host_runtime.cpp (control-plane helpers; no CUDA) with the host compiler."""
+    src = CSRC / "host" / "host_runtime.cpp"
+    out = host_lib_path()
+    OUT_DIR.mkdir(exist_ok=True)
+    if not force and out.exists() and out.stat().st_mtime >= src.stat().st_mtime:
+        return out
+    cxx = os.environ.get("CXX", "g++")
+    r = subprocess.run([cxx, "-O2", "-std=c++17", "-shared", "-fPIC", str(src), "-o", str(out)],
+                       capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"host library build failed:\n{r.stdout}\n{r.stderr}")
+    return out
+
+
 if __name__ == "__main__":
+    build_host_lib(force="--force" in sys.argv)
     build_nccl_wrapper(force="--force" in sys.argv)
     print(build_extension(force="--force" in sys.argv, verbose="-v" in sys.argv))

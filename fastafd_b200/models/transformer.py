@@ -216,7 +216,8 @@ class AttentionStage:
 
     def _post_load(self) -> None:
         c = self.cfg
-        self.cos_sin = ref.build_cos_sin_cache(min(c.max_position, 1 << 17), c.rotary_dim, c.rope.theta, self.device)
+        self.cos_sin = ref.build_cos_sin_cache(min(c.max_position, 1 << 17), c.rotary_dim, c.rope.theta, self.device,
+                                              scaling=c.rope.scaling)
 
     # ------------------------------------------------------------------ forward pieces
     def embed(self, ids: Tensor, scatter: bool = False) -> Tensor:

@@ -29,9 +29,51 @@ def add_rmsnorm(x, residual, w, eps, offset1: bool = False):
 
 
 # ------------------------------------------------------------------------------ rope
-def build_cos_sin_cache(max_pos: int, rot_dim: int, theta: float, device=None) -> torch.Tensor:
+def scale_inv_freq(inv_freq: torch.Tensor, rot_dim: int, theta: float, scaling) -> torch.Tensor:
+    """Long-context frequency scaling of the RoPE table.
+
+    ``llama3``: wavelengths longer than orig/low_freq_factor are slowed by ``factor``, shorter
+    than orig/high_freq_factor are kept, with a linear blend in between. ``yarn``: frequencies
+    are divided by ``factor`` along a linear ramp between the dimensions that make beta_fast and
+    beta_slow rotations over the original window (no magnitude correction of cos/sin).
+    Reference: python/minisgl/layers/rotary.py:72-116."""
+    if not scaling:
+        return inv_freq
+    kind = scaling.get("rope_type", scaling.get("type", "default"))
+    if kind in ("default", "linear") and "factor" not in scaling:
+        return inv_freq
+    if kind == "linear":
+        return inv_freq / float(scaling["factor"])
+    if kind == "llama3":
+        f = float(scaling["factor"])
+        lo, hi = float(scaling["low_freq_factor"]), float(scaling["high_freq_factor"])
+        orig = float(scaling["original_max_position_embeddings"])
+        wave = 2 * math.pi / inv_freq
+        if lo == hi:
+            return torch.where(wave < orig / hi, inv_freq, inv_freq / f)
+        blend = ((orig / wave - lo) / (hi - lo)).clamp(0, 1)
+        return inv_freq * ((1 - blend) / f + blend)
+    if kind == "yarn":
+        f = float(scaling["factor"])
+        orig = float(scaling["original_max_position_embeddings"])
+        half = rot_dim // 2
+
+        def dim_of(rotations: float) -> float:
+            return rot_dim * math.log(orig / (rotations * 2 * math.pi)) / (2 * math.log(theta))
+
+        first = max(math.floor(dim_of(float(scaling.get("beta_fast", 32.0)))), 0)
+        last = min(math.ceil(dim_of(float(scaling.get("beta_slow", 1.0)))), half - 1)
+        ramp = ((torch.arange(half, dtype=torch.float32) - first) / max(last - first, 1)).clamp(0, 1)
+        return inv_freq / f * ramp + inv_freq * (1 - ramp)
+    if kind == "default":
+        return inv_freq
+    raise ValueError(f"unsupported rope scaling {scaling!r}")
+
+
+def build_cos_sin_cache(max_pos: int, rot_dim: int, theta: float, device=None, scaling=None) -> torch.Tensor:
     """[max_pos, rot_dim] fp32: first half cos, second half sin (NeoX pairing)."""
     inv_freq = 1.0 / (theta ** (torch.arange(0, rot_dim, 2, dtype=torch.float32) / rot_dim))
+    inv_freq = scale_inv_freq(inv_freq, rot_dim, theta, scaling)
     t = torch.arange(max_pos, dtype=torch.float32)
     freqs = torch.outer(t, inv_freq)
     return torch.cat([freqs.cos(), freqs.sin()], dim=-1).to(device)

@@ -79,12 +79,42 @@ class _Node:
     last_use: float = 0.0
 
 
+_HOST_LIB = None
+
+
+def _host_lib():
+    """The native control-plane helpers (csrc/host/host_runtime.cpp), built on first use;
+    None when no host compiler is available."""
+    global _HOST_LIB
+    if _HOST_LIB is None:
+        import ctypes as C
+
+        from ..build import build_host_lib
+        try:
+            lib = C.CDLL(str(build_host_lib()))
+            for fn in (lib.afd_mismatch_i32, lib.afd_mismatch_i64):
+                fn.restype = C.c_int64
+                fn.argtypes = [C.c_void_p, C.c_void_p, C.c_int64]
+            _HOST_LIB = lib
+        except (OSError, RuntimeError):
+            _HOST_LIB = False
+    return _HOST_LIB or None
+
+
 def mismatch_index(a: Sequence[int], b: Sequence[int]) -> int:
     """First index where two id sequences differ (the reference's native radix helper,
-    python/minisgl/kernel/csrc/src/radix.cpp)."""
+    python/minisgl/kernel/csrc/src/radix.cpp). Arrays of one integer dtype go to the native
+    routine; anything else is compared with numpy."""
     a = np.asarray(a)
     b = np.asarray(b)
     n = min(len(a), len(b))
+    if n == 0:
+        return 0
+    lib = _host_lib()
+    if lib is not None and a.dtype == b.dtype and a.dtype in (np.int32, np.int64) \
+            and a.flags.c_contiguous and b.flags.c_contiguous:
+        fn = lib.afd_mismatch_i32 if a.dtype == np.int32 else lib.afd_mismatch_i64
+        return int(fn(a.ctypes.data, b.ctypes.data, n))
     neq = np.nonzero(a[:n] != b[:n])[0]
     return int(neq[0]) if len(neq) else n
 

@@ -70,3 +70,31 @@ def test_hf_config_parsing():
         "shared_expert_intermediate_size": 1024, "full_attention_interval": 4, "partial_rotary_factor": 0.25}})
     assert q35.layer_types == ("linear", "linear", "linear", "full") * 2 and q35.rotary_dim == 64 and q35.norm_offset1
     assert q35.num_full_attn_layers == 2 and q35.kv_bytes_per_token() == 2 * 2 * 2 * 256 * 2
+
+
+def test_rope_scaling_tables():
+    import math
+
+    import torch
+
+    from fastafd_b200.reference import ops_ref as ref
+
+    rot, theta = 64, 10000.0
+    base = 1.0 / (theta ** (torch.arange(0, rot, 2, dtype=torch.float32) / rot))
+    assert torch.equal(ref.scale_inv_freq(base, rot, theta, None), base)
+    lin = ref.scale_inv_freq(base, rot, theta, {"rope_type": "linear", "factor": 4.0})
+    assert torch.allclose(lin, base / 4)
+    l3 = ref.scale_inv_freq(base, rot, theta, {"rope_type": "llama3", "factor": 8.0, "low_freq_factor": 1.0,
+                                                 "high_freq_factor": 4.0, "original_max_position_embeddings": 8192})
+    wave = 2 * math.pi / base
+    assert torch.allclose(l3[wave < 8192 / 4], base[wave < 8192 / 4])          # short wavelengths untouched
+    assert torch.allclose(l3[wave > 8192], base[wave > 8192] / 8)              # long ones slowed by the factor
+    mid = (wave >= 8192 / 4) & (wave <= 8192)
+    assert bool(((l3[mid] <= base[mid] + 1e-12) & (l3[mid] >= base[mid] / 8 - 1e-12)).all())
+    yarn = ref.scale_inv_freq(base, rot, theta, {"rope_type": "yarn", "factor": 4.0,
+                                                   "original_max_position_embeddings": 4096})
+    assert torch.allclose(yarn[0], base[0]) and torch.allclose(yarn[-1], base[-1] / 4)
+    assert bool((yarn[1:] / base[1:] <= yarn[:-1] / base[:-1] + 1e-7).all())   # monotone ramp
+    table = ref.build_cos_sin_cache(128, rot, theta, scaling={"rope_type": "yarn", "factor": 4.0,
+                                                               "original_max_position_embeddings": 4096})
+    assert table.shape == (128, rot)

@@ -119,3 +119,20 @@ def test_admission_waits_for_pages_then_admits():
     assert not s.waiting and s.cache.free_pages == 5
     with pytest.raises(AdmissionError):
         s.add_req(2, list(range(30)), SamplingParams(max_tokens=30))
+
+
+def test_native_mismatch_matches_numpy():
+    import numpy as np
+
+    from fastafd_b200.scheduler import cache
+
+    rng = np.random.default_rng(0)
+    for dt in (np.int32, np.int64):
+        a = rng.integers(0, 1000, 4096).astype(dt)
+        for cut in (0, 1, 17, 4095):
+            b = a.copy()
+            b[cut] += 1
+            assert cache.mismatch_index(a, b) == cut
+        assert cache.mismatch_index(a, a.copy()) == 4096
+        assert cache.mismatch_index(a, a[:100].copy()) == 100
+    assert cache._host_lib() is not None, "the host helper library should build with g++"
