@@ -116,6 +116,31 @@ def argmax(logits: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Te
     return out
 
 
+def sample(logits: torch.Tensor, temperatures: torch.Tensor, top_ks: torch.Tensor, top_ps: torch.Tensor,
+           generator: Optional[torch.Generator] = None, uniform: Optional[torch.Tensor] = None,
+           out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """One token per row: arg-max where temperature <= 0, else temperature softmax, top-k /
+    top-p filtering and a multinomial draw (inverse CDF from `uniform`, drawn from `generator`
+    when not given). CUDA rows run csrc/sampling.cu; CPU rows the oracle."""
+    if not logits.is_cuda:
+        return ref.sample(logits, temperatures, top_ks, top_ps, generator)
+    T, V = logits.shape
+    dev = logits.device
+    if logits.dtype not in (torch.bfloat16, torch.float32):
+        logits = logits.float()
+    if logits.stride(1) != 1:
+        logits = logits.contiguous()
+    if uniform is None:
+        uniform = torch.rand(T, device=dev, dtype=torch.float32, generator=generator)
+    out = torch.empty(T, dtype=torch.int32, device=dev) if out is None else out
+    t = temperatures.to(device=dev, dtype=torch.float32).contiguous()
+    k = top_ks.to(device=dev, dtype=torch.int32).contiguous()
+    p = top_ps.to(device=dev, dtype=torch.float32).contiguous()
+    check(lib().afd_sample(ptr(logits), logits.stride(0), T, V, int(logits.dtype == torch.bfloat16), ptr(t), ptr(k),
+                           ptr(p), ptr(uniform.contiguous()), ptr(out), cur_stream()), "sample")
+    return out
+
+
 def group_quant_fp8(x: torch.Tensor, group: int = 128, pow2: bool = False):
     if not x.is_cuda:
         return ref.group_quant_fp8(x, group, pow2)

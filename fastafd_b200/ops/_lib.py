@@ -96,6 +96,7 @@ _SIGNATURES = {
                                                VP, VP]),
     "afd_argmax": (C.c_int, [VP, VP, C.c_int, C.c_int, C.c_long, C.c_int, VP, VP]),
     "afd_argmax_chunks": (C.c_int, [C.c_int]),
+    "afd_sample": (C.c_int, [VP, C.c_long, C.c_int, C.c_int, C.c_int, VP, VP, VP, VP, VP, VP]),
     "afd_group_quant_fp8": (C.c_int, [VP, VP, VP, C.c_long, C.c_int, C.c_int, C.c_int, VP]),
     "afd_decode_attn_workspace_bytes": (C.c_long, [C.c_int] * 6),
     "afd_decode_attention": (C.c_int, [VP, VP, VP, VP, VP, VP, VP, C.c_int, C.c_int, C.c_int, C.c_int,
@@ -142,7 +143,7 @@ def lib() -> C.CDLL:
 # Kernel launches issued through this library since import (graph capture counts the
 # launches recorded into the graph once; replays are accounted for by the caller).
 LAUNCHES = {"count": 0}
-_KERNELS_PER_CALL = {"eg_group_gather": 2, "argmax": 2, "gdn_decode": 2}
+_KERNELS_PER_CALL = {"eg_group_gather": 2, "argmax": 2, "gdn_decode": 2, "gdn_prefill": 3}
 
 
 def check(code: int, what: str) -> None:

@@ -29,6 +29,9 @@ def gdn_block(mixed, z, a, b, conv_w, A_log, dt_bias, norm_w, conv_state, rec_st
     if mixed.is_cuda and not meta.is_prefill:
         return _gdn_decode_cuda(mixed, z, a, b, conv_w, A_log, dt_bias, norm_w, conv_state, rec_state, meta,
                                 hk, hv, dk, dv, eps)
+    if mixed.is_cuda:
+        return _gdn_prefill_cuda(mixed, z, a, b, conv_w, A_log, dt_bias, norm_w, conv_state, rec_state, meta,
+                                 hk, hv, dk, dv, eps)
     T = mixed.shape[0]
     slots = meta.state_slots.long()
     out = torch.empty(T, hv * dv, dtype=mixed.dtype, device=mixed.device)
@@ -86,3 +89,37 @@ def _gdn_decode_cuda(mixed, z, a, b, conv_w, A_log, dt_bias, norm_w, conv_state,
              C.c_int(conv_w.shape[1]), C.c_int(conv_state.shape[0]), C.c_float(eps), vp(ptr(meta.status)),
              vp(cur_stream())), "gdn_decode")
     return out
+
+
+def _gdn_prefill_cuda(mixed, z, a, b, conv_w, A_log, dt_bias, norm_w, conv_state, rec_state, meta, hk, hv, dk, dv, eps):
+    """Packed sequences of a prefill chunk through csrc/gdn.cu (conv, token-serial delta rule with
+    the state rows in registers, gated norm). A sequence whose chunk starts at position 0 starts
+    from zero state."""
+    import numpy as np
+
+    from ._lib import check, cur_stream, lib, ptr
+
+    T = mixed.shape[0]
+    dev = mixed.device
+    lens = np.asarray(meta.prefill_lens, dtype=np.int64)
+    n = len(lens)
+    cu = np.zeros(n + 1, dtype=np.int32)
+    cu[1:] = np.cumsum(lens)
+    starts = meta.seq_lens[:n].cpu().numpy().astype(np.int64) - lens
+    host = torch.from_numpy(np.concatenate([cu, (starts == 0).astype(np.int32)]))
+    meta_dev = host.to(dev, non_blocking=False)
+    cu_d, fresh_d = meta_dev[:n + 1], meta_dev[n + 1:]
+    out = torch.empty(T, hv * dv, dtype=torch.bfloat16, device=dev)
+    C_ = mixed.shape[1]
+    scratch = torch.empty(T * (C_ + hv * dv), dtype=torch.bfloat16, device=dev)
+    fn = lib().afd_gdn_prefill
+    fn.restype = C.c_int
+    vp = C.c_void_p
+    bf = lambda t: t if t.dtype == torch.bfloat16 else t.to(torch.bfloat16)  # noqa: E731
+    args = [bf(mixed.contiguous()), bf(z.contiguous()), bf(a.contiguous()), bf(b.contiguous()), bf(conv_w.contiguous()),
+            A_log.float().contiguous(), dt_bias.float().contiguous(), bf(norm_w.contiguous())]
+    check(fn(*[vp(ptr(t)) for t in args], vp(ptr(conv_state)), vp(ptr(rec_state)), vp(ptr(meta.state_slots)),
+             vp(ptr(cu_d)), vp(ptr(fresh_d)), vp(ptr(out)), vp(ptr(scratch)), C.c_int(T), C.c_int(int(cu[-1])),
+             C.c_int(n), C.c_int(hk), C.c_int(hv), C.c_int(dk), C.c_int(dv), C.c_int(conv_w.shape[1]),
+             C.c_int(conv_state.shape[0]), C.c_float(eps), vp(ptr(meta.status)), vp(cur_stream())), "gdn_prefill")
+    return out.to(mixed.dtype)

@@ -436,7 +436,7 @@ class AttentionWorker:
             b, n = self.bufs[lane], plan.bucket
             t = torch.from_numpy(plan.temperatures[off:off + n]).to(self.device)
             if bool((t > 0).any()):
-                toks = ref.sample(b.logits.float(), t, torch.from_numpy(plan.top_ks[off:off + n]).to(self.device),
+                toks = ops.sample(b.logits, t, torch.from_numpy(plan.top_ks[off:off + n]).to(self.device),
                                   torch.from_numpy(plan.top_ps[off:off + n]).to(self.device))
                 b.next_tokens[:n].copy_(toks)
                 self.token_pool[b.rows[:n], b.seq_lens[:n].long()] = b.next_tokens[:n]
@@ -492,7 +492,7 @@ class AttentionWorker:
                         mask = mbp.sample_rows
                         temps = torch.from_numpy(plan.temperatures[base:base + B][mask]).to(dev)
                         if bool((temps > 0).any()):
-                            t = ref.sample(logits.float(), temps, torch.from_numpy(plan.top_ks[base:base + B][mask]).to(dev),
+                            t = ops.sample(logits, temps, torch.from_numpy(plan.top_ks[base:base + B][mask]).to(dev),
                                            torch.from_numpy(plan.top_ps[base:base + B][mask]).to(dev))
                     rows_s = torch.from_numpy(mbp.rows[mbp.sample_rows].astype(np.int64)).to(dev)
                     lens_s = torch.from_numpy(mbp.seq_lens[mbp.sample_rows].astype(np.int64)).to(dev)

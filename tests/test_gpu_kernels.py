@@ -190,3 +190,96 @@ def test_gdn_decode_step(hk, hv, dk, dv):
     torch.testing.assert_close(conv_state.cpu(), cs_ref)
     torch.testing.assert_close(rec_state.cpu(), rs_ref, atol=2e-3, rtol=2e-3)
     torch.testing.assert_close(got.cpu().float(), exp.float(), atol=4e-2, rtol=4e-2)
+
+
+@pytest.mark.parametrize("hk,hv,dk,dv", [(2, 4, 32, 32), (2, 8, 128, 128)])
+def test_gdn_prefill_matches_token_serial_oracle(hk, hv, dk, dv):
+    """Packed prefill of three sequences (one continuing from a stored state, two fresh, plus
+    padding rows) against the CPU oracle path of the same block."""
+    from fastafd_b200.models.transformer import AttnMeta
+    from fastafd_b200.ops import gdn as gdn_ops
+
+    lens, slots, W = [7, 0, 12, 5], 6, 4
+    T = sum(lens) + 3                       # 3 padding rows
+    Cc = 2 * hk * dk + hv * dv
+    mixed, z = _bf(T, Cc, seed=30), _bf(T, hv * dv, seed=31)
+    a, b = _bf(T, hv, seed=32), _bf(T, hv, seed=33)
+    conv_w = _bf(Cc, W, scale=0.5, seed=34)
+    A_log = torch.randn(hv, generator=torch.Generator().manual_seed(35)).to(DEV) * 0.5
+    dt_bias = torch.randn(hv, generator=torch.Generator().manual_seed(36)).to(DEV) * 0.5
+    norm_w = _bf(dv, seed=37) + 1
+    conv_state = _bf(slots, W - 1, Cc, seed=38)
+    rec_state = torch.randn(slots, hv, dv, dk, generator=torch.Generator().manual_seed(39)).to(DEV) * 0.1
+    sl = torch.tensor([4, 2, 0, 5], dtype=torch.int32, device=DEV)
+    # sequence 0 continues (3 tokens already cached), the others start at position 0
+    seq_lens = torch.tensor([3 + 7, 0, 12, 5], dtype=torch.int32, device=DEV)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    kw = dict(positions=None, out_loc=None, page_table=None, is_prefill=True, prefill_lens=lens)
+    meta = AttnMeta(seq_lens=seq_lens, state_slots=sl, status=status, **kw)
+    meta_cpu = AttnMeta(seq_lens=seq_lens.cpu(), state_slots=sl.cpu(), **kw)
+    cs_ref, rs_ref = conv_state.cpu().clone(), rec_state.cpu().clone()
+    exp = gdn_ops.gdn_block(mixed.cpu(), z.cpu(), a.cpu(), b.cpu(), conv_w.cpu(), A_log.cpu(), dt_bias.cpu(), norm_w.cpu(),
+                            cs_ref, rs_ref, meta_cpu, hk, hv, dk, dv, 1e-6)
+    got = gdn_ops.gdn_block(mixed, z, a, b, conv_w, A_log, dt_bias, norm_w, conv_state, rec_state, meta, hk, hv, dk, dv, 1e-6)
+    torch.cuda.synchronize()
+    assert int(status) == 0
+    used = [4, 0, 5]
+    torch.testing.assert_close(conv_state.cpu()[used], cs_ref[used])
+    torch.testing.assert_close(rec_state.cpu()[used], rs_ref[used], atol=3e-3, rtol=3e-3)
+    torch.testing.assert_close(got.cpu().float(), exp.float(), atol=5e-2, rtol=5e-2)
+    assert float(got[sum(lens):].abs().max()) == 0.0
+
+
+# ----------------------------------------------------------------------------- sampling
+def _kept_set(logits_row, temp, k, tp):
+    """Oracle: tokens that survive top-k then top-p (ops_ref.sample semantics) and their
+    renormalised probabilities."""
+    p = torch.softmax(logits_row.double() / temp, -1)
+    V = p.numel()
+    if 0 < k < V:
+        kth = p.topk(k).values[-1]
+        p = torch.where(p < kth, torch.zeros_like(p), p)
+    if tp < 1.0:
+        sp, si = p.sort(descending=True)
+        cum = sp.cumsum(0)
+        sp = torch.where((cum - sp) > tp, torch.zeros_like(sp), sp)
+        p = torch.zeros_like(p).scatter_(0, si, sp)
+    return p / p.sum()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("V,temp,k,tp", [(1000, 1.0, 0, 1.0), (1000, 0.7, 20, 1.0), (1000, 1.3, 0, 0.8),
+                                          (5000, 1.0, 50, 0.9), (151936, 0.8, 40, 0.95)])
+def test_sample_kernel_distribution(V, temp, k, tp):
+    torch.manual_seed(V + k)
+    row = (torch.randn(V, device=DEV) * 3).float()
+    want = _kept_set(row.cpu(), temp, k, tp)
+    N = 20000
+    logits = row[None, :].expand(N, V)          # stride-0 rows: every draw sees the same logits
+    u = (torch.arange(N, device=DEV, dtype=torch.float32) + 0.5) / N
+    toks = ops.sample(logits, torch.full((N,), temp), torch.full((N,), k, dtype=torch.int32),
+                      torch.full((N,), tp), uniform=u)
+    torch.cuda.synchronize()
+    counts = torch.bincount(toks.long().cpu(), minlength=V).double()
+    kept = want > 0
+    # every draw lies in the oracle's kept set (a token at the top-p border may differ by rounding)
+    outside = counts[~kept].sum().item()
+    assert outside <= N * 2e-3, outside
+    got = counts / N
+    # a stratified uniform grid reproduces each probability to about 1/N per token
+    err = (got - want).abs()
+    assert err.max().item() < 3e-3, err.max().item()
+    assert (got[kept] - want[kept]).abs().sum().item() < kept.sum().item() / N + 0.01
+
+
+@pytest.mark.gpu
+def test_sample_kernel_greedy_rows_and_bf16():
+    torch.manual_seed(3)
+    T, V = 7, 4099
+    logits = torch.randn(T, V, device=DEV).to(torch.bfloat16)
+    logits[2, 100] = logits[2, 50] = 9.0        # tie: lowest index wins
+    temps = torch.tensor([0.0, 1.0, 0.0, 0.5, 0.0, 1.0, 0.0])
+    toks = ops.sample(logits, temps, torch.ones(T, dtype=torch.int32), torch.ones(T))   # top_k = 1 -> mode
+    torch.cuda.synchronize()
+    want = ref.argmax_lowest(logits.float().cpu())
+    assert toks.cpu().tolist() == want.tolist()
