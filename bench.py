@@ -51,6 +51,8 @@ def parse_args():
     ap.add_argument("--block-tok", type=int, default=16)
     ap.add_argument("--layers", type=int, default=0, help="debug only: truncate the model (marks the result invalid)")
     ap.add_argument("--no-graph", action="store_true")
+    ap.add_argument("--attn-gpus", type=int, default=0, help="attention GPUs of the N (0 = N/2, the 1:1 split)")
+    ap.add_argument("--attn-tp", type=int, default=1, help="tensor-parallel size of an attention DP lane")
     return ap.parse_args()
 
 
@@ -143,20 +145,23 @@ def main():
     if args.layers and args.layers < cfg.num_layers:
         cfg = cfg.with_layers(args.layers)
         truncated = True
-    topo = AfdTopology.for_world(world)
+    topo = AfdTopology.for_world(world, attn_tp=args.attn_tp, attn_gpus=args.attn_gpus)
     if args.num_mb <= 0:
         args.num_mb = 1 if topo.colocated else 2
     b = args.batch_per_attn_gpu
-    per_mb = (b + args.num_mb - 1) // args.num_mb
+    tp = topo.attn_tp
+    lane_b = b * tp                      # a TP lane serves tp GPUs' worth of requests
+    per_mb = (lane_b + args.num_mb - 1) // args.num_mb
+    per_mb = (per_mb + tp - 1) // tp * tp
     total_steps = 2 * (args.steps + args.warmup) + 8
-    rt = RuntimeConfig(model_path=args.model, num_mb=args.num_mb, page_size=16, max_running_requests=b,
+    rt = RuntimeConfig(model_path=args.model, num_mb=args.num_mb, page_size=16, max_running_requests=lane_b,
                        max_seq_len=args.context + total_steps + 16, cuda_graph_max_bs=per_mb,
                        decode_graph_bs=(per_mb,), use_cuda_graph=not args.no_graph, moe_block_tok=args.block_tok,
                        max_batched_tokens=per_mb * args.num_mb, device="cuda")
     t_build = time.time()
-    eng = AfdEngine(cfg, rt, topo, rank, device, group=None, seed=0, fast_init=True, max_comm_tokens=per_mb)
+    eng = AfdEngine(cfg, rt, topo, rank, device, group=None, seed=0, fast_init=True, max_comm_tokens=per_mb // tp)
     drv = SpmdDriver(eng)
-    drv.install_prefilled(b, args.context, max_tokens=total_steps + 4)
+    drv.install_prefilled(lane_b, args.context, max_tokens=total_steps + 4)
     torch.cuda.synchronize()
     build_s = time.time() - t_build
 
@@ -244,7 +249,7 @@ def main():
             "tpot_ms": round(dev_ms / args.steps, 4),
             "config": {"model": args.model, "global_batch": b * n_attn, "seq_len": args.context,
                        "decode_tokens_timed": args.steps, "micro_batches": args.num_mb, "page_size": 16,
-                       "parallelism": "colocated-1gpu" if topo.colocated else f"attn_dp{topo.attn_dp}+mlp_ep{topo.mlp_ep}",
+                       "parallelism": "colocated-1gpu" if topo.colocated else (f"attn_dp{topo.attn_dp}" + (f"xtp{tp}" if tp > 1 else "") + f"+mlp_ep{topo.mlp_ep}"),
                        "l2": "per-step working set (expert weights + KV) is far larger than the 126 MB L2; no flush needed",
                        "layers": cfg.num_layers, "truncated_model": truncated},
             "clocks": clocks,

@@ -93,12 +93,15 @@ class AfdTopology:
         return self.expert_index(rank) % self.mlp_replica
 
     @staticmethod
-    def for_world(world: int, attn_tp: int = 1) -> "AfdTopology":
-        """Even split of `world` GPUs into attention and expert halves (world 1 = colocated)."""
+    def for_world(world: int, attn_tp: int = 1, attn_gpus: int = 0) -> "AfdTopology":
+        """Split `world` GPUs into attention and expert GPUs: `attn_gpus` attention GPUs (0 = half
+        of them) in DP lanes of `attn_tp`, the rest expert-parallel. World 1 = colocated."""
         if world == 1:
             return AfdTopology(colocated=True)
-        half = world // 2
-        return AfdTopology(attn_dp=half // attn_tp, attn_tp=attn_tp, mlp_dp=1, mlp_tp=1, mlp_ep=world - half)
+        n_attn = attn_gpus if attn_gpus > 0 else world // 2
+        if not 0 < n_attn < world or n_attn % attn_tp != 0:
+            raise ValueError(f"cannot place {n_attn} attention GPUs (TP {attn_tp}) in a world of {world}")
+        return AfdTopology(attn_dp=n_attn // attn_tp, attn_tp=attn_tp, mlp_dp=1, mlp_tp=1, mlp_ep=world - n_attn)
 
 
 def validate_parallel_args(topo: AfdTopology, num_experts: int, num_q_heads: int, num_kv_heads: int) -> None:

@@ -1,0 +1,51 @@
+"""Benchmark suite: every configuration is well formed; the statistics match hand-computed values."""
+import json
+
+import pytest
+
+from fastafd_b200.benchmark import run_stats, suite
+
+
+def test_every_config_is_well_formed_and_has_a_command():
+    cfgs = suite.load_configs()
+    assert suite.validate(cfgs) == []
+    for name, c in cfgs["configs"].items():
+        cmd = suite.command(name, c, steps=4, warmup=3)
+        assert "bench.py" in cmd and str(c["batch"]) in cmd
+        assert ("torch.distributed.run" in cmd) == (c["gpus"] > 1)
+
+
+def test_throughput_formula_and_verdict():
+    # 4+4 GPUs, 108 requests per attention GPU, 35.008 ms per step -> 1542 tok/s/GPU
+    assert run_stats.throughput_per_gpu(108, 35.008, 4, 4) == pytest.approx(1542.5, abs=0.5)
+    # 6+2 (3:1), 106 requests, 34.735 ms -> 2289
+    assert run_stats.throughput_per_gpu(106, 34.735, 6, 2) == pytest.approx(2288.8, abs=0.5)
+    assert run_stats.verdict(35.9, 35.0)[0] == "pass"
+    assert run_stats.verdict(36.2, 35.0)[0] == "fail"
+    assert run_stats.verdict(36.2, None) == ("unrecorded", None)
+
+
+def test_decode_window_and_step_mean():
+    lines = [f"[afd-step-time] step={i} phase=prefill bucket=0 num_mb=2 ms=50.0 real=8" for i in range(3)]
+    lines += [f"[afd-step-time] step={3 + i} phase=decode bucket=8 num_mb=2 ms={10 + (i == 0) * 5:.3f} real=8" for i in range(6)]
+    lines += ["[afd-step-time] step=9 phase=decode bucket=8 num_mb=2 ms=7.000 real=5"]       # batch draining
+    s = run_stats.parse_step_lines(["noise"] + lines)
+    assert len(s) == 10
+    w = run_stats.decode_window(s)
+    assert [x.step for x in w] == [3, 4, 5, 6, 7, 8]
+    assert run_stats.step_mean(w, skip=1) == pytest.approx(10.0)
+
+
+def test_wall_period_is_inverse_slope():
+    ids = list(range(100, 200))
+    ts = [5.0 + 0.0125 * (i - 100) for i in ids]
+    assert run_stats.wall_period(ids, ts) == pytest.approx(0.0125)
+
+
+def test_evaluate_bench_line():
+    cfgs = suite.load_configs()
+    c = cfgs["configs"]["qwen3-235b-8k-1to1"]
+    line = json.dumps({"metric": "m", "value": 9046.6, "n_gpus": 8, "ms_per_step": 38.91, "e2e": {"ms_per_step": 39.7}})
+    res = suite.evaluate(c, line, 0.03)
+    assert res["verdict"] == "pass" and res["tok_s_per_gpu"] == pytest.approx(1130.8, abs=1.0)
+    assert res["vs_published"] == pytest.approx(0.733, abs=0.005)
