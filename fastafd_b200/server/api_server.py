@@ -231,6 +231,9 @@ def run_api_server(args, start_backend: Callable[[], Any], stop_backend: Callabl
     addrs = start_backend()
     manager = FrontendManager(addrs.to_tokenizer, addrs.from_tokenizer)
     app = create_app(manager, args.model_path)
+    # uvicorn re-raises the signal that stopped it once its loop has ended, which ends the
+    # process before a `finally` here could run: stop the backend from the shutdown hook too.
+    app.add_event_handler("shutdown", stop_backend)
     try:
         uvicorn.run(app, host=args.host, port=args.port, log_level=args.log_level.lower())
     finally:

@@ -100,6 +100,22 @@ def _coordinator_main(server_args: ServerArgs, addrs: Dict[str, object], world: 
         coord.shutdown()
 
 
+def _child_entry(target, args) -> None:
+    """Entry of every backend process: leave when the parent is gone (killed without running
+    its shutdown), so that no worker outlives the server holding a GPU."""
+    import multiprocessing as mp
+    import os
+    import threading
+
+    parent = mp.parent_process()
+    if parent is not None:
+        def watch():
+            parent.join()
+            os._exit(1)
+        threading.Thread(target=watch, name="parent-watch", daemon=True).start()
+    target(*args)
+
+
 class LocalSupervisor:
     def __init__(self, args: ServerArgs):
         self.args = args
@@ -149,7 +165,7 @@ class LocalSupervisor:
         return FrontendAddrs(self.addrs["front_to_tok"], self.addrs["tok_to_front"])
 
     def _spawn(self, name: str, target, args) -> None:
-        p = self.ctx.Process(target=target, args=args, name=name, daemon=True)
+        p = self.ctx.Process(target=_child_entry, args=(target, args), name=name, daemon=True)
         p.start()
         self.names[p.pid] = name
         self.procs.append(p)
