@@ -101,6 +101,7 @@ class AfdEngine:
         client, server = MoeClient(), None      # dense models: no experts to reach
         eg_status = None
         import os as _os
+        tp_heap_base = 0
         if _os.environ.get("FASTAFD_DEBUG_NULL_MOE") == "1" and cfg.is_moe:
             from .worker.moe_client import NullMoeClient
 
@@ -123,6 +124,13 @@ class AfdEngine:
                     eg_status = eg_ep.status
                 else:
                     size = ag_layout(mcfg).size if self.is_attention else eg_layout(mcfg).size
+                    fuse_tp = (self.is_attention and topo.attn_tp > 1 and cfg.hidden_size % 128 == 0
+                               and _os.environ.get("FASTAFD_TP_FUSED", "1") != "0")
+                    if fuse_tp:
+                        from .parallel.tp_fused import tp_layout
+
+                        tp_heap_base = size
+                        size += tp_layout(topo.attn_tp, rt.num_mb, self.max_comm_tokens, cfg.hidden_size).size
                     self.fabric = Fabric.ipc(size, self.device, group)
                     if self.is_attention:
                         client = FabricMoeClient(AgMoeEndpoint(mcfg, self.fabric, rank, topo.expert_ranks(), self.device, timeout_ns))
@@ -140,6 +148,13 @@ class AfdEngine:
                     server = GlooMoeServer(stage, topo.attention_ranks(), cfg.hidden_size, cfg.num_experts_per_tok,
                                            self.dtype, group)
         tp_comm = make_tp_comms(topo, rank, self.device, group)
+        if tp_comm is not None and cuda and cfg.is_moe and self.fabric is not None and self.is_attention \
+                and not self.colocated and tp_heap_base > 0:
+            from .parallel.tp_fused import TpFusedComm
+
+            lane_ranks = topo.attn_tp_group(topo.attn_lane(rank))
+            tp_comm = TpFusedComm(tp_comm, self.fabric, lane_ranks, topo.attn_tp_rank(rank), tp_heap_base, rt.num_mb,
+                                  self.max_comm_tokens, cfg.hidden_size, self.device, int(rt.flag_timeout_s * 1e9))
         if self.is_attention:
             tp_rank = 0 if self.colocated else topo.attn_tp_rank(rank)
             self.attn = AttentionWorker(cfg, rt, self.device, client, tp_rank=tp_rank, tp_size=topo.attn_tp,

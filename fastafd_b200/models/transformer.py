@@ -62,6 +62,7 @@ class AttnMeta:
     q_len: int = 1             # tokens per request in this step (decode 1, verify block)
     is_prefill: bool = False
     prefill_lens: Optional[List[int]] = None   # tokens of each request in this prefill step
+    lane: int = -1                             # micro-batch lane (per-lane buffers of fused collectives)
     state_slots: Optional[Tensor] = None       # [B] int32 GDN state slot per request
     splits: int = 1
     workspace: Optional[Tensor] = None
@@ -244,12 +245,14 @@ class AttentionStage:
         if self.cfg.layer_type(layer) == "linear":
             out = self._linear_attention(layer, x, meta, gdn)
         else:
-            out = self._full_attention(layer, x, meta, kv)
+            out = self._full_attention(layer, x, meta, kv, fuse_scatter=(self.tp_size > 1 and reduce == "scatter"))
+            if isinstance(out, tuple):          # o_proj already reduce-scattered by the fused path
+                return out[0]
         if self.tp_size > 1 and reduce != "none":
             out = self.comm.reduce_scatter(out) if reduce == "scatter" else self.comm.all_reduce(out)
         return out
 
-    def _full_attention(self, layer: int, x: Tensor, meta: AttnMeta, kv: KVPool) -> Tensor:
+    def _full_attention(self, layer: int, x: Tensor, meta: AttnMeta, kv: KVPool, fuse_scatter: bool = False):
         c, D = self.cfg, self.cfg.head_dim
         p = f"model.layers.{layer}.self_attn."
         qkv = _linear(x, self.w[p + "qkv_proj.weight"], self.w.get(p + "qkv_proj.bias"))
@@ -281,7 +284,12 @@ class AttentionStage:
         o = o.reshape(T, self.hq * D)
         if gate is not None:
             o = (o.float() * torch.sigmoid(gate.float())).to(o.dtype)
-        return _linear(o, self.w[p + "o_proj.weight"])
+        w_o = self.w[p + "o_proj.weight"]
+        if (fuse_scatter and meta.lane >= 0 and o.is_cuda and o.dtype == torch.bfloat16
+                and hasattr(self.comm, "oproj_reduce_scatter") and self.comm.can_fuse_oproj(T, o.shape[1])):
+            # GEMM epilogue pushes the partial rows to their owners; returns this rank's summed rows
+            return (self.comm.oproj_reduce_scatter(meta.lane, o.contiguous(), w_o),)
+        return _linear(o, w_o)
 
     def _prefill_attention(self, q: Tensor, kc: Tensor, vc: Tensor, meta: AttnMeta, scale: float, page_size: int) -> Tensor:
         """Causal attention of each request's new chunk against its paged KV (which already holds

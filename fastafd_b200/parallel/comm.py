@@ -27,7 +27,9 @@ class TpComm:
     def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
         return x
 
-    def all_gather(self, x: torch.Tensor) -> torch.Tensor:
+    def all_gather(self, x: torch.Tensor, lane: int = -1) -> torch.Tensor:
+        """Concatenate the ranks' rows. `lane` names the micro-batch for communicators that keep
+        per-lane buffers; the others ignore it."""
         return x
 
     def all_gather_last_dim(self, x: torch.Tensor) -> torch.Tensor:
@@ -47,7 +49,7 @@ class TorchDistComm(TpComm):
         dist.all_reduce(x, group=self.group)
         return x
 
-    def all_gather(self, x):
+    def all_gather(self, x, lane: int = -1):
         x = x.contiguous()
         out = torch.empty(self.size * x.shape[0], *x.shape[1:], dtype=x.dtype, device=x.device)
         dist.all_gather_into_tensor(out, x, group=self.group) if x.is_cuda else \
@@ -117,7 +119,7 @@ class NcclComm(TpComm):
                                                  _DTYPES[x.dtype], self._stream()), "all_reduce")
         return x
 
-    def all_gather(self, x):
+    def all_gather(self, x, lane: int = -1):
         x = x.contiguous()
         out = torch.empty(self.size * x.shape[0], *x.shape[1:], dtype=x.dtype, device=x.device)
         self._check(self.lib.afd_nccl_all_gather(self.handle, C.c_void_p(x.data_ptr()), C.c_void_p(out.data_ptr()),

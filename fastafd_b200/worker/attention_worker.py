@@ -206,7 +206,7 @@ class AttentionWorker:
         fused = (moe and self.cuda and not mb.meta.is_prefill and c.n_group == 1
                  and self.client.can_fuse_route(mb.Tl, c.num_experts, c.hidden_size))
         with nvtx_range(f"AFD_AG_Attn_L{layer}_mb{mb.lane}"):
-            x_in = self.tp.all_gather(mb.normed) if self.tp.size > 1 else mb.normed
+            x_in = self.tp.all_gather(mb.normed, lane=mb.lane) if self.tp.size > 1 else mb.normed
             attn_out = m.attention(layer, x_in, mb.meta, self.kv, self.gdn, reduce="scatter")
             if fused:
                 p = f"model.layers.{layer}."
@@ -304,7 +304,7 @@ class AttentionWorker:
         b = self.bufs[lane]
         T = bucket * q_len
         meta = AttnMeta(positions=b.positions[:T], out_loc=b.out_loc[:T], page_table=b.page_table[:bucket],
-                        seq_lens=b.seq_lens[:bucket], q_len=q_len, state_slots=b.rows[:bucket].to(torch.int32) if self.gdn else None,
+                        seq_lens=b.seq_lens[:bucket], q_len=q_len, lane=lane, state_slots=b.rows[:bucket].to(torch.int32) if self.gdn else None,
                         status=self.status)
         if self.cuda:
             max_kv = self.max_seq_len
@@ -414,7 +414,10 @@ class AttentionWorker:
                 for lane in range(self.num_mb):
                     b = self.bufs[lane]
                     b.host_out[slot, :bucket].copy_(b.next_tokens[:bucket], non_blocking=True)
-                for i, st in enumerate([self.status] + self.client.status_tensors()):
+                words = [self.status] + self.client.status_tensors()
+                if getattr(self.tp, "status", None) is not None:
+                    words.append(self.tp.status)
+                for i, st in enumerate(words[:self.status_host.shape[1]]):
                     self.status_host[slot, i:i + 1].copy_(st, non_blocking=True)
                 self.d2h_events[slot].record()
 
@@ -471,7 +474,7 @@ class AttentionWorker:
                                 torch.zeros(0, self.max_pages, dtype=torch.int32, device=dev),
                                 seq_lens=torch.from_numpy(mbp.seq_lens).to(dev), is_prefill=True,
                                 prefill_lens=[int(n) for n in mbp.extend_lens],
-                                state_slots=rows_t.to(torch.int32), status=self.status)
+                                state_slots=rows_t.to(torch.int32), status=self.status, lane=lane)
                 mb = self.make_ctx(lane, torch.from_numpy(ids).to(dev), meta)
                 mb.pad_from = T_real
                 if self.spec is not None:
@@ -532,4 +535,7 @@ class AttentionWorker:
         code = int(self.status.item()) if self.status is not None else 0
         for s in self.client.status_tensors():
             code = code or int(s.item())
+        tp_status = getattr(self.tp, "status", None)       # fused TP collectives keep their own word
+        if tp_status is not None:
+            code = code or int(tp_status.item())
         return code

@@ -155,3 +155,43 @@ def test_fused_route_dispatch_matches_separate_ops(scoring, gate_fp32):
         assert int(eg.n2m_flag[0][0]) == 1
     for f in fabs:
         f.close()
+
+
+# ------------------------------------------------------------- fused attention-TP collectives
+@pytest.mark.parametrize("tp,T,K", [(2, 32, 512), (4, 64, 1024), (2, 24, 256)])
+def test_tp_fused_oproj_reduce_scatter_and_all_gather_loopback(tp, T, K):
+    """tp ranks emulated on one GPU over a local fabric: every producer launch is queued before
+    any consumer launch (kernels that wait for one another never run as separate launches on one
+    GPU). The fused o_proj -> reduce-scatter must equal the fp32 sum of the partial GEMMs, the
+    all-gather the concatenation of the ranks' rows; two rounds check the epoch protocol."""
+    from fastafd_b200.parallel.fabric import Fabric
+    from fastafd_b200.parallel.tp_fused import TpFusedComm, tp_layout
+
+    H, lanes, cap = 256, 2, 32
+    Tl = T // tp
+    size = tp_layout(tp, lanes, cap, H).size
+    fabs = Fabric.local([size] * tp, DEV)
+    comms = [TpFusedComm(None, fabs[r], list(range(tp)), r, 0, lanes, cap, H, DEV, timeout_ns=int(2e9))
+             for r in range(tp)]
+    g = torch.Generator(device="cpu").manual_seed(tp * 100 + T)
+    for rnd in range(2):
+        lane = rnd % lanes
+        o = [(torch.randn(T, K, generator=g) * 0.5).to(torch.bfloat16).to(DEV) for _ in range(tp)]
+        w = [(torch.randn(H, K, generator=g) * 0.1).to(torch.bfloat16).to(DEV) for _ in range(tp)]
+        for r in range(tp):
+            comms[r].oproj_push(lane, o[r], w[r])
+        ys = [comms[r].reduce_wait(lane, Tl) for r in range(tp)]
+        torch.cuda.synchronize()
+        full = sum((o[r].float() @ w[r].float().t()).to(torch.bfloat16).float() for r in range(tp))
+        for r in range(tp):
+            assert int(comms[r].status) == 0
+            torch.testing.assert_close(ys[r].float(), full[r * Tl:(r + 1) * Tl], atol=3e-2, rtol=3e-2)
+        xs = [(torch.randn(Tl, H, generator=g)).to(torch.bfloat16).to(DEV) for _ in range(tp)]
+        for r in range(tp):
+            comms[r].gather_push(lane, xs[r])
+        got = [comms[r].gather_wait(lane, Tl).clone() for r in range(tp)]
+        torch.cuda.synchronize()
+        want = torch.cat(xs, 0)
+        for r in range(tp):
+            assert int(comms[r].status) == 0
+            assert torch.equal(got[r], want)

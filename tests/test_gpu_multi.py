@@ -33,7 +33,7 @@ def _prompts(cfg):
     return [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (32, 17, 5, 40, 9, 23)]
 
 
-def _worker(rank, world, port, out_path, n_new, tp=1):
+def _worker(rank, world, port, out_path, n_new, tp=1, tp_fused="1"):
     import torch.distributed as dist
     from fastafd_b200.core import SamplingParams
     from fastafd_b200.engine import AfdEngine, SpmdDriver
@@ -41,6 +41,7 @@ def _worker(rank, world, port, out_path, n_new, tp=1):
 
     os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
     os.environ["NCCL_NVLS_ENABLE"] = "0"
+    os.environ["FASTAFD_TP_FUSED"] = tp_fused
     torch.cuda.set_device(rank)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     cfg = _cfg()
@@ -74,10 +75,13 @@ def test_disaggregated_equals_colocated(world):
     assert got == exp
 
 
-def test_attention_tp2_tracks_colocated():
-    """4 GPUs: one attention lane over 2 TP ranks (token-sharded residual stream, NCCL
-    reduce-scatter / all-gather) + 2 expert ranks. bf16 sums are ordered differently than on one
-    GPU, so tokens are compared with a tolerance."""
+@pytest.mark.parametrize("tp_fused", ["1", "0"], ids=["fabric-fused", "nccl"])
+def test_attention_tp2_tracks_colocated(tp_fused):
+    """4 GPUs: one attention lane over 2 TP ranks (token-sharded residual stream) + 2 expert
+    ranks. The per-layer collectives run either fused with their GEMMs over the fabric (o_proj
+    epilogue -> peer stores -> sum; all-gather by peer stores) or as NCCL reduce-scatter /
+    all-gather. bf16 sums are ordered differently than on one GPU, so tokens are compared with a
+    tolerance."""
     if torch.cuda.device_count() < 4:
         pytest.skip("needs 4 GPUs")
     import torch.multiprocessing as mp
@@ -91,7 +95,7 @@ def test_attention_tp2_tracks_colocated():
     single.close()
     with tempfile.TemporaryDirectory() as d:
         path = os.path.join(d, "out.pt")
-        mp.spawn(_worker, args=(4, _free_port(), path, n_new, 2), nprocs=4, join=True)
+        mp.spawn(_worker, args=(4, _free_port(), path, n_new, 2, tp_fused), nprocs=4, join=True)
         got = torch.load(path)
     same = sum(a == b for g, e in zip(got, exp) for a, b in zip(g, e))
     assert same >= 0.7 * sum(len(e) for e in exp), (got, exp)
