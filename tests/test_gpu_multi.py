@@ -97,5 +97,69 @@ def test_attention_tp2_tracks_colocated(tp_fused):
         path = os.path.join(d, "out.pt")
         mp.spawn(_worker, args=(4, _free_port(), path, n_new, 2, tp_fused), nprocs=4, join=True)
         got = torch.load(path)
+    # Random weights make generation chaotic after the first near-tie, so agreement is judged on
+    # the first tokens (prefill + one decode step, no accumulated divergence) and loosely overall.
+    first = sum(g[:2] == e[:2] for g, e in zip(got, exp))
     same = sum(a == b for g, e in zip(got, exp) for a, b in zip(g, e))
-    assert same >= 0.7 * sum(len(e) for e in exp), (got, exp)
+    assert first >= len(exp) - 1, (got, exp)
+    assert same >= 0.5 * sum(len(e) for e in exp), (got, exp)
+
+
+def _tp_stress_worker(rank, world, port, out_path, rounds):
+    """Every rank of a TP group runs `rounds` reduce-scatter / all-gather pairs on two lanes
+    back to back without host synchronisation, then checks its results against values computed
+    from the shared seed."""
+    import torch.distributed as dist
+    from fastafd_b200.parallel.fabric import Fabric
+    from fastafd_b200.parallel.tp_fused import TpFusedComm, tp_layout
+
+    os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    H, K, T, lanes, cap = 512, 512, 32, 2, 16
+    Tl = T // world
+    fab = Fabric.ipc(tp_layout(world, lanes, cap, H).size, dev, None)
+    comm = TpFusedComm(None, fab, list(range(world)), rank, 0, lanes, cap, H, dev, timeout_ns=int(5e9))
+    g = torch.Generator().manual_seed(7)
+    o_all = [(torch.randn(world, T, K, generator=g) * 0.5).to(torch.bfloat16) for _ in range(rounds)]
+    w_all = (torch.randn(world, H, K, generator=g) * 0.1).to(torch.bfloat16)
+    x_all = [torch.randn(world, Tl, H, generator=g).to(torch.bfloat16) for _ in range(rounds)]
+    w_dev = w_all[rank].to(dev)
+    o_dev = [o[rank].to(dev) for o in o_all]
+    x_dev = [x[rank].to(dev) for x in x_all]
+    dist.barrier()
+    ys, gs = [], []
+    for i in range(rounds):
+        lane = i % lanes
+        gs.append(comm.all_gather_rows(lane, x_dev[i]).clone())
+        ys.append(comm.oproj_reduce_scatter(lane, o_dev[i], w_dev))
+    torch.cuda.synchronize()
+    bad = int(comm.status.item())
+    errs = 0
+    for i in range(rounds):
+        want_g = x_all[i].reshape(world * Tl, H).to(dev)
+        errs += int(not torch.equal(gs[i], want_g))
+        full = sum((o_all[i][r].float() @ w_all[r].float().t()).to(torch.bfloat16).float() for r in range(world))
+        want_y = full[rank * Tl:(rank + 1) * Tl].to(dev)
+        errs += int(not torch.allclose(ys[i].float(), want_y, atol=3e-2, rtol=3e-2))
+    res = torch.tensor([bad, errs])
+    out = [torch.zeros(2, dtype=torch.int64) for _ in range(world)]
+    dist.all_gather(out, res)
+    if rank == 0:
+        torch.save(torch.stack(out), out_path)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_tp_fused_collectives_stress(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch.multiprocessing as mp
+
+    with tempfile.TemporaryDirectory() as d:
+        path = os.path.join(d, "out.pt")
+        mp.spawn(_tp_stress_worker, args=(world, _free_port(), path, 200), nprocs=world, join=True)
+        res = torch.load(path)
+    assert res.sum().item() == 0, res
