@@ -51,3 +51,28 @@ def test_smoke_entry():
     from fastafd_b200.smoke import run_smoke
 
     run_smoke()
+
+
+@pytest.mark.parametrize("block", [2, 4])
+def test_speculative_decoding_on_gpu_tracks_plain_greedy(block):
+    """EAGLE-3 style verify steps on the GPU (multi-token attention kernel, dispatch with a given
+    routing, greedy acceptance): the emitted tokens are the target model's own greedy tokens, so
+    they must follow plain greedy decoding. In bf16 a verify step scores several positions in one
+    pass (different reduction order than one-token steps), so a near-tie may flip a token; the
+    comparison is by common prefix."""
+    cfg = PRESETS["tiny-qwen3-moe"]
+    g = torch.Generator().manual_seed(0)
+    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (30, 7, 18, 25)]
+    sp = SamplingParams(max_tokens=12, ignore_eos=True)
+    kw = dict(max_seq_len=160, num_pages=96, max_running_requests=8)
+    plain_eng = AfdEngine(cfg, _rt("cuda:0", False, **kw), AfdTopology(colocated=True), 0, "cuda:0", seed=0)
+    plain = SpmdDriver(plain_eng).generate(prompts, sp)
+    plain_eng.close()
+    eng = AfdEngine(cfg, _rt("cuda:0", False, spec_block=block, **kw), AfdTopology(colocated=True), 0, "cuda:0", seed=0)
+    spec = SpmdDriver(eng).generate(prompts, sp)
+    hist, mean = eng.attn.spec.accept_hist.sum(), eng.attn.spec.mean_accept()
+    eng.close()
+    assert [len(s) for s in spec] == [len(p) for p in plain]
+    prefix = sum(next((i for i, (a, b) in enumerate(zip(s, p)) if a != b), len(p)) for s, p in zip(spec, plain))
+    assert prefix >= 0.7 * sum(len(p) for p in plain), (spec, plain)
+    assert hist > 0 and 1.0 <= mean <= block

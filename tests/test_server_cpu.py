@@ -146,3 +146,17 @@ def test_step_profiler_window_and_client_summary():
     assert abs(tr.ttft - 0.5) < 1e-9 and abs(tr.tpot - 0.1) < 1e-9
     s = summarize([tr, RequestTrace(start=0.0, error="x")], 1.0)
     assert s["failed"] == 1 and s["output_tokens"] == 3 and s["tpot_ms_p50"] == 100.0
+
+
+def test_interactive_shell_keeps_context_and_resets():
+    import io
+
+    from fastafd_b200.llm import LLM
+    from fastafd_b200.shell import run_shell
+
+    llm = LLM("tiny-qwen3-moe", device="cpu", max_seq_len=128, num_pages=64, max_running_requests=4, cuda_graph_max_bs=4)
+    out = io.StringIO()
+    turns = run_shell(llm, max_tokens=4, inp=io.StringIO("hello there\n\nagain\n/reset\nthird\n/exit\nnot read\n"), out=out)
+    assert turns == 3
+    assert "(conversation cleared)" in out.getvalue()
+    assert out.getvalue().count(">>> ") == 6
