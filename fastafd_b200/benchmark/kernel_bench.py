@@ -128,6 +128,50 @@ def bench_gemm(a):
            extra={"E": E, "N": N, "K": K, "rows": row, "block_tok": bt})
 
 
+def time_graph(launch_all, n_launches: int, reps: int = 5) -> float:
+    """Device time per launch (us) of a sequence captured into one CUDA graph: removes the host
+    launch cost that dominates event timing of kernels of a few microseconds."""
+    launch_all()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        launch_all()
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize()
+    best = float("inf")
+    for _ in range(reps):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        best = min(best, e0.elapsed_time(e1) * 1e3 / n_launches)
+    return best
+
+
+def bench_dense(a):
+    """Decode-shaped dense GEMM out[M,N] = x[M,K] @ w[N,K]^T: the tcgen05 kernel (weights on the
+    UMMA M side) against cuBLAS through torch. Weights rotate over enough copies to exceed the L2."""
+    dev = "cuda"
+    M, N, K = a.tokens, a.n, a.k
+    copies = max(2, int(160e6 // (N * K * 2)) + 1)
+    ws = [(torch.randn(N, K, device=dev, dtype=torch.bfloat16) * 0.05) for _ in range(copies)]
+    x = torch.randn(M, K, device=dev, dtype=torch.bfloat16)
+    ref_out = torch.nn.functional.linear(x, ws[0])
+    got = ops.dense_gemm(x, ws[0])
+    torch.cuda.synchronize()
+    err = (got.float() - ref_out.float()).abs().max().item()
+    own = time_graph(lambda: [ops.dense_gemm(x, w) for w in ws], copies)
+    lib_t = time_graph(lambda: [torch.nn.functional.linear(x, w) for w in ws], copies)
+    hbm, _, how = measured_peaks()
+    wbytes = N * K * 2
+    print(json.dumps({"kernel": "dense_gemm", "M": M, "N": N, "K": K, "us_own_tcgen05": round(own, 2),
+                      "us_cublas": round(lib_t, 2), f"own_frac_of_{how}_hbm": round(wbytes / own / 1e3 / hbm, 3),
+                      f"cublas_frac_of_{how}_hbm": round(wbytes / lib_t / 1e3 / hbm, 3), "max_abs_diff": round(err, 4),
+                      "weight_copies": copies}))
+
+
 def bench_route(a):
     from ..moe.afd_moe import AgMoeEndpoint, MoeCommConfig, ag_layout, eg_layout
     from ..parallel.fabric import Fabric
@@ -170,6 +214,10 @@ def main(argv=None):
     p.add_argument("--block-tok", type=int, default=16)
     p.add_argument("--swiglu", action="store_true")
     p.add_argument("--fp8", action="store_true")
+    p = sub.add_parser("dense")
+    p.add_argument("--tokens", type=int, default=32)
+    p.add_argument("--n", type=int, default=5120)
+    p.add_argument("--k", type=int, default=2048)
     p = sub.add_parser("route")
     p.add_argument("--tokens", type=int, default=32)
     p.add_argument("--experts", type=int, default=128)
@@ -177,7 +225,7 @@ def main(argv=None):
     p.add_argument("--topk", type=int, default=8)
     p.add_argument("--num-eg", type=int, default=4)
     a = ap.parse_args(argv)
-    {"attention": bench_attention, "gemm": bench_gemm, "route": bench_route}[a.case](a)
+    {"attention": bench_attention, "gemm": bench_gemm, "route": bench_route, "dense": bench_dense}[a.case](a)
 
 
 if __name__ == "__main__":

@@ -121,10 +121,17 @@ def test_combine_times_out_when_expert_rank_is_silent():
         f.close()
 
 
-@pytest.mark.parametrize("scoring,gate_fp32", [("softmax", False), ("sigmoid", True)])
-def test_fused_route_dispatch_matches_separate_ops(scoring, gate_fp32):
+@pytest.mark.parametrize("scoring,gate_fp32,H,E,K", [
+    ("softmax", False, 512, 16, 4),        # FMA logits loop (shape outside the tensor-core GEMV)
+    ("sigmoid", True, 512, 16, 4),         # fp32 gate
+    ("softmax", False, 2048, 128, 8),      # tensor-core GEMV: 8 expert tiles x 4 slices of H
+    ("softmax", False, 4096, 512, 10),     # 32 expert tiles, one slice
+    ("sigmoid", False, 1024, 64, 6),       # 4 expert tiles x 8 slices
+    ("softmax", False, 2048, 120, 8),      # 120 experts: last tile partly empty, 8 tiles
+])
+def test_fused_route_dispatch_matches_separate_ops(scoring, gate_fp32, H, E, K):
     """residual add + RMSNorm + router + push in one launch == the four separate ops."""
-    H, I, E, K, T = 512, 256, 16, 4, 19
+    I, T = 256, 19
     cfg = MoeCommConfig(num_ag=1, num_eg=2, num_lanes=1, max_tokens=32, hidden=H, topk=K, num_experts=E,
                         intermediate=I, block_tok=16)
     fabs, ags, egs = _setup(cfg)
