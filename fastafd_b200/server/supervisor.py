@@ -100,6 +100,24 @@ def _coordinator_main(server_args: ServerArgs, addrs: Dict[str, object], world: 
         coord.shutdown()
 
 
+def make_addresses(world: int, probe_host: str = "127.0.0.1", head_host: str = "127.0.0.1",
+                   rank_hosts: Optional[Dict[int, str]] = None):
+    """ZMQ endpoints of one server: a command queue per worker rank (bound on that rank's node),
+    the shared reply queue and the tokenizer queues on the head node. Returns (addresses, ports);
+    ports[world + 5] is the torch.distributed rendezvous port."""
+    ports = pick_free_ports(world + 6, probe_host)
+    rank_hosts = rank_hosts or {}
+    tcp = lambda h, p: f"tcp://{h}:{p}"  # noqa: E731
+    addrs = {
+        "cmd": {r: tcp(rank_hosts.get(r, head_host), ports[r]) for r in range(world)},
+        "reply": tcp(head_host, ports[world]),
+        "front_to_tok": tcp(head_host, ports[world + 1]), "tok_to_front": tcp(head_host, ports[world + 2]),
+        "tok_to_backend": tcp(head_host, ports[world + 3]), "backend_to_tok": tcp(head_host, ports[world + 4]),
+        "master_addr": head_host,
+    }
+    return addrs, ports
+
+
 def _child_entry(target, args) -> None:
     """Entry of every backend process: leave when the parent is gone (killed without running
     its shutdown), so that no worker outlives the server holding a GPU."""
@@ -133,15 +151,21 @@ class LocalSupervisor:
 
         a = self.args
         world = a.topology.world
-        ports = pick_free_ports(world + 6, a.host if a.host != "0.0.0.0" else "127.0.0.1")
-        tcp = lambda p: f"tcp://127.0.0.1:{p}"  # noqa: E731
-        self.addrs = {
-            "cmd": {r: tcp(ports[r]) for r in range(world)},
-            "reply": tcp(ports[world]),
-            "front_to_tok": tcp(ports[world + 1]), "tok_to_front": tcp(ports[world + 2]),
-            "tok_to_backend": tcp(ports[world + 3]), "backend_to_tok": tcp(ports[world + 4]),
-        }
+        self.addrs, ports = make_addresses(world, a.host if a.host != "0.0.0.0" else "127.0.0.1")
         master_port = ports[world + 5]
+        for r in range(world):
+            self._spawn(f"worker{r}", worker_main, (r, world, a, self.addrs, master_port))
+        return self.start_frontend_side(self.addrs)
+
+    def start_frontend_side(self, addrs: Dict[str, object]) -> FrontendAddrs:
+        """Tokenizer and coordinator processes on this node; the workers are already starting
+        (here, or as remote actors under the multi-node supervisor)."""
+        from ..config import get_model_config
+        from ..tokenizer import tokenize_worker
+
+        a = self.args
+        world = a.topology.world
+        self.addrs = addrs
         cfg = get_model_config(a.model_path)
         rt = a.runtime_config()
         tok_ready, coord_ready = self.ctx.Event(), self.ctx.Event()
@@ -149,8 +173,6 @@ class LocalSupervisor:
                                                    self.addrs["front_to_tok"], self.addrs["tok_to_backend"],
                                                    self.addrs["backend_to_tok"], self.addrs["tok_to_front"], tok_ready))
         self._spawn("coordinator", _coordinator_main, (a, self.addrs, world, coord_ready, self.stop_evt))
-        for r in range(world):
-            self._spawn(f"worker{r}", worker_main, (r, world, a, self.addrs, master_port))
         deadline = time.monotonic() + ENV.STARTUP_TIMEOUT_S.value
         while not (tok_ready.is_set() and coord_ready.is_set()):
             dead = self.get_failures()
@@ -202,5 +224,11 @@ class LocalSupervisor:
                 p.kill()
 
 
-def create_backend_supervisor(args: ServerArgs) -> LocalSupervisor:
+def create_backend_supervisor(args: ServerArgs):
+    """`--launch-backend mp` (default): processes on this node; `ray`: one actor per rank across a
+    Ray cluster (raises where Ray is not installed)."""
+    if getattr(args, "launch_backend", "mp") == "ray":
+        from .supervisor_ray import RaySupervisor
+
+        return RaySupervisor(args)
     return LocalSupervisor(args)

@@ -40,7 +40,8 @@ def worker_main(rank: int, world: int, server_args, addrs: Dict[str, object], ma
             device = torch.device("cpu")
             torch.set_num_threads(1)
         if world > 1:
-            os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(master_port)
+            os.environ["MASTER_ADDR"] = str(addrs.get("master_addr", "127.0.0.1"))     # the head node under a multi-node launch
+            os.environ["MASTER_PORT"] = str(master_port)
             dist.init_process_group("cpu:gloo,cuda:nccl" if cuda else "gloo", rank=rank, world_size=world,
                                     **({"device_id": device} if cuda else {}))
         engine = AfdEngine(cfg, rt, topo, rank, device, seed=server_args.seed, fast_init=cuda,

@@ -1,0 +1,63 @@
+"""Multi-node launch planning on fake node reports: placement, forwarded environment, version
+guard, and the refusal where Ray is missing."""
+import pytest
+
+from fastafd_b200.protocol import AfdTopology
+from fastafd_b200.server import supervisor_ray as sr
+
+
+def _nodes(*gpus, head=0):
+    return [sr.NodeReport(address=f"10.0.0.{i + 1}", gpus=g, is_head=(i == head),
+                          versions={"torch": "2.11", "cuda": "12.8", "package": "0.1.0"}) for i, g in enumerate(gpus)]
+
+
+def test_placement_fills_head_first_and_keeps_tp_groups_on_one_node():
+    topo = AfdTopology(attn_dp=2, attn_tp=2, mlp_ep=4)          # 4 attention + 4 expert ranks
+    plan = sr.plan_placement(_nodes(4, 4, head=1), topo)
+    assert [s.rank for s in plan] == list(range(8))
+    assert [s.role for s in plan] == ["attention"] * 4 + ["expert"] * 4
+    assert {s.node for s in plan[:4]} == {"10.0.0.2"}           # the head node is taken first
+    assert {s.node for s in plan[4:]} == {"10.0.0.1"}
+    assert sorted(s.gpu for s in plan[:4]) == [0, 1, 2, 3]
+    # a TP group does not straddle nodes: 3 + 3 GPUs cannot hold two TP-2 lanes + 2 experts on the
+    # first node, so the second lane moves to the next node as a whole
+    plan = sr.plan_placement(_nodes(3, 3), AfdTopology(attn_dp=2, attn_tp=2, mlp_ep=2))
+    lanes = [{s.node for s in plan if s.rank in (0, 1)}, {s.node for s in plan if s.rank in (2, 3)}]
+    assert all(len(l) == 1 for l in lanes) and lanes[0] != lanes[1]
+    assert len({(s.node, s.gpu) for s in plan}) == 6
+
+
+def test_placement_refuses_what_does_not_fit():
+    with pytest.raises(ValueError, match="need 8 GPUs"):
+        sr.plan_placement(_nodes(4, 2), AfdTopology(attn_dp=4, attn_tp=1, mlp_ep=4))
+    with pytest.raises(ValueError, match="tensor-parallel group"):
+        sr.plan_placement(_nodes(2, 2, 2, 2, 2), AfdTopology(attn_dp=1, attn_tp=4, mlp_ep=4))
+
+
+def test_actor_env_forwards_knobs_but_not_node_scoped_keys():
+    env = {"FASTAFD_NUM_MB": "2", "MINISGL_AFD_MODE": "cad", "NCCL_DEBUG": "INFO", "CUDA_VISIBLE_DEVICES": "3",
+           "TMPDIR": "/scratch", "HOME": "/root", "PYTHONPATH": "/x", "FASTAFD_LOG_DIR": "/logs", "MY_FLAG": "1"}
+    out = sr.actor_env(env, extra_keys=("MY_FLAG",))
+    assert out == {"FASTAFD_NUM_MB": "2", "MINISGL_AFD_MODE": "cad", "NCCL_DEBUG": "INFO", "PYTHONPATH": "/x", "MY_FLAG": "1"}
+
+
+def test_version_guard_names_the_node_that_differs():
+    nodes = _nodes(4, 4)
+    assert sr.check_runtime_versions(nodes) == []
+    odd = sr.NodeReport(address="10.0.0.9", gpus=4, versions={"torch": "2.10", "cuda": "12.8", "package": "0.1.0"})
+    problems = sr.check_runtime_versions(nodes + [odd])
+    assert len(problems) == 1 and "10.0.0.9" in problems[0] and "torch" in problems[0]
+
+
+def test_ray_backend_is_refused_where_ray_is_missing():
+    try:
+        import ray  # noqa: F401
+        pytest.skip("ray is installed here")
+    except ImportError:
+        pass
+    from fastafd_b200.server.args import parse_args
+
+    with pytest.raises(ValueError, match="ray"):                  # refused when the flags are parsed
+        parse_args(["--mode", "afd-serve", "--model-path", "tiny-qwen3-moe", "--device", "cpu", "--launch-backend", "ray"])
+    with pytest.raises(sr.RayUnavailable):                        # and by the supervisor itself
+        sr.RaySupervisor(server_args=None)
