@@ -265,14 +265,23 @@ def grouped_gemm(*, w, x, num_experts, n_per_expert, k, tile_info, num_tok_tiles
     check(lib().afd_grouped_gemm(C.byref(d), cur_stream()), "grouped_gemm")
 
 
-def dense_gemm(x: torch.Tensor, w: torch.Tensor, block_tok: Optional[int] = None, status=None):
-    """out = x @ w.T on the tcgen05 path (bf16, N % 128 == 0, K % 64 == 0)."""
+_DENSE_SCHEDULES: dict = {}
+
+
+def dense_gemm(x: torch.Tensor, w: torch.Tensor, block_tok: Optional[int] = None, status=None,
+               out: Optional[torch.Tensor] = None):
+    """out = x @ w.T on the tcgen05 path (bf16, N % 128 == 0, K % 64 == 0). The tile schedule of a
+    shape is built once and kept on the device, so later calls can be captured into a CUDA graph."""
     M, K = x.shape
     N = w.shape[0]
     if block_tok is None:
         block_tok = 16 if M <= 16 else 32 if M <= 32 else 64 if M <= 64 else 128
-    info, n = dense_tile_schedule(M, block_tok, x.device)
-    out = torch.empty(M, N, dtype=torch.bfloat16, device=x.device)
+    key = (M, block_tok, x.device)
+    if key not in _DENSE_SCHEDULES:
+        _DENSE_SCHEDULES[key] = dense_tile_schedule(M, block_tok, x.device)
+    info, n = _DENSE_SCHEDULES[key]
+    if out is None:
+        out = torch.empty(M, N, dtype=torch.bfloat16, device=x.device)
     grouped_gemm(w=w, x=x, num_experts=1, n_per_expert=N, k=K, tile_info=info, num_tok_tiles=n,
                  block_tok=block_tok, epilogue=EPI_STORE, out=out, out_ld=N, status=status)
     return out
