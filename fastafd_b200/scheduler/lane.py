@@ -65,6 +65,8 @@ class LaneScheduler:
         self.records: Dict[int, StepRecord] = {}
         self._pending_free_rows: List[int] = []
         self._carry_grants: List[Tuple[int, int, int]] = []     # grants made outside a plan
+        from ..env import ENV
+        self.page_audit = bool(ENV.PAGE_AUDIT.value)
 
     # ------------------------------------------------------------------ admission
     def add_req(self, uid: int, input_ids: Sequence[int], sampling: SamplingParams) -> None:
@@ -193,6 +195,8 @@ class LaneScheduler:
             plan.top_ks = np.asarray([-1 if s is None else s.req.sampling.top_k for s in sampling_rows], np.int32)
             plan.top_ps = np.asarray([1.0 if s is None else s.req.sampling.top_p for s in sampling_rows], np.float32)
         self.records[step_id] = record
+        if self.page_audit:
+            self.audit_pages()
         return plan
 
     def schedule_prefill(self, step_id: int) -> AgStepPlan:
@@ -355,6 +359,8 @@ class LaneScheduler:
                 out.append((uid, new, finished))
                 if finished:
                     self._retire(st)
+        if self.page_audit:
+            self.audit_pages()
         return out
 
     def check_integrity(self) -> None:
@@ -362,3 +368,36 @@ class LaneScheduler:
         rows = [s.req.table_idx for s in self.states.values()]
         if len(set(rows)) != len(rows) or set(rows) & set(self.free_rows):
             raise RuntimeError("request table rows corrupted")
+
+    def audit_pages(self) -> None:
+        """Page ledger audit (``FASTAFD_PAGE_AUDIT=1`` runs it after every planned and every
+        completed step): no page is both free and held, a page is held by two requests only as a
+        shared cached prefix, every request holds enough pages for its planned length, and free +
+        held + cached-only pages account for the whole pool.
+        Reference: the PAGE_AUDIT knob of python/minisgl/afd_scheduler.py."""
+        self.check_integrity()
+        c = self.cache
+        free = set(int(p) for p in c._free[:c._n_free])
+        held: Dict[int, int] = {}
+        for st in self.states.values():
+            need = c.pages_for(st.planned_len)
+            if len(st.req.pages) < need:
+                raise RuntimeError(f"page audit: request {st.req.uid} holds {len(st.req.pages)} pages, needs {need}")
+            for p in st.req.pages:
+                if p <= 0 or p >= c.num_pages:
+                    raise RuntimeError(f"page audit: request {st.req.uid} holds page {p} outside the pool")
+                held[p] = held.get(p, 0) + 1
+        both = free & set(held)
+        if both:
+            raise RuntimeError(f"page audit: pages {sorted(both)[:8]} are free and held at once")
+        cached = set()
+        if hasattr(c, "_iter_nodes"):
+            cached = {int(n.page) for n in c._iter_nodes()}
+            if cached & free:
+                raise RuntimeError("page audit: a cached page is on the free list")
+        shared_wrongly = [p for p, n in held.items() if n > 1 and p not in cached]
+        if shared_wrongly:
+            raise RuntimeError(f"page audit: pages {sorted(shared_wrongly)[:8]} are held twice without being a cached prefix")
+        accounted = len(free) + len(set(held) | cached)
+        if accounted != c.num_pages - 1:
+            raise RuntimeError(f"page audit: {accounted} pages accounted for, the pool has {c.num_pages - 1}")

@@ -136,3 +136,33 @@ def test_native_mismatch_matches_numpy():
         assert cache.mismatch_index(a, a.copy()) == 4096
         assert cache.mismatch_index(a, a[:100].copy()) == 100
     assert cache._host_lib() is not None, "the host helper library should build with g++"
+
+
+@pytest.mark.parametrize("cache_type", ["naive", "radix"])
+def test_page_audit_runs_every_step_and_catches_a_corrupted_ledger(monkeypatch, cache_type):
+    import numpy as np
+
+    from fastafd_b200.core import SamplingParams
+    from fastafd_b200.scheduler.lane import LaneScheduler
+
+    monkeypatch.setenv("FASTAFD_PAGE_AUDIT", "1")
+    s = LaneScheduler(0, num_pages=64, page_size=4, max_running=4, max_seq_len=64, num_mb=2, cache_type=cache_type)
+    assert s.page_audit
+    shared = list(range(100, 112))
+    for uid in range(3):
+        s.add_req(uid, shared + [200 + uid, 300 + uid], SamplingParams(max_tokens=6, ignore_eos=True))
+    step = 0
+    while not s.idle():
+        plan = s.schedule_prefill(step) if s.has_prefill() else s.schedule_decode(step, 4)
+        n = sum(len(m.rows) for m in plan.mbs)
+        s.complete(step, np.full(n, 7, dtype=np.int32))           # audits inside plan and complete
+        step += 1
+    s.audit_pages()
+    # a page that is free and held at once must be reported
+    s.add_req(9, shared + [1, 2, 3], SamplingParams(max_tokens=2, ignore_eos=True))
+    s.schedule_prefill(step)
+    st = next(iter(s.states.values()))
+    s.cache._free[s.cache._n_free] = st.req.pages[-1]
+    s.cache._n_free += 1
+    with pytest.raises(RuntimeError, match="page audit|corrupted"):
+        s.audit_pages()
