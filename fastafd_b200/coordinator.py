@@ -18,6 +18,7 @@ get_failure :615, _log_step_time :1537).
 """
 from __future__ import annotations
 
+import os
 import time
 from collections import deque
 from dataclasses import dataclass, field
@@ -93,6 +94,12 @@ class AfdCoordinator:
         self.stopped = False
         self.step_times: List[Tuple[int, str, int, float]] = []
         self.log_step_times = False
+        from .env import ENV
+        self.log_steps = bool(ENV.LOG_STEPS.value)        # one line per launched step (plan summary)
+        self._log_file = None
+        if ENV.LOG_DIR.value:
+            from .utils.logger import BufferedLogFile
+            self._log_file = BufferedLogFile(os.path.join(ENV.LOG_DIR.value, "coordinator.log"))
 
     # ------------------------------------------------------------------ admission
     def _pick_lane(self, input_ids: Sequence[int]) -> int:
@@ -172,7 +179,19 @@ class AfdCoordinator:
                 rec.waiting_eg.add(r)
         self.transport.send_step(sid, ag_plans, eg_plans)
         self.inflight.append(rec)
+        if self.log_steps:
+            self._step_log(f"[afd-step] launch step={sid} phase={phase} bucket={bucket} mb_tokens={list(mb_tokens)} "
+                           f"real={rec.real} inflight={len(self.inflight)} waiting="
+                           f"{sum(len(l.waiting) for l in self.lanes)}")
         return True
+
+    def _step_log(self, text: str) -> None:
+        """Step lines go to the buffered per-process file under FASTAFD_LOG_DIR when set (no write
+        syscall per step on the hot loop), else to the logger."""
+        if self._log_file is not None:
+            self._log_file.line(text)
+        else:
+            logger.info(text)
 
     # ------------------------------------------------------------------ completion
     def _on_reply(self, msg) -> None:
@@ -200,8 +219,8 @@ class AfdCoordinator:
         ms = (time.perf_counter() - rec.t_launch) * 1e3
         self.step_times.append((rec.step_id, rec.phase, rec.bucket, ms))
         if self.log_step_times:
-            logger.info(f"[afd-step-time] step={rec.step_id} phase={rec.phase} bucket={rec.bucket} "
-                        f"num_mb={self.rt.num_mb} ms={ms:.3f} real={rec.real}")
+            self._step_log(f"[afd-step-time] step={rec.step_id} phase={rec.phase} bucket={rec.bucket} "
+                           f"num_mb={self.rt.num_mb} ms={ms:.3f} real={rec.real}")
         for uid, _toks, fin in items:
             if fin:
                 self.uid_lane.pop(uid, None)
