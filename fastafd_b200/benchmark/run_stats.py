@@ -20,7 +20,7 @@ import statistics
 from dataclasses import dataclass
 from typing import Dict, Iterable, List, Optional, Sequence, Tuple
 
-_STEP_RE = re.compile(r"\[afd-step-time\] step=(\d+) phase=(\w+) bucket=(\d+) num_mb=(\d+) ms=([0-9.]+) real=(\d+)")
+_STEP_RE = re.compile(r"\[afd-step-time\] step=(\d+) phase=(\w+) bucket=(\d+) num_mb=(\d+) ms=([0-9.]+) real=(\[[^\]]*\]|\d+)")
 
 
 @dataclass(frozen=True)
@@ -38,7 +38,8 @@ def parse_step_lines(lines: Iterable[str]) -> List[StepSample]:
     for ln in lines:
         m = _STEP_RE.search(ln)
         if m:
-            out.append(StepSample(int(m[1]), m[2], int(m[3]), int(m[4]), float(m[5]), int(m[6])))
+            real = sum(int(v) for v in m[6].strip("[]").split(",") if v.strip())      # per-lane list or a total
+            out.append(StepSample(int(m[1]), m[2], int(m[3]), int(m[4]), float(m[5]), real))
     return out
 
 

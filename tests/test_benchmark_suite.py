@@ -28,7 +28,7 @@ def test_throughput_formula_and_verdict():
 def test_decode_window_and_step_mean():
     lines = [f"[afd-step-time] step={i} phase=prefill bucket=0 num_mb=2 ms=50.0 real=8" for i in range(3)]
     lines += [f"[afd-step-time] step={3 + i} phase=decode bucket=8 num_mb=2 ms={10 + (i == 0) * 5:.3f} real=8" for i in range(6)]
-    lines += ["[afd-step-time] step=9 phase=decode bucket=8 num_mb=2 ms=7.000 real=5"]       # batch draining
+    lines += ["[afd-step-time] step=9 phase=decode bucket=8 num_mb=2 ms=7.000 real=[3, 2]"]  # batch draining, per-lane counts
     s = run_stats.parse_step_lines(["noise"] + lines)
     assert len(s) == 10
     w = run_stats.decode_window(s)
