@@ -34,3 +34,28 @@ def test_chunked_prefill_and_single_mb():
     out = SpmdDriver(eng).generate(prompts, SamplingParams(max_tokens=4, ignore_eos=True))
     exp = greedy_generate_reference(cfg, eng.attn.model, [eng.expert_stage], prompts, 4)
     assert out == exp
+
+
+def test_radix_prefix_cache_through_the_engine_gives_the_same_tokens_and_shares_pages():
+    """Two waves of requests with a long common prefix: with the radix cache the second wave reuses
+    the first wave's KV pages (fewer prefill tokens are computed) and must produce exactly the
+    tokens of the naive ledger."""
+    cfg = PRESETS["tiny-qwen3-moe"]
+    g = torch.Generator().manual_seed(5)
+    prefix = torch.randint(0, cfg.vocab_size, (48,), generator=g).tolist()
+    waves = [[prefix + torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (5, 9)] for _ in range(2)]
+    sp = SamplingParams(max_tokens=5, ignore_eos=True)
+
+    def run(cache_type):
+        eng = AfdEngine(cfg, _rt(cache_type=cache_type, num_pages=96), AfdTopology(colocated=True), 0, "cpu", seed=0)
+        drv = SpmdDriver(eng)
+        outs = [drv.generate(w, sp) for w in waves]
+        lane = drv.lanes[0]
+        lane.check_integrity()
+        return outs, lane
+
+    naive, _ = run("naive")
+    radix, lane = run("radix")
+    assert radix == naive
+    assert lane.cache.cached_pages >= len(prefix) // 16          # the shared prefix stayed cached
+    assert lane.prefix_hit_len(prefix + [1, 2, 3]) >= (len(prefix) // 16) * 16

@@ -71,16 +71,20 @@ def _free_port():
 
 
 @pytest.mark.timeout(300)
-def test_http_round_trip_cpu_afd():
+@pytest.mark.parametrize("mode,cache", [("afd-serve", "naive"), ("serve", "radix")],
+                         ids=["afd-two-roles", "colocated-serve-radix"])
+def test_http_round_trip_cpu_afd(mode, cache):
+    """HTTP -> tokenizer -> coordinator -> workers and back, in AFD mode (attention and expert
+    processes) and in the colocated `serve` mode with the radix prefix cache."""
     import requests
     import uvicorn
 
     from fastafd_b200.server.api_server import FrontendManager, create_app
     from fastafd_b200.server.supervisor import LocalSupervisor
 
-    args = parse_args(["--mode", "afd-serve", "--model-path", "tiny-qwen3-moe", "--device", "cpu", "--afd-num-mb", "2",
+    args = parse_args(["--mode", mode, "--model-path", "tiny-qwen3-moe", "--device", "cpu", "--afd-num-mb", "2",
                        "--num-pages", "64", "--max-seq-len-override", "128", "--afd-max-running-requests", "8",
-                       "--cuda-graph-max-bs", "8"])
+                       "--cuda-graph-max-bs", "8", "--cache-type", cache])
     sup = LocalSupervisor(args)
     addrs = sup.start()
     port = _free_port()
