@@ -86,13 +86,26 @@ class AfdEngine:
         self.fabric = None
         self.attn: Optional[AttentionWorker] = None
         self.expert: Optional[ExpertWorker] = None
-        num_eg = 1 if self.colocated else topo.mlp_world
-        num_ag = 1 if self.colocated else topo.attn_world
+        if not self.colocated and topo.mlp_tp > 1:
+            raise NotImplementedError("experts are sharded by expert parallelism only (mlp_tp must be 1)")
+        # One replica of the expert set (mlp_dp of them) serves the lanes l with l % mlp_dp == replica:
+        # an attention rank talks to its replica's expert ranks, an expert rank to its lanes' ranks.
+        if self.colocated:
+            eg_ranks, ag_ranks, my_ag_index = [0], [0], 0
+        elif self.is_attention:
+            eg_ranks = topo.expert_ranks_for(rank)
+            ag_ranks = topo.attention_ranks_for(eg_ranks[0])
+            my_ag_index = ag_ranks.index(rank)
+        else:
+            ag_ranks = topo.attention_ranks_for(rank)
+            eg_ranks = topo.expert_ranks_for(ag_ranks[0])
+            my_ag_index = -1
+        num_eg, num_ag = len(eg_ranks), len(ag_ranks)
 
         stage = None
         import os as _os0
         if self.is_expert and cfg.is_moe and _os0.environ.get("FASTAFD_DEBUG_NULL_MOE") != "1":
-            ep_rank = 0 if self.colocated else topo.expert_index(rank)
+            ep_rank = 0 if self.colocated else topo.ep_rank(rank)
             stage = ExpertStage(cfg, self.device, self.dtype, ep_rank, num_eg).init_random(seed, fast=fast_init)
         self.expert_stage = stage
 
@@ -133,9 +146,9 @@ class AfdEngine:
                         size += tp_layout(topo.attn_tp, rt.num_mb, self.max_comm_tokens, cfg.hidden_size).size
                     self.fabric = Fabric.ipc(size, self.device, group)
                     if self.is_attention:
-                        client = FabricMoeClient(AgMoeEndpoint(mcfg, self.fabric, rank, topo.expert_ranks(), self.device, timeout_ns))
+                        client = FabricMoeClient(AgMoeEndpoint(mcfg, self.fabric, my_ag_index, eg_ranks, self.device, timeout_ns))
                     else:
-                        eg_ep = EgMoeEndpoint(mcfg, self.fabric, topo.expert_index(rank), topo.attention_ranks(),
+                        eg_ep = EgMoeEndpoint(mcfg, self.fabric, topo.ep_rank(rank), ag_ranks,
                                               self.device, timeout_ns)
                         server = FabricMoeServer(eg_ep, stage)
                         eg_status = eg_ep.status
@@ -143,9 +156,9 @@ class AfdEngine:
                 if self.colocated:
                     client = LocalMoeClient([stage])
                 elif self.is_attention:
-                    client = GlooMoeClient(topo.expert_ranks(), cfg.hidden_size, cfg.num_experts_per_tok, group)
+                    client = GlooMoeClient(eg_ranks, cfg.hidden_size, cfg.num_experts_per_tok, group)
                 else:
-                    server = GlooMoeServer(stage, topo.attention_ranks(), cfg.hidden_size, cfg.num_experts_per_tok,
+                    server = GlooMoeServer(stage, ag_ranks, cfg.hidden_size, cfg.num_experts_per_tok,
                                            self.dtype, group)
         tp_comm = make_tp_comms(topo, rank, self.device, group)
         if tp_comm is not None and cuda and cfg.is_moe and self.fabric is not None and self.is_attention \

@@ -38,6 +38,8 @@ class AfdTopology:
             if getattr(self, name) < 1:
                 raise ValueError(f"{name} must be >= 1")
         mlp_world = self.mlp_world
+        if self.attn_dp % self.mlp_dp != 0:
+            raise ValueError("attn_dp must be a multiple of mlp_dp (every expert replica serves the same number of lanes)")
         if self.mlp_ep not in (1, self.mlp_tp, mlp_world // self.mlp_dp):
             raise ValueError("mlp_ep must be 1, mlp_tp or the size of one MLP replica")
 
@@ -81,6 +83,24 @@ class AfdTopology:
 
     def attention_ranks(self) -> List[int]:
         return list(range(self.attn_world))
+
+    # ---- MLP data parallelism: mlp_dp replicas of the expert set; lane l uses replica l % mlp_dp
+    def replica_of_lane(self, lane: int) -> int:
+        return lane % self.mlp_dp
+
+    def replica_of_expert_rank(self, rank: int) -> int:
+        return self.expert_index(rank) // self.mlp_replica
+
+    def expert_ranks_for(self, attn_rank: int) -> List[int]:
+        """Expert ranks that serve the lane of `attn_rank` (one replica of the expert set)."""
+        rep = self.replica_of_lane(self.attn_lane(attn_rank))
+        first = self.attn_world + rep * self.mlp_replica
+        return list(range(first, first + self.mlp_replica))
+
+    def attention_ranks_for(self, expert_rank: int) -> List[int]:
+        """Attention ranks (dispatch sources) whose lanes are served by the replica of `expert_rank`."""
+        rep = self.replica_of_expert_rank(expert_rank)
+        return [r for r in range(self.attn_world) if self.replica_of_lane(self.attn_lane(r)) == rep]
 
     def dispatch_sources(self) -> List[int]:
         """Attention ranks that push tokens into the experts. After the TP all-reduce every
