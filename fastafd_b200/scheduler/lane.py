@@ -267,8 +267,10 @@ class LaneScheduler:
             rows = np.full(bucket, self.dummy_row, np.int32)
             seq = np.full(bucket, tokens_per_req, np.int32)
             slots: List[Tuple[int, bool]] = []
+            ps = self.page_size
             for i, st in enumerate(part):
-                self._grow_pages(st, st.planned_len + tokens_per_req, grants)
+                if (st.planned_len + tokens_per_req + ps - 1) // ps > len(st.req.pages):   # a new page only every ps tokens
+                    self._grow_pages(st, st.planned_len + tokens_per_req, grants)
                 st.planned_len += tokens_per_req
                 st.planned_out += 1 if tokens_per_req == 1 else 0
                 st.inflight += 1
@@ -322,13 +324,16 @@ class LaneScheduler:
         out: List[Tuple[int, List[int], bool]] = []
         i = 0
         blk = self.spec_block if rec.phase == "verify" else 1
+        tok_list = next_tokens.tolist()            # one conversion; per-row numpy slices cost more than the work
+        acc_list = accepted.tolist() if (accepted is not None and blk > 1) else None
         for slots in rec.slots:
             for uid, emits in slots:
-                toks = next_tokens[i * blk:(i + 1) * blk] if blk > 1 else next_tokens[i:i + 1]
-                n_acc = int(accepted[i]) if (accepted is not None and blk > 1) else 1
+                row = i
                 i += 1
                 if uid < 0:
                     continue
+                n_acc = int(acc_list[row]) if acc_list is not None else 1
+                toks = tok_list[row * blk:row * blk + n_acc] if blk > 1 else tok_list[row:row + 1]
                 st = self.states.get(uid)
                 if st is None:
                     continue
@@ -344,10 +349,10 @@ class LaneScheduler:
                     continue
                 new: List[int] = []
                 finished = False
-                for t in toks[:n_acc].tolist():
-                    req.output_ids.append(int(t))
-                    new.append(int(t))
-                    if (int(t) in self.eos and not req.sampling.ignore_eos) or int(t) in req.sampling.stop_token_ids \
+                for t in toks:
+                    req.output_ids.append(t)
+                    new.append(t)
+                    if (t in self.eos and not req.sampling.ignore_eos) or t in req.sampling.stop_token_ids \
                             or len(req.output_ids) >= req.sampling.max_tokens:
                         finished = True
                         break
