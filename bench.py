@@ -153,7 +153,7 @@ def main():
     lane_b = b * tp                      # a TP lane serves tp GPUs' worth of requests
     per_mb = (lane_b + args.num_mb - 1) // args.num_mb
     per_mb = (per_mb + tp - 1) // tp * tp
-    total_steps = 2 * (args.steps + args.warmup) + 8
+    total_steps = 3 * args.steps + 2 * args.warmup + 8
     rt = RuntimeConfig(model_path=args.model, num_mb=args.num_mb, page_size=16, max_running_requests=lane_b,
                        max_seq_len=args.context + total_steps + 16, cuda_graph_max_bs=per_mb,
                        decode_graph_bs=(per_mb,), use_cuda_graph=not args.no_graph, moe_block_tok=args.block_tok,
@@ -207,6 +207,15 @@ def main():
     e2e_ms = (time.perf_counter() - t0) * 1e3
     barrier()
     e2e_ms = max_over_ranks(e2e_ms)
+    # the same public call in the server's default mode: step n+1 is planned and its inputs are
+    # copied while step n runs (one step ahead); every step still has its H2D and D2H copies
+    barrier()
+    t0 = time.perf_counter()
+    drv.run_decode_steps(args.steps, pipelined=True)
+    torch.cuda.synchronize()
+    ahead_ms = (time.perf_counter() - t0) * 1e3
+    barrier()
+    ahead_ms = max_over_ranks(ahead_ms)
     status = eng.synchronize()
 
     trace_info = None
@@ -255,7 +264,9 @@ def main():
             "clocks": clocks,
             "e2e": {"value": round(e2e_value, 2), "unit": "tok/s", "ms_per_step": round(e2e_ms / args.steps, 4),
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "how": "SpmdDriver.run_decode_steps(pipelined=False): host plan -> pinned H2D -> graph replay -> D2H tokens -> host completion, per step"},
+                    "how": "SpmdDriver.run_decode_steps(pipelined=False): host plan -> pinned H2D -> graph replay -> D2H tokens -> host completion, per step",
+                    "one_step_ahead": {"value": round(tokens / (ahead_ms / 1e3), 2), "ms_per_step": round(ahead_ms / args.steps, 4),
+                                       "how": "wall clock of run_decode_steps(pipelined=True), the serving default: step n+1 planned and copied while step n runs"}},
             "gpu_launches": kernels_per_step * args.steps,
             "kernels_per_step_rank0": kernels_per_step,
             "device_status": status, "build_s": round(build_s, 1),
