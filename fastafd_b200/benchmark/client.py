@@ -5,7 +5,15 @@ throughput.
 
     python -m fastafd_b200.benchmark.client --port 1919 --num 64 --prompt-len 1024 --max-tokens 128
 
-Reference: python/minisgl/benchmark/client.py:18-60 (per-request tick lists), perf.py.
+A recorded arrival trace can be replayed instead of a closed batch:
+
+    python -m fastafd_b200.benchmark.client --port 1919 --trace trace.jsonl --time-scale 0.5 --max-requests 200
+
+Trace lines are JSON objects with ``timestamp`` (ms since the first request), ``input_length`` and
+``output_length`` (the Mooncake / Qwen trace layout); prompts are random ids of the recorded lengths.
+
+Reference: python/minisgl/benchmark/client.py:18-60 (per-request tick lists), :407-500 (trace
+readers and scaling), perf.py.
 """
 from __future__ import annotations
 
@@ -35,6 +43,43 @@ class RequestTrace:
         if len(self.ticks) < 2:
             return float("nan")
         return (self.ticks[-1] - self.ticks[0]) / (len(self.ticks) - 1)
+
+
+@dataclass(frozen=True)
+class TraceEntry:
+    at_s: float           # arrival offset from the start of the replay
+    input_length: int
+    output_length: int
+
+
+def read_trace(path: str) -> List[TraceEntry]:
+    """One JSON object per line: timestamp (ms), input_length, output_length. Lines that lack a
+    field or have non-positive lengths are skipped; arrivals are re-based to start at 0."""
+    out = []
+    with open(path) as f:
+        for line in f:
+            line = line.strip()
+            if not line:
+                continue
+            try:
+                o = json.loads(line)
+                e = TraceEntry(float(o["timestamp"]) / 1e3, int(o["input_length"]), int(o["output_length"]))
+            except (ValueError, KeyError, TypeError):
+                continue
+            if e.input_length > 0 and e.output_length > 0:
+                out.append(e)
+    out.sort(key=lambda e: e.at_s)
+    t0 = out[0].at_s if out else 0.0
+    return [TraceEntry(e.at_s - t0, e.input_length, e.output_length) for e in out]
+
+
+def scale_trace(entries: List[TraceEntry], time_scale: float = 1.0, max_requests: int = 0, max_input: int = 0,
+                max_output: int = 0) -> List[TraceEntry]:
+    """Compress or stretch arrivals by `time_scale` (0.5 = twice the request rate), keep the first
+    `max_requests`, and clip lengths to what the server under test accepts."""
+    out = entries[:max_requests] if max_requests > 0 else list(entries)
+    return [TraceEntry(e.at_s * time_scale, min(e.input_length, max_input) if max_input > 0 else e.input_length,
+                       min(e.output_length, max_output) if max_output > 0 else e.output_length) for e in out]
 
 
 def summarize(traces: List[RequestTrace], wall_s: float) -> dict:
@@ -88,6 +133,24 @@ async def run(host: str, port: int, num: int, prompt_len: int, max_tokens: int, 
     return summarize(list(traces), time.perf_counter() - t0)
 
 
+async def replay(host: str, port: int, entries: List[TraceEntry], vocab: int, seed: int = 0) -> dict:
+    """Open-loop replay: every request is sent at its recorded arrival time whatever the state of
+    the earlier ones."""
+    import aiohttp
+
+    rng = random.Random(seed)
+    url = f"http://{host}:{port}/v1/chat/completions"
+    t0 = time.perf_counter()
+
+    async def later(session, e: TraceEntry):
+        await asyncio.sleep(max(0.0, e.at_s - (time.perf_counter() - t0)))
+        return await _one(session, url, [rng.randrange(vocab) for _ in range(e.input_length)], e.output_length)
+
+    async with aiohttp.ClientSession(timeout=aiohttp.ClientTimeout(total=None)) as s:
+        traces = await asyncio.gather(*[later(s, e) for e in entries])
+    return summarize(list(traces), time.perf_counter() - t0)
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--host", default="127.0.0.1")
@@ -96,7 +159,16 @@ def main(argv=None):
     ap.add_argument("--prompt-len", type=int, default=128)
     ap.add_argument("--max-tokens", type=int, default=32)
     ap.add_argument("--vocab", type=int, default=1024)
+    ap.add_argument("--trace", default="", help="JSONL arrival trace to replay instead of a closed batch")
+    ap.add_argument("--time-scale", type=float, default=1.0)
+    ap.add_argument("--max-requests", type=int, default=0)
+    ap.add_argument("--max-input", type=int, default=0)
+    ap.add_argument("--max-output", type=int, default=0)
     a = ap.parse_args(argv)
+    if a.trace:
+        entries = scale_trace(read_trace(a.trace), a.time_scale, a.max_requests, a.max_input, a.max_output)
+        print(json.dumps(asyncio.run(replay(a.host, a.port, entries, a.vocab))))
+        return
     print(json.dumps(asyncio.run(run(a.host, a.port, a.num, a.prompt_len, a.max_tokens, a.vocab))))
 
 

@@ -49,3 +49,20 @@ def test_evaluate_bench_line():
     res = suite.evaluate(c, line, 0.03)
     assert res["verdict"] == "pass" and res["tok_s_per_gpu"] == pytest.approx(1130.8, abs=1.0)
     assert res["vs_published"] == pytest.approx(0.733, abs=0.005)
+
+
+def test_trace_reader_and_scaling(tmp_path):
+    from fastafd_b200.benchmark.client import read_trace, scale_trace
+
+    p = tmp_path / "trace.jsonl"
+    p.write_text("\n".join([
+        json.dumps({"timestamp": 5000, "input_length": 100, "output_length": 20, "hash_ids": [1, 2]}),
+        json.dumps({"timestamp": 3000, "input_length": 50, "output_length": 10}),
+        "not json",
+        json.dumps({"timestamp": 9000, "input_length": 0, "output_length": 10}),           # dropped: empty prompt
+        json.dumps({"timestamp": 7000, "input_length": 4000, "output_length": 900}),
+    ]))
+    tr = read_trace(str(p))
+    assert [(e.at_s, e.input_length) for e in tr] == [(0.0, 50), (2.0, 100), (4.0, 4000)]
+    sc = scale_trace(tr, time_scale=0.5, max_requests=3, max_input=1024, max_output=128)
+    assert [(e.at_s, e.input_length, e.output_length) for e in sc] == [(0.0, 50, 10), (1.0, 100, 20), (2.0, 1024, 128)]
