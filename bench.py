@@ -260,6 +260,8 @@ def main():
                        "decode_tokens_timed": args.steps, "micro_batches": args.num_mb, "page_size": 16,
                        "parallelism": "colocated-1gpu" if topo.colocated else (f"attn_dp{topo.attn_dp}" + (f"xtp{tp}" if tp > 1 else "") + f"+mlp_ep{topo.mlp_ep}"),
                        "l2": "per-step working set (expert weights + KV) is far larger than the 126 MB L2; no flush needed",
+                       "attention_parallelism_note": "attention GPUs are data-parallel lanes by default; --attn-tp N makes a lane "
+                                                     "tensor-parallel over N GPUs (token-sharded residual, collectives fused with the GEMMs)",
                        "layers": cfg.num_layers, "truncated_model": truncated},
             "clocks": clocks,
             "e2e": {"value": round(e2e_value, 2), "unit": "tok/s", "ms_per_step": round(e2e_ms / args.steps, 4),
