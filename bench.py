@@ -247,6 +247,22 @@ def main():
         h2d = 2 * per_mb * 4 * args.num_mb + 24 * ((b + 15) // 16)   # rows + seq_lens (+ page grants, amortised)
         d2h = per_mb * 4 * args.num_mb + 8
     published = PUBLISHED_TOK_S_PER_GPU.get(args.model)
+    # N2M / M2N traffic of one attention GPU per step (bytes that cross NVLink; 0 when colocated):
+    # up = one row per expert GPU that owns one of the token's experts (expectation under uniform
+    # routing), down = one bf16 row per (token, k).
+    comm = None
+    if cfg.is_moe and not topo.colocated:
+        n_eg, K, H = topo.mlp_ep, cfg.num_experts_per_tok, cfg.hidden_size
+        moe_layers = sum(1 for l in range(cfg.num_layers) if cfg.is_moe_layer(l))
+        row_up = H * (1 if cfg.quant.is_fp8 else 2) + (H // 128 * 4 if cfg.quant.is_fp8 else 0)
+        copies = n_eg * (1.0 - (1.0 - 1.0 / n_eg) ** K)
+        per_tok_up, per_tok_down = row_up * copies + K * 4 * n_eg, K * H * 2
+        step_s = dev_ms / args.steps / 1e3
+        comm = {"n2m_bytes_per_step_per_attn_gpu": int(moe_layers * b * per_tok_up),
+                "m2n_bytes_per_step_per_attn_gpu": int(moe_layers * b * per_tok_down),
+                "n2m_GB_s_avg_over_step": round(moe_layers * b * per_tok_up / step_s / 1e9, 2),
+                "m2n_GB_s_avg_over_step": round(moe_layers * b * per_tok_down / step_s / 1e9, 2),
+                "note": "averaged over the whole step; the transfers ride in the GEMM epilogues and the route kernel"}
     if rank == 0:
         out = {
             "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -273,6 +289,8 @@ def main():
             "kernels_per_step_rank0": kernels_per_step,
             "device_status": status, "build_s": round(build_s, 1),
         }
+        if comm is not None:
+            out["n2m_m2n"] = comm
         if trace_info is not None:
             out["comm_trace"] = trace_info
         if truncated:
