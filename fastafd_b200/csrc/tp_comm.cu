@@ -56,16 +56,17 @@ __global__ void __launch_bounds__(256) tp_allgather_push_kernel(const TpGatherAr
 struct TpWaitArgs {
   const uint32_t* flags;   // [tp] local flag words, one per source rank
   int tp;
-  uint32_t* epoch;         // expected value, incremented after the wait
+  uint32_t* epoch;         // expected value, incremented after the wait when `bump` is set
   uint64_t timeout_ns;
   int* status;
+  int bump;
 };
 
 __global__ void tp_allgather_wait_kernel(const TpWaitArgs a) {
   const uint32_t e = *a.epoch;
   if (threadIdx.x < a.tp) wait_flag_ge(a.flags + threadIdx.x, e, a.timeout_ns, a.status);
   __syncthreads();
-  if (threadIdx.x == 0) {
+  if (threadIdx.x == 0 && a.bump) {
     *a.epoch = e + 1;
     __threadfence();
   }
@@ -105,7 +106,21 @@ extern "C" int afd_tp_allgather_wait(const void* flags, int tp, void* epoch, uns
   using namespace afd;
   if (tp < 1 || tp > kMaxTp) return -1;
   TpWaitArgs a{static_cast<const uint32_t*>(flags), tp, static_cast<uint32_t*>(epoch), timeout_ns,
-               static_cast<int*>(status)};
+               static_cast<int*>(status), 1};
+  tp_allgather_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(a);
+  AFD_CHECK_LAUNCH();
+  return 0;
+}
+
+// One-warp bounded wait until `n` flag words reach the epoch stored at `epoch` (which is left
+// unchanged): put in front of a many-CTA consumer so that the consumer's CTAs are not resident,
+// holding shared memory and registers, while the producers are still working.
+extern "C" int afd_wait_flags_epoch(const void* flags, int n, const void* epoch, unsigned long long timeout_ns,
+                                    void* status, void* stream) {
+  using namespace afd;
+  if (n < 1 || n > 32) return -1;
+  TpWaitArgs a{static_cast<const uint32_t*>(flags), n, const_cast<uint32_t*>(static_cast<const uint32_t*>(epoch)),
+               timeout_ns, static_cast<int*>(status), 0};
   tp_allgather_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(a);
   AFD_CHECK_LAUNCH();
   return 0;

@@ -28,6 +28,14 @@ DEFAULT_TIMEOUT_NS = int(float(os.environ.get("FASTAFD_FLAG_TIMEOUT_S", "20")) *
 TRACE_LEN = 1024      # rows of the device-side timeline ring (kTraceLen in csrc/common.cuh)
 
 
+# A consumer kernel that spins on peer flags with all its CTAs resident takes SM slots, shared memory
+# and issue bandwidth from whatever else runs meanwhile (the other micro-batch's attention, the
+# other lane's GEMM): measured on the attention side, the lane's own chain shrank from 274 to 188 us
+# (Qwen3-235B shapes) and from 65 to 58 us (Qwen3-30B shapes) once the wait ran as a single warp in
+# a launch of its own in front of the consumer. FASTAFD_SPLIT_WAIT=0 puts the wait back inside.
+_SPLIT_WAIT = os.environ.get("FASTAFD_SPLIT_WAIT", "1") != "0"
+
+
 def _trace_enabled() -> bool:
     return os.environ.get("FASTAFD_COMM_TRACE", "0") == "1"
 
@@ -172,6 +180,10 @@ class AgMoeEndpoint:
         d.extra, d.y, d.residual, d.norm_w, d.normed = ptr(extra), ptr(y), ptr(residual), ptr(norm_w), ptr(normed)
         d.eps, d.offset1, d.timeout_ns, d.status = eps, int(offset1), self.timeout_ns, ptr(self.status)
         d.trace = ptr(self.trace[lane]) if self.trace else None
+        if _SPLIT_WAIT and cfg.num_lanes > 1:     # with one lane nothing else runs that a resident spin could slow
+            # the wait of the flags runs as one warp; the T-CTA reduction launches once they are set
+            check(lib().afd_wait_flags_epoch(ptr(self.m2n_flag[lane]), cfg.num_eg, ptr(w.epoch2),
+                                             C.c_ulonglong(self.timeout_ns), ptr(self.status), cur_stream()), "wait_flags")
         check(lib().afd_ag_combine(C.byref(d), cur_stream()), "ag_combine")
         return y if normed is None else normed
 
@@ -228,6 +240,9 @@ class EgMoeEndpoint:
         d.row_bytes, d.scale_per_row = cfg.row_bytes, cfg.hidden // 128
         d.trace = ptr(self.trace[lane]) if self.trace else None
         d.done_counter = ptr(w.done)
+        if _SPLIT_WAIT and cfg.num_lanes > 1:
+            check(lib().afd_wait_flags_epoch(ptr(self.n2m_flag[lane]), cfg.num_ag, ptr(w.epoch),
+                                             C.c_ulonglong(self.timeout_ns), ptr(self.status), cur_stream()), "wait_flags")
         fused = cfg.num_ag * T * cfg.topk <= 8192 and cfg.block_tok <= 128      # one launch, else two
         check(lib().afd_eg_group_gather(C.byref(d), cur_stream()), "eg_group_gather_fused" if fused else "eg_group_gather")
 
@@ -257,7 +272,8 @@ class EgMoeEndpoint:
 def summarize_trace(trace: torch.Tensor, role: str, last: int = 256) -> dict:
     """Mean durations (microseconds) over the most recent `last` rounds of one lane's timeline.
     attention: wait = combine start -> flags seen (idle time waiting for the experts),
-               reduce = flags seen -> combine end, round = dispatch released -> combine end.
+               reduce = flags seen -> combine end, round = dispatch released -> combine end,
+               chain = combine end -> next dispatch released (median; the lane's own compute chain).
     expert   : wait = group start -> flags seen (idle time waiting for attention ranks),
                busy = flags seen -> down-projection flags released."""
     t = trace.cpu().numpy().astype("int64")
@@ -267,8 +283,17 @@ def summarize_trace(trace: torch.Tensor, role: str, last: int = 256) -> dict:
         return {}
     us = lambda a: float(a.mean()) / 1e3  # noqa: E731
     if role == "attention":
-        return {"wait_us": us(rows[:, 2] - rows[:, 1]), "reduce_us": us(rows[:, 3] - rows[:, 2]),
-                "round_trip_us": us(rows[:, 3] - rows[:, 0]), "rounds": len(rows)}
+        out = {"wait_us": us(rows[:, 2] - rows[:, 1]), "reduce_us": us(rows[:, 3] - rows[:, 2]),
+               "round_trip_us": us(rows[:, 3] - rows[:, 0]), "rounds": len(rows)}
+        # attention-side chain of the lane: combine end of one round -> dispatch released of the next
+        # (qkv, norm + RoPE + store, attention, o_proj, route + dispatch, plus whatever the other
+        # micro-batch put on the GPU in between); step boundaries (long gaps) are left out
+        gaps = rows[1:, 0] - rows[:-1, 3]
+        gaps = gaps[(gaps > 0) & (gaps < 5_000_000)]
+        if len(gaps):
+            import numpy as _np
+            out["chain_us"] = float(_np.median(gaps)) / 1e3
+        return out
     return {"wait_us": us(rows[:, 1] - rows[:, 0]), "busy_us": us(rows[:, 3] - rows[:, 1]), "rounds": len(rows)}
 
 

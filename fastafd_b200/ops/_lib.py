@@ -98,6 +98,7 @@ _SIGNATURES = {
     "afd_argmax_chunks": (C.c_int, [C.c_int]),
     "afd_tp_allgather_push": (C.c_int, [VP, VP]),
     "afd_tp_allgather_wait": (C.c_int, [VP, C.c_int, VP, C.c_ulonglong, VP, VP]),
+    "afd_wait_flags_epoch": (C.c_int, [VP, C.c_int, VP, C.c_ulonglong, VP, VP]),
     "afd_sample": (C.c_int, [VP, C.c_long, C.c_int, C.c_int, C.c_int, VP, VP, VP, VP, VP, VP]),
     "afd_group_quant_fp8": (C.c_int, [VP, VP, VP, C.c_long, C.c_int, C.c_int, C.c_int, VP]),
     "afd_decode_attn_workspace_bytes": (C.c_long, [C.c_int] * 6),

@@ -164,6 +164,9 @@ class TpFusedComm(TpComm):
         c.scale = 1.0
         c.extra, c.y, c.residual, c.norm_w, c.normed = None, ptr(y), None, None, None
         c.eps, c.offset1, c.timeout_ns, c.status, c.trace = 1e-6, 0, self.timeout_ns, ptr(self.status), None
+        # one-warp wait first, so that the Tl reduction CTAs are not resident while peers still compute
+        check(lib().afd_wait_flags_epoch(ptr(self.rs_flag[lane]), tp, ptr(wd[2:3]), C.c_ulonglong(self.timeout_ns),
+                                         ptr(self.status), cur_stream()), "wait_flags")
         check(lib().afd_ag_combine(C.byref(c), cur_stream()), "ag_combine")
         return y
 
