@@ -45,10 +45,15 @@ def test_wall_period_is_inverse_slope():
 def test_evaluate_bench_line():
     cfgs = suite.load_configs()
     c = cfgs["configs"]["qwen3-235b-8k-1to1"]
-    line = json.dumps({"metric": "m", "value": 9046.6, "n_gpus": 8, "ms_per_step": 38.91, "e2e": {"ms_per_step": 39.7}})
+    rec = c["recorded"]["step_ms"]
+    line = json.dumps({"metric": "m", "value": 4 * c["batch"] / (rec * 1.01 / 1e3), "n_gpus": 8, "ms_per_step": rec * 1.01,
+                       "e2e": {"ms_per_step": rec * 1.03}})
     res = suite.evaluate(c, line, 0.03)
-    assert res["verdict"] == "pass" and res["tok_s_per_gpu"] == pytest.approx(1130.8, abs=1.0)
-    assert res["vs_published"] == pytest.approx(0.733, abs=0.005)
+    want = 4 * c["batch"] / (rec * 1.01 / 1e3) / 8
+    assert res["verdict"] == "pass" and res["tok_s_per_gpu"] == pytest.approx(want, rel=1e-3)
+    assert res["vs_published"] == pytest.approx(want / c["published"]["tok_s_per_gpu"], abs=0.002)
+    slow = json.dumps({"metric": "m", "value": 1.0, "n_gpus": 8, "ms_per_step": rec * 1.05, "e2e": {"ms_per_step": rec * 1.06}})
+    assert suite.evaluate(c, slow, 0.03)["verdict"] == "fail"
 
 
 def test_trace_reader_and_scaling(tmp_path):
