@@ -18,6 +18,8 @@ python/minisgl/engine/engine.py:212-433 (colocated Engine).
 """
 from __future__ import annotations
 
+import os
+
 import time
 from typing import Dict, List, Optional, Sequence, Tuple
 
@@ -103,8 +105,7 @@ class AfdEngine:
         num_eg, num_ag = len(eg_ranks), len(ag_ranks)
 
         stage = None
-        import os as _os0
-        if self.is_expert and cfg.is_moe and _os0.environ.get("FASTAFD_DEBUG_NULL_MOE") != "1":
+        if self.is_expert and cfg.is_moe and os.environ.get("FASTAFD_DEBUG_NULL_MOE") != "1":
             ep_rank = 0 if self.colocated else topo.ep_rank(rank)
             stage = ExpertStage(cfg, self.device, self.dtype, ep_rank, num_eg).init_random(seed, fast=fast_init)
         self.expert_stage = stage
@@ -113,9 +114,8 @@ class AfdEngine:
 
         client, server = MoeClient(), None      # dense models: no experts to reach
         eg_status = None
-        import os as _os
         tp_heap_base = 0
-        if _os.environ.get("FASTAFD_DEBUG_NULL_MOE") == "1" and cfg.is_moe:
+        if os.environ.get("FASTAFD_DEBUG_NULL_MOE") == "1" and cfg.is_moe:
             from .worker.moe_client import NullMoeClient
 
             client, stage = NullMoeClient(), None
@@ -138,7 +138,7 @@ class AfdEngine:
                 else:
                     size = ag_layout(mcfg).size if self.is_attention else eg_layout(mcfg).size
                     fuse_tp = (self.is_attention and topo.attn_tp > 1 and cfg.hidden_size % 128 == 0
-                               and _os.environ.get("FASTAFD_TP_FUSED", "0") == "1")     # opt-in, see parallel/tp_fused.py
+                               and os.environ.get("FASTAFD_TP_FUSED", "0") == "1")     # opt-in, see parallel/tp_fused.py
                     if fuse_tp:
                         from .parallel.tp_fused import tp_layout
 
@@ -174,12 +174,11 @@ class AfdEngine:
                                         tp_comm=tp_comm, dtype=self.dtype, rank=rank, max_bucket=cap,
                                         weight_init=lambda m: m.init_random(seed, fast=fast_init))
         if self.attn is not None and rt.spec_block > 1:
-            import os as _os1
 
             from .spec.attn_side import SpecRunner
 
             self.attn.spec = SpecRunner(self.attn, rt.spec_block, rt.spec_draft_path, seed,
-                                        float(_os1.environ.get("FASTAFD_SPEC_SIM_ACCEPT", "0") or 0))
+                                        float(os.environ.get("FASTAFD_SPEC_SIM_ACCEPT", "0") or 0))
         if self.is_expert and not self.colocated:
             self.expert = ExpertWorker(cfg, rt, self.device, stage, server, rank, eg_status)
         self._server = server
