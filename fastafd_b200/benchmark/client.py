@@ -21,7 +21,6 @@ import argparse
 import asyncio
 import json
 import random
-import statistics
 import time
 from dataclasses import dataclass, field
 from typing import List

@@ -15,12 +15,10 @@ import argparse
 import json
 import math
 import os
-import sys
 
 import torch
 
 from .. import ops
-from ..reference import ops_ref as ref
 
 
 def measured_peaks():

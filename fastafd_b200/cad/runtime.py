@@ -17,8 +17,8 @@ python/minisgl/kernel/cad_hop.py:42-204 (wait / copy / flag / epoch semantics).
 from __future__ import annotations
 
 import time
-from dataclasses import dataclass, field
-from typing import Dict, List, Optional, Tuple
+from dataclasses import dataclass
+from typing import List, Optional, Tuple
 
 import torch
 import torch.nn.functional as F
@@ -28,7 +28,7 @@ from ..config import ModelConfig
 from ..models.transformer import AttentionStage, ExpertStage, combine_rows
 from ..reference import ops_ref as ref
 from .config import CadConfig
-from .program import Task, attention_program, check_balanced, model_program
+from .program import attention_program, check_balanced, model_program
 
 
 class CadStepAborted(RuntimeError):

@@ -24,13 +24,12 @@ from collections import deque
 from dataclasses import dataclass, field
 from typing import Callable, Deque, Dict, List, Optional, Sequence, Tuple
 
-import numpy as np
 
 from .config import ModelConfig, RuntimeConfig
 from .core import SamplingParams
 from .protocol import AfdTopology, AgStepPlan, AgStepReply, EgStepPlan, EgStepReply, WorkerFailure
 from .scheduler.buckets import normalize_buckets, per_mb_real, select_bucket
-from .scheduler.lane import AdmissionError, LaneScheduler
+from .scheduler.lane import LaneScheduler
 from .utils.logger import init_logger
 
 logger = init_logger("coordinator")

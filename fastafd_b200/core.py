@@ -5,7 +5,7 @@ Reference: python/minisgl/core.py (SamplingParams :16, Req :29, Batch :72).
 from __future__ import annotations
 
 from dataclasses import dataclass, field
-from typing import List, Optional, Tuple
+from typing import List, Tuple
 
 
 @dataclass

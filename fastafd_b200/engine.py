@@ -20,7 +20,6 @@ from __future__ import annotations
 
 import os
 
-import time
 from typing import Dict, List, Optional, Sequence, Tuple
 
 import numpy as np
@@ -30,7 +29,7 @@ import torch.distributed as dist
 from .config import ModelConfig, RuntimeConfig
 from .core import SamplingParams
 from .models.transformer import ExpertStage
-from .protocol import AfdTopology, AgStepPlan, AgStepReply, EgStepPlan, EgStepReply
+from .protocol import AfdTopology, AgStepPlan, AgStepReply, EgStepPlan
 from .scheduler.buckets import normalize_buckets, per_mb_real, select_bucket
 from .scheduler.lane import LaneScheduler
 from .worker.attention_worker import AttentionWorker

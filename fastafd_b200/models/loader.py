@@ -22,7 +22,6 @@ role split :506-513, dtype casting :123-139).
 from __future__ import annotations
 
 import glob
-import json
 import os
 import re
 from typing import Dict, Iterator, List, Optional, Tuple

@@ -13,7 +13,7 @@ AfdEGStepPlan :485-509, commands/replies :260-296,927-1000, codec :1023-1101).
 from __future__ import annotations
 
 from dataclasses import dataclass, field
-from typing import Any, Dict, List, Optional, Sequence, Tuple
+from typing import Any, Dict, List, Optional
 
 import msgpack
 import numpy as np

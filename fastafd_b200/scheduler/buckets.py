@@ -7,7 +7,7 @@ _balanced_decode_padded_reqs, _select_padded_size).
 """
 from __future__ import annotations
 
-from typing import List, Optional, Sequence, Tuple
+from typing import List, Sequence, Tuple
 
 
 def default_decode_buckets(max_bs: int) -> List[int]:

@@ -19,7 +19,7 @@ import numpy as np
 
 from ..core import Req, SamplingParams
 from ..protocol import AgStepPlan, MicroBatchPlan
-from .buckets import balanced_split, per_mb_real, select_bucket, split_prefill
+from .buckets import balanced_split, per_mb_real, split_prefill
 from .cache import NaivePageLedger, OutOfPages, make_page_cache
 
 

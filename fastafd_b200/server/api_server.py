@@ -20,7 +20,7 @@ from typing import Any, AsyncIterator, Callable, Dict, List, Optional
 
 from fastapi import FastAPI, Request
 from fastapi.responses import JSONResponse, StreamingResponse
-from pydantic import BaseModel, Field
+from pydantic import BaseModel
 
 from ..core import SamplingParams
 from ..message import AbortMsg, TokenizeMsg, UserReply

@@ -8,8 +8,8 @@ nothing here (there is one implementation per path).
 from __future__ import annotations
 
 import argparse
-from dataclasses import dataclass, field
-from typing import List, Optional, Sequence, Tuple
+from dataclasses import dataclass
+from typing import Optional, Sequence, Tuple
 
 from ..config import RuntimeConfig, get_model_config
 from ..protocol import AfdTopology, validate_parallel_args

@@ -16,7 +16,7 @@ import re
 import threading
 import time
 from contextlib import contextmanager
-from typing import Dict, List, Optional
+from typing import Dict, List
 
 _ENABLED_NVTX = os.environ.get("FASTAFD_NVTX", "0") == "1"
 _STEP_RE = re.compile(r"step[=_]?(\d+)")

@@ -33,8 +33,7 @@ import torch
 from .. import ops
 from ..config import ModelConfig, RuntimeConfig
 from ..models.transformer import AttentionStage, AttnMeta, GDNStatePool, KVPool
-from ..protocol import AgStepPlan, AgStepReply, MicroBatchPlan
-from ..reference import ops_ref as ref
+from ..protocol import AgStepPlan, AgStepReply
 from ..utils.trace import nvtx_range
 from .moe_client import MoeClient
 
