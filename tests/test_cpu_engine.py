@@ -59,3 +59,14 @@ def test_radix_prefix_cache_through_the_engine_gives_the_same_tokens_and_shares_
     assert radix == naive
     assert lane.cache.cached_pages >= len(prefix) // 16          # the shared prefix stayed cached
     assert lane.prefix_hit_len(prefix + [1, 2, 3]) >= (len(prefix) // 16) * 16
+
+
+def test_validate_cli_reports_full_agreement_on_cpu(capsys):
+    import json
+
+    from fastafd_b200 import validate
+
+    rc = validate.main(["--device", "cpu", "--prompts", "2", "--prompt-len", "12", "--decode", "5"])
+    out = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert rc == 0 and out["verdict"] == "pass" and out["match"] == 1.0 and out["tokens"] == 10
+    assert validate.first_divergence([1, 2, 3], [1, 2, 4]) == 2 and validate.first_divergence([1], [1, 2]) == 1

@@ -61,3 +61,52 @@ def test_ray_backend_is_refused_where_ray_is_missing():
         parse_args(["--mode", "afd-serve", "--model-path", "tiny-qwen3-moe", "--device", "cpu", "--launch-backend", "ray"])
     with pytest.raises(sr.RayUnavailable):                        # and by the supervisor itself
         sr.RaySupervisor(server_args=None)
+
+
+def _sleep_forever(path):
+    import os
+    import time
+    with open(path, "w") as f:
+        f.write(str(os.getpid()))
+    time.sleep(600)
+
+
+def _parent_that_dies(path):
+    """Starts a backend-style child through the supervisor's entry, then dies without any clean-up."""
+    import multiprocessing as mp
+    import os
+    import time
+
+    from fastafd_b200.server.supervisor import _child_entry
+    p = mp.get_context("spawn").Process(target=_child_entry, args=(_sleep_forever, (path,)), daemon=False)
+    p.start()
+    for _ in range(200):
+        if os.path.exists(path) and os.path.getsize(path) > 0:
+            break
+        time.sleep(0.05)
+    os._exit(0)            # no atexit, no join: the child is orphaned
+
+
+def test_backend_process_leaves_when_its_parent_is_gone(tmp_path):
+    import multiprocessing as mp
+    import os
+    import time
+
+    path = str(tmp_path / "child.pid")
+    parent = mp.get_context("spawn").Process(target=_parent_that_dies, args=(path,))
+    parent.start()
+    parent.join(60)
+    assert os.path.exists(path)
+    pid = int(open(path).read())
+    deadline = time.time() + 20
+    alive = True
+    while time.time() < deadline:
+        try:
+            os.kill(pid, 0)
+        except ProcessLookupError:
+            alive = False
+            break
+        time.sleep(0.2)
+    if alive:
+        os.kill(pid, 9)        # exact PID of the child this test started
+    assert not alive, "the child outlived its parent"
