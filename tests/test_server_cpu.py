@@ -164,3 +164,43 @@ def test_interactive_shell_keeps_context_and_resets():
     assert turns == 3
     assert "(conversation cleared)" in out.getvalue()
     assert out.getvalue().count(">>> ") == 6
+
+
+def test_load_client_against_cpu_server_closed_batch_and_trace_replay():
+    """The benchmark client (closed batch and open-loop trace replay) against a colocated CPU
+    server: every request streams its tokens, TTFT / TPOT come out finite."""
+    import asyncio
+
+    import requests
+    import uvicorn
+
+    from fastafd_b200.benchmark import client
+    from fastafd_b200.server.api_server import FrontendManager, create_app
+    from fastafd_b200.server.supervisor import LocalSupervisor
+
+    args = parse_args(["--mode", "serve", "--model-path", "tiny-qwen3-moe", "--device", "cpu", "--num-pages", "64",
+                       "--max-seq-len-override", "128", "--afd-max-running-requests", "8", "--cuda-graph-max-bs", "8"])
+    sup = LocalSupervisor(args)
+    addrs = sup.start()
+    port = _free_port()
+    server = None
+    try:
+        app = create_app(FrontendManager(addrs.to_tokenizer, addrs.from_tokenizer), args.model_path)
+        server = uvicorn.Server(uvicorn.Config(app, host="127.0.0.1", port=port, log_level="warning"))
+        threading.Thread(target=server.run, daemon=True).start()
+        for _ in range(100):
+            try:
+                if requests.get(f"http://127.0.0.1:{port}/v1/models", timeout=1).ok:
+                    break
+            except Exception:
+                time.sleep(0.1)
+        res = asyncio.run(client.run("127.0.0.1", port, num=3, prompt_len=12, max_tokens=4, vocab=1024))
+        assert res["requests"] == 3 and res["failed"] == 0 and res["output_tokens"] == 12
+        assert res["ttft_ms_p50"] > 0 and res["tpot_ms_p50"] > 0
+        entries = [client.TraceEntry(0.0, 8, 3), client.TraceEntry(0.2, 10, 2)]
+        rep = asyncio.run(client.replay("127.0.0.1", port, entries, vocab=1024))
+        assert rep["requests"] == 2 and rep["failed"] == 0 and rep["output_tokens"] == 5
+    finally:
+        if server is not None:
+            server.should_exit = True
+        sup.shutdown()
