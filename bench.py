@@ -60,7 +60,8 @@ def reference_arm(args) -> None:
     """The unmodified reference (baseline/_ref) cannot serve on this image: its AFD mode starts
     every worker as a Ray actor and Ray is not installed; its colocated mode needs a Hugging
     Face checkpoint directory plus FlashInfer trtllm-gen cubins fetched at run time (no network)."""
-    reason = "reference needs Ray actors (not installed) and run-time cubin/JIT downloads; see DESIGN.md"
+    reason = ("reference AFD workers are Ray actors (Ray is not installed); its kernels need tvm_ffi (absent) and "
+              "FlashInfer cubin downloads (no network); its vendored DeepEP names a call that is closed on this pool")
     try:
         import ray  # noqa: F401
         reason = "reference AFD needs a HF checkpoint on disk and FlashInfer cubin downloads (no network)"
