@@ -347,38 +347,35 @@ class SpmdDriver:
             self.step_id += 1
             real = max(l.decode_real() for l in self.lanes)
             bucket = select_bucket(per_mb_real(real, rt.num_mb), e.buckets)
-            plans = [l.schedule_decode(sid, bucket) for l in self.lanes]
+            # Only this rank's lane is planned in full; the other lanes are advanced as shadows
+            # (their sizes decide the common bucket, their pages and plans belong to other ranks).
+            mine = None
+            for lane, l in enumerate(self.lanes):
+                if e.attn is not None and lane == self.my_lane:
+                    mine = l.schedule_decode(sid, bucket)
+                else:
+                    l.shadow_decode()
             if e.attn is not None:
-                mine = plans[self.my_lane]
                 e.attn.launch_decode(mine)
                 if pending is not None:
                     produced += self._finish_fast(*pending)
                     pending = None
                 if pipelined:
-                    pending = (sid, plans, mine)
+                    pending = (sid, mine)
                 else:
-                    produced += self._finish_fast(sid, plans, mine)
+                    produced += self._finish_fast(sid, mine)
             if e.expert is not None:
                 e.step(EgStepPlan(step_id=sid, phase="decode", tokens_per_mb=[bucket // e.topo.attn_tp] * rt.num_mb))
-            if e.attn is None:
-                for lane, l in enumerate(self.lanes):
-                    l.complete(sid, np.zeros(sum(len(mb.rows) for mb in plans[lane].mbs), np.int32))
         if pending is not None:
             produced += self._finish_fast(*pending)
         return produced
 
-    def _finish_fast(self, sid: int, plans, mine) -> int:
+    def _finish_fast(self, sid: int, mine) -> int:
         reply = self.e.attn.finish_decode(mine)
         if reply.status:
             raise RuntimeError(f"device status {reply.status} in step {sid}")
-        n = 0
-        for lane, l in enumerate(self.lanes):
-            size = sum(len(mb.rows) for mb in plans[lane].mbs)
-            toks = reply.next_tokens if lane == self.my_lane else np.zeros(size, np.int32)
-            out = l.complete(sid, toks)
-            if lane == self.my_lane:
-                n += sum(len(t) for _, t, _ in out)
-        return n
+        out = self.lanes[self.my_lane].complete(sid, reply.next_tokens)
+        return sum(len(t) for _, t, _ in out)
 
     def generate(self, prompts: Sequence[Sequence[int]], sampling: SamplingParams) -> List[List[int]]:
         uids = self.add_requests(prompts, sampling)

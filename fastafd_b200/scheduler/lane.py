@@ -283,6 +283,19 @@ class LaneScheduler:
             record.slots.append(slots)
         return self._finish_plan(step_id, record.phase, bucket, mbs, grants, record, sampling_rows)
 
+    def shadow_decode(self, tokens_per_req: int = 1) -> int:
+        """Advance this lane by one decode step without planning it: only the counters that decide
+        how many requests are still decoding move (no pages, no plan, no record). For a process
+        that does not serve this lane but must know its size to agree on the step's bucket.
+        Returns the number of requests that took part."""
+        n = 0
+        for st in self.states.values():
+            if not st.dead and st.planned_len >= st.req.prompt_len and st.planned_out < st.req.sampling.max_tokens:
+                st.planned_len += tokens_per_req
+                st.planned_out += 1
+                n += 1
+        return n
+
     def dummy_step(self, step_id: int, phase: str, bucket: int, prefill_tokens: Sequence[int] = ()) -> AgStepPlan:
         """A lane with nothing to do still takes part in every step (N2M / M2N involve all ranks)."""
         mbs, record = [], StepRecord(step_id, phase)

@@ -61,3 +61,42 @@ def test_gloo_afd_matches_single_process(topo_kw):
         mp.spawn(_worker, args=(world, _free_port(), topo_kw, path, n_new), nprocs=world, join=True)
         got = torch.load(path)
     assert got == exp
+
+
+def _steps_worker(rank, world, port, topo_kw, out_path):
+    """The benchmark's flow: prefilled requests, then decode steps in lock-step and one step ahead."""
+    os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    torch.set_num_threads(1)
+    cfg = PRESETS["tiny-qwen3-moe"]
+    topo = AfdTopology(**topo_kw)
+    eng = AfdEngine(cfg, _rt(), topo, rank, "cpu", seed=0)
+    drv = SpmdDriver(eng)
+    # 9 tokens each, the first of which the (skipped) prefill already produced: 8 decode steps drain the batch
+    drv.install_prefilled(6, 20, max_tokens=9)
+    a = drv.run_decode_steps(4, pipelined=False)
+    b = drv.run_decode_steps(5, pipelined=True)
+    c = drv.run_decode_steps(3, pipelined=False)         # nothing left to decode: empty steps
+    res = torch.tensor([a, b, c, max(l.decode_real() for l in drv.lanes)])
+    out = [torch.zeros(4, dtype=torch.int64) for _ in range(world)]
+    dist.all_gather(out, res)
+    if rank == 0:
+        torch.save(torch.stack(out), out_path)
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_decode_step_driver_keeps_ranks_in_step_with_shadow_lanes():
+    """Every rank plans only its own lane and advances the others as shadows; all ranks must agree
+    on the bucket of every step (else the gloo exchange would block) and attention ranks must
+    produce exactly their lane's tokens, including the steps in which the batch runs dry."""
+    topo_kw = dict(attn_dp=2, mlp_ep=2)
+    world = 4
+    with tempfile.TemporaryDirectory() as d:
+        path = os.path.join(d, "out.pt")
+        mp.spawn(_steps_worker, args=(world, _free_port(), topo_kw, path), nprocs=world, join=True)
+        res = torch.load(path)
+    for r in range(2):                                   # attention ranks: 6 requests x (4 + 4) tokens, then none
+        assert res[r].tolist() == [24, 24, 0, 0]
+    for r in range(2, 4):                                # expert ranks produce no tokens but see the same drain
+        assert res[r].tolist() == [0, 0, 0, 0]
