@@ -87,8 +87,12 @@ class AfdEngine:
         self.fabric = None
         self.attn: Optional[AttentionWorker] = None
         self.expert: Optional[ExpertWorker] = None
-        if not self.colocated and topo.mlp_tp > 1:
-            raise NotImplementedError("experts are sharded by expert parallelism only (mlp_tp must be 1)")
+        # MLP TP with mlp_ep == 1: the ranks of a replica all hold every expert with a slice of the
+        # intermediate dimension and return partial sums (host path only). mlp_ep == mlp_tp means
+        # expert parallelism inside the TP group, i.e. plain EP.
+        mlp_tp_shard = (not self.colocated) and topo.mlp_tp > 1 and topo.mlp_ep == 1
+        if mlp_tp_shard and cuda:
+            raise NotImplementedError("MLP tensor parallelism is built for the gloo path only; use expert parallelism on GPUs")
         # One replica of the expert set (mlp_dp of them) serves the lanes l with l % mlp_dp == replica:
         # an attention rank talks to its replica's expert ranks, an expert rank to its lanes' ranks.
         if self.colocated:
@@ -106,7 +110,11 @@ class AfdEngine:
         stage = None
         if self.is_expert and cfg.is_moe and os.environ.get("FASTAFD_DEBUG_NULL_MOE") != "1":
             ep_rank = 0 if self.colocated else topo.ep_rank(rank)
-            stage = ExpertStage(cfg, self.device, self.dtype, ep_rank, num_eg).init_random(seed, fast=fast_init)
+            if mlp_tp_shard:
+                stage = ExpertStage(cfg, self.device, self.dtype, 0, 1, tp_rank=ep_rank, tp_size=topo.mlp_tp)
+            else:
+                stage = ExpertStage(cfg, self.device, self.dtype, ep_rank, num_eg)
+            stage.init_random(seed, fast=fast_init)
         self.expert_stage = stage
 
         from .worker.moe_client import MoeClient

@@ -458,9 +458,19 @@ class ExpertStage:
     On CUDA the gate/up rows are re-laid out for the SWIGLU epilogue of the grouped GEMM, and
     with block-FP8 weights the scales are turned into per-tile scale tables."""
 
-    def __init__(self, cfg: ModelConfig, device, dtype, ep_rank: int = 0, ep_size: int = 1):
+    def __init__(self, cfg: ModelConfig, device, dtype, ep_rank: int = 0, ep_size: int = 1,
+                 tp_rank: int = 0, tp_size: int = 1):
         self.cfg, self.device, self.dtype = cfg, torch.device(device), dtype
         self.ep_rank, self.ep_size = ep_rank, ep_size
+        # MLP tensor parallelism: every rank of the TP group holds all of its experts with 1/tp of
+        # the intermediate dimension (gate / up rows and down columns) and returns partial rows
+        # that the attention side sums. Host (gloo) path only.
+        self.tp_rank, self.tp_size = tp_rank, tp_size
+        if tp_size > 1:
+            if self.device.type == "cuda":
+                raise NotImplementedError("MLP tensor parallelism is built for the gloo path only")
+            if cfg.moe_intermediate_size % tp_size != 0:
+                raise ValueError("moe_intermediate_size must be a multiple of the MLP TP size")
         self.experts_local = (cfg.num_experts + ep_size - 1) // ep_size
         self.expert_base = ep_rank * self.experts_local
         self.moe_layers = [i for i in range(cfg.num_layers) if cfg.is_moe_layer(i)]
@@ -506,7 +516,12 @@ class ExpertStage:
             if gate_up.dtype == torch.float8_e4m3fn:
                 gate_up = torch.stack([ref.block_dequant_fp8(gate_up[e], gate_up_scale[e]) for e in range(gate_up.shape[0])])
                 down = torch.stack([ref.block_dequant_fp8(down[e], down_scale[e]) for e in range(down.shape[0])])
-            self.gate_up[layer], self.down[layer] = gate_up.to(self.dtype), down.to(self.dtype)
+            if self.tp_size > 1:
+                I = c.moe_intermediate_size
+                lo, hi = self.tp_rank * (I // self.tp_size), (self.tp_rank + 1) * (I // self.tp_size)
+                gate_up = torch.cat([gate_up[:, lo:hi], gate_up[:, I + lo:I + hi]], dim=1)
+                down = down[:, :, lo:hi]
+            self.gate_up[layer], self.down[layer] = gate_up.to(self.dtype).contiguous(), down.to(self.dtype).contiguous()
             return
         if c.quant.is_fp8:
             if gate_up.dtype != torch.float8_e4m3fn:

@@ -48,8 +48,9 @@ def _worker(rank, world, port, topo_kw, out_path, n_new):
 
 @pytest.mark.parametrize("topo_kw", [dict(attn_dp=1, mlp_ep=1), dict(attn_dp=2, mlp_ep=2),
                                      dict(attn_dp=1, attn_tp=2, mlp_ep=2),
-                                     dict(attn_dp=2, mlp_dp=2, mlp_ep=1)],          # two expert replicas, one per lane
-                         ids=["1+1", "dp2+ep2", "tp2+ep2", "dp2+mlpdp2"])
+                                     dict(attn_dp=2, mlp_dp=2, mlp_ep=1),           # two expert replicas, one per lane
+                                     dict(attn_dp=1, mlp_tp=2, mlp_ep=1)],          # experts sharded along the intermediate dim
+                         ids=["1+1", "dp2+ep2", "tp2+ep2", "dp2+mlpdp2", "1+mlptp2"])
 def test_gloo_afd_matches_single_process(topo_kw):
     cfg = PRESETS["tiny-qwen3-moe"]
     n_new = 16
