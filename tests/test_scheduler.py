@@ -166,3 +166,32 @@ def test_page_audit_runs_every_step_and_catches_a_corrupted_ledger(monkeypatch, 
     s.cache._n_free += 1
     with pytest.raises(RuntimeError, match="page audit|corrupted"):
         s.audit_pages()
+
+
+def test_kv_page_sizing(monkeypatch):
+    """Pages from free memory: bytes per page follow the model (full-attention layers only for the
+    hybrid family, KV heads per TP rank), an explicit count wins, and the request cap bounds it."""
+    import torch
+
+    from fastafd_b200.config import PRESETS, RuntimeConfig
+    from fastafd_b200.models.transformer import KVPool
+    from fastafd_b200.worker import attention_worker as aw
+
+    cfg = PRESETS["qwen3-235b-a22b-fp8"]
+    per_page = KVPool.bytes_per_page(cfg, 16, cfg.num_kv_heads)
+    assert per_page == 94 * 2 * 16 * 4 * 128 * 2                    # layers x (K, V) x tokens x heads x dim x bf16
+    assert KVPool.bytes_per_page(cfg, 16, 1) * 4 == per_page        # TP-4 rank holds one KV head
+    hybrid = PRESETS["qwen3.5-397b-a17b-fp8"]
+    full_layers = sum(1 for l in range(hybrid.num_layers) if hybrid.layer_type(l) == "full")
+    assert KVPool.bytes_per_page(hybrid, 16, 2) == full_layers * 2 * 16 * 2 * hybrid.head_dim * 2
+
+    rt = RuntimeConfig(page_size=16, max_running_requests=88, max_seq_len=8400, memory_ratio=0.9, device="cuda")
+    monkeypatch.setattr(torch.cuda, "mem_get_info", lambda d: (170 << 30, 180 << 30))
+    dev = torch.device("cuda", 0)
+    want = 88 * (8400 // 16) + 1
+    assert aw.determine_num_pages(cfg, rt, dev, cfg.num_kv_heads) == want          # everything fits: the request cap rules
+    monkeypatch.setattr(torch.cuda, "mem_get_info", lambda d: (40 << 30, 180 << 30))
+    got = aw.determine_num_pages(cfg, rt, dev, cfg.num_kv_heads)
+    assert got == (int((40 << 30) * 0.9) - (2 << 30)) // per_page < want          # memory rules
+    rt2 = RuntimeConfig(page_size=16, max_running_requests=88, max_seq_len=8400, num_pages=777, device="cuda")
+    assert aw.determine_num_pages(cfg, rt2, dev, cfg.num_kv_heads) == 777
