@@ -95,6 +95,9 @@ def _host_lib():
             for fn in (lib.afd_mismatch_i32, lib.afd_mismatch_i64):
                 fn.restype = C.c_int64
                 fn.argtypes = [C.c_void_p, C.c_void_p, C.c_int64]
+            lib.afd_decode_out_loc.restype = C.c_int64
+            lib.afd_decode_out_loc.argtypes = [C.c_void_p, C.c_int64, C.c_void_p, C.c_void_p, C.c_int64, C.c_int32,
+                                               C.c_int64, C.c_void_p]
             _HOST_LIB = lib
         except (OSError, RuntimeError):
             _HOST_LIB = False
@@ -117,6 +120,32 @@ def mismatch_index(a: Sequence[int], b: Sequence[int]) -> int:
         return int(fn(a.ctypes.data, b.ctypes.data, n))
     neq = np.nonzero(a[:n] != b[:n])[0]
     return int(neq[0]) if len(neq) else n
+
+
+def decode_out_loc(page_table: np.ndarray, rows: np.ndarray, positions: np.ndarray, page_size: int,
+                   num_pages: int) -> np.ndarray:
+    """KV slot of each request's next token: page_table[row][pos // page_size] * page_size +
+    pos % page_size, for int32 arrays (page_table 2-D, C-contiguous). Raises if a request's page is
+    missing (negative entry) or outside the pool - the host-side twin of the bounds check that the
+    store kernel makes on the device."""
+    pt = np.ascontiguousarray(page_table, dtype=np.int32)
+    rows = np.ascontiguousarray(rows, dtype=np.int32)
+    pos = np.ascontiguousarray(positions, dtype=np.int32)
+    out = np.empty(len(rows), dtype=np.int32)
+    lib = _host_lib()
+    if lib is not None:
+        bad = int(lib.afd_decode_out_loc(pt.ctypes.data, pt.shape[1], rows.ctypes.data, pos.ctypes.data, len(rows),
+                                         page_size, num_pages, out.ctypes.data))
+    else:
+        col = pos // page_size
+        ok = (pos >= 0) & (col < pt.shape[1])
+        pages = np.where(ok, pt[rows, np.minimum(col, pt.shape[1] - 1)], -1)
+        ok &= (pages >= 0) & (pages < num_pages)
+        bad = int(np.argmin(ok)) if not ok.all() else -1
+        out[:] = pages * page_size + pos % page_size
+    if bad >= 0:
+        raise IndexError(f"request {bad} (table row {int(rows[bad])}, position {int(pos[bad])}) has no valid KV page")
+    return out
 
 
 class RadixPageCache(NaivePageLedger):

@@ -195,3 +195,22 @@ def test_kv_page_sizing(monkeypatch):
     assert got == (int((40 << 30) * 0.9) - (2 << 30)) // per_page < want          # memory rules
     rt2 = RuntimeConfig(page_size=16, max_running_requests=88, max_seq_len=8400, num_pages=777, device="cuda")
     assert aw.determine_num_pages(cfg, rt2, dev, cfg.num_kv_heads) == 777
+
+
+def test_decode_out_loc_native_and_bounds():
+    import numpy as np
+
+    from fastafd_b200.scheduler import cache
+
+    rng = np.random.default_rng(1)
+    pt = rng.integers(1, 50, size=(8, 6)).astype(np.int32)
+    rows = np.array([3, 0, 7, 3], np.int32)
+    pos = np.array([0, 17, 95, 40], np.int32)
+    got = cache.decode_out_loc(pt, rows, pos, 16, 50)
+    want = pt[rows, pos // 16] * 16 + pos % 16
+    assert got.tolist() == want.tolist()
+    pt[7, 5] = -1
+    with pytest.raises(IndexError, match="request 2"):
+        cache.decode_out_loc(pt, rows, pos, 16, 50)
+    with pytest.raises(IndexError, match="request 1"):
+        cache.decode_out_loc(pt, rows, np.array([0, 96, 1, 1], np.int32), 16, 50)     # past the last column
