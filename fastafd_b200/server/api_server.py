@@ -172,6 +172,19 @@ def create_app(manager: FrontendManager, model_name: str) -> FastAPI:
             return JSONResponse({"error": "give exactly one of prompt, messages, input_ids"}, status_code=400)
         msgs = [m.model_dump() for m in req.messages] if req.messages else None
         uid = await manager.submit(text=req.prompt, messages=msgs, input_ids=req.input_ids, sampling=_sampling(req))
+        if not req.stream:
+            # one JSON body once the request has finished (OpenAI "stream": false)
+            r = await manager.collect(uid)
+            choice: Dict[str, Any] = {"index": 0, "message": {"role": "assistant", "content": r.text},
+                                      "finish_reason": "error" if r.error else "stop"}
+            if req.return_token_ids:
+                choice["token_ids"] = r.token_ids
+            body: Dict[str, Any] = {"id": f"cmpl-{uid}", "object": "chat.completion", "created": created,
+                                    "model": model_name, "choices": [choice],
+                                    "usage": {"completion_tokens": len(r.token_ids or [])}}
+            if r.error:
+                body["error"] = r.error
+            return JSONResponse(body, status_code=400 if r.error else 200)
         first = {"sent_role": False}
 
         def chunk(delta: Dict[str, Any], finish=None, token_ids=None) -> str:

@@ -120,6 +120,11 @@ def test_http_round_trip_cpu_afd(mode, cache):
                                                                       "temperature": 0, "ignore_eos": True,
                                                                       "return_token_ids": True}, timeout=120).json()
         assert [len(c["token_ids"]) for c in rb["choices"]] == [3, 3]
+        whole = requests.post(base + "/v1/chat/completions", json={"input_ids": [1, 2, 3, 4, 5], "max_tokens": 4, "temperature": 0,
+                                                                   "ignore_eos": True, "return_token_ids": True,
+                                                                   "stream": False}, timeout=120).json()
+        assert whole["object"] == "chat.completion" and whole["choices"][0]["token_ids"] == toks      # same greedy tokens
+        assert whole["usage"]["completion_tokens"] == 4 and whole["choices"][0]["finish_reason"] == "stop"
         bad = requests.post(base + "/v1/chat/completions", json={"input_ids": [99999], "max_tokens": 2}, stream=True, timeout=60)
         assert "outside the vocabulary" in bad.text
         assert sup.get_failures() == []
