@@ -205,6 +205,13 @@ def create_app(manager: FrontendManager, model_name: str) -> FastAPI:
         tail = [chunk({}, finish="stop"), "data: [DONE]\n\n"]
         return StreamingResponse(sse_with_abort(request, uid, fmt, tail), media_type="text/event-stream")
 
+    # text-completion clients post {"prompt": ...} to /v1/completions: same request model and replies
+    app.post("/v1/completions")(chat)
+
+    @app.get("/health")
+    async def health():
+        return {"status": "ok"}
+
     @app.post("/v1/chat/completions/batch")
     async def chat_batch(req: BatchCompletionRequest):
         if (req.prompts is None) == (req.messages_batch is None):

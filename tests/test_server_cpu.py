@@ -125,6 +125,10 @@ def test_http_round_trip_cpu_afd(mode, cache):
                                                                    "stream": False}, timeout=120).json()
         assert whole["object"] == "chat.completion" and whole["choices"][0]["token_ids"] == toks      # same greedy tokens
         assert whole["usage"]["completion_tokens"] == 4 and whole["choices"][0]["finish_reason"] == "stop"
+        assert requests.get(base + "/health").json() == {"status": "ok"}
+        legacy = requests.post(base + "/v1/completions", json={"prompt": "ab", "max_tokens": 3, "temperature": 0, "ignore_eos": True,
+                                                               "return_token_ids": True, "stream": False}, timeout=120).json()
+        assert len(legacy["choices"][0]["token_ids"]) == 3
         bad = requests.post(base + "/v1/chat/completions", json={"input_ids": [99999], "max_tokens": 2}, stream=True, timeout=60)
         assert "outside the vocabulary" in bad.text
         assert sup.get_failures() == []
