@@ -106,6 +106,10 @@ def validate(args: ServerArgs) -> None:
         raise ValueError("--page-size must be a power of two")
     if not 1 <= args.afd_num_mb <= 4:
         raise ValueError("--afd-num-mb must be between 1 and 4")
+    from ..spec.config import SpecConfig
+    spec = SpecConfig.from_env(args.spec_block, args.spec_draft_path)     # FASTAFD_SPEC* may switch it on without flags
+    if spec.enabled:
+        args.spec_block, args.spec_draft_path = spec.block, spec.draft_path
     if args.spec_block and args.afd_attn_tp_size != 1:
         raise ValueError("speculative decoding needs attention TP 1")
     if args.spec_block and args.cache_type != "naive":

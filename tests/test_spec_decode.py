@@ -53,3 +53,29 @@ def test_self_draft_accepts_everything():
     target = torch.tensor([[3, 4, 5, 6]])
     n, _ = ref.greedy_accept(target[:, :3], target)
     assert n.tolist() == [4]
+
+
+def test_spec_config_from_flags_and_environment(monkeypatch):
+    from fastafd_b200.server.args import parse_args
+    from fastafd_b200.spec.config import SpecConfig, SpecConfigError
+
+    for k in ("FASTAFD_SPEC", "FASTAFD_SPEC_BLOCK", "FASTAFD_SPEC_DRAFT", "FASTAFD_SPEC_SIM_ACCEPT", "MINISGL_AFD_SPEC"):
+        monkeypatch.delenv(k, raising=False)
+    assert SpecConfig.from_env() == SpecConfig()                                   # off by default
+    c = SpecConfig.from_env(block_flag=4, draft_flag="/d")
+    assert c.enabled and c.block == 4 and c.num_draft_tokens == 3 and c.draft_path == "/d"
+    monkeypatch.setenv("MINISGL_AFD_SPEC", "1")                                    # the reference's name works too
+    monkeypatch.setenv("FASTAFD_SPEC_BLOCK", "8")
+    monkeypatch.setenv("FASTAFD_SPEC_SIM_ACCEPT", "1.8")
+    c = SpecConfig.from_env()
+    assert c.enabled and c.block == 8 and c.sim_accept == 1.8
+    a = parse_args(["--model-path", "tiny-qwen3-moe", "--device", "cpu"])
+    assert a.spec_block == 8                                                       # environment reached the server flags
+    assert parse_args(["--model-path", "tiny-qwen3-moe", "--device", "cpu", "--spec-block", "2"]).spec_block == 2
+    monkeypatch.setenv("FASTAFD_SPEC_SIM_ACCEPT", "9.5")
+    with pytest.raises(SpecConfigError):
+        SpecConfig.from_env()
+    monkeypatch.setenv("FASTAFD_SPEC_SIM_ACCEPT", "0")
+    monkeypatch.setenv("FASTAFD_SPEC_BLOCK", "1")
+    with pytest.raises(SpecConfigError):
+        SpecConfig.from_env()
