@@ -4,6 +4,7 @@
     python -m fastafd_b200.benchmark.suite command qwen3-235b-8k-1to1
     python -m fastafd_b200.benchmark.suite run qwen3-235b-8k-1to1 --out runs/
     python -m fastafd_b200.benchmark.suite summary runs/
+    python -m fastafd_b200.benchmark.suite record qwen3-235b-8k-1to1 runs/qwen3-235b-8k-1to1-<UTC>
 
 ``run`` launches ``bench.py`` of the repository root (one process per GPU through
 ``torch.distributed.run``), stores ``result.json`` (measured step time, throughput, the verdict
@@ -116,6 +117,19 @@ def summary(root: Path) -> List[Dict]:
     return rows
 
 
+def record(name: str, run_dir: Path, path: Path = HERE / "configs.json") -> Dict:
+    """Make the result of a finished run the recorded value of its configuration."""
+    res = json.loads((run_dir / "result.json").read_text())
+    if "step_ms" not in res:
+        raise ValueError(f"{run_dir} holds no measured step time (verdict {res.get('verdict')})")
+    cfgs = json.loads(path.read_text())
+    if name not in cfgs["configs"]:
+        raise KeyError(name)
+    cfgs["configs"][name]["recorded"] = {"step_ms": round(res["step_ms"], 3), "tok_s_per_gpu": round(res["tok_s_per_gpu"])}
+    path.write_text(json.dumps(cfgs, indent=1))
+    return cfgs["configs"][name]["recorded"]
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(prog="fastafd_b200.benchmark.suite")
     sub = ap.add_subparsers(dest="cmd", required=True)
@@ -128,6 +142,9 @@ def main(argv=None) -> int:
         sp.add_argument("--out", default="benchmark-runs")
     sp = sub.add_parser("summary")
     sp.add_argument("root")
+    sp = sub.add_parser("record")
+    sp.add_argument("name")
+    sp.add_argument("run_dir")
     a = ap.parse_args(argv)
     cfgs = load_configs()
     if a.cmd == "list":
@@ -145,6 +162,9 @@ def main(argv=None) -> int:
         res = run(a.name, Path(a.out), a.steps, a.warmup)
         print(json.dumps(res))
         return 0 if res.get("verdict") in ("pass", "unrecorded") else 1
+    if a.cmd == "record":
+        print(json.dumps(record(a.name, Path(a.run_dir))))
+        return 0
     for row in summary(Path(a.root)):
         print(json.dumps(row))
     return 0

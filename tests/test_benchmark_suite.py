@@ -71,3 +71,22 @@ def test_trace_reader_and_scaling(tmp_path):
     assert [(e.at_s, e.input_length) for e in tr] == [(0.0, 50), (2.0, 100), (4.0, 4000)]
     sc = scale_trace(tr, time_scale=0.5, max_requests=3, max_input=1024, max_output=128)
     assert [(e.at_s, e.input_length, e.output_length) for e in sc] == [(0.0, 50, 10), (1.0, 100, 20), (2.0, 1024, 128)]
+
+
+def test_record_and_summary(tmp_path):
+    import shutil
+
+    cfg_copy = tmp_path / "configs.json"
+    shutil.copy(suite.HERE / "configs.json", cfg_copy)
+    run_dir = tmp_path / "runs" / "qwen3-235b-8k-1to1-20260101T000000Z"
+    run_dir.mkdir(parents=True)
+    (run_dir / "config.json").write_text(json.dumps({"name": "qwen3-235b-8k-1to1"}))
+    (run_dir / "result.json").write_text(json.dumps({"step_ms": 33.3333, "tok_s_per_gpu": 1320.4, "verdict": "unrecorded"}))
+    rec = suite.record("qwen3-235b-8k-1to1", run_dir, cfg_copy)
+    assert rec == {"step_ms": 33.333, "tok_s_per_gpu": 1320}
+    assert json.loads(cfg_copy.read_text())["configs"]["qwen3-235b-8k-1to1"]["recorded"] == rec
+    rows = suite.summary(tmp_path / "runs")
+    assert len(rows) == 1 and rows[0]["step_ms"] == 33.3333
+    (run_dir / "result.json").write_text(json.dumps({"verdict": "error", "returncode": 1}))
+    with pytest.raises(ValueError):
+        suite.record("qwen3-235b-8k-1to1", run_dir, cfg_copy)
