@@ -213,3 +213,33 @@ def test_load_client_against_cpu_server_closed_batch_and_trace_replay():
         if server is not None:
             server.should_exit = True
         sup.shutdown()
+
+
+def test_cpu_trace_mirrors_ranges_and_parses_step_ids(tmp_path):
+    import json as _json
+
+    from fastafd_b200.utils import trace
+
+    trace.CPU_TRACE.clear()
+    old = trace.CPU_TRACE.enabled
+    trace.CPU_TRACE.enabled = True
+    try:
+        class Worker:
+            @trace.nvtx_annotate("AFD_AG_Attn_L{}_mb{}")
+            def attn(self, layer, mb):
+                return layer * 10 + mb
+
+        with trace.nvtx_range("decode step=17"):
+            assert Worker().attn(3, 1) == 31
+        names = [e["name"] for e in trace.CPU_TRACE.events]
+        assert names == ["AFD_AG_Attn_L3_mb1", "decode step=17"]        # inner range closes first
+        assert trace.CPU_TRACE.events[1]["step"] == 17 and trace.CPU_TRACE.events[0]["step"] is None
+        assert all(e["dur_us"] >= 0 for e in trace.CPU_TRACE.events)
+        path = trace.CPU_TRACE.dump(str(tmp_path / "run"))
+        assert len(_json.load(open(path))["traceEvents"]) == 2
+    finally:
+        trace.CPU_TRACE.enabled = old
+        trace.CPU_TRACE.clear()
+    with trace.nvtx_range("off"):                                        # disabled: no event, no error
+        pass
+    assert trace.CPU_TRACE.events == []
