@@ -243,3 +243,38 @@ def test_cpu_trace_mirrors_ranges_and_parses_step_ids(tmp_path):
     with trace.nvtx_range("off"):                                        # disabled: no event, no error
         pass
     assert trace.CPU_TRACE.events == []
+
+
+def test_env_knobs_answer_to_all_prefixes_and_reject_bad_values(monkeypatch):
+    from fastafd_b200.env import ENV, afd_env
+
+    for n in ENV.FLAG_TIMEOUT_S.names():
+        monkeypatch.delenv(n, raising=False)
+    assert ENV.FLAG_TIMEOUT_S.value == 20.0
+    monkeypatch.setenv("MINISGL_FLAG_TIMEOUT_S", "3")           # least specific name
+    assert ENV.FLAG_TIMEOUT_S.value == 3.0
+    monkeypatch.setenv("MINISGL_AFD_FLAG_TIMEOUT_S", "5")       # the reference's AFD prefix wins over it
+    assert ENV.FLAG_TIMEOUT_S.value == 5.0
+    monkeypatch.setenv("FASTAFD_FLAG_TIMEOUT_S", "7.5")         # this framework's own name wins over both
+    assert ENV.FLAG_TIMEOUT_S.value == 7.5
+    monkeypatch.setenv("FASTAFD_FLAG_TIMEOUT_S", "soon")
+    with pytest.raises(ValueError, match="FASTAFD_FLAG_TIMEOUT_S"):
+        ENV.FLAG_TIMEOUT_S.value
+    monkeypatch.setenv("MINISGL_AFD_MODE", "cad")
+    monkeypatch.delenv("FASTAFD_MODE", raising=False)
+    assert afd_env("MODE") == "cad" and afd_env("NO_SUCH_KNOB", "x") == "x"
+
+
+def test_buffered_log_file_flushes_by_count_and_on_demand(tmp_path):
+    from fastafd_b200.utils.logger import BufferedLogFile
+
+    path = tmp_path / "logs" / "w.log"
+    log = BufferedLogFile(str(path), interval_s=3600.0, max_lines=3)
+    log.line("a")
+    log.line("b")
+    assert not path.exists() or path.read_text() == ""          # still buffered
+    log.line("c")                                               # third line reaches max_lines
+    assert [ln.split(" ", 1)[1] for ln in path.read_text().splitlines()] == ["a", "b", "c"]
+    log.line("d")
+    log.flush()
+    assert path.read_text().splitlines()[-1].endswith(" d")
