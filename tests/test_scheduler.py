@@ -214,3 +214,22 @@ def test_decode_out_loc_native_and_bounds():
         cache.decode_out_loc(pt, rows, pos, 16, 50)
     with pytest.raises(IndexError, match="request 1"):
         cache.decode_out_loc(pt, rows, np.array([0, 96, 1, 1], np.int32), 16, 50)     # past the last column
+
+
+def test_attention_split_policy_matches_the_measured_optima():
+    """pick_attn_splits is fitted to a sweep on B200 (profiles/decode_attention_paged_gqa.txt): these
+    are the cases of that sweep, with the split count that was fastest (or within noise of it)."""
+    from fastafd_b200.ops import pick_attn_splits as pick
+
+    assert pick(64, 4, 1, 1040) == 1          # 256 CTAs already: more splits would need a second wave
+    assert pick(32, 4, 1, 1040) == 2
+    assert pick(16, 4, 1, 4096) == 4
+    assert pick(44, 4, 1, 8200) == 2
+    assert pick(8, 4, 1, 1040) == 4           # bounded by 256 tokens per split
+    assert pick(1, 1, 1, 100) == 1            # never splits below 256 tokens
+    assert pick(1, 4, 1, 131072) <= 32        # bounded by the merge table
+    for B in (1, 3, 17, 100, 300):
+        for kv in (64, 1000, 9000, 70000):
+            s = pick(B, 4, 1, kv)
+            assert 1 <= s <= 32 and (s == 1 or kv // s >= 256) and (s == 1 or B * 4 * s <= 148 * 3)
+    assert pick(8, 2, 1, 16384, D=256) >= 1 and pick(200, 2, 1, 16384, D=256) == 1   # head_dim 256: one CTA per SM
