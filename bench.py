@@ -33,7 +33,7 @@ import time
 HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, HERE)
 
-# Published reference numbers (GB200 NVL72, 4 attention + 4 FFN GPUs), tok/s/GPU; BASELINE.md.
+# Published reference numbers (GB200 NVL72, 4 attention + 4 FFN GPUs, scripts/benchmark/configs.json:366), tok/s/GPU.
 PUBLISHED_TOK_S_PER_GPU = {"qwen3-235b-a22b-fp8": 1542.0}
 METRIC = "decode tok/s, AFD (attention + expert GPUs), aggregate over all GPUs"
 
@@ -57,18 +57,16 @@ def parse_args():
 
 
 def reference_arm(args) -> None:
-    """The unmodified reference (baseline/_ref) cannot serve on this image: its AFD mode starts
-    every worker as a Ray actor and Ray is not installed; its colocated mode needs a Hugging
-    Face checkpoint directory plus FlashInfer trtllm-gen cubins fetched at run time (no network)."""
-    reason = ("reference AFD workers are Ray actors (Ray is not installed); its kernels need tvm_ffi (absent) and "
-              "FlashInfer cubin downloads (no network); its vendored DeepEP names a call that is closed on this pool")
-    try:
-        import ray  # noqa: F401
-        reason = "reference AFD needs a HF checkpoint on disk and FlashInfer cubin downloads (no network)"
-    except Exception:
-        pass
+    """Runs the unmodified reference (baseline/_ref) through its own offline API; see
+    baseline/reference_arm.py. Prints the same JSON line with "impl": "reference", or an
+    "unavailable" line whose reason is the text of the failed attempt."""
+    sys.path.insert(0, os.path.join(HERE, "baseline"))
+    import reference_arm as ref
+
+    args.metric = METRIC
+    out = ref.run(args, clock_sampler_cls=ClockSampler)
     if int(os.environ.get("RANK", "0")) == 0:
-        print(json.dumps({"impl": "reference", "unavailable": reason}))
+        print(json.dumps(out), flush=True)
 
 
 class ClockSampler:

@@ -521,13 +521,20 @@ static int launch_decode(const DecodeAttnArgs& a, cudaStream_t st) {
 
 }  // namespace afd
 
-// Workspace needed for `splits` > 1, in bytes: part_o then part_lse.
+// Split-KV workspace layout, in bytes from the start:
+//   [0, kCounterRegionBytes)   one arrival counter per (request, kv head, row tile); they must be
+//                              zero when a launch starts and every launch leaves them zero again
+//   then part_o  [tiles][16][D] fp32, then part_lse [tiles][16] fp32
+// The counters sit in FRONT of the partials at an offset that does not depend on (B, splits), so a
+// workspace that is zeroed once can be shared by launches of any shape: a later launch never finds
+// its counters on top of an earlier launch's partial results.
+static constexpr long kCounterRegionBytes = 256 * 1024;
+
 extern "C" long afd_decode_attn_workspace_bytes(int B, int Hq, int Hkv, int q_len, int D, int splits) {
   const int G = Hq / Hkv;
   const long m_tiles = (G * q_len + 15) / 16;
   const long tiles = static_cast<long>(B) * Hkv * m_tiles * splits;
-  // partial outputs, partial log-sum-exps, and one arrival counter per (request, head, row tile)
-  return tiles * 16 * D * 4 + tiles * 16 * 4 + static_cast<long>(B) * Hkv * m_tiles * 4;
+  return kCounterRegionBytes + tiles * 16 * D * 4 + tiles * 16 * 4;
 }
 
 extern "C" int afd_decode_attention_strided(const void* q, long q_stride, const void* k_cache,
@@ -574,9 +581,10 @@ extern "C" int afd_decode_attention_strided(const void* q, long q_stride, const 
   a.scale_log2 = sm_scale * 1.4426950408889634f;
   a.status = static_cast<int*>(status);
   const long tiles = static_cast<long>(B) * Hkv * a.m_tiles * splits;
-  a.part_o = static_cast<float*>(workspace);
+  if (splits > 1 && static_cast<long>(B) * Hkv * a.m_tiles * 4 > kCounterRegionBytes) return -7;
+  a.part_count = static_cast<unsigned int*>(workspace);
+  a.part_o = workspace ? reinterpret_cast<float*>(static_cast<char*>(workspace) + kCounterRegionBytes) : nullptr;
   a.part_lse = a.part_o ? a.part_o + tiles * 16 * D : nullptr;
-  a.part_count = a.part_o ? reinterpret_cast<unsigned int*>(a.part_lse + tiles * 16) : nullptr;
   if ((page_size & (page_size - 1)) != 0) return -4;
   if (cache_slots > 0x7fffffffL) return -6;     // page sizes are powers of two
   a.page_shift = 0;

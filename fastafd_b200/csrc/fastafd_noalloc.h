@@ -35,9 +35,15 @@ extern "C" {
 //   (cudaGetSymbolAddress, with that device current). Make that first call outside of any
 //   stream capture.
 // * All calls on a device share the one array and it keeps whatever the previous call left
-//   there. The kernel writes every partial it later reads, so no clearing is needed, but two
-//   calls whose kernels overlap in time on the same GPU (different streams) race on it:
-//   serialise them.
+//   there. Two things live in it. The per-tile arrival counters occupy a fixed region at the
+//   front of the array, whatever B and splits are; they start at zero (the array is
+//   zero-initialised when the library is loaded) and every finished call leaves them at zero,
+//   so the next call, of any shape, finds them clear. The partial results behind them are
+//   written by a call before that call reads them, so their leftovers need no clearing.
+//   A call that was cut short (its status word reports a timeout) can leave counters non-zero:
+//   do not reuse the entry point on that device after such a failure.
+// * Two calls whose kernels overlap in time on the same GPU (different streams) race on the
+//   array: serialise them.
 // Returns 0, a positive cudaError_t, or a negative argument error (see
 // afd_noalloc_strerror).
 int afd_decode_attention_noalloc(const void* q, const void* k_cache, const void* v_cache,

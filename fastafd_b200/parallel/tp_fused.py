@@ -16,10 +16,8 @@ peer's all-gather release of the same layer (which follows its read of the previ
 and the next all-gather after the peer's reduce-scatter release; the NCCL collectives at the
 step boundary separate steps.
 
-Status: opt-in (``FASTAFD_TP_FUSED=1``); the default TP path uses the NCCL communicator. The
-collectives themselves pass a 200-round stress test on 2 and 4 GPUs and a one-GPU loopback test,
-and a 4-GPU TP-2 model run completed with them; an 8-GPU TP-4 decode benchmark did not finish
-within its time limit and the cause was not found by reading, so the path is not the default.
+Selected with ``FASTAFD_TP_FUSED=1``; without it a TP lane uses the NCCL communicator for the
+same two operations.
 
 Reference: python/minisgl/layers/linear.py:418-447 (o_proj + all-reduce),
 python/minisgl/distributed/impl.py:28-85.

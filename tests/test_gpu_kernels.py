@@ -103,6 +103,29 @@ def test_decode_attention(Hq, Hkv, D, q_len, page, splits):
     torch.testing.assert_close(out.cpu().float(), exp.float(), atol=2e-2, rtol=2e-2)
 
 
+def test_decode_attention_one_workspace_shared_by_different_shapes():
+    """One zeroed workspace serves launches of different (B, splits): the arrival counters sit at a
+    fixed place in front of the partial results, so a smaller launch after a larger one still finds
+    them at zero and merges its splits."""
+    Hq, Hkv, D, page = 32, 4, 128, 16
+    scale = 1 / math.sqrt(D)
+    ws = ops.decode_attn_workspace(8, Hq, Hkv, 1, D, 8, DEV)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    for i, (B, splits) in enumerate([(8, 8), (4, 8), (8, 4), (3, 2), (2, 5), (1, 3), (8, 8)]):
+        lens = torch.tensor([2049, 300, 1025, 513, 1800, 77, 4000, 1234], dtype=torch.int32)[:B]
+        max_pages = (int(lens.max()) + page - 1) // page + 1
+        n_pages = B * max_pages + 3
+        pt = torch.randperm(n_pages)[:B * max_pages].view(B, max_pages).to(torch.int32)
+        kc, vc = _bf(n_pages * page, Hkv, D, seed=31 + i), _bf(n_pages * page, Hkv, D, seed=41 + i)
+        q = _bf(B, Hq, D, seed=51 + i)
+        out = torch.full((B, Hq, D), float("nan"), dtype=torch.bfloat16, device=DEV)
+        ops.decode_attention(q, kc, vc, pt.to(DEV), lens.to(DEV), Hq, Hkv, D, 1, page, scale, splits=splits,
+                             workspace=ws, out=out, status=status)
+        exp = ref.decode_attention(q.cpu(), kc.cpu(), vc.cpu(), pt, lens, Hq, Hkv, D, 1, page, scale)
+        assert int(status) == 0
+        torch.testing.assert_close(out.cpu().float(), exp.float(), atol=2e-2, rtol=2e-2)
+
+
 @pytest.mark.parametrize("M,N,K,bt", [(16, 256, 128, 16), (32, 512, 2048, 32), (77, 1536, 2048, 32), (64, 2048, 768, 64), (200, 1024, 512, 128), (5, 128, 64, 16)])
 def test_dense_gemm_tcgen05(M, N, K, bt):
     x, w = _bf(M, K, seed=14), _bf(N, K, scale=0.05, seed=15)

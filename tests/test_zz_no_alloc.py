@@ -4,8 +4,8 @@ Some users of the kernel library cannot allocate device memory when they call it
 already belongs to their KV pool, or their decode loop forbids cudaMalloc). For them the
 library offers ``afd_decode_attention_noalloc``, which keeps the split-KV partial results in
 an array inside the library image. This test checks that it returns what the regular entry
-point (caller-provided workspace) returns, twice in a row on different inputs - the second
-call reuses the array with the first call's leftovers in it - and that an oversized request
+point (caller-provided workspace) returns, on calls in a row that differ in inputs, batch and
+split count - the later calls reuse the array with the first call's leftovers in it - and that an oversized request
 is refused with a clear error instead of being launched."""
 import ctypes as C
 import math
@@ -42,9 +42,11 @@ def _case(seed, B, Hq, Hkv, D, page, lens):
 
 def test_noalloc_entry_matches_regular_entry_twice():
     fn = _entry()
-    Hq, Hkv, D, page, splits = 32, 4, 128, 16, 3
+    Hq, Hkv, D, page = 32, 4, 128, 16
     status = torch.zeros(1, dtype=torch.int32, device=DEV)
-    for seed, lens in ((0, [700, 33, 1500, 257]), (1, [64, 1200, 5, 900])):
+    # the calls differ in batch and in splits: the second and third find the first one's partial
+    # results in the array, but their arrival counters at the same fixed place, left at zero
+    for seed, lens, splits in ((0, [700, 33, 1500, 257], 3), (1, [64, 1200], 5), (2, [900, 5, 2000, 640, 31], 2)):
         q, kc, vc, pt, sl = _case(seed, len(lens), Hq, Hkv, D, page, lens)
         expect = ops.decode_attention(q, kc, vc, pt, sl, Hq, Hkv, D, 1, page, 1 / math.sqrt(D), splits=splits)
         out = torch.empty_like(q)
