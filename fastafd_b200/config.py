@@ -204,6 +204,48 @@ class ModelConfig:
                       attn_output_gate=True, norm_offset1=True)
         return ModelConfig(**kw)
 
+    def to_hf(self) -> Dict[str, Any]:
+        """The ``config.json`` dict that :meth:`from_hf` reads back into this configuration
+        (used when a synthetic checkpoint is written for tests or offline conversion)."""
+        out: Dict[str, Any] = dict(
+            architectures=[self.architecture], hidden_size=self.hidden_size, num_hidden_layers=self.num_layers,
+            num_attention_heads=self.num_q_heads, num_key_value_heads=self.num_kv_heads, head_dim=self.head_dim,
+            vocab_size=self.vocab_size, rms_norm_eps=self.rms_eps, rope_theta=self.rope.theta,
+            max_position_embeddings=self.max_position, tie_word_embeddings=self.tie_embeddings,
+            attention_bias=self.attention_bias, intermediate_size=self.intermediate_size, torch_dtype=self.dtype)
+        if self.rope.rotary_dim:
+            out["rotary_dim"] = self.rope.rotary_dim
+        if self.rope.scaling:
+            out["rope_scaling"] = dict(self.rope.scaling)
+        if self.eos_token_ids:
+            out["eos_token_id"] = list(self.eos_token_ids)
+        if self.quant.is_fp8:
+            out["quantization_config"] = {"quant_method": "fp8", "modules_to_not_convert": list(self.quant.ignored_modules)}
+            if self.quant.method == "fp8":
+                out["quantization_config"]["weight_block_size"] = list(self.quant.block)
+        a = self.architecture
+        if a == "Qwen3MoeForCausalLM":
+            out.update(num_experts=self.num_experts, num_experts_per_tok=self.num_experts_per_tok,
+                       moe_intermediate_size=self.moe_intermediate_size, norm_topk_prob=self.norm_topk_prob)
+        elif a == "MiniMaxM2ForCausalLM":
+            out.update(use_qk_norm=self.qk_norm == "cross_head", num_local_experts=self.num_experts,
+                       num_experts_per_tok=self.num_experts_per_tok, intermediate_size=self.moe_intermediate_size)
+        elif a == "Glm4MoeForCausalLM":
+            out.update(use_qk_norm=self.qk_norm == "head", n_routed_experts=self.num_experts,
+                       num_experts_per_tok=self.num_experts_per_tok, moe_intermediate_size=self.moe_intermediate_size,
+                       norm_topk_prob=self.norm_topk_prob, routed_scaling_factor=self.routed_scaling_factor,
+                       n_group=self.n_group, topk_group=self.topk_group, n_shared_experts=self.num_shared_experts,
+                       first_k_dense_replace=self.first_k_dense)
+        elif a in ("Qwen3_5MoeForCausalLM", "Qwen3_5MoeForConditionalGeneration", "Qwen3NextForCausalLM"):
+            out.update(num_experts=self.num_experts, num_experts_per_tok=self.num_experts_per_tok,
+                       moe_intermediate_size=self.moe_intermediate_size, norm_topk_prob=self.norm_topk_prob,
+                       shared_expert_intermediate_size=self.shared_expert_intermediate_size,
+                       layer_types=["full_attention" if t == "full" else "linear_attention" for t in self.layer_types],
+                       linear_num_key_heads=self.gdn_num_k_heads, linear_num_value_heads=self.gdn_num_v_heads,
+                       linear_key_head_dim=self.gdn_head_k_dim, linear_value_head_dim=self.gdn_head_v_dim,
+                       linear_conv_kernel_dim=self.gdn_conv_kernel)
+        return out
+
     @staticmethod
     def from_path(path: str) -> "ModelConfig":
         return ModelConfig.from_hf(json.loads((Path(path) / "config.json").read_text()))
@@ -283,6 +325,6 @@ class RuntimeConfig:
     spec_block: int = 0                     # 0 = off; else verified tokens per step (drafts + 1)
     spec_draft_path: str = ""
     seed: int = 0
-    dummy_weights: bool = True              # random-init when the path is a preset
+    dummy_weights: bool = False             # a checkpoint directory is served with random-init weights instead of its own
     dtype: str = "bfloat16"
     device: str = "cuda"

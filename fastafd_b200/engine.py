@@ -43,6 +43,22 @@ def _torch_dtype(name: str, device: torch.device) -> torch.dtype:
     return {"bfloat16": torch.bfloat16, "float16": torch.float16, "float32": torch.float32}[name]
 
 
+def resolve_checkpoint(rt: RuntimeConfig) -> Optional[str]:
+    """Directory whose safetensors files hold the served weights, or None for random-init
+    weights (a preset name, or ``dummy_weights`` with a directory that only has config.json).
+    A directory without safetensors files is refused rather than served with random weights.
+    Reference: python/minisgl/engine/engine.py:330 (use_dummy_weight), models/weight.py:419."""
+    path = rt.model_path
+    if not os.path.isdir(path) or rt.dummy_weights:
+        return None
+    import glob
+
+    if not glob.glob(os.path.join(path, "*.safetensors")):
+        raise FileNotFoundError(f"{path} has no .safetensors files; pass --dummy-weights to serve random weights "
+                                f"of the architecture in its config.json")
+    return path
+
+
 def decode_buckets(rt: RuntimeConfig, topo: AfdTopology) -> List[int]:
     """Decode graph sizes; with attention TP every bucket is a multiple of the TP size (the
     residual stream is sharded by tokens across the TP ranks)."""
@@ -107,6 +123,8 @@ class AfdEngine:
             my_ag_index = -1
         num_eg, num_ag = len(eg_ranks), len(ag_ranks)
 
+        ckpt = resolve_checkpoint(rt)
+        self.checkpoint = ckpt
         stage = None
         if self.is_expert and cfg.is_moe and os.environ.get("FASTAFD_DEBUG_NULL_MOE") != "1":
             ep_rank = 0 if self.colocated else topo.ep_rank(rank)
@@ -114,7 +132,12 @@ class AfdEngine:
                 stage = ExpertStage(cfg, self.device, self.dtype, 0, 1, tp_rank=ep_rank, tp_size=topo.mlp_tp)
             else:
                 stage = ExpertStage(cfg, self.device, self.dtype, ep_rank, num_eg)
-            stage.init_random(seed, fast=fast_init)
+            if ckpt is not None:
+                from .models.loader import load_expert_stage
+
+                load_expert_stage(stage, ckpt)
+            else:
+                stage.init_random(seed, fast=fast_init)
         self.expert_stage = stage
 
         from .worker.moe_client import MoeClient
@@ -179,7 +202,7 @@ class AfdEngine:
             tp_rank = 0 if self.colocated else topo.attn_tp_rank(rank)
             self.attn = AttentionWorker(cfg, rt, self.device, client, tp_rank=tp_rank, tp_size=topo.attn_tp,
                                         tp_comm=tp_comm, dtype=self.dtype, rank=rank, max_bucket=cap,
-                                        weight_init=lambda m: m.init_random(seed, fast=fast_init))
+                                        weight_init=self._attention_weight_init(ckpt, seed, fast_init))
         if self.attn is not None and rt.spec_block > 1:
 
             from .spec.attn_side import SpecRunner
@@ -189,6 +212,14 @@ class AfdEngine:
         if self.is_expert and not self.colocated:
             self.expert = ExpertWorker(cfg, rt, self.device, stage, server, rank, eg_status)
         self._server = server
+
+    @staticmethod
+    def _attention_weight_init(ckpt: Optional[str], seed: int, fast_init: bool):
+        if ckpt is None:
+            return lambda m: m.init_random(seed, fast=fast_init)
+        from .models.loader import load_attention_stage
+
+        return lambda m: load_attention_stage(m, ckpt)
 
     # ------------------------------------------------------------------ stepping
     def step(self, plan, mb_tokens: Optional[List[int]] = None):

@@ -24,6 +24,7 @@ from __future__ import annotations
 import glob
 import os
 import re
+from dataclasses import replace
 from typing import Dict, Iterator, List, Optional, Tuple
 
 import torch
@@ -52,7 +53,10 @@ def normalize_key(name: str) -> Optional[str]:
     return name
 
 
-def iter_checkpoint(path: str) -> Iterator[Tuple[str, torch.Tensor]]:
+def iter_checkpoint(path: str, want=None) -> Iterator[Tuple[str, torch.Tensor]]:
+    """(key, tensor) of every tensor in the directory's safetensors files; with `want`, only
+    keys for which it returns True are read from disk (an attention rank never touches the
+    bytes of the routed experts and the other way round)."""
     from safetensors import safe_open
 
     files = sorted(glob.glob(os.path.join(path, "*.safetensors")))
@@ -61,7 +65,8 @@ def iter_checkpoint(path: str) -> Iterator[Tuple[str, torch.Tensor]]:
     for f in files:
         with safe_open(f, framework="pt", device="cpu") as sf:
             for k in sf.keys():
-                yield k, sf.get_tensor(k)
+                if want is None or want(k):
+                    yield k, sf.get_tensor(k)
 
 
 def _dequant_if_fp8(w: torch.Tensor, scale: Optional[torch.Tensor]) -> torch.Tensor:
@@ -78,10 +83,12 @@ def load_attention_stage(stage: AttentionStage, path: str) -> None:
     need = stage.param_shapes()
     raw: Dict[str, torch.Tensor] = {}
     scales: Dict[str, torch.Tensor] = {}
-    for key, t in iter_checkpoint(path):
+    def wanted(key: str) -> bool:                     # skip_expert_weights
         k = normalize_key(key)
-        if k is None or _EXPERT_RE.search(k):
-            continue                                  # skip_expert_weights
+        return k is not None and not _EXPERT_RE.search(k)
+
+    for key, t in iter_checkpoint(path, wanted):
+        k = normalize_key(key)
         if k.endswith(".weight_scale_inv"):
             scales[k[:-len("_scale_inv")]] = t
         else:
@@ -120,16 +127,15 @@ def load_expert_stage(stage: ExpertStage, path: str) -> None:
     lo, hi = stage.expert_base, min(stage.expert_base + E, cfg.num_experts)
     I, H = cfg.moe_intermediate_size, cfg.hidden_size
     parts: Dict[int, Dict[Tuple[int, str, str], torch.Tensor]] = {}
-    for key, t in iter_checkpoint(path):
+    def wanted(key: str) -> bool:                     # skip_non_expert_weights, other ranks' experts
         k = normalize_key(key)
-        if k is None:
-            continue
+        m = _EXPERT_RE.search(k) if k is not None else None
+        return m is not None and lo <= int(m.group(1)) < hi
+
+    for key, t in iter_checkpoint(path, wanted):
+        k = normalize_key(key)
         m = _EXPERT_RE.search(k)
-        if not m:
-            continue                                  # skip_non_expert_weights
         e = int(m.group(1))
-        if not lo <= e < hi:
-            continue
         layer = int(re.search(r"layers\.(\d+)\.", k).group(1))
         proj = _EXPERT_ALIAS.get(m.group(2), m.group(2))
         parts.setdefault(layer, {})[(e - lo, proj, m.group(3))] = t
@@ -160,9 +166,15 @@ def save_checkpoint(cfg: ModelConfig, attn: AttentionStage, experts: List[Expert
     """Write single-rank stages as a Hugging Face style checkpoint (separate q/k/v and gate/up
     tensors, per-expert tensors, optional block-FP8 experts). Used to build synthetic
     checkpoints for tests and for offline conversion."""
+    import json
+
     from safetensors.torch import save_file
 
     os.makedirs(path, exist_ok=True)
+    with open(os.path.join(path, "config.json"), "w") as f:
+        from ..config import QuantConfig
+
+        json.dump((replace(cfg, quant=QuantConfig("fp8")) if fp8_experts and not cfg.quant.is_fp8 else cfg).to_hf(), f)
     out: Dict[str, torch.Tensor] = {}
     D = cfg.head_dim
     for name, t in attn.w.items():

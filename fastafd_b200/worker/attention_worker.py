@@ -419,6 +419,13 @@ class AttentionWorker:
                 for i, st in enumerate(words[:self.status_host.shape[1]]):
                     self.status_host[slot, i:i + 1].copy_(st, non_blocking=True)
                 self.d2h_events[slot].record()
+            else:
+                # the host path runs a step to completion here; keep its tokens per ring slot, since
+                # the next step may be launched (and overwrite next_tokens) before this one is finished
+                if not hasattr(self, "_host_tokens"):
+                    self._host_tokens = [None] * RING
+                self._host_tokens[plan.step_id % RING] = np.concatenate(
+                    [self.bufs[l].next_tokens[:bucket].numpy().copy() for l in range(self.num_mb)])
 
     def finish_decode(self, plan: AgStepPlan) -> AgStepReply:
         bucket = plan.bucket
@@ -428,7 +435,7 @@ class AttentionWorker:
             toks = np.concatenate([self.bufs[l].host_out[slot, :bucket].numpy().copy() for l in range(self.num_mb)])
             status = int(self.status_host[slot].max())
         else:
-            toks = np.concatenate([self.bufs[l].next_tokens[:bucket].numpy().copy() for l in range(self.num_mb)])
+            toks = self._host_tokens[plan.step_id % RING]
             status = self.read_status()
         return AgStepReply(step_id=plan.step_id, rank=self.rank, next_tokens=toks.astype(np.int32), status=status)
 
