@@ -160,7 +160,7 @@ def main():
     rt = RuntimeConfig(model_path=args.model, num_mb=args.num_mb, page_size=16, max_running_requests=lane_b,
                        max_seq_len=args.context + total_steps + 16, cuda_graph_max_bs=per_mb,
                        decode_graph_bs=(per_mb,), use_cuda_graph=not args.no_graph, moe_block_tok=args.block_tok,
-                       max_batched_tokens=per_mb * args.num_mb, device="cuda")
+                       max_batched_tokens=per_mb * args.num_mb, device="cuda", flag_timeout_s=2.0)
     t_build = time.time()
     eng = AfdEngine(cfg, rt, topo, rank, device, group=None, seed=0, fast_init=True, max_comm_tokens=per_mb // tp)
     drv = SpmdDriver(eng)

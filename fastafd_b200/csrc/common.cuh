@@ -96,6 +96,12 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
       if (mbar_try_wait(bar, parity)) return true;
     }
     if (*abort_flag) return false;
+    // a wait that ran out earlier on this GPU (this kernel or any before it): stop at once, so that
+    // only the first failed wait of a step costs its full time limit
+    if (status != nullptr && *reinterpret_cast<volatile int*>(status) != 0) {
+      *abort_flag = 1;
+      return false;
+    }
     if (globaltimer_ns() - t0 > kMbarTimeoutNs) break;
   }
   *abort_flag = 1;

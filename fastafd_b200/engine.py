@@ -125,6 +125,11 @@ class AfdEngine:
 
         ckpt = resolve_checkpoint(rt)
         self.checkpoint = ckpt
+        # ONE device status word per process: every kernel of every communicator on this GPU reports
+        # into it and polls it inside its waits, so the first wait that runs out is the only one that
+        # costs its full time limit; the rest of the step drains at once and the host raises.
+        self.status_word = torch.zeros(1, dtype=torch.int32, device=self.device) if cuda else None
+        sw = self.status_word
         stage = None
         if self.is_expert and cfg.is_moe and os.environ.get("FASTAFD_DEBUG_NULL_MOE") != "1":
             ep_rank = 0 if self.colocated else topo.ep_rank(rank)
@@ -161,9 +166,9 @@ class AfdEngine:
                 if self.colocated:
                     fabs = Fabric.local([ag_layout(mcfg).size, eg_layout(mcfg).size], self.device)
                     self.fabric = fabs
-                    eg_ep = EgMoeEndpoint(mcfg, fabs[1], 0, [0], self.device, timeout_ns)
+                    eg_ep = EgMoeEndpoint(mcfg, fabs[1], 0, [0], self.device, timeout_ns, status=sw)
                     server = FabricMoeServer(eg_ep, stage)
-                    client = FabricMoeClient(AgMoeEndpoint(mcfg, fabs[0], 0, [1], self.device, timeout_ns), colocated=server)
+                    client = FabricMoeClient(AgMoeEndpoint(mcfg, fabs[0], 0, [1], self.device, timeout_ns, status=sw), colocated=server)
                     eg_status = eg_ep.status
                 else:
                     size = ag_layout(mcfg).size if self.is_attention else eg_layout(mcfg).size
@@ -176,10 +181,10 @@ class AfdEngine:
                         size += tp_layout(topo.attn_tp, rt.num_mb, self.max_comm_tokens, cfg.hidden_size).size
                     self.fabric = Fabric.ipc(size, self.device, group)
                     if self.is_attention:
-                        client = FabricMoeClient(AgMoeEndpoint(mcfg, self.fabric, my_ag_index, eg_ranks, self.device, timeout_ns))
+                        client = FabricMoeClient(AgMoeEndpoint(mcfg, self.fabric, my_ag_index, eg_ranks, self.device, timeout_ns, status=sw))
                     else:
                         eg_ep = EgMoeEndpoint(mcfg, self.fabric, topo.ep_rank(rank), ag_ranks,
-                                              self.device, timeout_ns)
+                                              self.device, timeout_ns, status=sw)
                         server = FabricMoeServer(eg_ep, stage)
                         eg_status = eg_ep.status
             else:
@@ -197,11 +202,11 @@ class AfdEngine:
 
             lane_ranks = topo.attn_tp_group(topo.attn_lane(rank))
             tp_comm = TpFusedComm(tp_comm, self.fabric, lane_ranks, topo.attn_tp_rank(rank), tp_heap_base, rt.num_mb,
-                                  self.max_comm_tokens, cfg.hidden_size, self.device, int(rt.flag_timeout_s * 1e9))
+                                  self.max_comm_tokens, cfg.hidden_size, self.device, int(rt.flag_timeout_s * 1e9), status=sw)
         if self.is_attention:
             tp_rank = 0 if self.colocated else topo.attn_tp_rank(rank)
             self.attn = AttentionWorker(cfg, rt, self.device, client, tp_rank=tp_rank, tp_size=topo.attn_tp,
-                                        tp_comm=tp_comm, dtype=self.dtype, rank=rank, max_bucket=cap,
+                                        tp_comm=tp_comm, dtype=self.dtype, rank=rank, max_bucket=cap, status=sw,
                                         weight_init=self._attention_weight_init(ckpt, seed, fast_init))
         if self.attn is not None and rt.spec_block > 1:
 

@@ -197,14 +197,20 @@ class AttentionStage:
             elif self.tp_size == 1:
                 self.w[name] = seeded_normal(name, shape, std, seed, self.device, dt, fast)
             else:
-                self.w[name] = self._tp_slice(name, seed, std, dt)
+                self.w[name] = self._tp_slice(name, seed, std, dt, fast)
         self._post_load()
         return self
 
-    def _tp_slice(self, name: str, seed: int, std: float, dt) -> Tensor:
-        """Slice of the full-size random tensor that this TP rank owns (CPU init only)."""
-        single = AttentionStage(self.cfg, "cpu", torch.float32)
-        full_shape = single.param_shapes()[name][0]
+    def _tp_slice(self, name: str, seed: int, std: float, dt, fast: bool = False) -> Tensor:
+        """Slice of the full-size random tensor that this TP rank owns. With `fast` the full
+        tensor is drawn on the target GPU (every rank of the lane draws the same numbers from the
+        same seed) instead of on the host."""
+        if not hasattr(self, "_full_shapes"):
+            self._full_shapes = {k: v[0] for k, v in AttentionStage(self.cfg, "cpu", torch.float32).param_shapes().items()}
+        full_shape = self._full_shapes[name]
+        if fast and self.device.type == "cuda":
+            full = seeded_normal(name, full_shape, std, seed, self.device, dt, True)
+            return shard_attention_param(self.cfg, name, full, self.tp_rank, self.tp_size).clone()
         full = seeded_normal(name, full_shape, std, seed, "cpu", torch.float32)
         return shard_attention_param(self.cfg, name, full, self.tp_rank, self.tp_size).to(dt).to(self.device)
 

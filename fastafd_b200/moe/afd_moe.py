@@ -110,11 +110,13 @@ class AgMoeEndpoint:
     GPU i."""
 
     def __init__(self, cfg: MoeCommConfig, fabric: Fabric, ag_index: int, eg_ranks: List[int],
-                 device: torch.device, timeout_ns: int = DEFAULT_TIMEOUT_NS):
+                 device: torch.device, timeout_ns: int = DEFAULT_TIMEOUT_NS, status: Optional[torch.Tensor] = None):
         self.cfg, self.fabric, self.ag_index, self.eg_ranks, self.device = cfg, fabric, ag_index, eg_ranks, device
         self.timeout_ns = timeout_ns
         self.lay, self.eg_lay = ag_layout(cfg), eg_layout(cfg)
-        self.status = torch.zeros(1, dtype=torch.int32, device=device)
+        # `status`: the process-wide device status word when the caller has one, so that a wait that
+        # ran out anywhere on this GPU makes every later wait of every kernel return at once
+        self.status = status if status is not None else torch.zeros(1, dtype=torch.int32, device=device)
         self.lanes = [_LaneWords(device) for _ in range(cfg.num_lanes)]
         self.trace = ([torch.zeros(TRACE_LEN, 4, dtype=torch.int64, device=device) for _ in range(cfg.num_lanes)]
                       if _trace_enabled() else None)
@@ -193,11 +195,12 @@ class EgMoeEndpoint:
     with the M2N store epilogue."""
 
     def __init__(self, cfg: MoeCommConfig, fabric: Fabric, eg_index: int, ag_ranks: List[int],
-                 device: torch.device, timeout_ns: int = DEFAULT_TIMEOUT_NS, grid: int = NUM_SMS):
+                 device: torch.device, timeout_ns: int = DEFAULT_TIMEOUT_NS, grid: int = NUM_SMS,
+                 status: Optional[torch.Tensor] = None):
         self.cfg, self.fabric, self.eg_index, self.ag_ranks, self.device = cfg, fabric, eg_index, ag_ranks, device
         self.timeout_ns, self.grid = timeout_ns, grid
         self.lay, self.ag_lay = eg_layout(cfg), ag_layout(cfg)
-        self.status = torch.zeros(1, dtype=torch.int32, device=device)
+        self.status = status if status is not None else torch.zeros(1, dtype=torch.int32, device=device)
         self.lanes = [_LaneWords(device) for _ in range(cfg.num_lanes)]
         self.trace = ([torch.zeros(TRACE_LEN, 4, dtype=torch.int64, device=device) for _ in range(cfg.num_lanes)]
                       if _trace_enabled() else None)

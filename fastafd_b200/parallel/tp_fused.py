@@ -60,7 +60,7 @@ class TpFusedComm(TpComm):
 
     def __init__(self, base: TpComm, fabric: Fabric, ranks: List[int], my_index: int, heap_base: int,
                  num_lanes: int, max_tokens_local: int, hidden: int, device: torch.device,
-                 timeout_ns: int = int(20e9), block_tok: int = 0):
+                 timeout_ns: int = int(20e9), block_tok: int = 0, status=None):
         assert len(ranks) <= MAX_TP and hidden % 128 == 0
         self.base, self.fabric, self.ranks, self.rank, self.size = base, fabric, list(ranks), my_index, len(ranks)
         self.cap, self.H, self.device, self.timeout_ns = max_tokens_local, hidden, device, timeout_ns
@@ -68,7 +68,7 @@ class TpFusedComm(TpComm):
         self.lay = tp_layout(self.size, num_lanes, max_tokens_local, hidden)
         self.off = heap_base
         heap = fabric.heap
-        self.status = torch.zeros(1, dtype=torch.int32, device=device)
+        self.status = status if status is not None else torch.zeros(1, dtype=torch.int32, device=device)
         tp = self.size
         self.rs_buf = [heap.view(heap_base + self.lay.offset(f"tp_rs{l}"), (tp, max_tokens_local, hidden), torch.bfloat16)
                        for l in range(num_lanes)]

@@ -100,7 +100,7 @@ def determine_num_pages(cfg: ModelConfig, rt: RuntimeConfig, device: torch.devic
 class AttentionWorker:
     def __init__(self, cfg: ModelConfig, rt: RuntimeConfig, device, client: MoeClient, *, num_pages: int = 0,
                  tp_rank: int = 0, tp_size: int = 1, tp_comm=None, dtype=None, rank: int = 0,
-                 max_bucket: Optional[int] = None, weight_init=None):
+                 max_bucket: Optional[int] = None, weight_init=None, status: Optional[torch.Tensor] = None):
         self.cfg, self.rt, self.device, self.client, self.rank = cfg, rt, torch.device(device), client, rank
         self.cuda = self.device.type == "cuda"
         self.dtype = dtype or (torch.bfloat16 if self.cuda else torch.float32)
@@ -123,7 +123,7 @@ class AttentionWorker:
         self.token_pool = torch.zeros(self.max_running + 1, self.max_seq_len + 8, dtype=torch.int32, device=self.device)
         self.page_table_all = torch.zeros(self.max_running + 1, self.max_pages, dtype=torch.int32, device=self.device)
         self.page_table_host = np.zeros((self.max_running + 1, self.max_pages), np.int32)
-        self.status = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.status = status if status is not None else torch.zeros(1, dtype=torch.int32, device=self.device)
         self.cap = max_bucket or max(rt.cuda_graph_max_bs, 1)
         self.bufs = [self._make_bufs(self.cap) for _ in range(self.num_mb)]
         self.graphs: Dict[int, "torch.cuda.CUDAGraph"] = {}
