@@ -31,6 +31,7 @@
 // (AG kernel :212-1265; EG pull + pool :2023-2254) and python/minisgl/moe/megamoe_m2n_afd.py:336-470.
 // This design pushes instead of pulling and needs no global barrier.
 #include "common.cuh"
+#include "route_common.cuh"
 
 namespace afd {
 
@@ -144,14 +145,6 @@ __global__ void dispatch_push_kernel(const DispatchArgs a) {
 // (which can also emit the dispatch quantisation) and the AG kernel's in-kernel gate
 // (sm100_mega_moe_m2n.cuh:571-712).
 // ---------------------------------------------------------------------------------------
-__device__ __forceinline__ void mma_gemv_16816(float* c, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
-                                               uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
-}
-
 struct RouteDispatchArgs {
   const __nv_bfloat16* attn_out;   // [T][H]
   __nv_bfloat16* residual;         // [T][H] in/out
@@ -166,85 +159,6 @@ struct RouteDispatchArgs {
   float eps, route_scale;
   DispatchArgs d;                  // d.x / d.topk_idx are ignored (produced here)
 };
-
-template <int MAX_PER_LANE>
-__device__ __forceinline__ void warp_topk(const float* s_logit, const float* bias, int E, int K, int scoring,
-                                          int renorm, float scale, int* out_idx, float* out_w, int lane) {
-  float sc[MAX_PER_LANE], sel[MAX_PER_LANE];
-  float mx = -INFINITY;
-#pragma unroll
-  for (int j = 0; j < MAX_PER_LANE; ++j) {
-    const int e = j * 32 + lane;
-    sc[j] = e < E ? s_logit[e] : -INFINITY;
-    mx = fmaxf(mx, sc[j]);
-  }
-  if (scoring == 0) {
-    mx = warp_max(mx);
-    float sum = 0.f;
-#pragma unroll
-    for (int j = 0; j < MAX_PER_LANE; ++j) {
-      const int e = j * 32 + lane;
-      sc[j] = e < E ? expf(sc[j] - mx) : 0.f;
-      sum += sc[j];
-    }
-    sum = warp_sum(sum);
-    const float inv = 1.f / sum;
-#pragma unroll
-    for (int j = 0; j < MAX_PER_LANE; ++j) {
-      const int e = j * 32 + lane;
-      sc[j] *= inv;
-      sel[j] = e < E ? sc[j] : -INFINITY;
-    }
-  } else {
-#pragma unroll
-    for (int j = 0; j < MAX_PER_LANE; ++j) {
-      const int e = j * 32 + lane;
-      sc[j] = e < E ? 1.f / (1.f + expf(-sc[j])) : 0.f;
-      sel[j] = e < E ? sc[j] + (bias ? bias[e] : 0.f) : -INFINITY;
-    }
-  }
-  float wsum = 0.f, my_w = 0.f;
-  int my_i = 0;
-  for (int k = 0; k < K; ++k) {
-    float best = -INFINITY;
-    int bi = 0x7fffffff;
-#pragma unroll
-    for (int j = 0; j < MAX_PER_LANE; ++j) {
-      if (sel[j] > best) {
-        best = sel[j];
-        bi = j * 32 + lane;
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float ob = __shfl_xor_sync(0xffffffffu, best, o);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
-      if (ob > best || (ob == best && oi < bi)) {
-        best = ob;
-        bi = oi;
-      }
-    }
-    float wv = 0.f;
-#pragma unroll
-    for (int j = 0; j < MAX_PER_LANE; ++j) {
-      if (j * 32 + lane == bi) {
-        wv = sc[j];
-        sel[j] = -INFINITY;
-      }
-    }
-    wv = warp_sum(wv);
-    wsum += wv;
-    if (lane == k) {
-      my_w = wv;
-      my_i = bi;
-    }
-  }
-  const float mul = (renorm ? 1.f / fmaxf(wsum, 1e-20f) : 1.f) * scale;
-  if (lane < K) {
-    out_idx[lane] = my_i;
-    out_w[lane] = my_w * mul;
-  }
-}
 
 __global__ void __launch_bounds__(1024) ag_route_dispatch_kernel(const RouteDispatchArgs a) {
   // shared: x as bf16 (H * 2 bytes, 16-byte aligned rows read as uint4: conflict-free) |

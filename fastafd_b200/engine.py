@@ -159,9 +159,14 @@ class AfdEngine:
                 from .moe.afd_moe import AgMoeEndpoint, EgMoeEndpoint, MoeCommConfig, ag_layout, eg_layout
                 from .parallel.fabric import Fabric
 
+                # decode-sized steps store rows straight into the experts' pool stripes (moe/afd_moe.py)
+                direct = min(self.max_comm_tokens, max(cap // topo.attn_tp, 1))
+                if os.environ.get("FASTAFD_DIRECT", "1") == "0" or num_ag * direct > 1024:
+                    direct = 0
                 mcfg = MoeCommConfig(num_ag=num_ag, num_eg=num_eg, num_lanes=rt.num_mb, max_tokens=self.max_comm_tokens,
                                      hidden=cfg.hidden_size, topk=cfg.num_experts_per_tok, num_experts=cfg.num_experts,
-                                     intermediate=cfg.moe_intermediate_size, fp8=cfg.quant.is_fp8, block_tok=rt.moe_block_tok)
+                                     intermediate=cfg.moe_intermediate_size, fp8=cfg.quant.is_fp8, block_tok=rt.moe_block_tok,
+                                     direct_tokens=direct)
                 timeout_ns = int(rt.flag_timeout_s * 1e9)
                 if self.colocated:
                     fabs = Fabric.local([ag_layout(mcfg).size, eg_layout(mcfg).size], self.device)

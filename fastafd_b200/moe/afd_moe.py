@@ -21,7 +21,8 @@ from typing import List, Optional
 import torch
 
 from ..ops import EPI_COMBINE, EPI_SWIGLU, NUM_SMS, grouped_gemm
-from ..ops._lib import CombineDesc, DispatchDesc, GroupDesc, RouteDispatchDesc, check, cur_stream, lib, ptr
+from ..ops._lib import (CombineDesc, DirectDesc, DispatchDesc, GroupDesc, RouteDirectDesc, RouteDispatchDesc, ScheduleDesc,
+                        check, cur_stream, lib, ptr)
 from ..parallel.fabric import Fabric, Layout
 
 DEFAULT_TIMEOUT_NS = int(float(os.environ.get("FASTAFD_FLAG_TIMEOUT_S", "20")) * 1e9)
@@ -52,6 +53,23 @@ class MoeCommConfig:
     intermediate: int
     fp8: bool = False
     block_tok: int = 32
+    # Steps with at most this many tokens per attention rank use the direct exchange: rows are stored
+    # straight into per-expert stripes of the expert GPU's pool (slot claimed with an atomic add), so
+    # the expert side neither groups nor gathers. 0 switches it off (receive slots + grouping only).
+    direct_tokens: int = 0
+
+    @property
+    def direct_cap(self) -> int:
+        """Rows per expert stripe: every token of every source may choose the same expert."""
+        n = self.num_ag * self.direct_tokens
+        return (n + self.block_tok - 1) // self.block_tok * self.block_tok
+
+    @property
+    def direct_rows(self) -> int:
+        return self.experts_per_eg * self.direct_cap
+
+    def use_direct(self, tokens: int) -> bool:
+        return 0 < tokens <= self.direct_tokens
 
     @property
     def experts_per_eg(self) -> int:
@@ -87,6 +105,11 @@ def eg_layout(cfg: MoeCommConfig) -> Layout:
         lay.add(f"recv_scale{lane}", cfg.num_ag * cfg.max_tokens * (cfg.hidden // 128) * 4)
         lay.add(f"recv_idx{lane}", cfg.num_ag * cfg.max_tokens * cfg.topk * 4)
         lay.add(f"n2m_flag{lane}", 4 * cfg.num_ag)
+        if cfg.direct_tokens > 0:
+            lay.add(f"dpool_x{lane}", cfg.direct_rows * cfg.row_bytes)
+            lay.add(f"dpool_scale{lane}", cfg.direct_rows * (cfg.hidden // 128) * 4)
+            lay.add(f"dmeta{lane}", cfg.direct_rows * 4)
+            lay.add(f"dcount{lane}", cfg.experts_per_eg * 4)
     return lay
 
 
@@ -126,6 +149,24 @@ class AgMoeEndpoint:
         self.m2n_flag = [heap.view(self.lay.offset(f"m2n_flag{l}"), (cfg.num_eg,), torch.int32)
                          for l in range(cfg.num_lanes)]
         self._dispatch_desc = [self._make_dispatch_desc(l) for l in range(cfg.num_lanes)]
+        self._direct_desc = [self._make_direct_desc(l) for l in range(cfg.num_lanes)] if cfg.direct_tokens > 0 else None
+        self.route_tokens_per_cta = int(os.environ.get("FASTAFD_ROUTE_TPC", "0"))
+        self.route_cluster = int(os.environ.get("FASTAFD_ROUTE_CLUSTER", "0"))
+
+    def _make_direct_desc(self, lane: int) -> DirectDesc:
+        cfg, d = self.cfg, DirectDesc()
+        d.num_eg, d.experts_per_eg, d.cap, d.fp8 = cfg.num_eg, cfg.experts_per_eg, cfg.direct_cap, int(cfg.fp8)
+        d.H, d.K, d.src_rank = cfg.hidden, cfg.topk, self.ag_index
+        for i, r in enumerate(self.eg_ranks):
+            d.peer_pool[i] = self.fabric.peer_ptr(r, self.eg_lay.offset(f"dpool_x{lane}"))
+            d.peer_scale[i] = self.fabric.peer_ptr(r, self.eg_lay.offset(f"dpool_scale{lane}"))
+            d.peer_meta[i] = self.fabric.peer_ptr(r, self.eg_lay.offset(f"dmeta{lane}"))
+            d.peer_count[i] = self.fabric.peer_ptr(r, self.eg_lay.offset(f"dcount{lane}"))
+            d.peer_flag[i] = self.fabric.peer_ptr(r, self.eg_lay.offset(f"n2m_flag{lane}")) + 4 * self.ag_index
+        w = self.lanes[lane]
+        d.epoch, d.done_counter, d.status = ptr(w.epoch), ptr(w.done), ptr(self.status)
+        d.trace = ptr(self.trace[lane]) if self.trace else None
+        return d
 
     def _make_dispatch_desc(self, lane: int) -> DispatchDesc:
         cfg, d = self.cfg, DispatchDesc()
@@ -143,8 +184,13 @@ class AgMoeEndpoint:
 
     def dispatch(self, lane: int, x: torch.Tensor, topk_idx: torch.Tensor) -> None:
         """Push x [T,H] bf16 (rows of tokens routed to each expert GPU) and the top-k ids."""
-        d = self._dispatch_desc[lane]
         assert x.is_contiguous() and topk_idx.is_contiguous() and topk_idx.dtype == torch.int32
+        if self.cfg.use_direct(x.shape[0]):
+            dd = self._direct_desc[lane]
+            dd.T = x.shape[0]
+            check(lib().afd_dispatch_direct(ptr(x), ptr(topk_idx), C.byref(dd), cur_stream()), "dispatch_direct")
+            return
+        d = self._dispatch_desc[lane]
         d.x, d.topk_idx, d.T = ptr(x), ptr(topk_idx), x.shape[0]
         check(lib().afd_dispatch_push(C.byref(d), cur_stream()), "dispatch_push")
 
@@ -153,6 +199,19 @@ class AgMoeEndpoint:
                        topk_idx: torch.Tensor, topk_w: torch.Tensor, *, scoring: str, renorm: bool, eps: float,
                        offset1: bool = False, route_scale: float = 1.0) -> None:
         """One launch for: residual += attn_out; x = rmsnorm(residual); router; push to experts."""
+        if self.cfg.use_direct(attn_out.shape[0]):
+            r = RouteDirectDesc()
+            C.memmove(C.byref(r.d), C.byref(self._direct_desc[lane]), C.sizeof(DirectDesc))
+            r.d.T = attn_out.shape[0]
+            r.attn_out, r.residual, r.norm_w = ptr(attn_out), ptr(residual), ptr(norm_w)
+            r.gate_w, r.gate_bias = ptr(gate_w), ptr(gate_bias)
+            r.x_out, r.topk_idx_out, r.topk_w_out = ptr(x_out), ptr(topk_idx), ptr(topk_w)
+            r.E, r.gate_fp32 = gate_w.shape[0], int(gate_w.dtype == torch.float32)
+            r.scoring, r.renorm, r.offset1 = (0 if scoring == "softmax" else 1), int(renorm), int(offset1)
+            r.eps, r.route_scale = eps, route_scale
+            r.tokens_per_cta, r.cluster = self.route_tokens_per_cta, self.route_cluster
+            check(lib().afd_ag_route_direct(C.byref(r), cur_stream()), "ag_route_direct")
+            return
         r = RouteDispatchDesc()
         C.memmove(C.byref(r.d), C.byref(self._dispatch_desc[lane]), C.sizeof(DispatchDesc))
         r.d.T = attn_out.shape[0]
@@ -225,6 +284,18 @@ class EgMoeEndpoint:
         self.expert_counts = torch.zeros(cfg.experts_per_eg, dtype=torch.int32, device=device)
         self.expert_base = eg_index * cfg.experts_per_eg
         self.experts_local = cfg.experts_per_eg
+        if cfg.direct_tokens > 0:
+            DR = cfg.direct_rows
+            self.dpool_x = [heap.view(self.lay.offset(f"dpool_x{l}"), (DR, cfg.hidden), xdt) for l in range(L)]
+            self.dpool_xs = [heap.view(self.lay.offset(f"dpool_scale{l}"), (DR, cfg.hidden // 128), torch.float32)
+                             for l in range(L)] if cfg.fp8 else [None] * L
+            self.dmeta = [heap.view(self.lay.offset(f"dmeta{l}"), (DR,), torch.int32) for l in range(L)]
+            self.dcount = [heap.view(self.lay.offset(f"dcount{l}"), (cfg.experts_per_eg,), torch.int32) for l in range(L)]
+            for c in self.dcount:
+                c.zero_()
+            self.dpool_h = torch.zeros(DR, I, dtype=xdt, device=device)
+            self.dpool_hs = torch.ones(DR, max(I // 128, 1), dtype=torch.float32, device=device) if cfg.fp8 else None
+            self.dtile_info = torch.zeros(cfg.experts_per_eg * (cfg.direct_cap // cfg.block_tok), 4, dtype=torch.int32, device=device)
         self.peer_combine = [[fabric.peer_ptr(r, self.ag_lay.offset(f"combine{l}")) for r in ag_ranks] for l in range(L)]
         self.peer_flag = [[fabric.peer_ptr(r, self.ag_lay.offset(f"m2n_flag{l}")) + 4 * eg_index for r in ag_ranks]
                           for l in range(L)]
@@ -254,6 +325,8 @@ class EgMoeEndpoint:
         """One MoE layer for one lane. w13: [E_local, 2I, H] gate/up interleaved (see
         ops.interleave_gate_up); w2: [E_local, H, I]. FP8 mode takes per-tile scales."""
         cfg = self.cfg
+        if cfg.use_direct(T):
+            return self._run_layer_direct(lane, w13, w2, w13_scale, w2_scale)
         self.group_gather(lane, T)
         ntiles = self.counters[0:1]
         grouped_gemm(w=w13, x=self.pool_x, num_experts=self.experts_local, n_per_expert=2 * cfg.intermediate,
@@ -267,6 +340,35 @@ class EgMoeEndpoint:
                      k=cfg.intermediate, tile_info=self.tile_info, num_tok_tiles=ntiles,
                      block_tok=cfg.block_tok, epilogue=EPI_COMBINE, fp8=cfg.fp8, x_scale=self.pool_hs,
                      w_scale=w2_scale, row_meta=self.row_meta, peer_combine=self.peer_combine[lane],
+                     peer_flag=self.peer_flag[lane], combine_tokens=cfg.max_tokens, hidden=cfg.hidden,
+                     epoch=w.epoch2, done_counter=w.done2, status=self.status, grid=self.grid,
+                     trace=self.trace[lane] if self.trace else None)
+
+
+    def _run_layer_direct(self, lane: int, w13, w2, w13_scale, w2_scale) -> None:
+        """The layer when the sources stored their rows straight into the expert stripes: one warp
+        waits for the flags and turns the slot counters into the tile schedule, then the two GEMMs."""
+        cfg, w = self.cfg, self.lanes[lane]
+        s = ScheduleDesc()
+        s.n2m_flag, s.A, s.epoch, s.counts = ptr(self.n2m_flag[lane]), cfg.num_ag, ptr(w.epoch), ptr(self.dcount[lane])
+        s.experts_local, s.cap, s.block_tok = self.experts_local, cfg.direct_cap, cfg.block_tok
+        s.max_tok_tiles = self.dtile_info.shape[0]
+        s.tile_info, s.counters, s.expert_counts = ptr(self.dtile_info), ptr(self.counters), ptr(self.expert_counts)
+        s.timeout_ns, s.status = self.timeout_ns, ptr(self.status)
+        s.trace = ptr(self.trace[lane]) if self.trace else None
+        check(lib().afd_eg_schedule(C.byref(s), cur_stream()), "eg_schedule")
+        ntiles = self.counters[0:1]
+        DR = cfg.direct_rows
+        grouped_gemm(w=w13, x=self.dpool_x[lane], num_experts=self.experts_local, n_per_expert=2 * cfg.intermediate,
+                     k=cfg.hidden, tile_info=self.dtile_info, num_tok_tiles=ntiles, block_tok=cfg.block_tok,
+                     epilogue=EPI_SWIGLU, out=None if cfg.fp8 else self.dpool_h, out_ld=cfg.intermediate,
+                     fp8=cfg.fp8, x_scale=self.dpool_xs[lane], w_scale=w13_scale,
+                     out_q=self.dpool_h if cfg.fp8 else None, out_scale=self.dpool_hs,
+                     status=self.status, grid=self.grid)
+        grouped_gemm(w=w2, x=self.dpool_h, num_experts=self.experts_local, n_per_expert=cfg.hidden,
+                     k=cfg.intermediate, tile_info=self.dtile_info, num_tok_tiles=ntiles,
+                     block_tok=cfg.block_tok, epilogue=EPI_COMBINE, fp8=cfg.fp8, x_scale=self.dpool_hs,
+                     w_scale=w2_scale, row_meta=self.dmeta[lane], peer_combine=self.peer_combine[lane],
                      peer_flag=self.peer_flag[lane], combine_tokens=cfg.max_tokens, hidden=cfg.hidden,
                      epoch=w.epoch2, done_counter=w.done2, status=self.status, grid=self.grid,
                      trace=self.trace[lane] if self.trace else None)

@@ -53,6 +53,37 @@ class RouteDispatchDesc(C.Structure):
     ]
 
 
+class DirectDesc(C.Structure):
+    _fields_ = [
+        ("peer_pool", VP * MAX_PEERS), ("peer_scale", VP * MAX_PEERS), ("peer_meta", VP * MAX_PEERS),
+        ("peer_count", VP * MAX_PEERS), ("peer_flag", VP * MAX_PEERS),
+        ("num_eg", C.c_int), ("experts_per_eg", C.c_int), ("cap", C.c_int), ("fp8", C.c_int),
+        ("T", C.c_int), ("H", C.c_int), ("K", C.c_int), ("src_rank", C.c_int),
+        ("epoch", VP), ("done_counter", VP), ("status", VP), ("trace", VP),
+    ]
+
+
+class RouteDirectDesc(C.Structure):
+    _fields_ = [
+        ("attn_out", VP), ("residual", VP), ("norm_w", VP), ("gate_w", VP), ("gate_bias", VP),
+        ("x_out", VP), ("topk_idx_out", VP), ("topk_w_out", VP),
+        ("E", C.c_int), ("gate_fp32", C.c_int), ("scoring", C.c_int), ("renorm", C.c_int), ("offset1", C.c_int),
+        ("eps", C.c_float), ("route_scale", C.c_float),
+        ("tokens_per_cta", C.c_int), ("cluster", C.c_int),
+        ("d", DirectDesc),
+    ]
+
+
+class ScheduleDesc(C.Structure):
+    _fields_ = [
+        ("n2m_flag", VP), ("A", C.c_int), ("epoch", VP), ("counts", VP),
+        ("experts_local", C.c_int), ("cap", C.c_int), ("block_tok", C.c_int), ("max_tok_tiles", C.c_int),
+        ("tile_info", VP), ("counters", VP), ("expert_counts", VP),
+        ("timeout_ns", C.c_ulonglong),
+        ("status", VP), ("trace", VP),
+    ]
+
+
 class GroupDesc(C.Structure):
     _fields_ = [
         ("recv_idx", VP), ("n2m_flag", VP), ("epoch", VP),
@@ -107,6 +138,9 @@ _SIGNATURES = {
     "afd_dispatch_push": (C.c_int, [C.POINTER(DispatchDesc), VP]),
     "afd_ag_route_dispatch": (C.c_int, [C.POINTER(RouteDispatchDesc), VP]),
     "afd_eg_group_gather": (C.c_int, [C.POINTER(GroupDesc), VP]),
+    "afd_dispatch_direct": (C.c_int, [VP, VP, C.POINTER(DirectDesc), VP]),
+    "afd_ag_route_direct": (C.c_int, [C.POINTER(RouteDirectDesc), VP]),
+    "afd_eg_schedule": (C.c_int, [C.POINTER(ScheduleDesc), VP]),
     "afd_ag_combine": (C.c_int, [C.POINTER(CombineDesc), VP]),
     "afd_wait_flag": (C.c_int, [VP, C.c_uint, C.c_ulonglong, VP, VP]),
     "afd_set_flag": (C.c_int, [VP, C.c_uint, VP]),

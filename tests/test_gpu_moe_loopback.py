@@ -25,14 +25,18 @@ def _setup(cfg, timeout_ns=int(2e9)):
     return fabs, ags, egs
 
 
+@pytest.mark.parametrize("direct", [False, True], ids=["recv-slots", "direct-stripes"])
 @pytest.mark.parametrize("fp8", [False, True])
 @pytest.mark.parametrize("num_ag,num_eg,T,bt", [(2, 2, 24, 16), (1, 1, 7, 32), (3, 2, 33, 32), (3, 2, 700, 64)])
-def test_moe_roundtrip(num_ag, num_eg, T, bt, fp8):
+def test_moe_roundtrip(num_ag, num_eg, T, bt, fp8, direct):
+    """`direct`: rows are stored straight into per-expert stripes of the expert GPU's pool (slots
+    claimed with atomic adds) and the expert side only builds the tile schedule; otherwise rows go
+    to per-source receive slots and the expert side groups and gathers them."""
     H, I, E, K = 512, 256, 16, 4
-    if T > 100 and fp8:
-        pytest.skip("the per-token fp8 oracle loop is too slow for the large case")
+    if T > 100 and (fp8 or direct):
+        pytest.skip("large case: bf16 receive-slot path only (the direct exchange is for decode-sized steps)")
     cfg = MoeCommConfig(num_ag=num_ag, num_eg=num_eg, num_lanes=2, max_tokens=max(40, T), hidden=H, topk=K,
-                        num_experts=E, intermediate=I, fp8=fp8, block_tok=bt)
+                        num_experts=E, intermediate=I, fp8=fp8, block_tok=bt, direct_tokens=40 if direct else 0)
     fabs, ags, egs = _setup(cfg)
     g = torch.Generator().manual_seed(0)
     wgu = (torch.randn(E, 2 * I, H, generator=g) * 0.05).to(torch.bfloat16)
@@ -130,11 +134,34 @@ def test_combine_times_out_when_expert_rank_is_silent():
     ("softmax", False, 2048, 120, 8),      # 120 experts: last tile partly empty, 8 tiles
 ])
 def test_fused_route_dispatch_matches_separate_ops(scoring, gate_fp32, H, E, K):
+    _route_dispatch_case(scoring, gate_fp32, H, E, K, direct=False)
+
+
+@pytest.mark.parametrize("tpc,cluster", [(0, 0), (4, 1), (8, 1), (4, 2), (8, 4), (8, 8)])
+@pytest.mark.parametrize("scoring,gate_fp32,H,E,K,fp8", [
+    ("softmax", False, 2048, 128, 8, False),     # tensor-core logits
+    ("softmax", False, 4096, 128, 8, True),      # 235B shape, FP8 rows with 1x128 scales
+    ("sigmoid", True, 3072, 256, 8, False),      # fp32 gate + bias (SIMT logits)
+    ("softmax", False, 4096, 512, 10, False),    # 512 experts top-10
+    ("softmax", False, 512, 16, 4, False),       # tiny: SIMT bf16 logits
+])
+def test_fused_route_direct_dispatch(scoring, gate_fp32, H, E, K, fp8, tpc, cluster):
+    """The direct variant: TPC tokens per CTA, optional cluster split of the expert range; rows,
+    scales and meta words land in the experts' stripes, counters hold the per-expert counts."""
+    if cluster and (E % (cluster * 16) != 0 and not gate_fp32 and E >= 128):
+        pytest.skip("expert range does not split over this cluster size")
+    if cluster and E % cluster != 0:
+        pytest.skip("expert range does not split over this cluster size")
+    _route_dispatch_case(scoring, gate_fp32, H, E, K, direct=True, fp8=fp8, tpc=tpc, cluster=cluster)
+
+
+def _route_dispatch_case(scoring, gate_fp32, H, E, K, direct, fp8=False, tpc=0, cluster=0):
     """residual add + RMSNorm + router + push in one launch == the four separate ops."""
     I, T = 256, 19
     cfg = MoeCommConfig(num_ag=1, num_eg=2, num_lanes=1, max_tokens=32, hidden=H, topk=K, num_experts=E,
-                        intermediate=I, block_tok=16)
+                        intermediate=I, block_tok=16, fp8=fp8, direct_tokens=32 if direct else 0)
     fabs, ags, egs = _setup(cfg)
+    ags[0].route_tokens_per_cta, ags[0].route_cluster = tpc, cluster
     g = torch.Generator().manual_seed(3)
     attn_out = torch.randn(T, H, generator=g).to(torch.bfloat16).to(DEV)
     residual = torch.randn(T, H, generator=g).to(torch.bfloat16).to(DEV)
@@ -154,6 +181,38 @@ def test_fused_route_dispatch_matches_separate_ops(scoring, gate_fp32, H, E, K):
     assert torch.equal(residual, res_ref) and torch.equal(x_out, x_ref)
     assert torch.equal(idx.cpu(), idx_ref)
     torch.testing.assert_close(w.cpu(), w_ref, atol=1e-5, rtol=1e-4)
+    if direct:
+        # what landed in the expert stripes: every (token, k) exactly once, with its row (and scales)
+        El, cap = cfg.experts_per_eg, cfg.direct_cap
+        xq_ref, xs_ref = (ref.group_quant_fp8(x_ref.cpu(), 128) if fp8 else (None, None))
+        seen = set()
+        for e, eg in enumerate(egs):
+            counts = eg.dcount[0].cpu()
+            want = torch.bincount((idx_ref[(idx_ref // El) == e] - e * El).flatten().long(), minlength=El)
+            assert torch.equal(counts.long(), want)
+            meta, pool = eg.dmeta[0].cpu(), eg.dpool_x[0]
+            for el in range(El):
+                for s_ in range(int(counts[el])):
+                    row = el * cap + s_
+                    m = int(meta[row]) & 0xffffffff
+                    src, k, t = m >> 24, (m >> 16) & 0xff, m & 0xffff
+                    assert src == 0 and int(idx_ref[t, k]) == e * El + el and (t, k) not in seen
+                    seen.add((t, k))
+                    if fp8:
+                        sc = eg.dpool_xs[0][row].cpu()
+                        torch.testing.assert_close(sc, xs_ref[t], rtol=1e-6, atol=0)
+                        deq = pool[row].cpu().float().view(-1, 128) * sc[:, None]
+                        want_deq = xq_ref[t].float().view(-1, 128) * xs_ref[t][:, None]
+                        # same scale; the quantised value may differ by one e4m3 step where x / scale and
+                        # x * (1 / scale) round differently
+                        torch.testing.assert_close(deq, want_deq, rtol=0.13, atol=1e-6)
+                    else:
+                        assert torch.equal(pool[row], x_ref[t])
+            assert int(eg.n2m_flag[0][0]) == 1
+        assert len(seen) == T * K
+        for f in fabs:
+            f.close()
+        return
     # what landed in the expert GPUs' receive slots
     for e, eg in enumerate(egs):
         assert torch.equal(eg.recv_idx[0][0, :T].cpu(), idx_ref)
