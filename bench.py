@@ -35,7 +35,8 @@ sys.path.insert(0, HERE)
 
 # Published reference numbers (GB200 NVL72, 4 attention + 4 FFN GPUs, scripts/benchmark/configs.json:366), tok/s/GPU.
 PUBLISHED_TOK_S_PER_GPU = {"qwen3-235b-a22b-fp8": 1542.0}
-METRIC = "decode tok/s, AFD (attention + expert GPUs), aggregate over all GPUs"
+METRIC = ("decode tok/s of the whole job, AFD attention + expert GPUs on N x B200, max over ranks "
+          "(per-GPU decode tok/s: per_gpu_tok_s; TPOT p50: tpot_p50_ms; N2M/M2N GB/s: n2m_m2n)")
 
 
 def parse_args():
@@ -136,6 +137,9 @@ def main():
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
     if world > 1:
+        # device-side timeline of the N2M / M2N exchange (a few timer stores per kernel): the measured
+        # round-trip and expert-busy times behind the n2m_m2n figures
+        os.environ.setdefault("FASTAFD_COMM_TRACE", "1")
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
         dist.init_process_group(backend="cpu:gloo,cuda:nccl", rank=rank, world_size=world, device_id=device)
 
@@ -194,13 +198,17 @@ def main():
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     stream = eng.attn.main_stream if eng.attn is not None else eng.expert.stream
     ev0.record(stream)
-    drv.run_decode_steps(args.steps, pipelined=True)
+    step_events = [ev0]
+    drv.run_decode_steps(args.steps, pipelined=True, events=step_events, event_stream=stream)
     ev1.record(stream)
     torch.cuda.synchronize()
     dev_ms = ev0.elapsed_time(ev1)
+    per_step = sorted(step_events[i].elapsed_time(step_events[i + 1]) for i in range(len(step_events) - 1))
+    tpot_p50 = per_step[len(per_step) // 2] if per_step else dev_ms / args.steps
     barrier()
     clocks = sampler.stop()
     dev_ms = max_over_ranks(dev_ms)
+    tpot_p50 = max_over_ranks(tpot_p50)
 
     # ---- end-to-end region: one step at a time through the public API ----------------------
     barrier()
@@ -222,7 +230,7 @@ def main():
     status = eng.synchronize()
 
     trace_info = None
-    if os.environ.get("FASTAFD_COMM_TRACE") == "1":
+    if os.environ.get("FASTAFD_COMM_TRACE") == "1" and cfg.is_moe:
         from fastafd_b200.moe.afd_moe import summarize_trace
 
         mine = []
@@ -261,11 +269,28 @@ def main():
         copies = n_eg * (1.0 - (1.0 - 1.0 / n_eg) ** K)
         per_tok_up, per_tok_down = row_up * copies + K * 4 * n_eg, K * H * 2
         step_s = dev_ms / args.steps / 1e3
+        if os.environ.get("FASTAFD_DIRECT", "1") != "0":
+            per_tok_up = K * (row_up + 4)          # direct exchange: one row copy (+ meta word) per chosen expert
         comm = {"n2m_bytes_per_step_per_attn_gpu": int(moe_layers * b * per_tok_up),
                 "m2n_bytes_per_step_per_attn_gpu": int(moe_layers * b * per_tok_down),
                 "n2m_GB_s_avg_over_step": round(moe_layers * b * per_tok_up / step_s / 1e9, 2),
                 "m2n_GB_s_avg_over_step": round(moe_layers * b * per_tok_down / step_s / 1e9, 2),
-                "note": "averaged over the whole step; the transfers ride in the GEMM epilogues and the route kernel"}
+                "note": "bytes counted from the exchanged tensors; averaged over the whole step (the transfers ride in "
+                        "the route kernel and the down-projection epilogue)"}
+        if trace_info is not None:
+            # measured on the device timeline: the part of a micro-batch's round trip through the expert
+            # GPUs that is not expert compute = both transfers + flag latencies
+            rt_us = [v["round_trip_us"] for info in trace_info.values() for role, lanes in info if role == "attention"
+                     for v in lanes if v.get("round_trip_us")]
+            busy_us = [v["busy_us"] for info in trace_info.values() for role, lanes in info if role == "expert"
+                       for v in lanes if v.get("busy_us")]
+            if rt_us and busy_us:
+                exposed = max(statistics.median(rt_us) - statistics.median(busy_us), 1e-3)
+                per_round = (per_tok_up + per_tok_down) * b / args.num_mb
+                comm.update({"round_trip_us_median": round(statistics.median(rt_us), 2),
+                             "expert_busy_us_median": round(statistics.median(busy_us), 2),
+                             "exposed_exchange_us": round(exposed, 2),
+                             "n2m_plus_m2n_GB_s_over_exposed_time": round(per_round / exposed / 1e3, 2)})
     if rank == 0:
         out = {
             "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
@@ -274,7 +299,7 @@ def main():
             "dtype": "fp8-block128 weights, bf16 attention/KV" if cfg.quant.is_fp8 else "bf16",
             "data": "synthetic (random-init weights, random KV cache and token ids)",
             "per_gpu_tok_s": round(value / world, 2),
-            "tpot_ms": round(dev_ms / args.steps, 4),
+            "tpot_ms": round(dev_ms / args.steps, 4), "tpot_p50_ms": round(tpot_p50, 4),
             "config": {"model": args.model, "global_batch": b * n_attn, "seq_len": args.context,
                        "decode_tokens_timed": args.steps, "micro_batches": args.num_mb, "page_size": 16,
                        "parallelism": "colocated-1gpu" if topo.colocated else (f"attn_dp{topo.attn_dp}" + (f"xtp{tp}" if tp > 1 else "") + f"+mlp_ep{topo.mlp_ep}"),
@@ -294,7 +319,7 @@ def main():
         }
         if comm is not None:
             out["n2m_m2n"] = comm
-        if trace_info is not None:
+        if trace_info is not None and os.environ.get("FASTAFD_COMM_TRACE_FULL") == "1":
             out["comm_trace"] = trace_info
         if truncated:
             out["invalid"] = "model truncated with --layers (debug run)"

@@ -84,7 +84,7 @@ __global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, __nv_bfloat1
 // then NeoX RoPE on the first rot_dim dims (pairs (i, i + rot_dim/2)), in place.
 // K (after rope) and V are also stored to the paged cache at slot out_loc[token].
 template <int D>
-__global__ void qk_norm_rope_store_kernel(__nv_bfloat16* qkv, const __nv_bfloat16* __restrict__ qw,
+__global__ void qk_norm_rope_store_kernel(__nv_bfloat16* qkv, long ld, const __nv_bfloat16* __restrict__ qw,
                                           const __nv_bfloat16* __restrict__ kw,
                                           const float* __restrict__ cos_sin,  // [max_pos][rot_dim]
                                           const int* __restrict__ positions,
@@ -97,7 +97,7 @@ __global__ void qk_norm_rope_store_kernel(__nv_bfloat16* qkv, const __nv_bfloat1
   const int lane = threadIdx.x & 31;
   if (gw >= static_cast<long>(T) * heads) return;
   const int tok = gw / heads, head = gw % heads;
-  __nv_bfloat16* p = qkv + (static_cast<size_t>(tok) * heads + head) * D;
+  __nv_bfloat16* p = qkv + static_cast<size_t>(tok) * ld + static_cast<size_t>(head) * D;   // rows `ld` elements apart
   const bool is_q = head < Hq, is_k = !is_q && head < Hq + Hkv;
   // lane holds dims [lane*PER/2 .. ) of the first half and the same of the second half
   // so that rope pairs (i, i + D/2) sit in one lane when rot_dim == D.
@@ -431,20 +431,20 @@ extern "C" int afd_rmsnorm(const void* x, void* residual, const void* w, void* o
   return 0;
 }
 
-extern "C" int afd_qk_norm_rope_store(void* qkv, const void* qw, const void* kw, const void* cos_sin,
+extern "C" int afd_qk_norm_rope_store(void* qkv, long ld, const void* qw, const void* kw, const void* cos_sin,
                                       const void* positions, const void* out_loc, void* k_cache,
                                       void* v_cache, int T, int Hq, int Hkv, int D, int rot_dim,
                                       float eps, int max_pos, long cache_slots, void* status,
                                       void* stream) {
   if (T == 0) return 0;
-  if (rot_dim > D || rot_dim % 2 != 0) return -1;
+  if (rot_dim > D || rot_dim % 2 != 0 || ld < static_cast<long>(Hq + 2 * Hkv) * D) return -1;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const long warps = static_cast<long>(T) * (Hq + 2 * Hkv);
   const int threads = 256;
   const int blocks = static_cast<int>((warps * 32 + threads - 1) / threads);
 #define LAUNCH_QK(DD)                                                                                   \
   qk_norm_rope_store_kernel<DD><<<blocks, threads, 0, st>>>(                                            \
-      static_cast<__nv_bfloat16*>(qkv), static_cast<const __nv_bfloat16*>(qw),                          \
+      static_cast<__nv_bfloat16*>(qkv), ld, static_cast<const __nv_bfloat16*>(qw),                      \
       static_cast<const __nv_bfloat16*>(kw), static_cast<const float*>(cos_sin),                        \
       static_cast<const int*>(positions), static_cast<const int*>(out_loc),                             \
       static_cast<__nv_bfloat16*>(k_cache), static_cast<__nv_bfloat16*>(v_cache), T, Hq, Hkv, rot_dim,  \

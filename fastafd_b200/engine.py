@@ -381,13 +381,14 @@ class SpmdDriver:
             a.token_pool.copy_(torch.randint(0, self.e.cfg.vocab_size, a.token_pool.shape, generator=g,
                                              device=a.device, dtype=torch.int32))
 
-    def run_decode_steps(self, n: int, pipelined: bool = True) -> int:
+    def run_decode_steps(self, n: int, pipelined: bool = True, events: Optional[list] = None, event_stream=None) -> int:
         """n decode steps of the running batch through plan -> H2D -> replay -> D2H -> complete.
         Requests must be greedy / ignore_eos with enough max_tokens left, so that every rank can
         plan without exchanging tokens (the one-step-ahead assumption of the coordinator: step
         N+1 is planned as if step N produced one token per request). With `pipelined`, step N+1
-        is planned and queued before step N's tokens are read back. Returns tokens generated by
-        this rank's lane."""
+        is planned and queued before step N's tokens are read back. `events`: a list that receives one
+        CUDA timing event per step, recorded on `event_stream` behind the step's work. Returns tokens
+        generated by this rank's lane."""
         e, rt = self.e, self.e.rt
         produced = 0
         pending = None
@@ -415,6 +416,10 @@ class SpmdDriver:
                     produced += self._finish_fast(sid, mine)
             if e.expert is not None:
                 e.step(EgStepPlan(step_id=sid, phase="decode", tokens_per_mb=[bucket // e.topo.attn_tp] * rt.num_mb))
+            if events is not None:          # one timing event per queued step (per-step device times)
+                ev = torch.cuda.Event(enable_timing=True)
+                ev.record(event_stream)
+                events.append(ev)
         if pending is not None:
             produced += self._finish_fast(*pending)
         return produced

@@ -222,9 +222,29 @@ class AttentionStage:
         self._post_load()
 
     def _post_load(self) -> None:
-        c = self.cfg
+        c, D = self.cfg, self.cfg.head_dim
         self.cos_sin = ref.build_cos_sin_cache(min(c.max_position, 1 << 17), c.rotary_dim, c.rope.theta, self.device,
                                               scaling=c.rope.scaling)
+        # kernel-ready forms (CUDA): per-head norm weights with the +1 offset folded in once, and for
+        # gated attention the projection rows re-ordered from [q | gate | k | v] to [q | k | v | gate],
+        # so that q, k, v are a contiguous prefix of every output row (norm + RoPE + store and the
+        # attention kernel read them in place) and the gate is a strided view behind them.
+        self.qk_w: Dict[int, Tuple[Tensor, Tensor]] = {}
+        self.gate_last = False
+        for i in range(c.num_layers):
+            if c.layer_type(i) != "full":
+                continue
+            p = f"model.layers.{i}.self_attn."
+            if c.qk_norm == "head":
+                qw, kw = self.w[p + "q_norm.weight"], self.w[p + "k_norm.weight"]
+                self.qk_w[i] = (qw + 1, kw + 1) if c.norm_offset1 else (qw, kw)
+            if c.attn_output_gate and self.device.type == "cuda":
+                n = self.hq * D
+                for suffix in ("qkv_proj.weight", "qkv_proj.bias"):
+                    w = self.w.get(p + suffix)
+                    if w is not None:
+                        self.w[p + suffix] = torch.cat([w[:n], w[2 * n:], w[n:2 * n]], 0).contiguous()
+                self.gate_last = True
 
     # ------------------------------------------------------------------ forward pieces
     def embed(self, ids: Tensor, scatter: bool = False) -> Tensor:
@@ -264,22 +284,32 @@ class AttentionStage:
         qkv = _linear(x, self.w[p + "qkv_proj.weight"], self.w.get(p + "qkv_proj.bias"))
         T = x.shape[0]
         gate = None
-        if c.attn_output_gate:
+        nqkv = (self.hq + 2 * self.hkv) * D
+        if c.attn_output_gate and self.gate_last:
+            gate = qkv[:, nqkv:]                       # rows are [q | k | v | gate]: nothing is copied
+        elif c.attn_output_gate:
             # rows are [q(hq*D) | gate(hq*D) | k | v]
             q_part, gate, kv_part = qkv[:, :self.hq * D], qkv[:, self.hq * D:2 * self.hq * D], qkv[:, 2 * self.hq * D:]
             qkv = torch.cat([q_part, kv_part], dim=-1).contiguous()
         li = self.full_index[layer]
         kc, vc = kv.k[li], kv.v[li]
-        qw = kw = None
-        if c.qk_norm == "head":
-            qw, kw = self.w[p + "q_norm.weight"], self.w[p + "k_norm.weight"]
-            if c.norm_offset1:
-                qw, kw = qw + 1, kw + 1
-        elif c.qk_norm == "cross_head":
-            qkv = self._cross_head_norm(qkv, self.w[p + "q_norm.weight"], self.w[p + "k_norm.weight"])
-        ops.qk_norm_rope_store(qkv, qw, kw, self.cos_sin, meta.positions, meta.out_loc, kc, vc, self.hq, self.hkv,
-                               D, c.rotary_dim, c.rms_eps, status=meta.status)
-        q = qkv.view(T, self.hq + 2 * self.hkv, D)[:, :self.hq]
+        qw, kw = self.qk_w.get(layer, (None, None))
+        if c.qk_norm == "cross_head" and qkv.is_cuda:
+            # one launch: joint RMSNorm over the q heads / k heads + RoPE + paged store
+            qn, kn = self.hq * D, self.hkv * D
+            sq = None
+            if self.tp_size > 1:
+                sq = self.comm.all_reduce(ops.qk_square_sums(qkv, qn, kn))
+            ops.cross_head_norm_rope_store(qkv, self.w[p + "q_norm.weight"], self.w[p + "k_norm.weight"], self.cos_sin,
+                                           meta.positions, meta.out_loc, kc, vc, self.hq, self.hkv, D, c.rotary_dim,
+                                           c.rms_eps, c.num_q_heads * D, max(c.num_kv_heads, self.tp_size) * D,
+                                           sq=sq, status=meta.status)
+        else:
+            if c.qk_norm == "cross_head":
+                qkv = self._cross_head_norm(qkv, self.w[p + "q_norm.weight"], self.w[p + "k_norm.weight"])
+            ops.qk_norm_rope_store(qkv, qw, kw, self.cos_sin, meta.positions, meta.out_loc, kc, vc, self.hq, self.hkv,
+                                   D, c.rotary_dim, c.rms_eps, status=meta.status)
+        q = qkv.view(T, -1, D)[:, :self.hq]
         scale = ref.softmax_scale(D)
         if meta.is_prefill:
             o = self._prefill_attention(q, kc, vc, meta, scale, kv.page_size)
@@ -289,7 +319,7 @@ class AttentionStage:
                                      workspace=meta.workspace, status=meta.status)
         o = o.reshape(T, self.hq * D)
         if gate is not None:
-            o = (o.float() * torch.sigmoid(gate.float())).to(o.dtype)
+            o = ops.sigmoid_gate_mul(o if o.is_contiguous() else o.contiguous(), gate)
         w_o = self.w[p + "o_proj.weight"]
         if (fuse_scatter and meta.lane >= 0 and o.is_cuda and o.dtype == torch.bfloat16
                 and hasattr(self.comm, "oproj_reduce_scatter") and self.comm.can_fuse_oproj(T, o.shape[1])):
@@ -364,11 +394,8 @@ class AttentionStage:
             logits = logits.float()
         bias = self.w.get(p + "e_score_correction_bias")
         if c.n_group > 1:
-            idx, w = ref.grouped_topk_route(logits, bias, c.num_experts_per_tok, c.n_group, c.topk_group,
-                                            c.norm_topk_prob, 1.0)
-            if out_idx is not None:
-                return out_idx.copy_(idx), out_w.copy_(w)
-            return idx, w
+            return ops.grouped_topk_route(logits, bias, c.num_experts_per_tok, c.n_group, c.topk_group,
+                                          c.norm_topk_prob, 1.0, out_idx=out_idx, out_w=out_w)
         return ops.topk_route(logits, bias, c.num_experts_per_tok, c.scoring, c.norm_topk_prob, 1.0,
                               out_idx=out_idx, out_w=out_w)
 
@@ -384,8 +411,7 @@ class AttentionStage:
             h = ops.silu_mul(_linear(x, self.w[p + "shared_expert.gate_up_proj.weight"]))
             out = _linear(h, self.w[p + "shared_expert.down_proj.weight"])
             if c.shared_expert_gate:
-                g = torch.sigmoid(_linear(x, self.w[p + "shared_expert_gate.weight"]).float())
-                out = (out.float() * g).to(out.dtype)
+                out = ops.shared_gate_mul(x, self.w[p + "shared_expert_gate.weight"], out)
         else:
             return None
         if self.tp_size > 1 and reduce != "none":

@@ -45,18 +45,89 @@ def add_rmsnorm(x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, eps: f
 
 def qk_norm_rope_store(qkv, qw, kw, cos_sin, positions, out_loc, k_cache, v_cache, Hq, Hkv, D,
                        rot_dim, eps, status=None):
-    """In place on qkv [T, (Hq+2Hkv)*D]: per-head RMSNorm of q/k (when weights given), NeoX
+    """In place on the first (Hq+2Hkv)*D columns of qkv [T, >= (Hq+2Hkv)*D] (rows may carry more
+    columns behind them, e.g. an output gate): per-head RMSNorm of q/k (when weights given), NeoX
     RoPE, and a store of k/v into the paged cache ([slots,Hkv,D]) at out_loc (-1 skips)."""
     if not qkv.is_cuda:
+        n = (Hq + 2 * Hkv) * D
+        if qkv.shape[1] != n:
+            part = qkv[:, :n].contiguous()
+            ref.qk_norm_rope_store(part, qw, kw, cos_sin, positions, out_loc, k_cache, v_cache, Hq, Hkv, D, rot_dim, eps)
+            qkv[:, :n] = part
+            return qkv
         return ref.qk_norm_rope_store(qkv, qw, kw, cos_sin, positions, out_loc, k_cache, v_cache,
                                       Hq, Hkv, D, rot_dim, eps)
     T = qkv.shape[0]
+    assert qkv.stride(1) == 1
     slots = k_cache.shape[0] if k_cache is not None else 0
-    check(lib().afd_qk_norm_rope_store(ptr(qkv), ptr(qw), ptr(kw), ptr(cos_sin), ptr(positions),
+    check(lib().afd_qk_norm_rope_store(ptr(qkv), qkv.stride(0), ptr(qw), ptr(kw), ptr(cos_sin), ptr(positions),
                                        ptr(out_loc), ptr(k_cache), ptr(v_cache), T, Hq, Hkv, D,
                                        rot_dim, eps, cos_sin.shape[0], slots, ptr(status),
                                        cur_stream()), "qk_norm_rope_store")
     return qkv
+
+
+def cross_head_norm_rope_store(qkv, qw, kw, cos_sin, positions, out_loc, k_cache, v_cache, Hq, Hkv, D, rot_dim, eps,
+                               q_denom: int, k_denom: int, sq: Optional[torch.Tensor] = None, status=None):
+    """MiniMax-M2 attention prologue in one launch, in place on qkv [T, (Hq+2Hkv)*D] bf16 (CUDA):
+    RMSNorm over all q heads jointly and all k heads jointly (`q_denom` / `k_denom` = element
+    counts of the full, unsharded q and k; `sq` [T,2] = all-reduced sums of squares under TP, else
+    computed here), weights per element, then RoPE and the paged K/V store."""
+    T = qkv.shape[0]
+    assert qkv.is_cuda and qkv.stride(1) == 1
+    slots = k_cache.shape[0] if k_cache is not None else 0
+    check(lib().afd_cross_head_norm_rope_store(ptr(qkv), qkv.stride(0), ptr(qw), ptr(kw), ptr(sq), float(q_denom),
+                                               float(k_denom), ptr(cos_sin), ptr(positions), ptr(out_loc), ptr(k_cache),
+                                               ptr(v_cache), T, Hq, Hkv, D, rot_dim, eps, cos_sin.shape[0], slots,
+                                               ptr(status), cur_stream()), "cross_head_norm_rope_store")
+    return qkv
+
+
+def qk_square_sums(qkv, q_elems: int, k_elems: int) -> torch.Tensor:
+    """[T,2] fp32 sums of squares of the first q_elems and the next k_elems columns of each row."""
+    out = torch.empty(qkv.shape[0], 2, dtype=torch.float32, device=qkv.device)
+    check(lib().afd_qk_square_sums(ptr(qkv), qkv.stride(0), ptr(out), qkv.shape[0], q_elems, k_elems, cur_stream()),
+          "qk_square_sums")
+    return out
+
+
+def grouped_topk_route(logits, bias, K: int, n_group: int, topk_group: int, renorm: bool = True, scale: float = 1.0,
+                       out_idx=None, out_w=None):
+    """GLM-4 / DeepSeek routing (sigmoid scores, group-limited top-k). logits [T,E] fp32 or bf16."""
+    if not logits.is_cuda:
+        idx, w = ref.grouped_topk_route(logits, bias, K, n_group, topk_group, renorm, scale)
+        if out_idx is not None:
+            return out_idx.copy_(idx), out_w.copy_(w)
+        return idx, w
+    T, E = logits.shape
+    if logits.dtype not in (torch.float32, torch.bfloat16) or not logits.is_contiguous():
+        logits = logits.float().contiguous()
+    idx = torch.empty(T, K, dtype=torch.int32, device=logits.device) if out_idx is None else out_idx
+    w = torch.empty(T, K, dtype=torch.float32, device=logits.device) if out_w is None else out_w
+    check(lib().afd_grouped_topk_route(ptr(logits), ptr(bias), ptr(idx), ptr(w), T, E, K, n_group, topk_group,
+                                       int(renorm), scale, int(logits.dtype == torch.bfloat16), cur_stream()),
+          "grouped_topk_route")
+    return idx, w
+
+
+def shared_gate_mul(x, gate_w, y):
+    """y[t] *= sigmoid(x[t] . gate_w) in place (Qwen3.5 shared-expert gate); gate_w [1,H] or [H]."""
+    if not y.is_cuda:
+        g = torch.sigmoid(torch.nn.functional.linear(x, gate_w.view(1, -1)).float())
+        return y.copy_((y.float() * g).to(y.dtype))
+    assert x.is_contiguous() and y.is_contiguous() and x.dtype == torch.bfloat16 and gate_w.dtype == torch.bfloat16
+    check(lib().afd_shared_gate_mul(ptr(x), ptr(gate_w), ptr(y), x.shape[0], x.shape[1], cur_stream()), "shared_gate_mul")
+    return y
+
+
+def sigmoid_gate_mul(o, gate):
+    """o *= sigmoid(gate) in place; o contiguous [T,n] bf16, gate a [T,n] view whose rows may be strided."""
+    if not o.is_cuda:
+        return o.copy_((o.float() * torch.sigmoid(gate.float())).to(o.dtype))
+    assert o.is_contiguous() and gate.stride(1) == 1 and gate.shape == o.shape
+    check(lib().afd_sigmoid_gate_mul(ptr(o), ptr(gate), gate.stride(0), o.shape[0], o.shape[1], cur_stream()),
+          "sigmoid_gate_mul")
+    return o
 
 
 def embedding(ids: torch.Tensor, table: torch.Tensor, vocab_start: int = 0,

@@ -116,10 +116,18 @@ class CombineDesc(C.Structure):
 _SIGNATURES = {
     "afd_grouped_gemm": (C.c_int, [C.POINTER(GroupedGemmDesc), VP]),
     "afd_rmsnorm": (C.c_int, [VP, VP, VP, VP, C.c_long, C.c_int, C.c_float, C.c_int, VP]),
-    "afd_qk_norm_rope_store": (C.c_int, [VP, VP, VP, VP, VP, VP, VP, VP, C.c_int, C.c_int, C.c_int,
+    "afd_qk_norm_rope_store": (C.c_int, [VP, C.c_long, VP, VP, VP, VP, VP, VP, VP, C.c_int, C.c_int, C.c_int,
                                          C.c_int, C.c_int, C.c_float, C.c_int, C.c_long, VP, VP]),
     "afd_embedding": (C.c_int, [VP, VP, VP, C.c_int, C.c_int, C.c_int, C.c_int, VP]),
     "afd_silu_mul": (C.c_int, [VP, VP, C.c_long, C.c_int, VP]),
+    "afd_cross_head_norm_rope_store": (C.c_int, [VP, C.c_long, VP, VP, VP, C.c_float, C.c_float, VP, VP, VP, VP, VP,
+                                                 C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_float, C.c_int,
+                                                 C.c_long, VP, VP]),
+    "afd_qk_square_sums": (C.c_int, [VP, C.c_long, VP, C.c_int, C.c_int, C.c_int, VP]),
+    "afd_grouped_topk_route": (C.c_int, [VP, VP, VP, VP, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                         C.c_float, C.c_int, VP]),
+    "afd_shared_gate_mul": (C.c_int, [VP, VP, VP, C.c_int, C.c_int, VP]),
+    "afd_sigmoid_gate_mul": (C.c_int, [VP, VP, C.c_long, C.c_long, C.c_int, VP]),
     "afd_topk_route": (C.c_int, [VP, VP, VP, VP, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
                                  C.c_float, C.c_int, VP]),
     "afd_decode_attention_strided": (C.c_int, [VP, C.c_long, VP, VP, VP, VP, VP, VP, C.c_int, C.c_int, C.c_int,

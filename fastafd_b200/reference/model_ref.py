@@ -148,3 +148,62 @@ def greedy_generate_reference(cfg: ModelConfig, stage, expert_stages, prompts: L
             new.append(tok)
         outs.append(new)
     return outs
+
+
+def logit_check(cfg: ModelConfig, stage, expert_stages, prompts: List[List[int]], outputs: List[List[int]], taps,
+                rel_tol: float = 0.04) -> dict:
+    """Compare the logits a serving engine produced with this reference forward, teacher-forced on
+    the engine's own tokens.
+
+    `taps` are the engine's (table rows, kv lengths, logits) records (AttentionWorker.logit_tap);
+    prompts must have distinct lengths (a row is matched to its request by the length of its first
+    record). For every record the reference recomputes the whole sequence (prompt + the tokens the
+    engine emitted so far) in fp32 from `stage` / `expert_stages` (give it the same weight values
+    the engine computes with, e.g. bf16-rounded). Tolerance: `rel_tol` x the standard deviation of
+    the reference logits of that position. The engine's argmax must equal the reference's whenever
+    the reference's top-2 gap exceeds twice that tolerance.
+    Returns {"positions", "max_err_over_tol", "argmax_checked", "argmax_equal"}; raises AssertionError
+    with the first offending position."""
+    by_len = {len(p): i for i, p in enumerate(prompts)}
+    assert len(by_len) == len(prompts), "prompts must have distinct lengths"
+    row_req = {}
+    n_pos = n_arg = n_arg_ok = 0
+    worst = 0.0
+    for rows, lens, logits in taps:
+        for row, L, lg in zip(rows.tolist(), lens.tolist(), logits):
+            if row not in row_req:
+                if L not in by_len:
+                    continue                      # a padding row
+                row_req[row] = by_len[L]
+            r = row_req[row]
+            j = L - len(prompts[r])
+            if j < 0 or j >= len(outputs[r]):
+                continue
+            want = forward_logits(cfg, stage, expert_stages, list(prompts[r]) + list(outputs[r][:j]))
+            tol = rel_tol * float(want.std())
+            err = float((lg[:cfg.vocab_size] - want).abs().max())
+            worst = max(worst, err / tol)
+            assert err <= tol, f"request {r} token {j}: |logit - reference| = {err:.4f} > {tol:.4f}"
+            top2 = want.topk(2).values
+            n_pos += 1
+            if float(top2[0] - top2[1]) > 2 * tol:
+                n_arg += 1
+                n_arg_ok += int(int(lg[:cfg.vocab_size].argmax()) == int(want.argmax()))
+                assert int(lg[:cfg.vocab_size].argmax()) == int(want.argmax()), f"request {r} token {j}: argmax differs"
+    return {"positions": n_pos, "max_err_over_tol": round(worst, 3), "argmax_checked": n_arg, "argmax_equal": n_arg_ok}
+
+
+def bf16_rounded_copy(stage):
+    """A CPU fp32 copy of a stage whose weights hold the values a bf16 engine built from the same
+    seed computes with: everything the engine keeps in bf16 is rounded to bf16, tensors it keeps in
+    fp32 (router gate of fp32-routed models, selection bias, A_log, dt_bias) are left as they are."""
+    import copy
+
+    c = copy.copy(stage)
+    if hasattr(stage, "param_shapes"):
+        kinds = {k: kind for k, (_, kind) in stage.param_shapes().items()}
+        c.w = {k: (v if kinds.get(k) == "fp32" else v.to(torch.bfloat16).float()) for k, v in stage.w.items()}
+    else:
+        c.gate_up = {k: v.to(torch.bfloat16).float() for k, v in stage.gate_up.items()}
+        c.down = {k: v.to(torch.bfloat16).float() for k, v in stage.down.items()}
+    return c

@@ -129,6 +129,9 @@ class AttentionWorker:
         self.graphs: Dict[int, "torch.cuda.CUDAGraph"] = {}
         self.kernels_per_step: Dict[int, int] = {}
         self.spec = None          # SpecRunner when speculative decoding is on
+        # validation hook: a list that receives (rows, kv lengths, fp32 logits) of every sampled row of
+        # every eager step, so that logits can be compared with a reference forward (never set in serving)
+        self.logit_tap: Optional[list] = None
         if self.cuda:
             self.main_stream = torch.cuda.Stream(self.device)
             self.lane_streams = [torch.cuda.Stream(self.device) for _ in range(self.num_mb)]
@@ -339,6 +342,8 @@ class AttentionWorker:
         b = self.bufs[lane]
         logits = self.model.lm_head(self.full_tokens(mb.normed))
         b.logits = logits
+        if self.logit_tap is not None and not (self.cuda and torch.cuda.is_current_stream_capturing()):
+            self.logit_tap.append((b.rows[:bucket].cpu().clone(), b.seq_lens[:bucket].cpu().clone(), logits[:bucket].float().cpu().clone()))
         ops.argmax(logits, out=b.next_tokens[:bucket]) if self.cuda else b.next_tokens[:bucket].copy_(ops.argmax(logits))
         self.token_pool[b.rows[:bucket], b.seq_lens[:bucket].long()] = b.next_tokens[:bucket]
 
@@ -506,6 +511,8 @@ class AttentionWorker:
                     rows_s = torch.from_numpy(mbp.rows[mbp.sample_rows].astype(np.int64)).to(dev)
                     lens_s = torch.from_numpy(mbp.seq_lens[mbp.sample_rows].astype(np.int64)).to(dev)
                     self.token_pool[rows_s, lens_s] = t.to(torch.int32)
+                    if self.logit_tap is not None:
+                        self.logit_tap.append((rows_s.cpu().clone(), lens_s.cpu().clone(), logits.float().cpu().clone()))
                     toks[mbp.sample_rows] = t.cpu().numpy()
                 else:
                     t = None

@@ -47,6 +47,44 @@ def test_gpu_generation_graph_equals_eager_and_tracks_oracle(cfg):
     assert same >= 0.8 * total, (graph, oracle)
 
 
+FAMILY_CFGS = {
+    "qwen3_moe": MID,
+    "minimax_m2": ModelConfig(architecture="MiniMaxM2ForCausalLM", num_layers=3, hidden_size=512, num_q_heads=8, num_kv_heads=2,
+                              head_dim=128, vocab_size=2048, rope=RopeConfig(5e6, 64), qk_norm="cross_head", num_experts=16,
+                              num_experts_per_tok=4, moe_intermediate_size=256, scoring="sigmoid", router_bias=True,
+                              router_fp32=True),
+    "glm4_moe": ModelConfig(architecture="Glm4MoeForCausalLM", num_layers=3, hidden_size=512, num_q_heads=8, num_kv_heads=2,
+                            head_dim=128, vocab_size=2048, rope=RopeConfig(1e6, 64), qk_norm="none", attention_bias=True,
+                            intermediate_size=384, num_experts=16, num_experts_per_tok=4, moe_intermediate_size=256,
+                            scoring="sigmoid", router_bias=True, routed_scaling_factor=2.5, n_group=4, topk_group=2,
+                            num_shared_experts=1, shared_expert_intermediate_size=256, first_k_dense=1),
+    "qwen35_hybrid": HYBRID,
+}
+
+
+@pytest.mark.parametrize("name", list(FAMILY_CFGS))
+def test_logits_of_every_family_match_the_reference_forward(name):
+    """Whole model on the GPU (eager, so that every step's logits can be tapped) against the
+    whole-sequence fp32 reference forward on the same bf16-rounded weights, teacher-forced on the
+    GPU's own tokens: every logit within 4 % of the position's logit spread, argmax equal wherever
+    the reference's top-2 gap is larger than twice that."""
+    from fastafd_b200.reference.model_ref import bf16_rounded_copy, logit_check
+
+    cfg = FAMILY_CFGS[name]
+    g = torch.Generator().manual_seed(1)
+    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (33, 20, 7, 48)]
+    eng = AfdEngine(cfg, _rt("cuda:0", False), AfdTopology(colocated=True), 0, "cuda:0", seed=0)
+    eng.attn.logit_tap = []
+    out = SpmdDriver(eng).generate(prompts, SamplingParams(max_tokens=5, ignore_eos=True))
+    taps = eng.attn.logit_tap
+    eng.close()
+    cpu = AfdEngine(cfg, _rt("cpu", False), AfdTopology(colocated=True), 0, "cpu", seed=0)
+    stage = bf16_rounded_copy(cpu.attn.model)
+    experts = [bf16_rounded_copy(cpu.expert_stage)]
+    stats = logit_check(cfg, stage, experts, prompts, out, taps)
+    assert stats["positions"] == 4 * 5 and stats["argmax_checked"] > 0, stats
+
+
 def test_smoke_entry():
     from fastafd_b200.smoke import run_smoke
 

@@ -306,3 +306,70 @@ def test_sample_kernel_greedy_rows_and_bf16():
     torch.cuda.synchronize()
     want = ref.argmax_lowest(logits.float().cpu())
     assert toks.cpu().tolist() == want.tolist()
+
+
+# ------------------------------------------------------------- model-family kernels
+@pytest.mark.parametrize("D,rot,Hq,Hkv,ld_extra", [(128, 64, 6, 2, 0), (128, 128, 4, 1, 0), (64, 32, 8, 4, 256)])
+def test_cross_head_norm_rope_store(D, rot, Hq, Hkv, ld_extra):
+    """Joint RMSNorm over all q heads / all k heads + RoPE + paged store in one launch, against the
+    unfused form (fp32 norm rounded to bf16, then the per-head kernel's oracle without weights)."""
+    T, slots = 21, 64
+    n = (Hq + 2 * Hkv) * D
+    buf = _bf(T, n + ld_extra, seed=61)
+    qkv = buf[:, :n] if ld_extra else buf
+    qw, kw = _bf(Hq * D, seed=62) * 0.2 + 1, _bf(Hkv * D, seed=63) * 0.2 + 1
+    cs = ref.build_cos_sin_cache(512, rot, 5e6).to(DEV)
+    pos = torch.randint(0, 512, (T,), dtype=torch.int32, device=DEV)
+    loc = torch.randperm(slots, device=DEV)[:T].to(torch.int32)
+    loc[5] = -1
+    kc = torch.zeros(slots, Hkv, D, dtype=torch.bfloat16, device=DEV)
+    vc = torch.zeros_like(kc)
+    # oracle
+    x = qkv.cpu().clone().contiguous()
+    q, k = x[:, :Hq * D].float(), x[:, Hq * D:(Hq + Hkv) * D].float()
+    x[:, :Hq * D] = (q * torch.rsqrt(q.pow(2).mean(-1, keepdim=True) + 1e-6) * qw.cpu().float()).to(torch.bfloat16)
+    x[:, Hq * D:(Hq + Hkv) * D] = (k * torch.rsqrt(k.pow(2).mean(-1, keepdim=True) + 1e-6) * kw.cpu().float()).to(torch.bfloat16)
+    kc_ref, vc_ref = kc.cpu().clone(), vc.cpu().clone()
+    ref.qk_norm_rope_store(x, None, None, cs.cpu(), pos.cpu(), loc.cpu(), kc_ref, vc_ref, Hq, Hkv, D, rot, 1e-6)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    ops.cross_head_norm_rope_store(qkv, qw, kw, cs, pos, loc, kc, vc, Hq, Hkv, D, rot, 1e-6, Hq * D, Hkv * D, status=status)
+    assert int(status) == 0
+    qk_cols = (Hq + Hkv) * D
+    torch.testing.assert_close(qkv.cpu().float()[:, :qk_cols], x.float()[:, :qk_cols], atol=6e-2, rtol=3e-2)
+    torch.testing.assert_close(kc.cpu().float(), kc_ref.float(), atol=6e-2, rtol=3e-2)
+    torch.testing.assert_close(vc.cpu(), vc_ref)
+    # TP form: sums of squares given from outside (here: the local ones, i.e. the same result)
+    qkv2 = (buf.clone()[:, :n] if ld_extra else _bf(T, n, seed=61))
+    sq = ops.qk_square_sums(qkv2, Hq * D, Hkv * D)
+    torch.testing.assert_close(sq[:, 0].cpu(), qkv2[:, :Hq * D].float().pow(2).sum(-1).cpu(), rtol=1e-4, atol=1e-3)
+
+
+@pytest.mark.parametrize("E,K,n_group,topk_group,bf16", [(256, 8, 8, 4, False), (128, 8, 4, 2, True), (160, 6, 5, 3, False), (8, 2, 2, 1, False)])
+def test_grouped_topk_route(E, K, n_group, topk_group, bf16):
+    T = 37
+    g = torch.Generator().manual_seed(9)
+    logits = torch.randn(T, E, generator=g)
+    if bf16:
+        logits = logits.to(torch.bfloat16)
+    bias = torch.randn(E, generator=g) * 0.1
+    idx, w = ops.grouped_topk_route(logits.to(DEV), bias.to(DEV), K, n_group, topk_group, True, 2.5)
+    ridx, rw = ref.grouped_topk_route(logits.float(), bias, K, n_group, topk_group, True, 2.5)
+    assert torch.equal(idx.cpu(), ridx)
+    torch.testing.assert_close(w.cpu(), rw, atol=1e-5, rtol=1e-4)
+
+
+def test_shared_gate_and_attention_gate_kernels():
+    T, H = 23, 1024
+    x, gw, y = _bf(T, H, seed=71), _bf(1, H, scale=0.05, seed=72), _bf(T, H, seed=73)
+    g = torch.sigmoid(torch.nn.functional.linear(x, gw).float())
+    want = (y.float() * g).to(torch.bfloat16)
+    got = ops.shared_gate_mul(x, gw, y.clone())
+    torch.testing.assert_close(got.float(), want.float(), atol=2e-2, rtol=2e-2)
+    # attention output gate read through a row stride
+    n = 512
+    merged = _bf(T, 3 * n, seed=74)
+    gate = merged[:, 2 * n:]
+    o = _bf(T, n, seed=75)
+    want = (o.float() * torch.sigmoid(gate.float())).to(torch.bfloat16)
+    got = ops.sigmoid_gate_mul(o.clone(), gate)
+    torch.testing.assert_close(got.float(), want.float(), atol=1e-2, rtol=1e-2)
