@@ -90,6 +90,56 @@ def bench_attention(a):
                                                           "q_len": a.q_len, "splits": splits})
 
 
+def bench_attention_vs_library(a):
+    """The paged decode attention kernel of this repository next to the TRT-LLM-gen decode kernel that
+    FlashInfer ships as cubins (what the reference calls: python/minisgl/attention/trtllm.py:136-178),
+    same shapes, same page table. Each launch follows a write of a buffer larger than the L2 inside one
+    CUDA graph; the time of the flush-only graph is subtracted, so both numbers are device times per
+    launch with KV read from HBM and without host launch cost."""
+    from flashinfer.decode import trtllm_batch_decode_with_kv_cache
+
+    dev = "cuda"
+    B, Hq, Hkv, D, page = a.batch, a.hq, a.hkv, a.head_dim, 16
+    pages_per = (a.ctx + page - 1) // page
+    n_pages = B * pages_per + 1
+    pt = (torch.arange(B * pages_per, dtype=torch.int32, device=dev) + 1).view(B, pages_per)
+    kc = torch.randn(n_pages * page, Hkv, D, device=dev, dtype=torch.bfloat16)
+    vc = torch.randn_like(kc)
+    q = torch.randn(B, Hq, D, device=dev, dtype=torch.bfloat16)
+    lens = torch.full((B,), a.ctx, dtype=torch.int32, device=dev)
+    scale = 1 / math.sqrt(D)
+    m_tiles = (Hq // Hkv + 15) // 16
+    splits = a.splits or ops.pick_attn_splits(B, Hkv, m_tiles, a.ctx, D)
+    ws = ops.decode_attn_workspace(B, Hq, Hkv, 1, D, splits, dev)
+    out = torch.empty_like(q)
+    lib_ws = torch.zeros(128 << 20, dtype=torch.uint8, device=dev)
+    kv4 = (kc.view(n_pages, page, Hkv, D), vc.view(n_pages, page, Hkv, D))
+    flush = L2Flusher(dev)
+
+    def own():
+        ops.decode_attention(q, kc, vc, pt, lens, Hq, Hkv, D, 1, page, scale, splits=splits, workspace=ws, out=out)
+
+    def lib():
+        return trtllm_batch_decode_with_kv_cache(query=q, kv_cache=kv4, workspace_buffer=lib_ws, block_tables=pt, seq_lens=lens,
+                                                 max_seq_len=a.ctx, bmm1_scale=scale, bmm2_scale=1.0, kv_layout="NHD",
+                                                 out_dtype=q.dtype, q_len_per_req=1)
+
+    own()
+    got_lib = lib()
+    torch.cuda.synchronize()
+    diff = (out.float() - got_lib.float().view_as(out)).abs().max().item()
+    n = 10
+    t_flush = time_graph(lambda: [flush() for _ in range(n)], n)
+    t_own = time_graph(lambda: [(flush(), own()) for _ in range(n)], n) - t_flush
+    t_lib = time_graph(lambda: [(flush(), lib()) for _ in range(n)], n) - t_flush
+    hbm, _, how = measured_peaks()
+    kv_bytes = 2 * B * a.ctx * Hkv * D * 2
+    print(json.dumps({"kernel": "decode_attention_vs_trtllm_gen", "B": B, "ctx": a.ctx, "Hq": Hq, "Hkv": Hkv, "D": D,
+                      "splits_own": splits, "us_own": round(t_own, 2), "us_trtllm_gen": round(t_lib, 2),
+                      f"own_frac_of_{how}_hbm": round(kv_bytes / t_own / 1e3 / hbm, 3),
+                      f"trtllm_frac_of_{how}_hbm": round(kv_bytes / t_lib / 1e3 / hbm, 3), "max_abs_diff": round(diff, 4)}))
+
+
 def bench_gemm(a):
     dev = "cuda"
     E, N, K, bt = a.experts, a.n, a.k, a.block_tok
@@ -193,6 +243,56 @@ def bench_route(a):
     report("ag_route_dispatch", med, mn, T * H * 2 * 4 + E * H * 2, extra={"T": T, "E": E, "H": H, "K": K})
 
 
+def bench_moe_layer(a):
+    """One colocated MoE layer as the decode graph runs it - fused route + dispatch, expert-side
+    schedule (or group + gather), the two grouped GEMMs, combine - captured `--reps` times into one
+    CUDA graph and timed per layer; `front_us` times the part in front of the GEMMs alone. With
+    --direct the rows go straight into per-expert pool stripes."""
+    from ..moe.afd_moe import AgMoeEndpoint, EgMoeEndpoint, MoeCommConfig, ag_layout, eg_layout
+    from ..parallel.fabric import Fabric
+
+    dev = torch.device("cuda:0")
+    T, E, H, K, I = a.tokens, a.experts, a.hidden, a.topk, a.intermediate
+    cfg = MoeCommConfig(num_ag=1, num_eg=1, num_lanes=1, max_tokens=T, hidden=H, topk=K, num_experts=E, intermediate=I,
+                        block_tok=a.block_tok, direct_tokens=T if a.direct else 0)
+    fabs = Fabric.local([ag_layout(cfg).size, eg_layout(cfg).size], dev)
+    ag = AgMoeEndpoint(cfg, fabs[0], 0, [1], dev, int(2e9))
+    eg = EgMoeEndpoint(cfg, fabs[1], 0, [0], dev, int(2e9), status=ag.status)
+    ag.route_tokens_per_cta, ag.route_cluster = a.tpc, a.cluster
+    w13 = ops.interleave_gate_up((torch.randn(E, 2 * I, H, device=dev, dtype=torch.bfloat16) * 0.02))
+    w2 = torch.randn(E, H, I, device=dev, dtype=torch.bfloat16) * 0.02
+    attn_out = torch.randn(T, H, device=dev, dtype=torch.bfloat16) * 0.1
+    residual = torch.randn(T, H, device=dev, dtype=torch.bfloat16)
+    res0 = residual.clone()
+    norm_w = torch.ones(H, device=dev, dtype=torch.bfloat16)
+    gate = torch.randn(E, H, device=dev, dtype=torch.bfloat16) * 0.1
+    x_out, normed = torch.empty_like(attn_out), torch.empty_like(attn_out)
+    idx = torch.empty(T, K, dtype=torch.int32, device=dev)
+    w = torch.empty(T, K, dtype=torch.float32, device=dev)
+
+    def layer(full=True):
+        ag.route_dispatch(0, attn_out, residual, norm_w, gate, None, x_out, idx, w, scoring="softmax", renorm=True, eps=1e-6)
+        if full:
+            eg.run_layer(0, T, w13, w2)
+            ag.combine_reduce(0, w, idx, T, residual=residual, norm_w=norm_w, normed=normed)
+        elif a.direct:
+            eg._schedule(0)
+        else:
+            eg.group_gather(0, T)
+
+    reps = a.reps
+    full_us = time_graph(lambda: [layer(True) for _ in range(reps)], reps)
+    residual.copy_(res0)
+    # the front part alone leaves the M2N epochs untouched, so a full layer must not follow it
+    front_us = time_graph(lambda: [layer(False) for _ in range(reps)], reps)
+    torch.cuda.synchronize()
+    hbm, _, how = measured_peaks()
+    wbytes = E * 3 * I * H * 2
+    print(json.dumps({"kernel": "moe_layer_colocated", "direct": bool(a.direct), "tpc": a.tpc, "cluster": a.cluster, "T": T,
+                      "E": E, "H": H, "I": I, "layer_us": round(full_us, 2), "front_us": round(front_us, 2),
+                      "weight_stream_us_at_copy_bw": round(wbytes / hbm / 1e3, 2), "status": int(ag.status)}))
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     sub = ap.add_subparsers(dest="case", required=True)
@@ -203,6 +303,13 @@ def main(argv=None):
     p.add_argument("--hkv", type=int, default=4)
     p.add_argument("--head-dim", type=int, default=128)
     p.add_argument("--q-len", type=int, default=1)
+    p.add_argument("--splits", type=int, default=0)
+    p = sub.add_parser("attention-vs-library")
+    p.add_argument("--batch", type=int, default=32)
+    p.add_argument("--ctx", type=int, default=1040)
+    p.add_argument("--hq", type=int, default=32)
+    p.add_argument("--hkv", type=int, default=4)
+    p.add_argument("--head-dim", type=int, default=128)
     p.add_argument("--splits", type=int, default=0)
     p = sub.add_parser("gemm")
     p.add_argument("--experts", type=int, default=32)
@@ -222,8 +329,20 @@ def main(argv=None):
     p.add_argument("--hidden", type=int, default=2048)
     p.add_argument("--topk", type=int, default=8)
     p.add_argument("--num-eg", type=int, default=4)
+    p = sub.add_parser("moe-layer")
+    p.add_argument("--tokens", type=int, default=64)
+    p.add_argument("--experts", type=int, default=128)
+    p.add_argument("--hidden", type=int, default=2048)
+    p.add_argument("--intermediate", type=int, default=768)
+    p.add_argument("--topk", type=int, default=8)
+    p.add_argument("--block-tok", type=int, default=16)
+    p.add_argument("--direct", type=int, default=1)
+    p.add_argument("--tpc", type=int, default=0)
+    p.add_argument("--cluster", type=int, default=0)
+    p.add_argument("--reps", type=int, default=20)
     a = ap.parse_args(argv)
-    {"attention": bench_attention, "gemm": bench_gemm, "route": bench_route, "dense": bench_dense}[a.case](a)
+    {"attention": bench_attention, "gemm": bench_gemm, "route": bench_route, "dense": bench_dense,
+     "moe-layer": bench_moe_layer, "attention-vs-library": bench_attention_vs_library}[a.case](a)
 
 
 if __name__ == "__main__":

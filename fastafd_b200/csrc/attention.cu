@@ -115,6 +115,8 @@ __global__ void __launch_bounds__(128, AttnCfg<D>::CTAS_PER_SM) decode_attn_kern
   const int b = blockIdx.z;
   const int G = a.Hq / a.Hkv;
   const int M = G * a.q_len;                   // valid query rows of this (b, kvh)
+  pdl_trigger();
+  pdl_wait();
   int kv_len = a.seq_lens[b];
   if (kv_len < 0) kv_len = 0;
   if (kv_len > a.max_pages * a.page_size) {
@@ -508,8 +510,8 @@ static int launch_decode_nq(const DecodeAttnArgs& a, cudaStream_t st) {
     set = true;
   }
   dim3 grid(a.splits, a.Hkv * a.m_tiles, a.B);
-  kern<<<grid, 128, Cfg::SMEM, st>>>(a);
-  AFD_CHECK_LAUNCH();
+  cudaError_t le = launch_pdl(kern, grid, dim3(128), Cfg::SMEM, st, 1, a);
+  if (le != cudaSuccess) return static_cast<int>(le);
   return 0;
 }
 

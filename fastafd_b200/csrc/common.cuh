@@ -273,6 +273,17 @@ __device__ __forceinline__ void trace_stamp(unsigned long long* trace, uint32_t 
   if (trace != nullptr) trace[(epoch % kTraceLen) * 4 + event] = globaltimer_ns();
 }
 
+// ---- programmatic dependent launch ---------------------------------------------------
+// A kernel launched with the programmatic-serialization attribute may start while its predecessor
+// in the stream is still running. pdl_trigger() (early in the predecessor) allows that start once
+// every CTA of the predecessor has issued it; pdl_wait() (in the successor, after a prologue that
+// touches no global data) blocks until the predecessor has finished and its writes are visible.
+// Every kernel that can be launched with the attribute calls pdl_wait() on all paths, so that
+// "my predecessor has finished" carries through a chain of such kernels. Both are no-ops in a
+// kernel launched without the attribute.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 // ---- math ----------------------------------------------------------------------------
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
@@ -286,6 +297,47 @@ __device__ __forceinline__ float warp_max(float v) {
 }
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
 
+}  // namespace afd
+
+// Host side: whether launches of the PDL-aware kernels carry the programmatic-serialization
+// attribute (FASTAFD_PDL=0 switches it off), and one launch helper for them.
+#include <cstdlib>
+namespace afd {
+inline bool pdl_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = std::getenv("FASTAFD_PDL");
+    v = (e != nullptr && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              unsigned int cluster_x, Args&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  unsigned int n = 0;
+  if (pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  if (cluster_x > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster_x;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
 }  // namespace afd
 
 // Host-side error helper for launchers: returns the CUDA error code as int.

@@ -95,6 +95,8 @@ __global__ void qk_norm_rope_store_kernel(__nv_bfloat16* qkv, long ld, const __n
   const int heads = Hq + 2 * Hkv;
   const long gw = (static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
+  pdl_trigger();
+  pdl_wait();
   if (gw >= static_cast<long>(T) * heads) return;
   const int tok = gw / heads, head = gw % heads;
   __nv_bfloat16* p = qkv + static_cast<size_t>(tok) * ld + static_cast<size_t>(head) * D;   // rows `ld` elements apart
@@ -442,8 +444,9 @@ extern "C" int afd_qk_norm_rope_store(void* qkv, long ld, const void* qw, const 
   const long warps = static_cast<long>(T) * (Hq + 2 * Hkv);
   const int threads = 256;
   const int blocks = static_cast<int>((warps * 32 + threads - 1) / threads);
+  cudaError_t le = cudaSuccess;
 #define LAUNCH_QK(DD)                                                                                   \
-  qk_norm_rope_store_kernel<DD><<<blocks, threads, 0, st>>>(                                            \
+  le = launch_pdl(qk_norm_rope_store_kernel<DD>, dim3(blocks), dim3(threads), 0, st, 1,                 \
       static_cast<__nv_bfloat16*>(qkv), ld, static_cast<const __nv_bfloat16*>(qw),                      \
       static_cast<const __nv_bfloat16*>(kw), static_cast<const float*>(cos_sin),                        \
       static_cast<const int*>(positions), static_cast<const int*>(out_loc),                             \
@@ -454,7 +457,7 @@ extern "C" int afd_qk_norm_rope_store(void* qkv, long ld, const void* qw, const 
   else if (D == 64) LAUNCH_QK(64);
   else return -2;
 #undef LAUNCH_QK
-  AFD_CHECK_LAUNCH();
+  if (le != cudaSuccess) return static_cast<int>(le);
   return 0;
 }
 

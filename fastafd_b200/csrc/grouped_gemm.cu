@@ -68,6 +68,14 @@ struct GroupedGemmArgs {
   unsigned int* done_counter;  // device word for the last-CTA election (COMBINE), starts 0
   int* status;
   unsigned long long* trace;   // optional timeline ring (COMBINE: event 3 = flags released)
+  // STORE only: split-K. Each work unit covers k_blocks / k_splits of the K blocks and writes an fp32
+  // partial tile; the unit that arrives last at the tile's counter sums the partials and stores the
+  // tile. Decode-sized dense projections have too few (token tile, weight tile) pairs to fill the GPU
+  // otherwise. Counters are zero between launches (the last arriver resets its counter).
+  int k_splits;
+  float* splitk_ws;            // [tok_tiles * n_tiles][k_splits][BLOCK_TOK][128]
+  unsigned int* splitk_cnt;    // [tok_tiles * n_tiles]
+  const __nv_bfloat16* bias;   // STORE only: optional [n_per_expert], added to every row
 };
 
 template <int BLOCK_TOK, bool FP8>
@@ -110,6 +118,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
+  pdl_trigger();       // the next kernel may set itself up while this one streams the weights
   if (threadIdx.x == 0) {
     for (int s = 0; s < Cfg::kStages; ++s) {
       mbar_init(&full_bar[s], 1);
@@ -133,6 +142,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
+  pdl_wait();          // barriers, TMEM and descriptors are ready; now the predecessor's outputs may be read
   int num_tok_tiles = *args.num_tok_tiles;
   if (num_tok_tiles > args.max_tok_tiles) {
     if (threadIdx.x == 0) set_status(args.status, kStatusCapacity);
@@ -142,8 +152,10 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
   // it can compute the 1x128 activation scale; the work unit is then a tile pair.
   constexpr int kTilesPerUnit = (FP8 && EPI == EPI_SWIGLU) ? 2 : 1;
   const int n_units = args.n_tiles / kTilesPerUnit;
-  const int total_units = num_tok_tiles * n_units;
+  const int ks_n = (EPI == EPI_STORE && args.k_splits > 1) ? args.k_splits : 1;
+  const int total_units = num_tok_tiles * n_units * ks_n;
   const int k_blocks = args.k_blocks;
+  const int kb_per = k_blocks / ks_n;       // K blocks of one unit (whole K unless split)
 
   if (warp == 0) {
     // ---------------- TMA producer ----------------
@@ -152,13 +164,14 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
       uint32_t phase = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
-        const int tok_tile = u / n_units;
-        const int unit = u - tok_tile * n_units;
+        const int ks = u % ks_n, uu = u / ks_n;
+        const int tok_tile = uu / n_units;
+        const int unit = uu - tok_tile * n_units;
         const int4 ti = args.tile_info[tok_tile];
         for (int sub = 0; sub < kTilesPerUnit && ok; ++sub) {
           const int n_tile = unit * kTilesPerUnit + sub;
           const int w_row = ti.x * args.n_per_expert + n_tile * 128;
-          for (int kb = 0; kb < k_blocks; ++kb) {
+          for (int kb = ks * kb_per; kb < (ks + 1) * kb_per; ++kb) {
             if (!mbar_wait(&empty_bar[stage], phase ^ 1u, abort_flag, args.status)) {
               ok = false;
               break;
@@ -192,7 +205,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
             if (!mbar_wait(&tempty_bar[as], aphase ^ 1u, abort_flag, args.status)) { ok = false; break; }
             tc_fence_after();
           }
-          for (int kb = 0; kb < k_blocks; ++kb) {
+          for (int kb = 0; kb < kb_per; ++kb) {      // relative index: only "first block of the unit" matters here
             if (FP8) {
               if (!mbar_wait(&tempty_bar[as], aphase ^ 1u, abort_flag, args.status)) { ok = false; break; }
               tc_fence_after();
@@ -237,12 +250,14 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
     __nv_bfloat16* stile = reinterpret_cast<__nv_bfloat16*>(epi_smem);   // [BLOCK_TOK][136]
     float* hbuf = reinterpret_cast<float*>(epi_smem + BLOCK_TOK * 136 * 2);  // fp8: [BLOCK_TOK][64]
     constexpr int kSL = 136;
+    volatile int* s_flag = abort_flag + 1;     // split-K: "this unit arrived last" (epilogue warps only)
     int as = 0;
     uint32_t aphase = 0;
     bool ok = true;
     for (int u = blockIdx.x; u < total_units && ok; u += gridDim.x) {
-      const int tok_tile = u / n_units;
-      const int unit = u - tok_tile * n_units;
+      const int ks = u % ks_n, uu = u / ks_n;
+      const int tok_tile = uu / n_units;
+      const int unit = uu - tok_tile * n_units;
       const int4 ti = args.tile_info[tok_tile];
       int valid = ti.z;
       if (valid > BLOCK_TOK) valid = BLOCK_TOK;
@@ -260,7 +275,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
           for (int c = 0; c < BLOCK_TOK; ++c) acc[c] = 0.f;
           const float* wsc = args.w_scale +
               ((static_cast<size_t>(ti.x) * args.n_tiles + n_tile) * 2 + ((lane >> 4) & 1)) * k_blocks;
-          for (int kb = 0; kb < k_blocks; ++kb) {
+          for (int kb = ks * kb_per; kb < (ks + 1) * kb_per; ++kb) {
             if (!mbar_wait(&tfull_bar[as], aphase, abort_flag, args.status)) { ok = false; break; }
             tc_fence_after();
             const float ws = __ldg(wsc + kb);
@@ -377,6 +392,36 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
             }
           }
         } else {
+          if (EPI == EPI_STORE && ks_n > 1) {
+            // split-K: park this unit's fp32 partial; the last unit of the tile sums all of them
+            const int tile_id = tok_tile * args.n_tiles + n_tile;
+            float* wsp = args.splitk_ws + (static_cast<size_t>(tile_id) * ks_n + ks) * (BLOCK_TOK * 128);
+#pragma unroll
+            for (int c = 0; c < BLOCK_TOK; ++c) wsp[c * 128 + q * 32 + lane] = acc[c];
+            __threadfence();
+            epi_bar_sync();
+            if (ethread == 0) {
+              const unsigned int prev = atomicAdd(args.splitk_cnt + tile_id, 1u);
+              const int last = prev == static_cast<unsigned int>(ks_n) - 1u;
+              if (last) args.splitk_cnt[tile_id] = 0;
+              *s_flag = last;
+            }
+            epi_bar_sync();
+            if (!*s_flag) continue;
+            __threadfence();
+            const float* wst = args.splitk_ws + static_cast<size_t>(tile_id) * ks_n * (BLOCK_TOK * 128);
+#pragma unroll
+            for (int c = 0; c < BLOCK_TOK; ++c) acc[c] = 0.f;
+            for (int s = 0; s < ks_n; ++s) {
+#pragma unroll
+              for (int c = 0; c < BLOCK_TOK; ++c) acc[c] += __ldcg(wst + (static_cast<size_t>(s) * BLOCK_TOK + c) * 128 + q * 32 + lane);
+            }
+          }
+          if (EPI == EPI_STORE && args.bias != nullptr) {
+            const float bv = __bfloat162float(args.bias[n_tile * 128 + q * 32 + lane]);
+#pragma unroll
+            for (int c = 0; c < BLOCK_TOK; ++c) acc[c] += bv;
+          }
           // STORE / COMBINE: transpose through shared memory so that each warp writes
           // whole 256-byte token rows (8 bytes per lane).
           epi_bar_sync();   // previous tile's readers are done with stile
@@ -489,8 +534,8 @@ static int launch_cfg(const CUtensorMap& tw, const CUtensorMap& tx, const Groupe
     if (e != cudaSuccess) return static_cast<int>(e);
     attr_set = true;
   }
-  kern<<<grid, 192, Cfg::kSmemBytes, stream>>>(tw, tx, a);
-  AFD_CHECK_LAUNCH();
+  cudaError_t le = launch_pdl(kern, dim3(grid), dim3(192), Cfg::kSmemBytes, stream, 1, tw, tx, a);
+  if (le != cudaSuccess) return static_cast<int>(le);
   return 0;
 }
 
@@ -527,6 +572,7 @@ struct AfdGroupedGemmDesc {
   void* peer_flag[afd::kMaxPeers];
   int num_peers, combine_tokens, hidden;
   void* epoch; void* done_counter; void* status; void* trace;
+  int k_splits; void* splitk_ws; void* splitk_cnt; const void* bias;
 };
 
 extern "C" int afd_grouped_gemm(const AfdGroupedGemmDesc* d, void* stream_v) {
@@ -568,6 +614,14 @@ extern "C" int afd_grouped_gemm(const AfdGroupedGemmDesc* d, void* stream_v) {
   a.done_counter = static_cast<unsigned int*>(d->done_counter);
   a.status = static_cast<int*>(d->status);
   a.trace = static_cast<unsigned long long*>(d->trace);
+  a.k_splits = d->k_splits > 1 ? d->k_splits : 1;
+  a.splitk_ws = static_cast<float*>(d->splitk_ws);
+  a.splitk_cnt = static_cast<unsigned int*>(d->splitk_cnt);
+  a.bias = static_cast<const __nv_bfloat16*>(d->bias);
+  if (a.k_splits > 1 && (d->epilogue != EPI_STORE || a.k_blocks % a.k_splits != 0 || a.splitk_ws == nullptr ||
+                         a.splitk_cnt == nullptr))
+    return -13;
+  if (a.bias != nullptr && d->epilogue != EPI_STORE) return -14;
   const int grid = d->grid > 0 ? d->grid : 148;
   if (d->fp8) {
     switch (d->epilogue) {

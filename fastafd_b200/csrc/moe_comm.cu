@@ -814,6 +814,8 @@ __global__ void ag_combine_kernel(const CombineArgs a) {
   extern __shared__ float sbuf[];   // H floats + 32
   float* red = sbuf + a.H;
   __shared__ uint32_t s_epoch;
+  pdl_trigger();
+  pdl_wait();
   if (threadIdx.x == 0) {
     s_epoch = *a.epoch;
     if (blockIdx.x == 0) trace_stamp(a.trace, s_epoch, 1);
@@ -1098,8 +1100,9 @@ extern "C" int afd_ag_combine(const AfdCombineDesc* d, void* stream) {
   a.status = static_cast<int*>(d->status);
   a.trace = static_cast<unsigned long long*>(d->trace);
   const int threads = d->H / 8 >= 512 ? 512 : 256;
-  ag_combine_kernel<<<d->T, threads, (d->H + 32) * sizeof(float), static_cast<cudaStream_t>(stream)>>>(a);
-  AFD_CHECK_LAUNCH();
+  cudaError_t le = launch_pdl(ag_combine_kernel, dim3(d->T), dim3(threads), (d->H + 32) * sizeof(float),
+                              static_cast<cudaStream_t>(stream), 1, a);
+  if (le != cudaSuccess) return static_cast<int>(le);
   return 0;
 }
 

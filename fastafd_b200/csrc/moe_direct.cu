@@ -101,6 +101,8 @@ __global__ void __launch_bounds__(256) dispatch_direct_kernel(const DispatchDire
   const int t = blockIdx.x, H = d.H;
   __shared__ uint32_t s_dst[kMaxTopk];
   extern __shared__ __align__(16) uint8_t dsm_raw[];     // fp8: quantised row + scales
+  pdl_trigger();
+  pdl_wait();
   if (threadIdx.x < d.K) s_dst[threadIdx.x] = claim_slot(d, t, threadIdx.x, a.topk_idx[static_cast<size_t>(t) * d.K + threadIdx.x]);
   const __nv_bfloat16* xr = a.x + static_cast<size_t>(t) * H;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
@@ -199,7 +201,8 @@ __global__ void __launch_bounds__(kRouteThreads) ag_route_direct_kernel(const Ro
   __shared__ float s_w[TPC][kMaxTopk];
   __shared__ uint32_t s_dst[TPC][kMaxTopk];
 
-  // 0. pull this CTA's gate slice towards L2 while the norm runs
+  // 0. pull this CTA's gate slice towards L2 (weights: independent of the predecessor kernel)
+  pdl_trigger();
   {
     const size_t row_b = static_cast<size_t>(H) * (a.gate_fp32 ? 4 : 2);
     const char* gp = static_cast<const char*>(a.gate_w) + static_cast<size_t>(e_lo) * row_b;
@@ -211,6 +214,7 @@ __global__ void __launch_bounds__(kRouteThreads) ag_route_direct_kernel(const Ro
     }
   }
 
+  pdl_wait();
   // 1. residual add + RMSNorm of the group's rows. Every CTA of the cluster computes the rows (it
   //    needs them for its logits); CTA 0 alone writes residual and x_out, and only after all CTAs
   //    have loaded the old residual (cluster barrier between the loads and the stores).
@@ -469,6 +473,8 @@ struct ScheduleArgs {
 
 __global__ void __launch_bounds__(32) eg_schedule_kernel(const ScheduleArgs a) {
   const int lane = threadIdx.x;
+  pdl_trigger();
+  pdl_wait();
   const uint32_t e0 = *a.epoch;
   if (lane == 0) trace_stamp(a.trace, e0, 0);
   if (lane < a.A) wait_flag_ge(a.n2m_flag + lane, e0, a.timeout_ns, a.status);
@@ -556,8 +562,8 @@ extern "C" int afd_dispatch_direct(const void* x, const void* topk_idx, const Af
   a.x = static_cast<const __nv_bfloat16*>(x);
   a.topk_idx = static_cast<const int*>(topk_idx);
   const size_t smem = d->fp8 ? static_cast<size_t>(d->H) + (d->H / 128) * sizeof(float) : 0;
-  dispatch_direct_kernel<<<d->T, 256, smem, static_cast<cudaStream_t>(stream)>>>(a);
-  AFD_CHECK_LAUNCH();
+  cudaError_t le = launch_pdl(dispatch_direct_kernel, dim3(d->T), dim3(256), smem, static_cast<cudaStream_t>(stream), 1, a);
+  if (le != cudaSuccess) return static_cast<int>(le);
   return 0;
 }
 
@@ -581,19 +587,7 @@ static int launch_route_direct(const RouteDirectArgs& a, int cluster, size_t sme
     smem_set = smem;
   }
   const int groups = (a.d.T + TPC - 1) / TPC;
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(groups * cluster);
-  cfg.blockDim = dim3(kRouteThreads);
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = cluster;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, a);
+  cudaError_t e = launch_pdl(kern, dim3(groups * cluster), dim3(kRouteThreads), smem, st, static_cast<unsigned int>(cluster), a);
   if (e != cudaSuccess) return static_cast<int>(e);
   return 0;
 }
@@ -661,7 +655,7 @@ extern "C" int afd_eg_schedule(const AfdScheduleDesc* d, void* stream) {
   a.timeout_ns = d->timeout_ns;
   a.status = static_cast<int*>(d->status);
   a.trace = static_cast<unsigned long long*>(d->trace);
-  eg_schedule_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(a);
-  AFD_CHECK_LAUNCH();
+  cudaError_t le = launch_pdl(eg_schedule_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream), 1, a);
+  if (le != cudaSuccess) return static_cast<int>(le);
   return 0;
 }

@@ -63,6 +63,8 @@ struct TpWaitArgs {
 };
 
 __global__ void tp_allgather_wait_kernel(const TpWaitArgs a) {
+  pdl_trigger();
+  pdl_wait();
   const uint32_t e = *a.epoch;
   if (threadIdx.x < a.tp) wait_flag_ge(a.flags + threadIdx.x, e, a.timeout_ns, a.status);
   __syncthreads();
@@ -121,7 +123,7 @@ extern "C" int afd_wait_flags_epoch(const void* flags, int n, const void* epoch,
   if (n < 1 || n > 32) return -1;
   TpWaitArgs a{static_cast<const uint32_t*>(flags), n, const_cast<uint32_t*>(static_cast<const uint32_t*>(epoch)),
                timeout_ns, static_cast<int*>(status), 0};
-  tp_allgather_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(a);
-  AFD_CHECK_LAUNCH();
+  cudaError_t le = launch_pdl(tp_allgather_wait_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream), 1, a);
+  if (le != cudaSuccess) return static_cast<int>(le);
   return 0;
 }

@@ -25,6 +25,7 @@ Stage API parity with the reference: python/minisgl/models/qwen3_moe_afd.py:201-
 from __future__ import annotations
 
 import hashlib
+import os
 from dataclasses import dataclass
 from typing import Dict, List, Optional, Tuple
 
@@ -104,6 +105,13 @@ def _linear(x: Tensor, w: Tensor, b: Optional[Tensor] = None) -> Tensor:
     return F.linear(x, w, b)
 
 
+# Decode-sized dense projections (qkv, o_proj, GDN in/out projections, dense and shared-expert MLPs,
+# LM head) run on the tcgen05 kernel with split-K; larger token counts (prefill) are plain library
+# GEMMs. FASTAFD_OWN_DENSE=0 sends everything to the library.
+_OWN_DENSE = os.environ.get("FASTAFD_OWN_DENSE", "1") != "0"
+_OWN_DENSE_MAX_TOKENS = 128
+
+
 class AttentionStage:
     """Everything of the model that runs on an attention GPU. Tensor-parallel over `tp`
     ranks (heads split; o_proj row-parallel; vocab-parallel embedding and LM head); the
@@ -126,6 +134,8 @@ class AttentionStage:
             else:
                 self.lin_index[i] = len(self.lin_index)
         self.cos_sin: Optional[Tensor] = None
+        self.status: Optional[Tensor] = None      # device status word of the process (set by the worker)
+        self.w_fp8: Dict[str, Tuple[Tensor, Tensor]] = {}
         self.vocab_local = (cfg.vocab_size + tp_size - 1) // tp_size
         self.vocab_start = tp_rank * self.vocab_local
 
@@ -245,6 +255,36 @@ class AttentionStage:
                     if w is not None:
                         self.w[p + suffix] = torch.cat([w[:n], w[2 * n:], w[n:2 * n]], 0).contiguous()
                 self.gate_last = True
+        self._quantize_dense_weights()
+
+    def _quantize_dense_weights(self) -> None:
+        """Block-FP8 checkpoints keep their dense projections in e4m3 with 128x128 scales on the GPU
+        (half the bytes of the decode-time weight stream); the bf16 copies serve prefill-sized GEMMs."""
+        c = self.cfg
+        self.w_fp8: Dict[str, Tuple[Tensor, Tensor]] = {}
+        if not (c.quant.is_fp8 and self.device.type == "cuda" and _OWN_DENSE):
+            return
+        for name, w in self.w.items():
+            if not name.endswith(("qkv_proj.weight", "o_proj.weight", "in_proj_qkv.weight", "in_proj_z.weight",
+                                  "out_proj.weight", "gate_up_proj.weight", "down_proj.weight")):
+                continue
+            if w.dtype != torch.bfloat16 or w.shape[0] % 128 or w.shape[1] % 128 or not c.quant.applies_to(name):
+                continue
+            q, sc = ref.block_quant_fp8(w.float())
+            self.w_fp8[name] = (q.contiguous(), ops.plain_tile_scales(sc[None].float()).contiguous())
+
+    def _proj(self, x: Tensor, name: str, bias: Optional[Tensor] = None) -> Tensor:
+        """x @ w[name].T (+ bias)."""
+        w = self.w[name]
+        if (_OWN_DENSE and x.is_cuda and x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16 and x.dim() == 2
+                and 0 < x.shape[0] <= _OWN_DENSE_MAX_TOKENS and w.shape[0] % 128 == 0 and w.shape[1] % 64 == 0
+                and x.is_contiguous()):
+            q = self.w_fp8.get(name)
+            if q is not None:
+                xq, xs = ops.group_quant_fp8(x, 128)
+                return ops.dense_gemm(xq, q[0], x_scale=xs, w_scale=q[1], bias=bias, status=self.status)
+            return ops.dense_gemm(x, w, bias=bias, status=self.status)
+        return F.linear(x, w, bias)
 
     # ------------------------------------------------------------------ forward pieces
     def embed(self, ids: Tensor, scatter: bool = False) -> Tensor:
@@ -281,7 +321,7 @@ class AttentionStage:
     def _full_attention(self, layer: int, x: Tensor, meta: AttnMeta, kv: KVPool, fuse_scatter: bool = False):
         c, D = self.cfg, self.cfg.head_dim
         p = f"model.layers.{layer}.self_attn."
-        qkv = _linear(x, self.w[p + "qkv_proj.weight"], self.w.get(p + "qkv_proj.bias"))
+        qkv = self._proj(x, p + "qkv_proj.weight", self.w.get(p + "qkv_proj.bias"))
         T = x.shape[0]
         gate = None
         nqkv = (self.hq + 2 * self.hkv) * D
@@ -325,7 +365,7 @@ class AttentionStage:
                 and hasattr(self.comm, "oproj_reduce_scatter") and self.comm.can_fuse_oproj(T, o.shape[1])):
             # GEMM epilogue pushes the partial rows to their owners; returns this rank's summed rows
             return (self.comm.oproj_reduce_scatter(meta.lane, o.contiguous(), w_o),)
-        return _linear(o, w_o)
+        return self._proj(o, p + "o_proj.weight")
 
     def _prefill_attention(self, q: Tensor, kc: Tensor, vc: Tensor, meta: AttnMeta, scale: float, page_size: int) -> Tensor:
         """Causal attention of each request's new chunk against its paged KV (which already holds
@@ -371,13 +411,13 @@ class AttentionStage:
         li = self.lin_index[layer]
         hk, hv = c.gdn_num_k_heads // self.tp_size, c.gdn_num_v_heads // self.tp_size
         dk, dv = c.gdn_head_k_dim, c.gdn_head_v_dim
-        mixed = _linear(x, self.w[p + "in_proj_qkv.weight"])
-        z = _linear(x, self.w[p + "in_proj_z.weight"])
+        mixed = self._proj(x, p + "in_proj_qkv.weight")
+        z = self._proj(x, p + "in_proj_z.weight")
         b = _linear(x, self.w[p + "in_proj_b.weight"])
         a = _linear(x, self.w[p + "in_proj_a.weight"])
         out = gdn_ops.gdn_block(mixed, z, a, b, self.w[p + "conv1d.weight"], self.w[p + "A_log"], self.w[p + "dt_bias"],
                                 self.w[p + "norm.weight"], gdn.conv[li], gdn.rec[li], meta, hk, hv, dk, dv, c.rms_eps)
-        return _linear(out, self.w[p + "out_proj.weight"])
+        return self._proj(out if out.is_contiguous() else out.contiguous(), p + "out_proj.weight")
 
     def post_attn_norm(self, layer: int, attn_out: Tensor, residual: Tensor, out: Optional[Tensor] = None) -> Tensor:
         w = self.w[f"model.layers.{layer}.post_attention_layernorm.weight"]
@@ -405,11 +445,11 @@ class AttentionStage:
         c = self.cfg
         p = f"model.layers.{layer}.mlp."
         if not c.is_moe_layer(layer):
-            h = ops.silu_mul(_linear(x, self.w[p + "gate_up_proj.weight"]))
-            out = _linear(h, self.w[p + "down_proj.weight"])
+            h = ops.silu_mul(self._proj(x, p + "gate_up_proj.weight"))
+            out = self._proj(h, p + "down_proj.weight")
         elif c.num_shared_experts > 0:
-            h = ops.silu_mul(_linear(x, self.w[p + "shared_expert.gate_up_proj.weight"]))
-            out = _linear(h, self.w[p + "shared_expert.down_proj.weight"])
+            h = ops.silu_mul(self._proj(x, p + "shared_expert.gate_up_proj.weight"))
+            out = self._proj(h, p + "shared_expert.down_proj.weight")
             if c.shared_expert_gate:
                 out = ops.shared_gate_mul(x, self.w[p + "shared_expert_gate.weight"], out)
         else:
@@ -422,8 +462,7 @@ class AttentionStage:
         return ops.add_rmsnorm(x, residual, self.w["model.norm.weight"], self.cfg.rms_eps, self.cfg.norm_offset1)
 
     def lm_head(self, x: Tensor) -> Tensor:
-        w = self.w["model.embed_tokens.weight"] if self.cfg.tie_embeddings else self.w["lm_head.weight"]
-        logits = _linear(x, w)
+        logits = self._proj(x, "model.embed_tokens.weight" if self.cfg.tie_embeddings else "lm_head.weight")
         if self.tp_size > 1:
             logits = self.comm.all_gather_last_dim(logits)[:, :self.cfg.vocab_size]
         return logits

@@ -345,9 +345,8 @@ class EgMoeEndpoint:
                      trace=self.trace[lane] if self.trace else None)
 
 
-    def _run_layer_direct(self, lane: int, w13, w2, w13_scale, w2_scale) -> None:
-        """The layer when the sources stored their rows straight into the expert stripes: one warp
-        waits for the flags and turns the slot counters into the tile schedule, then the two GEMMs."""
+    def _schedule(self, lane: int) -> None:
+        """One warp: bounded wait for the sources' flags, slot counters -> tile schedule, counters reset."""
         cfg, w = self.cfg, self.lanes[lane]
         s = ScheduleDesc()
         s.n2m_flag, s.A, s.epoch, s.counts = ptr(self.n2m_flag[lane]), cfg.num_ag, ptr(w.epoch), ptr(self.dcount[lane])
@@ -357,6 +356,12 @@ class EgMoeEndpoint:
         s.timeout_ns, s.status = self.timeout_ns, ptr(self.status)
         s.trace = ptr(self.trace[lane]) if self.trace else None
         check(lib().afd_eg_schedule(C.byref(s), cur_stream()), "eg_schedule")
+
+    def _run_layer_direct(self, lane: int, w13, w2, w13_scale, w2_scale) -> None:
+        """The layer when the sources stored their rows straight into the expert stripes: one warp
+        waits for the flags and turns the slot counters into the tile schedule, then the two GEMMs."""
+        cfg, w = self.cfg, self.lanes[lane]
+        self._schedule(lane)
         ntiles = self.counters[0:1]
         DR = cfg.direct_rows
         grouped_gemm(w=w13, x=self.dpool_x[lane], num_experts=self.experts_local, n_per_expert=2 * cfg.intermediate,

@@ -316,7 +316,8 @@ def dense_tile_schedule(M: int, block_tok: int, device) -> tuple[torch.Tensor, t
 def grouped_gemm(*, w, x, num_experts, n_per_expert, k, tile_info, num_tok_tiles, block_tok,
                  epilogue, out=None, out_ld=0, fp8=False, x_scale=None, w_scale=None, out_q=None,
                  out_scale=None, row_meta=None, peer_combine=(), peer_flag=(), combine_tokens=0,
-                 hidden=0, epoch=None, done_counter=None, status=None, grid=NUM_SMS, trace=None):
+                 hidden=0, epoch=None, done_counter=None, status=None, grid=NUM_SMS, trace=None,
+                 k_splits=1, splitk_ws=None, splitk_cnt=None, bias=None):
     """Low-level launcher of the tcgen05 grouped GEMM (see csrc/grouped_gemm.cu)."""
     d = GroupedGemmDesc()
     d.w, d.x = ptr(w), ptr(x)
@@ -333,26 +334,71 @@ def grouped_gemm(*, w, x, num_experts, n_per_expert, k, tile_info, num_tok_tiles
         d.peer_flag[i] = p
     d.num_peers, d.combine_tokens, d.hidden = len(peer_combine), combine_tokens, hidden
     d.epoch, d.done_counter, d.status, d.trace = ptr(epoch), ptr(done_counter), ptr(status), ptr(trace)
+    d.k_splits, d.splitk_ws, d.splitk_cnt, d.bias = k_splits, ptr(splitk_ws), ptr(splitk_cnt), ptr(bias)
     check(lib().afd_grouped_gemm(C.byref(d), cur_stream()), "grouped_gemm")
 
 
 _DENSE_SCHEDULES: dict = {}
 
 
+_SPLITK_WS: dict = {}
+
+
+def pick_k_splits(tok_tiles: int, n_tiles: int, k_blocks: int) -> int:
+    """K splits of a dense GEMM with tok_tiles x n_tiles output tiles: enough work units to give every
+    SM one (up to about two), a split never shorter than 4 K blocks, and an exact division of K."""
+    tiles = max(1, tok_tiles * n_tiles)
+    best = 1
+    for s in range(1, 33):
+        if k_blocks % s != 0 or k_blocks // s < 4:
+            continue
+        if tiles * s <= 2 * NUM_SMS:
+            best = s
+    return best
+
+
+def _splitk_buffers(tiles: int, k_splits: int, block_tok: int, device):
+    """Workspace + zeroed arrival counters of the current stream (kernels on one stream run in order;
+    two streams must not share them). Sized once for the largest split launch there can be
+    (pick_k_splits keeps tiles x splits within two units per SM, a tile is at most 128 x 128 fp32), so
+    the addresses captured in CUDA graphs never change."""
+    key = (str(device), cur_stream())
+    if key not in _SPLITK_WS:
+        _SPLITK_WS[key] = (torch.empty(2 * NUM_SMS * 128 * 128, dtype=torch.float32, device=device),
+                           torch.zeros(2 * NUM_SMS, dtype=torch.int32, device=device))
+    ws, cnt = _SPLITK_WS[key]
+    if tiles * k_splits * block_tok * 128 > ws.numel() or tiles > cnt.numel():
+        raise ValueError("split-K launch larger than the fixed workspace; pass fewer k_splits")
+    return ws, cnt
+
+
 def dense_gemm(x: torch.Tensor, w: torch.Tensor, block_tok: Optional[int] = None, status=None,
-               out: Optional[torch.Tensor] = None):
-    """out = x @ w.T on the tcgen05 path (bf16, N % 128 == 0, K % 64 == 0). The tile schedule of a
-    shape is built once and kept on the device, so later calls can be captured into a CUDA graph."""
+               out: Optional[torch.Tensor] = None, bias: Optional[torch.Tensor] = None, k_splits: int = 0,
+               x_scale: Optional[torch.Tensor] = None, w_scale: Optional[torch.Tensor] = None):
+    """out = x @ w.T (+ bias) on the tcgen05 path, weights on the UMMA M side (N % 128 == 0).
+    bf16: x [M,K] bf16, w [N,K] bf16, K % 64 == 0. Block-FP8: x e4m3 with `x_scale` [M, K/128] (1x128
+    groups), w e4m3 with `w_scale` in the kernel's per-tile layout (ops.plain_tile_scales), K % 128 == 0.
+    With few output tiles the K dimension is split over several CTAs whose fp32 partials the last one
+    sums (`k_splits` 0 = choose). Tile schedules and split-K buffers are built once per shape / stream
+    and kept on the device, so calls can be captured into a CUDA graph."""
     M, K = x.shape
     N = w.shape[0]
+    fp8 = x.dtype == torch.float8_e4m3fn
     if block_tok is None:
-        block_tok = 16 if M <= 16 else 32 if M <= 32 else 64 if M <= 64 else 128
+        block_tok = 16 if M <= 16 else 32 if M <= 32 else 64 if (M <= 64 or fp8) else 128
     key = (M, block_tok, x.device)
     if key not in _DENSE_SCHEDULES:
         _DENSE_SCHEDULES[key] = dense_tile_schedule(M, block_tok, x.device)
     info, n = _DENSE_SCHEDULES[key]
+    tok_tiles, n_tiles, k_blocks = info.shape[0], N // 128, K // (128 if fp8 else 64)
+    if k_splits <= 0:
+        k_splits = pick_k_splits(tok_tiles, n_tiles, k_blocks)
+    ws = cnt = None
+    if k_splits > 1:
+        ws, cnt = _splitk_buffers(tok_tiles * n_tiles, k_splits, block_tok, x.device)
     if out is None:
         out = torch.empty(M, N, dtype=torch.bfloat16, device=x.device)
     grouped_gemm(w=w, x=x, num_experts=1, n_per_expert=N, k=K, tile_info=info, num_tok_tiles=n,
-                 block_tok=block_tok, epilogue=EPI_STORE, out=out, out_ld=N, status=status)
+                 block_tok=block_tok, epilogue=EPI_STORE, out=out, out_ld=N, status=status, fp8=fp8,
+                 x_scale=x_scale, w_scale=w_scale, k_splits=k_splits, splitk_ws=ws, splitk_cnt=cnt, bias=bias)
     return out

@@ -29,6 +29,7 @@ class GroupedGemmDesc(C.Structure):
         ("peer_combine", VP * MAX_PEERS), ("peer_flag", VP * MAX_PEERS),
         ("num_peers", C.c_int), ("combine_tokens", C.c_int), ("hidden", C.c_int),
         ("epoch", VP), ("done_counter", VP), ("status", VP), ("trace", VP),
+        ("k_splits", C.c_int), ("splitk_ws", VP), ("splitk_cnt", VP), ("bias", VP),
     ]
 
 

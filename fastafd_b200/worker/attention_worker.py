@@ -124,6 +124,7 @@ class AttentionWorker:
         self.page_table_all = torch.zeros(self.max_running + 1, self.max_pages, dtype=torch.int32, device=self.device)
         self.page_table_host = np.zeros((self.max_running + 1, self.max_pages), np.int32)
         self.status = status if status is not None else torch.zeros(1, dtype=torch.int32, device=self.device)
+        self.model.status = self.status if self.cuda else None
         self.cap = max_bucket or max(rt.cuda_graph_max_bs, 1)
         self.bufs = [self._make_bufs(self.cap) for _ in range(self.num_mb)]
         self.graphs: Dict[int, "torch.cuda.CUDAGraph"] = {}

@@ -137,6 +137,36 @@ def test_dense_gemm_tcgen05(M, N, K, bt):
     torch.testing.assert_close(out.float(), exp, atol=3e-2, rtol=2e-2)
 
 
+@pytest.mark.parametrize("M,N,K,splits,with_bias", [(64, 5120, 2048, 0, False), (64, 2048, 4096, 8, False), (32, 1024, 2048, 4, True),
+                                                     (7, 256, 512, 2, True), (128, 2048, 2048, 0, False), (64, 1280, 2048, 0, True)])
+def test_dense_gemm_split_k_and_bias(M, N, K, splits, with_bias):
+    """Split-K: several CTAs share one output tile, the last one to arrive sums the fp32 partials.
+    Three calls in a row on the same buffers (the counters must come back to zero)."""
+    x, w = _bf(M, K, seed=24), _bf(N, K, scale=0.05, seed=25)
+    bias = _bf(N, seed=26) if with_bias else None
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    exp = x.float() @ w.float().t() + (bias.float() if with_bias else 0)
+    for _ in range(3):
+        out = ops.dense_gemm(x, w, status=status, bias=bias, k_splits=splits)
+        torch.cuda.synchronize()
+        assert int(status) == 0
+        torch.testing.assert_close(out.float(), exp, atol=4e-2, rtol=2e-2)
+
+
+def test_dense_gemm_block_fp8_split_k():
+    """Block-FP8 dense projection: e4m3 weights with 128x128 scales, 1x128 activation scales, split-K."""
+    M, N, K = 48, 1536, 4096
+    x, w = _bf(M, K, seed=27), _bf(N, K, scale=0.05, seed=28)
+    wq, wsc = ref.block_quant_fp8(w.cpu().float())
+    xq, xs = ops.group_quant_fp8(x, 128)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    out = ops.dense_gemm(xq, wq.to(DEV), status=status, x_scale=xs, w_scale=ops.plain_tile_scales(wsc[None].float()).to(DEV))
+    torch.cuda.synchronize()
+    assert int(status) == 0
+    exp = ref.fp8_gemm_nt(xq.cpu(), xs.cpu(), wq, wsc, torch.float32)
+    torch.testing.assert_close(out.cpu().float(), exp, atol=6e-2, rtol=3e-2)
+
+
 def _tile_schedule(counts, bt):
     info, row = [], 0
     for e, c in enumerate(counts):
