@@ -165,15 +165,27 @@ def bench_gemm(a):
                                       fp8=True, x_scale=xs, w_scale=ws, status=status)
         wbytes = E * N * K
     else:
+        if a.tile_major:
+            ref_out = torch.empty_like(out)
+            ops.grouped_gemm(w=w, x=x, num_experts=E, n_per_expert=N, k=K, tile_info=info_t, num_tok_tiles=ntile,
+                             block_tok=bt, epilogue=epi, out=ref_out, out_ld=out.shape[1], status=status)
+            w = ops.tile_major(w)
         fn = lambda: ops.grouped_gemm(w=w, x=x, num_experts=E, n_per_expert=N, k=K, tile_info=info_t,  # noqa: E731
                                       num_tok_tiles=ntile, block_tok=bt, epilogue=epi, out=out,
-                                      out_ld=out.shape[1], status=status)
+                                      out_ld=out.shape[1], status=status, w_tile_major=bool(a.tile_major))
         wbytes = E * N * K * 2
     med, mn = time_kernel(fn, flush=L2Flusher(dev))
+    graph_us = time_graph(lambda: [fn() for _ in range(4)], 4)       # back to back, 1.2 GB of weights each: no L2 reuse
     assert int(status) == 0
+    extra = {"E": E, "N": N, "K": K, "rows": row, "block_tok": bt, "tile_major": bool(a.tile_major),
+             "us_in_graph": round(graph_us, 2), "GB_s_in_graph": round(wbytes / graph_us / 1e3, 1)}
+    if a.tile_major and not a.fp8:
+        valid = torch.zeros(row, dtype=torch.bool, device=dev)
+        for e_, r0, n_, _ in info:
+            valid[r0:r0 + n_] = True
+        extra["max_abs_diff_vs_row_major"] = round((out[valid].float() - ref_out[valid].float()).abs().max().item(), 5)
     report("grouped_gemm" + ("_swiglu" if a.swiglu else "") + ("_fp8" if a.fp8 else ""), med, mn,
-           wbytes + x.numel() * x.element_size(), flops=2.0 * row * N * K,
-           extra={"E": E, "N": N, "K": K, "rows": row, "block_tok": bt})
+           wbytes + x.numel() * x.element_size(), flops=2.0 * row * N * K, extra=extra)
 
 
 def time_graph(launch_all, n_launches: int, reps: int = 5) -> float:
@@ -210,14 +222,20 @@ def bench_dense(a):
     got = ops.dense_gemm(x, ws[0])
     torch.cuda.synchronize()
     err = (got.float() - ref_out.float()).abs().max().item()
-    own = time_graph(lambda: [ops.dense_gemm(x, w) for w in ws], copies)
     lib_t = time_graph(lambda: [torch.nn.functional.linear(x, w) for w in ws], copies)
     hbm, _, how = measured_peaks()
     wbytes = N * K * 2
-    print(json.dumps({"kernel": "dense_gemm", "M": M, "N": N, "K": K, "us_own_tcgen05": round(own, 2),
-                      "us_cublas": round(lib_t, 2), f"own_frac_of_{how}_hbm": round(wbytes / own / 1e3 / hbm, 3),
-                      f"cublas_frac_of_{how}_hbm": round(wbytes / lib_t / 1e3 / hbm, 3), "max_abs_diff": round(err, 4),
-                      "weight_copies": copies}))
+    for ksp in ([a.k_splits] if a.k_splits >= 0 else [0, 1, 2, 4, 8, 16]):
+        if ksp > 1 and (K // 64) % ksp:
+            continue
+        try:
+            own = time_graph(lambda: [ops.dense_gemm(x, w, k_splits=ksp) for w in ws], copies)
+        except ValueError:
+            continue
+        print(json.dumps({"kernel": "dense_gemm", "M": M, "N": N, "K": K, "k_splits": ksp, "us_own_tcgen05": round(own, 2),
+                          "us_cublas": round(lib_t, 2), f"own_frac_of_{how}_hbm": round(wbytes / own / 1e3 / hbm, 3),
+                          f"cublas_frac_of_{how}_hbm": round(wbytes / lib_t / 1e3 / hbm, 3), "max_abs_diff": round(err, 4),
+                          "weight_copies": copies}))
 
 
 def bench_route(a):
@@ -319,10 +337,12 @@ def main(argv=None):
     p.add_argument("--block-tok", type=int, default=16)
     p.add_argument("--swiglu", action="store_true")
     p.add_argument("--fp8", action="store_true")
+    p.add_argument("--tile-major", type=int, default=0)
     p = sub.add_parser("dense")
     p.add_argument("--tokens", type=int, default=32)
     p.add_argument("--n", type=int, default=5120)
     p.add_argument("--k", type=int, default=2048)
+    p.add_argument("--k-splits", type=int, default=-1, help="-1: sweep; 0: the heuristic")
     p = sub.add_parser("route")
     p.add_argument("--tokens", type=int, default=32)
     p.add_argument("--experts", type=int, default=128)

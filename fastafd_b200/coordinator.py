@@ -81,10 +81,17 @@ class AfdCoordinator:
         self.lanes = [LaneScheduler(l, num_pages=num_pages, page_size=rt.page_size, max_running=rt.max_running_requests,
                                     max_seq_len=rt.max_seq_len or cfg.max_position, num_mb=rt.num_mb,
                                     max_batched_tokens=rt.max_batched_tokens, max_comm_tokens=max_comm_tokens,
-                                    cache_type=rt.cache_type, eos_token_ids=cfg.eos_token_ids, spec_block=rt.spec_block)
+                                    cache_type=rt.cache_type, eos_token_ids=cfg.eos_token_ids, spec_block=rt.spec_block,
+                                    spec_pending=2)
                       for l in range(self.num_lanes)]
-        # verify steps need the accepted lengths of the previous step: no planning ahead under speculation
-        self.pending = 1 if (rt.disable_overlap or rt.spec_block > 1) else max(1, rt.async_pending_steps)
+        # Under speculation the committed lengths live on the attention GPUs, so verify steps are planned
+        # ahead too (two in flight: the lane scheduler reserves KV for the unknown acceptance).
+        if rt.disable_overlap:
+            self.pending = 1
+        elif rt.spec_block > 1:
+            self.pending = min(2, max(1, rt.async_pending_steps))
+        else:
+            self.pending = max(1, rt.async_pending_steps)
         self.inflight: Deque[_Inflight] = deque()
         self.step_id = 0
         self.uid_lane: Dict[int, int] = {}

@@ -59,6 +59,9 @@ struct DecodeAttnArgs {
   float* part_lse;               // [B][Hkv][m_tiles][splits][16]
   unsigned int* part_count;      // [B][Hkv][m_tiles] arrival counters (zero between launches)
   int B, Hq, Hkv, q_len, page_size, page_shift, max_pages, splits, m_tiles;
+  // Var-len mode (prefill chunks of several requests in one launch): request b owns the query rows
+  // [q_starts[b], q_starts[b + 1]) of `q` / `out`; q_len is then the longest chunk (it sizes the grid).
+  const int* q_starts;
   long cache_slots;
   float scale_log2;              // softmax scale * log2(e)
   int* status;
@@ -114,9 +117,16 @@ __global__ void __launch_bounds__(128, AttnCfg<D>::CTAS_PER_SM) decode_attn_kern
   const int kvh = blockIdx.y / a.m_tiles, mt = blockIdx.y % a.m_tiles;
   const int b = blockIdx.z;
   const int G = a.Hq / a.Hkv;
-  const int M = G * a.q_len;                   // valid query rows of this (b, kvh)
   pdl_trigger();
   pdl_wait();
+  int q_len = a.q_len;
+  size_t q_base = static_cast<size_t>(b) * a.q_len;
+  if (a.q_starts != nullptr) {
+    q_base = static_cast<size_t>(a.q_starts[b]);
+    q_len = a.q_starts[b + 1] - a.q_starts[b];
+  }
+  const int M = G * q_len;                     // valid query rows of this (b, kvh)
+  if (mt * ROWS >= M) return;                  // var-len: a row tile past this request's rows (all its splits leave)
   int kv_len = a.seq_lens[b];
   if (kv_len < 0) kv_len = 0;
   if (kv_len > a.max_pages * a.page_size) {
@@ -131,15 +141,15 @@ __global__ void __launch_bounds__(128, AttnCfg<D>::CTAS_PER_SM) decode_attn_kern
     uint4 v = make_uint4(0, 0, 0, 0);
     if (row < M && r < ROWS) {
       const int j = row / G, g = row % G;
-      v = *reinterpret_cast<const uint4*>(a.q + (static_cast<size_t>(b) * a.q_len + j) * a.q_stride + (kvh * G + g) * D + c * 8);
+      v = *reinterpret_cast<const uint4*>(a.q + (q_base + j) * a.q_stride + (kvh * G + g) * D + c * 8);
     }
     *reinterpret_cast<uint4*>(sq + tile_off<D>(r, c)) = v;
   }
   __syncthreads();
 
   // ---- this CTA's KV range: only what the rows of this tile may see (causal) ----
-  const int j_max = min((mt * ROWS + ROWS - 1) / G, a.q_len - 1);
-  const int visible = max(0, kv_len - a.q_len + 1 + j_max);
+  const int j_max = min((mt * ROWS + ROWS - 1) / G, q_len - 1);
+  const int visible = max(0, kv_len - q_len + 1 + j_max);
   const int per_split = ((visible + a.splits - 1) / a.splits + TOK * 4 - 1) / (TOK * 4) * (TOK * 4);
   const int kv_begin = split * per_split;
   const int kv_end = min(visible, kv_begin + per_split);
@@ -254,13 +264,13 @@ __global__ void __launch_bounds__(128, AttnCfg<D>::CTAS_PER_SM) decode_attn_kern
       l_run[n][c] = 0.f;
       const int row = mt * ROWS + n * 8 + (lane & 3) * 2 + c;
       const int j = row < M ? row / G : 0;
-      lim[n][c] = row < M ? kv_len - a.q_len + 1 + j : 0;
+      lim[n][c] = row < M ? kv_len - q_len + 1 + j : 0;
     }
 
   // Smallest causal limit among the valid rows of this CTA, never past kv_end. Padding rows
   // hold q = 0 and are never written, so a tile below this limit needs no masking at all.
   const int first_row = mt * ROWS;
-  const int min_lim = first_row < M ? min(kv_end, kv_len - a.q_len + 1 + first_row / G) : kv_end;
+  const int min_lim = first_row < M ? min(kv_end, kv_len - q_len + 1 + first_row / G) : kv_end;
   int stage = 0;
   for (int tile = warp; tile < n_tiles; tile += 4) {
     {
@@ -436,7 +446,7 @@ __global__ void __launch_bounds__(128, AttnCfg<D>::CTAS_PER_SM) decode_attn_kern
         uint2 o;
         o.x = pack_bf16(acc.x, acc.y);
         o.y = pack_bf16(acc.z, acc.w);
-        *reinterpret_cast<uint2*>(a.out + ((static_cast<size_t>(b) * a.q_len + j) * a.Hq + kvh * G + g) * D + d) = o;
+        *reinterpret_cast<uint2*>(a.out + ((q_base + j) * a.Hq + kvh * G + g) * D + d) = o;
       }
     } else {
       const size_t pidx = tile_id * a.splits + split;
@@ -495,7 +505,7 @@ __global__ void __launch_bounds__(128, AttnCfg<D>::CTAS_PER_SM) decode_attn_kern
     uint2 o;
     o.x = pack_bf16(acc.x, acc.y);
     o.y = pack_bf16(acc.z, acc.w);
-    *reinterpret_cast<uint2*>(a.out + ((static_cast<size_t>(b) * a.q_len + j) * a.Hq + kvh * G + g) * D + d) = o;
+    *reinterpret_cast<uint2*>(a.out + ((q_base + j) * a.Hq + kvh * G + g) * D + d) = o;
   }
 }
 
@@ -556,6 +566,11 @@ extern "C" int afd_decode_attention(const void* q, const void* k_cache, const vo
                                       sm_scale, status, stream);
 }
 
+static int launch_attention(const void* q, long q_stride, const void* k_cache, const void* v_cache,
+                            const void* page_table, const void* seq_lens, const void* q_starts, void* out,
+                            void* workspace, int B, int Hq, int Hkv, int D, int q_len, int page_size, int max_pages,
+                            long cache_slots, int splits, float sm_scale, void* status, void* stream);
+
 // Same, with q rows `q_stride` elements apart (q read in place from a merged qkv buffer).
 extern "C" int afd_decode_attention_strided(const void* q, long q_stride, const void* k_cache,
                                             const void* v_cache, const void* page_table,
@@ -563,6 +578,27 @@ extern "C" int afd_decode_attention_strided(const void* q, long q_stride, const 
                                             int Hq, int Hkv, int D, int q_len, int page_size,
                                             int max_pages, long cache_slots, int splits, float sm_scale,
                                             void* status, void* stream) {
+  return launch_attention(q, q_stride, k_cache, v_cache, page_table, seq_lens, nullptr, out, workspace, B, Hq, Hkv, D,
+                          q_len, page_size, max_pages, cache_slots, splits, sm_scale, status, stream);
+}
+
+// Causal attention of the new chunk of every request against its paged KV in ONE launch: request b
+// owns the query rows [q_starts[b], q_starts[b + 1]) (chunks of different lengths, `max_q_len` the
+// longest) and sees the first seq_lens[b] - chunk_len + 1 + j cached tokens from its j-th row.
+extern "C" int afd_prefill_attention_varlen(const void* q, long q_stride, const void* k_cache, const void* v_cache,
+                                            const void* page_table, const void* seq_lens, const void* q_starts,
+                                            void* out, int B, int Hq, int Hkv, int D, int max_q_len, int page_size,
+                                            int max_pages, long cache_slots, float sm_scale, void* status,
+                                            void* stream) {
+  if (q_starts == nullptr || max_q_len < 1) return -8;
+  return launch_attention(q, q_stride, k_cache, v_cache, page_table, seq_lens, q_starts, out, nullptr, B, Hq, Hkv, D,
+                          max_q_len, page_size, max_pages, cache_slots, 1, sm_scale, status, stream);
+}
+
+static int launch_attention(const void* q, long q_stride, const void* k_cache, const void* v_cache,
+                            const void* page_table, const void* seq_lens, const void* q_starts, void* out,
+                            void* workspace, int B, int Hq, int Hkv, int D, int q_len, int page_size, int max_pages,
+                            long cache_slots, int splits, float sm_scale, void* status, void* stream) {
   using namespace afd;
   if (B == 0) return 0;
   if (Hq % Hkv != 0 || splits < 1 || splits > afd::kMaxSplits || page_size < 1) return -1;
@@ -575,6 +611,7 @@ extern "C" int afd_decode_attention_strided(const void* q, long q_stride, const 
   a.v_cache = static_cast<const __nv_bfloat16*>(v_cache);
   a.page_table = static_cast<const int*>(page_table);
   a.seq_lens = static_cast<const int*>(seq_lens);
+  a.q_starts = static_cast<const int*>(q_starts);
   a.out = static_cast<__nv_bfloat16*>(out);
   a.B = B; a.Hq = Hq; a.Hkv = Hkv; a.q_len = q_len; a.page_size = page_size; a.max_pages = max_pages;
   a.splits = splits;
@@ -583,6 +620,7 @@ extern "C" int afd_decode_attention_strided(const void* q, long q_stride, const 
   a.scale_log2 = sm_scale * 1.4426950408889634f;
   a.status = static_cast<int*>(status);
   const long tiles = static_cast<long>(B) * Hkv * a.m_tiles * splits;
+  if (static_cast<long>(Hkv) * a.m_tiles > 65535 || B > 65535) return -9;      // grid y / z limits
   if (splits > 1 && static_cast<long>(B) * Hkv * a.m_tiles * 4 > kCounterRegionBytes) return -7;
   a.part_count = static_cast<unsigned int*>(workspace);
   a.part_o = workspace ? reinterpret_cast<float*>(static_cast<char*>(workspace) + kCounterRegionBytes) : nullptr;

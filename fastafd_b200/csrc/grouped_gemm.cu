@@ -72,6 +72,11 @@ struct GroupedGemmArgs {
   // partial tile; the unit that arrives last at the tile's counter sums the partials and stores the
   // tile. Decode-sized dense projections have too few (token tile, weight tile) pairs to fill the GPU
   // otherwise. Counters are zero between launches (the last arriver resets its counter).
+  // Weights stored tile by tile: [row tile][k block][128 rows][128 bytes], so that one TMA box
+  // (a 128 x 128-byte weight tile) is 16 KB of consecutive memory instead of 128 pieces a whole
+  // weight row apart. The tensor map is then [(tiles) * 128][128 bytes] and the box's y coordinate is
+  // (row_tile * k_blocks + kb) * 128.
+  int w_tile_major;
   int k_splits;
   float* splitk_ws;            // [tok_tiles * n_tiles][k_splits][BLOCK_TOK][128]
   unsigned int* splitk_cnt;    // [tok_tiles * n_tiles]
@@ -180,7 +185,8 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
             uint8_t* sx = sw + Cfg::kWBytes;
             mbar_expect_tx(&full_bar[stage], Cfg::kWBytes + Cfg::kXBytes);
             const int kx = kb * (FP8 ? 128 : 64);
-            tma_load_2d(sw, &tmap_w, &full_bar[stage], kx, w_row);
+            if (args.w_tile_major) tma_load_2d(sw, &tmap_w, &full_bar[stage], 0, ((w_row >> 7) * k_blocks + kb) * 128);
+            else tma_load_2d(sw, &tmap_w, &full_bar[stage], kx, w_row);
             tma_load_2d(sx, &tmap_x, &full_bar[stage], kx, ti.y);
             if (++stage == Cfg::kStages) {
               stage = 0;
@@ -573,6 +579,7 @@ struct AfdGroupedGemmDesc {
   int num_peers, combine_tokens, hidden;
   void* epoch; void* done_counter; void* status; void* trace;
   int k_splits; void* splitk_ws; void* splitk_cnt; const void* bias;
+  int w_tile_major;
 };
 
 extern "C" int afd_grouped_gemm(const AfdGroupedGemmDesc* d, void* stream_v) {
@@ -584,7 +591,9 @@ extern "C" int afd_grouped_gemm(const AfdGroupedGemmDesc* d, void* stream_v) {
   if (d->fp8 && d->epilogue == EPI_SWIGLU && (d->n_per_expert / 128) % 2 != 0) return -11;
   if (d->num_peers > kMaxPeers) return -12;
   CUtensorMap tw, tx;
-  int r = make_tmap_2d(&tw, d->w, eb, static_cast<uint64_t>(d->num_experts) * d->n_per_expert, d->k, 128);
+  int r = d->w_tile_major
+              ? make_tmap_2d(&tw, d->w, eb, static_cast<uint64_t>(d->num_experts) * d->n_per_expert * (d->k / kblk), kblk, 128)
+              : make_tmap_2d(&tw, d->w, eb, static_cast<uint64_t>(d->num_experts) * d->n_per_expert, d->k, 128);
   if (r != 0) return r;
   r = make_tmap_2d(&tx, d->x, eb, d->pool_rows, d->k, d->block_tok);
   if (r != 0) return r;
@@ -614,6 +623,7 @@ extern "C" int afd_grouped_gemm(const AfdGroupedGemmDesc* d, void* stream_v) {
   a.done_counter = static_cast<unsigned int*>(d->done_counter);
   a.status = static_cast<int*>(d->status);
   a.trace = static_cast<unsigned long long*>(d->trace);
+  a.w_tile_major = d->w_tile_major;
   a.k_splits = d->k_splits > 1 ? d->k_splits : 1;
   a.splitk_ws = static_cast<float*>(d->splitk_ws);
   a.splitk_cnt = static_cast<unsigned int*>(d->splitk_cnt);

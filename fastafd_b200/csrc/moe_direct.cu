@@ -72,11 +72,12 @@ __device__ __forceinline__ uint32_t claim_slot(const DirectArgs& d, int t, int k
 }
 
 // The last pushing CTA publishes this source's epoch on every expert GPU (data -> fence.gpu ->
-// counter -> fence.sys -> flags), then advances the epoch.
-__device__ __forceinline__ void release_flags(const DirectArgs& d, unsigned int pushing_ctas) {
+// counter -> fence.sys -> flags), then advances the epoch. Returns whether this CTA was the last.
+__device__ __forceinline__ bool release_flags(const DirectArgs& d, unsigned int pushing_ctas) {
   __threadfence();
   const unsigned int prev = atomicAdd(d.done_counter, 1u);
-  if (prev == pushing_ctas - 1) {
+  const bool last = prev == pushing_ctas - 1;
+  if (last) {
     __threadfence_system();
     const uint32_t e = *d.epoch;
     for (int g = 0; g < d.num_eg; ++g) st_relaxed_sys(d.peer_flag[g], e);
@@ -85,6 +86,7 @@ __device__ __forceinline__ void release_flags(const DirectArgs& d, unsigned int 
     *d.done_counter = 0;
     __threadfence();
   }
+  return last;
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -152,6 +154,82 @@ __global__ void __launch_bounds__(256) dispatch_direct_kernel(const DispatchDire
 }
 
 // ---------------------------------------------------------------------------------------------
+// Expert side: flags -> tile schedule. One warp.
+// ---------------------------------------------------------------------------------------------
+struct ScheduleArgs {
+  const uint32_t* n2m_flag;   // [A]
+  int A;
+  uint32_t* epoch;            // expected epoch; advanced here
+  uint32_t* counts;           // [experts_local] slot counters, reset here
+  int experts_local, cap, block_tok, max_tok_tiles;
+  int4* tile_info;            // {expert, first pool row, valid rows, 0}
+  int* counters;              // [0] tiles, [1] padded rows, [2] routed rows
+  int* expert_counts;         // optional copy of the counts (load statistics)
+  uint64_t timeout_ns;
+  int* status;
+  unsigned long long* trace;
+};
+
+// One warp turns the slot counters into the tile schedule and clears them. `wait`: first wait
+// (bounded) for every source's flag; without it the caller guarantees that all sources are done
+// (the single source's own last CTA, when attention and experts share the GPU).
+__device__ __forceinline__ void schedule_warp(const ScheduleArgs& a, int lane, bool wait) {
+  const uint32_t e0 = *a.epoch;
+  if (lane == 0) trace_stamp(a.trace, e0, 0);
+  if (wait && lane < a.A) wait_flag_ge(a.n2m_flag + lane, e0, a.timeout_ns, a.status);
+  __syncwarp();
+  __threadfence();
+  if (lane == 0) trace_stamp(a.trace, e0, 1);
+  const int per = (a.experts_local + 31) / 32;
+  const int lo = min(lane * per, a.experts_local), hi = min(lo + per, a.experts_local);
+  int tiles = 0, routed = 0;
+  for (int e = lo; e < hi; ++e) {
+    int c = static_cast<int>(__ldcg(a.counts + e));
+    if (c > a.cap) c = a.cap;             // a source that overran the stripe has set the status
+    tiles += (c + a.block_tok - 1) / a.block_tok;
+    routed += c;
+  }
+  int incl = tiles, rincl = routed;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, o);
+    const int vr = __shfl_up_sync(0xffffffffu, rincl, o);
+    if (lane >= o) {
+      incl += v;
+      rincl += vr;
+    }
+  }
+  int t = incl - tiles;
+  for (int e = lo; e < hi; ++e) {
+    int c = static_cast<int>(__ldcg(a.counts + e));
+    if (c > a.cap) c = a.cap;
+    if (a.expert_counts) a.expert_counts[e] = c;
+    a.counts[e] = 0;                      // the lane's next round starts from empty stripes
+    for (int j = 0; j * a.block_tok < c; ++j, ++t) {
+      if (t < a.max_tok_tiles) a.tile_info[t] = make_int4(e, e * a.cap + j * a.block_tok, min(a.block_tok, c - j * a.block_tok), 0);
+    }
+  }
+  if (lane == 31) {
+    int total = incl;
+    if (total > a.max_tok_tiles) {
+      set_status(a.status, kStatusCapacity);
+      total = a.max_tok_tiles;
+    }
+    a.counters[0] = total;
+    a.counters[1] = total * a.block_tok;
+    a.counters[2] = rincl;
+    trace_stamp(a.trace, e0, 2);
+    *a.epoch = e0 + 1;
+  }
+}
+
+__global__ void __launch_bounds__(32) eg_schedule_kernel(const ScheduleArgs a) {
+  pdl_trigger();
+  pdl_wait();
+  schedule_warp(a, threadIdx.x, true);
+}
+
+// ---------------------------------------------------------------------------------------------
 // Fused post-attention step with direct dispatch.
 // ---------------------------------------------------------------------------------------------
 struct RouteDirectArgs {
@@ -166,6 +244,10 @@ struct RouteDirectArgs {
   int E, gate_fp32, scoring, renorm, offset1, mma_logits;
   float eps, route_scale;
   DirectArgs d;
+  // Attention and experts on one GPU, a single source: the last pushing CTA also builds the expert
+  // side's tile schedule (one launch less in front of the grouped GEMMs).
+  int fuse_schedule;
+  ScheduleArgs sched;
 };
 
 // Dynamic shared memory, in order:
@@ -451,76 +533,11 @@ __global__ void __launch_bounds__(kRouteThreads) ag_route_direct_kernel(const Ro
     }
   }
   __syncthreads();
-  if (tid == 0) release_flags(d, static_cast<unsigned int>(ngroups));
-}
-
-// ---------------------------------------------------------------------------------------------
-// Expert side: flags -> tile schedule. One warp.
-// ---------------------------------------------------------------------------------------------
-struct ScheduleArgs {
-  const uint32_t* n2m_flag;   // [A]
-  int A;
-  uint32_t* epoch;            // expected epoch; advanced here
-  uint32_t* counts;           // [experts_local] slot counters, reset here
-  int experts_local, cap, block_tok, max_tok_tiles;
-  int4* tile_info;            // {expert, first pool row, valid rows, 0}
-  int* counters;              // [0] tiles, [1] padded rows, [2] routed rows
-  int* expert_counts;         // optional copy of the counts (load statistics)
-  uint64_t timeout_ns;
-  int* status;
-  unsigned long long* trace;
-};
-
-__global__ void __launch_bounds__(32) eg_schedule_kernel(const ScheduleArgs a) {
-  const int lane = threadIdx.x;
-  pdl_trigger();
-  pdl_wait();
-  const uint32_t e0 = *a.epoch;
-  if (lane == 0) trace_stamp(a.trace, e0, 0);
-  if (lane < a.A) wait_flag_ge(a.n2m_flag + lane, e0, a.timeout_ns, a.status);
-  __syncwarp();
-  __threadfence();
-  if (lane == 0) trace_stamp(a.trace, e0, 1);
-  const int per = (a.experts_local + 31) / 32;
-  const int lo = min(lane * per, a.experts_local), hi = min(lo + per, a.experts_local);
-  int tiles = 0, routed = 0;
-  for (int e = lo; e < hi; ++e) {
-    int c = static_cast<int>(__ldcg(a.counts + e));
-    if (c > a.cap) c = a.cap;             // a source that overran the stripe has set the status
-    tiles += (c + a.block_tok - 1) / a.block_tok;
-    routed += c;
-  }
-  int incl = tiles, rincl = routed;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int v = __shfl_up_sync(0xffffffffu, incl, o);
-    const int vr = __shfl_up_sync(0xffffffffu, rincl, o);
-    if (lane >= o) {
-      incl += v;
-      rincl += vr;
-    }
-  }
-  int t = incl - tiles;
-  for (int e = lo; e < hi; ++e) {
-    int c = static_cast<int>(__ldcg(a.counts + e));
-    if (c > a.cap) c = a.cap;
-    if (a.expert_counts) a.expert_counts[e] = c;
-    a.counts[e] = 0;                      // the lane's next round starts from empty stripes
-    for (int j = 0; j * a.block_tok < c; ++j, ++t) {
-      if (t < a.max_tok_tiles) a.tile_info[t] = make_int4(e, e * a.cap + j * a.block_tok, min(a.block_tok, c - j * a.block_tok), 0);
-    }
-  }
-  if (lane == 31) {
-    int total = incl;
-    if (total > a.max_tok_tiles) {
-      set_status(a.status, kStatusCapacity);
-      total = a.max_tok_tiles;
-    }
-    a.counters[0] = total;
-    a.counters[1] = total * a.block_tok;
-    a.counters[2] = rincl;
-    trace_stamp(a.trace, e0, 2);
-    *a.epoch = e0 + 1;
+  __shared__ int s_last;
+  if (tid == 0) s_last = release_flags(d, static_cast<unsigned int>(ngroups)) ? 1 : 0;
+  if (a.fuse_schedule) {
+    __syncthreads();
+    if (s_last && warp == 0) schedule_warp(a.sched, lane, false);
   }
 }
 
@@ -575,7 +592,29 @@ struct AfdRouteDirectDesc {
   int tokens_per_cta;      // 0 = choose; 4 or 8
   int cluster;             // 0 = choose; CTAs that share a token group's expert range (1, 2, 4, 8)
   AfdDirectDesc d;
+  int fuse_schedule;       // 1: `sched` describes the expert side of the same GPU (single source)
+  struct AfdScheduleDesc {
+    const void* n2m_flag; int A; void* epoch; void* counts;
+    int experts_local, cap, block_tok, max_tok_tiles;
+    void* tile_info; void* counters; void* expert_counts;
+    unsigned long long timeout_ns;
+    void* status; void* trace;
+  } sched;
 };
+
+static void fill_schedule(ScheduleArgs& a, const AfdRouteDirectDesc::AfdScheduleDesc* d) {
+  a.n2m_flag = static_cast<const uint32_t*>(d->n2m_flag);
+  a.A = d->A;
+  a.epoch = static_cast<uint32_t*>(d->epoch);
+  a.counts = static_cast<uint32_t*>(d->counts);
+  a.experts_local = d->experts_local; a.cap = d->cap; a.block_tok = d->block_tok; a.max_tok_tiles = d->max_tok_tiles;
+  a.tile_info = static_cast<int4*>(d->tile_info);
+  a.counters = static_cast<int*>(d->counters);
+  a.expert_counts = static_cast<int*>(d->expert_counts);
+  a.timeout_ns = d->timeout_ns;
+  a.status = static_cast<int*>(d->status);
+  a.trace = static_cast<unsigned long long*>(d->trace);
+}
 
 template <int TPC>
 static int launch_route_direct(const RouteDirectArgs& a, int cluster, size_t smem, cudaStream_t st) {
@@ -608,14 +647,21 @@ extern "C" int afd_ag_route_direct(const AfdRouteDirectDesc* r, void* stream) {
   a.topk_w_out = static_cast<float*>(r->topk_w_out);
   a.E = E; a.gate_fp32 = r->gate_fp32; a.scoring = r->scoring; a.renorm = r->renorm; a.offset1 = r->offset1;
   a.eps = r->eps; a.route_scale = r->route_scale;
-  const int tpc = r->tokens_per_cta > 0 ? r->tokens_per_cta : (r->d.T > 32 ? 8 : 4);
+  a.fuse_schedule = 0;
+  if (r->fuse_schedule) {
+    if (r->d.num_eg != 1 || r->sched.A != 1 || r->sched.cap % r->sched.block_tok != 0) return -5;
+    a.fuse_schedule = 1;
+    fill_schedule(a.sched, &r->sched);
+  }
+  // Measured on B200 (64 tokens, 128 experts, H 2048): 4 tokens per CTA with the expert range split
+  // over 4 CTAs is the fastest form (more CTAs in flight, 128 KB of gate each).
+  const int tpc = r->tokens_per_cta > 0 ? r->tokens_per_cta : 4;
   if (tpc != 4 && tpc != 8) return -3;
-  // cluster: aim at <= 256 KB of gate per CTA, experts per CTA a multiple of 16
   int cluster = r->cluster;
   if (cluster <= 0) {
     const size_t gate_bytes = static_cast<size_t>(E) * H * (r->gate_fp32 ? 4 : 2);
     cluster = 1;
-    while (cluster < 8 && gate_bytes / cluster > 256 * 1024 && E % (cluster * 2 * 16) == 0) cluster *= 2;
+    while (cluster < 8 && gate_bytes / cluster > 128 * 1024 && E % (cluster * 2 * 16) == 0) cluster *= 2;
   }
   if (cluster != 1 && cluster != 2 && cluster != 4 && cluster != 8) return -4;
   if (E % cluster != 0) return -4;
@@ -633,28 +679,12 @@ extern "C" int afd_ag_route_direct(const AfdRouteDirectDesc* r, void* stream) {
   return tpc == 8 ? launch_route_direct<8>(a, cluster, smem, st) : launch_route_direct<4>(a, cluster, smem, st);
 }
 
-struct AfdScheduleDesc {
-  const void* n2m_flag; int A; void* epoch; void* counts;
-  int experts_local, cap, block_tok, max_tok_tiles;
-  void* tile_info; void* counters; void* expert_counts;
-  unsigned long long timeout_ns;
-  void* status; void* trace;
-};
+typedef AfdRouteDirectDesc::AfdScheduleDesc AfdScheduleDesc;
 
 extern "C" int afd_eg_schedule(const AfdScheduleDesc* d, void* stream) {
   if (d->A < 1 || d->A > 32 || d->cap % d->block_tok != 0 || d->experts_local < 1) return -1;
   ScheduleArgs a{};
-  a.n2m_flag = static_cast<const uint32_t*>(d->n2m_flag);
-  a.A = d->A;
-  a.epoch = static_cast<uint32_t*>(d->epoch);
-  a.counts = static_cast<uint32_t*>(d->counts);
-  a.experts_local = d->experts_local; a.cap = d->cap; a.block_tok = d->block_tok; a.max_tok_tiles = d->max_tok_tiles;
-  a.tile_info = static_cast<int4*>(d->tile_info);
-  a.counters = static_cast<int*>(d->counters);
-  a.expert_counts = static_cast<int*>(d->expert_counts);
-  a.timeout_ns = d->timeout_ns;
-  a.status = static_cast<int*>(d->status);
-  a.trace = static_cast<unsigned long long*>(d->trace);
+  fill_schedule(a, d);
   cudaError_t le = launch_pdl(eg_schedule_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream), 1, a);
   if (le != cudaSuccess) return static_cast<int>(le);
   return 0;

@@ -160,7 +160,7 @@ class AfdEngine:
                 from .parallel.fabric import Fabric
 
                 # decode-sized steps store rows straight into the experts' pool stripes (moe/afd_moe.py)
-                direct = min(self.max_comm_tokens, max(cap // topo.attn_tp, 1))
+                direct = min(self.max_comm_tokens, max(cap * max(rt.spec_block, 1) // topo.attn_tp, 1))
                 if os.environ.get("FASTAFD_DIRECT", "1") == "0" or num_ag * direct > 1024:
                     direct = 0
                 mcfg = MoeCommConfig(num_ag=num_ag, num_eg=num_eg, num_lanes=rt.num_mb, max_tokens=self.max_comm_tokens,
@@ -284,7 +284,8 @@ class SpmdDriver:
         self.lanes = [LaneScheduler(l, num_pages=pages, page_size=rt.page_size, max_running=rt.max_running_requests,
                                     max_seq_len=rt.max_seq_len or cfg.max_position, num_mb=rt.num_mb,
                                     max_batched_tokens=rt.max_batched_tokens, max_comm_tokens=engine.max_comm_tokens,
-                                    cache_type=rt.cache_type, eos_token_ids=cfg.eos_token_ids, spec_block=rt.spec_block)
+                                    cache_type=rt.cache_type, eos_token_ids=cfg.eos_token_ids, spec_block=rt.spec_block,
+                                    spec_pending=2)
                       for l in range(self.num_lanes)]
         self.step_id = 0
         self.my_lane = None
@@ -367,12 +368,18 @@ class SpmdDriver:
         filled with N(0,1) values and each request's last token is a random id, so decode steps
         do the same work as after a real prefill of random prompts."""
         sp = SamplingParams(max_tokens=max_tokens, ignore_eos=True)
-        for lane in self.lanes:
+        my_rows = []
+        for li, lane in enumerate(self.lanes):
             for _ in range(per_lane):
                 uid = getattr(self, "_next_uid", 0)
                 self._next_uid = uid + 1
-                lane.add_prefilled(uid, prompt_len, sp)
+                req = lane.add_prefilled(uid, prompt_len, sp)
+                if li == self.my_lane:
+                    my_rows.append(req.table_idx)
         a = self.e.attn
+        if a is not None and a.spec is not None and my_rows:
+            rows = torch.tensor(my_rows, dtype=torch.int64, device=a.device)
+            a.spec.set_committed(rows, torch.full((len(my_rows),), prompt_len, dtype=torch.int32, device=a.device))
         if a is not None:
             g = torch.Generator(device=a.device).manual_seed(seed + 17 * self.e.rank)
             for t in (a.kv.k, a.kv.v):
@@ -392,6 +399,7 @@ class SpmdDriver:
         e, rt = self.e, self.e.rt
         produced = 0
         pending = None
+        q = rt.spec_block if rt.spec_block > 1 else 1       # verify steps: q tokens per request
         for _ in range(n):
             sid = self.step_id
             self.step_id += 1
@@ -402,9 +410,9 @@ class SpmdDriver:
             mine = None
             for lane, l in enumerate(self.lanes):
                 if e.attn is not None and lane == self.my_lane:
-                    mine = l.schedule_decode(sid, bucket)
+                    mine = l.schedule_decode(sid, bucket, q)
                 else:
-                    l.shadow_decode()
+                    l.shadow_decode(q)
             if e.attn is not None:
                 e.attn.launch_decode(mine)
                 if pending is not None:
@@ -415,7 +423,8 @@ class SpmdDriver:
                 else:
                     produced += self._finish_fast(sid, mine)
             if e.expert is not None:
-                e.step(EgStepPlan(step_id=sid, phase="decode", tokens_per_mb=[bucket // e.topo.attn_tp] * rt.num_mb))
+                e.step(EgStepPlan(step_id=sid, phase="decode" if q == 1 else "verify",
+                                  tokens_per_mb=[bucket * q // e.topo.attn_tp] * rt.num_mb))
             if events is not None:          # one timing event per queued step (per-step device times)
                 ev = torch.cuda.Event(enable_timing=True)
                 ev.record(event_stream)
@@ -428,7 +437,7 @@ class SpmdDriver:
         reply = self.e.attn.finish_decode(mine)
         if reply.status:
             raise RuntimeError(f"device status {reply.status} in step {sid}")
-        out = self.lanes[self.my_lane].complete(sid, reply.next_tokens)
+        out = self.lanes[self.my_lane].complete(sid, reply.next_tokens, reply.accepted)
         return sum(len(t) for _, t, _ in out)
 
     def generate(self, prompts: Sequence[Sequence[int]], sampling: SamplingParams) -> List[List[int]]:

@@ -105,10 +105,16 @@ def _linear(x: Tensor, w: Tensor, b: Optional[Tensor] = None) -> Tensor:
     return F.linear(x, w, b)
 
 
-# Decode-sized dense projections (qkv, o_proj, GDN in/out projections, dense and shared-expert MLPs,
-# LM head) run on the tcgen05 kernel with split-K; larger token counts (prefill) are plain library
-# GEMMs. FASTAFD_OWN_DENSE=0 sends everything to the library.
-_OWN_DENSE = os.environ.get("FASTAFD_OWN_DENSE", "1") != "0"
+# Dense projections (qkv, o_proj, GDN in/out projections, dense and shared-expert MLPs, LM head).
+# bf16 weights: plain library GEMMs. Measured on B200 in CUDA-graph replay, the split-K tcgen05
+# kernel of this repository needs 10.1 us for the 64 x 5120 x 2048 qkv projection and 11.3 us for the
+# 64 x 2048 x 4096 o_proj against 6.8 / 8.4 us of the library, so it is opt-in for bf16
+# (FASTAFD_OWN_DENSE=1). Block-FP8 checkpoints: decode-sized projections run on the own kernel with
+# the e4m3 weights and their exact 128x128 scales (half the bytes of a bf16 copy); FASTAFD_OWN_DENSE=0
+# sends those to the library on dequantised weights too.
+_OWN_DENSE_ENV = os.environ.get("FASTAFD_OWN_DENSE", "")
+_OWN_DENSE = _OWN_DENSE_ENV == "1"
+_OWN_DENSE_FP8 = _OWN_DENSE_ENV != "0"
 _OWN_DENSE_MAX_TOKENS = 128
 
 
@@ -262,7 +268,7 @@ class AttentionStage:
         (half the bytes of the decode-time weight stream); the bf16 copies serve prefill-sized GEMMs."""
         c = self.cfg
         self.w_fp8: Dict[str, Tuple[Tensor, Tensor]] = {}
-        if not (c.quant.is_fp8 and self.device.type == "cuda" and _OWN_DENSE):
+        if not (c.quant.is_fp8 and self.device.type == "cuda" and _OWN_DENSE_FP8):
             return
         for name, w in self.w.items():
             if not name.endswith(("qkv_proj.weight", "o_proj.weight", "in_proj_qkv.weight", "in_proj_z.weight",
@@ -276,10 +282,10 @@ class AttentionStage:
     def _proj(self, x: Tensor, name: str, bias: Optional[Tensor] = None) -> Tensor:
         """x @ w[name].T (+ bias)."""
         w = self.w[name]
-        if (_OWN_DENSE and x.is_cuda and x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16 and x.dim() == 2
-                and 0 < x.shape[0] <= _OWN_DENSE_MAX_TOKENS and w.shape[0] % 128 == 0 and w.shape[1] % 64 == 0
-                and x.is_contiguous()):
-            q = self.w_fp8.get(name)
+        q = self.w_fp8.get(name)
+        if ((_OWN_DENSE or q is not None) and x.is_cuda and x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16
+                and x.dim() == 2 and 0 < x.shape[0] <= _OWN_DENSE_MAX_TOKENS and w.shape[0] % 128 == 0
+                and w.shape[1] % 64 == 0 and x.is_contiguous()):
             if q is not None:
                 xq, xs = ops.group_quant_fp8(x, 128)
                 return ops.dense_gemm(xq, q[0], x_scale=xs, w_scale=q[1], bias=bias, status=self.status)
@@ -369,12 +375,19 @@ class AttentionStage:
 
     def _prefill_attention(self, q: Tensor, kc: Tensor, vc: Tensor, meta: AttnMeta, scale: float, page_size: int) -> Tensor:
         """Causal attention of each request's new chunk against its paged KV (which already holds
-        the chunk: K/V were stored before this call). Runs the multi-token mode of the paged
-        kernel per request on CUDA; the oracle on CPU."""
+        the chunk: K/V were stored before this call). On CUDA all requests run in one var-len launch
+        of the paged kernel's multi-token mode; on CPU the oracle, request by request."""
         D = self.cfg.head_dim
+        lens = list(meta.prefill_lens)
+        if q.is_cuda and lens and max(lens) > 0:
+            # one launch over (request, query-row tile, kv head); rows past a request's chunk leave at once
+            starts = torch.zeros(len(lens) + 1, dtype=torch.int32)
+            starts[1:] = torch.tensor(lens, dtype=torch.int32).cumsum(0)
+            return ops.prefill_attention_varlen(q, kc, vc, meta.page_table, meta.seq_lens, starts.to(q.device), max(lens),
+                                                self.hq, self.hkv, D, page_size, scale, status=meta.status)
         out = torch.zeros_like(q)
         off = 0
-        for b, n in enumerate(meta.prefill_lens):
+        for b, n in enumerate(lens):
             if n == 0:
                 continue
             qb = q[off:off + n].contiguous()

@@ -197,7 +197,7 @@ class AgMoeEndpoint:
     def route_dispatch(self, lane: int, attn_out: torch.Tensor, residual: torch.Tensor, norm_w: torch.Tensor,
                        gate_w: torch.Tensor, gate_bias: Optional[torch.Tensor], x_out: torch.Tensor,
                        topk_idx: torch.Tensor, topk_w: torch.Tensor, *, scoring: str, renorm: bool, eps: float,
-                       offset1: bool = False, route_scale: float = 1.0) -> None:
+                       offset1: bool = False, route_scale: float = 1.0, local_schedule: Optional[ScheduleDesc] = None) -> bool:
         """One launch for: residual += attn_out; x = rmsnorm(residual); router; push to experts."""
         if self.cfg.use_direct(attn_out.shape[0]):
             r = RouteDirectDesc()
@@ -210,8 +210,12 @@ class AgMoeEndpoint:
             r.scoring, r.renorm, r.offset1 = (0 if scoring == "softmax" else 1), int(renorm), int(offset1)
             r.eps, r.route_scale = eps, route_scale
             r.tokens_per_cta, r.cluster = self.route_tokens_per_cta, self.route_cluster
+            fused = local_schedule is not None and self.cfg.num_eg == 1 and self.cfg.num_ag == 1
+            if fused:       # experts on this GPU, single source: the kernel's last CTA builds their tile schedule
+                r.fuse_schedule = 1
+                C.memmove(C.byref(r.sched), C.byref(local_schedule), C.sizeof(ScheduleDesc))
             check(lib().afd_ag_route_direct(C.byref(r), cur_stream()), "ag_route_direct")
-            return
+            return fused
         r = RouteDispatchDesc()
         C.memmove(C.byref(r.d), C.byref(self._dispatch_desc[lane]), C.sizeof(DispatchDesc))
         r.d.T = attn_out.shape[0]
@@ -222,6 +226,7 @@ class AgMoeEndpoint:
         r.scoring, r.renorm, r.offset1 = (0 if scoring == "softmax" else 1), int(renorm), int(offset1)
         r.eps, r.route_scale = eps, route_scale
         check(lib().afd_ag_route_dispatch(C.byref(r), cur_stream()), "ag_route_dispatch")
+        return False
 
     def combine_reduce(self, lane: int, topk_w: torch.Tensor, topk_idx: Optional[torch.Tensor], T: int,
                        scale: float = 1.0, extra: Optional[torch.Tensor] = None,
@@ -321,12 +326,13 @@ class EgMoeEndpoint:
         check(lib().afd_eg_group_gather(C.byref(d), cur_stream()), "eg_group_gather_fused" if fused else "eg_group_gather")
 
     def run_layer(self, lane: int, T: int, w13: torch.Tensor, w2: torch.Tensor,
-                  w13_scale: Optional[torch.Tensor] = None, w2_scale: Optional[torch.Tensor] = None) -> None:
+                  w13_scale: Optional[torch.Tensor] = None, w2_scale: Optional[torch.Tensor] = None,
+                  scheduled: bool = False) -> None:
         """One MoE layer for one lane. w13: [E_local, 2I, H] gate/up interleaved (see
         ops.interleave_gate_up); w2: [E_local, H, I]. FP8 mode takes per-tile scales."""
         cfg = self.cfg
         if cfg.use_direct(T):
-            return self._run_layer_direct(lane, w13, w2, w13_scale, w2_scale)
+            return self._run_layer_direct(lane, w13, w2, w13_scale, w2_scale, scheduled)
         self.group_gather(lane, T)
         ntiles = self.counters[0:1]
         grouped_gemm(w=w13, x=self.pool_x, num_experts=self.experts_local, n_per_expert=2 * cfg.intermediate,
@@ -345,8 +351,7 @@ class EgMoeEndpoint:
                      trace=self.trace[lane] if self.trace else None)
 
 
-    def _schedule(self, lane: int) -> None:
-        """One warp: bounded wait for the sources' flags, slot counters -> tile schedule, counters reset."""
+    def schedule_desc(self, lane: int) -> ScheduleDesc:
         cfg, w = self.cfg, self.lanes[lane]
         s = ScheduleDesc()
         s.n2m_flag, s.A, s.epoch, s.counts = ptr(self.n2m_flag[lane]), cfg.num_ag, ptr(w.epoch), ptr(self.dcount[lane])
@@ -355,15 +360,19 @@ class EgMoeEndpoint:
         s.tile_info, s.counters, s.expert_counts = ptr(self.dtile_info), ptr(self.counters), ptr(self.expert_counts)
         s.timeout_ns, s.status = self.timeout_ns, ptr(self.status)
         s.trace = ptr(self.trace[lane]) if self.trace else None
-        check(lib().afd_eg_schedule(C.byref(s), cur_stream()), "eg_schedule")
+        return s
 
-    def _run_layer_direct(self, lane: int, w13, w2, w13_scale, w2_scale) -> None:
+    def _schedule(self, lane: int) -> None:
+        """One warp: bounded wait for the sources' flags, slot counters -> tile schedule, counters reset."""
+        check(lib().afd_eg_schedule(C.byref(self.schedule_desc(lane)), cur_stream()), "eg_schedule")
+
+    def _run_layer_direct(self, lane: int, w13, w2, w13_scale, w2_scale, scheduled: bool = False) -> None:
         """The layer when the sources stored their rows straight into the expert stripes: one warp
         waits for the flags and turns the slot counters into the tile schedule, then the two GEMMs."""
         cfg, w = self.cfg, self.lanes[lane]
-        self._schedule(lane)
+        if not scheduled:                       # else the (single, local) source's route kernel already did it
+            self._schedule(lane)
         ntiles = self.counters[0:1]
-        DR = cfg.direct_rows
         grouped_gemm(w=w13, x=self.dpool_x[lane], num_experts=self.experts_local, n_per_expert=2 * cfg.intermediate,
                      k=cfg.hidden, tile_info=self.dtile_info, num_tok_tiles=ntiles, block_tok=cfg.block_tok,
                      epilogue=EPI_SWIGLU, out=None if cfg.fp8 else self.dpool_h, out_ld=cfg.intermediate,

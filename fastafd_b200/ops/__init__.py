@@ -224,6 +224,22 @@ def group_quant_fp8(x: torch.Tensor, group: int = 128, pow2: bool = False):
 
 
 # ------------------------------------------------------------------------- attention
+def prefill_attention_varlen(q, k_cache, v_cache, page_table, seq_lens, q_starts, max_q_len: int, Hq, Hkv, D, page_size,
+                             sm_scale, out=None, status=None):
+    """Causal attention of every request's new chunk against its paged KV, all requests in one launch
+    (CUDA). q [sum of chunk lengths, Hq, D] bf16 (rows may be strided); q_starts int32 [B+1] = row
+    offsets of the chunks; seq_lens [B] = KV length including the chunk. Returns [rows, Hq, D]."""
+    B = seq_lens.shape[0]
+    if q.stride(2) != 1 or q.stride(1) != D:
+        q = q.contiguous()
+    out = torch.zeros(q.shape, dtype=q.dtype, device=q.device) if out is None else out
+    check(lib().afd_prefill_attention_varlen(ptr(q), q.stride(0), ptr(k_cache), ptr(v_cache), ptr(page_table), ptr(seq_lens),
+                                             ptr(q_starts), ptr(out), B, Hq, Hkv, D, max_q_len, page_size,
+                                             page_table.shape[1], k_cache.shape[0], sm_scale, ptr(status), cur_stream()),
+          "prefill_attention_varlen")
+    return out
+
+
 def decode_attn_workspace(B, Hq, Hkv, q_len, D, splits, device) -> Optional[torch.Tensor]:
     if splits <= 1:
         return None
@@ -297,6 +313,17 @@ def interleave_gate_up_scales(scale: torch.Tensor, I: int, block: int = 128) -> 
     return torch.stack([scale[:, gb], scale[:, ub]], dim=2).contiguous()
 
 
+def tile_major(w: torch.Tensor) -> torch.Tensor:
+    """[..., N, K] weights (N % 128 == 0, K a multiple of the 128-byte k block) -> the same bytes stored
+    tile by tile, [..., N/128, K/kblk, 128, kblk]: each 128-row x 128-byte tile the GEMM loads is one
+    consecutive 16 KB piece of memory. Pass the result with ``w_tile_major=True``."""
+    kblk = 128 // w.element_size()
+    *lead, N, K = w.shape
+    t = w.reshape(*lead, N // 128, 128, K // kblk, kblk)
+    nd = t.dim()
+    return t.permute(*range(nd - 4), nd - 4, nd - 2, nd - 3, nd - 1).contiguous()
+
+
 def plain_tile_scales(scale: torch.Tensor) -> torch.Tensor:
     """[E, N/128, K/128] -> [E, n_tiles, 2, K/128] for non-interleaved weights."""
     return torch.stack([scale, scale], dim=2).contiguous()
@@ -317,7 +344,7 @@ def grouped_gemm(*, w, x, num_experts, n_per_expert, k, tile_info, num_tok_tiles
                  epilogue, out=None, out_ld=0, fp8=False, x_scale=None, w_scale=None, out_q=None,
                  out_scale=None, row_meta=None, peer_combine=(), peer_flag=(), combine_tokens=0,
                  hidden=0, epoch=None, done_counter=None, status=None, grid=NUM_SMS, trace=None,
-                 k_splits=1, splitk_ws=None, splitk_cnt=None, bias=None):
+                 k_splits=1, splitk_ws=None, splitk_cnt=None, bias=None, w_tile_major=False):
     """Low-level launcher of the tcgen05 grouped GEMM (see csrc/grouped_gemm.cu)."""
     d = GroupedGemmDesc()
     d.w, d.x = ptr(w), ptr(x)
@@ -335,6 +362,7 @@ def grouped_gemm(*, w, x, num_experts, n_per_expert, k, tile_info, num_tok_tiles
     d.num_peers, d.combine_tokens, d.hidden = len(peer_combine), combine_tokens, hidden
     d.epoch, d.done_counter, d.status, d.trace = ptr(epoch), ptr(done_counter), ptr(status), ptr(trace)
     d.k_splits, d.splitk_ws, d.splitk_cnt, d.bias = k_splits, ptr(splitk_ws), ptr(splitk_cnt), ptr(bias)
+    d.w_tile_major = int(w_tile_major)
     check(lib().afd_grouped_gemm(C.byref(d), cur_stream()), "grouped_gemm")
 
 
@@ -345,14 +373,16 @@ _SPLITK_WS: dict = {}
 
 
 def pick_k_splits(tok_tiles: int, n_tiles: int, k_blocks: int) -> int:
-    """K splits of a dense GEMM with tok_tiles x n_tiles output tiles: enough work units to give every
-    SM one (up to about two), a split never shorter than 4 K blocks, and an exact division of K."""
+    """K splits of a dense GEMM with tok_tiles x n_tiles output tiles. Measured on B200: a split pays
+    only while the launch stays within one wave of SMs and each unit keeps a long K range (the fence +
+    arrival counter + partial sum of a split cost about as much as 16 K blocks of streaming), so: at
+    most one unit per SM, at least 16 K blocks per unit, an exact division of K."""
     tiles = max(1, tok_tiles * n_tiles)
     best = 1
     for s in range(1, 33):
-        if k_blocks % s != 0 or k_blocks // s < 4:
+        if k_blocks % s != 0 or k_blocks // s < 16:
             continue
-        if tiles * s <= 2 * NUM_SMS:
+        if tiles * s <= NUM_SMS:
             best = s
     return best
 

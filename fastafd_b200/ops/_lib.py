@@ -30,6 +30,7 @@ class GroupedGemmDesc(C.Structure):
         ("num_peers", C.c_int), ("combine_tokens", C.c_int), ("hidden", C.c_int),
         ("epoch", VP), ("done_counter", VP), ("status", VP), ("trace", VP),
         ("k_splits", C.c_int), ("splitk_ws", VP), ("splitk_cnt", VP), ("bias", VP),
+        ("w_tile_major", C.c_int),
     ]
 
 
@@ -64,6 +65,16 @@ class DirectDesc(C.Structure):
     ]
 
 
+class ScheduleDesc(C.Structure):
+    _fields_ = [
+        ("n2m_flag", VP), ("A", C.c_int), ("epoch", VP), ("counts", VP),
+        ("experts_local", C.c_int), ("cap", C.c_int), ("block_tok", C.c_int), ("max_tok_tiles", C.c_int),
+        ("tile_info", VP), ("counters", VP), ("expert_counts", VP),
+        ("timeout_ns", C.c_ulonglong),
+        ("status", VP), ("trace", VP),
+    ]
+
+
 class RouteDirectDesc(C.Structure):
     _fields_ = [
         ("attn_out", VP), ("residual", VP), ("norm_w", VP), ("gate_w", VP), ("gate_bias", VP),
@@ -72,16 +83,7 @@ class RouteDirectDesc(C.Structure):
         ("eps", C.c_float), ("route_scale", C.c_float),
         ("tokens_per_cta", C.c_int), ("cluster", C.c_int),
         ("d", DirectDesc),
-    ]
-
-
-class ScheduleDesc(C.Structure):
-    _fields_ = [
-        ("n2m_flag", VP), ("A", C.c_int), ("epoch", VP), ("counts", VP),
-        ("experts_local", C.c_int), ("cap", C.c_int), ("block_tok", C.c_int), ("max_tok_tiles", C.c_int),
-        ("tile_info", VP), ("counters", VP), ("expert_counts", VP),
-        ("timeout_ns", C.c_ulonglong),
-        ("status", VP), ("trace", VP),
+        ("fuse_schedule", C.c_int), ("sched", ScheduleDesc),
     ]
 
 
@@ -134,6 +136,8 @@ _SIGNATURES = {
     "afd_decode_attention_strided": (C.c_int, [VP, C.c_long, VP, VP, VP, VP, VP, VP, C.c_int, C.c_int, C.c_int,
                                                C.c_int, C.c_int, C.c_int, C.c_int, C.c_long, C.c_int, C.c_float,
                                                VP, VP]),
+    "afd_prefill_attention_varlen": (C.c_int, [VP, C.c_long, VP, VP, VP, VP, VP, VP, C.c_int, C.c_int, C.c_int, C.c_int,
+                                               C.c_int, C.c_int, C.c_int, C.c_long, C.c_float, VP, VP]),
     "afd_argmax": (C.c_int, [VP, VP, C.c_int, C.c_int, C.c_long, C.c_int, VP, VP]),
     "afd_argmax_chunks": (C.c_int, [C.c_int]),
     "afd_tp_allgather_push": (C.c_int, [VP, VP]),

@@ -50,12 +50,17 @@ class StepRecord:
 class LaneScheduler:
     def __init__(self, lane: int, *, num_pages: int, page_size: int, max_running: int, max_seq_len: int,
                  num_mb: int = 2, max_batched_tokens: int = 8192, max_comm_tokens: int = 2048,
-                 cache_type: str = "naive", eos_token_ids: Sequence[int] = (), spec_block: int = 0):
+                 cache_type: str = "naive", eos_token_ids: Sequence[int] = (), spec_block: int = 0,
+                 spec_pending: int = 1):
         self.lane, self.page_size, self.max_running, self.max_seq_len = lane, page_size, max_running, max_seq_len
         self.num_mb, self.max_batched_tokens, self.max_comm_tokens = num_mb, max_batched_tokens, max_comm_tokens
         self.cache: NaivePageLedger = make_page_cache(cache_type, num_pages, page_size)
         self.eos = set(int(e) for e in eos_token_ids)
         self.spec_block = spec_block
+        # Verify steps are planned before the acceptance of the steps in flight is known, so a
+        # request's planned length is an upper bound that runs ahead of its committed length by up to
+        # one block per step in flight (plus the block being planned): that much KV is reserved.
+        self.spec_slack = spec_block * (max(spec_pending, 1) + 1) if spec_block > 1 else 0
         self.max_pages_per_req = (max_seq_len + page_size - 1) // page_size
         self.dummy_row = max_running                    # extra row owned by padding requests
         self.waiting: Deque[Req] = deque()
@@ -70,7 +75,7 @@ class LaneScheduler:
 
     # ------------------------------------------------------------------ admission
     def add_req(self, uid: int, input_ids: Sequence[int], sampling: SamplingParams) -> None:
-        total = len(input_ids) + sampling.max_tokens + self.spec_block
+        total = len(input_ids) + sampling.max_tokens + self.spec_slack
         if len(input_ids) == 0:
             raise AdmissionError(f"request {uid} has an empty prompt")
         if total > self.max_seq_len:
@@ -87,7 +92,7 @@ class LaneScheduler:
             raise AdmissionError("no free request row")
         req = Req(uid=uid, input_ids=[0] * prompt_len, sampling=sampling, lane=self.lane)
         req.table_idx = self.free_rows.pop()
-        need = self.cache.pages_for(req.max_total_len + self.spec_block)
+        need = self.cache.pages_for(req.max_total_len + self.spec_slack)
         if self.reserved_pages + need > self.cache.num_pages - 1:
             self.free_rows.append(req.table_idx)
             raise AdmissionError(f"request {uid} needs {need} pages; lane has {self.cache.num_pages - 1 - self.reserved_pages}")
@@ -124,7 +129,7 @@ class LaneScheduler:
             return False
         req = self.waiting[0]
         shared, handle = self.cache.match_prefix(req.input_ids)
-        need = self.cache.pages_for(req.max_total_len + self.spec_block) - len(shared)
+        need = self.cache.pages_for(req.max_total_len + self.spec_slack) - len(shared)
         if self.reserved_pages + need > self.cache.num_pages - 1:
             if handle:
                 for n in handle:
@@ -147,7 +152,8 @@ class LaneScheduler:
 
     def decodable(self) -> List[_ReqState]:
         return [s for s in self.states.values()
-                if not s.dead and s.planned_len >= s.req.prompt_len and s.planned_out < s.req.sampling.max_tokens]
+                if not s.dead and s.planned_len >= s.req.prompt_len and s.planned_out < s.req.sampling.max_tokens
+                and (self.spec_block <= 1 or s.planned_len + self.spec_block <= s.req.max_total_len + self.spec_slack)]
 
     def decode_real(self) -> int:
         return len(self.decodable())
@@ -291,8 +297,9 @@ class LaneScheduler:
         n = 0
         for st in self.states.values():
             if not st.dead and st.planned_len >= st.req.prompt_len and st.planned_out < st.req.sampling.max_tokens:
-                st.planned_len += tokens_per_req
-                st.planned_out += 1
+                if tokens_per_req == 1:      # a verify step's progress depends on acceptance, known to its own rank only
+                    st.planned_len += 1
+                    st.planned_out += 1
                 n += 1
         return n
 

@@ -396,6 +396,8 @@ class AttentionWorker:
 
     def launch_decode(self, plan: AgStepPlan) -> None:
         """Queue one decode step (H2D of the plan, graph replay or eager body, D2H of tokens)."""
+        if plan.phase == "verify":
+            return self.spec.launch_verify(plan)
         bucket = plan.bucket
         ctx = torch.cuda.stream(self.main_stream) if self.cuda else nullcontext()
         with ctx:
@@ -434,6 +436,8 @@ class AttentionWorker:
                     [self.bufs[l].next_tokens[:bucket].numpy().copy() for l in range(self.num_mb)])
 
     def finish_decode(self, plan: AgStepPlan) -> AgStepReply:
+        if plan.phase == "verify":
+            return self.spec.finish_verify(plan)
         bucket = plan.bucket
         if self.cuda:
             slot = plan.step_id % RING
@@ -512,6 +516,8 @@ class AttentionWorker:
                     rows_s = torch.from_numpy(mbp.rows[mbp.sample_rows].astype(np.int64)).to(dev)
                     lens_s = torch.from_numpy(mbp.seq_lens[mbp.sample_rows].astype(np.int64)).to(dev)
                     self.token_pool[rows_s, lens_s] = t.to(torch.int32)
+                    if self.spec is not None:
+                        self.spec.set_committed(rows_s, lens_s)
                     if self.logit_tap is not None:
                         self.logit_tap.append((rows_s.cpu().clone(), lens_s.cpu().clone(), logits.float().cpu().clone()))
                     toks[mbp.sample_rows] = t.cpu().numpy()
@@ -536,9 +542,7 @@ class AttentionWorker:
             tp = self.tp.size
             reply = self.run_prefill(plan, mb_tokens or [(mb.num_tokens + tp - 1) // tp for mb in plan.mbs])
         elif plan.phase == "verify":
-            ctx = torch.cuda.stream(self.main_stream) if self.cuda else nullcontext()
-            with ctx:
-                reply = self.spec.run_verify(plan)
+            reply = self.spec.run_verify(plan)
         else:
             self.launch_decode(plan)
             reply = self.finish_decode(plan)

@@ -136,13 +136,18 @@ class FabricMoeClient(MoeClient):
 
     def route_dispatch(self, lane, layer, attn_out, residual, norm_w, gate_w, gate_bias, x_out, topk_idx, topk_w, *,
                        scoring, renorm, eps, offset1=False):
-        self.ep.route_dispatch(lane, attn_out, residual, norm_w, gate_w, gate_bias, x_out, topk_idx, topk_w,
-                               scoring=scoring, renorm=renorm, eps=eps, offset1=offset1)
+        local = None
+        if self.colocated is not None and self.ep.cfg.use_direct(attn_out.shape[0]):
+            local = self.colocated.ep.schedule_desc(lane)
+        self._scheduled = self.ep.route_dispatch(lane, attn_out, residual, norm_w, gate_w, gate_bias, x_out, topk_idx, topk_w,
+                                                 scoring=scoring, renorm=renorm, eps=eps, offset1=offset1,
+                                                 local_schedule=local)
 
     def after_dispatch(self, lane, layer, T):
         """Work that follows a push in the same process (colocated expert stage)."""
         if self.colocated is not None:
-            self.colocated.serve(lane, layer, T)
+            self.colocated.serve(lane, layer, T, scheduled=bool(getattr(self, "_scheduled", False)))
+            self._scheduled = False
 
     def combine(self, lane, layer, T, topk_w, topk_idx, residual, norm_w, eps, *, extra=None, scale=1.0,
                 offset1=False, normed_out=None):
@@ -159,7 +164,7 @@ class FabricMoeClient(MoeClient):
 
 
 class MoeServer:
-    def serve(self, lane: int, layer: int, T: int) -> None:
+    def serve(self, lane: int, layer: int, T: int, scheduled: bool = False) -> None:
         raise NotImplementedError
 
 
@@ -167,16 +172,16 @@ class FabricMoeServer(MoeServer):
     def __init__(self, endpoint, stage: ExpertStage):
         self.ep, self.stage = endpoint, stage
 
-    def serve(self, lane, layer, T):
+    def serve(self, lane, layer, T, scheduled=False):
         s = self.stage
-        self.ep.run_layer(lane, T, s.w13[layer], s.w2[layer], s.w13_scale[layer], s.w2_scale[layer])
+        self.ep.run_layer(lane, T, s.w13[layer], s.w2[layer], s.w13_scale[layer], s.w2_scale[layer], scheduled=scheduled)
 
 
 class GlooMoeServer(MoeServer):
     def __init__(self, stage: ExpertStage, source_ranks: Sequence[int], hidden: int, topk: int, dtype, group=None):
         self.stage, self.sources, self.hidden, self.topk, self.dtype, self.group = stage, list(source_ranks), hidden, topk, dtype, group
 
-    def serve(self, lane, layer, T):
+    def serve(self, lane, layer, T, scheduled=False):
         """T is ignored: each source announces its own token count."""
         outs = []
         for r in self.sources:

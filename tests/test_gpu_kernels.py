@@ -403,3 +403,31 @@ def test_shared_gate_and_attention_gate_kernels():
     want = (o.float() * torch.sigmoid(gate.float())).to(torch.bfloat16)
     got = ops.sigmoid_gate_mul(o.clone(), gate)
     torch.testing.assert_close(got.float(), want.float(), atol=1e-2, rtol=1e-2)
+
+
+def test_prefill_attention_varlen_one_launch():
+    """Chunks of different lengths (one of them empty, one continuing an earlier chunk) in one launch
+    against the per-request oracle."""
+    Hq, Hkv, D, page = 8, 2, 128, 16
+    chunk = [37, 0, 5, 64, 1]
+    seq = [37, 12, 50, 64, 200]            # KV length including the chunk (requests 2 and 4 continue)
+    B = len(chunk)
+    max_pages = (max(seq) + page - 1) // page + 1
+    n_pages = B * max_pages + 3
+    pt = torch.randperm(n_pages)[:B * max_pages].view(B, max_pages).to(torch.int32)
+    kc, vc = _bf(n_pages * page, Hkv, D, seed=81), _bf(n_pages * page, Hkv, D, seed=82)
+    q = _bf(sum(chunk), Hq, D, seed=83)
+    starts = torch.tensor([0] + list(torch.tensor(chunk).cumsum(0)), dtype=torch.int32)
+    scale = 1 / math.sqrt(D)
+    status = torch.zeros(1, dtype=torch.int32, device=DEV)
+    out = ops.prefill_attention_varlen(q, kc, vc, pt.to(DEV), torch.tensor(seq, dtype=torch.int32, device=DEV),
+                                       starts.to(DEV), max(chunk), Hq, Hkv, D, page, scale, status=status)
+    torch.cuda.synchronize()
+    assert int(status) == 0
+    off = 0
+    for b, n in enumerate(chunk):
+        if n:
+            exp = ref.decode_attention(q[off:off + n].cpu(), kc.cpu(), vc.cpu(), pt[b:b + 1], torch.tensor([seq[b]], dtype=torch.int32),
+                                       Hq, Hkv, D, n, page, scale)
+            torch.testing.assert_close(out[off:off + n].cpu().float(), exp.float(), atol=2e-2, rtol=2e-2)
+        off += n
