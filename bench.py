@@ -35,6 +35,8 @@ sys.path.insert(0, HERE)
 
 # Published reference numbers (GB200 NVL72, 4 attention + 4 FFN GPUs, scripts/benchmark/configs.json:366), tok/s/GPU.
 PUBLISHED_TOK_S_PER_GPU = {"qwen3-235b-a22b-fp8": 1542.0}
+# the same model with EAGLE-3, 3 draft tokens, 4K context, 194 requests per attention GPU (configs.json:403)
+PUBLISHED_SPEC_TOK_S_PER_GPU = {("qwen3-235b-a22b-fp8", 4): 3764.0}
 METRIC = ("decode tok/s of the whole job, AFD attention + expert GPUs on N x B200, max over ranks "
           "(per-GPU decode tok/s: per_gpu_tok_s; TPOT p50: tpot_p50_ms; N2M/M2N GB/s: n2m_m2n)")
 
@@ -54,6 +56,10 @@ def parse_args():
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--attn-gpus", type=int, default=0, help="attention GPUs of the N (0 = N/2, the 1:1 split)")
     ap.add_argument("--attn-tp", type=int, default=1, help="tensor-parallel size of an attention DP lane")
+    ap.add_argument("--router-bias", default="", help="zipf:S - router selection bias drawn so that expert popularity follows "
+                                                      "Zipf(S) (models with a selection bias, e.g. minimax-m2.5-fp8)")
+    ap.add_argument("--spec-block", type=int, default=0, help="speculative decoding: verified tokens per step (drafts + 1)")
+    ap.add_argument("--spec-sim-accept", type=float, default=0.0, help="fixed mean acceptance (tokens per verify step) for timing runs")
     return ap.parse_args()
 
 
@@ -68,6 +74,25 @@ def reference_arm(args) -> None:
     out = ref.run(args, clock_sampler_cls=ClockSampler)
     if int(os.environ.get("RANK", "0")) == 0:
         print(json.dumps(out), flush=True)
+
+
+def apply_router_bias(eng, cfg, spec: str) -> None:
+    """`zipf:S`: the selection bias of every MoE layer is set so that expert popularity is skewed like a
+    Zipf(S) law over the experts (a different expert order per layer): bias = popularity / max popularity,
+    on the scale of the sigmoid scores it is added to."""
+    import torch
+
+    kind, _, val = spec.partition(":")
+    if kind != "zipf" or not cfg.router_bias:
+        raise SystemExit(f"--router-bias {spec}: needs zipf:S and a model whose router has a selection bias")
+    if eng.attn is None:
+        return
+    s_exp, E = float(val or 1.2), cfg.num_experts
+    pop = 1.0 / torch.arange(1, E + 1, dtype=torch.float32) ** s_exp
+    g = torch.Generator().manual_seed(1234)
+    for name, w in eng.attn.model.w.items():
+        if name.endswith("mlp.gate.e_score_correction_bias"):
+            w.copy_((pop / pop.max())[torch.randperm(E, generator=g)].to(w.device))
 
 
 class ClockSampler:
@@ -161,14 +186,20 @@ def main():
     per_mb = (lane_b + args.num_mb - 1) // args.num_mb
     per_mb = (per_mb + tp - 1) // tp * tp
     total_steps = 3 * args.steps + 2 * args.warmup + 8
+    q = args.spec_block if args.spec_block > 1 else 1
+    if q > 1:
+        os.environ["FASTAFD_SPEC_SIM_ACCEPT"] = str(args.spec_sim_accept or 0)
     rt = RuntimeConfig(model_path=args.model, num_mb=args.num_mb, page_size=16, max_running_requests=lane_b,
-                       max_seq_len=args.context + total_steps + 16, cuda_graph_max_bs=per_mb,
+                       max_seq_len=args.context + total_steps * q + 4 * q + 16, cuda_graph_max_bs=per_mb,
                        decode_graph_bs=(per_mb,), use_cuda_graph=not args.no_graph, moe_block_tok=args.block_tok,
-                       max_batched_tokens=per_mb * args.num_mb, device="cuda", flag_timeout_s=2.0)
+                       max_batched_tokens=per_mb * args.num_mb * q, device="cuda", flag_timeout_s=2.0,
+                       spec_block=args.spec_block if q > 1 else 0)
     t_build = time.time()
-    eng = AfdEngine(cfg, rt, topo, rank, device, group=None, seed=0, fast_init=True, max_comm_tokens=per_mb // tp)
+    eng = AfdEngine(cfg, rt, topo, rank, device, group=None, seed=0, fast_init=True, max_comm_tokens=per_mb * q // tp)
+    if args.router_bias:
+        apply_router_bias(eng, cfg, args.router_bias)
     drv = SpmdDriver(eng)
-    drv.install_prefilled(lane_b, args.context, max_tokens=total_steps + 4)
+    drv.install_prefilled(lane_b, args.context, max_tokens=total_steps * q + 4)
     torch.cuda.synchronize()
     build_s = time.time() - t_build
 
@@ -246,6 +277,17 @@ def main():
             trace_info = {"rank0": mine}
     n_attn = 1 if topo.colocated else topo.attn_world
     tokens = b * n_attn * args.steps
+    spec_info = None
+    if q > 1:
+        # a verify step commits the accepted drafts + 1 token per request: count what was committed
+        acc = eng.attn.spec.mean_accept() if eng.attn is not None else 0.0
+        if world > 1:
+            t_acc = torch.tensor([acc], dtype=torch.float64)
+            dist.all_reduce(t_acc, op=dist.ReduceOp.MAX)
+            acc = float(t_acc[0])
+        tokens = b * n_attn * args.steps * acc
+        spec_info = {"block": q, "drafts": q - 1, "mean_tokens_per_step": round(acc, 3),
+                     "acceptance": "simulated fixed mean" if args.spec_sim_accept else "greedy verification of a random-init draft head"}
     value = tokens / (dev_ms / 1e3)
     e2e_value = tokens / (e2e_ms / 1e3)
     kernels_per_step = 0
@@ -257,7 +299,7 @@ def main():
     if eng.attn is not None:
         h2d = 2 * per_mb * 4 * args.num_mb + 24 * ((b + 15) // 16)   # rows + seq_lens (+ page grants, amortised)
         d2h = per_mb * 4 * args.num_mb + 8
-    published = PUBLISHED_TOK_S_PER_GPU.get(args.model)
+    published = PUBLISHED_SPEC_TOK_S_PER_GPU.get((args.model, q)) if q > 1 else PUBLISHED_TOK_S_PER_GPU.get(args.model)
     # N2M / M2N traffic of one attention GPU per step (bytes that cross NVLink; 0 when colocated):
     # up = one row per expert GPU that owns one of the token's experts (expectation under uniform
     # routing), down = one bf16 row per (token, k).
@@ -317,6 +359,10 @@ def main():
             "kernels_per_step_rank0": kernels_per_step,
             "device_status": status, "build_s": round(build_s, 1),
         }
+        if spec_info is not None:
+            out["speculative"] = spec_info
+        if args.router_bias:
+            out["config"]["router_bias"] = args.router_bias
         if comm is not None:
             out["n2m_m2n"] = comm
         if trace_info is not None and os.environ.get("FASTAFD_COMM_TRACE_FULL") == "1":

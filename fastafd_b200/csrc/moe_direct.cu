@@ -29,7 +29,7 @@ namespace afd {
 
 constexpr int kMaxDirectRanks = 16;
 constexpr int kRouteThreads = 512;
-constexpr int kMaxTopk = 16;
+constexpr int kMaxTopk = 32;
 
 struct DirectArgs {
   void* peer_pool[kMaxDirectRanks];          // [E_local * cap][row_bytes] on each expert GPU

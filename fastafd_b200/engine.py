@@ -104,11 +104,15 @@ class AfdEngine:
         self.attn: Optional[AttentionWorker] = None
         self.expert: Optional[ExpertWorker] = None
         # MLP TP with mlp_ep == 1: the ranks of a replica all hold every expert with a slice of the
-        # intermediate dimension and return partial sums (host path only). mlp_ep == mlp_tp means
-        # expert parallelism inside the TP group, i.e. plain EP.
+        # intermediate dimension and return partial sums. mlp_ep == mlp_tp means expert parallelism
+        # inside the TP group, i.e. plain EP. On GPUs the slices are "virtual experts": slice r of
+        # expert e is expert r * E + e, owned by expert rank r, and a token that chose e with weight w
+        # chooses all its slices with weight w - dispatch, grouping and the combine sum then work
+        # unchanged on E * tp experts with top-(K * tp) routing.
         mlp_tp_shard = (not self.colocated) and topo.mlp_tp > 1 and topo.mlp_ep == 1
-        if mlp_tp_shard and cuda:
-            raise NotImplementedError("MLP tensor parallelism is built for the gloo path only; use expert parallelism on GPUs")
+        tp_expand = topo.mlp_tp if (mlp_tp_shard and cuda) else 1
+        if tp_expand > 1 and cfg.num_experts_per_tok * tp_expand > 32:
+            raise ValueError("MLP TP on GPUs needs num_experts_per_tok x mlp_tp <= 32")
         # One replica of the expert set (mlp_dp of them) serves the lanes l with l % mlp_dp == replica:
         # an attention rank talks to its replica's expert ranks, an expert rank to its lanes' ranks.
         if self.colocated:
@@ -164,9 +168,10 @@ class AfdEngine:
                 if os.environ.get("FASTAFD_DIRECT", "1") == "0" or num_ag * direct > 1024:
                     direct = 0
                 mcfg = MoeCommConfig(num_ag=num_ag, num_eg=num_eg, num_lanes=rt.num_mb, max_tokens=self.max_comm_tokens,
-                                     hidden=cfg.hidden_size, topk=cfg.num_experts_per_tok, num_experts=cfg.num_experts,
-                                     intermediate=cfg.moe_intermediate_size, fp8=cfg.quant.is_fp8, block_tok=rt.moe_block_tok,
-                                     direct_tokens=direct)
+                                     hidden=cfg.hidden_size, topk=cfg.num_experts_per_tok * tp_expand,
+                                     num_experts=cfg.num_experts * tp_expand,
+                                     intermediate=cfg.moe_intermediate_size // tp_expand, fp8=cfg.quant.is_fp8,
+                                     block_tok=rt.moe_block_tok, direct_tokens=direct)
                 timeout_ns = int(rt.flag_timeout_s * 1e9)
                 if self.colocated:
                     fabs = Fabric.local([ag_layout(mcfg).size, eg_layout(mcfg).size], self.device)
@@ -186,7 +191,8 @@ class AfdEngine:
                         size += tp_layout(topo.attn_tp, rt.num_mb, self.max_comm_tokens, cfg.hidden_size).size
                     self.fabric = Fabric.ipc(size, self.device, group)
                     if self.is_attention:
-                        client = FabricMoeClient(AgMoeEndpoint(mcfg, self.fabric, my_ag_index, eg_ranks, self.device, timeout_ns, status=sw))
+                        client = FabricMoeClient(AgMoeEndpoint(mcfg, self.fabric, my_ag_index, eg_ranks, self.device, timeout_ns, status=sw),
+                                                 tp_expand=tp_expand, base_experts=cfg.num_experts)
                     else:
                         eg_ep = EgMoeEndpoint(mcfg, self.fabric, topo.ep_rank(rank), ag_ranks,
                                               self.device, timeout_ns, status=sw)

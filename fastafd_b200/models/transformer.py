@@ -548,13 +548,13 @@ class ExpertStage:
         self.ep_rank, self.ep_size = ep_rank, ep_size
         # MLP tensor parallelism: every rank of the TP group holds all of its experts with 1/tp of
         # the intermediate dimension (gate / up rows and down columns) and returns partial rows
-        # that the attention side sums. Host (gloo) path only.
+        # that the attention side sums (on GPUs: one combine slot per (TP rank, k), see
+        # worker/moe_client.py:FabricMoeClient).
         self.tp_rank, self.tp_size = tp_rank, tp_size
         if tp_size > 1:
-            if self.device.type == "cuda":
-                raise NotImplementedError("MLP tensor parallelism is built for the gloo path only")
-            if cfg.moe_intermediate_size % tp_size != 0:
-                raise ValueError("moe_intermediate_size must be a multiple of the MLP TP size")
+            unit = 128 if self.device.type == "cuda" else 1
+            if cfg.moe_intermediate_size % (tp_size * unit) != 0:
+                raise ValueError(f"moe_intermediate_size must be a multiple of {unit} x the MLP TP size")
         self.experts_local = (cfg.num_experts + ep_size - 1) // ep_size
         self.expert_base = ep_rank * self.experts_local
         self.moe_layers = [i for i in range(cfg.num_layers) if cfg.is_moe_layer(i)]
@@ -607,11 +607,19 @@ class ExpertStage:
                 down = down[:, :, lo:hi]
             self.gate_up[layer], self.down[layer] = gate_up.to(self.dtype).contiguous(), down.to(self.dtype).contiguous()
             return
+        I = c.moe_intermediate_size
+        if self.tp_size > 1:            # this rank's slice of the intermediate dimension (whole 128-blocks)
+            lo, hi = self.tp_rank * (I // self.tp_size), (self.tp_rank + 1) * (I // self.tp_size)
+            if gate_up_scale is not None:
+                gate_up_scale = torch.cat([gate_up_scale[:, lo // 128:hi // 128], gate_up_scale[:, (I + lo) // 128:(I + hi) // 128]], dim=1)
+                down_scale = down_scale[:, :, lo // 128:hi // 128]
+            gate_up = torch.cat([gate_up[:, lo:hi], gate_up[:, I + lo:I + hi]], dim=1)
+            down = down[:, :, lo:hi]
+            I = hi - lo
         if c.quant.is_fp8:
             if gate_up.dtype != torch.float8_e4m3fn:
                 gate_up, gate_up_scale = _block_quant_experts(gate_up)
                 down, down_scale = _block_quant_experts(down)
-            I = c.moe_intermediate_size
             self.w13[layer] = ops.interleave_gate_up(gate_up.view(torch.uint8)).view(torch.float8_e4m3fn)
             self.w13_scale[layer] = ops.interleave_gate_up_scales(gate_up_scale.float(), I)
             self.w2[layer] = down.contiguous()

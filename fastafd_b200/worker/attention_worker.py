@@ -183,7 +183,9 @@ class AttentionWorker:
     def _on_lane(self, lane: int, after_main: bool = True):
         """Run the enclosed launches on the lane's stream, ordered after what `main` has queued
         so far; the caller orders `main` after the lane later with `_join_lane`."""
-        if not self.cuda:
+        if not self.cuda or self.num_mb == 1:
+            # one micro-batch: nothing to overlap with, so everything stays on the main stream and
+            # consecutive kernels keep their programmatic (early-launch) dependencies
             yield
             return
         s = self.lane_streams[lane]
@@ -193,7 +195,7 @@ class AttentionWorker:
             yield
 
     def _join_lane(self, lane: int) -> None:
-        if self.cuda:
+        if self.cuda and self.num_mb > 1:
             torch.cuda.current_stream().wait_stream(self.lane_streams[lane])
 
     def _next_norm_weight(self, layer: int) -> torch.Tensor:

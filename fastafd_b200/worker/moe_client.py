@@ -123,16 +123,29 @@ class FabricMoeClient(MoeClient):
     """CUDA: the fused kernels. `colocated` is an expert server living in the same process
     and GPU (single-GPU runs): its layer is launched right after the push on the same stream."""
 
-    def __init__(self, endpoint, colocated: Optional["FabricMoeServer"] = None):
+    def __init__(self, endpoint, colocated: Optional["FabricMoeServer"] = None, tp_expand: int = 1, base_experts: int = 0):
         self.ep, self.colocated = endpoint, colocated
+        # MLP tensor parallelism: expert e's slice r is virtual expert r * base_experts + e on expert
+        # rank r; every routing entry is repeated for the tp slices (same weight).
+        self.tp_expand, self.base_experts = tp_expand, base_experts
+        self._expanded = {}
+
+    def _expand(self, lane, topk_idx, topk_w):
+        n, E = self.tp_expand, self.base_experts
+        idx = torch.cat([torch.where(topk_idx >= 0, topk_idx + r * E, topk_idx) for r in range(n)], dim=1).contiguous()
+        w = torch.cat([topk_w] * n, dim=1).contiguous()
+        self._expanded[lane] = (idx, w)
+        return idx, w
 
     def dispatch(self, lane, layer, x, topk_idx, topk_w):
+        if self.tp_expand > 1:
+            topk_idx, topk_w = self._expand(lane, topk_idx, topk_w)
         self.ep.dispatch(lane, x, topk_idx)
         if self.colocated is not None:
             self.colocated.serve(lane, layer, x.shape[0])
 
     def can_fuse_route(self, T, num_experts, hidden):
-        return T <= 256 and num_experts <= 512 and hidden % 256 == 0 and hidden <= 4096
+        return self.tp_expand == 1 and T <= 256 and num_experts <= 512 and hidden % 256 == 0 and hidden <= 4096
 
     def route_dispatch(self, lane, layer, attn_out, residual, norm_w, gate_w, gate_bias, x_out, topk_idx, topk_w, *,
                        scoring, renorm, eps, offset1=False):
@@ -153,6 +166,8 @@ class FabricMoeClient(MoeClient):
                 offset1=False, normed_out=None):
         if normed_out is None:
             normed_out = torch.empty_like(residual)
+        if self.tp_expand > 1:
+            topk_idx, topk_w = self._expanded.pop(lane)
         return self.ep.combine_reduce(lane, topk_w, topk_idx, T, scale=scale, extra=extra, residual=residual,
                                       norm_w=norm_w, normed=normed_out, eps=eps, offset1=offset1)
 

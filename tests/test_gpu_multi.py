@@ -166,3 +166,54 @@ def test_tp_fused_collectives_stress(world):
         mp.spawn(_tp_stress_worker, args=(world, _free_port(), path, 200), nprocs=world, join=True)
         res = torch.load(path)
     assert res.sum().item() == 0, res
+
+
+def _topo_worker(rank, world, port, out_path, n_new, topo_kw):
+    import torch.distributed as dist
+    from fastafd_b200.core import SamplingParams
+    from fastafd_b200.engine import AfdEngine, SpmdDriver
+    from fastafd_b200.protocol import AfdTopology
+
+    os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    cfg = _cfg()
+    eng = AfdEngine(cfg, _rt(), AfdTopology(**topo_kw), rank, f"cuda:{rank}", seed=0)
+    out = SpmdDriver(eng).generate(_prompts(cfg), SamplingParams(max_tokens=n_new, ignore_eos=True))
+    if rank == 0:
+        torch.save(out, out_path)
+    dist.barrier()
+    eng.close()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("topo_kw,exact", [(dict(attn_dp=2, mlp_dp=2, mlp_ep=1), True),
+                                           (dict(attn_dp=2, mlp_tp=2, mlp_ep=1), False)], ids=["mlp-dp2", "mlp-tp2"])
+def test_mlp_replicas_and_mlp_tensor_parallel_on_gpus(topo_kw, exact):
+    """4 GPUs, 2 attention lanes. MLP DP: two replicas of the whole expert set, lane l served by
+    replica l % 2 - same arithmetic as one GPU, so the tokens are equal. MLP TP: both expert ranks hold
+    every expert with half of the intermediate dimension and return partial rows that the attention
+    side sums (bf16 partials: compared with a tolerance on the tokens)."""
+    if torch.cuda.device_count() < 4:
+        pytest.skip("needs 4 GPUs")
+    import torch.multiprocessing as mp
+    from fastafd_b200.core import SamplingParams
+    from fastafd_b200.engine import AfdEngine, SpmdDriver
+    from fastafd_b200.protocol import AfdTopology
+
+    cfg, n_new = _cfg(), 16
+    single = AfdEngine(cfg, _rt(), AfdTopology(colocated=True), 0, "cuda:0", seed=0)
+    exp = SpmdDriver(single).generate(_prompts(cfg), SamplingParams(max_tokens=n_new, ignore_eos=True))
+    single.close()
+    with tempfile.TemporaryDirectory() as d:
+        path = os.path.join(d, "out.pt")
+        mp.spawn(_topo_worker, args=(4, _free_port(), path, n_new, topo_kw), nprocs=4, join=True)
+        got = torch.load(path)
+    if exact:
+        assert got == exp
+    else:
+        first = sum(g[0] == e[0] for g, e in zip(got, exp))
+        same = sum(a == b for g, e in zip(got, exp) for a, b in zip(g, e))
+        assert first >= len(exp) - 1, (got, exp)
+        assert same >= 0.5 * sum(len(e) for e in exp), (got, exp)

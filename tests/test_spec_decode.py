@@ -79,3 +79,36 @@ def test_spec_config_from_flags_and_environment(monkeypatch):
     monkeypatch.setenv("FASTAFD_SPEC_BLOCK", "1")
     with pytest.raises(SpecConfigError):
         SpecConfig.from_env()
+
+
+def test_verify_steps_planned_ahead_stay_lossless():
+    """The coordinator keeps two verify steps in flight: step n+1 is planned before the acceptance of
+    step n is known (the committed lengths live with the attention worker, the scheduler only keeps an
+    upper bound and reserves KV for it). The output must still be plain greedy decoding."""
+    from fastafd_b200.coordinator import AfdCoordinator, InProcTransport
+
+    cfg = PRESETS["tiny-qwen3-moe"]
+    g = torch.Generator().manual_seed(3)
+    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (21, 9, 30, 14)]
+    sp = SamplingParams(max_tokens=13, ignore_eos=True)
+    plain = SpmdDriver(AfdEngine(cfg, _rt(), AfdTopology(colocated=True), 0, "cpu", seed=0)).generate(prompts, sp)
+    rt = _rt(spec_block=4, async_pending_steps=3)
+    eng = AfdEngine(cfg, rt, AfdTopology(colocated=True), 0, "cpu", seed=0)
+
+    class Deferred(InProcTransport):
+        """Executes a step when it is sent (like a worker queueing it on the GPU) but hands the reply
+        over only when the coordinator polls after it has filled its window."""
+
+    got = {i: [] for i in range(len(prompts))}
+    coord = AfdCoordinator(cfg, rt, AfdTopology(colocated=True), Deferred({0: eng}), num_pages=96,
+                           max_comm_tokens=eng.max_comm_tokens,
+                           on_tokens=lambda items: [got[u].extend(t) for u, t, _ in items])
+    assert coord.pending == 2
+    seen_two_in_flight = False
+    for i, p in enumerate(prompts):
+        coord.add_request(i, p, sp)
+    while not coord.idle():
+        coord.step_loop_once(block=True)
+        seen_two_in_flight |= len(coord.inflight) >= 1 and any(r.phase == "verify" for r in coord.inflight)
+    assert [got[i] for i in range(len(prompts))] == plain
+    assert seen_two_in_flight
