@@ -63,7 +63,7 @@ __global__ void __launch_bounds__(256) cross_head_norm_rope_store_kernel(
   }
   const float* cs = cos_sin + static_cast<size_t>(pos) * rot_dim;
   const int half = rot_dim / 2;
-  const long slot = out_loc[tok];
+  const long slot = k_cache != nullptr ? out_loc[tok] : -1;
   for (int h = warp; h < Hq + 2 * Hkv; h += nw) {
     __nv_bfloat16* p = row + h * D;
     const bool is_q = h < Hq, is_k = !is_q && h < Hq + Hkv;

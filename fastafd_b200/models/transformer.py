@@ -141,6 +141,7 @@ class AttentionStage:
                 self.lin_index[i] = len(self.lin_index)
         self.cos_sin: Optional[Tensor] = None
         self.status: Optional[Tensor] = None      # device status word of the process (set by the worker)
+        self.cad = None                           # cad.gpu.CadModelHook: the attention core runs on other GPUs
         self.w_fp8: Dict[str, Tuple[Tensor, Tensor]] = {}
         self.vocab_local = (cfg.vocab_size + tp_size - 1) // tp_size
         self.vocab_start = tp_rank * self.vocab_local
@@ -339,6 +340,9 @@ class AttentionStage:
             qkv = torch.cat([q_part, kv_part], dim=-1).contiguous()
         li = self.full_index[layer]
         kc, vc = kv.k[li], kv.v[li]
+        remote = self.cad is not None and not meta.is_prefill and qkv.is_cuda
+        if remote:
+            kc = vc = None            # core-attention disaggregation: K/V are stored by the attention GPUs
         qw, kw = self.qk_w.get(layer, (None, None))
         if c.qk_norm == "cross_head" and qkv.is_cuda:
             # one launch: joint RMSNorm over the q heads / k heads + RoPE + paged store
@@ -357,7 +361,9 @@ class AttentionStage:
                                    D, c.rotary_dim, c.rms_eps, status=meta.status)
         q = qkv.view(T, -1, D)[:, :self.hq]
         scale = ref.softmax_scale(D)
-        if meta.is_prefill:
+        if remote:
+            o = self.cad.attention(layer, meta.lane, qkv[:, :nqkv] if qkv.shape[1] != nqkv else qkv)
+        elif meta.is_prefill:
             o = self._prefill_attention(q, kc, vc, meta, scale, kv.page_size)
         else:
             o = ops.decode_attention(q, kc, vc, meta.page_table, meta.seq_lens, self.hq, self.hkv, D,

@@ -269,7 +269,7 @@ def pick_attn_splits(B: int, Hkv: int, m_tiles: int, max_kv: int, D: int = 128) 
 
 
 def decode_attention(q, k_cache, v_cache, page_table, seq_lens, Hq, Hkv, D, q_len, page_size,
-                     sm_scale, splits: int = 1, workspace=None, out=None, status=None):
+                     sm_scale, splits: int = 1, workspace=None, out=None, status=None, out_ptr: Optional[int] = None):
     """Paged GQA decode attention. q [B*q_len, Hq, D] bf16 (rows may be strided, e.g. a view
     into a merged qkv buffer); caches [slots, Hkv, D]. Returns a contiguous [B*q_len, Hq, D]."""
     if not q.is_cuda:
@@ -278,11 +278,14 @@ def decode_attention(q, k_cache, v_cache, page_table, seq_lens, Hq, Hkv, D, q_le
     B = seq_lens.shape[0]
     if q.stride(2) != 1 or q.stride(1) != D:
         q = q.contiguous()
-    out = torch.empty(q.shape, dtype=q.dtype, device=q.device) if out is None else out
+    if out_ptr is None:
+        out = torch.empty(q.shape, dtype=q.dtype, device=q.device) if out is None else out
+        out_ptr = ptr(out)
+    # (`out_ptr`: a raw device address for the [B*q_len, Hq, D] result, e.g. a peer GPU's buffer)
     if splits > 1 and workspace is None:
         workspace = decode_attn_workspace(B, Hq, Hkv, q_len, D, splits, q.device)
     check(lib().afd_decode_attention_strided(ptr(q), q.stride(0), ptr(k_cache), ptr(v_cache), ptr(page_table),
-                                     ptr(seq_lens), ptr(out), ptr(workspace), B, Hq, Hkv, D, q_len,
+                                     ptr(seq_lens), out_ptr, ptr(workspace), B, Hq, Hkv, D, q_len,
                                      page_size, page_table.shape[1], k_cache.shape[0], splits,
                                      sm_scale, ptr(status), cur_stream()), "decode_attention")
     return out
