@@ -350,11 +350,15 @@ def main():
                                                      "tensor-parallel over N GPUs (token-sharded residual, collectives fused with the GEMMs)",
                        "layers": cfg.num_layers, "truncated_model": truncated},
             "clocks": clocks,
-            "e2e": {"value": round(e2e_value, 2), "unit": "tok/s", "ms_per_step": round(e2e_ms / args.steps, 4),
+            # end to end through the public engine API in its serving mode (one step ahead): every step is
+            # planned on the host, its inputs are copied from pinned memory, the graph is replayed and the
+            # sampled tokens are read back; step n+1 is planned and copied while step n runs
+            "e2e": {"value": round(tokens / (ahead_ms / 1e3), 2), "unit": "tok/s", "ms_per_step": round(ahead_ms / args.steps, 4),
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-                    "how": "SpmdDriver.run_decode_steps(pipelined=False): host plan -> pinned H2D -> graph replay -> D2H tokens -> host completion, per step",
-                    "one_step_ahead": {"value": round(tokens / (ahead_ms / 1e3), 2), "ms_per_step": round(ahead_ms / args.steps, 4),
-                                       "how": "wall clock of run_decode_steps(pipelined=True), the serving default: step n+1 planned and copied while step n runs"}},
+                    "how": "wall clock of SpmdDriver.run_decode_steps(pipelined=True), the serving default: host plan -> pinned "
+                           "H2D -> graph replay -> D2H tokens -> host completion per step, step n+1 planned and copied while step n runs",
+                    "lock_step": {"value": round(e2e_value, 2), "ms_per_step": round(e2e_ms / args.steps, 4),
+                                  "how": "the same with run_decode_steps(pipelined=False): nothing of step n+1 starts before step n's tokens are on the host"}},
             "gpu_launches": kernels_per_step * args.steps,
             "kernels_per_step_rank0": kernels_per_step,
             "device_status": status, "build_s": round(build_s, 1),
