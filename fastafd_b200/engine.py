@@ -218,6 +218,7 @@ class AfdEngine:
             tp_rank = 0 if self.colocated else topo.attn_tp_rank(rank)
             self.attn = AttentionWorker(cfg, rt, self.device, client, tp_rank=tp_rank, tp_size=topo.attn_tp,
                                         tp_comm=tp_comm, dtype=self.dtype, rank=rank, max_bucket=cap, status=sw,
+                                        dp_lane=0 if self.colocated else topo.attn_lane(rank),
                                         weight_init=self._attention_weight_init(ckpt, seed, fast_init))
         if self.attn is not None and rt.spec_block > 1:
 

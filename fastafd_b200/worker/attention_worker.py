@@ -100,9 +100,11 @@ def determine_num_pages(cfg: ModelConfig, rt: RuntimeConfig, device: torch.devic
 class AttentionWorker:
     def __init__(self, cfg: ModelConfig, rt: RuntimeConfig, device, client: MoeClient, *, num_pages: int = 0,
                  tp_rank: int = 0, tp_size: int = 1, tp_comm=None, dtype=None, rank: int = 0,
-                 max_bucket: Optional[int] = None, weight_init=None, status: Optional[torch.Tensor] = None):
+                 max_bucket: Optional[int] = None, weight_init=None, status: Optional[torch.Tensor] = None,
+                 dp_lane: int = 0):
         self.cfg, self.rt, self.device, self.client, self.rank = cfg, rt, torch.device(device), client, rank
         self.cuda = self.device.type == "cuda"
+        self.dp_lane = dp_lane          # data-parallel lane this rank serves (all its TP ranks share it)
         self.dtype = dtype or (torch.bfloat16 if self.cuda else torch.float32)
         from ..parallel.comm import TpComm
 
@@ -451,6 +453,14 @@ class AttentionWorker:
             status = self.read_status()
         return AgStepReply(step_id=plan.step_id, rank=self.rank, next_tokens=toks.astype(np.int32), status=status)
 
+    def sampling_generator(self, step_id: int, mb: int) -> torch.Generator:
+        """Random stream of one (step, micro-batch): a function of the configured seed, the DP lane,
+        the step id and the micro-batch only - the same on every tensor-parallel rank of the lane (they
+        must sample the same tokens) and reproducible from `--seed`, whatever else drew random numbers."""
+        g = torch.Generator(device=self.device)
+        g.manual_seed((int(self.rt.seed) * 1000003 + self.dp_lane * 7919 + mb) * 2654435761 % (1 << 62) + int(step_id))
+        return g
+
     def _resample(self, plan: AgStepPlan) -> None:
         off = 0
         for lane in range(self.num_mb):
@@ -458,7 +468,8 @@ class AttentionWorker:
             t = torch.from_numpy(plan.temperatures[off:off + n]).to(self.device)
             if bool((t > 0).any()):
                 toks = ops.sample(b.logits, t, torch.from_numpy(plan.top_ks[off:off + n]).to(self.device),
-                                  torch.from_numpy(plan.top_ps[off:off + n]).to(self.device))
+                                  torch.from_numpy(plan.top_ps[off:off + n]).to(self.device),
+                                  generator=self.sampling_generator(plan.step_id, lane))
                 b.next_tokens[:n].copy_(toks)
                 self.token_pool[b.rows[:n], b.seq_lens[:n].long()] = b.next_tokens[:n]
             off += n
@@ -514,7 +525,8 @@ class AttentionWorker:
                         temps = torch.from_numpy(plan.temperatures[base:base + B][mask]).to(dev)
                         if bool((temps > 0).any()):
                             t = ops.sample(logits, temps, torch.from_numpy(plan.top_ks[base:base + B][mask]).to(dev),
-                                           torch.from_numpy(plan.top_ps[base:base + B][mask]).to(dev))
+                                           torch.from_numpy(plan.top_ps[base:base + B][mask]).to(dev),
+                                           generator=self.sampling_generator(plan.step_id, lane))
                     rows_s = torch.from_numpy(mbp.rows[mbp.sample_rows].astype(np.int64)).to(dev)
                     lens_s = torch.from_numpy(mbp.seq_lens[mbp.sample_rows].astype(np.int64)).to(dev)
                     self.token_pool[rows_s, lens_s] = t.to(torch.int32)

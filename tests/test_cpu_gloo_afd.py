@@ -101,3 +101,37 @@ def test_decode_step_driver_keeps_ranks_in_step_with_shadow_lanes():
         assert res[r].tolist() == [24, 24, 0, 0]
     for r in range(2, 4):                                # expert ranks produce no tokens but see the same drain
         assert res[r].tolist() == [0, 0, 0, 0]
+
+
+def _sampling_worker(rank, world, port, out_dir, seed, extra_draw_on):
+    os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    torch.set_num_threads(1)
+    cfg = PRESETS["tiny-qwen3-moe"]
+    rt = _rt()
+    rt.seed = seed
+    if rank == extra_draw_on:
+        torch.rand(7)                     # an unrelated draw on ONE rank must not desynchronise the lane
+    eng = AfdEngine(cfg, rt, AfdTopology(attn_dp=1, attn_tp=2, mlp_ep=2), rank, "cpu", seed=0)
+    sp = SamplingParams(max_tokens=10, ignore_eos=True, temperature=0.9, top_k=40, top_p=0.95)
+    out = SpmdDriver(eng).generate(_prompts(cfg), sp)
+    if eng.attn is not None:
+        # what this TP rank itself sampled sits in its token pool: rows of the first request
+        torch.save({"out": out, "pool": eng.attn.token_pool[:4, 32:42].clone()}, os.path.join(out_dir, f"r{rank}.pt"))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_sampled_tokens_agree_across_tp_ranks_and_follow_the_seed():
+    """Temperature sampling under attention TP: every TP rank of a lane draws from a generator seeded
+    by (seed, lane, step, micro-batch), so the ranks pick the same tokens even if one of them consumed
+    other random numbers, and the output is a function of --seed."""
+    runs = {}
+    for seed, extra in ((5, 0), (5, 1), (6, -1)):
+        with tempfile.TemporaryDirectory() as d:
+            mp.spawn(_sampling_worker, args=(4, _free_port(), d, seed, extra), nprocs=4, join=True)
+            r0, r1 = torch.load(os.path.join(d, "r0.pt")), torch.load(os.path.join(d, "r1.pt"))
+        assert torch.equal(r0["pool"], r1["pool"])             # both TP ranks wrote the same sampled tokens
+        runs[(seed, extra)] = r0["out"]
+    assert runs[(5, 0)] == runs[(5, 1)]                        # same seed -> same tokens, whoever drew extra numbers
+    assert runs[(5, 0)] != runs[(6, -1)]                       # another seed -> other tokens
