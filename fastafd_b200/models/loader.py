@@ -93,24 +93,31 @@ def load_attention_stage(stage: AttentionStage, path: str) -> None:
             scales[k[:-len("_scale_inv")]] = t
         else:
             raw[k] = t
+    was_fp8 = set()
     for k in list(raw):
         if k in scales or raw[k].dtype == torch.float8_e4m3fn:
-            raw[k] = _dequant_if_fp8(raw[k], scales.get(k))
+            raw[k] = _dequant_if_fp8(raw[k], scales.get(k))       # exact in fp32: code x block scale
+            was_fp8.add(k)
     full: Dict[str, torch.Tensor] = {}
     for i in range(cfg.num_layers):
         p = f"model.layers.{i}."
         a = p + "self_attn."
         if a + "q_proj.weight" in raw:
+            if a + "q_proj.weight" in was_fp8:
+                was_fp8.add(a + "qkv_proj.weight")
             full[a + "qkv_proj.weight"] = torch.cat([raw.pop(a + n + ".weight") for n in ("q_proj", "k_proj", "v_proj")], 0)
             if a + "q_proj.bias" in raw:
                 full[a + "qkv_proj.bias"] = torch.cat([raw.pop(a + n + ".bias") for n in ("q_proj", "k_proj", "v_proj")], 0)
         for m in (p + "mlp.", p + "mlp.shared_expert."):
             if m + "gate_proj.weight" in raw:
+                if m + "gate_proj.weight" in was_fp8:
+                    was_fp8.add(m + "gate_up_proj.weight")
                 full[m + "gate_up_proj.weight"] = torch.cat([raw.pop(m + "gate_proj.weight"), raw.pop(m + "up_proj.weight")], 0)
     full.update(raw)
     if cfg.tie_embeddings:
         full.pop("lm_head.weight", None)
     state = {}
+    fp8_src = {}
     for name, (shape, kind) in need.items():
         if name not in full:
             raise KeyError(f"checkpoint lacks {name}")
@@ -118,7 +125,15 @@ def load_attention_stage(stage: AttentionStage, path: str) -> None:
         if tuple(t.shape) != tuple(shape):
             raise ValueError(f"{name}: checkpoint shape {tuple(t.shape)} != expected {shape}")
         state[name] = t
+        if name in was_fp8:
+            # The dense projection was block-FP8 in the checkpoint. Its fp32 values (code x scale) go to the
+            # stage beside the bf16 copy: re-quantising a 128x128-aligned shard of them gives back the
+            # checkpoint's codes and scales (the block maximum is +-448 x scale by construction), so the
+            # GPU keeps the checkpoint's own e4m3 weights instead of a bf16 rounding of them.
+            fp8_src[name] = t.float()
+    stage._fp8_src = fp8_src
     stage.load_state(state)
+    stage._fp8_src = {}
 
 
 def load_expert_stage(stage: ExpertStage, path: str) -> None:

@@ -277,7 +277,8 @@ class AttentionStage:
                 continue
             if w.dtype != torch.bfloat16 or w.shape[0] % 128 or w.shape[1] % 128 or not c.quant.applies_to(name):
                 continue
-            q, sc = ref.block_quant_fp8(w.float())
+            src = getattr(self, "_fp8_src", {}).get(name)         # the checkpoint's exact values, when it was FP8
+            q, sc = ref.block_quant_fp8(src.to(self.device) if src is not None else w.float())
             self.w_fp8[name] = (q.contiguous(), ops.plain_tile_scales(sc[None].float()).contiguous())
 
     def _proj(self, x: Tensor, name: str, bias: Optional[Tensor] = None) -> Tensor:
