@@ -58,6 +58,8 @@ def parse_args():
     ap.add_argument("--attn-tp", type=int, default=1, help="tensor-parallel size of an attention DP lane")
     ap.add_argument("--router-bias", default="", help="zipf:S - router selection bias drawn so that expert popularity follows "
                                                       "Zipf(S) (models with a selection bias, e.g. minimax-m2.5-fp8)")
+    ap.add_argument("--also-router-bias", default="", help="after the main measurement, apply this router bias (zipf:S) in the "
+                                                           "same process and time the decode steps again (extra JSON field)")
     ap.add_argument("--spec-block", type=int, default=0, help="speculative decoding: verified tokens per step (drafts + 1)")
     ap.add_argument("--spec-sim-accept", type=float, default=0.0, help="fixed mean acceptance (tokens per verify step) for timing runs")
     return ap.parse_args()
@@ -185,7 +187,7 @@ def main():
     lane_b = b * tp                      # a TP lane serves tp GPUs' worth of requests
     per_mb = (lane_b + args.num_mb - 1) // args.num_mb
     per_mb = (per_mb + tp - 1) // tp * tp
-    total_steps = 3 * args.steps + 2 * args.warmup + 8
+    total_steps = (4 if args.also_router_bias else 3) * args.steps + 2 * args.warmup + 12
     q = args.spec_block if args.spec_block > 1 else 1
     if q > 1:
         os.environ["FASTAFD_SPEC_SIM_ACCEPT"] = str(args.spec_sim_accept or 0)
@@ -259,6 +261,21 @@ def main():
     barrier()
     ahead_ms = max_over_ranks(ahead_ms)
     status = eng.synchronize()
+    skewed = None
+    if args.also_router_bias:
+        apply_router_bias(eng, cfg, args.also_router_bias)
+        barrier()
+        drv.run_decode_steps(3, pipelined=True)
+        barrier()
+        ev2, ev3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev2.record(stream)
+        drv.run_decode_steps(args.steps, pipelined=True)
+        ev3.record(stream)
+        torch.cuda.synchronize()
+        skew_ms = max_over_ranks(ev2.elapsed_time(ev3))
+        barrier()
+        status = status or eng.synchronize()
+        skewed = {"router_bias": args.also_router_bias, "ms_per_step": round(skew_ms / args.steps, 4)}
 
     trace_info = None
     if os.environ.get("FASTAFD_COMM_TRACE") == "1" and cfg.is_moe:
@@ -367,6 +384,9 @@ def main():
             out["speculative"] = spec_info
         if args.router_bias:
             out["config"]["router_bias"] = args.router_bias
+        if skewed is not None:
+            skewed["value"] = round(tokens / (skewed["ms_per_step"] * args.steps / 1e3), 2)
+            out["skewed_routing"] = skewed
         if comm is not None:
             out["n2m_m2n"] = comm
         if trace_info is not None and os.environ.get("FASTAFD_COMM_TRACE_FULL") == "1":
