@@ -364,7 +364,30 @@ class AttentionWorker:
         self._pipeline(mbs)
         for lane, mb in enumerate(mbs):
             self._sample_and_writeback(lane, mb, bucket)
+        if self.model.cad is not None:
+            self.model.cad.end_step()          # core-attention disaggregation: the epoch bump closes the step
         self._last_mbs = mbs
+
+    def cad_serve_step(self, plan: AgStepPlan, server) -> None:
+        """Attention-GPU side of a core-attention-disaggregated decode step: this process holds the KV
+        cache and the page table, takes the same plan as the model GPU, and serves every (layer,
+        micro-batch) hop in program order (`server`: cad.gpu.CadAttentionServer bound to this
+        worker's KV pool)."""
+        bucket = plan.bucket
+        with torch.cuda.stream(self.main_stream):
+            self.apply_grants(plan)
+            self._stage_decode(plan)
+            for lane in range(self.num_mb):
+                self._prepare_decode_inputs(lane, bucket)
+                b = self.bufs[lane]
+                server.n_rows[lane] = bucket
+                server.out_loc[lane], server.seq_lens[lane], server.page_table[lane] = b.out_loc, b.seq_lens, b.page_table[:bucket]
+            for layer in range(self.cfg.num_layers):
+                if self.cfg.layer_type(layer) != "full":
+                    continue
+                for lane in range(self.num_mb):
+                    server.serve(layer, lane)
+            server.end_step()
 
     def capture_decode_graph(self, bucket: int) -> None:
         """Warm up eagerly (sets kernel attributes, primes allocators), then capture the whole

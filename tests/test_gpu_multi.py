@@ -217,3 +217,92 @@ def test_mlp_replicas_and_mlp_tensor_parallel_on_gpus(topo_kw, exact):
         same = sum(a == b for g, e in zip(got, exp) for a, b in zip(g, e))
         assert first >= len(exp) - 1, (got, exp)
         assert same >= 0.5 * sum(len(e) for e in exp), (got, exp)
+
+
+def _cad_worker(rank, world, port, out_path, steps):
+    """rank 0: model GPU (everything but the attention core); rank 1: attention GPU (KV cache, page
+    table, decode attention). Both hold the same scheduler state, so they plan the same steps."""
+    import torch.distributed as dist
+    from fastafd_b200.cad.gpu import CadAttentionServer, CadModelHook, attention_window_layout, model_window_layout
+    from fastafd_b200.engine import AfdEngine, SpmdDriver
+    from fastafd_b200.parallel.fabric import Fabric
+    from fastafd_b200.protocol import AfdTopology
+    from fastafd_b200.scheduler.buckets import per_mb_real, select_bucket
+
+    os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    cfg = _cfg()
+    rt = _rt()
+    rt.use_cuda_graph = False
+    rt.decode_graph_bs = (8,)
+    eng = AfdEngine(cfg, rt, AfdTopology(colocated=True), 0, dev, seed=0)
+    drv = SpmdDriver(eng)
+    drv.install_prefilled(12, 40, max_tokens=64)
+    w = eng.attn
+    lanes, cap = w.num_mb, w.cap
+    size = max(model_window_layout(cfg, 1, lanes, cap).size, attention_window_layout(cfg, lanes, cap).size)
+    fab = Fabric.ipc(size, dev, None)
+    toks = []
+    if rank == 0:
+        hook = CadModelHook(cfg, fab, [1], lanes, cap, servers=None, timeout_ns=int(5e9))
+        for lane in range(lanes):
+            hook.set_step(lane, torch.zeros(cap, dtype=torch.int32, device=dev))
+        w.model.cad = hook
+        dist.barrier()
+        for _ in range(steps):
+            drv.run_decode_steps(1, pipelined=False)
+            toks.append(torch.cat([b.next_tokens.clone() for b in w.bufs]).cpu())
+        hook.check()
+        torch.save(torch.stack(toks), out_path)
+    else:
+        server = CadAttentionServer(cfg, fab, model_rank=0, index=0, num_attn=1, num_lanes=lanes, max_tokens=cap,
+                                    num_pages=2, page_size=w.page_size, timeout_ns=int(5e9))
+        server.k, server.v = w.kv.k, w.kv.v
+        dist.barrier()
+        lane_sched = drv.lanes[0]
+        for sid in range(steps):
+            real = lane_sched.decode_real()
+            bucket = select_bucket(per_mb_real(real, rt.num_mb), eng.buckets)
+            plan = lane_sched.schedule_decode(drv.step_id, bucket)
+            drv.step_id += 1
+            w.cad_serve_step(plan, server)
+            torch.cuda.synchronize()
+            # this side never learns the tokens: advance its scheduler as if one token per request came back
+            import numpy as np
+            lane_sched.complete(plan.step_id, np.zeros(sum(len(mb.rows) for mb in plan.mbs), np.int32))
+        server.check()
+    dist.barrier()
+    eng.close()
+    fab.close()
+    dist.destroy_process_group()
+
+
+def test_core_attention_disaggregation_on_two_gpus():
+    """CAD across two GPUs: the model GPU puts q|k|v rows into the attention GPU's window, the
+    attention GPU stores K/V, attends and writes the output rows straight back into the model GPU's
+    window (peer stores from the attention kernel). Same tokens as the all-local engine."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import torch.multiprocessing as mp
+    from fastafd_b200.engine import AfdEngine, SpmdDriver
+    from fastafd_b200.protocol import AfdTopology
+
+    cfg, steps = _cfg(), 6
+    rt = _rt()
+    rt.use_cuda_graph = False
+    rt.decode_graph_bs = (8,)
+    single = AfdEngine(cfg, rt, AfdTopology(colocated=True), 0, "cuda:0", seed=0)
+    drv = SpmdDriver(single)
+    drv.install_prefilled(12, 40, max_tokens=64)
+    want = []
+    for _ in range(steps):
+        drv.run_decode_steps(1, pipelined=False)
+        want.append(torch.cat([b.next_tokens.clone() for b in single.attn.bufs]).cpu())
+    single.close()
+    with tempfile.TemporaryDirectory() as d:
+        path = os.path.join(d, "out.pt")
+        mp.spawn(_cad_worker, args=(2, _free_port(), path, steps), nprocs=2, join=True)
+        got = torch.load(path)
+    assert torch.equal(got, torch.stack(want))
