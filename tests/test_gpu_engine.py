@@ -92,8 +92,8 @@ def test_smoke_entry():
     run_smoke()
 
 
-@pytest.mark.parametrize("block", [2, 4])
-def test_speculative_decoding_on_gpu_tracks_plain_greedy(block):
+@pytest.mark.parametrize("block,graph", [(2, False), (4, False), (4, True)], ids=["block2-eager", "block4-eager", "block4-graph"])
+def test_speculative_decoding_on_gpu_tracks_plain_greedy(block, graph):
     """EAGLE-3 style verify steps on the GPU (multi-token attention kernel, dispatch with a given
     routing, greedy acceptance): the emitted tokens are the target model's own greedy tokens, so
     they must follow plain greedy decoding. In bf16 a verify step scores several positions in one
@@ -107,7 +107,8 @@ def test_speculative_decoding_on_gpu_tracks_plain_greedy(block):
     plain_eng = AfdEngine(cfg, _rt("cuda:0", False, **kw), AfdTopology(colocated=True), 0, "cuda:0", seed=0)
     plain = SpmdDriver(plain_eng).generate(prompts, sp)
     plain_eng.close()
-    eng = AfdEngine(cfg, _rt("cuda:0", False, spec_block=block, **kw), AfdTopology(colocated=True), 0, "cuda:0", seed=0)
+    # graph: the whole verify step (target pipeline, head + acceptance, draft chain) is one captured graph
+    eng = AfdEngine(cfg, _rt("cuda:0", graph, spec_block=block, **kw), AfdTopology(colocated=True), 0, "cuda:0", seed=0)
     spec = SpmdDriver(eng).generate(prompts, sp)
     hist, mean = eng.attn.spec.accept_hist.sum(), eng.attn.spec.mean_accept()
     eng.close()
