@@ -65,7 +65,7 @@ class Sim:
             _, pkey, slots, flag_keys = op
             e = self.publish.setdefault(pkey, 1)
             for s in slots:
-                if self.slot_written.get(s, 0) > self.slot_consumed.get(s, 0):
+                if getattr(self, "check_races", True) and self.slot_written.get(s, 0) > self.slot_consumed.get(s, 0):
                     raise Race(f"{name}: slot {s} overwritten (epoch {e}) before epoch {self.slot_written[s]} was read")
                 self.slot_written[s] = e
             for k in flag_keys:
@@ -199,3 +199,52 @@ def test_reduce_scatter_without_anything_in_between_is_a_race():
         except Race:
             hit += 1
     assert hit > 0
+
+
+def _run_with_timeouts(sim, rank_of):
+    """Like Sim.run, with the failure behaviour of the kernels: when nothing can move, every stream
+    whose head is an unsatisfied flag wait lets that wait run out (one time limit passes for all of
+    them at once, they wait in parallel); the rank's status word is then set, and every later flag
+    wait of that rank returns at once (all its communicators share the word). Returns the number of
+    time limits that passed and the set of ranks whose status word is set."""
+    names = list(sim.streams)
+    failed, limits = set(), 0
+    while any(sim.pos[n] < len(sim.streams[n]) for n in names):
+        sim.rng.shuffle(names)
+        moved = False
+        for n in names:
+            i = sim.pos[n]
+            if i < len(sim.streams[n]) and sim.streams[n][i][0] == "wait" and rank_of(n) in failed:
+                _, keys, ekey = sim.streams[n][i]          # status already set: the wait gives up at once
+                sim.expect[ekey] = sim.expect.setdefault(ekey, 1) + 1
+                sim.pos[n] = i + 1
+                moved = True
+            elif sim.step(n):
+                moved = True
+        if moved:
+            continue
+        stuck = [n for n in names if sim.pos[n] < len(sim.streams[n]) and sim.streams[n][sim.pos[n]][0] == "wait"]
+        if not stuck:
+            raise Deadlock("stuck without a waiting kernel")
+        limits += 1
+        sim.check_races = False          # a failed step's data is discarded; only termination matters from here
+        for n in stuck:
+            failed.add(rank_of(n))
+        assert limits <= 8, "time-outs keep cascading"
+    return limits, failed
+
+
+@pytest.mark.parametrize("drop", [3, 5, 12])
+def test_a_withheld_flag_ends_the_step_on_all_eight_ranks_within_two_time_limits(drop):
+    """4 attention TP ranks + 4 expert ranks, one flag release withheld. The ranks that wait for it
+    give up after one time limit and set their status word; everything they do afterwards drains
+    without waiting (their flags are still released, with garbage behind them), so no rank waits for
+    a second full limit in sequence: the whole step ends on all eight ranks after at most two limits,
+    and at least one rank carries the error that the step's token exchange then spreads."""
+    for seed in range(10):
+        sim = Sim(seed)
+        build(sim, tp=4, n_eg=4, lanes=2, layers=3, steps=1, drop_release=drop)
+        limits, failed = _run_with_timeouts(sim, lambda n: n.split(".")[0])
+        assert all(sim.pos[n] == len(sim.streams[n]) for n in sim.streams)       # every rank returned
+        assert 1 <= limits <= 2, limits
+        assert failed, "nobody noticed the withheld flag"
