@@ -78,6 +78,33 @@ def reference_arm(args) -> None:
         print(json.dumps(out), flush=True)
 
 
+def pick_num_mb(cfg, topo, batch_per_attn_gpu: int, context: int) -> int:
+    """1 or 2 micro-batches from a two-term model of a layer (times in us, constants fitted to the
+    device timelines measured on B200). A second micro-batch hides the expert round trip behind the
+    other one's attention, but every micro-batch streams the expert weights again, so it pays only
+    when an expert GPU's weight stream per pass is short next to the attention-side chain:
+        chain(b)  = 35 + KV bytes of b requests / 5.0 TB/s      attention GPU, one micro-batch of b requests
+        expert    = 12 + local expert bytes / 6.0 TB/s          expert GPU, one pass over its experts
+        2 micro-batches: max(2 x expert, chain(b/2) + expert + 20)   per layer
+        1 micro-batch  : chain(b) + expert + 20
+    Measured: 1+1 GPUs 12.7 ms (1) against 16.8 ms (2); 4+4 GPUs 7.2 ms with 2."""
+    if topo.colocated or not cfg.is_moe:
+        return 1
+    wbytes = 1 if cfg.quant.is_fp8 else 2
+    e_local = (cfg.num_experts + topo.mlp_ep - 1) // topo.mlp_ep
+    expert_us = 12 + e_local * 3 * cfg.moe_intermediate_size * cfg.hidden_size * wbytes / 6.0e6
+    kv_per_req = context * max(1, cfg.num_kv_heads // topo.attn_tp) * cfg.head_dim * 2 * 2 * (
+        cfg.num_full_attn_layers / max(cfg.num_layers, 1))
+
+    def chain(b):
+        return 35 + b * kv_per_req / 5.0e6
+
+    b = batch_per_attn_gpu
+    two = max(2 * expert_us, chain(b / 2) + expert_us + 20)
+    one = chain(b) + expert_us + 20
+    return 2 if two < one else 1
+
+
 def apply_router_bias(eng, cfg, spec: str) -> None:
     """`zipf:S`: the selection bias of every MoE layer is set so that expert popularity is skewed like a
     Zipf(S) law over the experts (a different expert order per layer): bias = popularity / max popularity,
@@ -168,8 +195,23 @@ def main():
         # round-trip and expert-busy times behind the n2m_m2n figures
         os.environ.setdefault("FASTAFD_COMM_TRACE", "1")
         os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
-        dist.init_process_group(backend="cpu:gloo,cuda:nccl", rank=rank, world_size=world, device_id=device)
+        # host-side group: plans, tokens, barriers (gloo). Device collectives use the framework's own
+        # NCCL communicator and fabric kernels, so torch needs no NCCL group of its own here.
+        dist.init_process_group(backend="gloo", rank=rank, world_size=world)
 
+    t_start = time.time()
+    # A step that cannot finish (a peer that never arrives) must end the run with an error and the
+    # Python stacks of every thread, not hold the GPUs until someone kills the job.
+    import faulthandler
+
+    watchdog_s = float(os.environ.get("FASTAFD_BENCH_WATCHDOG_S", "240"))
+
+    def phase(name: str) -> None:
+        print(f"[bench rank {rank}] {name} at +{time.time() - t_start:.1f}s", file=sys.stderr, flush=True)
+        if watchdog_s > 0:
+            faulthandler.dump_traceback_later(watchdog_s, exit=True)
+
+    phase("process group up")
     cfg = get_model_config(args.model)
     truncated = False
     if args.layers and args.layers < cfg.num_layers:
@@ -177,11 +219,7 @@ def main():
         truncated = True
     topo = AfdTopology.for_world(world, attn_tp=args.attn_tp, attn_gpus=args.attn_gpus)
     if args.num_mb <= 0:
-        # A second micro-batch hides the expert round trip behind the other one's attention, but
-        # every micro-batch streams the expert weights again: with a single expert GPU (all experts
-        # on it) that doubles the step's dominant cost, so one micro-batch is faster there
-        # (measured on 1+1 GPUs: 12.7 ms against 16.8 ms per step).
-        args.num_mb = 1 if (topo.colocated or topo.mlp_ep == 1) else 2
+        args.num_mb = pick_num_mb(cfg, topo, args.batch_per_attn_gpu, args.context)
     b = args.batch_per_attn_gpu
     tp = topo.attn_tp
     lane_b = b * tp                      # a TP lane serves tp GPUs' worth of requests
@@ -205,6 +243,8 @@ def main():
     torch.cuda.synchronize()
     build_s = time.time() - t_build
 
+    phase("engine built")
+
     def barrier():
         torch.cuda.synchronize()
         if world > 1:
@@ -221,6 +261,7 @@ def main():
     # ---- warm-up (captures the graphs) -------------------------------------------------
     drv.run_decode_steps(max(args.warmup, 3), pipelined=False)
     barrier()
+    phase("warm-up done")
 
     # ---- device-timed region: K steps queued back to back --------------------------------
     sampler = ClockSampler(local_rank)
@@ -244,6 +285,7 @@ def main():
     tpot_p50 = max_over_ranks(tpot_p50)
 
     # ---- end-to-end region: one step at a time through the public API ----------------------
+    phase("device-timed region done")
     barrier()
     t0 = time.perf_counter()
     drv.run_decode_steps(args.steps, pipelined=False)
@@ -261,6 +303,7 @@ def main():
     barrier()
     ahead_ms = max_over_ranks(ahead_ms)
     status = eng.synchronize()
+    phase("end-to-end regions done")
     skewed = None
     if args.also_router_bias:
         apply_router_bias(eng, cfg, args.also_router_bias)
@@ -398,6 +441,7 @@ def main():
         dist.barrier()
         dist.destroy_process_group()
     eng.close()
+    faulthandler.cancel_dump_traceback_later()
 
 
 if __name__ == "__main__":

@@ -67,23 +67,27 @@ def decode_buckets(rt: RuntimeConfig, topo: AfdTopology) -> List[int]:
 
 
 def make_tp_comms(topo: AfdTopology, rank: int, device: torch.device, group=None):
-    """One communicator per attention lane; every rank of the world takes part in creating each
-    group (torch.distributed requires it). Returns this rank's communicator or None."""
+    """One communicator per attention lane. Every rank of the world takes part in the set-up, in the
+    same order. On CUDA the lane leaders' NCCL ids travel in one all-gather over the host group and no
+    sub-group is made (torch's new_group on a default group that is bound to a device splits an NCCL
+    communicator on the non-member ranks only, and blocks there if the new group is a gloo group). On
+    CPU each lane gets a gloo sub-group. Returns this rank's communicator or None."""
     if topo.colocated or topo.attn_tp == 1:
         return None
     from .parallel.comm import NcclComm, TorchDistComm
 
+    lanes = [topo.attn_tp_group(lane) for lane in range(topo.attn_dp)]
+    if device.type == "cuda":
+        my_lane = next((r for r in lanes if rank in r), None)
+        uid = NcclComm.new_unique_id() if my_lane is not None and my_lane[0] == rank else None
+        ids = [None] * dist.get_world_size(group)
+        dist.all_gather_object(ids, uid, group=group)
+        return NcclComm(my_lane, device, uid=ids[my_lane[0]]) if my_lane is not None else None
     mine = None
-    for lane in range(topo.attn_dp):
-        ranks = topo.attn_tp_group(lane)
-        if device.type == "cuda":
-            g = dist.new_group(ranks, backend="gloo")
-            if rank in ranks:
-                mine = NcclComm(ranks, device, host_group=g)
-        else:
-            g = dist.new_group(ranks)
-            if rank in ranks:
-                mine = TorchDistComm(g, ranks)
+    for ranks in lanes:
+        g = dist.new_group(ranks)
+        if rank in ranks:
+            mine = TorchDistComm(g, ranks)
     return mine
 
 

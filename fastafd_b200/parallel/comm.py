@@ -83,25 +83,41 @@ class NcclError(RuntimeError):
 class NcclComm(TpComm):
     """Own NCCL communicator over `ranks` of the default (host-side) process group."""
 
-    def __init__(self, ranks: List[int], device: torch.device, host_group=None, max_buffer_bytes: int = 64 << 20):
+    @staticmethod
+    def _load():
         from ..build import build_nccl_wrapper, nccl_lib_path
 
         path = nccl_lib_path()
         if not path.exists():
             path = build_nccl_wrapper()
-        self.lib = C.CDLL(str(path))
-        self.lib.afd_nccl_error_string.restype = C.c_char_p
+        lib = C.CDLL(str(path))
+        lib.afd_nccl_error_string.restype = C.c_char_p
+        return lib
+
+    @classmethod
+    def new_unique_id(cls) -> bytes:
+        """A fresh NCCL unique id (128 bytes), made by the rank that will be rank 0 of the communicator."""
+        lib, uid = cls._load(), C.create_string_buffer(128)
+        code = lib.afd_nccl_unique_id(uid)
+        if code != 0:
+            raise NcclError(f"nccl unique_id: {lib.afd_nccl_error_string(code).decode()} ({code})")
+        return uid.raw
+
+    def __init__(self, ranks: List[int], device: torch.device, host_group=None, max_buffer_bytes: int = 64 << 20,
+                 uid: Optional[bytes] = None):
+        """`uid`: the unique id from the communicator's rank 0 (`new_unique_id`), already delivered to
+        every member; without it the id is broadcast over `host_group`, which must contain exactly `ranks`."""
+        self.lib = self._load()
         self.ranks, self.size, self.device = list(ranks), len(ranks), device
         me = dist.get_rank()
         self.rank = self.ranks.index(me)
-        uid = C.create_string_buffer(128)
-        if self.rank == 0:
-            self._check(self.lib.afd_nccl_unique_id(uid), "unique_id")
-        box = [uid.raw if self.rank == 0 else None]
-        dist.broadcast_object_list(box, src=self.ranks[0], group=host_group)
+        if uid is None:
+            box = [self.new_unique_id() if self.rank == 0 else None]
+            dist.broadcast_object_list(box, src=self.ranks[0], group=host_group)
+            uid = box[0]
         self.handle = C.c_void_p()
         with torch.cuda.device(device):
-            self._check(self.lib.afd_nccl_init(self.rank, self.size, C.create_string_buffer(box[0], 128),
+            self._check(self.lib.afd_nccl_init(self.rank, self.size, C.create_string_buffer(uid, 128),
                                                C.c_size_t(max_buffer_bytes), C.byref(self.handle)), "init")
 
     def _check(self, code: int, what: str) -> None:

@@ -42,8 +42,11 @@ def worker_main(rank: int, world: int, server_args, addrs: Dict[str, object], ma
         if world > 1:
             os.environ["MASTER_ADDR"] = str(addrs.get("master_addr", "127.0.0.1"))     # the head node under a multi-node launch
             os.environ["MASTER_PORT"] = str(master_port)
-            dist.init_process_group("cpu:gloo,cuda:nccl" if cuda else "gloo", rank=rank, world_size=world,
-                                    **({"device_id": device} if cuda else {}))
+            # The host-side group is gloo only: it carries plans, tokens and barriers. Device
+            # collectives go through the framework's own NCCL communicator / fabric kernels. (A default
+            # group bound to a device makes torch split its NCCL communicator inside new_group on
+            # non-member ranks only, which blocks when the new group itself is a gloo group.)
+            dist.init_process_group("gloo", rank=rank, world_size=world)
         engine = AfdEngine(cfg, rt, topo, rank, device, seed=server_args.seed, fast_init=cuda,
                            max_comm_tokens=addrs.get("max_comm_tokens"))
         cmd_q = ZmqPullQueue(addrs["cmd"][rank], bind=True, encode=encode, decode=decode)

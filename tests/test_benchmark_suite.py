@@ -90,3 +90,22 @@ def test_record_and_summary(tmp_path):
     (run_dir / "result.json").write_text(json.dumps({"verdict": "error", "returncode": 1}))
     with pytest.raises(ValueError):
         suite.record("qwen3-235b-8k-1to1", run_dir, cfg_copy)
+
+
+def test_bench_picks_micro_batches_from_the_layer_model():
+    """Two micro-batches only where an expert GPU's weight stream is short next to the attention chain."""
+    import importlib.util
+    import os
+
+    from fastafd_b200.config import get_model_config
+    from fastafd_b200.protocol import AfdTopology
+
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "bench.py")
+    spec = importlib.util.spec_from_file_location("bench_under_test", path)
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    cfg = get_model_config("qwen3-30b-a3b")
+    picks = {w: bench.pick_num_mb(cfg, AfdTopology.for_world(w), 64, 1024) for w in (1, 2, 4, 8)}
+    assert picks == {1: 1, 2: 1, 4: 1, 8: 2}
+    big = get_model_config("qwen3-235b-a22b-fp8")
+    assert bench.pick_num_mb(big, AfdTopology.for_world(8), 88, 8192) == 2
