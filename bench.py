@@ -434,6 +434,8 @@ def main():
             out["n2m_m2n"] = comm
         if trace_info is not None and os.environ.get("FASTAFD_COMM_TRACE_FULL") == "1":
             out["comm_trace"] = trace_info
+        if world == 8 and tp == 1:
+            out["config"]["deviation"] = "attention DP4, BASELINE names TP4 (--attn-tp 4 runs that configuration)"
         if truncated:
             out["invalid"] = "model truncated with --layers (debug run)"
         print(json.dumps(out))

@@ -21,7 +21,7 @@ __global__ void gdn_conv_step_kernel(const __nv_bfloat16* __restrict__ x, __nv_b
                                      const __nv_bfloat16* __restrict__ w,   // [C][W]
                                      __nv_bfloat16* conv_state,             // [slots][W-1][C]
                                      const int* __restrict__ slots, int T, int C, int W, int num_slots,
-                                     int* status) {
+                                     int* status, long x_ld) {
   const int t = blockIdx.y;
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= C) return;
@@ -31,7 +31,7 @@ __global__ void gdn_conv_step_kernel(const __nv_bfloat16* __restrict__ x, __nv_b
     return;
   }
   __nv_bfloat16* st = conv_state + static_cast<size_t>(slot) * (W - 1) * C + c;
-  const float xin = __bfloat162float(x[static_cast<size_t>(t) * C + c]);
+  const float xin = __bfloat162float(x[static_cast<size_t>(t) * x_ld + c]);
   float acc = xin * __bfloat162float(w[c * W + W - 1]);
   float prev[8];
   for (int i = 0; i < W - 1; ++i) {
@@ -52,7 +52,7 @@ __global__ void __launch_bounds__(256) gdn_recurrent_kernel(
     const __nv_bfloat16* __restrict__ norm_w,                                   // [Dv]
     float* rec_state,                        // [slots][Hv][Dv][DK]
     const int* __restrict__ slots, __nv_bfloat16* __restrict__ out, int T, int Hk, int Hv, int Dv, int num_slots,
-    float eps, int* status) {
+    float eps, int* status, long z_ld, long a_ld, long b_ld) {
   constexpr int PER = DK / 32;
   const int t = blockIdx.y, h = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
@@ -84,10 +84,10 @@ __global__ void __launch_bounds__(256) gdn_recurrent_kernel(
     q[i] *= qn;
     k[i] *= kn;
   }
-  const float av = __bfloat162float(a[static_cast<size_t>(t) * Hv + h]) + dt_bias[h];
+  const float av = __bfloat162float(a[static_cast<size_t>(t) * a_ld + h]) + dt_bias[h];
   const float sp = av > 20.f ? av : log1pf(expf(av));
   const float decay = expf(-expf(A_log[h]) * sp);
-  const float beta = 1.f / (1.f + expf(-__bfloat162float(b[static_cast<size_t>(t) * Hv + h])));
+  const float beta = 1.f / (1.f + expf(-__bfloat162float(b[static_cast<size_t>(t) * b_ld + h])));
   float* S = rec_state + (static_cast<size_t>(slot) * Hv + h) * Dv * DK;
   const __nv_bfloat16* vrow = row + 2 * Hk * DK + h * Dv;
   for (int r = warp; r < Dv; r += nw) {
@@ -122,7 +122,7 @@ __global__ void __launch_bounds__(256) gdn_recurrent_kernel(
   tot = warp_sum(tot);
   const float inv = rsqrtf(tot / Dv + eps);
   for (int r = threadIdx.x; r < Dv; r += blockDim.x) {
-    const float zz = __bfloat162float(z[(static_cast<size_t>(t) * Hv + h) * Dv + r]);
+    const float zz = __bfloat162float(z[static_cast<size_t>(t) * z_ld + static_cast<size_t>(h) * Dv + r]);
     out[(static_cast<size_t>(t) * Hv + h) * Dv + r] =
         __float2bfloat16(s_o[r] * inv * __bfloat162float(norm_w[r]) * silu(zz));
   }
@@ -295,22 +295,25 @@ __global__ void gdn_gated_norm_kernel(const __nv_bfloat16* __restrict__ o_raw, c
 
 }  // namespace afd
 
-// scratch: T * C bf16 (conv output). A_log / dt_bias fp32; everything else bf16.
-extern "C" int afd_gdn_decode(const void* mixed, const void* z, const void* a, const void* b, const void* conv_w,
-                              const void* A_log, const void* dt_bias, const void* norm_w, void* conv_state,
-                              void* rec_state, const void* slots, void* out, void* scratch, int T, int Hk, int Hv,
-                              int Dk, int Dv, int W, int num_slots, float eps, void* status, void* stream) {
+// scratch: T * C bf16 (conv output). A_log / dt_bias fp32; everything else bf16. ld_*: row strides in
+// elements of mixed, z, a and b, so that the four may be column ranges of one merged projection output.
+extern "C" int afd_gdn_decode_ld(const void* mixed, const void* z, const void* a, const void* b, const void* conv_w,
+                                 const void* A_log, const void* dt_bias, const void* norm_w, void* conv_state,
+                                 void* rec_state, const void* slots, void* out, void* scratch, int T, int Hk, int Hv,
+                                 int Dk, int Dv, int W, int num_slots, float eps, void* status, void* stream,
+                                 long ld_mixed, long ld_z, long ld_a, long ld_b) {
   using namespace afd;
   if (T == 0) return 0;
   if (W < 2 || W > 9 || Hv % Hk != 0 || Dv > 256 || Dv % 32 != 0 || scratch == nullptr) return -1;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const int C = 2 * Hk * Dk + Hv * Dv;
+  if (ld_mixed < C || ld_z < static_cast<long>(Hv) * Dv || ld_a < Hv || ld_b < Hv) return -3;
   auto y = static_cast<__nv_bfloat16*>(scratch);
   dim3 g1((C + 255) / 256, T);
   gdn_conv_step_kernel<<<g1, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(mixed), y,
                                            static_cast<const __nv_bfloat16*>(conv_w),
                                            static_cast<__nv_bfloat16*>(conv_state), static_cast<const int*>(slots), T,
-                                           C, W, num_slots, static_cast<int*>(status));
+                                           C, W, num_slots, static_cast<int*>(status), ld_mixed);
   AFD_CHECK_LAUNCH();
   dim3 g2(Hv, T);
 #define LAUNCH_REC(DKK)                                                                                          \
@@ -318,7 +321,7 @@ extern "C" int afd_gdn_decode(const void* mixed, const void* z, const void* a, c
       y, static_cast<const __nv_bfloat16*>(z), static_cast<const __nv_bfloat16*>(a),                            \
       static_cast<const __nv_bfloat16*>(b), static_cast<const float*>(A_log), static_cast<const float*>(dt_bias), \
       static_cast<const __nv_bfloat16*>(norm_w), static_cast<float*>(rec_state), static_cast<const int*>(slots),  \
-      static_cast<__nv_bfloat16*>(out), T, Hk, Hv, Dv, num_slots, eps, static_cast<int*>(status))
+      static_cast<__nv_bfloat16*>(out), T, Hk, Hv, Dv, num_slots, eps, static_cast<int*>(status), ld_z, ld_a, ld_b)
   if (Dk == 128) LAUNCH_REC(128);
   else if (Dk == 64) LAUNCH_REC(64);
   else if (Dk == 32) LAUNCH_REC(32);
@@ -327,6 +330,15 @@ extern "C" int afd_gdn_decode(const void* mixed, const void* z, const void* a, c
 #undef LAUNCH_REC
   AFD_CHECK_LAUNCH();
   return 0;
+}
+
+extern "C" int afd_gdn_decode(const void* mixed, const void* z, const void* a, const void* b, const void* conv_w,
+                              const void* A_log, const void* dt_bias, const void* norm_w, void* conv_state,
+                              void* rec_state, const void* slots, void* out, void* scratch, int T, int Hk, int Hv,
+                              int Dk, int Dv, int W, int num_slots, float eps, void* status, void* stream) {
+  return afd_gdn_decode_ld(mixed, z, a, b, conv_w, A_log, dt_bias, norm_w, conv_state, rec_state, slots, out, scratch,
+                           T, Hk, Hv, Dk, Dv, W, num_slots, eps, status, stream, 2L * Hk * Dk + static_cast<long>(Hv) * Dv,
+                           static_cast<long>(Hv) * Dv, Hv, Hv);
 }
 
 // Prefill of `num_seqs` sequences packed back to back (cu_seqlens int32 [num_seqs + 1], token

@@ -143,6 +143,7 @@ class AttentionStage:
         self.status: Optional[Tensor] = None      # device status word of the process (set by the worker)
         self.cad = None                           # cad.gpu.CadModelHook: the attention core runs on other GPUs
         self.w_fp8: Dict[str, Tuple[Tensor, Tensor]] = {}
+        self.w_merged: Dict[str, Tensor] = {}
         self.vocab_local = (cfg.vocab_size + tp_size - 1) // tp_size
         self.vocab_start = tp_rank * self.vocab_local
 
@@ -257,12 +258,46 @@ class AttentionStage:
                 self.qk_w[i] = (qw + 1, kw + 1) if c.norm_offset1 else (qw, kw)
             if c.attn_output_gate and self.device.type == "cuda":
                 n = self.hq * D
+                src = getattr(self, "_fp8_src", {})
                 for suffix in ("qkv_proj.weight", "qkv_proj.bias"):
                     w = self.w.get(p + suffix)
                     if w is not None:
                         self.w[p + suffix] = torch.cat([w[:n], w[2 * n:], w[n:2 * n]], 0).contiguous()
+                    if p + suffix in src:           # the checkpoint's FP8 values follow the same row order
+                        t = src[p + suffix]
+                        src[p + suffix] = torch.cat([t[:n], t[2 * n:], t[n:2 * n]], 0).contiguous()
                 self.gate_last = True
+        self._merge_gdn_in_proj()
         self._quantize_dense_weights()
+
+    def _merge_gdn_in_proj(self) -> None:
+        """Gated DeltaNet layers on CUDA: the four input projections become two GEMMs, [qkv | z] (the wide
+        pair, FP8 where the checkpoint is) and [b | a] (Hv rows each); the single tensors stay as row
+        views of the merged ones, so nothing is stored twice. The decode kernels read the column
+        ranges of the merged outputs in place. Reference: python/minisgl/models/qwen35_moe.py:124-151
+        (in_proj_qkvz / in_proj_ba)."""
+        c = self.cfg
+        self.w_merged: Dict[str, Tensor] = {}
+        if self.device.type != "cuda":
+            return
+        src = getattr(self, "_fp8_src", {})
+        for i in range(c.num_layers):
+            if c.layer_type(i) == "full":
+                continue
+            p = f"model.layers.{i}.linear_attn."
+            for merged, parts in (("in_proj_qkvz.weight", ("in_proj_qkv.weight", "in_proj_z.weight")),
+                                  ("in_proj_ba.weight", ("in_proj_b.weight", "in_proj_a.weight"))):
+                ws = [self.w.get(p + n) for n in parts]
+                if any(w is None for w in ws) or len({w.dtype for w in ws}) != 1:
+                    continue
+                m = torch.cat(ws, 0).contiguous()
+                self.w_merged[p + merged] = m
+                off = 0
+                for n, w in zip(parts, ws):
+                    self.w[p + n] = m[off:off + w.shape[0]]
+                    off += w.shape[0]
+                if all(p + n in src for n in parts):
+                    src[p + merged] = torch.cat([src[p + n] for n in parts], 0)
 
     def _quantize_dense_weights(self) -> None:
         """Block-FP8 checkpoints keep their dense projections in e4m3 with 128x128 scales on the GPU
@@ -271,10 +306,13 @@ class AttentionStage:
         self.w_fp8: Dict[str, Tuple[Tensor, Tensor]] = {}
         if not (c.quant.is_fp8 and self.device.type == "cuda" and _OWN_DENSE_FP8):
             return
-        for name, w in self.w.items():
+        for name, w in list(self.w.items()) + list(self.w_merged.items()):
             if not name.endswith(("qkv_proj.weight", "o_proj.weight", "in_proj_qkv.weight", "in_proj_z.weight",
-                                  "out_proj.weight", "gate_up_proj.weight", "down_proj.weight")):
+                                  "in_proj_qkvz.weight", "out_proj.weight", "gate_up_proj.weight", "down_proj.weight")):
                 continue
+            if name.endswith(("in_proj_qkv.weight", "in_proj_z.weight")) and \
+                    name.rsplit("in_proj_", 1)[0] + "in_proj_qkvz.weight" in self.w_merged:
+                continue                     # served by the merged projection
             if w.dtype != torch.bfloat16 or w.shape[0] % 128 or w.shape[1] % 128 or not c.quant.applies_to(name):
                 continue
             src = getattr(self, "_fp8_src", {}).get(name)         # the checkpoint's exact values, when it was FP8
@@ -283,7 +321,7 @@ class AttentionStage:
 
     def _proj(self, x: Tensor, name: str, bias: Optional[Tensor] = None) -> Tensor:
         """x @ w[name].T (+ bias)."""
-        w = self.w[name]
+        w = self.w[name] if name in self.w else self.w_merged[name]
         q = self.w_fp8.get(name)
         if ((_OWN_DENSE or q is not None) and x.is_cuda and x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16
                 and x.dim() == 2 and 0 < x.shape[0] <= _OWN_DENSE_MAX_TOKENS and w.shape[0] % 128 == 0
@@ -431,10 +469,16 @@ class AttentionStage:
         li = self.lin_index[layer]
         hk, hv = c.gdn_num_k_heads // self.tp_size, c.gdn_num_v_heads // self.tp_size
         dk, dv = c.gdn_head_k_dim, c.gdn_head_v_dim
-        mixed = self._proj(x, p + "in_proj_qkv.weight")
-        z = self._proj(x, p + "in_proj_z.weight")
-        b = _linear(x, self.w[p + "in_proj_b.weight"])
-        a = _linear(x, self.w[p + "in_proj_a.weight"])
+        if p + "in_proj_qkvz.weight" in self.w_merged and p + "in_proj_ba.weight" in self.w_merged:
+            C = 2 * hk * dk + hv * dv
+            qkvz = self._proj(x, p + "in_proj_qkvz.weight")
+            ba = _linear(x, self.w_merged[p + "in_proj_ba.weight"])
+            mixed, z, b, a = qkvz[:, :C], qkvz[:, C:], ba[:, :hv], ba[:, hv:]
+        else:
+            mixed = self._proj(x, p + "in_proj_qkv.weight")
+            z = self._proj(x, p + "in_proj_z.weight")
+            b = _linear(x, self.w[p + "in_proj_b.weight"])
+            a = _linear(x, self.w[p + "in_proj_a.weight"])
         out = gdn_ops.gdn_block(mixed, z, a, b, self.w[p + "conv1d.weight"], self.w[p + "A_log"], self.w[p + "dt_bias"],
                                 self.w[p + "norm.weight"], gdn.conv[li], gdn.rec[li], meta, hk, hv, dk, dv, c.rms_eps)
         return self._proj(out if out.is_contiguous() else out.contiguous(), p + "out_proj.weight")

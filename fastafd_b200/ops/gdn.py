@@ -78,16 +78,23 @@ def _gdn_decode_cuda(mixed, z, a, b, conv_w, A_log, dt_bias, norm_w, conv_state,
     dev = mixed.device
     out = torch.empty(T, hv * dv, dtype=mixed.dtype, device=dev)
     scratch = torch.empty(T, mixed.shape[1], dtype=mixed.dtype, device=dev)
-    fn = lib().afd_gdn_decode
+    fn = lib().afd_gdn_decode_ld
     fn.restype = C.c_int
     vp = C.c_void_p
     bf = lambda t: t if t.dtype == torch.bfloat16 else t.to(torch.bfloat16)  # noqa: E731
-    args = [bf(mixed.contiguous()), bf(z.contiguous()), bf(a.contiguous()), bf(b.contiguous()), bf(conv_w.contiguous()),
+
+    def rows(t):        # bf16 with unit column stride; the row stride is passed on (column ranges of one
+        t = bf(t)       # merged projection output are read in place)
+        return t if t.stride(1) == 1 else t.contiguous()
+
+    mixed, z, a, b = rows(mixed), rows(z), rows(a), rows(b)
+    args = [mixed, z, a, b, bf(conv_w.contiguous()),
             A_log.float().contiguous(), dt_bias.float().contiguous(), bf(norm_w.contiguous())]
     check(fn(*[vp(ptr(t)) for t in args], vp(ptr(conv_state)), vp(ptr(rec_state)), vp(ptr(meta.state_slots)),
              vp(ptr(out)), vp(ptr(scratch)), C.c_int(T), C.c_int(hk), C.c_int(hv), C.c_int(dk), C.c_int(dv),
              C.c_int(conv_w.shape[1]), C.c_int(conv_state.shape[0]), C.c_float(eps), vp(ptr(meta.status)),
-             vp(cur_stream())), "gdn_decode")
+             vp(cur_stream()), C.c_long(mixed.stride(0)), C.c_long(z.stride(0)), C.c_long(a.stride(0)),
+             C.c_long(b.stride(0))), "gdn_decode")
     return out
 
 

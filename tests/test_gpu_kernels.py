@@ -215,8 +215,10 @@ def test_fp8_block_scaled_gemm(bt):
     torch.testing.assert_close(out.cpu().float(), exp.float(), atol=3e-2, rtol=2e-2)
 
 
-@pytest.mark.parametrize("hk,hv,dk,dv", [(2, 4, 32, 32), (4, 16, 128, 128)])
-def test_gdn_decode_step(hk, hv, dk, dv):
+@pytest.mark.parametrize("hk,hv,dk,dv,merged", [(2, 4, 32, 32, False), (4, 16, 128, 128, False), (4, 16, 128, 128, True)])
+def test_gdn_decode_step(hk, hv, dk, dv, merged):
+    """`merged`: mixed | z and b | a are column ranges of two wider tensors (the outputs of the merged
+    input projections), read in place through their row strides."""
     from fastafd_b200.models.transformer import AttnMeta
     from fastafd_b200.ops import gdn as gdn_ops
 
@@ -224,6 +226,10 @@ def test_gdn_decode_step(hk, hv, dk, dv):
     Cc = 2 * hk * dk + hv * dv
     mixed, z = _bf(T, Cc, seed=20), _bf(T, hv * dv, seed=21)
     a, b = _bf(T, hv, seed=22), _bf(T, hv, seed=23)
+    if merged:
+        qkvz, ba = torch.cat([mixed, z], 1).contiguous(), torch.cat([b, a], 1).contiguous()
+        mixed, z, b, a = qkvz[:, :Cc], qkvz[:, Cc:], ba[:, :hv], ba[:, hv:]
+        assert not z.is_contiguous() and not a.is_contiguous()
     conv_w = _bf(Cc, W, scale=0.5, seed=24)
     A_log = torch.randn(hv, generator=torch.Generator().manual_seed(25)).to(DEV) * 0.5
     dt_bias = torch.randn(hv, generator=torch.Generator().manual_seed(26)).to(DEV) * 0.5
