@@ -344,8 +344,23 @@ class AttentionWorker:
         b.ids[:bucket].copy_(self.token_pool[rows, pos.long()])
 
     def _sample_and_writeback(self, lane: int, mb: _MbCtx, bucket: int) -> None:
+        self._sample_from_logits(lane, self.model.lm_head(self.full_tokens(mb.normed)), bucket)
+
+    def _sample_all(self, mbs: List[_MbCtx], bucket: int) -> None:
+        """LM head and greedy sampling of every micro-batch of a decode step. The vocabulary projection
+        is a weight stream (its rows outnumber the tokens by three orders of magnitude), so the
+        micro-batches go through it together: one pass over the matrix instead of one per micro-batch."""
+        if len(mbs) == 1:
+            return self._sample_and_writeback(0, mbs[0], bucket)
+        xs = [self.full_tokens(mb.normed) for mb in mbs]
+        logits = self.model.lm_head(torch.cat(xs, 0))
+        off = 0
+        for lane, x in enumerate(xs):
+            self._sample_from_logits(lane, logits[off:off + x.shape[0]], bucket)
+            off += x.shape[0]
+
+    def _sample_from_logits(self, lane: int, logits: torch.Tensor, bucket: int) -> None:
         b = self.bufs[lane]
-        logits = self.model.lm_head(self.full_tokens(mb.normed))
         b.logits = logits
         if self.logit_tap is not None and not (self.cuda and torch.cuda.is_current_stream_capturing()):
             self.logit_tap.append((b.rows[:bucket].cpu().clone(), b.seq_lens[:bucket].cpu().clone(), logits[:bucket].float().cpu().clone()))
@@ -362,8 +377,7 @@ class AttentionWorker:
             self._prepare_decode_inputs(lane, bucket)
             mbs.append(self._decode_ctx(lane, bucket))
         self._pipeline(mbs)
-        for lane, mb in enumerate(mbs):
-            self._sample_and_writeback(lane, mb, bucket)
+        self._sample_all(mbs, bucket)
         if self.model.cad is not None:
             self.model.cad.end_step()          # core-attention disaggregation: the epoch bump closes the step
         self._last_mbs = mbs
