@@ -21,6 +21,11 @@ from typing import List, Optional
 import torch
 
 from ..ops import EPI_COMBINE, EPI_SWIGLU, NUM_SMS, grouped_gemm
+
+# The gate/up GEMM is launched (programmatic dependent launch) while the kernel in front of it still
+# runs or waits for the sources' flags; HBM is idle then, and the GEMM's resident CTAs use the time to
+# pull this many bytes of their first weight tiles into L2 (FASTAFD_L2_PREFETCH_MB, 0 turns it off).
+L2_PREFETCH_BYTES = int(float(os.environ.get("FASTAFD_L2_PREFETCH_MB", "64")) * (1 << 20))
 from ..ops._lib import (CombineDesc, DirectDesc, DispatchDesc, GroupDesc, RouteDirectDesc, RouteDispatchDesc, ScheduleDesc,
                         check, cur_stream, lib, ptr)
 from ..parallel.fabric import Fabric, Layout
@@ -340,7 +345,7 @@ class EgMoeEndpoint:
                      epilogue=EPI_SWIGLU, out=None if cfg.fp8 else self.pool_h, out_ld=cfg.intermediate,
                      fp8=cfg.fp8, x_scale=self.pool_xs, w_scale=w13_scale,
                      out_q=self.pool_h if cfg.fp8 else None, out_scale=self.pool_hs,
-                     status=self.status, grid=self.grid)
+                     status=self.status, grid=self.grid, l2_prefetch_bytes=L2_PREFETCH_BYTES)
         w = self.lanes[lane]
         grouped_gemm(w=w2, x=self.pool_h, num_experts=self.experts_local, n_per_expert=cfg.hidden,
                      k=cfg.intermediate, tile_info=self.tile_info, num_tok_tiles=ntiles,
@@ -378,7 +383,7 @@ class EgMoeEndpoint:
                      epilogue=EPI_SWIGLU, out=None if cfg.fp8 else self.dpool_h, out_ld=cfg.intermediate,
                      fp8=cfg.fp8, x_scale=self.dpool_xs[lane], w_scale=w13_scale,
                      out_q=self.dpool_h if cfg.fp8 else None, out_scale=self.dpool_hs,
-                     status=self.status, grid=self.grid)
+                     status=self.status, grid=self.grid, l2_prefetch_bytes=L2_PREFETCH_BYTES)
         grouped_gemm(w=w2, x=self.dpool_h, num_experts=self.experts_local, n_per_expert=cfg.hidden,
                      k=cfg.intermediate, tile_info=self.dtile_info, num_tok_tiles=ntiles,
                      block_tok=cfg.block_tok, epilogue=EPI_COMBINE, fp8=cfg.fp8, x_scale=self.dpool_hs,

@@ -347,8 +347,10 @@ def grouped_gemm(*, w, x, num_experts, n_per_expert, k, tile_info, num_tok_tiles
                  epilogue, out=None, out_ld=0, fp8=False, x_scale=None, w_scale=None, out_q=None,
                  out_scale=None, row_meta=None, peer_combine=(), peer_flag=(), combine_tokens=0,
                  hidden=0, epoch=None, done_counter=None, status=None, grid=NUM_SMS, trace=None,
-                 k_splits=1, splitk_ws=None, splitk_cnt=None, bias=None, w_tile_major=False):
-    """Low-level launcher of the tcgen05 grouped GEMM (see csrc/grouped_gemm.cu)."""
+                 k_splits=1, splitk_ws=None, splitk_cnt=None, bias=None, w_tile_major=False, l2_prefetch_bytes=0):
+    """Low-level launcher of the tcgen05 grouped GEMM (see csrc/grouped_gemm.cu). `l2_prefetch_bytes`:
+    while the kernel still waits for its predecessor, its CTAs pull up to this many bytes (in total) of
+    the weights of their likely first work units into L2 (a hint; 0 = off)."""
     d = GroupedGemmDesc()
     d.w, d.x = ptr(w), ptr(x)
     d.num_experts, d.n_per_expert, d.k, d.pool_rows = num_experts, n_per_expert, k, x.shape[0]
@@ -366,6 +368,7 @@ def grouped_gemm(*, w, x, num_experts, n_per_expert, k, tile_info, num_tok_tiles
     d.epoch, d.done_counter, d.status, d.trace = ptr(epoch), ptr(done_counter), ptr(status), ptr(trace)
     d.k_splits, d.splitk_ws, d.splitk_cnt, d.bias = k_splits, ptr(splitk_ws), ptr(splitk_cnt), ptr(bias)
     d.w_tile_major = int(w_tile_major)
+    d.l2_prefetch_bytes = int(l2_prefetch_bytes)
     check(lib().afd_grouped_gemm(C.byref(d), cur_stream()), "grouped_gemm")
 
 

@@ -31,6 +31,7 @@ class GroupedGemmDesc(C.Structure):
         ("epoch", VP), ("done_counter", VP), ("status", VP), ("trace", VP),
         ("k_splits", C.c_int), ("splitk_ws", VP), ("splitk_cnt", VP), ("bias", VP),
         ("w_tile_major", C.c_int),
+        ("l2_prefetch_bytes", C.c_int),
     ]
 
 
