@@ -86,8 +86,6 @@ struct GroupedGemmArgs {
   // into L2: the unit it would get if token tile t held expert t (true when every expert has between
   // one and block_tok tokens, the common case in decode). A hint only: a wrong guess costs bandwidth,
   // never correctness. l2_prefetch_bytes = bytes per CTA (0: off).
-  const uint8_t* w_base;
-  long w_row_bytes;            // bytes of one weight row (K elements)
   int l2_prefetch_bytes;
   int num_experts;
 };
@@ -156,18 +154,18 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_w,
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  if (args.l2_prefetch_bytes > 0) {
+  if (args.l2_prefetch_bytes > 0 && warp == 0) {
+    // Same boxes as the producer's later loads of the guessed unit, as TMA prefetches into L2.
     constexpr int kTPU = (FP8 && EPI == EPI_SWIGLU) ? 2 : 1;
     const int units_per_tile = args.n_tiles / kTPU;
     const int guess_expert = static_cast<int>(blockIdx.x) / units_per_tile;
     const int guess_unit = static_cast<int>(blockIdx.x) - guess_expert * units_per_tile;
-    if (guess_expert < args.num_experts) {
-      const size_t row0 = static_cast<size_t>(guess_expert) * args.n_per_expert + static_cast<size_t>(guess_unit) * kTPU * 128;
-      const uint8_t* wp = args.w_base + row0 * static_cast<size_t>(args.w_row_bytes);
-      const size_t bytes = min(static_cast<size_t>(kTPU) * 128 * static_cast<size_t>(args.w_row_bytes),
-                               static_cast<size_t>(args.l2_prefetch_bytes));
-      for (size_t off = static_cast<size_t>(threadIdx.x) * 128; off < bytes; off += static_cast<size_t>(blockDim.x) * 128)
-        asm volatile("prefetch.global.L2 [%0];" ::"l"(wp + off));
+    if (guess_expert < args.num_experts && elect_one()) {
+      int boxes = args.l2_prefetch_bytes / Cfg::kWBytes;
+      for (int sub = 0; sub < kTPU && boxes > 0; ++sub) {
+        const int w_row = guess_expert * args.n_per_expert + (guess_unit * kTPU + sub) * 128;
+        for (int kb = 0; kb < args.k_blocks && boxes > 0; ++kb, --boxes) tma_prefetch_2d(&tmap_w, kb * (FP8 ? 128 : 64), w_row);
+      }
     }
   }
   pdl_wait();          // barriers, TMEM and descriptors are ready; now the predecessor's outputs may be read
@@ -652,8 +650,6 @@ extern "C" int afd_grouped_gemm(const AfdGroupedGemmDesc* d, void* stream_v) {
   a.splitk_ws = static_cast<float*>(d->splitk_ws);
   a.splitk_cnt = static_cast<unsigned int*>(d->splitk_cnt);
   a.bias = static_cast<const __nv_bfloat16*>(d->bias);
-  a.w_base = static_cast<const uint8_t*>(d->w);
-  a.w_row_bytes = static_cast<long>(d->k) * eb;
   a.num_experts = d->num_experts;
   a.l2_prefetch_bytes = (d->l2_prefetch_bytes > 0 && !d->w_tile_major && a.k_splits == 1)
                             ? d->l2_prefetch_bytes / (d->grid > 0 ? d->grid : 148) / 128 * 128 : 0;

@@ -73,12 +73,14 @@ __device__ __forceinline__ uint32_t claim_slot(const DirectArgs& d, int t, int k
 
 // The last pushing CTA publishes this source's epoch on every expert GPU (data -> fence.gpu ->
 // counter -> fence.sys -> flags), then advances the epoch. Returns whether this CTA was the last.
-__device__ __forceinline__ bool release_flags(const DirectArgs& d, unsigned int pushing_ctas) {
+__device__ __forceinline__ bool release_flags(const DirectArgs& d, unsigned int pushing_ctas, bool local_only = false) {
   __threadfence();
   const unsigned int prev = atomicAdd(d.done_counter, 1u);
   const bool last = prev == pushing_ctas - 1;
   if (last) {
-    __threadfence_system();
+    // every consumer on this GPU (and ordered behind this kernel): a device-scope fence is enough
+    if (local_only) __threadfence();
+    else __threadfence_system();
     const uint32_t e = *d.epoch;
     for (int g = 0; g < d.num_eg; ++g) st_relaxed_sys(d.peer_flag[g], e);
     trace_stamp(d.trace, e, 0);
@@ -182,10 +184,15 @@ __device__ __forceinline__ void schedule_warp(const ScheduleArgs& a, int lane, b
   if (lane == 0) trace_stamp(a.trace, e0, 1);
   const int per = (a.experts_local + 31) / 32;
   const int lo = min(lane * per, a.experts_local), hi = min(lo + per, a.experts_local);
+  constexpr int kMaxPer = 16;             // 512 local experts at most (host check)
+  int cs[kMaxPer];
   int tiles = 0, routed = 0;
-  for (int e = lo; e < hi; ++e) {
-    int c = static_cast<int>(__ldcg(a.counts + e));
+#pragma unroll
+  for (int i = 0; i < kMaxPer; ++i) {
+    const int e = lo + i;
+    int c = (i < per && e < hi) ? static_cast<int>(__ldcg(a.counts + e)) : 0;
     if (c > a.cap) c = a.cap;             // a source that overran the stripe has set the status
+    cs[i] = c;
     tiles += (c + a.block_tok - 1) / a.block_tok;
     routed += c;
   }
@@ -200,13 +207,16 @@ __device__ __forceinline__ void schedule_warp(const ScheduleArgs& a, int lane, b
     }
   }
   int t = incl - tiles;
-  for (int e = lo; e < hi; ++e) {
-    int c = static_cast<int>(__ldcg(a.counts + e));
-    if (c > a.cap) c = a.cap;
-    if (a.expert_counts) a.expert_counts[e] = c;
-    a.counts[e] = 0;                      // the lane's next round starts from empty stripes
-    for (int j = 0; j * a.block_tok < c; ++j, ++t) {
-      if (t < a.max_tok_tiles) a.tile_info[t] = make_int4(e, e * a.cap + j * a.block_tok, min(a.block_tok, c - j * a.block_tok), 0);
+#pragma unroll
+  for (int i = 0; i < kMaxPer; ++i) {
+    const int e = lo + i;
+    if (i < per && e < hi) {
+      const int c = cs[i];
+      if (a.expert_counts) a.expert_counts[e] = c;
+      a.counts[e] = 0;                    // the lane's next round starts from empty stripes
+      for (int j = 0; j * a.block_tok < c; ++j, ++t) {
+        if (t < a.max_tok_tiles) a.tile_info[t] = make_int4(e, e * a.cap + j * a.block_tok, min(a.block_tok, c - j * a.block_tok), 0);
+      }
     }
   }
   if (lane == 31) {
@@ -534,7 +544,7 @@ __global__ void __launch_bounds__(kRouteThreads) ag_route_direct_kernel(const Ro
   }
   __syncthreads();
   __shared__ int s_last;
-  if (tid == 0) s_last = release_flags(d, static_cast<unsigned int>(ngroups)) ? 1 : 0;
+  if (tid == 0) s_last = release_flags(d, static_cast<unsigned int>(ngroups), a.fuse_schedule != 0) ? 1 : 0;
   if (a.fuse_schedule) {
     __syncthreads();
     if (s_last && warp == 0) schedule_warp(a.sched, lane, false);
@@ -649,7 +659,9 @@ extern "C" int afd_ag_route_direct(const AfdRouteDirectDesc* r, void* stream) {
   a.eps = r->eps; a.route_scale = r->route_scale;
   a.fuse_schedule = 0;
   if (r->fuse_schedule) {
-    if (r->d.num_eg != 1 || r->sched.A != 1 || r->sched.cap % r->sched.block_tok != 0) return -5;
+    if (r->d.num_eg != 1 || r->sched.A != 1 || r->sched.cap % r->sched.block_tok != 0 || r->sched.experts_local < 1 ||
+        r->sched.experts_local > 512)
+      return -5;
     a.fuse_schedule = 1;
     fill_schedule(a.sched, &r->sched);
   }
@@ -682,7 +694,7 @@ extern "C" int afd_ag_route_direct(const AfdRouteDirectDesc* r, void* stream) {
 typedef AfdRouteDirectDesc::AfdScheduleDesc AfdScheduleDesc;
 
 extern "C" int afd_eg_schedule(const AfdScheduleDesc* d, void* stream) {
-  if (d->A < 1 || d->A > 32 || d->cap % d->block_tok != 0 || d->experts_local < 1) return -1;
+  if (d->A < 1 || d->A > 32 || d->cap % d->block_tok != 0 || d->experts_local < 1 || d->experts_local > 512) return -1;
   ScheduleArgs a{};
   fill_schedule(a, d);
   cudaError_t le = launch_pdl(eg_schedule_kernel, dim3(1), dim3(32), 0, static_cast<cudaStream_t>(stream), 1, a);

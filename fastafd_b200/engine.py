@@ -169,7 +169,8 @@ class AfdEngine:
 
                 # decode-sized steps store rows straight into the experts' pool stripes (moe/afd_moe.py)
                 direct = min(self.max_comm_tokens, max(cap * max(rt.spec_block, 1) // topo.attn_tp, 1))
-                if os.environ.get("FASTAFD_DIRECT", "1") == "0" or num_ag * direct > 1024:
+                experts_local = (cfg.num_experts * tp_expand + num_eg - 1) // num_eg
+                if os.environ.get("FASTAFD_DIRECT", "1") == "0" or num_ag * direct > 1024 or experts_local > 512:
                     direct = 0
                 mcfg = MoeCommConfig(num_ag=num_ag, num_eg=num_eg, num_lanes=rt.num_mb, max_tokens=self.max_comm_tokens,
                                      hidden=cfg.hidden_size, topk=cfg.num_experts_per_tok * tp_expand,
