@@ -23,7 +23,7 @@ import json
 import random
 import time
 from dataclasses import dataclass, field
-from typing import List
+from typing import List, Optional
 
 
 @dataclass
@@ -120,15 +120,19 @@ async def _one(session, url: str, ids: List[int], max_tokens: int) -> RequestTra
     return tr
 
 
-async def run(host: str, port: int, num: int, prompt_len: int, max_tokens: int, vocab: int, seed: int = 0) -> dict:
+async def run(host: str, port: int, num: int, prompt_len: int, max_tokens: int, vocab: int, seed: int = 0,
+              prompts: Optional[List[List[int]]] = None) -> dict:
+    """A closed batch of `num` requests sent at once. `prompts`: token ids to send (cycled when there
+    are fewer than `num`), e.g. a prompt base of benchmark/long_prompts.py; else uniform random ids."""
     import aiohttp
 
     rng = random.Random(seed)
     url = f"http://{host}:{port}/v1/chat/completions"
     t0 = time.perf_counter()
     async with aiohttp.ClientSession(timeout=aiohttp.ClientTimeout(total=None)) as s:
-        traces = await asyncio.gather(*[_one(s, url, [rng.randrange(vocab) for _ in range(prompt_len)], max_tokens)
-                                        for _ in range(num)])
+        traces = await asyncio.gather(*[_one(s, url, prompts[i % len(prompts)] if prompts else
+                                             [rng.randrange(vocab) for _ in range(prompt_len)], max_tokens)
+                                        for i in range(num)])
     return summarize(list(traces), time.perf_counter() - t0)
 
 
@@ -158,6 +162,7 @@ def main(argv=None):
     ap.add_argument("--prompt-len", type=int, default=128)
     ap.add_argument("--max-tokens", type=int, default=32)
     ap.add_argument("--vocab", type=int, default=1024)
+    ap.add_argument("--prompt-file", default="", help="JSON lines of {input_ids}: a prompt base of benchmark/long_prompts.py")
     ap.add_argument("--trace", default="", help="JSONL arrival trace to replay instead of a closed batch")
     ap.add_argument("--time-scale", type=float, default=1.0)
     ap.add_argument("--max-requests", type=int, default=0)
@@ -168,7 +173,12 @@ def main(argv=None):
         entries = scale_trace(read_trace(a.trace), a.time_scale, a.max_requests, a.max_input, a.max_output)
         print(json.dumps(asyncio.run(replay(a.host, a.port, entries, a.vocab))))
         return
-    print(json.dumps(asyncio.run(run(a.host, a.port, a.num, a.prompt_len, a.max_tokens, a.vocab))))
+    prompts = None
+    if a.prompt_file:
+        from .long_prompts import load
+
+        prompts = load(a.prompt_file, max_prompts=a.num, max_tokens=a.max_input)
+    print(json.dumps(asyncio.run(run(a.host, a.port, a.num, a.prompt_len, a.max_tokens, a.vocab, prompts=prompts))))
 
 
 if __name__ == "__main__":

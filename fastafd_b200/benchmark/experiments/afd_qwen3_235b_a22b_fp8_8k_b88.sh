@@ -1,0 +1,12 @@
+#!/usr/bin/env bash
+# Qwen3-235B-A22B-FP8 decode replay, 8K context, 88 requests per attention GPU, 2 micro-batches of 44.
+source "$(dirname "${BASH_SOURCE[0]}")/common.sh"
+export PRESET_NAME="afd_qwen3_235b_a22b_fp8_8k_b88"
+export MODEL="${MODEL:-qwen3-235b-a22b-fp8}"
+export PROMPT_LEN="${PROMPT_LEN:-8192}"
+export PER_ATTN_GPU_BSZ="${PER_ATTN_GPU_BSZ:-88}"
+export NUM_GPUS="${NUM_GPUS:-8}"
+export ATTN_GPUS="${ATTN_GPUS:-4}"
+export NUM_MB="${NUM_MB:-2}"
+export STEPS="${STEPS:-32}"
+fastafd_run_bench

@@ -109,3 +109,64 @@ def test_bench_picks_micro_batches_from_the_layer_model():
     assert picks == {1: 1, 2: 1, 4: 1, 8: 2}
     big = get_model_config("qwen3-235b-a22b-fp8")
     assert bench.pick_num_mb(big, AfdTopology.for_world(8), 88, 8192) == 2
+
+
+def test_experiment_presets_build_valid_bench_commands(tmp_path):
+    """Every preset is a thin wrapper around one runner: with DRY_RUN=1 it prints the bench command
+    it would launch; the model must be a known preset and the batch must split over the micro-batches."""
+    import glob
+    import os
+    import subprocess
+
+    from fastafd_b200.config import get_model_config
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    presets = sorted(p for p in glob.glob(os.path.join(root, "fastafd_b200", "benchmark", "experiments", "*.sh"))
+                     if not p.endswith("common.sh"))
+    assert len(presets) >= 8
+    for p in presets:
+        env = dict(os.environ, DRY_RUN="1", RUN_DIR=str(tmp_path / os.path.basename(p)))
+        out = subprocess.run(["bash", p], env=env, capture_output=True, text=True, timeout=60)
+        assert out.returncode == 0, (p, out.stderr)
+        cmd = next(ln for ln in out.stdout.splitlines() if ln.startswith("== ")).split(": ", 1)[1].split()
+        assert "bench.py" in cmd
+        arg = lambda k: cmd[cmd.index(k) + 1]  # noqa: E731
+        get_model_config(arg("--model"))
+        gpus = int(arg("--gpus"))
+        assert gpus in (1, 2, 4, 8) and int(arg("--batch-per-attn-gpu")) > 0 and int(arg("--context")) >= 1024
+        if gpus > 1:
+            assert f"--nproc-per-node {gpus}" in " ".join(cmd) and "127.0.0.1" in cmd
+            assert int(arg("--attn-gpus")) < gpus
+        if "--num-mb" in cmd:
+            assert int(arg("--batch-per-attn-gpu")) % int(arg("--num-mb")) == 0
+        if "SUITE_NAME" in open(p).read():
+            from fastafd_b200.benchmark import suite
+            name = [ln for ln in open(p).read().splitlines() if "SUITE_NAME" in ln][0].split(":-")[1].rstrip('}"')
+            assert name in suite.load_configs()["configs"]
+
+
+def test_long_prompt_base_is_deterministic_and_sliced_contiguously(tmp_path):
+    from fastafd_b200.benchmark import long_prompts as lp
+
+    a = lp.synthetic(6, 300, vocab=5000, seed=7, shared_prefix=64)
+    b = lp.synthetic(6, 300, vocab=5000, seed=7, shared_prefix=64)
+    assert a == b and all(len(p) == 300 for p in a)
+    assert all(p[:64] == a[0][:64] for p in a) and a[0][64:] != a[1][64:]
+    assert all(16 <= t < 5000 for p in a for t in p)
+    # Zipf-like: the most frequent id is far above the uniform share; phrases repeat inside a prompt
+    flat = [t for p in lp.synthetic(4, 4000, vocab=5000, seed=1) for t in p]
+    top = max(flat.count(t) for t in set(flat[:200]))
+    assert top > 20 * len(flat) / 5000
+    lp.save(a, tmp_path / "base.jsonl")
+    assert lp.load(str(tmp_path / "base.jsonl")) == a
+    assert lp.load(str(tmp_path / "base.jsonl"), max_prompts=2, max_tokens=10) == [p[:10] for p in a[:2]]
+    # document slices: contiguous, exact length, round-robin over documents, short documents skipped
+    docs = [list(range(1000, 1950)), list(range(5000, 5100)), list(range(9000, 9700))]
+    sl = lp.slices_of_documents(docs, 5, 200, seed=3)
+    assert len(sl) == 5 and all(len(s) == 200 and s == list(range(s[0], s[0] + 200)) for s in sl)
+    assert {s[0] // 1000 for s in sl} == {1, 9}
+    import pytest
+    with pytest.raises(ValueError):
+        lp.slices_of_documents(docs, 50, 200, seed=3)
+    assert lp.main(["--count", "3", "--target-tokens", "128", "--vocab", "1024", "--output", str(tmp_path / "o.jsonl")]) == 0
+    assert len(lp.load(str(tmp_path / "o.jsonl"))) == 3
