@@ -2,7 +2,7 @@
 # Shared part of the experiment presets: every preset sets a workload through environment variables
 # (each one keeps a value that the caller exported) and calls fastafd_run_bench, which launches
 # bench.py with one process per GPU, keeps stdout/stderr and the JSON line in a run directory and,
-# when SUITE_NAME names an entry of benchmark/configs.json, judges the step time against the value
+# when SUITE_NAME names an entry of benchmark/configs.json, checks the step time against the value
 # recorded there (+-3 % by default).
 #   MODEL PROMPT_LEN PER_ATTN_GPU_BSZ NUM_GPUS ATTN_GPUS ATTN_TP NUM_MB STEPS WARMUP SPEC_BLOCK
 #   SPEC_ACCEPT ROUTER_BIAS RUN_DIR MASTER_PORT TP_FUSED DRY_RUN

@@ -100,7 +100,7 @@ def test_attention_tp2_tracks_colocated(tp_fused):
         path = os.path.join(d, "out.pt")
         mp.spawn(_worker, args=(4, _free_port(), path, n_new, 2, tp_fused), nprocs=4, join=True)
         got = torch.load(path)
-    # Random weights make generation chaotic after the first near-tie, so agreement is judged on
+    # Random weights make generation chaotic after the first near-tie, so agreement is measured on
     # the first token (the prefill result, no accumulated divergence) and loosely overall.
     first = sum(g[0] == e[0] for g, e in zip(got, exp))
     same = sum(a == b for g, e in zip(got, exp) for a, b in zip(g, e))
