@@ -306,3 +306,37 @@ def test_core_attention_disaggregation_on_two_gpus():
         mp.spawn(_cad_worker, args=(2, _free_port(), path, steps), nprocs=2, join=True)
         got = torch.load(path)
     assert torch.equal(got, torch.stack(want))
+
+
+@pytest.mark.timeout(600)
+def test_served_afd_on_two_gpus_matches_the_colocated_engine():
+    """HTTP -> tokenizer -> coordinator -> ZeroMQ -> one attention process on GPU 0 and one expert
+    process on GPU 1 (fabric over CUDA IPC, CUDA graphs on both) and back: the greedy tokens are those of
+    the colocated engine on one GPU."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    import sys
+    sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
+    from serving_util import greedy_tokens, running_server
+
+    from fastafd_b200.config import PRESETS
+    from fastafd_b200.core import SamplingParams
+    from fastafd_b200.engine import AfdEngine, SpmdDriver
+    from fastafd_b200.protocol import AfdTopology
+    from fastafd_b200.server.args import parse_args
+
+    prompts = [[5, 9, 200, 31, 77, 4], [1000, 3, 3, 8], list(range(40, 75))]
+    args = parse_args(["--mode", "afd-serve", "--model-path", "tiny-qwen3-moe", "--device", "cuda", "--afd-num-mb", "2",
+                       "--num-pages", "64", "--max-seq-len-override", "128", "--afd-max-running-requests", "8",
+                       "--cuda-graph-max-bs", "8"])
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    with running_server(args) as (base, sup):
+        got = [greedy_tokens(base, p, 8) for p in prompts]
+        assert sup.get_failures() == []
+    eng = AfdEngine(PRESETS["tiny-qwen3-moe"], args.runtime_config(), AfdTopology(colocated=True), 0, "cuda:0",
+                    seed=args.seed, fast_init=True)
+    try:
+        expect = [SpmdDriver(eng).generate([p], SamplingParams(max_tokens=8, ignore_eos=True))[0] for p in prompts]
+    finally:
+        eng.close()
+    assert got == expect
