@@ -179,6 +179,26 @@ def bench_gemm(a):
     assert int(status) == 0
     extra = {"E": E, "N": N, "K": K, "rows": row, "block_tok": bt, "tile_major": bool(a.tile_major),
              "us_in_graph": round(graph_us, 2), "GB_s_in_graph": round(wbytes / graph_us / 1e3, 1)}
+    if a.l2_prefetch_mb > 0 and not a.fp8 and not a.tile_major:
+        # What the L2 hint is worth when it has time to land: a launch without work (zero token tiles)
+        # issues the prefetches, a spin kernel of about 20 us stands for the kernel in front of the GEMM,
+        # then the GEMM runs. Same sequence with the hint off for comparison. (Measured on B200: no
+        # difference in this form, where the issuing CTAs exit at once.)
+        zero = torch.zeros(1, dtype=torch.int32, device=dev)
+        ws_rot = [w, torch.randn_like(w) * 0.05]      # two weight sets in turn: nothing of a set survives in L2
+
+        def seq(pf_bytes):
+            for i in range(4):
+                wi = ws_rot[i % 2]
+                ops.grouped_gemm(w=wi, x=x, num_experts=E, n_per_expert=N, k=K, tile_info=info_t, num_tok_tiles=zero,
+                                 block_tok=bt, epilogue=epi, out=out, out_ld=out.shape[1], status=status,
+                                 l2_prefetch_bytes=pf_bytes)
+                torch.cuda._sleep(40000)
+                ops.grouped_gemm(w=wi, x=x, num_experts=E, n_per_expert=N, k=K, tile_info=info_t, num_tok_tiles=ntile,
+                                 block_tok=bt, epilogue=epi, out=out, out_ld=out.shape[1], status=status)
+
+        extra["seq_us_prefetch_off"] = round(time_graph(lambda: seq(0), 4), 2)
+        extra["seq_us_prefetch_on"] = round(time_graph(lambda: seq(a.l2_prefetch_mb << 20), 4), 2)
     if a.tile_major and not a.fp8:
         valid = torch.zeros(row, dtype=torch.bool, device=dev)
         for e_, r0, n_, _ in info:
@@ -338,6 +358,7 @@ def main(argv=None):
     p.add_argument("--swiglu", action="store_true")
     p.add_argument("--fp8", action="store_true")
     p.add_argument("--tile-major", type=int, default=0)
+    p.add_argument("--l2-prefetch-mb", type=int, default=0, help="also time the L2 weight hint (see bench_gemm)")
     p = sub.add_parser("dense")
     p.add_argument("--tokens", type=int, default=32)
     p.add_argument("--n", type=int, default=5120)
