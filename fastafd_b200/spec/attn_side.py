@@ -127,7 +127,8 @@ class SpecRunner:
             j = self._ar[None]
             if self.sim_accept > 0:
                 # timing runs: a fixed mean acceptance from a pre-drawn table, one row per step
-                n = self.sim_table[(self.sim_step % self.sim_table.shape[0]).long(), lane, :B].reshape(B)
+                step = (self.sim_step % self.sim_table.shape[0]).long().view(1)      # stays on the device (graph capture)
+                n = self.sim_table.index_select(0, step)[0, lane, :B].reshape(B)
                 emitted = torch.where(j < n[:, None], target, torch.full_like(target, -1))
             n = n.to(torch.int64)
             valid = j < n[:, None]
