@@ -118,8 +118,9 @@ def test_speculative_decoding_on_gpu_tracks_plain_greedy(block, graph, sim, monk
     hist, mean = eng.attn.spec.accept_hist.sum(), eng.attn.spec.mean_accept()
     eng.close()
     assert [len(s) for s in spec] == [len(p) for p in plain]
-    prefix = sum(next((i for i, (a, b) in enumerate(zip(s, p)) if a != b), len(p)) for s, p in zip(spec, plain))
-    assert prefix >= 0.7 * sum(len(p) for p in plain), (spec, plain)
+    if not sim:       # a forced acceptance commits tokens scored behind wrong drafts: a timing mode, not greedy output
+        prefix = sum(next((i for i, (a, b) in enumerate(zip(s, p)) if a != b), len(p)) for s, p in zip(spec, plain))
+        assert prefix >= 0.7 * sum(len(p) for p in plain), (spec, plain)
     assert hist > 0 and 1.0 <= mean <= block
     if sim:
         assert abs(mean - sim) < 0.7
