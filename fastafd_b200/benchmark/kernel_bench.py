@@ -245,6 +245,36 @@ def bench_dense(a):
     lib_t = time_graph(lambda: [torch.nn.functional.linear(x, w) for w in ws], copies)
     hbm, _, how = measured_peaks()
     wbytes = N * K * 2
+    if a.fp8:
+        # block-FP8 weights (e4m3, 128x128 scales): activation quantisation (1x128) + the FP8 kernel, which is
+        # what a projection of an FP8 checkpoint costs per call, against cuBLAS on a bf16 copy of the weights
+        from ..reference import ops_ref as ref
+
+        qs = []
+        for w in ws:
+            q, sc = ref.block_quant_fp8(w.float())
+            qs.append((q.contiguous(), ops.plain_tile_scales(sc[None].float()).contiguous()))
+
+        def own_fp8(q, ksp):
+            xq, xs = ops.group_quant_fp8(x, 128)
+            return ops.dense_gemm(xq, q[0], x_scale=xs, w_scale=q[1], k_splits=ksp)
+
+        got8 = own_fp8(qs[0], 0)
+        torch.cuda.synchronize()
+        err8 = (got8.float() - ref_out.float()).abs().max().item()
+        quant_t = time_graph(lambda: [ops.group_quant_fp8(x, 128) for _ in ws], copies)
+        for ksp in ([a.k_splits] if a.k_splits >= 0 else [0, 1, 2, 4, 8]):
+            if ksp > 1 and (K // 128) % ksp:
+                continue
+            try:
+                own = time_graph(lambda: [own_fp8(q, ksp) for q in qs], copies)
+            except ValueError:
+                continue
+            print(json.dumps({"kernel": "dense_gemm_fp8", "M": M, "N": N, "K": K, "k_splits": ksp,
+                              "us_own_fp8_with_quant": round(own, 2), "us_quant_alone": round(quant_t, 2),
+                              "us_cublas_bf16": round(lib_t, 2), f"own_frac_of_{how}_hbm": round(N * K / own / 1e3 / hbm, 3),
+                              "max_abs_diff_vs_bf16": round(err8, 4), "weight_copies": copies}))
+        return
     for ksp in ([a.k_splits] if a.k_splits >= 0 else [0, 1, 2, 4, 8, 16]):
         if ksp > 1 and (K // 64) % ksp:
             continue
@@ -364,6 +394,7 @@ def main(argv=None):
     p.add_argument("--n", type=int, default=5120)
     p.add_argument("--k", type=int, default=2048)
     p.add_argument("--k-splits", type=int, default=-1, help="-1: sweep; 0: the heuristic")
+    p.add_argument("--fp8", action="store_true", help="block-FP8 weights: quantise + FP8 kernel against cuBLAS on bf16")
     p = sub.add_parser("route")
     p.add_argument("--tokens", type=int, default=32)
     p.add_argument("--experts", type=int, default=128)

@@ -105,16 +105,19 @@ def _linear(x: Tensor, w: Tensor, b: Optional[Tensor] = None) -> Tensor:
     return F.linear(x, w, b)
 
 
-# Dense projections (qkv, o_proj, GDN in/out projections, dense and shared-expert MLPs, LM head).
-# bf16 weights: plain library GEMMs. Measured on B200 in CUDA-graph replay, the split-K tcgen05
-# kernel of this repository needs 10.1 us for the 64 x 5120 x 2048 qkv projection and 11.3 us for the
-# 64 x 2048 x 4096 o_proj against 6.8 / 8.4 us of the library, so it is opt-in for bf16
-# (FASTAFD_OWN_DENSE=1). Block-FP8 checkpoints: decode-sized projections run on the own kernel with
-# the e4m3 weights and their exact 128x128 scales (half the bytes of a bf16 copy); FASTAFD_OWN_DENSE=0
-# sends those to the library on dequantised weights too.
+# Dense projections (qkv, o_proj, GDN in/out projections, dense and shared-expert MLPs, LM head) are
+# plain library GEMMs by default, on bf16 weights (a block-FP8 checkpoint's dense weights are
+# dequantised once at load). Measured on B200 in CUDA-graph replay:
+#   bf16, split-K tcgen05 kernel of this repository against the library: 64 x 5120 x 2048 qkv 10.1 / 6.8 us,
+#   64 x 2048 x 4096 o_proj 11.3 / 8.4 us;
+#   block-FP8 (activation quantisation + e4m3 kernel with exact 128x128 scales, half the weight bytes)
+#   against the library on the bf16 copy: 44 x 9216 x 4096 29.0 / 16.9 us, 44 x 4096 x 8192 29.3 / 17.3 us,
+#   88 x 9216 x 4096 41.7 / 17.6 us - the per-K-block promotion of the accumulator through registers costs
+#   more than the halved weight stream saves.
+# So both own paths are opt-in: FASTAFD_OWN_DENSE=1 (bf16 and FP8 weights), FASTAFD_OWN_DENSE=fp8 (FP8 only).
 _OWN_DENSE_ENV = os.environ.get("FASTAFD_OWN_DENSE", "")
 _OWN_DENSE = _OWN_DENSE_ENV == "1"
-_OWN_DENSE_FP8 = _OWN_DENSE_ENV != "0"
+_OWN_DENSE_FP8 = _OWN_DENSE_ENV in ("1", "fp8")
 _OWN_DENSE_MAX_TOKENS = 128
 
 
