@@ -22,6 +22,7 @@ Reference: python/minisgl/afd_attention_worker.py:709-955 (_run_ag_pipeline_body
 """
 from __future__ import annotations
 
+import os
 import time
 from contextlib import contextmanager, nullcontext
 from dataclasses import dataclass, field
@@ -135,6 +136,15 @@ class AttentionWorker:
         # validation hook: a list that receives (rows, kv lengths, fp32 logits) of every sampled row of
         # every eager step, so that logits can be compared with a reference forward (never set in serving)
         self.logit_tap: Optional[list] = None
+        # Every micro-batch's whole chain on its own stream (FASTAFD_LANE_STREAMS=1): the attention kernel of
+        # one micro-batch (HBM-bound) then overlaps the projections and the route kernel of the other
+        # (latency-bound), and a late combine of one no longer holds back the other. Only for a
+        # disaggregated attention rank without TP: a colocated expert stage shares its buffers between
+        # the micro-batches, and TP collectives must be issued in one order on one stream.
+        self.lane_parallel = (self.cuda and self.num_mb > 1 and self.tp.size == 1
+                              and getattr(client, "colocated", None) is None
+                              and os.environ.get("FASTAFD_LANE_STREAMS", "0") == "1")
+        self._in_lane_mode = False
         if self.cuda:
             self.main_stream = torch.cuda.Stream(self.device)
             self.lane_streams = [torch.cuda.Stream(self.device) for _ in range(self.num_mb)]
@@ -185,9 +195,10 @@ class AttentionWorker:
     def _on_lane(self, lane: int, after_main: bool = True):
         """Run the enclosed launches on the lane's stream, ordered after what `main` has queued
         so far; the caller orders `main` after the lane later with `_join_lane`."""
-        if not self.cuda or self.num_mb == 1:
+        if not self.cuda or self.num_mb == 1 or self._in_lane_mode:
             # one micro-batch: nothing to overlap with, so everything stays on the main stream and
-            # consecutive kernels keep their programmatic (early-launch) dependencies
+            # consecutive kernels keep their programmatic (early-launch) dependencies. Lane mode: the
+            # caller already runs the micro-batch's whole chain on its stream.
             yield
             return
         s = self.lane_streams[lane]
@@ -197,7 +208,7 @@ class AttentionWorker:
             yield
 
     def _join_lane(self, lane: int) -> None:
-        if self.cuda and self.num_mb > 1:
+        if self.cuda and self.num_mb > 1 and not self._in_lane_mode:
             torch.cuda.current_stream().wait_stream(self.lane_streams[lane])
 
     def _next_norm_weight(self, layer: int) -> torch.Tensor:
@@ -291,20 +302,38 @@ class AttentionWorker:
         `capture_layers`: hidden states (residual stream after that layer) kept in mb.capture
         for the speculative draft head."""
         m, L = self.model, self.cfg.num_layers
-        for mb in mbs:
-            h = m.embed(mb.ids, scatter=True)
-            mb.residual.copy_(h)
-            n0 = ops.rmsnorm(h, m.w["model.layers.0.input_layernorm.weight"], self.cfg.rms_eps, self.cfg.norm_offset1)
-            mb.normed.copy_(n0)
-            mb.keep += [h, n0]
-            self._compute(0, mb)
-        for l in range(L):
+        lanes = self.lane_parallel and not mbs[0].meta.is_prefill and not capture_layers
+        main = torch.cuda.current_stream() if lanes else None
+        if lanes:
             for mb in mbs:
-                self._combine(l, mb)
-                if l in capture_layers:
-                    mb.capture[l] = mb.residual.clone()
-                if l + 1 < L:
-                    self._compute(l + 1, mb)
+                self.lane_streams[mb.lane].wait_stream(main)
+            self._in_lane_mode = True
+
+        def on(mb):          # the stream that carries this micro-batch's chain
+            return torch.cuda.stream(self.lane_streams[mb.lane]) if lanes else nullcontext()
+
+        try:
+            for mb in mbs:
+                with on(mb):
+                    h = m.embed(mb.ids, scatter=True)
+                    mb.residual.copy_(h)
+                    n0 = ops.rmsnorm(h, m.w["model.layers.0.input_layernorm.weight"], self.cfg.rms_eps, self.cfg.norm_offset1)
+                    mb.normed.copy_(n0)
+                    mb.keep += [h, n0]
+                    self._compute(0, mb)
+            for l in range(L):
+                for mb in mbs:
+                    with on(mb):
+                        self._combine(l, mb)
+                        if l in capture_layers:
+                            mb.capture[l] = mb.residual.clone()
+                        if l + 1 < L:
+                            self._compute(l + 1, mb)
+        finally:
+            if lanes:
+                self._in_lane_mode = False
+                for mb in mbs:
+                    main.wait_stream(self.lane_streams[mb.lane])
 
     # ------------------------------------------------------------------ decode
     def _decode_ctx(self, lane: int, bucket: int, q_len: int = 1) -> _MbCtx:

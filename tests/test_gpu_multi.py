@@ -33,7 +33,7 @@ def _prompts(cfg):
     return [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (32, 17, 5, 40, 9, 23)]
 
 
-def _worker(rank, world, port, out_path, n_new, tp=1, tp_fused="1"):
+def _worker(rank, world, port, out_path, n_new, tp=1, tp_fused="1", lane_streams="0"):
     import torch.distributed as dist
     from fastafd_b200.core import SamplingParams
     from fastafd_b200.engine import AfdEngine, SpmdDriver
@@ -42,6 +42,7 @@ def _worker(rank, world, port, out_path, n_new, tp=1, tp_fused="1"):
     os.environ["MASTER_ADDR"], os.environ["MASTER_PORT"] = "127.0.0.1", str(port)
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     os.environ["FASTAFD_TP_FUSED"] = tp_fused
+    os.environ["FASTAFD_LANE_STREAMS"] = lane_streams
     torch.cuda.set_device(rank)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     cfg = _cfg()
@@ -55,8 +56,11 @@ def _worker(rank, world, port, out_path, n_new, tp=1, tp_fused="1"):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 4])
-def test_disaggregated_equals_colocated(world):
+@pytest.mark.parametrize("world,lane_streams", [(2, "0"), (4, "0"), (2, "1"), (4, "1")],
+                         ids=["2gpu", "4gpu", "2gpu-lane-streams", "4gpu-lane-streams"])
+def test_disaggregated_equals_colocated(world, lane_streams):
+    """lane-streams: every micro-batch's chain on its own stream on the attention ranks
+    (FASTAFD_LANE_STREAMS=1) instead of all attention compute on one stream."""
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     import torch.multiprocessing as mp
@@ -70,7 +74,7 @@ def test_disaggregated_equals_colocated(world):
     single.close()
     with tempfile.TemporaryDirectory() as d:
         path = os.path.join(d, "out.pt")
-        mp.spawn(_worker, args=(world, _free_port(), path, n_new), nprocs=world, join=True)
+        mp.spawn(_worker, args=(world, _free_port(), path, n_new, 1, "1", lane_streams), nprocs=world, join=True)
         got = torch.load(path)
     assert got == exp
 
