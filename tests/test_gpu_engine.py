@@ -124,3 +124,23 @@ def test_speculative_decoding_on_gpu_tracks_plain_greedy(block, graph, sim, monk
     assert hist > 0 and 1.0 <= mean <= block
     if sim:
         assert abs(mean - sim) < 0.7
+
+
+def test_fp8_model_library_and_own_dense_projections_agree(monkeypatch):
+    """A block-FP8 model (FP8 experts through the grouped GEMM) runs its dense projections on the
+    library with bf16 copies by default and on the FP8 tcgen05 kernel when asked; the two paths see the
+    same weights up to the e4m3 re-quantisation of random bf16 values, so most tokens agree."""
+    from dataclasses import replace
+
+    import fastafd_b200.models.transformer as tr
+    from fastafd_b200.config import QuantConfig
+
+    cfg = replace(MID, quant=QuantConfig("fp8"))
+    g = torch.Generator().manual_seed(2)
+    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (32, 19, 7, 40)]
+    lib = _gen(cfg, "cuda:0", True, prompts, 8)
+    monkeypatch.setattr(tr, "_OWN_DENSE_FP8", True)
+    own = _gen(cfg, "cuda:0", True, prompts, 8)
+    assert [len(o) for o in own] == [8] * 4
+    first = sum(a[0] == b[0] for a, b in zip(lib, own))
+    assert first >= 3, (lib, own)          # the prefill token: no accumulated divergence
