@@ -55,7 +55,9 @@ def parse_args():
     ap.add_argument("--layers", type=int, default=0, help="debug only: truncate the model (marks the result invalid)")
     ap.add_argument("--no-graph", action="store_true")
     ap.add_argument("--attn-gpus", type=int, default=0, help="attention GPUs of the N (0 = N/2, the 1:1 split)")
-    ap.add_argument("--attn-tp", type=int, default=1, help="tensor-parallel size of an attention DP lane")
+    ap.add_argument("--attn-tp", type=int, default=0,
+                    help="tensor-parallel size of an attention lane (0 = the named configuration: one TP-4 lane on "
+                         "8 GPUs, data-parallel lanes otherwise; 1 = data-parallel lanes)")
     ap.add_argument("--router-bias", default="", help="zipf:S - router selection bias drawn so that expert popularity follows "
                                                       "Zipf(S) (models with a selection bias, e.g. minimax-m2.5-fp8)")
     ap.add_argument("--also-router-bias", default="", help="after the main measurement, apply this router bias (zipf:S) in the "
@@ -217,6 +219,10 @@ def main():
     if args.layers and args.layers < cfg.num_layers:
         cfg = cfg.with_layers(args.layers)
         truncated = True
+    if args.attn_tp <= 0:
+        # 8 GPUs: attention TP4 + MLP EP4, the configuration the benchmark is named for (it completes with
+        # the fused collectives; attention DP4, --attn-tp 1, is about 10 % faster on this model)
+        args.attn_tp = 4 if (world == 8 and args.attn_gpus in (0, 4)) else 1
     topo = AfdTopology.for_world(world, attn_tp=args.attn_tp, attn_gpus=args.attn_gpus)
     if args.num_mb <= 0:
         args.num_mb = pick_num_mb(cfg, topo, args.batch_per_attn_gpu, args.context)
@@ -435,7 +441,7 @@ def main():
         if trace_info is not None and os.environ.get("FASTAFD_COMM_TRACE_FULL") == "1":
             out["comm_trace"] = trace_info
         if world == 8 and tp == 1:
-            out["config"]["deviation"] = "attention DP4, BASELINE names TP4 (--attn-tp 4 runs that configuration)"
+            out["config"]["deviation"] = "attention DP4 by request (--attn-tp 1); the named configuration is TP4, the default"
         if truncated:
             out["invalid"] = "model truncated with --layers (debug run)"
         print(json.dumps(out))

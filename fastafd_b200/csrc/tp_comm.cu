@@ -63,7 +63,9 @@ struct TpWaitArgs {
 };
 
 __global__ void tp_allgather_wait_kernel(const TpWaitArgs a) {
-  pdl_trigger();
+  // No early trigger here: the kernel behind a flag wait is a many-CTA consumer, and launched early it
+  // would sit resident (registers, shared memory) for the whole wait and take SM slots from the other
+  // micro-batch's attention kernel. It starts when this warp exits.
   pdl_wait();
   const uint32_t e = *a.epoch;
   if (threadIdx.x < a.tp) wait_flag_ge(a.flags + threadIdx.x, e, a.timeout_ns, a.status);

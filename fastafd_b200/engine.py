@@ -188,7 +188,7 @@ class AfdEngine:
                 else:
                     size = ag_layout(mcfg).size if self.is_attention else eg_layout(mcfg).size
                     fuse_tp = (self.is_attention and topo.attn_tp > 1 and cfg.hidden_size % 128 == 0
-                               and os.environ.get("FASTAFD_TP_FUSED", "0") == "1")     # opt-in, see parallel/tp_fused.py
+                               and os.environ.get("FASTAFD_TP_FUSED", "1") == "1")     # FASTAFD_TP_FUSED=0: NCCL collectives
                     if fuse_tp:
                         from .parallel.tp_fused import tp_layout
 

@@ -16,8 +16,9 @@ peer's all-gather release of the same layer (which follows its read of the previ
 and the next all-gather after the peer's reduce-scatter release; the NCCL collectives at the
 step boundary separate steps.
 
-Selected with ``FASTAFD_TP_FUSED=1``; without it a TP lane uses the NCCL communicator for the
-same two operations.
+The default for a TP lane on CUDA; ``FASTAFD_TP_FUSED=0`` sends the same two operations through the
+NCCL communicator. Measured on B200 (Qwen3-30B-A3B shapes): TP-2 + EP-2 on 4 GPUs 9.78 ms/step fused
+against 10.10 ms over NCCL; TP-4 + EP-4 on 8 GPUs 7.85 ms/step fused.
 
 Reference: python/minisgl/layers/linear.py:418-447 (o_proj + all-reduce),
 python/minisgl/distributed/impl.py:28-85.

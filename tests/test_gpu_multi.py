@@ -88,9 +88,6 @@ def test_attention_tp2_tracks_colocated(tp_fused):
     tolerance."""
     if torch.cuda.device_count() < 4:
         pytest.skip("needs 4 GPUs")
-    if tp_fused == "1" and os.environ.get("FASTAFD_TEST_TP_FUSED_MODEL") != "1":
-        pytest.skip("model-level run of the opt-in fused TP path: set FASTAFD_TEST_TP_FUSED_MODEL=1 "
-                    "(the collectives themselves are covered by the stress and loopback tests)")
     import torch.multiprocessing as mp
     from fastafd_b200.core import SamplingParams
     from fastafd_b200.engine import AfdEngine, SpmdDriver
