@@ -8,4 +8,5 @@ export PER_ATTN_GPU_BSZ="${PER_ATTN_GPU_BSZ:-128}"
 export NUM_GPUS="${NUM_GPUS:-8}"
 export ATTN_GPUS="${ATTN_GPUS:-4}"
 export STEPS="${STEPS:-32}"
+export ATTN_TP="${ATTN_TP:-1}"     # attention data-parallel lanes (ATTN_TP=4: one tensor-parallel lane)
 fastafd_run_bench

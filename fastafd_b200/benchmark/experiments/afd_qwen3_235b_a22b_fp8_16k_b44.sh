@@ -9,4 +9,5 @@ export NUM_GPUS="${NUM_GPUS:-8}"
 export ATTN_GPUS="${ATTN_GPUS:-4}"
 export NUM_MB="${NUM_MB:-2}"
 export STEPS="${STEPS:-32}"
+export ATTN_TP="${ATTN_TP:-1}"     # attention data-parallel lanes (ATTN_TP=4: one tensor-parallel lane)
 fastafd_run_bench

@@ -11,4 +11,5 @@ export NUM_MB="${NUM_MB:-2}"
 export STEPS="${STEPS:-32}"
 export SPEC_BLOCK="${SPEC_BLOCK:-4}"
 export SPEC_ACCEPT="${SPEC_ACCEPT:-1.8}"
+export ATTN_TP="${ATTN_TP:-1}"     # attention data-parallel lanes (ATTN_TP=4: one tensor-parallel lane)
 fastafd_run_bench
