@@ -14,6 +14,7 @@ PyNCCLDistributedImpl), python/minisgl/kernel/pynccl.py:92-99 (unique id broadca
 from __future__ import annotations
 
 import ctypes as C
+import os
 from typing import List, Optional
 
 import torch
@@ -86,6 +87,12 @@ class NcclComm(TpComm):
     @staticmethod
     def _load():
         from ..build import build_nccl_wrapper, nccl_lib_path
+
+        # In-switch reduction (NVLS) stays off for this communicator unless the user sets the variable:
+        # its collectives move a few hundred KB per call (latency-bound, nothing for the switch to win),
+        # and a rank that dies while its memory is bound to an NVLink multicast object takes its peers'
+        # GPUs with it, which the failure handling here must not risk.
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
 
         path = nccl_lib_path()
         if not path.exists():
