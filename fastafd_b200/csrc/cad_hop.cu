@@ -91,7 +91,7 @@ __global__ void __launch_bounds__(128) cad_wait_store_kernel(const CadWaitStoreA
 
 __global__ void cad_wait_kernel(const uint32_t* flags, long flag_stride, int n, const uint32_t* epoch,
                                 uint64_t timeout_ns, int* err) {
-  // no early trigger: the consumer behind a flag wait must not sit resident while the flag is awaited
+  pdl_trigger();
   pdl_wait();
   if (threadIdx.x < n) wait_flag_ge(flags + static_cast<size_t>(threadIdx.x) * flag_stride, *epoch + 1u, timeout_ns, err);
 }
