@@ -193,6 +193,7 @@ def main():
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}: launch with torch.distributed.run for N > 1")
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
+    nccl_world = None
     if world > 1:
         # device-side timeline of the N2M / M2N exchange (a few timer stores per kernel): the measured
         # round-trip and expert-busy times behind the n2m_m2n figures
@@ -201,6 +202,14 @@ def main():
         # host-side group: plans, tokens, barriers (gloo). Device collectives use the framework's own
         # NCCL communicator and fabric kernels, so torch needs no NCCL group of its own here.
         dist.init_process_group(backend="gloo", rank=rank, world_size=world)
+        # ... and an NCCL group over all ranks for the harness's own device collectives (the barriers
+        # around the timed regions and the max over ranks travel over NVLink). It is a sub-group of a
+        # gloo default group, created by every rank, first used after the engine is built.
+        if os.environ.get("FASTAFD_BENCH_NCCL_WORLD", "1") == "1":
+            try:
+                nccl_world = dist.new_group(backend="nccl")
+            except Exception as e:      # noqa: BLE001 - fall back to host barriers, say so
+                print(f"[bench rank {rank}] no NCCL world group ({type(e).__name__}: {e}); host barriers", file=sys.stderr)
 
     t_start = time.time()
     # A step that cannot finish (a peer that never arrives) must end the run with an error and the
@@ -252,15 +261,24 @@ def main():
 
     phase("engine built")
 
+    sync_word = torch.zeros(1, device=device) if world > 1 else None
+
     def barrier():
         torch.cuda.synchronize()
         if world > 1:
-            dist.barrier()
+            if nccl_world is not None:
+                dist.all_reduce(sync_word, group=nccl_world)      # every rank's GPU has reached this point
+            else:
+                dist.barrier()
         torch.cuda.synchronize()
 
     def max_over_ranks(x: float) -> float:
         if world == 1:
             return x
+        if nccl_world is not None:
+            t = torch.tensor([x], dtype=torch.float64, device=device)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX, group=nccl_world)
+            return float(t.item())
         t = torch.tensor([x], dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t[0])
