@@ -80,6 +80,14 @@ def reference_arm(args) -> None:
         print(json.dumps(out), flush=True)
 
 
+def default_attn_tp(world: int, attn_gpus: int = 0) -> int:
+    """Tensor-parallel size of an attention lane when the caller names none. 8 GPUs split 4+4: one TP-4
+    lane + EP-4, the configuration the benchmark is named for (it runs with the fused collectives;
+    attention DP4, --attn-tp 1, measured 6.66 against 7.85 ms/step on Qwen3-30B-A3B). Otherwise
+    data-parallel lanes."""
+    return 4 if (world == 8 and attn_gpus in (0, 4)) else 1
+
+
 def pick_num_mb(cfg, topo, batch_per_attn_gpu: int, context: int) -> int:
     """1 or 2 micro-batches from a two-term model of a layer (times in us, constants fitted to the
     device timelines measured on B200). A second micro-batch hides the expert round trip behind the
@@ -230,9 +238,7 @@ def main():
         cfg = cfg.with_layers(args.layers)
         truncated = True
     if args.attn_tp <= 0:
-        # 8 GPUs: attention TP4 + MLP EP4, the configuration the benchmark is named for (it completes with
-        # the fused collectives; attention DP4, --attn-tp 1, is about 10 % faster on this model)
-        args.attn_tp = 4 if (world == 8 and args.attn_gpus in (0, 4)) else 1
+        args.attn_tp = default_attn_tp(world, args.attn_gpus)
     topo = AfdTopology.for_world(world, attn_tp=args.attn_tp, attn_gpus=args.attn_gpus)
     if args.num_mb <= 0:
         args.num_mb = pick_num_mb(cfg, topo, args.batch_per_attn_gpu, args.context)

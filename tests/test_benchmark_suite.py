@@ -109,6 +109,11 @@ def test_bench_picks_micro_batches_from_the_layer_model():
     assert picks == {1: 1, 2: 1, 4: 1, 8: 2}
     big = get_model_config("qwen3-235b-a22b-fp8")
     assert bench.pick_num_mb(big, AfdTopology.for_world(8), 88, 8192) == 2
+    # the 8-GPU default is the named configuration (one TP-4 attention lane + EP-4), data-parallel lanes elsewhere
+    assert [bench.default_attn_tp(w) for w in (1, 2, 4, 8)] == [1, 1, 1, 4]
+    assert bench.default_attn_tp(8, attn_gpus=6) == 1
+    t = AfdTopology.for_world(8, attn_tp=bench.default_attn_tp(8))
+    assert (t.attn_dp, t.attn_tp, t.mlp_ep) == (1, 4, 4)
 
 
 def test_experiment_presets_build_valid_bench_commands(tmp_path):
