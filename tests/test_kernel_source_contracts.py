@@ -78,3 +78,62 @@ def test_flag_protocol_uses_one_system_fence_per_launch(name):
         if "set_flag_kernel" in before:          # the one-thread helper kernel
             continue
         assert "gridDim.x - 1" in before, f"system fence outside the last-CTA branch in {name}"
+
+
+def _c_struct_fields(src: str, name: str):
+    """Field names of `struct name { ... };` in declaration order (nested struct bodies are skipped, their
+    instance name counts as one field)."""
+    import re
+
+    start = src.index("struct " + name + " {")
+    i = src.index("{", start) + 1
+    depth, body, nested = 1, [], 0
+    while depth:
+        ch = src[i]
+        if ch == "{":
+            depth += 1
+            nested += 1
+        elif ch == "}":
+            depth -= 1
+            if depth == 1:
+                body.append("NESTED_END ")
+        if depth == 1 and ch not in "{}":
+            body.append(ch)
+        i += 1
+    text = re.sub(r"//[^\n]*", "", "".join(body))
+    names = []
+    for decl in text.split(";"):
+        decl = decl.strip()
+        if not decl:
+            continue
+        if decl.startswith("struct") and "NESTED_END" in decl:        # `struct X { ... } inst`
+            names.append(decl.split("NESTED_END")[-1].strip())
+            continue
+        decl = decl.replace("NESTED_END", "")
+        for part in decl.split(","):
+            m = re.search(r"([A-Za-z_][A-Za-z_0-9]*)\s*(\[[^\]]*\])?\s*$", part.strip())
+            if m:
+                names.append(m.group(1))
+    return names
+
+
+@pytest.mark.parametrize("py_cls,c_file,c_name", [
+    ("GroupedGemmDesc", "grouped_gemm.cu", "AfdGroupedGemmDesc"),
+    ("DispatchDesc", "moe_comm.cu", "AfdDispatchDesc"),
+    ("RouteDispatchDesc", "moe_comm.cu", "AfdRouteDispatchDesc"),
+    ("GroupDesc", "moe_comm.cu", "AfdGroupDesc"),
+    ("CombineDesc", "moe_comm.cu", "AfdCombineDesc"),
+    ("DirectDesc", "moe_direct.cu", "AfdDirectDesc"),
+    ("RouteDirectDesc", "moe_direct.cu", "AfdRouteDirectDesc"),
+])
+def test_ctypes_descriptors_list_the_fields_of_their_c_structs_in_order(py_cls, c_file, c_name):
+    """A descriptor crosses the language boundary by layout: the ctypes class must name the same fields in
+    the same order as the C struct it is passed as (a mismatch would only show on a GPU)."""
+    import os
+
+    from fastafd_b200.ops import _lib
+
+    src = open(os.path.join(os.path.dirname(_lib.__file__), "..", "csrc", c_file)).read()
+    c_fields = _c_struct_fields(src, c_name)
+    py_fields = [f[0] for f in getattr(_lib, py_cls)._fields_]
+    assert py_fields == c_fields, (py_fields, c_fields)
