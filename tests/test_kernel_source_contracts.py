@@ -81,8 +81,8 @@ def test_flag_protocol_uses_one_system_fence_per_launch(name):
 
 
 def _c_struct_fields(src: str, name: str):
-    """Field names of `struct name { ... };` in declaration order (nested struct bodies are skipped, their
-    instance name counts as one field)."""
+    """(name, kind) of the fields of `struct name { ... };` in declaration order (a nested struct's body is
+    skipped, its instance counts as one field of kind struct)."""
     import re
 
     start = src.index("struct " + name + " {")
@@ -101,20 +101,33 @@ def _c_struct_fields(src: str, name: str):
             body.append(ch)
         i += 1
     text = re.sub(r"//[^\n]*", "", "".join(body))
-    names = []
+    fields = []          # (name, kind): kind in ptr, int, float, long, u64, struct, with "[]" appended for arrays
     for decl in text.split(";"):
         decl = decl.strip()
         if not decl:
             continue
         if decl.startswith("struct") and "NESTED_END" in decl:        # `struct X { ... } inst`
-            names.append(decl.split("NESTED_END")[-1].strip())
+            fields.append((decl.split("NESTED_END")[-1].strip(), "struct"))
             continue
-        decl = decl.replace("NESTED_END", "")
-        for part in decl.split(","):
-            m = re.search(r"([A-Za-z_][A-Za-z_0-9]*)\s*(\[[^\]]*\])?\s*$", part.strip())
-            if m:
-                names.append(m.group(1))
-    return names
+        decl = decl.replace("NESTED_END", "").strip()
+        m = re.match(r"(?:const\s+)?(unsigned long long|void|int|float|long|[A-Za-z_][A-Za-z_0-9:]*)\s*(\*?)\s*(.*)$", decl, re.S)
+        base, star, rest = m.group(1), m.group(2), m.group(3)
+        kind = "ptr" if star else {"int": "int", "float": "float", "long": "long", "unsigned long long": "u64"}.get(base, "struct")
+        for part in rest.split(","):
+            dm = re.match(r"\s*\*?\s*([A-Za-z_][A-Za-z_0-9]*)\s*(\[[^\]]*\])?\s*$", part)
+            fields.append((dm.group(1), kind + ("[]" if dm.group(2) else "")))
+    return fields
+
+
+def _ctypes_kind(t) -> str:
+    import ctypes as C
+
+    if hasattr(t, "_length_"):
+        return _ctypes_kind(t._type_) + "[]"
+    if issubclass(t, C.Structure):
+        return "struct"
+    return {C.c_void_p: "ptr", C.c_int: "int", C.c_float: "float", C.c_long: "long", C.c_ulonglong: "u64",
+            C.c_uint: "int"}[t]
 
 
 @pytest.mark.parametrize("py_cls,c_file,c_name", [
@@ -128,12 +141,13 @@ def _c_struct_fields(src: str, name: str):
 ])
 def test_ctypes_descriptors_list_the_fields_of_their_c_structs_in_order(py_cls, c_file, c_name):
     """A descriptor crosses the language boundary by layout: the ctypes class must name the same fields in
-    the same order as the C struct it is passed as (a mismatch would only show on a GPU)."""
+    the same order and with the same kind of type (pointer, int, float, long, 64-bit, struct, array) as the C
+    struct it is passed as; a mismatch would only show on a GPU."""
     import os
 
     from fastafd_b200.ops import _lib
 
     src = open(os.path.join(os.path.dirname(_lib.__file__), "..", "csrc", c_file)).read()
     c_fields = _c_struct_fields(src, c_name)
-    py_fields = [f[0] for f in getattr(_lib, py_cls)._fields_]
-    assert py_fields == c_fields, (py_fields, c_fields)
+    py_fields = [(f[0], _ctypes_kind(f[1])) for f in getattr(_lib, py_cls)._fields_]
+    assert py_fields == c_fields, [(a, b) for a, b in zip(py_fields, c_fields) if a != b] or (py_fields, c_fields)
