@@ -151,3 +151,40 @@ def test_ctypes_descriptors_list_the_fields_of_their_c_structs_in_order(py_cls, 
     c_fields = _c_struct_fields(src, c_name)
     py_fields = [(f[0], _ctypes_kind(f[1])) for f in getattr(_lib, py_cls)._fields_]
     assert py_fields == c_fields, [(a, b) for a, b in zip(py_fields, c_fields) if a != b] or (py_fields, c_fields)
+
+
+def _c_api_arity():
+    """name -> number of parameters of every `extern "C" ... afd_name(...)` in the sources."""
+    arity = {}
+    for path in sorted(CSRC.rglob("*.c*")):
+        code = re.sub(r"//[^\n]*", "", path.read_text())
+        for m in re.finditer(r'extern\s+"C"\s+[A-Za-z_ \*]+?\b(afd_[a-z0-9_]+)\s*\(([^)]*)\)', code, re.S):
+            params = m.group(2).strip()
+            arity[m.group(1)] = 0 if params in ("", "void") else params.count(",") + 1
+    return arity
+
+
+def test_python_call_sites_pass_as_many_arguments_as_the_c_functions_take():
+    """ctypes checks nothing: a call with one argument too few reads garbage on the GPU side. Every
+    direct call `lib().afd_x(a, b, ...)` (no star-arguments) must match the C parameter count."""
+    import ast
+
+    arity = _c_api_arity()
+    assert len(arity) > 30
+    pkg = CSRC.parent
+    checked, bad = 0, []
+    for path in sorted(pkg.rglob("*.py")):
+        tree = ast.parse(path.read_text())
+        for node in ast.walk(tree):
+            if not (isinstance(node, ast.Call) and isinstance(node.func, ast.Attribute) and node.func.attr.startswith("afd_")):
+                continue
+            if any(isinstance(a, ast.Starred) for a in node.args) or node.keywords:
+                continue
+            name = node.func.attr
+            if name not in arity:
+                continue                     # e.g. a symbol of the NCCL wrapper declared inside extern "C" { }
+            checked += 1
+            if len(node.args) != arity[name]:
+                bad.append((str(path.relative_to(pkg)), node.lineno, name, len(node.args), arity[name]))
+    assert checked > 30, checked
+    assert not bad, bad
