@@ -88,12 +88,6 @@ class NcclComm(TpComm):
     def _load():
         from ..build import build_nccl_wrapper, nccl_lib_path
 
-        # In-switch reduction (NVLS) stays off for this communicator unless the user sets the variable:
-        # its collectives move a few hundred KB per call (latency-bound, nothing for the switch to win),
-        # and a rank that dies while its memory is bound to an NVLink multicast object takes its peers'
-        # GPUs with it, which the failure handling here must not risk.
-        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
-
         path = nccl_lib_path()
         if not path.exists():
             path = build_nccl_wrapper()
