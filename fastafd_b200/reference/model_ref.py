@@ -150,6 +150,28 @@ def greedy_generate_reference(cfg: ModelConfig, stage, expert_stages, prompts: L
     return outs
 
 
+def score_continuations(cfg: ModelConfig, stage, expert_stages, prompts: List[List[int]], outputs: List[List[int]]) -> dict:
+    """Teacher-forced scoring of sampled continuations: for every emitted token, its rank in this
+    reference forward's logits at that position (0 = the reference's own greedy choice). The rates
+    say how close a serving engine stays to the reference even after a near-tie flipped one token
+    (after which a token-for-token comparison is meaningless).
+    Reference: scripts/validate/compare_minisgl_vllm.py + check_alignment_report.py (rank hit rates of
+    the engine's greedy continuations under another engine's logprobs)."""
+    ranks: List[List[int]] = []
+    for prompt, out in zip(prompts, outputs):
+        r = []
+        for j, tok in enumerate(out):
+            lg = forward_logits(cfg, stage, expert_stages, list(prompt) + list(out[:j]))
+            r.append(int((lg > lg[tok]).sum()))
+        ranks.append(r)
+    flat = [x for r in ranks for x in r]
+    n = max(len(flat), 1)
+    return {"ranks": ranks, "tokens": len(flat),
+            "top1_agreement_rate": sum(x == 0 for x in flat) / n,
+            "top10_hit_rate": sum(x < 10 for x in flat) / n,
+            "top100_hit_rate": sum(x < 100 for x in flat) / n}
+
+
 def logit_check(cfg: ModelConfig, stage, expert_stages, prompts: List[List[int]], outputs: List[List[int]], taps,
                 rel_tol: float = 0.05, min_within: float = 0.75) -> dict:
     """Compare the logits a serving engine produced with this reference forward, teacher-forced on

@@ -5,8 +5,10 @@
 
 Generates greedily with the engine (fused kernels, CUDA graphs, micro-batches) and with the
 single-process PyTorch model (`reference/model_ref.py`) from the same weights, and reports the
-fraction of identical tokens, the first divergence of every prompt and a pass/fail verdict
-against `--min-match`. On CPU in fp32 the two paths must agree token for token; in bf16 on a GPU
+fraction of identical tokens, the first divergence of every prompt, the rank of every served token
+in the oracle's logits when the served continuation is teacher-forced through it (top-1 / top-10 /
+top-100 hit rates, the reference's alignment gate) and a pass/fail verdict against `--min-match`
+and the rank thresholds. On CPU in fp32 the two paths must agree token for token; in bf16 on a GPU
 near-ties in the logits may flip a token, after which the continuations differ, so the
 comparison there is by prefix.
 Reference: scripts/validate (alignment of the reference against vLLM); here the oracle is the
@@ -39,6 +41,10 @@ def main(argv=None) -> int:
     ap.add_argument("--num-mb", type=int, default=2)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--min-match", type=float, default=-1.0, help="default: 1.0 on CPU, 0.8 on CUDA")
+    ap.add_argument("--min-top1", type=float, default=-1.0, help="rank gate: share of emitted tokens that are the "
+                                                                 "oracle's own choice (default 1.0 on CPU, 0.9 on CUDA)")
+    ap.add_argument("--min-top10", type=float, default=0.99, help="rank gate: share within the oracle's top 10")
+    ap.add_argument("--min-top100", type=float, default=1.0, help="rank gate: share within the oracle's top 100")
     a = ap.parse_args(argv)
 
     from .config import ModelConfig, RuntimeConfig, get_model_config
@@ -65,22 +71,35 @@ def main(argv=None) -> int:
                 from .reference.model_ref import greedy_generate_reference
 
                 ref_out = greedy_generate_reference(cfg, eng.attn.model, [eng.expert_stage], prompts, a.decode)
-            return out, ref_out
+            return out, ref_out, eng
+
         finally:
             eng.close()
 
     if a.device == "cpu":
-        served, oracle = generate("cpu", False, True)
+        served, oracle, ref_eng = generate("cpu", False, True)
     else:
-        served, _ = generate(a.device, True, False)
-        _, oracle = generate("cpu", False, True)
+        served, _, _ = generate(a.device, True, False)
+        _, oracle, ref_eng = generate("cpu", False, True)
+    # rank gate: the served continuation, teacher-forced through the oracle (the weights outlive close())
+    from .reference.model_ref import score_continuations
+
+    score = score_continuations(cfg, ref_eng.attn.model, [ref_eng.expert_stage], prompts, served)
+    need1 = a.min_top1 if a.min_top1 >= 0 else (1.0 if a.device == "cpu" else 0.9)
+    rank_ok = (score["top1_agreement_rate"] >= need1 and score["top10_hit_rate"] >= a.min_top10
+               and score["top100_hit_rate"] >= a.min_top100)
     total = sum(len(o) for o in oracle)
     same = sum(x == y for s, o in zip(served, oracle) for x, y in zip(s, o))
     div = [first_divergence(s, o) for s, o in zip(served, oracle)]
     need = a.min_match if a.min_match >= 0 else (1.0 if a.device == "cpu" else 0.8)
-    ok = same >= need * total
+    ok = same >= need * total and rank_ok
     print(json.dumps({"model": a.model_path or a.model, "device": a.device, "tokens": total, "identical": same,
                       "match": round(same / max(total, 1), 4), "first_divergence": div, "min_match": need,
+                      "overall_top1_agreement_rate": round(score["top1_agreement_rate"], 4),
+                      "overall_top10_hit_rate": round(score["top10_hit_rate"], 4),
+                      "overall_top100_hit_rate": round(score["top100_hit_rate"], 4),
+                      "rank_gate": {"min_top1": need1, "min_top10": a.min_top10, "min_top100": a.min_top100,
+                                    "worst_rank": max((x for r in score["ranks"] for x in r), default=0)},
                       "verdict": "pass" if ok else "fail"}))
     return 0 if ok else 1
 

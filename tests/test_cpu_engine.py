@@ -69,4 +69,25 @@ def test_validate_cli_reports_full_agreement_on_cpu(capsys):
     rc = validate.main(["--device", "cpu", "--prompts", "2", "--prompt-len", "12", "--decode", "5"])
     out = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
     assert rc == 0 and out["verdict"] == "pass" and out["match"] == 1.0 and out["tokens"] == 10
+    assert out["overall_top1_agreement_rate"] == 1.0 and out["overall_top100_hit_rate"] == 1.0
+    assert out["rank_gate"]["worst_rank"] == 0
     assert validate.first_divergence([1, 2, 3], [1, 2, 4]) == 2 and validate.first_divergence([1], [1, 2]) == 1
+
+
+def test_rank_scoring_of_continuations_sees_a_foreign_token():
+    """The rank gate: the oracle's own greedy continuation scores rank 0 everywhere; replacing one token by
+    the oracle's least likely one shows up as one position outside the top 100."""
+    from fastafd_b200.reference.model_ref import forward_logits, greedy_generate_reference, score_continuations
+
+    cfg = PRESETS["tiny-qwen3-moe"]
+    eng = AfdEngine(cfg, _rt(), AfdTopology(colocated=True), 0, "cpu", seed=0)
+    stage, experts = eng.attn.model, [eng.expert_stage]
+    prompts = [[5, 9, 200, 31], [7, 7, 7, 1, 2]]
+    outs = greedy_generate_reference(cfg, stage, experts, prompts, 4)
+    good = score_continuations(cfg, stage, experts, prompts, outs)
+    assert good["tokens"] == 8 and good["top1_agreement_rate"] == 1.0 and all(x == 0 for r in good["ranks"] for x in r)
+    worst = int(forward_logits(cfg, stage, experts, prompts[0] + outs[0][:2]).argmin())
+    bad_out = [outs[0][:2] + [worst] + outs[0][3:], outs[1]]
+    bad = score_continuations(cfg, stage, experts, prompts, bad_out)
+    assert bad["ranks"][0][2] == cfg.vocab_size - 1 and bad["top100_hit_rate"] < 1.0 and bad["top1_agreement_rate"] < 1.0
+    eng.close()
