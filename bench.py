@@ -469,11 +469,20 @@ def main():
             out["config"]["deviation"] = "attention DP4 by request (--attn-tp 1); the named configuration is TP4, the default"
         if truncated:
             out["invalid"] = "model truncated with --layers (debug run)"
-        print(json.dumps(out))
+        print(json.dumps(out), flush=True)
+    # The measurement is done and printed. Tearing down process groups and peer mappings needs every rank;
+    # if one of them is slow to arrive, leave after a minute instead of holding the GPUs.
+    import threading
+
+    faulthandler.cancel_dump_traceback_later()
+    quit_timer = threading.Timer(60.0, lambda: os._exit(0))
+    quit_timer.daemon = True
+    quit_timer.start()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     eng.close()
+    quit_timer.cancel()
     faulthandler.cancel_dump_traceback_later()
 
 
