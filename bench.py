@@ -135,50 +135,101 @@ def apply_router_bias(eng, cfg, spec: str) -> None:
             w.copy_((pop / pop.max())[torch.randperm(E, generator=g)].to(w.device))
 
 
-class ClockSampler:
-    """nvidia-smi clock / throttle-reason samples taken while the timed region runs."""
+def summarize_clock_samples(lines, t0=None, t1=None) -> dict:
+    """Median SM clock, maximum SM clock and the throttle reasons seen in nvidia-smi csv lines
+    (timestamp, index, clocks.sm, clocks.max.sm, power, reasons.active, hw_slowdown, hw_thermal_slowdown,
+    sw_thermal_slowdown, sw_power_cap). With [t0, t1] (epoch seconds) only the samples taken inside the
+    timed region count; if the region was shorter than the sampling period, the nearest sample on each
+    side stands in and `in_region` says 0."""
+    import datetime
 
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+    rows = []
+    for line in lines:
+        f = [x.strip() for x in line.split(",")]
+        if len(f) < 10:
+            continue
+        try:
+            ts = datetime.datetime.strptime(f[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+            rows.append((ts, float(f[2]), float(f[3]), [v.lower().startswith("active") for v in f[6:10]]))
+        except ValueError:
+            continue
+    out = {"sm_mhz": None, "sm_max_mhz": None, "reasons": []}
+    if not rows:
+        return out
+    used, inside = rows, None
+    if t0 is not None and t1 is not None:
+        inside = [r for r in rows if t0 <= r[0] <= t1]
+        used = inside
+        if not used:
+            before = [r for r in rows if r[0] < t0][-1:]
+            after = [r for r in rows if r[0] > t1][:1]
+            used = before + after or rows[-1:]
+    names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+    reasons = sorted({n for r in used for n, on in zip(names, r[3]) if on})
+    out = {"sm_mhz": statistics.median(r[1] for r in used), "sm_max_mhz": max(r[2] for r in used), "reasons": reasons,
+           "samples": len(used)}
+    if inside is not None:
+        out["in_region"] = len(inside)
+    return out
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples of one GPU. The process is started early (nvidia-smi takes
+    a few hundred ms to come up); `mark_start` / `mark_end` bracket the timed region and only samples
+    between them are reported."""
+
+    Q = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
          "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, gpu_index: int):
         self.gpu_index, self.proc, self.path = gpu_index, None, None
+        self.t0 = self.t1 = None
+
+    def _gpu_id(self) -> str:
+        try:        # the UUID survives a permuted CUDA_VISIBLE_DEVICES, the index does not
+            import torch
+
+            return "GPU-" + str(torch.cuda.get_device_properties(self.gpu_index).uuid)
+        except Exception:
+            return str(self.gpu_index)
+
+    def _spawn(self, gpu_id: str):
+        return subprocess.Popen(["nvidia-smi", "-i", gpu_id, f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                 "-lms", "25"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
 
     def start(self):
         try:
             fd, self.path = tempfile.mkstemp(suffix=".csv")
             os.close(fd)
-            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                                          "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            self.proc = self._spawn(self._gpu_id())
+            time.sleep(0.2)
+            if self.proc.poll() is not None:            # the id was refused: fall back to the plain index
+                self.proc = self._spawn(str(self.gpu_index))
         except Exception:
             self.proc = None
 
+    def mark_start(self):
+        self.t0 = time.time()
+
+    def mark_end(self):
+        self.t1 = time.time()
+
     def stop(self):
-        out = {"sm_mhz": None, "sm_max_mhz": None, "reasons": []}
         if self.proc is None:
-            return out
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": []}
+        if self.t1 is not None:
+            time.sleep(0.06)            # one more sample behind the region
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
         except Exception:
             self.proc.kill()
-        sm, mx, reasons = [], [], set()
         try:
-            for line in open(self.path):
-                f = [x.strip() for x in line.split(",")]
-                if len(f) < 9 or not f[0].isdigit() or int(f[0]) != self.gpu_index:
-                    continue
-                sm.append(float(f[1]))
-                mx.append(float(f[2]))
-                for name, v in zip(("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"), f[5:9]):
-                    if v.lower().startswith("active"):
-                        reasons.add(name)
+            lines = open(self.path).read().splitlines()
             os.unlink(self.path)
         except Exception:
-            pass
-        if sm:
-            out = {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons), "samples": len(sm)}
-        return out
+            lines = []
+        return summarize_clock_samples(lines, self.t0, self.t1)
 
 
 def main():
@@ -290,23 +341,25 @@ def main():
         return float(t[0])
 
     # ---- warm-up (captures the graphs) -------------------------------------------------
+    sampler = ClockSampler(local_rank)
+    sampler.start()                     # up and sampling by the time the timed region starts
     drv.run_decode_steps(max(args.warmup, 3), pipelined=False)
     barrier()
     phase("warm-up done")
 
     # ---- device-timed region: K steps queued back to back --------------------------------
-    sampler = ClockSampler(local_rank)
-    sampler.start()
     launches0 = _lib.LAUNCHES["count"]
     graph_kernels = getattr(eng.attn, "graph_kernel_count", 0) if eng.attn else 0
     barrier()
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     stream = eng.attn.main_stream if eng.attn is not None else eng.expert.stream
+    sampler.mark_start()
     ev0.record(stream)
     step_events = [ev0]
     drv.run_decode_steps(args.steps, pipelined=True, events=step_events, event_stream=stream)
     ev1.record(stream)
     torch.cuda.synchronize()
+    sampler.mark_end()
     dev_ms = ev0.elapsed_time(ev1)
     per_step = sorted(step_events[i].elapsed_time(step_events[i + 1]) for i in range(len(step_events) - 1))
     tpot_p50 = per_step[len(per_step) // 2] if per_step else dev_ms / args.steps

@@ -175,3 +175,31 @@ def test_long_prompt_base_is_deterministic_and_sliced_contiguously(tmp_path):
         lp.slices_of_documents(docs, 50, 200, seed=3)
     assert lp.main(["--count", "3", "--target-tokens", "128", "--vocab", "1024", "--output", str(tmp_path / "o.jsonl")]) == 0
     assert len(lp.load(str(tmp_path / "o.jsonl"))) == 3
+
+
+def test_clock_samples_are_taken_from_inside_the_timed_region():
+    import datetime
+    import importlib.util
+    import os
+
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "bench.py")
+    spec = importlib.util.spec_from_file_location("bench_under_test2", path)
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+
+    base = datetime.datetime(2026, 1, 2, 3, 4, 5).timestamp()
+
+    def line(dt, sm, cap="Not Active", hw="Not Active"):
+        ts = datetime.datetime.fromtimestamp(base + dt).strftime("%Y/%m/%d %H:%M:%S.%f")[:-3]
+        return f"{ts}, 3, {sm}, 1965, 712.5, 0x0000000000000004, {hw}, Not Active, Not Active, {cap}"
+
+    lines = [line(0.00, 345), line(0.10, 1965), line(0.20, 1905, cap="Active"), line(0.30, 1935), line(0.40, 600, hw="Active")]
+    inside = bench.summarize_clock_samples(lines, base + 0.05, base + 0.35)
+    assert inside == {"sm_mhz": 1935.0, "sm_max_mhz": 1965.0, "reasons": ["sw_power_cap"], "samples": 3, "in_region": 3}
+    # a region between two samples: the neighbours stand in, and the record says so
+    short = bench.summarize_clock_samples(lines, base + 0.21, base + 0.29)
+    assert short["in_region"] == 0 and short["samples"] == 2 and short["sm_mhz"] == 1920.0
+    # no marks (the reference arm): every sample counts, the idle ones and the throttled one included
+    whole = bench.summarize_clock_samples(lines)
+    assert whole["samples"] == 5 and "hw_slowdown" in whole["reasons"] and "in_region" not in whole
+    assert bench.summarize_clock_samples(["garbage", ""]) == {"sm_mhz": None, "sm_max_mhz": None, "reasons": []}
