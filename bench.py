@@ -229,7 +229,10 @@ class ClockSampler:
             os.unlink(self.path)
         except Exception:
             lines = []
-        return summarize_clock_samples(lines, self.t0, self.t1)
+        try:
+            return summarize_clock_samples(lines, self.t0, self.t1)
+        except Exception as e:          # noqa: BLE001 - a clock record must never cost the measurement
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "error": f"{type(e).__name__}: {e}"}
 
 
 def main():
