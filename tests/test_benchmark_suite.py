@@ -203,3 +203,36 @@ def test_clock_samples_are_taken_from_inside_the_timed_region():
     whole = bench.summarize_clock_samples(lines)
     assert whole["samples"] == 5 and "hw_slowdown" in whole["reasons"] and "in_region" not in whole
     assert bench.summarize_clock_samples(["garbage", ""]) == {"sm_mhz": None, "sm_max_mhz": None, "reasons": []}
+
+
+def test_clock_sampler_end_to_end_against_a_fake_nvidia_smi(tmp_path, monkeypatch):
+    """The sampler process, its csv and the region marks, with a stand-in for nvidia-smi that prints one
+    line every 25 ms in the queried format."""
+    import importlib.util
+    import os
+    import stat
+    import time
+
+    fake = tmp_path / "nvidia-smi"
+    fake.write_text("#!/usr/bin/env python3\n"
+                    "import datetime, sys, time\n"
+                    "assert '-i' in sys.argv and any(a.startswith('--query-gpu=timestamp,index,clocks.sm') for a in sys.argv)\n"
+                    "while True:\n"
+                    "    ts = datetime.datetime.now().strftime('%Y/%m/%d %H:%M:%S.%f')[:-3]\n"
+                    "    print(f'{ts}, 0, 1965, 1965, 640.0, 0x0000000000000004, Not Active, Not Active, Not Active, Active', flush=True)\n"
+                    "    time.sleep(0.025)\n")
+    fake.chmod(fake.stat().st_mode | stat.S_IEXEC)
+    monkeypatch.setenv("PATH", str(tmp_path) + os.pathsep + os.environ["PATH"])
+    path = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "bench.py")
+    spec = importlib.util.spec_from_file_location("bench_under_test3", path)
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    s = bench.ClockSampler(0)
+    s.start()
+    time.sleep(0.3)
+    s.mark_start()
+    time.sleep(0.2)
+    s.mark_end()
+    out = s.stop()
+    assert out["sm_mhz"] == 1965.0 and out["sm_max_mhz"] == 1965.0 and out["reasons"] == ["sw_power_cap"]
+    assert 3 <= out["in_region"] <= 12 and out["samples"] == out["in_region"]
