@@ -14,7 +14,6 @@ PyNCCLDistributedImpl), python/minisgl/kernel/pynccl.py:92-99 (unique id broadca
 from __future__ import annotations
 
 import ctypes as C
-import os
 from typing import List, Optional
 
 import torch
