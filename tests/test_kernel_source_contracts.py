@@ -188,3 +188,27 @@ def test_python_call_sites_pass_as_many_arguments_as_the_c_functions_take():
                 bad.append((str(path.relative_to(pkg)), node.lineno, name, len(node.args), arity[name]))
     assert checked > 30, checked
     assert not bad, bad
+
+
+def test_host_process_groups_are_not_bound_to_a_device():
+    """A default process group bound to a device (`device_id=`) makes torch split an NCCL communicator inside
+    every later `new_group` on the non-member ranks only; with a gloo sub-group the members never join the
+    split and the job deadlocks during start-up. The harness and the workers therefore create a plain gloo
+    default group, and the CUDA tensor-parallel set-up makes no sub-group at all."""
+    import ast
+
+    root = CSRC.parent.parent
+    for rel in ("bench.py", "fastafd_b200/worker/main.py"):
+        tree = ast.parse((root / rel).read_text())
+        calls = [n for n in ast.walk(tree) if isinstance(n, ast.Call) and isinstance(n.func, ast.Attribute)
+                 and n.func.attr == "init_process_group"]
+        assert calls, rel
+        for c in calls:
+            assert not any(k.arg == "device_id" for k in c.keywords), f"{rel}: device-bound default group"
+            args = [a.value for a in c.args if isinstance(a, ast.Constant)]
+            args += [k.value.value for k in c.keywords if k.arg == "backend" and isinstance(k.value, ast.Constant)]
+            assert args == ["gloo"], (rel, args)
+    src = (root / "fastafd_b200" / "engine.py").read_text()
+    body = src[src.index("def make_tp_comms("):src.index("class AfdEngine:")]
+    cuda_part = body[body.index('if device.type == "cuda":'):body.index("mine = None")]
+    assert "new_group" not in cuda_part
