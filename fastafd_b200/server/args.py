@@ -22,6 +22,12 @@ class ServerArgs:
     host: str = "127.0.0.1"
     port: int = 1919
     launch_backend: str = "mp"           # mp | ray (ray is accepted only when importable)
+    ray_address: str = "auto"            # cluster address for --launch-backend ray
+    ray_log_dir: str = ""                # per-rank actor logs (empty: Ray's own log directory)
+    ray_nsys: bool = False               # profile every rank's actor with Nsight Systems
+    ray_nsys_output_prefix: str = ""     # default <ray-log-dir>/nsys/fastafd, else fastafd-ray
+    ray_node_scoped_cache: bool = False  # keep compile / kernel caches per node instead of forwarding the driver's
+    control_host: str = "127.0.0.1"      # driver address for control sockets and the rendezvous
     afd_attn_dp_size: int = 1
     afd_attn_tp_size: int = 1
     afd_mlp_dp_size: int = 1
@@ -91,6 +97,14 @@ def validate(args: ServerArgs) -> None:
         raise ValueError("--mode must be serve or afd-serve")
     if args.launch_backend not in ("mp", "ray"):
         raise ValueError("--launch-backend must be mp or ray")
+    if args.ray_nsys:
+        # preflight: a profile that cannot start must stop the launch, not a rank later
+        import shutil
+
+        if args.launch_backend != "ray":
+            raise ValueError("--ray-nsys needs --launch-backend ray")
+        if shutil.which("nsys") is None:
+            raise ValueError("--ray-nsys: Nsight Systems (nsys) is not installed on this node")
     if args.launch_backend == "ray":
         try:
             import ray  # noqa: F401
@@ -130,6 +144,14 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--host", default=d.host)
     p.add_argument("--port", type=int, default=d.port)
     p.add_argument("--launch-backend", default=d.launch_backend)
+    p.add_argument("--ray-address", default=d.ray_address, help="Ray cluster address (--launch-backend ray)")
+    p.add_argument("--ray-log-dir", default=d.ray_log_dir, help="directory for per-rank actor logs")
+    p.add_argument("--ray-nsys", action="store_true", help="profile every rank's actor with Nsight Systems")
+    p.add_argument("--ray-nsys-output-prefix", default=d.ray_nsys_output_prefix,
+                   help="default: <ray-log-dir>/nsys/fastafd when --ray-log-dir is set, else fastafd-ray")
+    p.add_argument("--ray-node-scoped-cache", action="store_true",
+                   help="every node keeps its own compile / kernel caches (the driver's cache paths are not forwarded)")
+    p.add_argument("--control-host", default=d.control_host, help="driver address for control sockets and the rendezvous")
     for name in ("attn-dp", "mlp-dp", "attn-tp", "mlp-tp", "mlp-ep"):
         p.add_argument(f"--afd-{name}-size", type=int, default=1)
     p.add_argument("--afd-moe-a2a-backend", default=d.afd_moe_a2a_backend)

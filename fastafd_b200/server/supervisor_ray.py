@@ -98,6 +98,33 @@ def actor_env(env: Optional[Mapping[str, str]] = None, extra_keys: Sequence[str]
     return out
 
 
+CACHE_ENV_KEYS: Tuple[str, ...] = ("TVM_FFI_CACHE_DIR", "FLASHINFER_WORKSPACE_BASE", "XDG_CACHE_HOME", "CUDA_CACHE_PATH")
+
+
+def nsys_prefix(ray_log_dir: str = "", output_prefix: str = "") -> str:
+    """Where a rank's Nsight Systems report goes: the explicit prefix, else <ray-log-dir>/nsys/fastafd,
+    else fastafd-ray (in the actor's working directory). The rank number is appended per actor."""
+    if output_prefix:
+        return output_prefix
+    return os.path.join(ray_log_dir, "nsys", "fastafd") if ray_log_dir else "fastafd-ray"
+
+
+def actor_options(slot: "Slot", env: Mapping[str, str], *, ray_log_dir: str = "", ray_nsys: bool = False,
+                  nsys_output_prefix: str = "", node_scoped_cache: bool = False) -> Dict[str, object]:
+    """Ray options of one rank's actor: pinned to its node, the forwarded environment, the rank's log
+    file when a log directory is given, an `nsys` runtime-env entry when profiling is on, and - with
+    node-scoped caches - without the driver's cache directories (every node then builds its own)."""
+    env = {k: v for k, v in env.items() if not (node_scoped_cache and k in CACHE_ENV_KEYS)}
+    if ray_log_dir:
+        env["FASTAFD_LOG_DIR"] = ray_log_dir
+        env["FASTAFD_RANK_LOG"] = os.path.join(ray_log_dir, f"rank{slot.rank}.log")
+    runtime_env: Dict[str, object] = {"env_vars": env}
+    if ray_nsys:
+        runtime_env["nsight"] = {"o": f"{nsys_prefix(ray_log_dir, nsys_output_prefix)}-rank{slot.rank}", "t": "cuda,nvtx",
+                                 "cuda-graph-trace": "node"}
+    return {"resources": {f"node:{slot.node}": 0.001}, "runtime_env": runtime_env}
+
+
 def check_runtime_versions(nodes: Sequence[NodeReport], keys: Sequence[str] = ("torch", "cuda", "package")) -> List[str]:
     """Problems that would make ranks disagree at run time: differing versions of the named
     components between nodes. Returns human-readable lines (empty = compatible)."""
@@ -138,7 +165,8 @@ class RaySupervisor:
             raise RayUnavailable("Ray is not installed: use --launch-backend mp (one node) or install ray") from e
         self.ray = ray
         self.args = server_args
-        self.address = address or os.environ.get("FASTAFD_RAY_ADDRESS") or os.environ.get("MINISGL_RAY_ADDRESS") or "auto"
+        self.address = (address or os.environ.get("FASTAFD_RAY_ADDRESS") or os.environ.get("MINISGL_RAY_ADDRESS")
+                        or getattr(server_args, "ray_address", "") or "auto")
         self.actors: List[object] = []
         self.plan: List[Slot] = []
 
@@ -164,7 +192,9 @@ class RaySupervisor:
         topo = self.args.topology
         nodes = self.reports()
         self.plan = plan_placement(nodes, topo)
-        head = next((n.address for n in nodes if n.is_head), self.plan[0].node)
+        head = getattr(self.args, "control_host", "") or next((n.address for n in nodes if n.is_head), self.plan[0].node)
+        if head == "127.0.0.1" and len({sl.node for sl in self.plan}) > 1:     # more than one node: a routable address
+            head = next((n.address for n in nodes if n.is_head), self.plan[0].node)
         addrs, ports = make_addresses(topo.world, head, head, {s.rank: s.node for s in self.plan})
         env = actor_env()
 
@@ -173,8 +203,11 @@ class RaySupervisor:
             def run(self, rank, world, args, addresses, port):
                 return worker_main(rank, world, args, addresses, port)
 
+        a = self.args
         for s in self.plan:
-            opts = {"resources": {f"node:{s.node}": 0.001}, "runtime_env": {"env_vars": env}}
+            opts = actor_options(s, env, ray_log_dir=getattr(a, "ray_log_dir", ""), ray_nsys=getattr(a, "ray_nsys", False),
+                                 nsys_output_prefix=getattr(a, "ray_nsys_output_prefix", ""),
+                                 node_scoped_cache=getattr(a, "ray_node_scoped_cache", False))
             actor = _Rank.options(**opts).remote()
             self.actors.append((actor, actor.run.remote(s.rank, topo.world, self.args, addrs, ports[topo.world + 5])))
         self.local = LocalSupervisor(self.args)

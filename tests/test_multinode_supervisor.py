@@ -110,3 +110,37 @@ def test_backend_process_leaves_when_its_parent_is_gone(tmp_path):
     if alive:
         os.kill(pid, 9)        # exact PID of the child this test started
     assert not alive, "the child outlived its parent"
+
+
+def test_ray_flags_parse_and_the_nsys_preflight_refuses_a_node_without_nsys(monkeypatch):
+    """The reference's `--ray-*` and `--control-host` flags are accepted; `--ray-nsys` is checked when the
+    flags are parsed (backend and the nsys binary), not when a rank starts."""
+    import shutil
+
+    from fastafd_b200.server import args as sa
+
+    p = sa.build_parser()
+    a = p.parse_args(["--ray-address", "10.0.0.7:6379", "--ray-log-dir", "/var/log/afd", "--ray-nsys-output-prefix", "x",
+                      "--ray-node-scoped-cache", "--control-host", "10.0.0.7"])
+    assert (a.ray_address, a.ray_log_dir, a.ray_nsys_output_prefix, a.ray_node_scoped_cache, a.control_host, a.ray_nsys) == \
+        ("10.0.0.7:6379", "/var/log/afd", "x", True, "10.0.0.7", False)
+    with pytest.raises(ValueError, match="launch-backend ray"):
+        sa.parse_args(["--mode", "afd-serve", "--model-path", "tiny-qwen3-moe", "--device", "cpu", "--ray-nsys"])
+    monkeypatch.setattr(shutil, "which", lambda name: None)
+    with pytest.raises(ValueError, match="nsys"):
+        sa.parse_args(["--mode", "afd-serve", "--model-path", "tiny-qwen3-moe", "--device", "cpu", "--ray-nsys",
+                       "--launch-backend", "ray"])
+
+
+def test_actor_options_carry_logs_profile_and_cache_scope():
+    slot = sr.Slot(3, "expert", "10.0.0.8", 1)
+    env = {"FASTAFD_DIRECT": "1", "TVM_FFI_CACHE_DIR": "/driver/cache", "NCCL_DEBUG": "WARN"}
+    plain = sr.actor_options(slot, env)
+    assert plain["resources"] == {"node:10.0.0.8": 0.001} and plain["runtime_env"] == {"env_vars": env}
+    full = sr.actor_options(slot, env, ray_log_dir="/logs", ray_nsys=True, node_scoped_cache=True)
+    ev = full["runtime_env"]["env_vars"]
+    assert "TVM_FFI_CACHE_DIR" not in ev and ev["FASTAFD_DIRECT"] == "1"           # the node builds its own cache
+    assert ev["FASTAFD_RANK_LOG"] == "/logs/rank3.log" and ev["FASTAFD_LOG_DIR"] == "/logs"
+    assert full["runtime_env"]["nsight"]["o"] == "/logs/nsys/fastafd-rank3"
+    assert sr.actor_options(slot, env, ray_nsys=True, nsys_output_prefix="/p/run")["runtime_env"]["nsight"]["o"] == "/p/run-rank3"
+    assert env == {"FASTAFD_DIRECT": "1", "TVM_FFI_CACHE_DIR": "/driver/cache", "NCCL_DEBUG": "WARN"}    # not modified
