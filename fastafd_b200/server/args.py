@@ -60,6 +60,21 @@ class ServerArgs:
     spec_block: int = 0
     spec_draft_path: str = ""
     seed: int = 0
+    tp_size: int = 1                     # colocated tensor parallelism of the reference; here TP belongs to afd-serve lanes
+    shell_mode: bool = False             # an interactive shell on the started backend instead of the HTTP server
+    model_source: str = "huggingface"    # accepted for compatibility: models are read from local directories only
+    moe_backend: str = "auto"            # accepted for compatibility: one expert path (tcgen05 grouped GEMM)
+    disable_pynccl: bool = False         # TP collectives without the own NCCL communicator (= FASTAFD_TP_FUSED=1 only)
+    distributed_timeout: float = 0.0     # seconds for host rendezvous / collectives (0: library default)
+    afd_disable_attention_decode_graph: bool = False
+    afd_disable_model_decode_graph: bool = False
+    # runtime replay: prompts given on the command line run through the started backend once, the
+    # continuations go to a sample bundle (what the alignment scripts score), then the process leaves
+    afd_prompt: Tuple[str, ...] = ()
+    afd_prompt_file: str = ""
+    afd_prompt_repeat: int = 1
+    afd_report_dir: str = ""
+    afd_sample_json: str = ""
     log_level: str = "INFO"
 
     @property
@@ -97,6 +112,13 @@ def validate(args: ServerArgs) -> None:
         raise ValueError("--mode must be serve or afd-serve")
     if args.launch_backend not in ("mp", "ray"):
         raise ValueError("--launch-backend must be mp or ray")
+    if args.tp_size != 1:
+        raise ValueError("--tensor-parallel-size: the colocated mode runs on one GPU; tensor parallelism is "
+                         "--afd-attn-tp-size under --mode afd-serve")
+    if args.afd_prompt_repeat < 1:
+        raise ValueError("--afd-prompt-repeat must be at least 1")
+    if args.afd_disable_attention_decode_graph or args.afd_disable_model_decode_graph:
+        args.disable_cuda_graph = True          # one graph per decode bucket holds both sides' work here
     if args.ray_nsys:
         # preflight: a profile that cannot start must stop the launch, not a rank later
         import shutil
@@ -157,8 +179,10 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--afd-moe-a2a-backend", default=d.afd_moe_a2a_backend)
     p.add_argument("--afd-moe-runner-backend", default=d.afd_moe_runner_backend)
     p.add_argument("--afd-batch-size", type=int, default=0)
-    p.add_argument("--afd-max-batched-tokens", type=int, default=d.afd_max_batched_tokens)
-    p.add_argument("--afd-max-running-requests", type=int, default=d.afd_max_running_requests)
+    p.add_argument("--afd-max-batched-tokens", "--max-extend-length", "--max-prefill-length", dest="afd_max_batched_tokens",
+                   type=int, default=d.afd_max_batched_tokens, help="tokens of one step (the chunk size of chunked prefill)")
+    p.add_argument("--afd-max-running-requests", "--max-running-requests", dest="afd_max_running_requests", type=int,
+                   default=d.afd_max_running_requests)
     p.add_argument("--afd-max-new-tokens", type=int, default=d.afd_max_new_tokens)
     p.add_argument("--afd-decode-graph-bs", type=_int_list, default=())
     p.add_argument("--afd-num-mb", type=int, default=d.afd_num_mb)
@@ -167,26 +191,41 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--afd-force-multi-mb-graph-overlap", action="store_true")
     p.add_argument("--afd-device-comm-num-sms", type=int, default=0)
     p.add_argument("--cache-type", default=d.cache_type)
-    p.add_argument("--cuda-graph-max-bs", type=int, default=d.cuda_graph_max_bs)
+    p.add_argument("--cuda-graph-max-bs", "--graph", dest="cuda_graph_max_bs", type=int, default=d.cuda_graph_max_bs)
     p.add_argument("--page-size", type=int, default=d.page_size)
     p.add_argument("--num-pages", type=int, default=0)
     p.add_argument("--max-seq-len-override", type=int, default=0)
-    p.add_argument("--attention-backend", default="auto")
+    p.add_argument("--attention-backend", "--attn", dest="attention_backend", default="auto")
     p.add_argument("--memory-ratio", type=float, default=d.memory_ratio)
     p.add_argument("--device", default=d.device)
     p.add_argument("--dtype", default=d.dtype)
-    p.add_argument("--dummy-weights", action="store_true")
+    p.add_argument("--dummy-weights", "--dummy-weight", dest="dummy_weights", action="store_true")
     p.add_argument("--disable-cuda-graph", action="store_true")
-    p.add_argument("--num-tokenizers", type=int, default=1)
+    p.add_argument("--num-tokenizers", "--num-tokenizer", "--tokenizer-count", dest="num_tokenizers", type=int, default=1)
     p.add_argument("--spec-block", type=int, default=0)
     p.add_argument("--spec-draft-path", default="")
     p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--tensor-parallel-size", "--tp-size", dest="tp_size", type=int, default=1,
+                   help="the reference's colocated TP size; here 1 (tensor parallelism is --afd-attn-tp-size under afd-serve)")
+    p.add_argument("--shell-mode", action="store_true", help="interactive shell on the started backend instead of HTTP")
+    p.add_argument("--model-source", default=d.model_source, choices=["huggingface", "modelscope"])
+    p.add_argument("--moe-backend", default=d.moe_backend)
+    p.add_argument("--disable-pynccl", action="store_true")
+    p.add_argument("--distributed-timeout", type=float, default=0.0)
+    p.add_argument("--afd-disable-attention-decode-graph", action="store_true")
+    p.add_argument("--afd-disable-model-decode-graph", action="store_true")
+    p.add_argument("--afd-prompt", action="append", default=[], help="runtime prompt text (repeatable)")
+    p.add_argument("--afd-prompt-file", default="", help="UTF-8 file, one runtime prompt per line")
+    p.add_argument("--afd-prompt-repeat", type=int, default=1)
+    p.add_argument("--afd-report-dir", default="")
+    p.add_argument("--afd-sample-json", default="", help="where the runtime replay writes its sample bundle")
     p.add_argument("--log-level", default="INFO")
     return p
 
 
 def parse_args(argv: Optional[Sequence[str]] = None) -> ServerArgs:
     ns = build_parser().parse_args(argv)
+    ns.afd_prompt = tuple(ns.afd_prompt)
     args = ServerArgs(**{k: v for k, v in vars(ns).items() if k in ServerArgs.__dataclass_fields__})
     if args.afd_batch_size and not args.afd_decode_graph_bs:
         args.afd_decode_graph_bs = (args.afd_batch_size,)

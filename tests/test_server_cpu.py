@@ -278,3 +278,48 @@ def test_buffered_log_file_flushes_by_count_and_on_demand(tmp_path):
     log.line("d")
     log.flush()
     assert path.read_text().splitlines()[-1].endswith(" d")
+
+
+@pytest.mark.timeout(300)
+def test_runtime_replay_writes_the_sample_bundle(tmp_path):
+    """`--afd-prompt` / `--afd-prompt-file`: the prompts run once through the started backend (attention
+    and expert processes, the HTTP app on a private port) and the continuations land in the sample
+    bundle; the same prompt gives the same tokens, a repeat factor repeats the list."""
+    from fastafd_b200.server.launch import run_runtime_replay, runtime_prompts
+    from fastafd_b200.server.supervisor import create_backend_supervisor
+
+    pf = tmp_path / "prompts.txt"
+    pf.write_text("ab\n\ncde\n", encoding="utf-8")
+    out = tmp_path / "report" / "bundle.json"
+    args = parse_args(["--mode", "afd-serve", "--model-path", "tiny-qwen3-moe", "--device", "cpu", "--afd-num-mb", "2",
+                       "--num-pages", "64", "--max-seq-len-override", "128", "--max-running-requests", "8", "--graph", "8",
+                       "--afd-prompt", "hello", "--afd-prompt-file", str(pf), "--afd-prompt-repeat", "2",
+                       "--afd-max-new-tokens", "5", "--afd-sample-json", str(out), "--afd-report-dir", str(tmp_path / "report")])
+    assert runtime_prompts(args) == ["hello", "ab", "cde"] * 2
+    bundle = run_runtime_replay(args, create_backend_supervisor(args))
+    on_disk = json.loads(out.read_text())
+    assert on_disk == bundle and bundle["model"] == "tiny-qwen3-moe" and len(bundle["samples"]) == 6
+    for s in bundle["samples"]:
+        assert s["num_generated_tokens"] == len(s["generated_token_ids"]) and 1 <= s["num_generated_tokens"] <= 5
+    first, second = bundle["samples"][:3], bundle["samples"][3:]
+    assert [s["prompt"] for s in first] == ["hello", "ab", "cde"]
+    assert [s["generated_token_ids"] for s in first] == [s["generated_token_ids"] for s in second]     # greedy
+    report = json.loads((tmp_path / "report" / "runtime_report.json").read_text())
+    assert report["prompts"] == 6 and report["worker_failures"] == []
+
+
+@pytest.mark.timeout(300)
+def test_shell_mode_talks_to_the_started_backend():
+    import io
+
+    from fastafd_b200.server.launch import _HttpLlm, local_endpoint
+    from fastafd_b200.server.supervisor import create_backend_supervisor
+    from fastafd_b200.shell import run_shell
+
+    args = parse_args(["--mode", "serve", "--model-path", "tiny-qwen3-moe", "--device", "cpu", "--num-pages", "64",
+                       "--max-seq-len-override", "128", "--max-running-requests", "4", "--graph", "4", "--shell-mode"])
+    assert args.shell_mode
+    out = io.StringIO()
+    with local_endpoint(args, create_backend_supervisor(args)) as base:
+        turns = run_shell(_HttpLlm(args, base), max_tokens=4, inp=io.StringIO("hi\n/reset\nagain\n/exit\n"), out=out)
+    assert turns == 2 and "(conversation cleared)" in out.getvalue()
