@@ -69,6 +69,41 @@ class _Env:
 
 ENV = _Env()
 
+# Knobs of the hot path that are read where they act (some of them in C, by getenv), with the reference's
+# name for the same switch where it has one. `apply_reference_aliases` copies a reference name that is set
+# onto the new name that is not, once, when the package is imported.
+HOT_PATH_KNOBS = {
+    "FASTAFD_PDL": "programmatic dependent launch of the decode-path kernels (default 1)",
+    "FASTAFD_DIRECT": "slot-claiming N2M exchange (default 1; 0 = receive slots + group/gather)",
+    "FASTAFD_TP_FUSED": "attention-TP collectives fused with the GEMMs over the fabric (default 1; 0 = NCCL)",
+    "FASTAFD_OWN_DENSE": "own tcgen05 kernel for dense projections (1 = bf16 and FP8, fp8 = FP8 only; default library)",
+    "FASTAFD_L2_PREFETCH_MB": "weights the gate/up GEMM pulls into L2 while it waits for its predecessor (default 64)",
+    "FASTAFD_LANE_STREAMS": "every micro-batch's attention-side chain on its own stream (default 0)",
+    "FASTAFD_ROUTE_TPC": "tokens per CTA of the route kernel (default 4)",
+    "FASTAFD_ROUTE_CLUSTER": "CTAs that share a token group's expert range in the route kernel (default by gate size)",
+    "FASTAFD_COMM_TRACE": "device-side timeline of the N2M / M2N exchange",
+}
+REFERENCE_ALIASES = {
+    "MINISGL_PDL": "FASTAFD_PDL",
+    "MINISGL_AFD_LANE_COMPUTE_STREAMS": "FASTAFD_LANE_STREAMS",
+    "MINISGL_MEGAMOE_EG_PREFETCH_MB": "FASTAFD_L2_PREFETCH_MB",
+    "MINISGL_MEGAMOE_AG_TIMING": "FASTAFD_COMM_TRACE",
+    "MINISGL_MEGAMOE_EG_TIMING": "FASTAFD_COMM_TRACE",
+}
+
+
+def apply_reference_aliases(environ=None) -> dict:
+    """For every reference name that is set while its new name is not, set the new name to the same
+    value. Returns what was copied (new name -> value)."""
+    environ = os.environ if environ is None else environ
+    copied = {}
+    for old, new in REFERENCE_ALIASES.items():
+        v = environ.get(old)
+        if v not in (None, "") and environ.get(new) in (None, ""):
+            environ[new] = v
+            copied[new] = v
+    return copied
+
 
 def afd_env(suffix: str, default: Optional[str] = None) -> Optional[str]:
     """Raw lookup of an AFD knob by suffix (FASTAFD_<suffix>, then MINISGL_AFD_<suffix>)."""

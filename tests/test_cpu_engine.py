@@ -91,3 +91,14 @@ def test_rank_scoring_of_continuations_sees_a_foreign_token():
     bad = score_continuations(cfg, stage, experts, prompts, bad_out)
     assert bad["ranks"][0][2] == cfg.vocab_size - 1 and bad["top100_hit_rate"] < 1.0 and bad["top1_agreement_rate"] < 1.0
     eng.close()
+
+
+def test_reference_environment_names_act_under_their_new_names():
+    from fastafd_b200.env import HOT_PATH_KNOBS, REFERENCE_ALIASES, apply_reference_aliases
+
+    env = {"MINISGL_PDL": "0", "MINISGL_MEGAMOE_EG_PREFETCH_MB": "32", "FASTAFD_L2_PREFETCH_MB": "8", "MINISGL_AFD_LANE_COMPUTE_STREAMS": ""}
+    copied = apply_reference_aliases(env)
+    assert copied == {"FASTAFD_PDL": "0"} and env["FASTAFD_PDL"] == "0"
+    assert env["FASTAFD_L2_PREFETCH_MB"] == "8"                # the new name wins when both are set
+    assert "FASTAFD_LANE_STREAMS" not in env                   # an empty value is not a setting
+    assert set(REFERENCE_ALIASES.values()) <= set(HOT_PATH_KNOBS)

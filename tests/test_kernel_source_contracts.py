@@ -212,3 +212,11 @@ def test_host_process_groups_are_not_bound_to_a_device():
     body = src[src.index("def make_tp_comms("):src.index("class AfdEngine:")]
     cuda_part = body[body.index('if device.type == "cuda":'):body.index("mine = None")]
     assert "new_group" not in cuda_part
+
+
+def test_every_registered_hot_path_knob_is_read_somewhere():
+    from fastafd_b200.env import HOT_PATH_KNOBS
+
+    pkg = CSRC.parent
+    text = "".join(p.read_text() for p in list(pkg.rglob("*.py")) + list(CSRC.rglob("*.cu*")) if p.name != "env.py")
+    assert [k for k in HOT_PATH_KNOBS if k not in text] == []
