@@ -323,3 +323,26 @@ def test_shell_mode_talks_to_the_started_backend():
     with local_endpoint(args, create_backend_supervisor(args)) as base:
         turns = run_shell(_HttpLlm(args, base), max_tokens=4, inp=io.StringIO("hi\n/reset\nagain\n/exit\n"), out=out)
     assert turns == 2 and "(conversation cleared)" in out.getvalue()
+
+
+def test_serve_script_takes_the_reference_scripts_options(tmp_path):
+    """`fastafd_server.sh --model PATH --port P <CLI flags> --extra-args "..."`: the printed command parses,
+    and a flag given by the caller replaces the script's default (argparse keeps the last occurrence)."""
+    import os
+    import shlex
+    import subprocess
+
+    script = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "fastafd_b200", "server", "fastafd_server.sh")
+    out = subprocess.run(["bash", script, "--model", "tiny-qwen3-moe", "--port", "19193", "--afd-attn-tp-size", "2",
+                          "--afd-attn-dp-size", "1", "--afd-mlp-ep-size", "2", "--launch-backend", "mp", "--extra-args",
+                          "--afd-max-new-tokens 1 --device cpu"], env=dict(os.environ, DRY_RUN="1"),
+                         capture_output=True, text=True, timeout=60)
+    assert out.returncode == 0, out.stderr
+    words = shlex.split(out.stdout.strip())
+    assert words[:3] == ["python", "-m", "fastafd_b200"]
+    a = parse_args(words[3:])
+    assert (a.model_path, a.port, a.afd_attn_tp_size, a.afd_attn_dp_size, a.afd_mlp_ep_size, a.afd_max_new_tokens) == \
+        ("tiny-qwen3-moe", 19193, 2, 1, 2, 1)
+    bad = subprocess.run(["bash", script, "--env", "not-this-env", "--model", "x"],
+                         env={k: v for k, v in os.environ.items() if k != "CONDA_DEFAULT_ENV"}, capture_output=True, text=True)
+    assert bad.returncode == 2 and "not-this-env" in bad.stderr
