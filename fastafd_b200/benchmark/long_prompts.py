@@ -24,33 +24,40 @@ from pathlib import Path
 from typing import Iterable, List, Optional, Sequence
 
 
-def zipf_prompt(rng: random.Random, n: int, vocab: int, exponent: float = 1.1, phrase_prob: float = 0.15,
-                first_id: int = 16) -> List[int]:
-    """n token ids: ranks drawn from a truncated Zipf law (rank r with weight r**-exponent, mapped to
-    ids scattered over the vocabulary), and with probability `phrase_prob` a phrase of 3-12 tokens
-    seen earlier in the same prompt is repeated (natural text re-uses its own n-grams)."""
+_ZIPF_TABLES: dict = {}
+
+
+def _zipf_table(usable: int):
+    """Cumulative integer weights of ranks 1..usable under a Zipf law with exponent 1 (weight 2^40 // r):
+    integers only, so the same seed gives the same prompts on every platform."""
+    t = _ZIPF_TABLES.get(usable)
+    if t is None:
+        cum, total = [], 0
+        for r in range(1, usable + 1):
+            total += (1 << 40) // r
+            cum.append(total)
+        t = _ZIPF_TABLES[usable] = (cum, total)
+    return t
+
+
+def zipf_prompt(rng: random.Random, n: int, vocab: int, phrase_prob_pct: int = 15, first_id: int = 16) -> List[int]:
+    """n token ids: ranks drawn from a Zipf law (rank r with weight 1/r, mapped to ids scattered over
+    the vocabulary), and with probability `phrase_prob_pct` % a phrase of 3-12 tokens seen earlier in
+    the same prompt is repeated (natural text re-uses its own n-grams). Integer arithmetic only."""
+    import bisect
+
     usable = max(vocab - first_id, 2)
-    # inverse-CDF sampling of a continuous power law, good enough for rank statistics and O(1) per token
-    a = 1.0 - exponent
-    hi = float(usable) ** a if a != 0 else 0.0
-
-    def rank() -> int:
-        u = rng.random()
-        if a == 0:
-            r = usable ** u
-        else:
-            r = (1.0 + u * (hi - 1.0)) ** (1.0 / a)
-        return min(int(r), usable) - 1
-
+    cum, total = _zipf_table(usable)
     stride = 2654435761 % usable or 1        # scatter ranks over the id space (a rank is not an id)
     out: List[int] = []
     while len(out) < n:
-        if len(out) > 32 and rng.random() < phrase_prob:
+        if len(out) > 32 and rng.randrange(100) < phrase_prob_pct:
             ln = rng.randint(3, 12)
             st = rng.randrange(0, len(out) - ln)
             out.extend(out[st:st + ln])
         else:
-            out.append(first_id + (rank() * stride) % usable)
+            rank = bisect.bisect_right(cum, rng.randrange(total))
+            out.append(first_id + (rank * stride) % usable)
     return out[:n]
 
 
@@ -108,7 +115,55 @@ def load(path: str, max_prompts: int = 0, max_tokens: int = 0) -> List[List[int]
     return out
 
 
+POOLS_FILE = Path(__file__).with_name("prompt_pools.json")
+
+
+def pool_name(model: str, isl: int, rows: int) -> str:
+    return f"{model}_isl{isl}_r{rows}"
+
+
+def build_pool(model: str, isl: int, rows: int, out_dir: Path, registry: Optional[dict] = None) -> dict:
+    """One prompt pool of a benchmark model: `rows` synthetic prompts of `isl` tokens over the model's
+    vocabulary, from the registry's seed. The file's sha256 is compared with the registered one: the
+    recorded step times were measured on exactly these prompts (`ok` False = a different file)."""
+    import hashlib
+
+    from ..config import get_model_config
+
+    reg = json.loads(POOLS_FILE.read_text()) if registry is None else registry
+    name = pool_name(model, isl, rows)
+    entry = reg["pools"].get(name, {})
+    preset = reg["models"][model]
+    seed = int(entry.get("seed", reg.get("seed", 20260527)))
+    path = out_dir / (name + ".jsonl")
+    save(synthetic(rows, isl, get_model_config(preset).vocab_size, seed), path)
+    digest = hashlib.sha256(path.read_bytes()).hexdigest()
+    want = entry.get("sha256")
+    return {"pool": name, "path": str(path), "sha256": digest, "registered": want, "ok": want in (None, digest)}
+
+
+def pools_main(argv: Sequence[str]) -> int:
+    """python -m fastafd_b200.benchmark.long_prompts build-pools --model qwen3-235b --out DIR --pool 8192:128 ..."""
+    ap = argparse.ArgumentParser(prog="fastafd_b200.benchmark.long_prompts build-pools")
+    ap.add_argument("--model", required=True, help="a key of prompt_pools.json 'models'")
+    ap.add_argument("--out", required=True, type=Path)
+    ap.add_argument("--pool", action="append", default=[], help="ISL:ROWS (repeatable)")
+    a = ap.parse_args(argv)
+    bad = 0
+    for spec in a.pool:
+        isl, rows = (int(x) for x in spec.split(":"))
+        res = build_pool(a.model, isl, rows, a.out)
+        print(json.dumps(res))
+        bad += 0 if res["ok"] else 1
+    return 1 if bad else 0
+
+
 def main(argv: Optional[Sequence[str]] = None) -> int:
+    import sys
+
+    argv = list(sys.argv[1:] if argv is None else argv)
+    if argv and argv[0] == "build-pools":
+        return pools_main(argv[1:])
     ap = argparse.ArgumentParser(prog="fastafd_b200.benchmark.long_prompts")
     ap.add_argument("--target-tokens", type=int, default=8192)
     ap.add_argument("--count", type=int, default=512)

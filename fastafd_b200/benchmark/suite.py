@@ -108,6 +108,47 @@ def run(name: str, out_root: Path, steps: int, warmup: int) -> Dict:
     return res
 
 
+def resolve_model(key: str, env=None, path: Path = HERE / "models.json") -> str:
+    """Where a benchmark model key comes from: FASTAFD_MODEL_<KEY>, else $FASTAFD_MODEL_ROOT/<dir> when it
+    exists, else the preset name (random-init weights of the same architecture)."""
+    env = os.environ if env is None else env
+    m = json.loads(path.read_text())["models"][key]
+    override = env.get("FASTAFD_MODEL_" + key.upper().replace("-", "_").replace(".", "_"))
+    if override:
+        return override
+    root = env.get("FASTAFD_MODEL_ROOT")
+    if root and (Path(root) / m["dir"]).is_dir():
+        return str(Path(root) / m["dir"])
+    return m["preset"]
+
+
+def prepare_draft(name: str, src: Path, dst: Path, path: Path = HERE / "models.json") -> Dict:
+    """Copy a downloaded draft-head directory to `dst` with the registry's changes to its config.json
+    (the Qwen3 EAGLE-3 head needs max_position_embeddings raised for 32K contexts). Weights are linked, not
+    copied, where the file system allows."""
+    import shutil
+
+    spec = json.loads(path.read_text())["drafts"][name]
+    dst.mkdir(parents=True, exist_ok=True)
+    for f in sorted(src.iterdir()):
+        if f.name == "config.json" or not f.is_file():
+            continue
+        target = dst / f.name
+        if target.exists():
+            target.unlink()
+        try:
+            os.link(f, target)
+        except OSError:
+            shutil.copy2(f, target)
+    cfg = json.loads((src / "config.json").read_text())
+    changed = {}
+    if "max_position_embeddings" in spec and cfg.get("max_position_embeddings") != spec["max_position_embeddings"]:
+        changed["max_position_embeddings"] = [cfg.get("max_position_embeddings"), spec["max_position_embeddings"]]
+        cfg["max_position_embeddings"] = spec["max_position_embeddings"]
+    (dst / "config.json").write_text(json.dumps(cfg, indent=1))
+    return {"draft": name, "dst": str(dst), "changed": changed}
+
+
 def summary(root: Path) -> List[Dict]:
     rows = []
     for d in sorted(root.iterdir()):
@@ -145,6 +186,12 @@ def main(argv=None) -> int:
     sp = sub.add_parser("record")
     sp.add_argument("name")
     sp.add_argument("run_dir")
+    sp = sub.add_parser("prepare-draft")
+    sp.add_argument("name")
+    sp.add_argument("src")
+    sp.add_argument("dst")
+    sp = sub.add_parser("resolve-model")
+    sp.add_argument("key")
     a = ap.parse_args(argv)
     cfgs = load_configs()
     if a.cmd == "list":
@@ -164,6 +211,12 @@ def main(argv=None) -> int:
         return 0 if res.get("verdict") in ("pass", "unrecorded") else 1
     if a.cmd == "record":
         print(json.dumps(record(a.name, Path(a.run_dir))))
+        return 0
+    if a.cmd == "prepare-draft":
+        print(json.dumps(prepare_draft(a.name, Path(a.src), Path(a.dst))))
+        return 0
+    if a.cmd == "resolve-model":
+        print(resolve_model(a.key))
         return 0
     for row in summary(Path(a.root)):
         print(json.dumps(row))

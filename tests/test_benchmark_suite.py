@@ -236,3 +236,47 @@ def test_clock_sampler_end_to_end_against_a_fake_nvidia_smi(tmp_path, monkeypatc
     out = s.stop()
     assert out["sm_mhz"] == 1965.0 and out["sm_max_mhz"] == 1965.0 and out["reasons"] == ["sw_power_cap"]
     assert 3 <= out["in_region"] <= 12 and out["samples"] == out["in_region"]
+
+
+def test_prompt_pools_are_pinned_by_sha256(tmp_path):
+    """A pool is a function of its name and the registry's seed; the builder compares the file's sha256
+    with the registered one (the recorded step times belong to exactly these prompts)."""
+    import json
+
+    from fastafd_b200.benchmark import long_prompts as lp
+
+    reg = json.loads(lp.POOLS_FILE.read_text())
+    assert len(reg["pools"]) >= 8 and all(len(p["sha256"]) == 64 for p in reg["pools"].values())
+    res = lp.build_pool("qwen3-30b", 1024, 256, tmp_path)
+    assert res["ok"] and res["sha256"] == reg["pools"]["qwen3-30b_isl1024_r256"]["sha256"]
+    rows = lp.load(res["path"])
+    assert len(rows) == 256 and all(len(r) == 1024 for r in rows)
+    tampered = json.loads(json.dumps(reg))
+    tampered["pools"]["qwen3-30b_isl1024_r256"]["sha256"] = "0" * 64
+    assert not lp.build_pool("qwen3-30b", 1024, 256, tmp_path, tampered)["ok"]
+    assert lp.pools_main(["--model", "qwen3-30b", "--out", str(tmp_path), "--pool", "1024:256"]) == 0
+    assert lp.build_pool("qwen3-30b", 512, 4, tmp_path)["registered"] is None        # an unregistered pool is only built
+
+
+def test_model_registry_and_draft_preparation(tmp_path):
+    import json
+
+    from fastafd_b200.benchmark import suite
+    from fastafd_b200.config import get_model_config
+
+    reg = json.loads((suite.HERE / "models.json").read_text())
+    for key, m in reg["models"].items():
+        get_model_config(m["preset"])
+        assert suite.resolve_model(key, env={}) == m["preset"]
+    (tmp_path / "Qwen3-30B-A3B").mkdir()
+    assert suite.resolve_model("qwen3-30b", env={"FASTAFD_MODEL_ROOT": str(tmp_path)}) == str(tmp_path / "Qwen3-30B-A3B")
+    assert suite.resolve_model("qwen3.5-397b", env={"FASTAFD_MODEL_QWEN3_5_397B": "/x/y"}) == "/x/y"
+    src, dst = tmp_path / "draft", tmp_path / "draft-pos262k"
+    src.mkdir()
+    (src / "config.json").write_text(json.dumps({"max_position_embeddings": 40960, "hidden_size": 4096}))
+    (src / "model.safetensors").write_bytes(b"weights")
+    out = suite.prepare_draft("eagle3-qwen3-235b", src, dst)
+    cfg = json.loads((dst / "config.json").read_text())
+    assert cfg == {"max_position_embeddings": 262144, "hidden_size": 4096} and out["changed"] == {"max_position_embeddings": [40960, 262144]}
+    assert (dst / "model.safetensors").read_bytes() == b"weights"
+    assert json.loads((src / "config.json").read_text())["max_position_embeddings"] == 40960       # the source is untouched
