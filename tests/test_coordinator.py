@@ -138,3 +138,20 @@ def test_shutdown_is_idempotent():
     coord.shutdown()
     coord.shutdown()
     assert t.stops == 1
+
+
+@pytest.mark.parametrize("kw,want", [(dict(async_pending_steps=3), 3), (dict(async_pending_steps=0), 1),
+                                     (dict(async_pending_steps=3, disable_overlap=True), 1),
+                                     (dict(async_pending_steps=3, spec_block=4), 2),
+                                     (dict(async_pending_steps=1, spec_block=4), 1)])
+def test_overlap_policy_steps_in_flight(kw, want):
+    """--afd-async-pending-steps steps are planned ahead; --afd-disable-overlap keeps one in flight;
+    speculative decoding keeps at most two (the committed lengths live on the attention GPUs)."""
+    from fastafd_b200.server.args import parse_args
+
+    coord = AfdCoordinator(PRESETS["tiny-qwen3-moe"], _rt(**kw), AfdTopology(colocated=True), FakeWorkers(),
+                           num_pages=64, max_comm_tokens=64)
+    assert coord.pending == want
+    a = parse_args(["--mode", "afd-serve", "--model-path", "tiny-qwen3-moe", "--device", "cpu", "--afd-disable-overlap",
+                    "--afd-async-pending-steps", "3"])
+    assert a.runtime_config().disable_overlap and a.runtime_config().async_pending_steps == 3
