@@ -17,15 +17,50 @@ from .protocol import AfdTopology
 from .tokenizer import load_tokenizer
 
 
+# The reference's keyword names for the same settings (python/minisgl/engine/config.py:20-37,
+# python/minisgl/scheduler/config.py:16-18) -> RuntimeConfig fields; None = accepted, nothing to set here.
+REFERENCE_KWARGS = {
+    "use_dummy_weight": "dummy_weights", "max_running_req": "max_running_requests",
+    "max_seq_len_override": "max_seq_len", "max_extend_tokens": "max_batched_tokens",
+    "num_page_override": "num_pages", "cuda_graph_bs": "decode_graph_bs",
+    "attention_backend": None, "moe_backend": None, "distributed_timeout": None, "use_pynccl": None,
+    "offline_mode": None, "ep_size": None, "dp_size": None, "dp_rank": None,
+}
+
+
+def translate_kwargs(kw: Dict[str, object]) -> Dict[str, object]:
+    """Keyword arguments of the reference's `LLM(...)` under this package's names. A value of None for a
+    size override means "not given" there and is dropped."""
+    out: Dict[str, object] = {}
+    for k, v in kw.items():
+        if k in REFERENCE_KWARGS:
+            new = REFERENCE_KWARGS[k]
+            if new is None or v is None:
+                continue
+            if k == "cuda_graph_bs":
+                v = tuple(int(x) for x in v)
+            out[new] = v
+        else:
+            out[k] = v
+    return out
+
+
 class LLM:
-    def __init__(self, model_path: str, device: Optional[str] = None, **runtime_kw):
+    def __init__(self, model_path: str, dtype=None, device: Optional[str] = None, **runtime_kw):
+        """`dtype`: a torch dtype or its name (default bfloat16 on CUDA, float32 on CPU). Keyword arguments are
+        RuntimeConfig fields; the reference's names (`use_dummy_weight`, `max_running_req`,
+        `max_seq_len_override`, `max_extend_tokens`, ...) are accepted too."""
+        if isinstance(dtype, str) and device is None and (dtype == "cpu" or dtype.startswith("cuda")):
+            dtype, device = None, dtype            # LLM(path, "cpu"): the device given positionally
         device = device or ("cuda" if torch.cuda.is_available() else "cpu")
         self.cfg = get_model_config(model_path)
         kw = dict(model_path=model_path, num_mb=1, max_running_requests=64, cuda_graph_max_bs=64,
                   max_seq_len=min(self.cfg.max_position, 4096), device=device,
                   dtype="bfloat16" if device.startswith("cuda") else "float32",
                   use_cuda_graph=device.startswith("cuda"))
-        kw.update(runtime_kw)
+        if dtype is not None:
+            kw["dtype"] = str(dtype).replace("torch.", "")
+        kw.update(translate_kwargs(runtime_kw))
         self.rt = RuntimeConfig(**kw)
         self.topo = AfdTopology(colocated=True)
         self.engine = AfdEngine(self.cfg, self.rt, self.topo, 0, device if ":" in device or device == "cpu" else device + ":0",
@@ -42,14 +77,17 @@ class LLM:
             self._out.setdefault(uid, []).extend(toks)
 
     def generate(self, prompts: Sequence[Union[str, Sequence[int]]],
-                 sampling_params: Optional[SamplingParams] = None) -> List[Dict[str, object]]:
+                 sampling_params: Union[None, SamplingParams, Sequence[SamplingParams]] = None) -> List[Dict[str, object]]:
         sp = sampling_params or SamplingParams(max_tokens=16)
+        sps = list(sp) if isinstance(sp, (list, tuple)) else [sp] * len(prompts)      # one for all, or one per prompt
+        if len(sps) != len(prompts):
+            raise ValueError(f"{len(prompts)} prompts but {len(sps)} sampling parameter sets")
         uids = []
-        for p in prompts:
+        for p, one in zip(prompts, sps):
             ids = list(self.tokenizer.encode(p)) if isinstance(p, str) else [int(t) for t in p]
             uid = self._uid
             self._uid += 1
-            self.coordinator.add_request(uid, ids, sp)
+            self.coordinator.add_request(uid, ids, one)
             uids.append(uid)
         self.coordinator.run_until_idle()
         out = []

@@ -346,3 +346,27 @@ def test_serve_script_takes_the_reference_scripts_options(tmp_path):
     bad = subprocess.run(["bash", script, "--env", "not-this-env", "--model", "x"],
                          env={k: v for k, v in os.environ.items() if k != "CONDA_DEFAULT_ENV"}, capture_output=True, text=True)
     assert bad.returncode == 2 and "not-this-env" in bad.stderr
+
+
+def test_offline_api_takes_the_reference_keywords_and_per_prompt_sampling():
+    """`LLM(path, dtype, use_dummy_weight=..., max_running_req=..., max_seq_len_override=..., ...)` and
+    `generate(prompts, [params per prompt])`, as a program written for the reference calls them."""
+    import torch
+
+    from fastafd_b200.llm import LLM, translate_kwargs
+
+    assert translate_kwargs({"use_dummy_weight": True, "max_running_req": 8, "max_seq_len_override": None,
+                             "cuda_graph_bs": [2, 4], "attention_backend": "auto", "page_size": 16}) == \
+        {"dummy_weights": True, "max_running_requests": 8, "decode_graph_bs": (2, 4), "page_size": 16}
+    llm = LLM("tiny-qwen3-moe", torch.float32, device="cpu", use_dummy_weight=True, max_running_req=4, cuda_graph_max_bs=4,
+              max_seq_len_override=128, num_page_override=64, max_extend_tokens=256, memory_ratio=0.9, cache_type="naive")
+    try:
+        assert (llm.rt.max_running_requests, llm.rt.max_seq_len, llm.rt.num_pages, llm.rt.max_batched_tokens, llm.rt.dtype) == \
+            (4, 128, 64, 256, "float32")
+        out = llm.generate([[5, 6, 7, 8], "ab"], [SamplingParams(max_tokens=3, ignore_eos=True),
+                                                  SamplingParams(max_tokens=5, ignore_eos=True)])
+        assert [len(o["token_ids"]) for o in out] == [3, 5] and all(isinstance(o["text"], str) for o in out)
+        with pytest.raises(ValueError):
+            llm.generate([[1, 2]], [SamplingParams(), SamplingParams()])
+    finally:
+        llm.shutdown()
