@@ -6,17 +6,20 @@
         --master-port P bench.py --gpus N --steps K --warmup W
 
 Layout: N = 1 runs attention and expert stages on one GPU; N >= 2 splits the GPUs into N/2
-attention ranks (data-parallel lanes) and N/2 expert ranks (expert-parallel), the 4+4 layout
-at N = 8. Per-attention-GPU batch is fixed (weak scaling). Data: synthetic - random-init
+attention ranks and N/2 expert ranks (expert-parallel). The attention ranks are data-parallel
+lanes at N = 2 and 4 and one tensor-parallel lane at N = 8 (attention TP4 + MLP EP4, the
+configuration the benchmark is named for; --attn-tp 1 gives four data-parallel lanes). The number
+of micro-batches comes from `pick_num_mb`. Per-attention-GPU batch is fixed (weak scaling). Data: synthetic - random-init
 weights of the named architecture, KV cache of `--context` tokens per request filled with
 random values, random token ids.
 
 Two numbers are produced:
   value : K decode steps queued back to back and timed on the device with CUDA events
           (max over ranks).
-  e2e   : the same K steps through the public engine API, one step at a time: plan on the
-          host, copy the step's inputs from pinned host memory, replay, read the sampled
-          tokens back to the host.
+  e2e   : the same K steps through the public engine API in its serving mode (one step ahead):
+          plan on the host, copy the step's inputs from pinned host memory, replay, read the
+          sampled tokens back to the host; `lock_step` is the same with nothing of step n+1 started
+          before step n's tokens are on the host.
 Prints one JSON line on rank 0.
 """
 from __future__ import annotations
