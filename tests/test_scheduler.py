@@ -233,3 +233,82 @@ def test_attention_split_policy_matches_the_measured_optima():
             s = pick(B, 4, 1, kv)
             assert 1 <= s <= 32 and (s == 1 or kv // s >= 256) and (s == 1 or B * 4 * s <= 148 * 3)
     assert pick(8, 2, 1, 16384, D=256) >= 1 and pick(200, 2, 1, 16384, D=256) == 1   # head_dim 256: one CTA per SM
+
+
+@pytest.mark.parametrize("cache_type,spec_block,seed", [("naive", 0, 1), ("radix", 0, 2), ("naive", 4, 3), ("radix", 0, 4), ("naive", 0, 5)])
+def test_randomised_soak_keeps_the_page_ledger_and_request_tables_consistent(monkeypatch, cache_type, spec_block, seed):
+    """Random arrivals (shared prefixes, long prompts that need chunked prefill), aborts, EOS and stop tokens,
+    steps planned one ahead of their completion (two under speculation) - with the page audit running
+    after every planned and every completed step. Every admitted request finishes or is aborted, every
+    output respects max_tokens, and at the end nothing is held."""
+    import random
+
+    import numpy as np
+
+    from fastafd_b200.core import SamplingParams
+    from fastafd_b200.scheduler.buckets import normalize_buckets, per_mb_real, select_bucket
+    from fastafd_b200.scheduler.lane import AdmissionError, LaneScheduler
+
+    monkeypatch.setenv("FASTAFD_PAGE_AUDIT", "1")
+    rng = random.Random(seed)
+    num_mb, max_running = 2, 6
+    s = LaneScheduler(0, num_pages=96, page_size=4, max_running=max_running, max_seq_len=96, num_mb=num_mb,
+                      max_batched_tokens=24, cache_type=cache_type, eos_token_ids=(3,), spec_block=spec_block, spec_pending=2)
+    buckets = normalize_buckets((), 8)
+    q = spec_block if spec_block > 1 else 1
+    window = 2
+    prefixes = [[50 + i for i in range(9)], [70 + i for i in range(5)]]
+    next_uid, step, inflight, outputs, limits, aborted, arrivals = 0, 0, [], {}, {}, set(), 40
+    for _ in range(3000):
+        # arrivals and aborts
+        if arrivals and rng.random() < 0.35:
+            ids = (rng.choice(prefixes) if rng.random() < 0.5 else []) + [rng.randrange(10, 40) for _ in range(rng.randint(1, 30))]
+            sp = SamplingParams(max_tokens=rng.randint(1, 12), ignore_eos=rng.random() < 0.5,
+                                stop_token_ids=(5,) if rng.random() < 0.2 else ())
+            try:
+                s.add_req(next_uid, ids, sp)
+                outputs[next_uid], limits[next_uid] = [], sp
+            except AdmissionError:
+                pass
+            next_uid += 1
+            arrivals -= 1
+        live = [u for u in outputs if u in s.states and u not in aborted]
+        if live and rng.random() < 0.05:
+            u = rng.choice(live)
+            s.abort(u)
+            aborted.add(u)
+        # plan a step when the window has room
+        if len(inflight) < window and not s.idle():
+            if s.has_prefill():
+                plan = s.schedule_prefill(step)
+            elif s.decode_real() > 0:
+                bucket = select_bucket(per_mb_real(s.decode_real(), num_mb), buckets)
+                plan = s.schedule_decode(step, bucket, q)
+            else:
+                plan = None
+                s.check_admission_stall()
+            if plan is not None:
+                inflight.append((step, plan))
+                step += 1
+        # complete the oldest step (always, when the window is full or nothing new can be planned)
+        if inflight and (len(inflight) >= window or rng.random() < 0.6 or s.idle()):
+            sid, plan = inflight.pop(0)
+            rows = sum(len(m.rows) for m in plan.mbs)
+            blk = q if plan.phase == "verify" else 1
+            toks = np.array([rng.choice([3, 5, 7, 8, 9, 11]) for _ in range(rows * blk)], dtype=np.int32)
+            acc = np.array([rng.randint(1, blk) for _ in range(rows)], dtype=np.int32) if blk > 1 else None
+            for uid, new, fin in s.complete(sid, toks, acc):
+                outputs[uid] += new
+                assert len(outputs[uid]) <= limits[uid].max_tokens
+                if fin:
+                    last = outputs[uid][-1]
+                    assert (len(outputs[uid]) == limits[uid].max_tokens or last in limits[uid].stop_token_ids
+                            or (last == 3 and not limits[uid].ignore_eos))
+        if not arrivals and s.idle() and not inflight:
+            break
+    else:
+        raise AssertionError("the lane did not drain")
+    s.audit_pages()
+    s.check_integrity()
+    assert not s.states and len(s.free_rows) == max_running
+    assert sum(1 for u in outputs if outputs[u]) > 10
