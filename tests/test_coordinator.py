@@ -155,3 +155,83 @@ def test_overlap_policy_steps_in_flight(kw, want):
     a = parse_args(["--mode", "afd-serve", "--model-path", "tiny-qwen3-moe", "--device", "cpu", "--afd-disable-overlap",
                     "--afd-async-pending-steps", "3"])
     assert a.runtime_config().disable_overlap and a.runtime_config().async_pending_steps == 3
+
+
+class RandomWorkers(WorkerTransport):
+    """Workers that answer with random tokens, out of order and late: a reply is released only after a
+    random number of polls, expert replies and attention replies of one step in any order."""
+
+    def __init__(self, seed):
+        import random
+
+        self.rng, self.waiting = random.Random(seed), []
+
+    def send_step(self, step_id, ag_plans, eg_plans):
+        for r, (plan, _) in ag_plans.items():
+            n = sum(len(mb.rows) for mb in plan.mbs)
+            toks = np.array([self.rng.choice([3, 7, 8, 9]) for _ in range(n)], np.int32)
+            self.waiting.append([self.rng.randint(0, 3), AgStepReply(step_id=step_id, rank=r, next_tokens=toks, status=0)])
+        for r in eg_plans:
+            self.waiting.append([self.rng.randint(0, 3), EgStepReply(step_id=step_id, rank=r)])
+
+    def poll(self, timeout_s):
+        out = []
+        for item in self.waiting:
+            item[0] -= 1
+        self.rng.shuffle(self.waiting)
+        out = [m for d, m in self.waiting if d < 0]
+        self.waiting = [it for it in self.waiting if it[0] >= 0]
+        return out
+
+
+@pytest.mark.parametrize("seed,cache", [(1, "naive"), (2, "radix"), (3, "naive")])
+def test_coordinator_soak_over_three_lanes(monkeypatch, seed, cache):
+    """Three attention lanes + two expert ranks, three steps in flight, replies late and out of order,
+    arrivals and aborts while steps are outstanding, page audit on in every lane: every request that was
+    not aborted gets all its tokens exactly once and in the end every lane is empty."""
+    import random
+
+    monkeypatch.setenv("FASTAFD_PAGE_AUDIT", "1")
+    rng = random.Random(seed)
+    cfg = PRESETS["tiny-qwen3-moe"]
+    topo = AfdTopology(attn_dp=3, mlp_ep=2)
+    got, done = {}, set()
+
+    def on_tokens(items):
+        for uid, toks, fin in items:
+            assert uid not in done, "tokens after the request finished"
+            got[uid] += toks
+            if fin:
+                done.add(uid)
+
+    coord = AfdCoordinator(cfg, _rt(async_pending_steps=3, cache_type=cache, max_batched_tokens=48), topo, RandomWorkers(seed),
+                           num_pages=64, max_comm_tokens=64, on_tokens=on_tokens)
+    limits, aborted, uid = {}, set(), 0
+    shared = [40 + i for i in range(10)]
+    for it in range(4000):
+        if uid < 45 and rng.random() < 0.3:
+            ids = (shared if rng.random() < 0.5 else []) + [rng.randrange(10, 30) for _ in range(rng.randint(1, 40))]
+            sp = SamplingParams(max_tokens=rng.randint(1, 10), ignore_eos=rng.random() < 0.6)
+            got[uid], limits[uid] = [], sp
+            coord.add_request(uid, ids, sp)
+            uid += 1
+        live = [u for u in got if u not in done and u not in aborted]
+        if live and rng.random() < 0.03:
+            u = rng.choice(live)
+            coord.abort(u)
+            aborted.add(u)
+        coord.step_loop_once(block=False)
+        assert coord.get_failure() is None
+        if uid >= 45 and coord.idle():
+            break
+    else:
+        raise AssertionError("the coordinator did not drain")
+    for u, sp in limits.items():
+        if u in aborted:
+            continue
+        assert u in done and 1 <= len(got[u]) <= sp.max_tokens
+        assert len(got[u]) == sp.max_tokens or (got[u][-1] in cfg.eos_token_ids and not sp.ignore_eos)
+    for lane in coord.lanes:
+        lane.audit_pages()
+        assert not lane.states
+    coord.shutdown()
