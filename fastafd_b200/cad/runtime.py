@@ -113,23 +113,22 @@ class CadAttentionRank:
         self.win.o[mb][:sel.shape[0]][sel] = o.reshape(-1, Hq * D).to(self.win.o.dtype)   # straight into the model rank's window
 
 
-class CadRuntime:
-    """One model rank with `r` attention ranks, experts local to the model rank."""
+class CadModelMath:
+    """Model-side layer math of a CAD decode step over `self.windows` (one per peer): a micro-batch's row `k`
+    belongs to peer `st.owner[k]` and travels at index `k` of that peer's window. Needs `self.cfg`,
+    `self.stage` (AttentionStage), `self.experts` (ExpertStage) and `self.windows`."""
 
-    def __init__(self, cfg: ModelConfig, stage: AttentionStage, experts: ExpertStage, ccfg: CadConfig, *, num_mb: int,
-                 max_tokens: int, page_size: int, num_pages: int, wait_timeout_s: float = 5.0):
-        if any(cfg.layer_type(i) != "full" for i in range(cfg.num_layers)):
-            raise ValueError("CAD serves full-attention layers only")
-        self.cfg, self.stage, self.experts, self.ccfg = cfg, stage, experts, ccfg
-        self.num_mb, self.page_size, self.wait_timeout_s = num_mb, page_size, wait_timeout_s
-        self.r = ccfg.attn_per_model
-        check_balanced(cfg.num_layers, num_mb, self.r)
-        lay = CadLayout(cfg.num_layers, num_mb, max_tokens, cfg.q_size, cfg.kv_size)
-        dt, dev = stage.dtype, stage.device
-        self.windows = [CadWindow.local(lay, dt, dev) for _ in range(self.r)]
-        self.attn = [CadAttentionRank(cfg, w, num_pages * page_size, dt, dev) for w in self.windows]
+    def embed_mb(self, ids: torch.Tensor, positions: torch.Tensor, owner: torch.Tensor) -> "_MbState":
+        c, m = self.cfg, self.stage
+        h = m.embed(ids)
+        st = _MbState(ids, positions, owner, residual=h.clone())
+        st.normed = ops.rmsnorm(h, m.w["model.layers.0.input_layernorm.weight"], c.rms_eps, c.norm_offset1)
+        return st
 
-    # ------------------------------------------------------------------ model-side tasks
+    def sample_mb(self, st: "_MbState") -> torch.Tensor:
+        st.logits = self.stage.lm_head(st.normed)
+        return ops.argmax(st.logits)
+
     def _hqkv(self, layer: int, mb: int, st: _MbState, slots, page_table, seq_lens) -> None:
         c, m = self.cfg, self.stage
         p = f"model.layers.{layer}.self_attn."
@@ -165,6 +164,23 @@ class CadRuntime:
         nw = (m.w[f"model.layers.{layer + 1}.input_layernorm.weight"] if layer + 1 < c.num_layers else m.w["model.norm.weight"])
         st.normed = ops.add_rmsnorm(y, st.residual, nw, c.rms_eps, c.norm_offset1)
 
+
+class CadRuntime(CadModelMath):
+    """One model rank with `r` attention ranks, experts local to the model rank."""
+
+    def __init__(self, cfg: ModelConfig, stage: AttentionStage, experts: ExpertStage, ccfg: CadConfig, *, num_mb: int,
+                 max_tokens: int, page_size: int, num_pages: int, wait_timeout_s: float = 5.0):
+        if any(cfg.layer_type(i) != "full" for i in range(cfg.num_layers)):
+            raise ValueError("CAD serves full-attention layers only")
+        self.cfg, self.stage, self.experts, self.ccfg = cfg, stage, experts, ccfg
+        self.num_mb, self.page_size, self.wait_timeout_s = num_mb, page_size, wait_timeout_s
+        self.r = ccfg.attn_per_model
+        check_balanced(cfg.num_layers, num_mb, self.r)
+        lay = CadLayout(cfg.num_layers, num_mb, max_tokens, cfg.q_size, cfg.kv_size)
+        dt, dev = stage.dtype, stage.device
+        self.windows = [CadWindow.local(lay, dt, dev) for _ in range(self.r)]
+        self.attn = [CadAttentionRank(cfg, w, num_pages * page_size, dt, dev) for w in self.windows]
+
     # ------------------------------------------------------------------ one decode step
     def decode_step(self, mbs: List[Tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]],
                     drop: Optional[Tuple[str, int, int]] = None) -> List[torch.Tensor]:
@@ -177,10 +193,7 @@ class CadRuntime:
         L, nmb = c.num_layers, self.num_mb
         states = []
         for ids, pos, pt, owner in mbs:
-            h = m.embed(ids)
-            st = _MbState(ids, pos, owner, residual=h.clone())
-            st.normed = ops.rmsnorm(h, m.w["model.layers.0.input_layernorm.weight"], c.rms_eps, c.norm_offset1)
-            states.append(st)
+            states.append(self.embed_mb(ids, pos, owner))
         ps = self.page_size
         seq_lens = [pos + 1 for _, pos, _, _ in mbs]
         slots = [torch.gather(pt, 1, (pos // ps).long()[:, None])[:, 0] * ps + pos % ps for _, pos, pt, _ in mbs]
@@ -227,8 +240,7 @@ class CadRuntime:
                 time.sleep(0.001)
         out = []
         for st in states:
-            st.logits = m.lm_head(st.normed)
-            out.append(ops.argmax(st.logits))
+            out.append(self.sample_mb(st))
         for w in self.windows:                                    # epoch bump is the last action of a step
             w.bump_epoch()
         return out

@@ -62,15 +62,37 @@ class LLM:
             kw["dtype"] = str(dtype).replace("torch.", "")
         kw.update(translate_kwargs(runtime_kw))
         self.rt = RuntimeConfig(**kw)
+        self.tokenizer = load_tokenizer(model_path)
+        self._out: Dict[int, List[int]] = {}
+        self._uid = 0
+        from .cad.config import CadConfig
+
+        cad = CadConfig.from_env()
+        if cad.enabled:
+            return self._init_cad(cad, device)
         self.topo = AfdTopology(colocated=True)
         self.engine = AfdEngine(self.cfg, self.rt, self.topo, 0, device if ":" in device or device == "cpu" else device + ":0",
                                 seed=self.rt.seed, fast_init=device.startswith("cuda"))
-        self.tokenizer = load_tokenizer(model_path)
-        self._out: Dict[int, List[int]] = {}
         self.coordinator = AfdCoordinator(self.cfg, self.rt, self.topo, InProcTransport({0: self.engine}),
                                           num_pages=self.engine.attn.num_pages,
                                           max_comm_tokens=self.engine.max_comm_tokens, on_tokens=self._on_tokens)
-        self._uid = 0
+
+    def _init_cad(self, cad, device: str) -> None:
+        """``FASTAFD_MODE=cad`` (the reference's ``MINISGL_AFD_MODE=cad``): core-attention disaggregation with
+        one model rank and ``FASTAFD_CAD_ATTN_PER_MODEL`` attention ranks, every rank an object of this process.
+        CPU only: between GPU processes the hop kernels and the two sides' hooks exist (cad/gpu.py), the worker
+        loops that take CAD commands from the coordinator do not."""
+        if device != "cpu":
+            raise NotImplementedError("CAD through the offline API runs on CPU (device='cpu')")
+        from .cad.coordinator import CadCoordinator
+        from .cad.deploy import CadLocalWorkers
+
+        self.engine = None
+        self.topo = AfdTopology(attn_dp=cad.attn_per_model, mlp_ep=1)
+        workers = CadLocalWorkers(self.cfg, self.rt, self.topo, seed=self.rt.seed, device=device)
+        comm = max(self.rt.cuda_graph_max_bs, min(2048, self.rt.max_batched_tokens // max(self.rt.num_mb, 1)))
+        self.coordinator = CadCoordinator(self.cfg, self.rt, self.topo, workers, num_pages=workers.num_pages,
+                                          max_comm_tokens=comm, on_tokens=self._on_tokens)
 
     def _on_tokens(self, items) -> None:
         for uid, toks, _fin in items:
@@ -98,4 +120,5 @@ class LLM:
 
     def shutdown(self) -> None:
         self.coordinator.shutdown()
-        self.engine.close()
+        if self.engine is not None:
+            self.engine.close()

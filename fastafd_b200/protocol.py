@@ -229,8 +229,41 @@ class WorkerFailure:
     error: str
 
 
+# ---- core-attention disaggregation: decode steps with the roles turned (cad/coordinator.py)
+@dataclass
+class CadInitCmd:
+    """Sent once to every rank before the first CAD step: the decode buckets, the largest bucket, the rows
+    of a lane's request table (with its padding row) and the micro-batches per step."""
+    buckets: List[int]
+    t_max: int
+    table_rows: int
+    num_mb: int
+    use_graph: bool = True
+
+
+@dataclass
+class CadStepCmd:
+    """One decode step. An attention rank gets its lane's `plan` (rows, lengths, page grants: the KV side of
+    the step); a model rank gets `rows`, int32 [n, 6] as cad.tokens.pack_rows lays them out."""
+    step_id: int
+    bucket: int
+    plan: Optional[AgStepPlan] = None
+    rows: Optional[np.ndarray] = None
+
+
+@dataclass
+class CadStepReply:
+    """`tokens`: peer index -> sampled tokens of that peer's lane in the lane scheduler's order (model ranks
+    only). `err` != 0: a wait ran out, the step's result is void and the rank keeps serving."""
+    step_id: int
+    rank: int
+    tokens: Dict[int, np.ndarray] = field(default_factory=dict)
+    err: int = 0
+    step_ms: float = 0.0
+
+
 _TYPES = {c.__name__: c for c in (MicroBatchPlan, AgStepPlan, EgStepPlan, RunStepCmd, StopCmd, AgStepReply,
-                                  EgStepReply, WorkerReady, WorkerFailure)}
+                                  EgStepReply, WorkerReady, WorkerFailure, CadInitCmd, CadStepCmd, CadStepReply)}
 
 
 def _enc(o: Any) -> Any:
