@@ -65,6 +65,7 @@ class CadAttentionSide:
         w, c, plan, B = self.w, self.cfg, cmd.plan, cmd.bucket
         if plan.phase != "decode" or plan.bucket != B:
             raise ValueError(f"CAD attention step {cmd.step_id}: phase {plan.phase}, bucket {plan.bucket} != {B}")
+        self.win.begin_step(B)
         w.apply_grants(plan)
         w._stage_decode(plan)
         for mb in range(w.num_mb):
@@ -88,6 +89,7 @@ class CadAttentionSide:
                                      1, w.page_size, ref.softmax_scale(D))
             self.win.o[t.mb][lo:lo + B] = o.reshape(B, Hq * D).to(self.win.o.dtype)
             self.win.release(1, t.layer, t.mb)
+        self.win.end_step()
 
 
 class CadModelRank(CadModelMath):
@@ -102,6 +104,8 @@ class CadModelRank(CadModelMath):
         c, tok, B = self.cfg, self.tokens, cmd.bucket
         tok.bind(B)
         tok.stage(unpack_rows(cmd.rows))
+        for w in self.windows:
+            w.begin_step(B)
         ids, pos = tok.input_ids(), tok.positions()
         owner = torch.arange(self.r, device=ids.device).repeat_interleave(B)
         states = [self.embed_mb(ids[tok.mb_rows(m)], pos[tok.mb_rows(m)], owner) for m in range(tok.num_mb)]
@@ -113,6 +117,8 @@ class CadModelRank(CadModelMath):
                     yield ("o", t.layer, t.mb)
                 self._hpost_ffn(t.layer, t.mb, states[t.mb])
         tok.record(torch.cat([self.sample_mb(st) for st in states]))
+        for w in self.windows:
+            w.end_step()
         return tokens_by_peer(tok.out[:tok.rows].tolist(), self.r, tok.num_mb, B)
 
 

@@ -71,6 +71,13 @@ class CadWindow:
     def ready(self, kind: int, layer: int, mb: int) -> bool:
         return int(self.flags[kind, layer, mb]) == self.epoch + 1
 
+    def begin_step(self, bucket: int) -> None:
+        """Rows per peer and micro-batch of the step that starts (a transport that moves rows needs the size)."""
+        self.bucket = bucket
+
+    def end_step(self) -> None:
+        """Called by each side after its last task of a step."""
+
     def set_err(self, code: int = 1) -> None:
         self.err[0] = code
 
@@ -155,7 +162,7 @@ class CadModelMath:
         x = m.post_attn_norm(layer, attn_out, st.residual)
         if c.is_moe_layer(layer):
             idx, wts = m.route(layer, x)
-            y = combine_rows(self.experts.run_experts_dense(layer, x, idx), wts, idx, c.routed_scaling_factor)
+            y = combine_rows(self.expert_rows(layer, x, idx), wts, idx, c.routed_scaling_factor)
             extra = m.local_mlp(layer, x)
             if extra is not None:
                 y = (y.float() + extra.float()).to(y.dtype)
@@ -163,6 +170,11 @@ class CadModelMath:
             y = m.local_mlp(layer, x)
         nw = (m.w[f"model.layers.{layer + 1}.input_layernorm.weight"] if layer + 1 < c.num_layers else m.w["model.norm.weight"])
         st.normed = ops.add_rmsnorm(y, st.residual, nw, c.rms_eps, c.norm_offset1)
+
+    def expert_rows(self, layer: int, x: torch.Tensor, idx: torch.Tensor) -> torch.Tensor:
+        """Expert outputs [K, T, H] of the routed rows. Here: every expert is local; a model rank that holds a
+        slice of the experts overrides this with the exchange among the model ranks."""
+        return self.experts.run_experts_dense(layer, x, idx)
 
 
 class CadRuntime(CadModelMath):

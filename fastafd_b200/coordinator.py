@@ -319,6 +319,15 @@ class ZmqWorkerTransport(WorkerTransport):
         for r, plan in eg_plans.items():
             self.cmd[r].put(self._Run(plan=plan))
 
+    def send_cad_init(self, cmd) -> None:
+        """Core-attention disaggregation (cad/coordinator.py): the init command goes to every rank."""
+        for q in self.cmd.values():
+            q.put(cmd)
+
+    def send_cad_step(self, step_id, attn_cmds, model_cmds) -> None:
+        for r, c in list(attn_cmds.items()) + list(model_cmds.items()):
+            self.cmd[r].put(c)
+
     def poll(self, timeout_s):
         out = []
         m = self.replies.get(timeout_ms=int(timeout_s * 1000)) if timeout_s > 0 else self.replies.get_nowait()

@@ -95,7 +95,7 @@ class AfdEngine:
     def __init__(self, cfg: ModelConfig, rt: RuntimeConfig, topo: AfdTopology, rank: int, device,
                  group=None, seed: int = 0, fast_init: bool = False, max_comm_tokens: Optional[int] = None):
         self.cfg, self.rt, self.topo, self.rank, self.group = cfg, rt, topo, rank, group
-        self.device = torch.device(device)
+        self.device, self.seed = torch.device(device), seed
         self.dtype = _torch_dtype(rt.dtype, self.device)
         self.colocated = topo.world == 1
         self.is_attention = self.colocated or topo.is_attention(rank)

@@ -66,7 +66,13 @@ def _coordinator_main(server_args: ServerArgs, addrs: Dict[str, object], world: 
     def emit(items):
         to_tok.put(BatchDetokenizeMsg([DetokenizeMsg(uid=u, token_ids=t, finished=f) for u, t, f in items]))
 
-    coord = AfdCoordinator(cfg, rt, topo, transport, num_pages=min(pages), max_comm_tokens=min(comm), on_tokens=emit)
+    from ..cad.config import CadConfig
+
+    if CadConfig.from_env().enabled:          # FASTAFD_MODE=cad: decode steps with the attention core on the attention ranks only
+        from ..cad.coordinator import CadCoordinator as Coordinator
+    else:
+        Coordinator = AfdCoordinator
+    coord = Coordinator(cfg, rt, topo, transport, num_pages=min(pages), max_comm_tokens=min(comm), on_tokens=emit)
     coord.log_step_times = bool(ENV.STEP_TIMES.value)
     ready_evt.set()
     gc.disable()          # the hot loop allocates little; collector pauses would show up as step jitter

@@ -16,7 +16,8 @@ import traceback
 from collections import deque
 from typing import Dict
 
-from ..protocol import (AgStepPlan, EgStepPlan, RunStepCmd, StopCmd, WorkerFailure, WorkerReady, decode, encode)
+from ..protocol import (AgStepPlan, CadInitCmd, CadStepCmd, EgStepPlan, RunStepCmd, StopCmd, WorkerFailure, WorkerReady,
+                        decode, encode)
 
 
 def worker_main(rank: int, world: int, server_args, addrs: Dict[str, object], master_port: int) -> None:
@@ -49,6 +50,13 @@ def worker_main(rank: int, world: int, server_args, addrs: Dict[str, object], ma
             dist.init_process_group("gloo", rank=rank, world_size=world)
         engine = AfdEngine(cfg, rt, topo, rank, device, seed=server_args.seed, fast_init=cuda,
                            max_comm_tokens=addrs.get("max_comm_tokens"))
+        cad = None
+        from ..cad.config import CadConfig
+
+        if CadConfig.from_env().enabled:        # core-attention disaggregation: decode steps arrive as CAD commands
+            from ..cad.worker import CadWorkerState
+
+            cad = CadWorkerState(engine, rank)
         cmd_q = ZmqPullQueue(addrs["cmd"][rank], bind=True, encode=encode, decode=decode)
         reply_q.put(WorkerReady(rank=rank, role="attention" if engine.attn is not None else "expert",
                                 num_pages=engine.attn.num_pages if engine.attn is not None else 0,
@@ -64,6 +72,13 @@ def worker_main(rank: int, world: int, server_args, addrs: Dict[str, object], ma
                 continue
             if isinstance(cmd, StopCmd):
                 break
+            if isinstance(cmd, CadInitCmd):
+                cad.init(cmd)
+                continue
+            if isinstance(cmd, CadStepCmd):
+                prof.on_step(cmd.step_id)
+                reply_q.put(cad.run(cmd))
+                continue
             plan = cmd.plan
             prof.on_step(plan.step_id)
             if isinstance(plan, EgStepPlan):

@@ -233,3 +233,42 @@ def test_soak_with_arrivals_aborts_and_shared_prefixes(monkeypatch, seed, cache)
     for lane in coord.lanes:
         lane.audit_pages()
         assert not lane.states
+
+
+@pytest.mark.timeout(300)
+@pytest.mark.parametrize("attn,model", [(2, 1), (2, 2)], ids=["2-attention-1-model", "2-attention-2-model"])
+def test_served_cad_deployment_of_separate_processes(monkeypatch, attn, model):
+    """HTTP -> tokenizer -> CAD coordinator -> ZeroMQ -> attention rank processes (KV cache, attention core) and
+    model rank processes (dense layers, a slice of the experts each, sampling) over gloo: the greedy tokens
+    are those of the colocated engine."""
+    import requests
+
+    from fastafd_b200.llm import LLM
+    from fastafd_b200.server.args import parse_args
+    from fastafd_b200.server.launch import local_endpoint
+    from fastafd_b200.server.supervisor import LocalSupervisor
+
+    prompts = [[5, 9, 2, 44, 17], [8, 3, 11], [61, 62, 63, 64, 65, 66, 67], [7]]
+    base = LLM("tiny-qwen3-moe", device="cpu", num_pages=64, max_seq_len=128)
+    want = [o["token_ids"] for o in base.generate(prompts, SamplingParams(max_tokens=5, ignore_eos=True))]
+    base.shutdown()
+    monkeypatch.setenv("FASTAFD_MODE", "cad")
+    args = parse_args(["--mode", "afd-serve", "--model-path", "tiny-qwen3-moe", "--device", "cpu", "--afd-num-mb", "2",
+                       "--afd-attn-dp-size", str(attn), "--afd-mlp-ep-size", str(model), "--num-pages", "64",
+                       "--max-seq-len-override", "128", "--afd-max-running-requests", "8", "--cuda-graph-max-bs", "8"])
+    sup = LocalSupervisor(args)
+    with local_endpoint(args, sup) as url:
+        got = []
+        for p in prompts:
+            r = requests.post(url + "/v1/chat/completions", json={"input_ids": p, "max_tokens": 5, "temperature": 0,
+                                                                  "ignore_eos": True, "return_token_ids": True, "stream": False},
+                              timeout=200).json()
+            got.append(r["choices"][0]["token_ids"])
+        batch = requests.post(url + "/v1/chat/completions/batch", json={"prompts": ["ab", "cde", "f"], "max_tokens": 3, "temperature": 0,
+                                                                       "ignore_eos": True, "return_token_ids": True}, timeout=200).json()
+        hot = requests.post(url + "/v1/chat/completions", json={"input_ids": [1, 2], "max_tokens": 2, "temperature": 0.9,
+                                                                "stream": False}, timeout=60)
+        assert sup.get_failures() == []
+    assert got == want
+    assert [len(c["token_ids"]) for c in batch["choices"]] == [3, 3, 3]
+    assert "greedily" in hot.text            # random sampling is refused with a reason, the server keeps running
