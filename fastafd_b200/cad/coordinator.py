@@ -29,7 +29,7 @@ import numpy as np
 
 from ..coordinator import AfdCoordinator, CoordinatorError, WorkerTransport, _Inflight
 from ..core import SamplingParams
-from ..protocol import AgStepReply, CadInitCmd, CadStepCmd, CadStepReply
+from ..protocol import AgStepReply, CadInitCmd, CadStepCmd, CadStepReply, WorkerReady
 from ..scheduler.buckets import per_mb_real, select_bucket
 from .ranks import CadRanks
 from .tokens import CadRow, host_token, pack_rows
@@ -47,7 +47,7 @@ class CadTransport(WorkerTransport):
 
 
 class CadCoordinator(AfdCoordinator):
-    def __init__(self, cfg, rt, topo, transport: CadTransport, **kw):
+    def __init__(self, cfg, rt, topo, transport: CadTransport, *, cad_init_timeout_s: Optional[float] = None, **kw):
         if rt.spec_block > 1:
             raise ValueError("CAD decode steps are plain decode steps: speculative decoding is off in this mode")
         super().__init__(cfg, rt, topo, transport, **kw)
@@ -55,6 +55,14 @@ class CadCoordinator(AfdCoordinator):
         self._dev_len: Dict[int, int] = {}      # uid -> KV length whose next input token sits in the model rank's slot
         self._cad_steps: Dict[int, dict] = {}   # step id -> {"err": int, "uids": [...]} of CAD steps in flight
         self.aborted_steps: List[int] = []
+        # Every rank acknowledges the init command once its CAD state is built. Nothing waits for that up front
+        # (commands reach a rank in order), but a decode step that gets no answer while ranks still owe the
+        # acknowledgement is reported as what it is: an init that did not finish, with the ranks named.
+        from .config import CadConfig
+
+        self.cad_init_timeout_s = CadConfig.from_env().init_timeout_s if cad_init_timeout_s is None else cad_init_timeout_s
+        self.cad_ready: set = set()
+        self._cad_init_at = time.monotonic()
         table_rows = self.lanes[0].max_running + 1
         transport.send_cad_init(CadInitCmd(buckets=list(self.buckets), t_max=self.buckets[-1], table_rows=table_rows,
                                            num_mb=rt.num_mb, use_graph=rt.use_cuda_graph))
@@ -115,6 +123,10 @@ class CadCoordinator(AfdCoordinator):
 
     # ------------------------------------------------------------------ completion
     def _on_reply(self, msg) -> None:
+        if isinstance(msg, WorkerReady):
+            if msg.role.startswith("cad-"):
+                self.cad_ready.add(msg.rank)
+            return
         if not isinstance(msg, CadStepReply):
             return super()._on_reply(msg)
         rec = next((r for r in self.inflight if r.step_id == msg.step_id), None)
@@ -130,6 +142,18 @@ class CadCoordinator(AfdCoordinator):
         for p, toks in msg.tokens.items():
             lane = peers[int(p)]
             rec.replies[lane] = AgStepReply(step_id=msg.step_id, rank=lane, next_tokens=np.asarray(toks, np.int32))
+
+    def collect(self, block: bool) -> bool:
+        owing = sorted(set(range(self.ranks.world)) - self.cad_ready)
+        if owing and self.inflight and self.inflight[0].step_id in self._cad_steps \
+                and time.monotonic() - self._cad_init_at > self.cad_init_timeout_s:
+            for m in self.transport.poll(0.0):
+                self._on_reply(m)
+            owing = sorted(set(range(self.ranks.world)) - self.cad_ready)
+            if owing:
+                self.failure = f"CAD init: ranks {owing} did not finish within {self.cad_init_timeout_s}s"
+                raise CoordinatorError(self.failure)
+        return super().collect(block)
 
     def _complete_oldest(self) -> None:
         info = self._cad_steps.pop(self.inflight[0].step_id, None)

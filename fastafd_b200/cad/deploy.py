@@ -28,7 +28,7 @@ from .. import ops
 from ..config import ModelConfig, RuntimeConfig
 from ..models.transformer import AttentionStage, ExpertStage
 from ..protocol import (AfdTopology, AgStepPlan, CadInitCmd, CadStepCmd, CadStepReply, EgStepPlan, EgStepReply,
-                        WorkerFailure)
+                        WorkerFailure, WorkerReady)
 from ..reference import ops_ref as ref
 from ..worker.attention_worker import AttentionWorker
 from ..worker.moe_client import LocalMoeClient
@@ -158,6 +158,7 @@ class CadLocalWorkers(CadTransport):
                 self.attn_sides[a] = CadAttentionSide(self.workers[a], win, p)
             self.model_sides[rank] = CadModelRank(cfg, stage, self.experts, wins,
                                                   CadTokenPath(rk.r, cmd.num_mb, cmd.t_max, cmd.table_rows, self.device))
+        self._out += [WorkerReady(rank=r, role="cad-" + rk.role(r)) for r in range(rk.world)]
 
     # ------------------------------------------------------------------ AFD steps (prefill)
     def send_step(self, step_id: int, ag_plans: Dict[int, Tuple[AgStepPlan, List[int]]], eg_plans: Dict[int, EgStepPlan]) -> None:

@@ -74,6 +74,7 @@ def worker_main(rank: int, world: int, server_args, addrs: Dict[str, object], ma
                 break
             if isinstance(cmd, CadInitCmd):
                 cad.init(cmd)
+                reply_q.put(WorkerReady(rank=rank, role="cad-" + cad.role))
                 continue
             if isinstance(cmd, CadStepCmd):
                 prof.on_step(cmd.step_id)

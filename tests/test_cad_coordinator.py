@@ -272,3 +272,32 @@ def test_served_cad_deployment_of_separate_processes(monkeypatch, attn, model):
     assert got == want
     assert [len(c["token_ids"]) for c in batch["choices"]] == [3, 3, 3]
     assert "greedily" in hot.text            # random sampling is refused with a reason, the server keeps running
+
+
+def test_an_init_that_never_finishes_is_reported_with_the_ranks_that_owe_it():
+    from fastafd_b200.cad.coordinator import CadTransport
+    from fastafd_b200.protocol import AgStepReply, EgStepReply, WorkerReady
+
+    class HalfReady(CadTransport):
+        """Answers prefill steps; acknowledges the CAD init on ranks 0 and 2 only; never answers a CAD step."""
+        def __init__(self):
+            self.out = []
+        def send_cad_init(self, cmd):
+            self.out += [WorkerReady(rank=0, role="cad-attn"), WorkerReady(rank=2, role="cad-model")]
+        def send_step(self, step_id, ag_plans, eg_plans):
+            for r, (plan, _) in ag_plans.items():
+                n = sum(len(mb.rows) for mb in plan.mbs)
+                self.out.append(AgStepReply(step_id=step_id, rank=r, next_tokens=np.full(n, 7, np.int32)))
+            self.out += [EgStepReply(step_id=step_id, rank=r) for r in eg_plans]
+        def send_cad_step(self, step_id, attn_cmds, model_cmds):
+            pass
+        def poll(self, timeout_s):
+            out, self.out = self.out, []
+            return out
+
+    topo = AfdTopology(attn_dp=2, mlp_ep=1)
+    coord = CadCoordinator(CFG, _rt(), topo, HalfReady(), num_pages=64, max_comm_tokens=64, cad_init_timeout_s=0.0)
+    coord.add_request(0, [1, 2, 3], SamplingParams(max_tokens=4, ignore_eos=True))
+    with pytest.raises(CoordinatorError, match=r"CAD init: ranks \[1\] did not finish"):
+        coord.run_until_idle()
+    assert coord.cad_ready == {0, 2}
