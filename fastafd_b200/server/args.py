@@ -75,6 +75,7 @@ class ServerArgs:
     afd_prompt_repeat: int = 1
     afd_report_dir: str = ""
     afd_sample_json: str = ""
+    pid_file: str = ""                   # the supervisor records its processes here; `python -m fastafd_b200.server.stop` ends exactly those
     log_level: str = "INFO"
 
     @property
@@ -219,6 +220,7 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--afd-prompt-repeat", type=int, default=1)
     p.add_argument("--afd-report-dir", default="")
     p.add_argument("--afd-sample-json", default="", help="where the runtime replay writes its sample bundle")
+    p.add_argument("--pid-file", default="", help="record the backend's process ids here (see fastafd_b200.server.stop)")
     p.add_argument("--log-level", default="INFO")
     return p
 

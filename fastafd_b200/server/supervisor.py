@@ -197,6 +197,10 @@ class LocalSupervisor:
         p.start()
         self.names[p.pid] = name
         self.procs.append(p)
+        if getattr(self.args, "pid_file", ""):
+            from .stop import record_process
+
+            record_process(self.args.pid_file, p.pid, name)
 
     def get_failures(self) -> List[str]:
         """Names of processes that exited although nobody asked them to."""

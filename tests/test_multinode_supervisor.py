@@ -144,3 +144,54 @@ def test_actor_options_carry_logs_profile_and_cache_scope():
     assert full["runtime_env"]["nsight"]["o"] == "/logs/nsys/fastafd-rank3"
     assert sr.actor_options(slot, env, ray_nsys=True, nsys_output_prefix="/p/run")["runtime_env"]["nsight"]["o"] == "/p/run-rank3"
     assert env == {"FASTAFD_DIRECT": "1", "TVM_FFI_CACHE_DIR": "/driver/cache", "NCCL_DEBUG": "WARN"}    # not modified
+
+
+def test_stop_ends_exactly_the_recorded_processes(tmp_path):
+    """The pid file names processes by pid and start time: the recorded sleeper is ended, an entry whose
+    start time does not match (a pid that was reused) and an entry whose process is gone are skipped."""
+    import subprocess
+    import sys
+
+    from fastafd_b200.server import stop
+
+    path = str(tmp_path / "run" / "server.pids.json")
+    sleeper = subprocess.Popen([sys.executable, "-c", "import time; time.sleep(600)"])
+    bystander = subprocess.Popen([sys.executable, "-c", "import time; time.sleep(600)"])
+    try:
+        stop.record_process(path, sleeper.pid, "worker0")
+        entries = stop.load(path)
+        assert entries[0]["role"] == "worker0" and entries[0]["start_ticks"] == stop.process_start_ticks(sleeper.pid)
+        # a reused pid: same number, another start time
+        entries.append({"pid": bystander.pid, "role": "worker1", "start_ticks": stop.process_start_ticks(bystander.pid) + 1})
+        entries.append({"pid": 2 ** 22 + 12345, "role": "gone", "start_ticks": 1})
+        import json as _json
+        open(path, "w").write(_json.dumps(entries))
+        res = stop.stop_recorded(path, grace_s=5.0)
+        assert res["terminated"] + res["killed"] == [sleeper.pid]
+        assert sorted(res["skipped"]) == sorted([bystander.pid, 2 ** 22 + 12345])
+        assert sleeper.wait(timeout=5) is not None and bystander.poll() is None
+        assert stop.main([path, "--grace", "0.5"]) == 0          # a second run finds nothing left to end
+    finally:
+        for p in (sleeper, bystander):
+            if p.poll() is None:
+                p.kill()
+            p.wait()
+
+
+def test_supervisor_records_its_processes_when_asked(tmp_path, monkeypatch):
+    from fastafd_b200.server import stop
+    from fastafd_b200.server.args import parse_args
+    from fastafd_b200.server.supervisor import LocalSupervisor
+
+    path = str(tmp_path / "pids.json")
+    args = parse_args(["--mode", "serve", "--model-path", "tiny-qwen3-moe", "--device", "cpu", "--pid-file", path])
+    sup = LocalSupervisor(args)
+
+    sup._spawn("worker0", __import__("time").sleep, (60,))
+    try:
+        e = stop.load(path)
+        assert len(e) == 1 and e[0]["role"] == "worker0" and stop.same_process(e[0])
+    finally:
+        for p in sup.procs:
+            p.terminate()
+            p.join(5)
