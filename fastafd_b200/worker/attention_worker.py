@@ -119,10 +119,13 @@ class AttentionWorker:
         self.max_pages = (self.max_seq_len + self.page_size - 1) // self.page_size
         self.max_running = rt.max_running_requests
         self.dummy_row = self.max_running
+        # The recurrent state of the linear-attention layers first (its size is fixed by max_running; for a large
+        # hybrid model it is tens of GB), then the KV pool from what is left: a page is priced as the pool
+        # allocates it, against the memory that is free once everything else is resident.
+        self.gdn = GDNStatePool(cfg, self.max_running + 1, self.device, self.dtype, tp_size) if cfg.num_linear_layers else None
         self.num_pages = num_pages = num_pages or determine_num_pages(
             cfg, rt, self.device, self.model.hkv, 2 if self.cuda else 4)
         self.kv = KVPool(cfg, num_pages, self.page_size, self.model.hkv, self.device, self.dtype)
-        self.gdn = GDNStatePool(cfg, self.max_running + 1, self.device, self.dtype, tp_size) if cfg.num_linear_layers else None
         self.token_pool = torch.zeros(self.max_running + 1, self.max_seq_len + 8, dtype=torch.int32, device=self.device)
         self.page_table_all = torch.zeros(self.max_running + 1, self.max_pages, dtype=torch.int32, device=self.device)
         self.page_table_host = np.zeros((self.max_running + 1, self.max_pages), np.int32)

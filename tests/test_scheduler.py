@@ -312,3 +312,40 @@ def test_randomised_soak_keeps_the_page_ledger_and_request_tables_consistent(mon
     s.check_integrity()
     assert not s.states and len(s.free_rows) == max_running
     assert sum(1 for u in outputs if outputs[u]) > 10
+
+
+def test_kv_pages_are_priced_as_the_pool_allocates_them(monkeypatch):
+    """Hybrid model (Qwen3.5-397B: 60 layers, every fourth with full attention, 2 KV heads of 256): a page costs
+    K and V of the full-attention layers only, the budget is memory_ratio of what is free at that moment minus a
+    reserve, the request table caps it, an explicit page count wins; and the worker builds the recurrent-state
+    pool (fixed size, tens of GB at this scale) before it sizes the KV pool from what is left."""
+    import inspect
+
+    import torch
+
+    from fastafd_b200.config import RuntimeConfig, get_model_config
+    from fastafd_b200.models.transformer import KVPool
+    from fastafd_b200.worker import attention_worker as aw
+
+    cfg = get_model_config("qwen3.5-397b-a17b-fp8")
+    assert cfg.num_full_attn_layers == 15 and cfg.num_linear_layers == 45
+    per_page = KVPool.bytes_per_page(cfg, 16, 2, 2)
+    assert per_page == 2 * 15 * 16 * 2 * 256 * 2
+    GIB = 1 << 30
+    free = {"now": 100 * GIB}
+    monkeypatch.setattr(torch.cuda, "mem_get_info", lambda dev=None: (free["now"], 180 * GIB))
+    dev = torch.device("cuda", 0)
+    rt = RuntimeConfig(page_size=16, max_running_requests=256, max_seq_len=262144, memory_ratio=0.9)
+    n_before = aw.determine_num_pages(cfg, rt, dev, 2, 2)
+    assert n_before == (int(100 * GIB * 0.9) - 2 * GIB) // per_page
+    free["now"] -= 46 * GIB                                   # the recurrent state of 257 request slots is resident
+    n_after = aw.determine_num_pages(cfg, rt, dev, 2, 2)
+    assert n_after == (int(54 * GIB * 0.9) - 2 * GIB) // per_page < n_before
+    short = RuntimeConfig(page_size=16, max_running_requests=8, max_seq_len=1024, memory_ratio=0.9)
+    assert aw.determine_num_pages(cfg, short, dev, 2, 2) == 8 * 64 + 1            # the request table cannot use more
+    assert aw.determine_num_pages(cfg, RuntimeConfig(num_pages=77), dev, 2, 2) == 77
+    src = inspect.getsource(aw.AttentionWorker.__init__)
+    assert src.index("GDNStatePool(") < src.index("determine_num_pages(") < src.index("KVPool(")
+    # the state pool's size at this scale: an fp32 [heads, dv, dk] matrix per linear-attention layer and request slot
+    slot_bytes = cfg.num_linear_layers * cfg.gdn_num_v_heads * cfg.gdn_head_v_dim * cfg.gdn_head_k_dim * 4
+    assert 40 * GIB < 257 * slot_bytes < 50 * GIB
