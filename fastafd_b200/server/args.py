@@ -65,7 +65,7 @@ class ServerArgs:
     model_source: str = "huggingface"    # accepted for compatibility: models are read from local directories only
     moe_backend: str = "auto"            # accepted for compatibility: one expert path (tcgen05 grouped GEMM)
     disable_pynccl: bool = False         # TP collectives without the own NCCL communicator (= FASTAFD_TP_FUSED=1 only)
-    distributed_timeout: float = 0.0     # seconds for host rendezvous / collectives (0: library default)
+    distributed_timeout: float = 0.0     # seconds for the workers' host-side process group: rendezvous and blocking receives (0: library default)
     afd_disable_attention_decode_graph: bool = False
     afd_disable_model_decode_graph: bool = False
     # runtime replay: prompts given on the command line run through the started backend once, the

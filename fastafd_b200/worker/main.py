@@ -20,6 +20,18 @@ from ..protocol import (AgStepPlan, CadInitCmd, CadStepCmd, EgStepPlan, RunStepC
                         decode, encode)
 
 
+def host_group_options(server_args) -> Dict[str, object]:
+    """Keyword arguments of the host-side process group: `--distributed-timeout SECONDS` bounds its rendezvous
+    and every blocking receive on it (0 keeps the library's default of half an hour).
+    Reference: python/minisgl/server/args.py (--distributed-timeout), forwarded to every worker."""
+    import datetime
+
+    t = float(getattr(server_args, "distributed_timeout", 0.0) or 0.0)
+    if t < 0:
+        raise ValueError("--distributed-timeout must not be negative")
+    return {"timeout": datetime.timedelta(seconds=t)} if t > 0 else {}
+
+
 def worker_main(rank: int, world: int, server_args, addrs: Dict[str, object], master_port: int) -> None:
     import torch
     import torch.distributed as dist
@@ -47,7 +59,7 @@ def worker_main(rank: int, world: int, server_args, addrs: Dict[str, object], ma
             # collectives go through the framework's own NCCL communicator / fabric kernels. (A default
             # group bound to a device makes torch split its NCCL communicator inside new_group on
             # non-member ranks only, which blocks when the new group itself is a gloo group.)
-            dist.init_process_group("gloo", rank=rank, world_size=world)
+            dist.init_process_group("gloo", rank=rank, world_size=world, **host_group_options(server_args))
         engine = AfdEngine(cfg, rt, topo, rank, device, seed=server_args.seed, fast_init=cuda,
                            max_comm_tokens=addrs.get("max_comm_tokens"))
         cad = None

@@ -195,3 +195,19 @@ def test_supervisor_records_its_processes_when_asked(tmp_path, monkeypatch):
         for p in sup.procs:
             p.terminate()
             p.join(5)
+
+
+def test_the_distributed_timeout_reaches_the_workers_process_group():
+    import ast
+    import datetime
+    import inspect
+
+    from fastafd_b200.server.args import parse_args
+    from fastafd_b200.worker import main as wm
+
+    base = ["--mode", "afd-serve", "--model-path", "tiny-qwen3-moe", "--device", "cpu"]
+    assert wm.host_group_options(parse_args(base)) == {}
+    assert wm.host_group_options(parse_args(base + ["--distributed-timeout", "90"])) == {"timeout": datetime.timedelta(seconds=90)}
+    tree = ast.parse(inspect.getsource(wm.worker_main))
+    calls = [n for n in ast.walk(tree) if isinstance(n, ast.Call) and getattr(n.func, "attr", "") == "init_process_group"]
+    assert len(calls) == 1 and any(k.arg is None and getattr(k.value.func, "id", "") == "host_group_options" for k in calls[0].keywords)
