@@ -29,6 +29,10 @@ def test_programs_and_flag_balance():
 
 
 def test_config_is_strict(monkeypatch):
+    for k in list(__import__("os").environ):
+        if k.startswith(("FASTAFD_CAD_", "MINISGL_AFD_CAD_")) or k in ("FASTAFD_MODE", "MINISGL_AFD_MODE"):
+            monkeypatch.delenv(k)
+    assert not CadConfig.from_env().enabled and CadConfig.from_env().env() == {}
     monkeypatch.setenv("FASTAFD_MODE", "cad")
     monkeypatch.setenv("FASTAFD_CAD_HANG_TIMEOUT_NS", "1000")
     c = CadConfig.from_env()
@@ -40,6 +44,23 @@ def test_config_is_strict(monkeypatch):
     monkeypatch.setenv("FASTAFD_MODE", "banana")
     with pytest.raises(CadConfigError):
         CadConfig.from_env()
+
+
+def test_config_takes_the_reference_names_and_spellings():
+    """The environment of a reference CAD benchmark configuration parses as it is; a CAD key without CAD mode, an
+    expert path that does not exist here and a malformed number are refused with the key named."""
+    ref_env = {"MINISGL_AFD_MODE": "cad", "MINISGL_AFD_CAD_HANG_TIMEOUT_NS": "300000000000", "MINISGL_AFD_CAD_HOP": "window",
+               "MINISGL_AFD_CAD_INIT_TIMEOUT_S": "900", "MINISGL_AFD_CAD_MOE": "megamoe_dual", "MINISGL_AFD_CAD_O_DTYPE": "bf16"}
+    c = CadConfig.from_env(ref_env)
+    assert c == CadConfig(mode="cad", o_dtype="bfloat16", hop="kernel", moe="dual", hang_timeout_ns=300_000_000_000, init_timeout_s=900.0)
+    assert CadConfig.from_env(c.env()) == c                       # what a child process is given parses back to the same
+    with pytest.raises(CadConfigError, match="without MODE=cad"):
+        CadConfig.from_env({"MINISGL_AFD_CAD_HOP": "window"})
+    with pytest.raises(CadConfigError, match="DeepEP"):
+        CadConfig.from_env(dict(ref_env, MINISGL_AFD_CAD_MOE="deepep"))
+    with pytest.raises(CadConfigError, match="CAD_HANG_TIMEOUT_NS"):
+        CadConfig.from_env(dict(ref_env, MINISGL_AFD_CAD_HANG_TIMEOUT_NS="soon"))
+    assert not CadConfig.from_env({"MINISGL_AFD_MODE": ""}).enabled
 
 
 def _runtime(r=2, timeout=2.0):
