@@ -134,6 +134,7 @@ class CadCoordinator(AfdCoordinator):
         if rec is None or info is None:
             return
         info["err"] = info["err"] or int(msg.err)
+        self._note_latency(msg.rank, rec)
         if self.ranks.role(msg.rank) == "attn":
             rec.waiting_ag.discard(msg.rank)
             return

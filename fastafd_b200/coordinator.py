@@ -100,6 +100,8 @@ class AfdCoordinator:
         self.stopped = False
         self.step_times: List[Tuple[int, str, int, float]] = []
         self.log_step_times = False
+        self.reply_latency: Dict[int, List[float]] = {}      # rank -> [replies, sum of ms, max ms] from launch to reply
+        self.spec_rows = self.spec_tokens = self.spec_steps = 0
         from .env import ENV
         self.log_steps = bool(ENV.LOG_STEPS.value)        # one line per launched step (plan summary)
         self._log_file = None
@@ -207,6 +209,7 @@ class AfdCoordinator:
         rec = next((r for r in self.inflight if r.step_id == msg.step_id), None)
         if rec is None:
             return
+        self._note_latency(msg.rank, rec)
         if msg.status:
             self.failure = f"rank {msg.rank} reported device status {msg.status} in step {msg.step_id}"
         if isinstance(msg, AgStepReply):
@@ -215,6 +218,27 @@ class AfdCoordinator:
         elif isinstance(msg, EgStepReply):
             rec.waiting_eg.discard(msg.rank)
 
+    def _note_latency(self, rank: int, rec: _Inflight) -> None:
+        ms = (time.perf_counter() - rec.t_launch) * 1e3
+        st = self.reply_latency.setdefault(rank, [0, 0.0, 0.0])
+        st[0] += 1
+        st[1] += ms
+        st[2] = max(st[2], ms)
+
+    def latency_summary(self) -> Dict[int, Dict[str, float]]:
+        """Per rank: replies seen, mean and worst time from a step's launch to that rank's reply (ms). A rank
+        whose mean stands out is the one the others wait for.
+        Reference: python/minisgl/afd_coordinator.py:484-528 (worker reply-latency logs)."""
+        return {r: {"replies": n, "mean_ms": round(tot / n, 3), "max_ms": round(mx, 3)}
+                for r, (n, tot, mx) in sorted(self.reply_latency.items()) if n}
+
+    def spec_stats(self) -> Dict[str, float]:
+        """Speculative decoding so far: verify steps, request rows verified, tokens emitted, and their ratio
+        (mean accepted length, between 1 and the block size).
+        Reference: python/minisgl/afd_attention_worker.py:1432 (acceptance statistics)."""
+        mean = self.spec_tokens / self.spec_rows if self.spec_rows else 0.0
+        return {"verify_steps": self.spec_steps, "rows": self.spec_rows, "tokens": self.spec_tokens, "mean_accepted": round(mean, 4)}
+
     def _complete_oldest(self) -> None:
         rec = self.inflight.popleft()
         items: List[Tuple[int, List[int], bool]] = []
@@ -222,6 +246,10 @@ class AfdCoordinator:
             src = 0 if self.topo.colocated else self.topo.attn_tp_group(lane)[0]
             reply = rec.replies[src]
             items += sched.complete(rec.step_id, reply.next_tokens, reply.accepted)
+        if rec.phase == "verify":
+            self.spec_steps += 1
+            self.spec_rows += sum(1 for _u, toks, _f in items if toks)
+            self.spec_tokens += sum(len(toks) for _u, toks, _f in items)
         ms = (time.perf_counter() - rec.t_launch) * 1e3
         self.step_times.append((rec.step_id, rec.phase, rec.bucket, ms))
         if self.log_step_times:
@@ -280,6 +308,10 @@ class AfdCoordinator:
     def shutdown(self) -> None:
         if not self.stopped:
             self.stopped = True
+            if self.log_step_times or self.log_steps:
+                self._step_log(f"[afd-summary] reply latency per rank (ms): {self.latency_summary()}")
+                if self.spec_steps:
+                    self._step_log(f"[afd-summary] speculative decoding: {self.spec_stats()}")
             self.transport.stop()
 
 

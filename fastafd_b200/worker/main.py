@@ -107,6 +107,10 @@ def worker_main(rank: int, world: int, server_args, addrs: Dict[str, object], ma
                     reply_q.put(engine.finish(pending.popleft()))
         prof.close()
         engine.synchronize()
+        if cuda:        # what this rank needed at its worst: the figure to size memory_ratio and the page count against
+            free, total = torch.cuda.mem_get_info(device)
+            print(f"[worker {rank}] peak device memory: {torch.cuda.max_memory_allocated(device) / 2**30:.2f} GiB allocated by torch, "
+                  f"{(total - free) / 2**30:.2f} of {total / 2**30:.2f} GiB in use at exit", flush=True)
         engine.close()
         if world > 1:
             dist.destroy_process_group()

@@ -235,3 +235,19 @@ def test_coordinator_soak_over_three_lanes(monkeypatch, seed, cache):
         lane.audit_pages()
         assert not lane.states
     coord.shutdown()
+
+
+def test_reply_latency_is_kept_per_rank_and_logged_at_shutdown(caplog):
+    topo = AfdTopology(attn_dp=2, mlp_ep=2)
+    coord = AfdCoordinator(PRESETS["tiny-qwen3-moe"], _rt(), topo, FakeWorkers(), num_pages=64, max_comm_tokens=64)
+    coord.log_step_times = True
+    coord.add_request(0, [1, 2, 3], SamplingParams(max_tokens=3, ignore_eos=True))
+    coord.run_until_idle()
+    summary = coord.latency_summary()
+    assert sorted(summary) == [0, 1, 2, 3]                      # both attention ranks and both expert ranks
+    assert all(v["replies"] == len(coord.step_times) and 0 <= v["mean_ms"] <= v["max_ms"] for v in summary.values())
+    assert coord.spec_stats() == {"verify_steps": 0, "rows": 0, "tokens": 0, "mean_accepted": 0.0}
+    import logging
+    with caplog.at_level(logging.INFO):
+        coord.shutdown()
+    assert any("reply latency per rank" in r.getMessage() for r in caplog.records)

@@ -112,3 +112,7 @@ def test_verify_steps_planned_ahead_stay_lossless():
         seen_two_in_flight |= len(coord.inflight) >= 1 and any(r.phase == "verify" for r in coord.inflight)
     assert [got[i] for i in range(len(prompts))] == plain
     assert seen_two_in_flight
+    # acceptance statistics: every token but each request's first (sampled by its prefill) came out of a verify step
+    st = coord.spec_stats()
+    assert st["verify_steps"] > 0 and st["tokens"] == sum(len(t) - 1 for t in plain)
+    assert 1.0 <= st["mean_accepted"] <= 4.0 and st["rows"] <= st["tokens"]
