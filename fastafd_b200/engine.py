@@ -268,6 +268,19 @@ class AfdEngine:
             code = code or self.expert.finish()
         return code
 
+    def describe_waits(self) -> Dict[str, object]:
+        """After a step that ended with a device status: where the flag protocols of this rank stand (which
+        peers' flags are behind). Never raises; what cannot be read is left out."""
+        out: Dict[str, object] = {}
+        for name, ep in (("dispatch_client", getattr(getattr(self.attn, "client", None), "ep", None)),
+                         ("expert_server", getattr(self._server, "ep", None))):
+            try:
+                if ep is not None and hasattr(ep, "flag_report"):
+                    out[name] = ep.flag_report()
+            except Exception as e:       # triage output must not mask the failure it describes
+                out[name] = f"unreadable: {e!r}"
+        return out
+
     def close(self) -> None:
         if self.fabric is None:
             return

@@ -16,7 +16,7 @@ from __future__ import annotations
 import ctypes as C
 import os
 from dataclasses import dataclass
-from typing import List, Optional
+from typing import Dict, List, Optional
 
 import torch
 
@@ -118,6 +118,17 @@ def eg_layout(cfg: MoeCommConfig) -> Layout:
     return lay
 
 
+def flag_report(flags: torch.Tensor, epoch_word: torch.Tensor, peer_ranks: List[int]) -> Dict[str, object]:
+    """Where a lane's flag protocol stands, for the triage of a wait that ran out: the epoch this rank publishes
+    or expects next, the last epoch each peer has written into this rank's flag words, and the peers that are
+    behind the others (the ones a wait was waiting for). Reads device memory: call it after the failure, not
+    on the hot path. Reference: python/minisgl/afd_worker_base.py:371-408 (barrier head dump)."""
+    vals = [int(v) for v in flags.reshape(-1).tolist()]
+    top = max(vals) if vals else 0
+    return {"next_epoch": int(epoch_word.reshape(-1)[0]), "flags": {int(r): v for r, v in zip(peer_ranks, vals)},
+            "behind": [int(r) for r, v in zip(peer_ranks, vals) if v < top]}
+
+
 class _LaneWords:
     """Small device words a lane's kernels keep between launches."""
 
@@ -157,6 +168,10 @@ class AgMoeEndpoint:
         self._direct_desc = [self._make_direct_desc(l) for l in range(cfg.num_lanes)] if cfg.direct_tokens > 0 else None
         self.route_tokens_per_cta = int(os.environ.get("FASTAFD_ROUTE_TPC", "0"))
         self.route_cluster = int(os.environ.get("FASTAFD_ROUTE_CLUSTER", "0"))
+
+    def flag_report(self) -> Dict[str, object]:
+        """Per lane: the combine flags the expert ranks write here (see `flag_report`)."""
+        return {f"lane{l}": flag_report(self.m2n_flag[l], self.lanes[l].epoch, self.eg_ranks) for l in range(self.cfg.num_lanes)}
 
     def _make_direct_desc(self, lane: int) -> DirectDesc:
         cfg, d = self.cfg, DirectDesc()
@@ -329,6 +344,10 @@ class EgMoeEndpoint:
                                              C.c_ulonglong(self.timeout_ns), ptr(self.status), cur_stream()), "wait_flags")
         fused = cfg.num_ag * T * cfg.topk <= 8192 and cfg.block_tok <= 128      # one launch, else two
         check(lib().afd_eg_group_gather(C.byref(d), cur_stream()), "eg_group_gather_fused" if fused else "eg_group_gather")
+
+    def flag_report(self) -> Dict[str, object]:
+        """Per lane: the dispatch flags the attention ranks write here (see `flag_report`)."""
+        return {f"lane{l}": flag_report(self.n2m_flag[l], self.lanes[l].epoch, self.ag_ranks) for l in range(self.cfg.num_lanes)}
 
     def run_layer(self, lane: int, T: int, w13: torch.Tensor, w2: torch.Tensor,
                   w13_scale: Optional[torch.Tensor] = None, w2_scale: Optional[torch.Tensor] = None,

@@ -77,10 +77,20 @@ def worker_main(rank: int, world: int, server_args, addrs: Dict[str, object], ma
 
         prof = StepProfiler()
         pending = deque()
+        send_reply, reported = reply_q.put, []
+
+        def put_reply(reply) -> None:
+            """Replies pass through here: the first one that carries a device status also prints where this rank's
+            flag protocols stand (which peers are behind), once."""
+            if getattr(reply, "status", 0) and not reported:
+                reported.append(reply.step_id)
+                print(f"[worker {rank}] step {reply.step_id} ended with device status {reply.status}; flags: "
+                      f"{engine.describe_waits()}", flush=True)
+            send_reply(reply)
         while True:
             cmd = cmd_q.get_nowait() if pending else cmd_q.get()
             if cmd is None:                      # nothing new: finish the oldest queued decode step
-                reply_q.put(engine.finish(pending.popleft()))
+                put_reply(engine.finish(pending.popleft()))
                 continue
             if isinstance(cmd, StopCmd):
                 break
@@ -95,16 +105,16 @@ def worker_main(rank: int, world: int, server_args, addrs: Dict[str, object], ma
             plan = cmd.plan
             prof.on_step(plan.step_id)
             if isinstance(plan, EgStepPlan):
-                reply_q.put(engine.step(plan))
+                put_reply(engine.step(plan))
             elif plan.phase == "prefill":
                 while pending:
-                    reply_q.put(engine.finish(pending.popleft()))
-                reply_q.put(engine.step(plan, cmd.mb_tokens))
+                    put_reply(engine.finish(pending.popleft()))
+                put_reply(engine.step(plan, cmd.mb_tokens))
             else:
                 engine.launch(plan)
                 pending.append(plan)
                 while len(pending) > 1:
-                    reply_q.put(engine.finish(pending.popleft()))
+                    put_reply(engine.finish(pending.popleft()))
         prof.close()
         engine.synchronize()
         if cuda:        # what this rank needed at its worst: the figure to size memory_ratio and the page count against

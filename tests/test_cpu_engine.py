@@ -102,3 +102,23 @@ def test_reference_environment_names_act_under_their_new_names():
     assert env["FASTAFD_L2_PREFETCH_MB"] == "8"                # the new name wins when both are set
     assert "FASTAFD_LANE_STREAMS" not in env                   # an empty value is not a setting
     assert set(REFERENCE_ALIASES.values()) <= set(HOT_PATH_KNOBS)
+
+
+def test_flag_report_names_the_peers_that_are_behind():
+    """Triage of a wait that ran out: the peers whose last written epoch is behind the others are the ones the wait
+    was waiting for. (Plain tensors stand in for the flag words of the peer-mapped heap.)"""
+    import torch
+
+    from fastafd_b200.moe.afd_moe import flag_report
+
+    rep = flag_report(torch.tensor([97, 96, 97, 97], dtype=torch.int32), torch.tensor([98], dtype=torch.int32), [4, 5, 6, 7])
+    assert rep == {"next_epoch": 98, "flags": {4: 97, 5: 96, 6: 97, 7: 97}, "behind": [5]}
+    assert flag_report(torch.tensor([3, 3], dtype=torch.int32), torch.tensor([4], dtype=torch.int32), [0, 1])["behind"] == []
+    # an engine without fabric endpoints (CPU) has nothing to report and says so without raising
+    from fastafd_b200.config import PRESETS, RuntimeConfig
+    from fastafd_b200.engine import AfdEngine
+    from fastafd_b200.protocol import AfdTopology
+
+    rt = RuntimeConfig(num_mb=1, page_size=16, num_pages=16, max_running_requests=2, max_seq_len=64, cuda_graph_max_bs=2,
+                       device="cpu", dtype="float32", use_cuda_graph=False)
+    assert AfdEngine(PRESETS["tiny-qwen3-moe"], rt, AfdTopology(colocated=True), 0, "cpu").describe_waits() == {}
