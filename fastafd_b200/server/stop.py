@@ -58,7 +58,9 @@ def stop_recorded(path: str, grace_s: float = 5.0) -> Dict[str, List[int]]:
     """Returns {"terminated": [...], "killed": [...], "skipped": [...]} (pids)."""
     out: Dict[str, List[int]] = {"terminated": [], "killed": [], "skipped": []}
     live = []
-    for e in load(path):
+    entries = load(path)
+    entries.sort(key=lambda e: e.get("role") == "server")      # the front end after the processes it started
+    for e in entries:
         pid = int(e["pid"])
         if pid == os.getpid() or not same_process(e):
             out["skipped"].append(pid)

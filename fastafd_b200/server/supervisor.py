@@ -24,6 +24,8 @@ python/minisgl/afd_worker_launcher.py:26-346 (start-up sequence, timeouts, early
 """
 from __future__ import annotations
 
+import os
+
 import multiprocessing as mp
 import time
 from dataclasses import dataclass
@@ -198,8 +200,10 @@ class LocalSupervisor:
         self.names[p.pid] = name
         self.procs.append(p)
         if getattr(self.args, "pid_file", ""):
-            from .stop import record_process
+            from .stop import load, record_process
 
+            if not any(e.get("pid") == os.getpid() for e in load(self.args.pid_file)):
+                record_process(self.args.pid_file, os.getpid(), "server")       # the front end itself, ended last
             record_process(self.args.pid_file, p.pid, name)
 
     def get_failures(self) -> List[str]:

@@ -190,7 +190,8 @@ def test_supervisor_records_its_processes_when_asked(tmp_path, monkeypatch):
     sup._spawn("worker0", __import__("time").sleep, (60,))
     try:
         e = stop.load(path)
-        assert len(e) == 1 and e[0]["role"] == "worker0" and stop.same_process(e[0])
+        assert [x["role"] for x in e] == ["server", "worker0"] and all(stop.same_process(x) for x in e)
+        assert e[0]["pid"] == __import__("os").getpid()            # the front end is on record too (and `stop` never signals itself)
     finally:
         for p in sup.procs:
             p.terminate()
