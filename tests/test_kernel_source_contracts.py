@@ -220,3 +220,43 @@ def test_every_registered_hot_path_knob_is_read_somewhere():
     pkg = CSRC.parent
     text = "".join(p.read_text() for p in list(pkg.rglob("*.py")) + list(CSRC.rglob("*.cu*")) if p.name != "env.py")
     assert [k for k in HOT_PATH_KNOBS if k not in text] == []
+
+
+def test_every_region_of_every_peer_heap_layout_is_aligned_and_disjoint():
+    """Peer heaps are carved by layouts that both sides compute on their own: regions must start on a 256-byte
+    boundary (bulk copies and tensor maps want 16, vector stores 16, the flag words their own cache line), must
+    not overlap, and the per-source / per-lane blocks inside a row region must start on 16 bytes too. Checked for
+    the model shapes that are served and for odd token counts."""
+    import itertools
+
+    from fastafd_b200.cad.gpu import attention_window_layout, model_window_layout
+    from fastafd_b200.config import get_model_config
+    from fastafd_b200.moe.afd_moe import MoeCommConfig, ag_layout, eg_layout
+    from fastafd_b200.parallel.tp_fused import tp_layout
+
+    def check(lay, what):
+        spans = sorted(lay.entries.values())
+        for (off, n), nxt in zip(spans, spans[1:] + [(lay.size, 0)]):
+            assert off % 256 == 0, (what, off)
+            assert off + n <= nxt[0], (what, "overlap", off, n, nxt)
+        assert lay.size % 256 == 0
+
+    for name, num_ag, num_eg, lanes, tokens, fp8 in itertools.product(
+            ("qwen3-30b-a3b", "qwen3-235b-a22b-fp8", "minimax-m2.5-fp8", "qwen3.5-397b-a17b-fp8", "glm-4.5-air"),
+            (1, 4, 6), (1, 2, 4), (1, 2, 3), (1, 44, 129, 2048), (False, True)):
+        c = get_model_config(name)
+        m = MoeCommConfig(num_ag=num_ag, num_eg=num_eg, num_lanes=lanes, max_tokens=tokens, hidden=c.hidden_size,
+                          topk=c.num_experts_per_tok, num_experts=c.num_experts, intermediate=c.moe_intermediate_size,
+                          fp8=fp8, block_tok=32, direct_tokens=min(tokens, 64))
+        check(ag_layout(m), (name, "ag"))
+        check(eg_layout(m), (name, "eg"))
+        assert (tokens * m.row_bytes) % 16 == 0 and (tokens * (c.hidden_size // 128) * 4) % 4 == 0      # per-source blocks
+        assert (m.direct_cap * m.row_bytes) % 16 == 0                                                   # per-expert stripes
+    for name, tp, lanes, tokens in itertools.product(("qwen3-30b-a3b", "qwen3-235b-a22b-fp8"), (2, 4, 8), (1, 2), (1, 11, 64)):
+        c = get_model_config(name)
+        check(tp_layout(tp, lanes, tokens, c.hidden_size), (name, "tp"))
+        assert (tokens * c.hidden_size * 2) % 16 == 0
+    for name, attn, lanes, tokens in itertools.product(("minimax-m2.5-fp8", "qwen3-30b-a3b"), (1, 2, 7), (1, 2), (1, 77, 256)):
+        c = get_model_config(name)
+        check(attention_window_layout(c, lanes, tokens), (name, "cad-attn"))
+        check(model_window_layout(c, attn, lanes, tokens), (name, "cad-model"))
