@@ -133,6 +133,14 @@ class ModelConfig:
                 inner.setdefault("quantization_config", cfg["quantization_config"])
             cfg = inner
         arch = (cfg.get("architectures") or ["LlamaForCausalLM"])[0]
+
+        def experts() -> int:
+            """Routed experts: the key differs by family and by the library version that wrote the file."""
+            for k in ("num_experts", "num_local_experts", "n_routed_experts"):
+                if cfg.get(k):
+                    return int(cfg[k])
+            raise KeyError(f"{arch}: config.json names no expert count (num_experts / num_local_experts / n_routed_experts)")
+
         hidden = cfg["hidden_size"]
         heads = cfg["num_attention_heads"]
         head_dim = cfg.get("head_dim") or hidden // heads
@@ -166,17 +174,17 @@ class ModelConfig:
         if arch in ("Qwen2ForCausalLM",):
             kw.update(attention_bias=True)
         if arch == "Qwen3MoeForCausalLM":
-            kw.update(qk_norm="head", num_experts=cfg["num_experts"], num_experts_per_tok=cfg["num_experts_per_tok"],
+            kw.update(qk_norm="head", num_experts=experts(), num_experts_per_tok=cfg["num_experts_per_tok"],
                       moe_intermediate_size=cfg["moe_intermediate_size"],
                       norm_topk_prob=bool(cfg.get("norm_topk_prob", True)))
         elif arch == "MiniMaxM2ForCausalLM":
             kw.update(qk_norm="cross_head" if cfg.get("use_qk_norm", True) else "none",
-                      num_experts=cfg["num_local_experts"], num_experts_per_tok=cfg["num_experts_per_tok"],
+                      num_experts=experts(), num_experts_per_tok=cfg["num_experts_per_tok"],
                       moe_intermediate_size=cfg["intermediate_size"], scoring="sigmoid", router_bias=True,
                       router_fp32=True, norm_topk_prob=True)
         elif arch == "Glm4MoeForCausalLM":
             kw.update(qk_norm="head" if cfg.get("use_qk_norm", False) else "none",
-                      num_experts=cfg["n_routed_experts"], num_experts_per_tok=cfg["num_experts_per_tok"],
+                      num_experts=experts(), num_experts_per_tok=cfg["num_experts_per_tok"],
                       moe_intermediate_size=cfg["moe_intermediate_size"], scoring="sigmoid", router_bias=True,
                       norm_topk_prob=bool(cfg.get("norm_topk_prob", True)),
                       routed_scaling_factor=float(cfg.get("routed_scaling_factor", 1.0)),
@@ -190,7 +198,7 @@ class ModelConfig:
             if lt is None:
                 interval = cfg.get("full_attention_interval", 4)
                 lt = ["full_attention" if (i + 1) % interval == 0 else "linear_attention" for i in range(n)]
-            kw.update(qk_norm="head", num_experts=cfg["num_experts"], num_experts_per_tok=cfg["num_experts_per_tok"],
+            kw.update(qk_norm="head", num_experts=experts(), num_experts_per_tok=cfg["num_experts_per_tok"],
                       moe_intermediate_size=cfg["moe_intermediate_size"],
                       norm_topk_prob=bool(cfg.get("norm_topk_prob", True)), num_shared_experts=1,
                       shared_expert_intermediate_size=cfg.get("shared_expert_intermediate_size", 0),

@@ -77,6 +77,42 @@ def _dequant_if_fp8(w: torch.Tensor, scale: Optional[torch.Tensor]) -> torch.Ten
     return w
 
 
+def split_q_gate_rows(t: torch.Tensor, heads: int, head_dim: int) -> torch.Tensor:
+    """Gated attention (Qwen3.5): the checkpoint's q_proj has 2 x head_dim rows per head, the head's query rows
+    and then its gate rows. Returns the rows as [query rows of all heads | gate rows of all heads].
+    Reference: python/minisgl/models/qwen35_moe.py:299-303 (split_query_gate on the projection's output)."""
+    per_head = t.reshape(heads, 2, head_dim, *t.shape[1:])
+    return torch.cat([per_head[:, 0].reshape(heads * head_dim, *t.shape[1:]),
+                      per_head[:, 1].reshape(heads * head_dim, *t.shape[1:])], 0).contiguous()
+
+
+def split_qwen3_next_projections(cfg, raw: Dict[str, torch.Tensor]) -> None:
+    """Qwen3-Next stores the gated-DeltaNet input projections as two matrices whose rows are grouped by key head:
+    ``in_proj_qkvz`` = per key head [q (dk) | k (dk) | v of its value heads | z of its value heads] and
+    ``in_proj_ba`` = per key head [b of its value heads | a of its value heads]. Qwen3.5 stores the four
+    projections on their own (q of all heads, k of all heads, v; z; b; a). Rewrites the former into the latter,
+    in place."""
+    hk, hv, dk, dv = cfg.gdn_num_k_heads, cfg.gdn_num_v_heads, cfg.gdn_head_k_dim, cfg.gdn_head_v_dim
+    per = hv // hk
+    for key in [k for k in raw if k.endswith("linear_attn.in_proj_qkvz.weight")]:
+        base = key[:-len("in_proj_qkvz.weight")]
+        w = raw.pop(key)
+        g = w.reshape(hk, 2 * dk + 2 * per * dv, w.shape[1])
+        q, k_, v, z = g[:, :dk], g[:, dk:2 * dk], g[:, 2 * dk:2 * dk + per * dv], g[:, 2 * dk + per * dv:]
+        raw[base + "in_proj_qkv.weight"] = torch.cat([q.reshape(hk * dk, -1), k_.reshape(hk * dk, -1), v.reshape(hv * dv, -1)], 0).contiguous()
+        raw[base + "in_proj_z.weight"] = z.reshape(hv * dv, -1).contiguous()
+        ba = raw.pop(base + "in_proj_ba.weight").reshape(hk, 2 * per, w.shape[1])
+        raw[base + "in_proj_b.weight"] = ba[:, :per].reshape(hv, -1).contiguous()
+        raw[base + "in_proj_a.weight"] = ba[:, per:].reshape(hv, -1).contiguous()
+
+
+def merge_q_gate_rows(t: torch.Tensor, heads: int, head_dim: int) -> torch.Tensor:
+    """Inverse of `split_q_gate_rows`: [queries | gates] back to the checkpoint's per-head [q | gate] rows."""
+    q, g = t[:heads * head_dim], t[heads * head_dim:]
+    both = torch.stack([q.reshape(heads, head_dim, *t.shape[1:]), g.reshape(heads, head_dim, *t.shape[1:])], 1)
+    return both.reshape(2 * heads * head_dim, *t.shape[1:]).contiguous()
+
+
 def load_attention_stage(stage: AttentionStage, path: str) -> None:
     """Fill an AttentionStage from a checkpoint directory (TP-sharded, merged, role-filtered)."""
     cfg = stage.cfg
@@ -93,16 +129,30 @@ def load_attention_stage(stage: AttentionStage, path: str) -> None:
             scales[k[:-len("_scale_inv")]] = t
         else:
             raw[k] = t
+    for k in list(raw):
+        # a depthwise Conv1d stores its taps as [channels, 1, kernel]; the stage keeps [channels, kernel]
+        if k.endswith("linear_attn.conv1d.weight") and raw[k].dim() == 3 and raw[k].shape[1] == 1:
+            raw[k] = raw[k].squeeze(1)
     was_fp8 = set()
     for k in list(raw):
         if k in scales or raw[k].dtype == torch.float8_e4m3fn:
             raw[k] = _dequant_if_fp8(raw[k], scales.get(k))       # exact in fp32: code x block scale
             was_fp8.add(k)
+    if cfg.num_linear_layers:                   # after the dequantisation: the values are exact in fp32, rows can move
+        for k in [k for k in raw if k.endswith(("in_proj_qkvz.weight", "in_proj_ba.weight")) and k in was_fp8]:
+            base = k.rsplit("in_proj_", 1)[0]
+            was_fp8.update(base + n for n in (("in_proj_qkv.weight", "in_proj_z.weight") if k.endswith("qkvz.weight")
+                                              else ("in_proj_b.weight", "in_proj_a.weight")))
+        split_qwen3_next_projections(cfg, raw)
     full: Dict[str, torch.Tensor] = {}
     for i in range(cfg.num_layers):
         p = f"model.layers.{i}."
         a = p + "self_attn."
         if a + "q_proj.weight" in raw:
+            if cfg.attn_output_gate:          # checkpoint rows: per head [q | gate]; the stage keeps [q of all heads | gates]
+                for suf in (".weight", ".bias"):
+                    if a + "q_proj" + suf in raw:
+                        raw[a + "q_proj" + suf] = split_q_gate_rows(raw[a + "q_proj" + suf], cfg.num_q_heads, cfg.head_dim)
             if a + "q_proj.weight" in was_fp8:
                 was_fp8.add(a + "qkv_proj.weight")
             full[a + "qkv_proj.weight"] = torch.cat([raw.pop(a + n + ".weight") for n in ("q_proj", "k_proj", "v_proj")], 0)
@@ -200,6 +250,8 @@ def save_checkpoint(cfg: ModelConfig, attn: AttentionStage, experts: List[Expert
             base, suf = name.rsplit("qkv_proj", 1)
             out[base + "q_proj" + suf], out[base + "k_proj" + suf], out[base + "v_proj" + suf] = \
                 t[:qn].contiguous(), t[qn:qn + kn].contiguous(), t[qn + kn:].contiguous()
+            if cfg.attn_output_gate:          # the checkpoint format keeps each head's query and gate rows together
+                out[base + "q_proj" + suf] = merge_q_gate_rows(out[base + "q_proj" + suf], cfg.num_q_heads, D)
         elif name.endswith("gate_up_proj.weight"):
             half = t.shape[0] // 2
             base = name[:-len("gate_up_proj.weight")]

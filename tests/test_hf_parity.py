@@ -1,0 +1,91 @@
+"""Every model family against its implementation in the `transformers` library (CPU, fp32, tiny random models).
+
+A model of the family is built with `transformers`, saved the way the library saves a checkpoint (safetensors,
+the family's own key names and row layouts, the `config.json` that version of the library writes), served by
+this package's engine from that directory, and the greedy continuations are compared with the library's own
+forward pass token by token. This pins, per family, the config parsing, the checkpoint key mapping and row
+layouts (merged projections, per-head query|gate rows, grouped gated-DeltaNet projections, depthwise conv
+taps), and the model math (norm variants, partial rotary embedding, q/k norms per head and across heads,
+softmax / sigmoid / grouped routing, shared experts and their gates, gated attention, gated DeltaNet).
+"""
+import pytest
+import torch
+
+transformers = pytest.importorskip("transformers")
+
+from fastafd_b200.core import SamplingParams  # noqa: E402
+from fastafd_b200.llm import LLM  # noqa: E402
+
+COMMON = dict(vocab_size=256, hidden_size=64, num_hidden_layers=3, num_attention_heads=4, num_key_value_heads=2,
+              max_position_embeddings=256, tie_word_embeddings=False)
+GDN = dict(head_dim=16, moe_intermediate_size=32, num_experts=8, num_experts_per_tok=2, shared_expert_intermediate_size=32,
+           linear_num_key_heads=2, linear_num_value_heads=4, linear_key_head_dim=16, linear_value_head_dim=16,
+           linear_conv_kernel_dim=4, layer_types=["linear_attention", "linear_attention", "full_attention"])
+
+FAMILIES = {
+    "llama": ("LlamaForCausalLM", "LlamaConfig", dict(intermediate_size=128, rope_theta=10000.0)),
+    "llama-tied-embeddings": ("LlamaForCausalLM", "LlamaConfig", dict(intermediate_size=128, tie_word_embeddings=True)),
+    "qwen2": ("Qwen2ForCausalLM", "Qwen2Config", dict(intermediate_size=128, rope_theta=1e6)),
+    "mistral": ("MistralForCausalLM", "MistralConfig", dict(intermediate_size=128, head_dim=16, sliding_window=None)),
+    "qwen3": ("Qwen3ForCausalLM", "Qwen3Config", dict(intermediate_size=128, head_dim=16)),
+    "qwen3-moe": ("Qwen3MoeForCausalLM", "Qwen3MoeConfig",
+                  dict(intermediate_size=128, head_dim=16, moe_intermediate_size=32, num_experts=8, num_experts_per_tok=2,
+                       norm_topk_prob=True, decoder_sparse_step=1, mlp_only_layers=[])),
+    "glm4-moe": ("Glm4MoeForCausalLM", "Glm4MoeConfig",
+                 dict(intermediate_size=128, head_dim=16, moe_intermediate_size=32, n_routed_experts=8, num_experts_per_tok=2,
+                      n_shared_experts=1, n_group=2, topk_group=1, first_k_dense_replace=1, norm_topk_prob=True,
+                      routed_scaling_factor=1.5, use_qk_norm=True, partial_rotary_factor=0.5)),
+    "minimax-m2": ("MiniMaxM2ForCausalLM", "MiniMaxM2Config",
+                   dict(intermediate_size=32, head_dim=16, num_local_experts=8, num_experts_per_tok=2, use_qk_norm=True,
+                        rope_parameters={"rope_theta": 5e6, "rope_type": "default", "partial_rotary_factor": 0.5})),
+    "qwen3.5-moe": ("Qwen3_5MoeForCausalLM", "Qwen3_5MoeTextConfig", dict(GDN)),
+    "qwen3-next": ("Qwen3NextForCausalLM", "Qwen3NextConfig", dict(GDN, decoder_sparse_step=1, mlp_only_layers=[])),
+}
+
+
+def _library_greedy(model, prompt, n):
+    """Greedy continuation by whole-sequence forward passes (no cache, no stop token)."""
+    ids = list(prompt)
+    with torch.no_grad():
+        for _ in range(n):
+            ids.append(int(model(torch.tensor([ids])).logits[0, -1].argmax()))
+    return ids[len(prompt):]
+
+
+@pytest.mark.parametrize("family", list(FAMILIES))
+def test_served_tokens_equal_the_transformers_implementation(family, tmp_path):
+    cls_name, cfg_name, extra = FAMILIES[family]
+    if not (hasattr(transformers, cls_name) and hasattr(transformers, cfg_name)):
+        pytest.skip(f"transformers {transformers.__version__} has no {cls_name}")
+    torch.manual_seed(0)
+    kw = dict(COMMON)
+    kw.update(extra)
+    model = getattr(transformers, cls_name)(getattr(transformers, cfg_name)(**kw)).float().eval()
+    with torch.no_grad():                      # norm weights, biases, decay and routing offsets away from their defaults
+        for _name, p in model.named_parameters():
+            if p.dim() == 1:
+                p.add_(0.1 * torch.randn_like(p))
+    path = str(tmp_path / family)
+    model.save_pretrained(path, safe_serialization=True)
+    g = torch.Generator().manual_seed(1)
+    prompts = [torch.randint(0, 256, (n,), generator=g).tolist() for n in (5, 11, 3)]
+    want = [_library_greedy(model, p, 6) for p in prompts]
+    llm = LLM(path, device="cpu", num_pages=64, max_seq_len=128)
+    try:
+        got = [o["token_ids"] for o in llm.generate(prompts, SamplingParams(max_tokens=6, ignore_eos=True))]
+    finally:
+        llm.shutdown()
+    assert got == want
+
+
+def test_q_gate_row_layout_round_trip():
+    from fastafd_b200.models.loader import merge_q_gate_rows, split_q_gate_rows
+
+    heads, d = 3, 4
+    w = torch.arange(heads * 2 * d * 5, dtype=torch.float32).reshape(heads * 2 * d, 5)
+    s = split_q_gate_rows(w, heads, d)
+    assert torch.equal(s[:heads * d].reshape(heads, d, 5), w.reshape(heads, 2, d, 5)[:, 0])       # queries of all heads first
+    assert torch.equal(s[heads * d:].reshape(heads, d, 5), w.reshape(heads, 2, d, 5)[:, 1])       # then the gates
+    assert torch.equal(merge_q_gate_rows(s, heads, d), w)
+    bias = torch.arange(heads * 2 * d, dtype=torch.float32)
+    assert torch.equal(merge_q_gate_rows(split_q_gate_rows(bias, heads, d), heads, d), bias)
