@@ -39,6 +39,25 @@ FAMILIES = {
                    dict(intermediate_size=32, head_dim=16, num_local_experts=8, num_experts_per_tok=2, use_qk_norm=True,
                         rope_parameters={"rope_theta": 5e6, "rope_type": "default", "partial_rotary_factor": 0.5})),
     "qwen3.5-moe": ("Qwen3_5MoeForCausalLM", "Qwen3_5MoeTextConfig", dict(GDN)),
+    # variants: rotary scaling rules, routing without renormalisation, attention bias, several shared experts
+    "llama-rope-llama3": ("LlamaForCausalLM", "LlamaConfig",
+                          dict(intermediate_size=128, rope_parameters={"rope_type": "llama3", "rope_theta": 10000.0, "factor": 8.0,
+                                                                       "low_freq_factor": 1.0, "high_freq_factor": 4.0,
+                                                                       "original_max_position_embeddings": 64})),
+    "qwen3-rope-yarn": ("Qwen3ForCausalLM", "Qwen3Config",
+                        dict(intermediate_size=128, head_dim=16, rope_parameters={"rope_type": "yarn", "rope_theta": 1e6, "factor": 4.0,
+                                                                                  "original_max_position_embeddings": 64})),
+    "llama-rope-linear": ("LlamaForCausalLM", "LlamaConfig",
+                          dict(intermediate_size=128, rope_parameters={"rope_type": "linear", "rope_theta": 10000.0, "factor": 2.0})),
+    "qwen2-tied-embeddings": ("Qwen2ForCausalLM", "Qwen2Config", dict(intermediate_size=128, tie_word_embeddings=True)),
+    "glm4-moe-bias-no-qk-norm": ("Glm4MoeForCausalLM", "Glm4MoeConfig",
+                                 dict(intermediate_size=128, head_dim=16, moe_intermediate_size=32, n_routed_experts=8,
+                                      num_experts_per_tok=2, n_shared_experts=2, n_group=1, topk_group=1, first_k_dense_replace=0,
+                                      norm_topk_prob=False, routed_scaling_factor=2.5, use_qk_norm=False, partial_rotary_factor=0.5,
+                                      attention_bias=True)),
+    "qwen3-moe-top3-no-renorm": ("Qwen3MoeForCausalLM", "Qwen3MoeConfig",
+                                 dict(intermediate_size=128, head_dim=16, moe_intermediate_size=32, num_experts=8, num_experts_per_tok=3,
+                                      norm_topk_prob=False, decoder_sparse_step=1, mlp_only_layers=[])),
     "qwen3-next": ("Qwen3NextForCausalLM", "Qwen3NextConfig", dict(GDN, decoder_sparse_step=1, mlp_only_layers=[])),
 }
 
