@@ -370,3 +370,41 @@ def test_offline_api_takes_the_reference_keywords_and_per_prompt_sampling():
             llm.generate([[1, 2]], [SamplingParams(), SamplingParams()])
     finally:
         llm.shutdown()
+
+
+def test_hugging_face_tokenizer_directory_chat_template_and_incremental_detokenise(tmp_path):
+    """A tokenizer directory as `transformers` saves it (byte-level BPE, a chat template): requests with
+    `messages` go through the template, and text streamed token by token equals the text decoded at once, also
+    where one character spans several tokens."""
+    tokenizers = pytest.importorskip("tokenizers")
+    from tokenizers import Tokenizer, decoders, models, pre_tokenizers, trainers
+    from transformers import PreTrainedTokenizerFast
+
+    from fastafd_b200.message import DetokenizeMsg, TokenizeMsg
+    from fastafd_b200.tokenizer import DetokenizeManager, load_tokenizer, tokenize_request
+
+    tk = Tokenizer(models.BPE(unk_token=None))
+    tk.pre_tokenizer = pre_tokenizers.ByteLevel(add_prefix_space=False)
+    tk.decoder = decoders.ByteLevel()
+    trainer = trainers.BpeTrainer(vocab_size=300, special_tokens=["<|im_start|>", "<|im_end|>"],
+                                  initial_alphabet=pre_tokenizers.ByteLevel.alphabet())
+    tk.train_from_iterator(["hello world, how are you today?", "the quick brown fox jumps over the lazy dog"] * 20, trainer)
+    template = ("{% for m in messages %}<|im_start|>{{ m['role'] }}\n{{ m['content'] }}<|im_end|>\n{% endfor %}"
+                "{% if add_generation_prompt %}<|im_start|>assistant\n{% endif %}")
+    PreTrainedTokenizerFast(tokenizer_object=tk, eos_token="<|im_end|>", chat_template=template).save_pretrained(str(tmp_path))
+    tok = load_tokenizer(str(tmp_path))
+    assert type(tok).__name__ != "ByteTokenizer"
+    ids = tokenize_request(tok, TokenizeMsg(uid=1, messages=[{"role": "user", "content": "hello world"}]), 300, 256)
+    text = tok.decode(ids)
+    assert text == "<|im_start|>user\nhello world<|im_end|>\n<|im_start|>assistant\n"
+    assert ids[0] == tok.convert_tokens_to_ids("<|im_start|>") and ids.count(ids[0]) == 2      # special tokens are single ids
+    plain = tokenize_request(tok, TokenizeMsg(uid=2, text="the lazy dog"), 300, 256)
+    assert tok.decode(plain) == "the lazy dog"
+    # streaming: characters outside the training text fall back to bytes, several tokens per character
+    sample = "hello wörld ✓ 你好, the fox"
+    out_ids = tok.encode(sample)
+    assert len(out_ids) > len(sample.split())
+    dm = DetokenizeManager(tok)
+    streamed = "".join(dm.step(DetokenizeMsg(uid=7, token_ids=[t], finished=(i == len(out_ids) - 1))).text
+                       for i, t in enumerate(out_ids))
+    assert streamed == sample and "�" not in streamed
