@@ -218,6 +218,10 @@ def load_expert_stage(stage: ExpertStage, path: str) -> None:
             except KeyError as err:
                 raise KeyError(f"checkpoint lacks expert {lo + e} of layer {layer}: {err}") from None
             if fp8:
+                if I % 128:
+                    # gate rows and up rows are merged into one matrix; with an intermediate size that is not a
+                    # multiple of the 128-row scale block, the last gate rows and the first up rows would share a block
+                    raise ValueError(f"block-FP8 experts need moe_intermediate_size to be a multiple of 128, got {I}")
                 gb = (I + 127) // 128
                 gus[e, :gb] = got[(e, "gate_proj", "weight_scale_inv")].float()
                 gus[e, gb:] = got[(e, "up_proj", "weight_scale_inv")].float()

@@ -108,3 +108,78 @@ def test_q_gate_row_layout_round_trip():
     assert torch.equal(merge_q_gate_rows(s, heads, d), w)
     bias = torch.arange(heads * 2 * d, dtype=torch.float32)
     assert torch.equal(merge_q_gate_rows(split_q_gate_rows(bias, heads, d), heads, d), bias)
+
+
+FP8_SKIP = ("embed_tokens", "lm_head", "norm", "mlp.gate.weight", "block_sparse_moe.gate.weight", "shared_expert_gate", "conv1d",
+            "A_log", "dt_bias", "in_proj_a", "in_proj_b", "in_proj_ba", "e_score")
+
+
+def _fp8_pair(family, tmp_path, inter):
+    """(directory with block-FP8 weights + scales, the library model holding the dequantised values)."""
+    import glob
+    import json
+
+    from safetensors.torch import load_file, save_file
+
+    from fastafd_b200.reference import ops_ref as ref
+
+    cls_name, cfg_name, extra = FAMILIES[family]
+    torch.manual_seed(0)
+    kw = dict(COMMON)
+    kw.update(extra)
+    kw["hidden_size"] = 128
+    for key in ("moe_intermediate_size", "shared_expert_intermediate_size"):
+        if key in kw:
+            kw[key] = inter
+    if family == "minimax-m2":
+        kw["intermediate_size"] = inter
+    cls = getattr(transformers, cls_name)
+    model = cls(getattr(transformers, cfg_name)(**kw)).float().eval()
+    fp8_dir, deq_dir = str(tmp_path / "fp8"), str(tmp_path / "dequantised")
+    model.save_pretrained(fp8_dir, safe_serialization=True)
+    model.save_pretrained(deq_dir, safe_serialization=True)
+    f = glob.glob(fp8_dir + "/*.safetensors")[0]
+    sd = {k: v.clone() for k, v in load_file(f).items()}
+    out = {}
+    for k, w in sd.items():
+        if w.dim() == 2 and k.endswith(".weight") and not any(s in k for s in FP8_SKIP):
+            q, s = ref.block_quant_fp8(w.float())
+            out[k], out[k[:-len("weight")] + "weight_scale_inv"] = q, s.float()
+            sd[k] = ref.block_dequant_fp8(q, s.float())
+        else:
+            out[k] = w
+    save_file(out, f, metadata={"format": "pt"})
+    save_file(sd, glob.glob(deq_dir + "/*.safetensors")[0], metadata={"format": "pt"})
+    cfg = json.load(open(fp8_dir + "/config.json"))
+    cfg["quantization_config"] = {"quant_method": "fp8", "fmt": "e4m3", "activation_scheme": "dynamic",
+                                  "weight_block_size": [128, 128], "modules_to_not_convert": ["lm_head"]}
+    json.dump(cfg, open(fp8_dir + "/config.json", "w"))
+    return fp8_dir, cls.from_pretrained(deq_dir, dtype=torch.float32).eval()
+
+
+@pytest.mark.parametrize("family", ["qwen3-moe", "glm4-moe", "minimax-m2", "qwen3.5-moe", "qwen3-next"])
+def test_block_fp8_checkpoints_equal_the_library_on_the_dequantised_weights(family, tmp_path):
+    """The same models with every projection and expert matrix stored as e4m3 codes + 128x128 `weight_scale_inv`
+    blocks under each family's key names: serving that directory gives the tokens of the library run on the
+    dequantised values (on CPU the engine computes with code x scale in fp32, so nothing else differs)."""
+    cls_name, cfg_name, _ = FAMILIES[family]
+    if not (hasattr(transformers, cls_name) and hasattr(transformers, cfg_name)):
+        pytest.skip(f"transformers {transformers.__version__} has no {cls_name}")
+    fp8_dir, model = _fp8_pair(family, tmp_path, 128)
+    g = torch.Generator().manual_seed(1)
+    prompts = [torch.randint(0, 256, (n,), generator=g).tolist() for n in (5, 11, 3)]
+    want = [_library_greedy(model, p, 6) for p in prompts]
+    llm = LLM(fp8_dir, device="cpu", num_pages=64, max_seq_len=128)
+    try:
+        got = [o["token_ids"] for o in llm.generate(prompts, SamplingParams(max_tokens=6, ignore_eos=True))]
+    finally:
+        llm.shutdown()
+    assert got == want
+
+
+def test_block_fp8_experts_with_ragged_gate_up_blocks_are_refused(tmp_path):
+    """Gate rows and up rows become one matrix; an intermediate size that is not a multiple of the scale block
+    would make them share a block of scales, so such a checkpoint is refused instead of served with wrong scales."""
+    fp8_dir, _ = _fp8_pair("qwen3-moe", tmp_path, 32)
+    with pytest.raises(ValueError, match="multiple of 128"):
+        LLM(fp8_dir, device="cpu", num_pages=64, max_seq_len=128)
