@@ -183,3 +183,45 @@ def test_block_fp8_experts_with_ragged_gate_up_blocks_are_refused(tmp_path):
     fp8_dir, _ = _fp8_pair("qwen3-moe", tmp_path, 32)
     with pytest.raises(ValueError, match="multiple of 128"):
         LLM(fp8_dir, device="cpu", num_pages=64, max_seq_len=128)
+
+
+@pytest.mark.timeout(300)
+@pytest.mark.parametrize("family", ["qwen3.5-moe", "minimax-m2"])
+def test_disaggregated_tensor_parallel_serving_of_a_library_checkpoint(family, tmp_path):
+    """The same checkpoints behind the HTTP server as four CPU processes: one attention lane of two tensor-parallel
+    ranks (head shards of the gated attention and of the gated DeltaNet, the cross-head q/k norm with its
+    all-reduce) and two expert-parallel ranks, each reading only its part of the directory."""
+    import requests
+
+    from fastafd_b200.server.args import parse_args
+    from fastafd_b200.server.launch import local_endpoint
+    from fastafd_b200.server.supervisor import LocalSupervisor
+
+    cls_name, cfg_name, extra = FAMILIES[family]
+    if not (hasattr(transformers, cls_name) and hasattr(transformers, cfg_name)):
+        pytest.skip(f"transformers {transformers.__version__} has no {cls_name}")
+    torch.manual_seed(0)
+    kw = dict(COMMON)
+    kw.update(extra)
+    model = getattr(transformers, cls_name)(getattr(transformers, cfg_name)(**kw)).float().eval()
+    with torch.no_grad():
+        for _name, p in model.named_parameters():
+            if p.dim() == 1:
+                p.add_(0.1 * torch.randn_like(p))
+    path = str(tmp_path / family)
+    model.save_pretrained(path, safe_serialization=True)
+    g = torch.Generator().manual_seed(1)
+    prompts = [torch.randint(0, 256, (n,), generator=g).tolist() for n in (5, 11, 3)]
+    want = [_library_greedy(model, p, 6) for p in prompts]
+    args = parse_args(["--mode", "afd-serve", "--model-path", path, "--device", "cpu", "--afd-num-mb", "2", "--afd-attn-dp-size", "1",
+                       "--afd-attn-tp-size", "2", "--afd-mlp-ep-size", "2", "--num-pages", "64", "--max-seq-len-override", "128",
+                       "--afd-max-running-requests", "8", "--cuda-graph-max-bs", "8"])
+    sup = LocalSupervisor(args)
+    got = []
+    with local_endpoint(args, sup) as url:
+        for p in prompts:
+            r = requests.post(url + "/v1/chat/completions", json={"input_ids": p, "max_tokens": 6, "temperature": 0, "ignore_eos": True,
+                                                                  "return_token_ids": True, "stream": False}, timeout=200).json()
+            got.append(r["choices"][0]["token_ids"])
+        assert sup.get_failures() == []
+    assert got == want
