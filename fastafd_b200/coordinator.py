@@ -68,12 +68,23 @@ class CoordinatorError(RuntimeError):
     pass
 
 
+def check_cache_type(cfg: ModelConfig, rt: RuntimeConfig) -> None:
+    """A prefix hit skips the cached tokens, which is sound for attention (their K/V are in the shared pages) but
+    not for the recurrent state of linear-attention layers: that state after the shared prefix is not kept
+    anywhere. Hybrid models therefore run without prefix reuse.
+    Reference: python/minisgl/scheduler/scheduler.py:155-159."""
+    if cfg.num_linear_layers and rt.cache_type != "naive":
+        raise ValueError(f"models with linear-attention layers need --cache-type naive (got {rt.cache_type!r}): the "
+                         "recurrent state at the end of a cached prefix is not kept")
+
+
 class AfdCoordinator:
     def __init__(self, cfg: ModelConfig, rt: RuntimeConfig, topo: AfdTopology, transport: WorkerTransport, *,
                  num_pages: int, max_comm_tokens: int = 2048,
                  on_tokens: Optional[Callable[[List[Tuple[int, List[int], bool]]], None]] = None,
                  worker_timeout_s: float = 120.0):
         self.cfg, self.rt, self.topo, self.transport = cfg, rt, topo, transport
+        check_cache_type(cfg, rt)
         self.on_tokens = on_tokens or (lambda items: None)
         self.worker_timeout_s = worker_timeout_s
         self.buckets = [b for b in normalize_buckets(rt.decode_graph_bs, rt.cuda_graph_max_bs) if b % topo.attn_tp == 0] or [topo.attn_tp]

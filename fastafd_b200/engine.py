@@ -300,6 +300,9 @@ class SpmdDriver:
     def __init__(self, engine: AfdEngine, num_pages: Optional[int] = None):
         self.e = engine
         topo, rt, cfg = engine.topo, engine.rt, engine.cfg
+        from .coordinator import check_cache_type
+
+        check_cache_type(cfg, rt)
         self.num_lanes = 1 if engine.colocated else topo.attn_dp
         pages = num_pages or (engine.attn.num_pages if engine.attn is not None else rt.num_pages)
         if not engine.colocated and dist.is_initialized():

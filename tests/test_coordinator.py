@@ -251,3 +251,18 @@ def test_reply_latency_is_kept_per_rank_and_logged_at_shutdown(caplog):
     with caplog.at_level(logging.INFO):
         coord.shutdown()
     assert any("reply latency per rank" in r.getMessage() for r in caplog.records)
+
+
+def test_hybrid_models_refuse_the_prefix_cache():
+    """The recurrent state of linear-attention layers at the end of a cached prefix is kept nowhere, so a prefix hit
+    would continue from a wrong state: refused at construction, by the coordinator and by the SPMD driver alike."""
+    import dataclasses
+
+    from fastafd_b200.config import get_model_config
+
+    hybrid = dataclasses.replace(get_model_config("qwen3.5-397b-a17b-fp8"), num_layers=4, layer_types=("linear", "linear", "linear", "full"))
+    topo = AfdTopology(attn_dp=1, mlp_ep=1)
+    with pytest.raises(ValueError, match="cache-type naive"):
+        AfdCoordinator(hybrid, _rt(cache_type="radix"), topo, FakeWorkers(), num_pages=64)
+    AfdCoordinator(hybrid, _rt(cache_type="naive"), topo, FakeWorkers(), num_pages=64)
+    AfdCoordinator(PRESETS["tiny-qwen3-moe"], _rt(cache_type="radix"), topo, FakeWorkers(), num_pages=64)
