@@ -76,6 +76,9 @@ def check_cache_type(cfg: ModelConfig, rt: RuntimeConfig) -> None:
     if cfg.num_linear_layers and rt.cache_type != "naive":
         raise ValueError(f"models with linear-attention layers need --cache-type naive (got {rt.cache_type!r}): the "
                          "recurrent state at the end of a cached prefix is not kept")
+    if cfg.num_linear_layers and rt.spec_block > 1:
+        raise ValueError("speculative decoding is not available for models with linear-attention layers: the recurrent "
+                         "state cannot be rolled back past rejected draft tokens")
 
 
 class AfdCoordinator:

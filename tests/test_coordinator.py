@@ -265,4 +265,6 @@ def test_hybrid_models_refuse_the_prefix_cache():
     with pytest.raises(ValueError, match="cache-type naive"):
         AfdCoordinator(hybrid, _rt(cache_type="radix"), topo, FakeWorkers(), num_pages=64)
     AfdCoordinator(hybrid, _rt(cache_type="naive"), topo, FakeWorkers(), num_pages=64)
+    with pytest.raises(ValueError, match="rolled back"):          # nor can rejected draft tokens be undone in that state
+        AfdCoordinator(hybrid, _rt(spec_block=4), topo, FakeWorkers(), num_pages=64)
     AfdCoordinator(PRESETS["tiny-qwen3-moe"], _rt(cache_type="radix"), topo, FakeWorkers(), num_pages=64)
