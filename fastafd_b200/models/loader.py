@@ -69,6 +69,16 @@ def iter_checkpoint(path: str, want=None) -> Iterator[Tuple[str, torch.Tensor]]:
                     yield k, sf.get_tensor(k)
 
 
+_LAYER_RE = re.compile(r"(?:^|\.)layers\.(\d+)\.")
+
+
+def _beyond_last_layer(key: str, num_layers: int) -> bool:
+    """Checkpoints of models with next-token-prediction heads store those as extra decoder layers behind the last
+    one (GLM-4.5: layer `num_hidden_layers`); they are not served and need not be read."""
+    m = _LAYER_RE.search(key)
+    return m is not None and int(m.group(1)) >= num_layers
+
+
 def _dequant_if_fp8(w: torch.Tensor, scale: Optional[torch.Tensor]) -> torch.Tensor:
     if w.dtype == torch.float8_e4m3fn:
         if scale is None:
@@ -121,7 +131,7 @@ def load_attention_stage(stage: AttentionStage, path: str) -> None:
     scales: Dict[str, torch.Tensor] = {}
     def wanted(key: str) -> bool:                     # skip_expert_weights
         k = normalize_key(key)
-        return k is not None and not _EXPERT_RE.search(k)
+        return k is not None and not _EXPERT_RE.search(k) and not _beyond_last_layer(k, cfg.num_layers)
 
     for key, t in iter_checkpoint(path, wanted):
         k = normalize_key(key)
@@ -195,7 +205,7 @@ def load_expert_stage(stage: ExpertStage, path: str) -> None:
     def wanted(key: str) -> bool:                     # skip_non_expert_weights, other ranks' experts
         k = normalize_key(key)
         m = _EXPERT_RE.search(k) if k is not None else None
-        return m is not None and lo <= int(m.group(1)) < hi
+        return m is not None and lo <= int(m.group(1)) < hi and not _beyond_last_layer(k, cfg.num_layers)
 
     for key, t in iter_checkpoint(path, wanted):
         k = normalize_key(key)

@@ -225,3 +225,34 @@ def test_disaggregated_tensor_parallel_serving_of_a_library_checkpoint(family, t
             got.append(r["choices"][0]["token_ids"])
         assert sup.get_failures() == []
     assert got == want
+
+
+def test_extra_layers_behind_the_last_one_are_not_read(tmp_path):
+    """GLM-4.5 checkpoints carry a next-token-prediction block as decoder layer `num_hidden_layers` (its own
+    experts included). It is not served; its tensors are skipped whatever their shapes."""
+    import glob
+
+    from safetensors.torch import load_file, save_file
+
+    cls_name, cfg_name, extra = FAMILIES["glm4-moe"]
+    torch.manual_seed(0)
+    kw = dict(COMMON)
+    kw.update(extra)
+    model = getattr(transformers, cls_name)(getattr(transformers, cfg_name)(**kw)).float().eval()
+    path = str(tmp_path / "glm")
+    model.save_pretrained(path, safe_serialization=True)
+    f = glob.glob(path + "/*.safetensors")[0]
+    sd = {k: v.clone() for k, v in load_file(f).items()}
+    n = kw["num_hidden_layers"]
+    sd[f"model.layers.{n}.eh_proj.weight"] = torch.randn(7, 3)
+    sd[f"model.layers.{n}.mlp.experts.0.gate_proj.weight"] = torch.randn(5, 5)
+    sd[f"model.layers.{n}.self_attn.q_proj.weight"] = torch.randn(2, 2)
+    save_file(sd, f, metadata={"format": "pt"})
+    prompts = [[5, 9, 2, 44, 17], [8, 3]]
+    want = [_library_greedy(model, p, 4) for p in prompts]
+    llm = LLM(path, device="cpu", num_pages=64, max_seq_len=128)
+    try:
+        got = [o["token_ids"] for o in llm.generate(prompts, SamplingParams(max_tokens=4, ignore_eos=True))]
+    finally:
+        llm.shutdown()
+    assert got == want
