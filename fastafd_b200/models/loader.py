@@ -37,14 +37,18 @@ _EXPERT_RE = re.compile(r"\.(?:mlp|block_sparse_moe)\.experts\.(\d+)\.(gate_proj
 _EXPERT_ALIAS = {"w1": "gate_proj", "w3": "up_proj", "w2": "down_proj"}
 
 
+_WRAPPER_RE = re.compile(r"^(?:model\.)?(?:language_model\.)+")
+
+
 def normalize_key(name: str) -> Optional[str]:
     """Checkpoint key -> internal key, or None for tensors this build does not use."""
-    if name.startswith("model.language_model."):
-        name = "model." + name[len("model.language_model."):]
-    if name.startswith("language_model."):
-        name = name[len("language_model."):]
     if ".visual." in name or name.startswith("visual.") or "mtp." in name:
         return None
+    # multimodal wrappers nest the text model: model.language_model.layers..., language_model.model.layers...
+    m = _WRAPPER_RE.match(name)
+    if m and m.group(0):
+        rest = name[m.end():]
+        name = rest if rest.startswith(("model.", "lm_head.")) else "model." + rest
     if name.endswith((".k_scale", ".v_scale", ".kv_scale", "rotary_emb.inv_freq")):
         return None
     name = name.replace(".block_sparse_moe.gate.", ".mlp.gate.")

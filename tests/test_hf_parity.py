@@ -256,3 +256,53 @@ def test_extra_layers_behind_the_last_one_are_not_read(tmp_path):
     finally:
         llm.shutdown()
     assert got == want
+
+
+def test_checkpoint_key_prefixes_of_multimodal_wrappers():
+    """Text models inside multimodal wrappers: every nesting of `language_model.` in front of the text model's keys
+    maps to the plain key; vision towers and next-token-prediction heads are not read."""
+    from fastafd_b200.models.loader import normalize_key as n
+
+    cases = {"model.language_model.layers.3.self_attn.q_proj.weight": "model.layers.3.self_attn.q_proj.weight",
+             "model.language_model.embed_tokens.weight": "model.embed_tokens.weight",
+             "language_model.model.layers.0.input_layernorm.weight": "model.layers.0.input_layernorm.weight",
+             "language_model.lm_head.weight": "lm_head.weight",
+             "model.language_model.language_model.norm.weight": "model.norm.weight",
+             "model.layers.0.mlp.gate.weight": "model.layers.0.mlp.gate.weight", "lm_head.weight": "lm_head.weight",
+             "model.layers.0.block_sparse_moe.gate.weight": "model.layers.0.mlp.gate.weight",
+             "model.layers.0.mlp.shared_experts.up_proj.weight": "model.layers.0.mlp.shared_expert.up_proj.weight",
+             "model.visual.blocks.0.attn.qkv.weight": None, "model.language_model.visual.merger.norm.weight": None,
+             "mtp.layers.0.self_attn.q_proj.weight": None, "model.layers.0.self_attn.rotary_emb.inv_freq": None}
+    for key, want in cases.items():
+        assert n(key) == want, (key, n(key), want)
+
+
+def test_qwen35_inside_its_multimodal_wrapper(tmp_path):
+    """Qwen3.5 as published: `Qwen3_5MoeForConditionalGeneration` with the text model under `text_config` and a
+    vision tower beside it. Text-only requests give the library's tokens; the tower is never read."""
+    T = transformers
+    if not all(hasattr(T, n) for n in ("Qwen3_5MoeForConditionalGeneration", "Qwen3_5MoeConfig", "Qwen3_5MoeTextConfig")):
+        pytest.skip("no Qwen3.5 multimodal classes in this transformers")
+    kw = dict(COMMON)
+    kw.update(GDN)
+    vision = dict(depth=1, hidden_size=32, intermediate_size=64, num_heads=2, out_hidden_size=64, patch_size=2, spatial_merge_size=1,
+                  temporal_patch_size=1, in_channels=3, num_position_embeddings=16)
+    torch.manual_seed(0)
+    model = T.Qwen3_5MoeForConditionalGeneration(T.Qwen3_5MoeConfig(text_config=T.Qwen3_5MoeTextConfig(**kw).to_dict(),
+                                                                   vision_config=vision)).float().eval()
+    path = str(tmp_path / "wrapped")
+    model.save_pretrained(path, safe_serialization=True)
+    prompts = [[5, 9, 2, 44, 17, 3, 200], [8, 3, 99]]
+    want = []
+    for p in prompts:
+        ids = list(p)
+        with torch.no_grad():
+            for _ in range(5):
+                ids.append(int(model(input_ids=torch.tensor([ids])).logits[0, -1].argmax()))
+        want.append(ids[len(p):])
+    llm = LLM(path, device="cpu", num_pages=64, max_seq_len=128)
+    try:
+        got = [o["token_ids"] for o in llm.generate(prompts, SamplingParams(max_tokens=5, ignore_eos=True))]
+    finally:
+        llm.shutdown()
+    assert got == want
