@@ -30,6 +30,33 @@ def first_divergence(a, b) -> int:
     return min(len(a), len(b))
 
 
+def library_reference(model_path: str, prompts, served, decode: int):
+    """(greedy continuations of the `transformers` model, rank scores of the served continuations under it).
+    Whole-sequence forward passes in fp32 on the CPU, no cache: slow and simple on purpose.
+    Reference: scripts/validate/compare_minisgl_vllm.py (alignment against an independent implementation; there vLLM,
+    here the library that defines the checkpoint format)."""
+    from transformers import AutoModelForCausalLM
+
+    model = AutoModelForCausalLM.from_pretrained(model_path, dtype=torch.float32).eval()
+    oracle, ranks = [], []
+    with torch.no_grad():
+        for p, s in zip(prompts, served):
+            ids = list(p)
+            for _ in range(decode):
+                ids.append(int(model(input_ids=torch.tensor([ids])).logits[0, -1].argmax()))
+            oracle.append(ids[len(p):])
+            logits = model(input_ids=torch.tensor([list(p) + list(s)])).logits[0]       # teacher-forced on what was served
+            r = []
+            for i, tok in enumerate(s):
+                row = logits[len(p) - 1 + i]
+                r.append(int((row > row[tok]).sum()))          # 0 = the library's own greedy choice
+            ranks.append(r)
+    flat = [x for r in ranks for x in r]
+    n = max(len(flat), 1)
+    return oracle, {"ranks": ranks, "tokens": len(flat), "top1_agreement_rate": sum(x == 0 for x in flat) / n,
+                    "top10_hit_rate": sum(x < 10 for x in flat) / n, "top100_hit_rate": sum(x < 100 for x in flat) / n}
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(prog="fastafd_b200.validate")
     ap.add_argument("--model", default="tiny-qwen3-moe", help="preset name (random-init weights)")
@@ -45,6 +72,10 @@ def main(argv=None) -> int:
                                                                  "oracle's own choice (default 1.0 on CPU, 0.9 on CUDA)")
     ap.add_argument("--min-top10", type=float, default=0.99, help="rank gate: share within the oracle's top 10")
     ap.add_argument("--min-top100", type=float, default=1.0, help="rank gate: share within the oracle's top 100")
+    ap.add_argument("--against", default="oracle", choices=["oracle", "transformers"],
+                    help="what the served tokens are compared with: this package's whole-sequence PyTorch forward of the "
+                         "same weights, or the `transformers` implementation of the model loading the same directory "
+                         "(CPU, fp32): an implementation that shares no code with this package")
     a = ap.parse_args(argv)
 
     from .config import ModelConfig, RuntimeConfig, get_model_config
@@ -52,7 +83,9 @@ def main(argv=None) -> int:
     from .engine import AfdEngine, SpmdDriver
     from .protocol import AfdTopology
 
-    cfg = ModelConfig.from_hf(a.model_path) if a.model_path else get_model_config(a.model)
+    cfg = get_model_config(a.model_path or a.model)
+    if a.against == "transformers" and not a.model_path:
+        ap.error("--against transformers needs --model-path (a checkpoint directory both sides can load)")
     g = torch.Generator().manual_seed(a.seed)
     prompts = [torch.randint(0, cfg.vocab_size, (a.prompt_len,), generator=g).tolist() for _ in range(a.prompts)]
     sp = SamplingParams(max_tokens=a.decode, ignore_eos=True)
@@ -76,15 +109,19 @@ def main(argv=None) -> int:
         finally:
             eng.close()
 
-    if a.device == "cpu":
-        served, oracle, ref_eng = generate("cpu", False, True)
+    if a.against == "transformers":
+        served, _, _ = generate(a.device, a.device != "cpu", False)
+        oracle, score = library_reference(a.model_path, prompts, served, a.decode)
     else:
-        served, _, _ = generate(a.device, True, False)
-        _, oracle, ref_eng = generate("cpu", False, True)
-    # rank gate: the served continuation, teacher-forced through the oracle (the weights outlive close())
-    from .reference.model_ref import score_continuations
+        if a.device == "cpu":
+            served, oracle, ref_eng = generate("cpu", False, True)
+        else:
+            served, _, _ = generate(a.device, True, False)
+            _, oracle, ref_eng = generate("cpu", False, True)
+        # rank gate: the served continuation, teacher-forced through the oracle (the weights outlive close())
+        from .reference.model_ref import score_continuations
 
-    score = score_continuations(cfg, ref_eng.attn.model, [ref_eng.expert_stage], prompts, served)
+        score = score_continuations(cfg, ref_eng.attn.model, [ref_eng.expert_stage], prompts, served)
     need1 = a.min_top1 if a.min_top1 >= 0 else (1.0 if a.device == "cpu" else 0.9)
     rank_ok = (score["top1_agreement_rate"] >= need1 and score["top10_hit_rate"] >= a.min_top10
                and score["top100_hit_rate"] >= a.min_top100)
@@ -93,7 +130,7 @@ def main(argv=None) -> int:
     div = [first_divergence(s, o) for s, o in zip(served, oracle)]
     need = a.min_match if a.min_match >= 0 else (1.0 if a.device == "cpu" else 0.8)
     ok = same >= need * total and rank_ok
-    print(json.dumps({"model": a.model_path or a.model, "device": a.device, "tokens": total, "identical": same,
+    print(json.dumps({"model": a.model_path or a.model, "device": a.device, "against": a.against, "tokens": total, "identical": same,
                       "match": round(same / max(total, 1), 4), "first_divergence": div, "min_match": need,
                       "overall_top1_agreement_rate": round(score["top1_agreement_rate"], 4),
                       "overall_top10_hit_rate": round(score["top10_hit_rate"], 4),

@@ -306,3 +306,26 @@ def test_qwen35_inside_its_multimodal_wrapper(tmp_path):
     finally:
         llm.shutdown()
     assert got == want
+
+
+def test_alignment_tool_against_the_library(tmp_path, capsys):
+    """`python -m fastafd_b200.validate --model-path DIR --against transformers`: the alignment report (identical
+    share, first divergence, rank gate) with the library's implementation as the other side; and with the package's
+    own whole-sequence forward of the same directory."""
+    import json
+
+    from fastafd_b200 import validate
+
+    cls_name, cfg_name, extra = FAMILIES["minimax-m2"]
+    torch.manual_seed(0)
+    kw = dict(COMMON)
+    kw.update(extra)
+    path = str(tmp_path / "m")
+    getattr(transformers, cls_name)(getattr(transformers, cfg_name)(**kw)).float().save_pretrained(path, safe_serialization=True)
+    common = ["--model-path", path, "--device", "cpu", "--prompts", "2", "--prompt-len", "9", "--decode", "4"]
+    assert validate.main(common + ["--against", "transformers"]) == 0
+    rep = json.loads(capsys.readouterr().out.strip().splitlines()[-1])
+    assert rep["against"] == "transformers" and rep["verdict"] == "pass" and rep["match"] == 1.0
+    assert rep["rank_gate"]["worst_rank"] == 0 and rep["first_divergence"] == [4, 4]
+    assert validate.main(common) == 0
+    assert json.loads(capsys.readouterr().out.strip().splitlines()[-1])["against"] == "oracle"
