@@ -50,11 +50,14 @@ class SpecRunner:
         self.w, self.block, self.sim_accept = worker, block, sim_accept
         self.rng = np.random.default_rng(seed)
         cfg = worker.cfg
-        self.dcfg = Eagle3Config.for_target(cfg)
+        # a published head brings its own sizes, vocabulary and auxiliary layers; a synthetic one follows the target
+        self.dcfg = Eagle3Config.from_dir(draft_path, cfg) if draft_path else Eagle3Config.for_target(cfg)
         slots = worker.kv.num_pages * worker.kv.page_size
         self.draft = Eagle3Draft(self.dcfg, worker.device, worker.dtype, slots)
         if draft_path:
-            self.draft.load(draft_path)
+            tw = worker.model.w
+            self.draft.load(draft_path, share_embedding=tw["model.embed_tokens.weight"],
+                            share_lm_head=tw.get("lm_head.weight", tw["model.embed_tokens.weight"]))
         else:
             self.draft.init_random(seed, share_embedding=worker.model.w["model.embed_tokens.weight"])
         self.capture_layers = list(self.dcfg.target_layers)

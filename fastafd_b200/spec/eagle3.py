@@ -48,6 +48,44 @@ class Eagle3Config:
                             draft_vocab or min(cfg.vocab_size, 32000), cfg.vocab_size, layers, cfg.rms_eps, cfg.rope.theta)
 
 
+    @staticmethod
+    def from_dir(path: str, target: ModelConfig) -> "Eagle3Config":
+        """The draft head's own ``config.json`` (a one-layer Llama-style decoder): sizes, heads, draft vocabulary
+        (``draft_vocab_size``, else the target's), rotary base, and the target layers whose outputs feed ``fc``
+        (``eagle_config.eagle_aux_hidden_state_layer_ids``, read as layer outputs; default: layers 1, L/2 - 1 and
+        L - 4; ``FASTAFD_SPEC_EAGLE3_LAYERS=a,b,c`` overrides). Variants this build does not run are refused.
+        Reference: python/minisgl/models/eagle3.py:110-144."""
+        import json
+        import os
+
+        raw = json.loads(open(os.path.join(path, "config.json")).read())
+        if int(raw.get("num_hidden_layers", 1)) != 1:
+            raise ValueError(f"EAGLE-3 draft with {raw.get('num_hidden_layers')} layers is not supported")
+        eagle = raw.get("eagle_config") or {}
+        if eagle.get("use_aux_hidden_state") is False:
+            raise ValueError("EAGLE-3 draft without auxiliary hidden states is not supported")
+        H = int(raw["hidden_size"])
+        if H != target.hidden_size:
+            raise ValueError(f"EAGLE-3 draft hidden size {H} != target hidden size {target.hidden_size}")
+        scaling = raw.get("rope_scaling") or {}
+        params = raw.get("rope_parameters") or {}
+        kind = scaling.get("rope_type", scaling.get("type")) or params.get("rope_type")
+        if kind not in (None, "default"):
+            raise ValueError(f"EAGLE-3 draft rotary scaling {kind!r} is not supported")
+        override = (os.environ.get("FASTAFD_SPEC_EAGLE3_LAYERS") or os.environ.get("MINISGL_AFD_SPEC_EAGLE3_LAYERS") or "").strip()
+        ids = [int(x) for x in override.split(",")] if override else eagle.get("eagle_aux_hidden_state_layer_ids")
+        L = target.num_layers
+        if not ids:
+            ids = [1, L // 2 - 1, L - 4]
+        if len(ids) != 3 or not all(0 <= int(i) < L for i in ids):
+            raise ValueError(f"EAGLE-3 auxiliary layers {ids} do not name three layers of a {L}-layer target")
+        heads = int(raw["num_attention_heads"])
+        return Eagle3Config(H, heads, int(raw.get("num_key_value_heads", heads)), int(raw.get("head_dim") or H // heads),
+                            int(raw["intermediate_size"]), int(raw.get("draft_vocab_size") or raw.get("vocab_size") or target.vocab_size),
+                            target.vocab_size, tuple(int(i) for i in ids), float(raw.get("rms_norm_eps", 1e-6)),
+                            float(raw.get("rope_theta") or params.get("rope_theta") or 10000.0))
+
+
 class Eagle3Draft:
     def __init__(self, cfg: Eagle3Config, device, dtype, num_slots: int):
         self.cfg, self.device, self.dtype = cfg, torch.device(device), dtype
@@ -83,9 +121,12 @@ class Eagle3Draft:
         self.d2t = torch.arange(c.draft_vocab, dtype=torch.int32, device=self.device)
         return self
 
-    def load(self, path: str) -> "Eagle3Draft":
+    def load(self, path: str, share_embedding: Optional[torch.Tensor] = None,
+             share_lm_head: Optional[torch.Tensor] = None) -> "Eagle3Draft":
         """Load a draft checkpoint (safetensors; q/k/v and gate/up stored separately or merged;
-        ``d2t`` stored as offsets relative to the draft index, as published EAGLE-3 heads do)."""
+        ``d2t`` stored as offsets relative to the draft index, as published EAGLE-3 heads do). A head that
+        ships no embedding uses the target's (`share_embedding`); one without its own LM head uses the target's
+        (`share_lm_head`, full vocabulary, identity map)."""
         from safetensors.torch import load_file
         import glob
         import os
@@ -98,6 +139,13 @@ class Eagle3Draft:
             raw["self_attn.qkv_proj.weight"] = torch.cat([raw.pop(f"self_attn.{n}_proj.weight") for n in "qkv"], 0)
         if "mlp.gate_proj.weight" in raw:
             raw["mlp.gate_up_proj.weight"] = torch.cat([raw.pop("mlp.gate_proj.weight"), raw.pop("mlp.up_proj.weight")], 0)
+        if "embed_tokens.weight" not in raw and share_embedding is not None:
+            raw["embed_tokens.weight"] = share_embedding
+        if "lm_head.weight" not in raw and share_lm_head is not None:
+            if self.cfg.draft_vocab != share_lm_head.shape[0]:
+                raise ValueError(f"draft without an LM head but draft vocabulary {self.cfg.draft_vocab} != target's {share_lm_head.shape[0]}")
+            raw["lm_head.weight"] = share_lm_head
+            raw.pop("d2t", None)
         for name, shape in self.shapes().items():
             if name not in raw:
                 raise KeyError(f"draft checkpoint lacks {name}")
@@ -106,6 +154,8 @@ class Eagle3Draft:
             self.w[name] = raw[name].to(self.device, self.dtype)
         if "d2t" in raw:
             off = raw["d2t"].to(torch.int64)
+            if off.numel() != self.cfg.draft_vocab:
+                raise ValueError(f"d2t has {off.numel()} entries, the draft LM head {self.cfg.draft_vocab} rows")
             self.d2t = (torch.arange(off.numel()) + off).to(torch.int32).to(self.device)
         else:
             self.d2t = torch.arange(self.cfg.draft_vocab, dtype=torch.int32, device=self.device)

@@ -116,3 +116,103 @@ def test_verify_steps_planned_ahead_stay_lossless():
     st = coord.spec_stats()
     assert st["verify_steps"] > 0 and st["tokens"] == sum(len(t) - 1 for t in plain)
     assert 1.0 <= st["mean_accepted"] <= 4.0 and st["rows"] <= st["tokens"]
+
+
+def _published_draft(path, cfg, *, hidden, heads, kv_heads, head_dim, inter, draft_vocab, layer_ids, with_embedding=False, with_head=True):
+    """A draft directory in the layout of published EAGLE-3 heads: its own config.json, `midlayer.*` keys with separate
+    q/k/v and gate/up, `fc`, `norm`, a small-vocabulary `lm_head` with `d2t` offsets (and the unused `t2d` mask)."""
+    import json
+    import os
+
+    from safetensors.torch import save_file
+
+    os.makedirs(path, exist_ok=True)
+    json.dump({"architectures": ["LlamaForCausalLMEagle3"], "hidden_size": hidden, "num_attention_heads": heads,
+               "num_key_value_heads": kv_heads, "head_dim": head_dim, "intermediate_size": inter, "num_hidden_layers": 1,
+               "vocab_size": cfg.vocab_size, "draft_vocab_size": draft_vocab, "rms_norm_eps": 1e-5, "rope_theta": 50000.0,
+               "eagle_config": {"eagle_aux_hidden_state_layer_ids": list(layer_ids), "use_aux_hidden_state": True}},
+              open(os.path.join(path, "config.json"), "w"))
+    g = torch.Generator().manual_seed(5)
+    r = lambda *s: torch.randn(*s, generator=g) * 0.05  # noqa: E731
+    sd = {"fc.weight": r(hidden, 3 * hidden), "norm.weight": torch.ones(hidden),
+          "midlayer.input_layernorm.weight": torch.ones(hidden), "midlayer.hidden_norm.weight": torch.ones(hidden),
+          "midlayer.post_attention_layernorm.weight": torch.ones(hidden),
+          "midlayer.self_attn.q_proj.weight": r(heads * head_dim, 2 * hidden),
+          "midlayer.self_attn.k_proj.weight": r(kv_heads * head_dim, 2 * hidden),
+          "midlayer.self_attn.v_proj.weight": r(kv_heads * head_dim, 2 * hidden),
+          "midlayer.self_attn.o_proj.weight": r(hidden, heads * head_dim),
+          "midlayer.mlp.gate_proj.weight": r(inter, hidden), "midlayer.mlp.up_proj.weight": r(inter, hidden),
+          "midlayer.mlp.down_proj.weight": r(hidden, inter)}
+    if with_head:
+        sd["lm_head.weight"] = r(draft_vocab, hidden)
+        picks = torch.randperm(cfg.vocab_size, generator=g)[:draft_vocab].sort().values          # draft id -> target id
+        sd["d2t"] = picks - torch.arange(draft_vocab)
+        mask = torch.zeros(cfg.vocab_size, dtype=torch.bool)
+        mask[picks] = True
+        sd["t2d"] = mask
+    if with_embedding:
+        sd["embed_tokens.weight"] = r(cfg.vocab_size, hidden)
+    save_file(sd, os.path.join(path, "model.safetensors"))
+    return sd
+
+
+@pytest.mark.parametrize("with_embedding,with_head", [(False, True), (True, False)])
+def test_published_draft_head_layout_is_loaded_from_its_own_config(tmp_path, with_embedding, with_head):
+    """A draft head whose sizes differ from what the target would suggest (heads, head dim, MLP width, a 100-token
+    draft vocabulary with a d2t map, its own auxiliary layers and rotary base), without an embedding of its own
+    (the target's is shared) or without an LM head (the target's is used): the engine takes every size from the
+    head's config.json, and greedy verification stays lossless whatever the head proposes."""
+    from fastafd_b200.spec.eagle3 import Eagle3Config
+
+    cfg = PRESETS["tiny-qwen3-moe"]
+    path = str(tmp_path / "draft")
+    dv = 100 if with_head else cfg.vocab_size
+    sd = _published_draft(path, cfg, hidden=cfg.hidden_size, heads=2, kv_heads=1, head_dim=32, inter=96, draft_vocab=dv,
+                          layer_ids=(0, 1, 2) if cfg.num_layers >= 3 else (0, 0, 1), with_embedding=with_embedding, with_head=with_head)
+    dc = Eagle3Config.from_dir(path, cfg)
+    assert (dc.num_q_heads, dc.num_kv_heads, dc.head_dim, dc.intermediate_size, dc.draft_vocab) == (2, 1, 32, 96, dv)
+    assert dc.rope_theta == 50000.0 and dc.rms_eps == 1e-5 and dc.target_vocab == cfg.vocab_size
+    g = torch.Generator().manual_seed(0)
+    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (30, 7, 18)]
+    sp = SamplingParams(max_tokens=9, ignore_eos=True)
+    plain = SpmdDriver(AfdEngine(cfg, _rt(), AfdTopology(colocated=True), 0, "cpu", seed=0)).generate(prompts, sp)
+    eng = AfdEngine(cfg, _rt(spec_block=3, spec_draft_path=path), AfdTopology(colocated=True), 0, "cpu", seed=0)
+    draft = eng.attn.spec.draft
+    assert draft.cfg == dc and list(eng.attn.spec.capture_layers) == list(dc.target_layers)
+    if with_head:
+        assert draft.d2t.tolist() == (sd["d2t"] + torch.arange(dv)).tolist() and draft.w["lm_head.weight"].shape[0] == dv
+        assert draft.w["embed_tokens.weight"] is eng.attn.model.w["model.embed_tokens.weight"]      # shared, not copied
+    else:
+        assert draft.w["lm_head.weight"].shape[0] == cfg.vocab_size and draft.d2t.tolist() == list(range(cfg.vocab_size))
+        assert torch.equal(draft.w["embed_tokens.weight"], sd["embed_tokens.weight"])
+    assert SpmdDriver(eng).generate(prompts, sp) == plain
+
+
+def test_draft_config_refusals(tmp_path, monkeypatch):
+    import json
+
+    from fastafd_b200.spec.eagle3 import Eagle3Config
+
+    cfg = PRESETS["tiny-qwen3-moe"]
+    path = str(tmp_path / "d")
+    _published_draft(path, cfg, hidden=cfg.hidden_size, heads=2, kv_heads=1, head_dim=32, inter=96, draft_vocab=50, layer_ids=(0, 1, 2))
+    base = json.load(open(path + "/config.json"))
+
+    def with_(**kw):
+        c = dict(base)
+        c.update(kw)
+        json.dump(c, open(path + "/config.json", "w"))
+
+    monkeypatch.setenv("MINISGL_AFD_SPEC_EAGLE3_LAYERS", "2,1,0")
+    assert Eagle3Config.from_dir(path, cfg).target_layers == (2, 1, 0)             # the reference's override knob
+    monkeypatch.delenv("MINISGL_AFD_SPEC_EAGLE3_LAYERS")
+    for bad, pattern in ((dict(num_hidden_layers=2), "layers"), (dict(hidden_size=cfg.hidden_size * 2), "hidden size"),
+                         (dict(rope_scaling={"rope_type": "yarn", "factor": 4.0}), "rotary scaling"),
+                         (dict(eagle_config={"use_aux_hidden_state": False}), "auxiliary"),
+                         (dict(eagle_config={"eagle_aux_hidden_state_layer_ids": [0, 1, 99]}), "auxiliary layers")):
+        with_(**bad)
+        with pytest.raises(ValueError, match=pattern):
+            Eagle3Config.from_dir(path, cfg)
+    big = PRESETS["qwen3-30b-a3b"]                      # no ids: the default rule, which needs a deep enough target
+    with_(eagle_config={}, hidden_size=big.hidden_size)
+    assert Eagle3Config.from_dir(path, big).target_layers == (1, big.num_layers // 2 - 1, big.num_layers - 4)
