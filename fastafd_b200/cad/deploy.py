@@ -131,10 +131,18 @@ class CadLocalWorkers(CadTransport):
             raise ValueError("CAD serves models whose layers all have full attention")
         self.cfg, self.rt, self.topo, self.ranks = cfg, rt, topo, CadRanks.of(topo)
         self.device, self.dtype, self.seed = torch.device(device), dtype, seed
+        from ..engine import resolve_checkpoint
+
+        self.checkpoint = resolve_checkpoint(rt)       # a checkpoint directory, or None: random weights from the seed
         self.experts = ExpertStage(cfg, self.device, dtype, 0, 1)
-        self.experts.init_random(seed)
+        if self.checkpoint is None:
+            self.experts.init_random(seed)
+        else:
+            from ..models.loader import load_expert_stage
+
+            load_expert_stage(self.experts, self.checkpoint)
         self.workers = {a: AttentionWorker(cfg, rt, self.device, LocalMoeClient([self.experts]), dtype=dtype, rank=a,
-                                           dp_lane=a, weight_init=lambda m: m.init_random(seed))
+                                           dp_lane=a, weight_init=self._init_dense)
                         for a in range(self.ranks.num_attn)}
         self.num_pages = min(w.num_pages for w in self.workers.values())
         self.attn_sides: Dict[int, CadAttentionSide] = {}
@@ -142,12 +150,20 @@ class CadLocalWorkers(CadTransport):
         self._out: List[object] = []
         self.steps_run = 0
 
+    def _init_dense(self, stage: AttentionStage) -> None:
+        if self.checkpoint is None:
+            stage.init_random(self.seed)
+        else:
+            from ..models.loader import load_attention_stage
+
+            load_attention_stage(stage, self.checkpoint)
+
     # ------------------------------------------------------------------ CAD init
     def send_cad_init(self, cmd: CadInitCmd) -> None:
         cfg, rk = self.cfg, self.ranks
         check_balanced(cfg.num_layers, cmd.num_mb, rk.r)
         stage = AttentionStage(cfg, self.device, self.dtype, 0, 1, None)      # the model ranks' dense weights
-        stage.init_random(self.seed)
+        self._init_dense(stage)
         lay = CadLayout(cfg.num_layers, cmd.num_mb, rk.r * cmd.t_max, cfg.q_size, cfg.kv_size)
         for j, rank in enumerate(rk.model_ranks()):
             wins = []

@@ -329,3 +329,33 @@ def test_alignment_tool_against_the_library(tmp_path, capsys):
     assert rep["rank_gate"]["worst_rank"] == 0 and rep["first_divergence"] == [4, 4]
     assert validate.main(common) == 0
     assert json.loads(capsys.readouterr().out.strip().splitlines()[-1])["against"] == "oracle"
+
+
+def test_core_attention_disaggregation_on_a_library_checkpoint(tmp_path, monkeypatch):
+    """MiniMax-M2 (the model the reference runs this mode on) saved by the library, served with the attention core on
+    two attention ranks and everything else on a model rank (one process, CPU): the library's tokens."""
+    cls_name, cfg_name, extra = FAMILIES["minimax-m2"]
+    if not (hasattr(transformers, cls_name) and hasattr(transformers, cfg_name)):
+        pytest.skip(f"transformers {transformers.__version__} has no {cls_name}")
+    torch.manual_seed(0)
+    kw = dict(COMMON)
+    kw.update(extra)
+    model = getattr(transformers, cls_name)(getattr(transformers, cfg_name)(**kw)).float().eval()
+    with torch.no_grad():
+        for _name, p in model.named_parameters():
+            if p.dim() == 1:
+                p.add_(0.1 * torch.randn_like(p))
+    path = str(tmp_path / "m2")
+    model.save_pretrained(path, safe_serialization=True)
+    g = torch.Generator().manual_seed(1)
+    prompts = [torch.randint(0, 256, (n,), generator=g).tolist() for n in (5, 11, 3, 20)]
+    want = [_library_greedy(model, p, 6) for p in prompts]
+    monkeypatch.setenv("MINISGL_AFD_MODE", "cad")
+    monkeypatch.setenv("FASTAFD_CAD_ATTN_PER_MODEL", "2")
+    llm = LLM(path, device="cpu", num_pages=64, max_seq_len=128, num_mb=2)
+    try:
+        assert type(llm.coordinator).__name__ == "CadCoordinator"
+        got = [o["token_ids"] for o in llm.generate(prompts, SamplingParams(max_tokens=6, ignore_eos=True))]
+    finally:
+        llm.shutdown()
+    assert got == want
