@@ -256,7 +256,19 @@ class ModelConfig:
 
     @staticmethod
     def from_path(path: str) -> "ModelConfig":
-        return ModelConfig.from_hf(json.loads((Path(path) / "config.json").read_text()))
+        """A checkpoint directory's ``config.json``; the stop tokens are those of ``config.json`` together with those
+        of ``generation_config.json`` when the directory has one (chat models list their end-of-turn token there)."""
+        cfg = ModelConfig.from_hf(json.loads((Path(path) / "config.json").read_text()))
+        gen = Path(path) / "generation_config.json"
+        if gen.exists():
+            try:
+                eos = json.loads(gen.read_text()).get("eos_token_id")
+            except (OSError, ValueError):
+                eos = None
+            more = tuple(eos) if isinstance(eos, (list, tuple)) else ((eos,) if eos is not None else ())
+            ids = tuple(dict.fromkeys(int(t) for t in cfg.eos_token_ids + more))
+            cfg = replace(cfg, eos_token_ids=ids)
+        return cfg
 
 
 def _hybrid_types(n: int, interval: int = 4) -> Tuple[str, ...]:

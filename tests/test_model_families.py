@@ -98,3 +98,20 @@ def test_rope_scaling_tables():
     table = ref.build_cos_sin_cache(128, rot, theta, scaling={"rope_type": "yarn", "factor": 4.0,
                                                                "original_max_position_embeddings": 4096})
     assert table.shape == (128, rot)
+
+
+def test_stop_tokens_come_from_config_and_generation_config(tmp_path):
+    import json
+
+    from fastafd_b200.config import PRESETS, ModelConfig, get_model_config
+
+    hf = PRESETS["tiny-qwen3-moe"].to_hf()
+    hf["eos_token_id"] = 7
+    (tmp_path / "config.json").write_text(json.dumps(hf))
+    assert get_model_config(str(tmp_path)).eos_token_ids == (7,)
+    (tmp_path / "generation_config.json").write_text(json.dumps({"eos_token_id": [9, 7], "temperature": 0.6}))
+    assert ModelConfig.from_path(str(tmp_path)).eos_token_ids == (7, 9)
+    (tmp_path / "generation_config.json").write_text(json.dumps({"eos_token_id": 11}))
+    assert ModelConfig.from_path(str(tmp_path)).eos_token_ids == (7, 11)
+    (tmp_path / "generation_config.json").write_text("{ not json")
+    assert ModelConfig.from_path(str(tmp_path)).eos_token_ids == (7,)
