@@ -173,6 +173,14 @@ class ModelConfig:
             kw.update(qk_norm="head")
         if arch in ("Qwen2ForCausalLM",):
             kw.update(attention_bias=True)
+        # Attention over a sliding window is not implemented; within the window it equals full attention, so a model
+        # that uses one is served up to its window length.
+        window = cfg.get("sliding_window")
+        if window and cfg.get("use_sliding_window", arch.startswith("Mistral")) and int(window) < kw["max_position"]:
+            kw["max_position"] = int(window)
+        if arch in ("Qwen3MoeForCausalLM", "Qwen3_5MoeForCausalLM", "Qwen3_5MoeForConditionalGeneration", "Qwen3NextForCausalLM"):
+            if cfg.get("mlp_only_layers") or int(cfg.get("decoder_sparse_step", 1) or 1) != 1:
+                raise ValueError(f"{arch}: dense layers among the MoE layers (mlp_only_layers / decoder_sparse_step) are not supported")
         if arch == "Qwen3MoeForCausalLM":
             kw.update(qk_norm="head", num_experts=experts(), num_experts_per_tok=cfg["num_experts_per_tok"],
                       moe_intermediate_size=cfg["moe_intermediate_size"],

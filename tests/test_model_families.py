@@ -115,3 +115,22 @@ def test_stop_tokens_come_from_config_and_generation_config(tmp_path):
     assert ModelConfig.from_path(str(tmp_path)).eos_token_ids == (7, 11)
     (tmp_path / "generation_config.json").write_text("{ not json")
     assert ModelConfig.from_path(str(tmp_path)).eos_token_ids == (7,)
+
+
+def test_config_variants_that_are_not_served_as_written():
+    import pytest
+
+    from fastafd_b200.config import PRESETS, ModelConfig
+
+    moe = PRESETS["tiny-qwen3-moe"].to_hf()
+    assert ModelConfig.from_hf(dict(moe, mlp_only_layers=[], decoder_sparse_step=1)).num_experts > 0
+    for bad in (dict(mlp_only_layers=[0]), dict(decoder_sparse_step=2)):
+        with pytest.raises(ValueError, match="dense layers among the MoE layers"):
+            ModelConfig.from_hf(dict(moe, **bad))
+    mistral = dict(architectures=["MistralForCausalLM"], hidden_size=64, num_hidden_layers=2, num_attention_heads=4,
+                   num_key_value_heads=2, vocab_size=256, intermediate_size=128, max_position_embeddings=32768)
+    assert ModelConfig.from_hf(dict(mistral, sliding_window=4096)).max_position == 4096          # served within its window
+    assert ModelConfig.from_hf(dict(mistral, sliding_window=None)).max_position == 32768
+    qwen2 = dict(mistral, architectures=["Qwen2ForCausalLM"], sliding_window=4096)
+    assert ModelConfig.from_hf(dict(qwen2, use_sliding_window=False)).max_position == 32768       # declared but switched off
+    assert ModelConfig.from_hf(dict(qwen2, use_sliding_window=True)).max_position == 4096
