@@ -173,6 +173,10 @@ class ModelConfig:
             kw.update(qk_norm="head")
         if arch in ("Qwen2ForCausalLM",):
             kw.update(attention_bias=True)
+        if cfg.get("mlp_bias"):
+            raise ValueError(f"{arch}: MLP projections with a bias (mlp_bias) are not supported")
+        if cfg.get("hidden_act", "silu") not in ("silu", "swish"):
+            raise ValueError(f"{arch}: activation {cfg.get('hidden_act')!r} is not supported (SwiGLU with SiLU only)")
         # Attention over a sliding window is not implemented; within the window it equals full attention, so a model
         # that uses one is served up to its window length.
         window = cfg.get("sliding_window")

@@ -131,6 +131,9 @@ def test_config_variants_that_are_not_served_as_written():
                    num_key_value_heads=2, vocab_size=256, intermediate_size=128, max_position_embeddings=32768)
     assert ModelConfig.from_hf(dict(mistral, sliding_window=4096)).max_position == 4096          # served within its window
     assert ModelConfig.from_hf(dict(mistral, sliding_window=None)).max_position == 32768
+    for bad, pattern in ((dict(mlp_bias=True), "mlp_bias"), (dict(hidden_act="gelu"), "activation")):
+        with pytest.raises(ValueError, match=pattern):
+            ModelConfig.from_hf(dict(mistral, **bad))
     qwen2 = dict(mistral, architectures=["Qwen2ForCausalLM"], sliding_window=4096)
     assert ModelConfig.from_hf(dict(qwen2, use_sliding_window=False)).max_position == 32768       # declared but switched off
     assert ModelConfig.from_hf(dict(qwen2, use_sliding_window=True)).max_position == 4096
