@@ -39,6 +39,11 @@ class RopeConfig:
     scaling: Optional[Dict[str, Any]] = None   # llama3 / yarn parameters
 
 
+SUPPORTED_ARCHITECTURES = ("LlamaForCausalLM", "MistralForCausalLM", "Qwen2ForCausalLM", "Qwen3ForCausalLM",
+                           "Qwen3MoeForCausalLM", "Glm4MoeForCausalLM", "MiniMaxM2ForCausalLM", "Qwen3_5MoeForCausalLM",
+                           "Qwen3_5MoeForConditionalGeneration", "Qwen3NextForCausalLM")
+
+
 @dataclass(frozen=True)
 class ModelConfig:
     architecture: str = "Qwen3MoeForCausalLM"
@@ -133,6 +138,9 @@ class ModelConfig:
                 inner.setdefault("quantization_config", cfg["quantization_config"])
             cfg = inner
         arch = (cfg.get("architectures") or ["LlamaForCausalLM"])[0]
+
+        if arch not in SUPPORTED_ARCHITECTURES:
+            raise ValueError(f"architecture {arch!r} is not served; supported: {', '.join(SUPPORTED_ARCHITECTURES)}")
 
         def experts() -> int:
             """Routed experts: the key differs by family and by the library version that wrote the file."""

@@ -137,3 +137,13 @@ def test_config_variants_that_are_not_served_as_written():
     qwen2 = dict(mistral, architectures=["Qwen2ForCausalLM"], sliding_window=4096)
     assert ModelConfig.from_hf(dict(qwen2, use_sliding_window=False)).max_position == 32768       # declared but switched off
     assert ModelConfig.from_hf(dict(qwen2, use_sliding_window=True)).max_position == 4096
+
+
+def test_unknown_architectures_are_refused_by_name():
+    import pytest
+
+    from fastafd_b200.config import PRESETS, SUPPORTED_ARCHITECTURES, ModelConfig
+
+    with pytest.raises(ValueError, match="DeepseekV3ForCausalLM.*not served"):
+        ModelConfig.from_hf({"architectures": ["DeepseekV3ForCausalLM"], "hidden_size": 64, "num_attention_heads": 4})
+    assert all(c.architecture in SUPPORTED_ARCHITECTURES for c in PRESETS.values())
