@@ -359,3 +359,33 @@ def test_core_attention_disaggregation_on_a_library_checkpoint(tmp_path, monkeyp
     finally:
         llm.shutdown()
     assert got == want
+
+
+def test_hybrid_model_under_queueing_slot_reuse_and_chunked_prefill(tmp_path):
+    """Ten requests through three request slots, prompts up to 40 tokens prefilled 16 tokens at a time, two
+    micro-batches: every request slot (and with it a recurrent-state slot and conv taps) is reused several times
+    and prompts are split over steps; each request still gets the library's tokens."""
+    cls_name, cfg_name, extra = FAMILIES["qwen3.5-moe"]
+    if not (hasattr(transformers, cls_name) and hasattr(transformers, cfg_name)):
+        pytest.skip(f"transformers {transformers.__version__} has no {cls_name}")
+    torch.manual_seed(0)
+    kw = dict(COMMON)
+    kw.update(extra)
+    model = getattr(transformers, cls_name)(getattr(transformers, cfg_name)(**kw)).float().eval()
+    with torch.no_grad():
+        for _name, p in model.named_parameters():
+            if p.dim() == 1:
+                p.add_(0.1 * torch.randn_like(p))
+    path = str(tmp_path / "hybrid")
+    model.save_pretrained(path, safe_serialization=True)
+    g = torch.Generator().manual_seed(3)
+    prompts = [torch.randint(0, 256, (n,), generator=g).tolist() for n in (7, 33, 12, 5, 40, 9, 21, 3, 18, 26)]
+    max_tokens = [3, 6, 2, 7, 4, 5, 1, 6, 3, 4]
+    want = [_library_greedy(model, p, n) for p, n in zip(prompts, max_tokens)]
+    llm = LLM(path, device="cpu", num_pages=64, max_seq_len=128, max_running_requests=3, cuda_graph_max_bs=4, num_mb=2,
+              max_batched_tokens=16)
+    try:
+        got = [o["token_ids"] for o in llm.generate(prompts, [SamplingParams(max_tokens=n, ignore_eos=True) for n in max_tokens])]
+    finally:
+        llm.shutdown()
+    assert got == want
