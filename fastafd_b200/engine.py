@@ -98,6 +98,12 @@ class AfdEngine:
         self.device, self.seed = torch.device(device), seed
         self.dtype = _torch_dtype(rt.dtype, self.device)
         self.colocated = topo.world == 1
+        if not self.colocated:
+            from .protocol import validate_parallel_args
+
+            validate_parallel_args(topo, max(cfg.num_experts, topo.mlp_ep), cfg.num_q_heads, cfg.num_kv_heads,
+                                   cfg.gdn_num_k_heads if cfg.num_linear_layers else 0,
+                                   cfg.gdn_num_v_heads if cfg.num_linear_layers else 0)
         self.is_attention = self.colocated or topo.is_attention(rank)
         self.is_expert = self.colocated or topo.is_expert(rank)
         cuda = self.device.type == "cuda"

@@ -124,8 +124,13 @@ class AfdTopology:
         return AfdTopology(attn_dp=n_attn // attn_tp, attn_tp=attn_tp, mlp_dp=1, mlp_tp=1, mlp_ep=world - n_attn)
 
 
-def validate_parallel_args(topo: AfdTopology, num_experts: int, num_q_heads: int, num_kv_heads: int) -> None:
-    """Mutual divisibility rules (python/minisgl/server/args.py:135-180)."""
+def validate_parallel_args(topo: AfdTopology, num_experts: int, num_q_heads: int, num_kv_heads: int,
+                           linear_k_heads: int = 0, linear_v_heads: int = 0) -> None:
+    """Mutual divisibility rules (python/minisgl/server/args.py:135-180). `linear_*_heads`: head counts of the
+    linear-attention layers of a hybrid model (0: none); they are sharded by heads like the attention heads."""
+    for name, n in (("linear-attention key", linear_k_heads), ("linear-attention value", linear_v_heads)):
+        if n and n % topo.attn_tp:
+            raise ValueError(f"attn_tp={topo.attn_tp} does not divide {n} {name} heads")
     if num_q_heads % topo.attn_tp:
         raise ValueError(f"attn_tp={topo.attn_tp} does not divide {num_q_heads} query heads")
     if num_kv_heads % topo.attn_tp and topo.attn_tp % num_kv_heads:

@@ -156,7 +156,9 @@ def validate(args: ServerArgs) -> None:
         topo = args.topology      # raises on bad ep / tp combinations
         if not cfg.is_moe:
             raise ValueError("afd-serve needs a mixture-of-experts model; use --mode serve for dense models")
-        validate_parallel_args(topo, cfg.num_experts, cfg.num_q_heads, cfg.num_kv_heads)
+        validate_parallel_args(topo, cfg.num_experts, cfg.num_q_heads, cfg.num_kv_heads,
+                               cfg.gdn_num_k_heads if cfg.num_linear_layers else 0,
+                               cfg.gdn_num_v_heads if cfg.num_linear_layers else 0)
 
 
 def build_parser() -> argparse.ArgumentParser:

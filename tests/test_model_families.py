@@ -147,3 +147,16 @@ def test_unknown_architectures_are_refused_by_name():
     with pytest.raises(ValueError, match="DeepseekV3ForCausalLM.*not served"):
         ModelConfig.from_hf({"architectures": ["DeepseekV3ForCausalLM"], "hidden_size": 64, "num_attention_heads": 4})
     assert all(c.architecture in SUPPORTED_ARCHITECTURES for c in PRESETS.values())
+
+
+def test_tensor_parallel_size_must_divide_the_linear_attention_heads():
+    import pytest
+
+    from fastafd_b200.protocol import AfdTopology, validate_parallel_args
+
+    ok = AfdTopology(attn_dp=1, attn_tp=2, mlp_ep=1)
+    validate_parallel_args(ok, 8, 4, 2, linear_k_heads=2, linear_v_heads=4)
+    with pytest.raises(ValueError, match="linear-attention key heads"):
+        validate_parallel_args(AfdTopology(attn_dp=1, attn_tp=4, mlp_ep=1), 8, 4, 2, linear_k_heads=2, linear_v_heads=4)
+    with pytest.raises(ValueError, match="linear-attention value heads"):
+        validate_parallel_args(AfdTopology(attn_dp=1, attn_tp=4, mlp_ep=1), 8, 4, 2, linear_k_heads=4, linear_v_heads=6)
