@@ -59,6 +59,14 @@ FAMILIES = {
                                  dict(intermediate_size=128, head_dim=16, moe_intermediate_size=32, num_experts=8, num_experts_per_tok=3,
                                       norm_topk_prob=False, decoder_sparse_step=1, mlp_only_layers=[])),
     "qwen3-next": ("Qwen3NextForCausalLM", "Qwen3NextConfig", dict(GDN, decoder_sparse_step=1, mlp_only_layers=[])),
+    # four value heads per key head (the ratio of the published models), key and value head dims that differ
+    "qwen3.5-moe-head-ratio-4": ("Qwen3_5MoeForCausalLM", "Qwen3_5MoeTextConfig",
+                                 dict(GDN, linear_num_key_heads=2, linear_num_value_heads=8, linear_key_head_dim=32,
+                                      linear_value_head_dim=16, num_attention_heads=8, num_key_value_heads=2, head_dim=32)),
+    "qwen3-next-head-ratio-4": ("Qwen3NextForCausalLM", "Qwen3NextConfig",
+                                dict(GDN, decoder_sparse_step=1, mlp_only_layers=[], linear_num_key_heads=2, linear_num_value_heads=8,
+                                     linear_key_head_dim=32, linear_value_head_dim=16, num_attention_heads=8, num_key_value_heads=2,
+                                     head_dim=32)),
 }
 
 
