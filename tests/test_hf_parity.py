@@ -59,6 +59,14 @@ FAMILIES = {
                                  dict(intermediate_size=128, head_dim=16, moe_intermediate_size=32, num_experts=8, num_experts_per_tok=3,
                                       norm_topk_prob=False, decoder_sparse_step=1, mlp_only_layers=[])),
     "qwen3-next": ("Qwen3NextForCausalLM", "Qwen3NextConfig", dict(GDN, decoder_sparse_step=1, mlp_only_layers=[])),
+    # routing: four groups of which two are kept, top-4 of 16 experts
+    "glm4-moe-groups-4-keep-2": ("Glm4MoeForCausalLM", "Glm4MoeConfig",
+                                 dict(intermediate_size=128, head_dim=16, moe_intermediate_size=32, n_routed_experts=16,
+                                      num_experts_per_tok=4, n_shared_experts=1, n_group=4, topk_group=2, first_k_dense_replace=1,
+                                      norm_topk_prob=True, routed_scaling_factor=1.0, use_qk_norm=True, partial_rotary_factor=0.5)),
+    "minimax-m2-top4-of-16": ("MiniMaxM2ForCausalLM", "MiniMaxM2Config",
+                              dict(intermediate_size=32, head_dim=16, num_local_experts=16, num_experts_per_tok=4, use_qk_norm=True,
+                                   rope_parameters={"rope_theta": 5e6, "rope_type": "default", "partial_rotary_factor": 0.5})),
     # four value heads per key head (the ratio of the published models), key and value head dims that differ
     "qwen3.5-moe-head-ratio-4": ("Qwen3_5MoeForCausalLM", "Qwen3_5MoeTextConfig",
                                  dict(GDN, linear_num_key_heads=2, linear_num_value_heads=8, linear_key_head_dim=32,
