@@ -75,6 +75,28 @@ def _sampling(req) -> SamplingParams:
                           top_p=getattr(req, "top_p", 1.0), ignore_eos=req.ignore_eos, max_tokens=req.max_tokens)
 
 
+class StopFilter:
+    """Stop strings of a request (`stop` of the OpenAI request body): text is passed on up to the first stop string,
+    which is not part of the output; the last characters are held back while they could still be the beginning of
+    a stop string that continues in the next piece."""
+
+    def __init__(self, stops: List[str]):
+        self.stops = [s for s in stops if s]
+        self.hold = max(len(s) for s in self.stops) - 1
+        self.buf = ""
+
+    def feed(self, text: str, final: bool):
+        """-> (text to emit now, whether a stop string was reached)."""
+        self.buf += text
+        cut = min((i for i in (self.buf.find(s) for s in self.stops) if i >= 0), default=-1)
+        if cut >= 0:
+            out, self.buf = self.buf[:cut], ""
+            return out, True
+        keep = 0 if final else min(self.hold, len(self.buf))
+        out, self.buf = self.buf[:len(self.buf) - keep], self.buf[len(self.buf) - keep:]
+        return out, False
+
+
 class FrontendManager:
     """uid allocation, per-request reply queues, and the reader task that routes
     ``UserReply`` messages from the detokenizer to the waiting HTTP handlers."""
@@ -86,6 +108,7 @@ class FrontendManager:
         self.pull = ZmqAsyncPullQueue(from_tokenizer_addr, bind=True)
         self.next_uid = 0
         self.queues: Dict[int, asyncio.Queue] = {}
+        self.stops: Dict[int, StopFilter] = {}
         self._reader: Optional[asyncio.Task] = None
 
     def start(self) -> None:
@@ -100,19 +123,30 @@ class FrontendManager:
                 if q is not None:
                     q.put_nowait(msg)
 
-    async def submit(self, *, text=None, messages=None, input_ids=None, sampling: SamplingParams) -> int:
+    async def submit(self, *, text=None, messages=None, input_ids=None, sampling: SamplingParams, stop=None) -> int:
         self.start()
         uid = self.next_uid
         self.next_uid += 1
         self.queues[uid] = asyncio.Queue()
+        stops = [stop] if isinstance(stop, str) else [s for s in (stop or []) if isinstance(s, str)]
+        if any(stops):
+            self.stops[uid] = StopFilter(stops)
         await self.push.put(TokenizeMsg(uid=uid, text=text, messages=messages, input_ids=input_ids, sampling=sampling))
         return uid
 
     async def stream(self, uid: int) -> AsyncIterator[UserReply]:
         q = self.queues[uid]
+        stop = self.stops.pop(uid, None)
         try:
             while True:
                 msg: UserReply = await q.get()
+                if stop is not None and not msg.error:
+                    text, hit = stop.feed(msg.text, msg.finished)
+                    msg = UserReply(uid=msg.uid, text=text, token_ids=msg.token_ids, finished=msg.finished or hit, error=msg.error)
+                    if hit and not msg.error:
+                        yield msg
+                        await self.push.put(AbortMsg(uid=uid))          # the backend stops generating for this request
+                        return
                 yield msg
                 if msg.finished:
                     return
@@ -121,6 +155,7 @@ class FrontendManager:
 
     async def abort(self, uid: int) -> None:
         self.queues.pop(uid, None)
+        self.stops.pop(uid, None)
         await self.push.put(AbortMsg(uid=uid))
 
     async def collect(self, uid: int) -> UserReply:
@@ -171,7 +206,7 @@ def create_app(manager: FrontendManager, model_name: str) -> FastAPI:
         if sum(given) != 1:
             return JSONResponse({"error": "give exactly one of prompt, messages, input_ids"}, status_code=400)
         msgs = [m.model_dump() for m in req.messages] if req.messages else None
-        uid = await manager.submit(text=req.prompt, messages=msgs, input_ids=req.input_ids, sampling=_sampling(req))
+        uid = await manager.submit(text=req.prompt, messages=msgs, input_ids=req.input_ids, sampling=_sampling(req), stop=req.stop)
         if not req.stream:
             # one JSON body once the request has finished (OpenAI "stream": false)
             r = await manager.collect(uid)

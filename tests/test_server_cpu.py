@@ -408,3 +408,52 @@ def test_hugging_face_tokenizer_directory_chat_template_and_incremental_detokeni
     streamed = "".join(dm.step(DetokenizeMsg(uid=7, token_ids=[t], finished=(i == len(out_ids) - 1))).text
                        for i, t in enumerate(out_ids))
     assert streamed == sample and "�" not in streamed
+
+
+def test_stop_strings_cut_the_output_and_hold_back_partial_matches():
+    from fastafd_b200.server.api_server import StopFilter
+
+    f = StopFilter(["</s>", "\n\n"])
+    out = []
+    for piece in ["Hello", " wor", "ld<", "/", "s", ">ignored"]:
+        text, hit = f.feed(piece, False)
+        out.append(text)
+        if hit:
+            break
+    assert "".join(out) == "Hello world" and hit                 # the stop string itself is not part of the output
+    assert all("<" not in t for t in out)                        # a possible beginning of a stop string is held back
+    g = StopFilter(["END"])
+    assert g.feed("abcE", False) == ("ab", False)                 # two characters held: they could start "END"
+    assert g.feed("Nx", False) == ("cE", False)
+    assert g.feed("y", True) == ("Nxy", False)                    # final piece: everything held is released
+    h = StopFilter(["a", "abc"])
+    assert h.feed("xxabc", False) == ("xx", True)                 # the earliest match wins
+
+
+def test_stop_strings_end_the_stream_and_abort_the_backend_request():
+    """The frontend's reply stream with a stop list: pieces are passed on up to the stop string, the reply that
+    reaches it is marked finished, an abort goes to the backend, and nothing later is delivered."""
+    import asyncio
+
+    from fastafd_b200.message import AbortMsg, UserReply
+    from fastafd_b200.server.api_server import FrontendManager, StopFilter
+
+    class Push:
+        def __init__(self):
+            self.sent = []
+
+        async def put(self, m):
+            self.sent.append(m)
+
+    async def run():
+        man = FrontendManager.__new__(FrontendManager)
+        man.queues, man.stops, man.push = {5: asyncio.Queue()}, {5: StopFilter(["STOP"])}, Push()
+        for i, piece in enumerate(["one ", "two S", "TO", "P three", " four"]):
+            man.queues[5].put_nowait(UserReply(uid=5, text=piece, token_ids=[i], finished=False))
+        got = [m async for m in man.stream(5)]
+        return man, got
+
+    man, got = asyncio.run(run())
+    assert "".join(m.text for m in got) == "one two " and got[-1].finished and not any(m.finished for m in got[:-1])
+    assert [type(m) for m in man.push.sent] == [AbortMsg] and man.push.sent[0].uid == 5
+    assert 5 not in man.queues and 5 not in man.stops
